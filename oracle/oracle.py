@@ -1,0 +1,295 @@
+"""ctypes view of the parity oracle (TEST INFRASTRUCTURE ONLY).
+
+Two libraries live under ``oracle/``:
+
+* ``libtsro.so`` -- this repository's C restatement of the reference numerics (``tsro.c``,
+  ``tsro_fa.c``); it is built from committed sources on any machine (``make -C oracle``).
+* ``_ref/libtsr_refdrv.so`` -- the reference's own ``sw/sim`` C library compiled where it lies,
+  plus ``ref_driver.c`` (``make -C oracle ref``). It exists only where the reference tree was
+  present when it was built; it travels with the working tree as a built file.
+
+Only the tests, ``__graft_entry__.smoke()`` and the CPU-baseline leg of ``bench.py`` import this
+module; the product never does.
+"""
+from __future__ import annotations
+
+import ctypes as ct
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+TSRO_PATH = os.path.join(HERE, "libtsro.so")
+REF_PATH = os.path.join(HERE, "_ref", "libtsr_refdrv.so")
+
+FMT_Q8_0, FMT_Q4_K = 0, 1
+MM_ADD, MM_SCALE, MM_SOFTCAP = 1, 2, 4
+
+_p = ct.c_void_p
+_u32, _i32, _f32, _sz = ct.c_uint32, ct.c_int32, ct.c_float, ct.c_size_t
+
+
+def _ptr(a):
+    return a.ctypes.data_as(_p) if a is not None else None
+
+
+def build(ref: bool = True) -> None:
+    """Builds libtsro.so (always) and, where the reference tree is present, the reference driver."""
+    subprocess.run(["make", "-s", "-C", HERE, "all"], check=True)
+    if ref and os.path.isdir(os.environ.get("REF_ROOT", "/root/reference") + "/sw/sim"):
+        subprocess.run(["make", "-s", "-C", HERE, "ref"], check=True)
+
+
+class FaParams(ct.Structure):
+    _fields_ = [("C", _u32), ("t_max", _u32), ("pcap", _u32), ("T", _u32), ("D", _u32), ("n_head", _u32),
+                ("n_head_kv", _u32), ("n_kv", _u32), ("scale", _f32), ("new_lo", _u32), ("new_hi", _u32)]
+
+
+class Tsro:
+    """The restatement (libtsro.so)."""
+
+    def __init__(self, path: str = TSRO_PATH):
+        if not os.path.exists(path):
+            build(ref=False)
+        L = self.lib = ct.CDLL(path)
+        for n in ("tsro_fadd", "tsro_fsub", "tsro_fmul", "tsro_fdiv"):
+            getattr(L, n).restype = _f32
+            getattr(L, n).argtypes = [_f32, _f32]
+        L.tsro_frecip.restype = _f32
+        L.tsro_frecip.argtypes = [_f32]
+        L.tsro_expk.restype = _f32
+        L.tsro_expk.argtypes = [_f32, ct.c_uint]
+        L.tsro_tanh.restype = _f32
+        L.tsro_tanh.argtypes = [_f32]
+        L.tsro_f32_to_fp16.restype = ct.c_uint16
+        L.tsro_f32_to_fp16.argtypes = [_f32]
+        L.tsro_qact_a32.argtypes = [_p, _u32, _p, _p]
+        L.tsro_qact_a256.argtypes = [_p, _u32, _p, _p, _p]
+        L.tsro_dot_q8_0.restype = _f32
+        L.tsro_dot_q8_0.argtypes = [_p, _u32, _p, _p, _p]
+        L.tsro_dot_q4_K.restype = _f32
+        L.tsro_dot_q4_K.argtypes = [_p, _u32, _p, _p, _p, _p]
+        L.tsro_matvec.restype = ct.c_int
+        L.tsro_matvec.argtypes = [_u32, _p, _u32, _u32, _p, _u32, _p, _u32, _u32, _f32, _f32, _p, ct.c_int]
+        L.tsro_fa.restype = ct.c_int
+        L.tsro_fa.argtypes = [ct.POINTER(FaParams), _p, _p, _p, _p, _sz, _p]
+        L.tsro_fa_qk_isums.argtypes = [ct.POINTER(FaParams), _p, _p, _p]
+        L.tsro_quantize_q8_0.argtypes = [_p, _u32, _p]
+        L.tsro_quantize_q4_K.argtypes = [_p, _u32, _p]
+
+    # -- scalar rules, vectorised by a Python loop (small inputs only) --
+    def fp(self, op: str, a, b=None):
+        a = np.asarray(a, np.float32).ravel()
+        f = getattr(self.lib, "tsro_" + op)
+        if op == "frecip":
+            return np.array([f(float(x)) for x in a], np.float32)
+        b = np.asarray(b, np.float32).ravel()
+        return np.array([f(float(x), float(y)) for x, y in zip(a, b)], np.float32)
+
+    def expk(self, v, kappa=0):
+        v = np.asarray(v, np.float32).ravel()
+        return np.array([self.lib.tsro_expk(float(x), kappa) for x in v], np.float32)
+
+    def tanh(self, v):
+        v = np.asarray(v, np.float32).ravel()
+        return np.array([self.lib.tsro_tanh(float(x)) for x in v], np.float32)
+
+    def qact(self, fmt: int, x):
+        """x [T, K] f32 -> (q [T, K] int8, d [T, K/bs] f32, bs [T, K/16] int16 or None)."""
+        x = np.ascontiguousarray(np.atleast_2d(x), np.float32)
+        T, K = x.shape
+        q = np.zeros((T, K), np.int8)
+        if fmt == FMT_Q8_0:
+            d = np.zeros((T, K // 32), np.float32)
+            for t in range(T):
+                self.lib.tsro_qact_a32(_ptr(x[t]), K, _ptr(q[t]), _ptr(d[t]))
+            return q, d, None
+        d = np.zeros((T, K // 256), np.float32)
+        bs = np.zeros((T, K // 16), np.int16)
+        for t in range(T):
+            self.lib.tsro_qact_a256(_ptr(x[t]), K, _ptr(q[t]), _ptr(d[t]), _ptr(bs[t]))
+        return q, d, bs
+
+    def block_isums(self, fmt: int, w, K: int, q, d, bs=None):
+        """Exact int32 block sums of every row against one QA vector: Q8_0 [N, K/32];
+        Q4_K [N, K/256, 2] ({sum sc*S, sum m*BS})."""
+        w = np.ascontiguousarray(w, np.uint8)
+        N = w.shape[0]
+        q = np.ascontiguousarray(q, np.int8)
+        d = np.ascontiguousarray(d, np.float32)
+        if fmt == FMT_Q8_0:
+            out = np.zeros((N, K // 32), np.int32)
+            for n in range(N):
+                self.lib.tsro_dot_q8_0(_ptr(w[n]), K, _ptr(q), _ptr(d), _ptr(out[n]))
+            return out
+        bs = np.ascontiguousarray(bs, np.int16)
+        out = np.zeros((N, K // 256, 2), np.int32)
+        for n in range(N):
+            self.lib.tsro_dot_q4_K(_ptr(w[n]), K, _ptr(q), _ptr(d), _ptr(bs), _ptr(out[n]))
+        return out
+
+    def matvec(self, fmt: int, w, K: int, x, add=None, add_stride=None, flags: int = 0, s0: float = 1.0,
+               s1: float = 1.0, threads: int | None = None):
+        """w: [N, row_bytes] ggml blocks; x: [T, K] f32 -> y [T, N] f32."""
+        w = np.ascontiguousarray(w, np.uint8)
+        x = np.ascontiguousarray(np.atleast_2d(x), np.float32)
+        N, T = w.shape[0], x.shape[0]
+        y = np.zeros((T, N), np.float32)
+        if add is not None:
+            add = np.ascontiguousarray(add, np.float32)
+            flags |= MM_ADD
+            if add_stride is None:
+                add_stride = N if add.ndim == 2 and add.shape[0] > 1 else 0
+        rc = self.lib.tsro_matvec(fmt, _ptr(w), N, K, _ptr(x), T, _ptr(add), add_stride or 0, flags, s0, s1,
+                                  _ptr(y), threads or os.cpu_count() or 1)
+        if rc != 0:
+            raise ValueError("tsro_matvec refused the arguments")
+        return y
+
+    def fa(self, q, k_rows, v_rows, *, D, n_head, n_head_kv, n_kv, scale, mask=None, C=4, t_max=4, pcap=9344,
+           new=(0, 0)):
+        """q [T, n_head, D] f32; k_rows / v_rows [kv_size, E/32*34] uint8; mask f16 [T, >= n_kv] or None."""
+        q = np.ascontiguousarray(q, np.float32)
+        T = q.shape[0]
+        p = FaParams(C, t_max, pcap, T, D, n_head, n_head_kv, n_kv, scale, new[0], new[1])
+        out = np.zeros((T, n_head, D), np.float32)
+        mk = None if mask is None else np.ascontiguousarray(mask, np.float16).view(np.uint16)
+        rc = self.lib.tsro_fa(ct.byref(p), _ptr(q), _ptr(np.ascontiguousarray(k_rows)),
+                              _ptr(np.ascontiguousarray(v_rows)), _ptr(mk), 0 if mk is None else mk.shape[1],
+                              _ptr(out))
+        return rc, out
+
+    def fa_qk_isums(self, q, k_rows, *, D, n_head, n_head_kv, n_kv):
+        q = np.ascontiguousarray(q, np.float32)
+        p = FaParams(4, 4, 9344, 1, D, n_head, n_head_kv, n_kv, 1.0, 0, 0)
+        out = np.zeros((n_head, n_kv, D // 32), np.int32)
+        self.lib.tsro_fa_qk_isums(ct.byref(p), _ptr(q), _ptr(np.ascontiguousarray(k_rows)), _ptr(out))
+        return out
+
+    def quantize(self, fmt: int, x):
+        """f32 rows [N, K] -> ggml blocks [N, row_bytes] uint8."""
+        x = np.ascontiguousarray(np.atleast_2d(x), np.float32)
+        N, K = x.shape
+        rb = K // 32 * 34 if fmt == FMT_Q8_0 else K // 256 * 144
+        out = np.zeros((N, rb), np.uint8)
+        f = self.lib.tsro_quantize_q8_0 if fmt == FMT_Q8_0 else self.lib.tsro_quantize_q4_K
+        for n in range(N):
+            f(_ptr(x[n]), K, _ptr(out[n]))
+        return out
+
+
+class Ref:
+    """The reference's own library (oracle/_ref/libtsr_refdrv.so), when it was built."""
+
+    @staticmethod
+    def available(path: str = REF_PATH) -> bool:
+        return os.path.exists(path)
+
+    def __init__(self, path: str = REF_PATH):
+        L = self.lib = ct.CDLL(path)
+        L.refdrv_expk_n.argtypes = [_p, _sz, ct.c_uint, _p]
+        L.refdrv_tanh_n.argtypes = [_p, _sz, _p]
+        L.refdrv_fp_n.argtypes = [ct.c_int, _p, _p, _sz, _p]
+        L.refdrv_f32_to_fp16_n.argtypes = [_p, _sz, _p]
+        L.refdrv_qact.argtypes = [_u32, _p, _u32, _p, _p, _p]
+        L.refdrv_row_bytes.restype = _sz
+        L.refdrv_row_bytes.argtypes = [_u32, _u32]
+        L.refdrv_repack.argtypes = [_u32, _p, _u32, _u32, _p]
+        L.refdrv_matvec_repacked.restype = ct.c_int
+        L.refdrv_matvec_repacked.argtypes = [_u32, _p, _u32, _u32, _p, _u32, _p, _u32, _u32, _f32, _f32, _p, ct.c_int]
+        L.refdrv_fa_prepare.restype = _p
+        L.refdrv_fa_prepare.argtypes = [_u32] * 9 + [_f32, _p, _p, _p, _sz, _u32, _u32]
+        L.refdrv_fa_run.restype = ct.c_int
+        L.refdrv_fa_run.argtypes = [_p, _p, _p]
+        L.refdrv_fa_free.argtypes = [_p]
+
+    def expk(self, v, kappa=0):
+        v = np.ascontiguousarray(v, np.float32).ravel()
+        out = np.empty_like(v)
+        self.lib.refdrv_expk_n(_ptr(v), v.size, kappa, _ptr(out))
+        return out
+
+    def tanh(self, v):
+        v = np.ascontiguousarray(v, np.float32).ravel()
+        out = np.empty_like(v)
+        self.lib.refdrv_tanh_n(_ptr(v), v.size, _ptr(out))
+        return out
+
+    def fp(self, op: str, a, b=None):
+        ops = {"fadd": 0, "fsub": 1, "fmul": 2, "fdiv": 3, "frecip": 4}
+        a = np.ascontiguousarray(a, np.float32).ravel()
+        b = a if b is None else np.ascontiguousarray(b, np.float32).ravel()
+        out = np.empty_like(a)
+        self.lib.refdrv_fp_n(ops[op], _ptr(a), _ptr(b), a.size, _ptr(out))
+        return out
+
+    def f32_to_fp16(self, a):
+        a = np.ascontiguousarray(a, np.float32).ravel()
+        out = np.empty(a.size, np.uint16)
+        self.lib.refdrv_f32_to_fp16_n(_ptr(a), a.size, _ptr(out))
+        return out
+
+    def qact(self, fmt: int, x):
+        x = np.ascontiguousarray(np.atleast_2d(x), np.float32)
+        T, K = x.shape
+        bsz = 32 if fmt == FMT_Q8_0 else 256
+        q = np.zeros((T, K), np.int8)
+        d = np.zeros((T, K // bsz), np.float32)
+        bs = np.zeros((T, K // 16), np.int16) if fmt == FMT_Q4_K else None
+        for t in range(T):
+            self.lib.refdrv_qact(fmt, _ptr(x[t]), K, _ptr(q[t]), _ptr(d[t]), _ptr(bs[t]) if bs is not None else None)
+        return q, d, bs
+
+    def repack(self, fmt: int, w, K: int):
+        w = np.ascontiguousarray(w, np.uint8)
+        rb = self.lib.refdrv_row_bytes(fmt, K)
+        out = np.zeros((w.shape[0], rb), np.uint8)
+        self.lib.refdrv_repack(fmt, _ptr(w), w.shape[0], K, _ptr(out))
+        return out
+
+    def matvec_repacked(self, fmt: int, rows, K: int, x, add=None, add_stride=None, flags: int = 0, s0=1.0, s1=1.0,
+                        threads: int | None = None, out=None):
+        x = np.ascontiguousarray(np.atleast_2d(x), np.float32)
+        N, T = rows.shape[0], x.shape[0]
+        y = out if out is not None else np.zeros((T, N), np.float32)
+        if add is not None:
+            add = np.ascontiguousarray(add, np.float32)
+            flags |= MM_ADD
+            if add_stride is None:
+                add_stride = N if add.ndim == 2 and add.shape[0] > 1 else 0
+        rc = self.lib.refdrv_matvec_repacked(fmt, _ptr(rows), N, K, _ptr(x), T, _ptr(add), add_stride or 0, flags,
+                                             s0, s1, _ptr(y), threads or os.cpu_count() or 1)
+        if rc != 0:
+            raise RuntimeError("refdrv_matvec_repacked failed")
+        return y
+
+    def matvec(self, fmt: int, w, K: int, x, **kw):
+        return self.matvec_repacked(fmt, self.repack(fmt, w, K), K, x, **kw)
+
+    def fa_prepare(self, k_rows, v_rows, *, T, D, n_head, n_head_kv, n_kv, scale, mask=None, C=4, t_max=4,
+                   pcap=9344, new=(0, 0)):
+        k_rows = np.ascontiguousarray(k_rows, np.uint8)
+        v_rows = np.ascontiguousarray(v_rows, np.uint8)
+        mk = None if mask is None else np.ascontiguousarray(mask, np.float16).view(np.uint16)
+        h = self.lib.refdrv_fa_prepare(C, t_max, pcap, T, D, n_head, n_head_kv, n_kv, k_rows.shape[0], scale,
+                                       _ptr(k_rows), _ptr(v_rows), _ptr(mk), 0 if mk is None else mk.shape[1],
+                                       new[0], new[1])
+        return h
+
+    def fa_run(self, h, q):
+        q = np.ascontiguousarray(q, np.float32)
+        out = np.zeros_like(q)
+        rc = self.lib.refdrv_fa_run(h, _ptr(q), _ptr(out))
+        return rc, out
+
+    def fa_free(self, h):
+        self.lib.refdrv_fa_free(h)
+
+    def fa(self, q, k_rows, v_rows, **kw):
+        q = np.ascontiguousarray(q, np.float32)
+        h = self.fa_prepare(k_rows, v_rows, T=q.shape[0], **kw)
+        try:
+            return self.fa_run(h, q)
+        finally:
+            self.fa_free(h)
