@@ -1,0 +1,379 @@
+"""Bench of the B200 hot path: decode MUL_MAT (QACT + Q4_K / Q8_0 matvec) through the C ABI.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config cfg2|cfg1]
+
+Metric: matvec HBM GB/s. The N = 1 workload is BASELINE config 2 (Q4_K
+14336 x 4096, one token); config 1 (Q8_0 4864 x 896) with --config cfg1. A step is one MUL_MAT of
+one token over one weight matrix: QACT of the f32 activation, then the matvec; on N > 1 GPUs each
+rank holds a contiguous row shard (the reference's symmetric row split) and the step ends with an
+NCCL all-gather of y. Algorithmic bytes per step: N*(K/256)*144 (or N*(K/32)*34) + 4K + 4N.
+
+  value      K steps with x resident in HBM, inputs larger than L2 (each step reads the next of a
+             ring of distinct weight copies, >= 4x L2 per GPU); CUDA graph replay on one GPU.
+  roofline   the matvec kernel alone (tsrc_mvm), CUDA events on its stream, same weight ring.
+  e2e        tsrc_mul_mat with the activation copied in from pinned host memory and y read back
+             to pinned host memory every step.
+  cpu_baseline  the reference's own CPU path (tsr_qact + tsr_dot_row, oracle/_ref) on the host's
+             cores for ~10 s, rank 0 at N = 1 only.
+--impl reference times that CPU path alone (rank 0; other ranks exit) on a bounded row sample.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "tesseract-npu_b200"))
+
+CONFIGS = {
+    # name: (fmt, N, K, weight seed, x seed, description)
+    "cfg2": (1, 14336, 4096, 201, 202, "BASELINE config 2: Q4_K matvec 14336x4096, one token (decode)"),
+    "cfg1": (0, 4864, 896, 101, 102, "BASELINE config 1: Q8_0 matvec 4864x896, one token (decode)"),
+}
+METRIC = "Q8_0/Q4_K matvec HBM GB/s"
+
+
+def row_bytes(fmt, K):
+    return K // 256 * 144 if fmt == 1 else K // 32 * 34
+
+
+def algo_bytes(fmt, N, K):
+    return N * row_bytes(fmt, K) + 4 * K + 4 * N
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+class Clocks:
+    """nvidia-smi samples (SM clock, max, throttle reasons) while the timed loops run."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, dev_index):
+        self.proc = None
+        self.dev_index = dev_index
+
+    def __enter__(self):
+        import torch
+        uuid = None
+        try:
+            uuid = "GPU-" + str(torch.cuda.get_device_properties(self.dev_index).uuid)
+        except Exception:
+            pass
+        cmd = ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "100"]
+        if uuid:
+            cmd[1:1] = ["-i", uuid]
+        try:
+            self.proc = subprocess.Popen(cmd, stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except FileNotFoundError:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        self.out = ""
+        if self.proc:
+            time.sleep(0.2)
+            self.proc.terminate()
+            try:
+                self.out, _ = self.proc.communicate(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        rows = []
+        for line in (self.out or "").strip().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 8:
+                continue
+            try:
+                rows.append((float(f[0]), float(f[1]), f[4:8]))
+            except ValueError:
+                continue
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no nvidia-smi samples"], "samples": 0}
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for _, _, r in rows for i, v in enumerate(r) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(r[0] for r in rows), "sm_max_mhz": max(r[1] for r in rows),
+                "reasons": reasons, "samples": len(rows)}
+
+
+def cpu_reference_matvec(fmt, N, K, x, seconds, threads):
+    """The reference's CPU path (oracle/_ref, else the oracle port) on rows of config-like weights.
+    Returns (GB/s, kind, sample description)."""
+    import numpy as np
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    import oracle
+    import helpers as H
+    tsro = oracle.Tsro()
+    rows = min(N, 2048)                       # weight rows generated on the host; cycled to N
+    w = H.weights(tsro, fmt, rows, K, 999)
+    if oracle.Ref.available():
+        ref = oracle.Ref()
+        packed = ref.repack(fmt, w, K)
+        tile = np.ascontiguousarray(np.tile(packed, (math.ceil(N / rows), 1))[:N])
+        y = np.zeros((1, N), np.float32)
+        run = lambda: ref.matvec_repacked(fmt, tile, K, x, threads=threads, out=y)  # noqa: E731
+        kind = "reference"
+    else:
+        tile = np.ascontiguousarray(np.tile(w, (math.ceil(N / rows), 1))[:N])
+        run = lambda: tsro.matvec(fmt, tile, K, x, threads=threads)  # noqa: E731
+        kind = "port"
+    run()
+    n, t0 = 0, time.perf_counter()
+    while True:
+        run()
+        n += 1
+        el = time.perf_counter() - t0
+        if el >= seconds:
+            break
+    gbs = n * algo_bytes(fmt, N, K) / el / 1e9
+    return gbs, kind, f"{n} full {N}x{K} matvecs in {el:.1f} s ({threads} threads)", el / n
+
+
+def run_reference(args, cfg):
+    """--impl reference: the reference's own CPU implementation of the path, rank 0 only."""
+    import numpy as np
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    fmt, N, K, ws, xs, desc = cfg
+    threads = len(os.sched_getaffinity(0))
+    x = np.random.default_rng(xs).standard_normal((1, K), dtype=np.float32)
+    # calibrate one full matvec, then size each step's row sample so the run ends in ~2 minutes
+    _, kind, _, t_full = cpu_reference_matvec(fmt, N, K, x, 0.5, threads)
+    steps_total = args.steps + args.warmup
+    budget = 120.0 / max(1, steps_total)
+    S = int(min(N, max(16 * threads, N * budget / t_full)))
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    import oracle
+    import helpers as H
+    tsro = oracle.Tsro()
+    w = H.weights(tsro, fmt, min(S, 2048), K, 999)
+    w = np.ascontiguousarray(np.tile(w, (math.ceil(S / w.shape[0]), 1))[:S])
+    if kind == "reference":
+        ref = oracle.Ref()
+        rows = ref.repack(fmt, w, K)
+        y = np.zeros((1, S), np.float32)
+        step = lambda: ref.matvec_repacked(fmt, rows, K, x, threads=threads, out=y)  # noqa: E731
+    else:
+        step = lambda: tsro.matvec(fmt, w, K, x, threads=threads)  # noqa: E731
+    for _ in range(args.warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    el = time.perf_counter() - t0
+    bytes_step = algo_bytes(fmt, S, K)
+    v = args.steps * bytes_step / el / 1e9
+    sample = f"rows [0, {S}) of {N} per step ({threads} host threads)"
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(v, 3), "unit": "GB/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(el / args.steps * 1e3, 4),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int8",
+        "data": "synthetic (seeded N(0,0.02) weights, N(0,1) activation)",
+        "config": {"workload": desc, "row_sample": S, "host_threads": threads},
+        "cpu_baseline": {"value": round(v, 3), "unit": "GB/s", "cores": threads, "kind": kind, "sample": sample},
+        "e2e": {"value": round(v, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50000)
+    ap.add_argument("--warmup", type=int, default=200)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--config", default="cfg2", choices=list(CONFIGS))
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--no-graph", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(3, args.warmup)
+    cfg = CONFIGS[args.config]
+    if args.impl == "reference":
+        return run_reference(args, cfg)
+
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    import tsrc
+
+    fmt, N, K, ws, xs, desc = cfg
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+    dev = tsrc.Device(local)
+    stream = torch.cuda.current_stream()
+
+    # row shard of this rank (symmetric split R = ceil(N / world), sw/sim/tsr_ref.c:335-357)
+    R = (N + world - 1) // world
+    row0, n_rows = rank * R, max(0, min(R, N - rank * R))
+    shard_bytes = n_rows * row_bytes(fmt, K)
+    l2 = torch.cuda.get_device_properties(local).L2_cache_size
+    n_copies = max(2, math.ceil(4 * l2 / max(1, shard_bytes)))
+    weights = [dev.synth(fmt, N, K, seed=ws + 1000 * c, row0=row0, n_rows=n_rows) for c in range(n_copies)]
+    torch.cuda.synchronize()
+
+    x = torch.from_numpy(np.random.default_rng(xs).standard_normal(K, dtype=np.float32)).cuda()
+    y_loc = torch.zeros(n_rows, device="cuda")
+    y_full = torch.zeros(R * world, device="cuda")
+    qa_q = torch.zeros(K, dtype=torch.int8, device="cuda")
+    qa_d = torch.zeros(K // (256 if fmt == 1 else 32), device="cuda")
+    qa_bs = torch.zeros(K // 16, dtype=torch.int16, device="cuda")
+
+    def step(i):
+        dev.mul_mat(weights[i % n_copies], x, y_loc, T=1)
+        if world > 1:
+            dist.all_gather_into_tensor(y_full, torch.nn.functional.pad(y_loc, (0, R - n_rows)))
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(v):
+        if world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def timed(fn, n):
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        fn(n)
+        e1.record(stream)
+        barrier()
+        return max_over_ranks(e0.elapsed_time(e1))
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+
+    use_graph = world == 1 and not args.no_graph
+    graph = None
+    if use_graph:
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            for i in range(n_copies):
+                step(i)
+        graph = g
+        graph.replay()
+        torch.cuda.synchronize()
+
+    def value_loop(n):
+        if graph is not None:
+            reps, rem = divmod(n, n_copies)
+            for _ in range(reps):
+                graph.replay()
+            for i in range(rem):
+                step(i)
+        else:
+            for i in range(n):
+                step(i)
+
+    # kernel-only loop: QACT once, then the matvec kernel over the ring of copies
+    dev.qact(tsrc.QA_A256 if fmt == 1 else tsrc.QA_A32, x, K, 1, qa_q, qa_d, qa_bs if fmt == 1 else None)
+    n_kernel = min(args.steps, 20000)
+
+    def kernel_loop(n):
+        for i in range(n):
+            dev.mvm(weights[i % n_copies], qa_q, qa_d, qa_bs if fmt == 1 else None, y_loc)
+
+    # e2e: pinned host activation in, y out, through the public MUL_MAT call
+    x_host = torch.from_numpy(np.random.default_rng(xs).standard_normal(K, dtype=np.float32)).pin_memory()
+    y_host = torch.zeros(R * world if world > 1 else n_rows).pin_memory()
+    n_e2e = min(args.steps, 20000)
+
+    def e2e_loop(n):
+        for i in range(n):
+            x.copy_(x_host, non_blocking=True)
+            step(i)
+            y_host.copy_(y_full if world > 1 else y_loc, non_blocking=True)
+
+    kernel_loop(50)
+    e2e_loop(10)
+    torch.cuda.synchronize()
+    with Clocks(local) as clk:
+        ms_value = timed(value_loop, args.steps)
+        ms_kernel = timed(kernel_loop, n_kernel)
+        ms_e2e = timed(e2e_loop, n_e2e)
+    clocks = clk.summary()
+
+    total_bytes = algo_bytes(fmt, N, K)
+    shard_algo = n_rows * row_bytes(fmt, K) + 4 * K + 4 * n_rows
+    value = args.steps * total_bytes / (ms_value * 1e-3) / 1e9
+    e2e = n_e2e * total_bytes / (ms_e2e * 1e-3) / 1e9
+    kern_us = ms_kernel * 1e3 / n_kernel
+    achieved = shard_algo / (kern_us * 1e-6) / 1e9
+    peak, peak_kind = peaks()
+
+    cpu = None
+    if rank == 0 and world == 1 and args.cpu_seconds > 0:
+        xn = x.cpu().numpy().reshape(1, K)
+        threads = len(os.sched_getaffinity(0))
+        gbs, kind, sample, _ = cpu_reference_matvec(fmt, N, K, xn, args.cpu_seconds, threads)
+        cpu = {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": kind, "sample": sample}
+
+    traffic = None
+    prof = os.path.join(ROOT, "profiles", f"traffic_{args.config}.json")
+    if os.path.exists(prof):
+        with open(prof) as f:
+            traffic = json.load(f).get("dram_bytes_per_launch")
+
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms_value / args.steps, 6), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "int8",
+        "data": "synthetic (seeded N(0,0.02) weights quantized on device, N(0,1) activation)",
+        "config": {"workload": desc, "rows_per_gpu": n_rows, "parallelism": f"row-split tp{world}" if world > 1 else "single",
+                   "l2": f"inputs larger than L2: ring of {n_copies} weight copies, {n_copies * shard_bytes / 1e6:.0f} MB per GPU",
+                   "cuda_graph": use_graph, "collective": "NCCL all_gather of y" if world > 1 else None},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "traffic": traffic, "peak_kind": peak_kind,
+                     "kernel": "mv_q4_K_kernel" if fmt == 1 else "mv_q8_0_kernel", "us_per_launch": round(kern_us, 3),
+                     "algorithmic_bytes_per_launch": shard_algo},
+        "e2e": {"value": round(e2e, 2), "unit": "GB/s", "h2d_bytes_per_step": 4 * K,
+                "d2h_bytes_per_step": 4 * (R * world if world > 1 else n_rows),
+                "ms_per_step": round(ms_e2e / n_e2e, 6)},
+        "gpu_launches": 2 * args.steps,
+        "clocks": clocks,
+        "cpu_baseline": cpu,
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    del graph
+    for w in weights:
+        w.free()
+    dev.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

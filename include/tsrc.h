@@ -1,0 +1,135 @@
+// tsrc.h -- C ABI of the B200 (sm_100a) hot path of the Tesseract stack: Q8_0 / Q4_K matrix-vector
+// products (MUL_MAT) and flash attention over a q8_0 KV cache (FLASH_ATTN_EXT, SET_ROWS).
+//
+// This is the seam a ggml backend adapter (the rewrite of jwkim04/tesseract-npu
+// sw/ggml-tesseract/ggml-tesseract.cpp) calls in place of the reference's op-list lowering,
+// transport and firmware: the adapter keeps the ggml backend interface llama.cpp reaches through
+// -ngl (registration, buffer types, supports_op, graph_compute) and calls these functions from
+// set_tensor / graph_compute. Plain C types only: pointers, sizes and an opaque CUDA stream
+// (cudaStream_t passed as void *; NULL = the legacy default stream).
+//
+// Numerics: every result is the reference's bit for bit (the spec's f32 rules: DAZ inputs, RNE,
+// flush of subnormal results, canonical NaN 0x7FC00000; QACT A32 / A256; the 16-partial row dot of
+// sw/sim/tsr_ref.c:592-635), for any input bytes.
+//
+// Errors: every function returns TSRC_OK (0) or a negative TSRC_E_* code and then sets a message
+// that tsrc_last_error() returns (per thread). Nothing aborts and no C++ exception crosses the ABI.
+// Kernels are queued on the given stream; functions that take host buffers synchronise as noted.
+// Threading: a context may be used from one thread at a time (the reference serialises every call
+// with one device mutex, ggml-tesseract.cpp:3932).
+#pragma once
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define TSRC_API __attribute__((visibility("default")))
+#else
+#define TSRC_API
+#endif
+
+#define TSRC_OK             0
+#define TSRC_E_ARG         (-1)   // a NULL handle / pointer, or a value out of range
+#define TSRC_E_SHAPE       (-2)   // a shape the path does not support (the supports_op refusals)
+#define TSRC_E_CUDA        (-3)   // a CUDA runtime error (message carries cudaGetErrorString)
+#define TSRC_E_NOMEM       (-4)   // device or host allocation failed
+#define TSRC_E_NODEV       (-5)   // no usable sm_100 device
+
+#define TSRC_FMT_Q8_0  0u         // ggml block_q8_0: {fp16 d; int8 qs[32]}, 34 B per 32 weights
+#define TSRC_FMT_Q4_K  1u         // ggml block_q4_K: {fp16 d, dmin; u8 scales[12]; u8 qs[128]}, 144 B per 256
+
+#define TSRC_QA_A32    0u         // QACT kind of Q8_0 (block 32, round half away, d = fp16(amax/127))
+#define TSRC_QA_A256   1u         // QACT kind of Q4_K (block 256, round half even, int16 sums of 16)
+
+// tsrc_mul_mat flags (the MVM epilogues, sw/sim/tsr_sim.c:1648-1670; MUL_MAT + ADD fusion,
+// ggml-tesseract.cpp:2897-2914)
+#define TSRC_MM_ADD     0x1u      // y = fadd(add[t * add_stride + n], dot)
+#define TSRC_MM_SCALE   0x2u      // y = fmul(dot, s1)
+#define TSRC_MM_SOFTCAP 0x4u      // y = fmul(tanh(fmul(dot, s0)), s1)
+
+typedef struct tsrc_ctx tsrc_ctx;
+typedef struct tsrc_weight tsrc_weight;
+
+// Last error message of the calling thread ("" if none). Replaces the reference's GGML_ABORT text
+// (ggml-tesseract.cpp:2260-2271) as a returned status.
+TSRC_API const char * tsrc_last_error(void);
+
+// Library version string ("tsrc <major>.<minor> sm_100a").
+TSRC_API const char * tsrc_version(void);
+
+// Opens CUDA device `device` (must be sm_100). Replaces tsr_dev_open_locked (ggml-tesseract.cpp:463)
+// and the backend init (tsr_dev_init_backend, :4079).
+TSRC_API int tsrc_open(int device, tsrc_ctx ** out);
+// Releases the context and every weight still attached to it (tsr_backend_free, :3799).
+TSRC_API int tsrc_close(tsrc_ctx * ctx);
+
+// ---- weights (the WEIGHTS buffer's set_tensor / get_tensor, ggml-tesseract.cpp:1905, :1947) -----
+
+// Uploads rows [row0, row0 + n_rows) of an N x K ggml weight (rows packed: K/32*34 or K/256*144
+// bytes each, host memory at ggml_rows, which holds exactly those rows) and repacks them on the
+// device into this library's layout. row0 / n_rows give a row shard for tensor parallelism (the
+// reference's symmetric row split, sw/sim/tsr_ref.c:335-357); pass 0 / N for the whole tensor.
+// Synchronous. Replaces tsr_store_weight_rows / tsr_repack_row (ggml-tesseract.cpp:852,
+// sw/sim/tsr_ref.c:296-314).
+TSRC_API int tsrc_weight_upload(tsrc_ctx * ctx, uint32_t fmt, const void * ggml_rows, uint32_t N, uint32_t K,
+                       uint32_t row0, uint32_t n_rows, tsrc_weight ** out);
+// The same from ggml rows already in device memory (e.g. a staging buffer); queued on `stream`.
+TSRC_API int tsrc_weight_upload_device(tsrc_ctx * ctx, uint32_t fmt, const void * ggml_rows_dev, uint32_t N, uint32_t K,
+                              uint32_t row0, uint32_t n_rows, void * stream, tsrc_weight ** out);
+// Seeded synthetic weight generated on the device (counter-based Philox4x32-10 normal values of
+// standard deviation sigma, quantized to fmt on the device); rows [row0, row0+n_rows) of an N x K
+// tensor, identical to the same rows of an unsharded generation. For benches and tests.
+TSRC_API int tsrc_weight_synth(tsrc_ctx * ctx, uint32_t fmt, uint32_t N, uint32_t K, uint32_t row0, uint32_t n_rows,
+                      uint64_t seed, float sigma, void * stream, tsrc_weight ** out);
+// Reads the shard back as ggml rows (n_rows rows) into host memory (get_tensor; the inverse repack,
+// tsr_unrepack_row, sw/sim/tsr_ref.c:316-333). Synchronous.
+TSRC_API int tsrc_weight_download(const tsrc_weight * w, void * ggml_rows);
+// fmt, N, K, row0, n_rows and the device bytes the shard occupies (any pointer may be NULL).
+TSRC_API int tsrc_weight_info(const tsrc_weight * w, uint32_t * fmt, uint32_t * N, uint32_t * K, uint32_t * row0,
+                     uint32_t * n_rows, uint64_t * device_bytes);
+TSRC_API int tsrc_weight_free(tsrc_weight * w);
+
+// ---- MUL_MAT (tsr_lower_mul_mat, ggml-tesseract.cpp:2790-2928; kind_mulmat, sw/ctrl/kernels/k_mulmat.cpp) ----
+
+// For t < T: y[t * y_stride + n] = epilogue(dot(W row n, QACT(x[t * x_stride .. + K]))) for the
+// shard's rows n < n_rows (y row t holds the shard's outputs only). Strides are in floats (0 =
+// dense: K for x, n_rows for y, n_rows for add, or 0 = row 0 for every token when add_stride is
+// 0). x, y, add are device pointers; y must not overlap x or add. s0 / s1: TSRC_MM_SOFTCAP /
+// TSRC_MM_SCALE factors. ADD cannot be combined with SCALE or SOFTCAP (the reference refuses it,
+// tsr_sim.c chk_mvm). Queued on `stream`; no host synchronisation.
+TSRC_API int tsrc_mul_mat(tsrc_ctx * ctx, const tsrc_weight * w, const float * x, uint32_t T, uint32_t x_stride, float * y,
+                 uint32_t y_stride, const float * add, uint32_t add_stride, uint32_t flags, float s0, float s1,
+                 void * stream);
+
+// The MVM tile op alone (ex_mvm, sw/sim/tsr_sim.c:1623-1671): tsrc_mul_mat on activations already
+// quantized by tsrc_qact (q [T][K], d [T][K/bs], bs [T][K/16] for Q4_K, dense), same epilogues
+// and strides. T <= 8 per call. Device pointers, queued on `stream`.
+TSRC_API int tsrc_mvm(tsrc_ctx * ctx, const tsrc_weight * w, const int8_t * q, const float * d, const int16_t * bs,
+                      uint32_t T, float * y, uint32_t y_stride, const float * add, uint32_t add_stride, uint32_t flags,
+                      float s0, float s1, void * stream);
+
+// Why a MUL_MAT of this weight shape could not run here (NULL if it can): the B200 counterpart of
+// the MUL_MAT branch of supports_op (ggml-tesseract.cpp:4199-4299).
+TSRC_API const char * tsrc_mul_mat_unsupported(uint32_t fmt, uint64_t N, uint64_t K, uint64_t T);
+
+// ---- test hooks (the reference exposes the same through get_proc_address, ggml-tesseract.cpp:4409-4431) ----
+
+// QACT alone (tsr_qact, sw/sim/tsr_ref.c:456-518): T vectors of K floats (x_stride floats apart, 0
+// = K) -> q [T][K] int8, d [T][K/bs] f32, bs [T][K/16] int16 (A256 only; NULL for A32). Device
+// pointers, queued on `stream`.
+TSRC_API int tsrc_qact(tsrc_ctx * ctx, uint32_t kind, const float * x, uint32_t K, uint32_t T, uint32_t x_stride,
+              int8_t * q, float * d, int16_t * bs, void * stream);
+// MUL_MAT of one token (x: K device floats -> y: n_rows floats) that also writes the kernel's own
+// exact int32 block sums: Q8_0 isum[n][K/32]; Q4_K isum[n][K/256][2] = {sum sc_j*S_j,
+// sum m_j*(BS_2j + BS_2j+1)} (the integer parts of sw/sim/tsr_ref.c:533-567), so that a test can
+// check them bit for bit. Device pointers, queued on `stream`.
+TSRC_API int tsrc_mul_mat_isums(tsrc_ctx * ctx, const tsrc_weight * w, const float * x, float * y, int32_t * isum,
+                       void * stream);
+
+#ifdef __cplusplus
+}
+#endif

@@ -1,0 +1,414 @@
+// tsrc_api.cu -- the C ABI (include/tsrc.h): argument checks, device memory, launches.
+//
+// Host side of the B200 path. It stands where the reference's ggml backend lowered a node into
+// an op-list record and ran it through the transport and the firmware
+// (jwkim04/tesseract-npu sw/ggml-tesseract/ggml-tesseract.cpp:2790-2928 for MUL_MAT); here a
+// call is a queue of kernel launches on the caller's stream. Refusals mirror supports_op
+// (:4199-4299) as TSRC_E_SHAPE with the reason in tsrc_last_error().
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <set>
+#include <string>
+
+#include "../../include/tsrc.h"
+#include "tsrc_internal.h"
+
+namespace {
+
+thread_local std::string g_err;
+
+int fail(int code, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    g_err = buf;
+    return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+    return fail(TSRC_E_CUDA, "%s: %s (%s)", what, cudaGetErrorString(e), cudaGetErrorName(e));
+}
+
+#define TSRC_CUDA(call, what)                      \
+    do {                                           \
+        cudaError_t e_ = (call);                   \
+        if (e_ != cudaSuccess) return cuda_fail(e_, what); \
+    } while (0)
+
+constexpr uint32_t kKMax = 131072;            // shared-memory bound of one token's QA image
+constexpr size_t kSmemBudget = 200u * 1024u;  // dynamic shared memory one matvec CTA may use
+
+uint32_t block_of(uint32_t fmt) { return fmt == TSRC_FMT_Q8_0 ? 32u : 256u; }
+size_t ggml_row_bytes(uint32_t fmt, uint32_t K) {
+    return fmt == TSRC_FMT_Q8_0 ? (size_t)(K / 32u) * 34u : (size_t)(K / 256u) * 144u;
+}
+size_t qs_row_bytes(uint32_t fmt, uint32_t K) { return fmt == TSRC_FMT_Q8_0 ? K : K / 2u; }
+size_t meta_row_bytes(uint32_t fmt, uint32_t K) { return fmt == TSRC_FMT_Q8_0 ? (size_t)(K / 32u) * 2u : (size_t)(K / 256u) * 16u; }
+size_t align256(size_t n) { return (n + 255u) & ~(size_t)255u; }
+
+// s0 / s1 enter the f32 rules as inputs: DAZ them once on the host.
+float daz_host(float v) {
+    uint32_t u;
+    std::memcpy(&u, &v, 4);
+    if ((u & 0x7F800000u) == 0) u &= 0x80000000u;
+    float r;
+    std::memcpy(&r, &u, 4);
+    return r;
+}
+
+// Bytes of the QA image of T tokens (q | d | bs, each 256-byte aligned).
+size_t qa_bytes(uint32_t fmt, uint32_t K, uint32_t T) {
+    return align256((size_t)T * K) + align256((size_t)T * (K / block_of(fmt)) * 4u) + align256((size_t)T * (K / 16u) * 2u);
+}
+
+}  // namespace
+
+struct tsrc_weight {
+    tsrc_ctx* ctx;
+    uint32_t fmt, N, K, row0, n_rows;
+    uint8_t* qs;
+    uint8_t* meta;
+    size_t bytes;
+};
+
+struct tsrc_ctx {
+    int device;
+    cudaDeviceProp prop;
+    uint8_t* scratch = nullptr;   // QA images of the tokens of one call
+    size_t scratch_bytes = 0;
+    std::set<tsrc_weight*> weights;
+};
+
+namespace {
+
+int use_device(const tsrc_ctx* ctx) {
+    int cur = -1;
+    TSRC_CUDA(cudaGetDevice(&cur), "cudaGetDevice");
+    if (cur != ctx->device) TSRC_CUDA(cudaSetDevice(ctx->device), "cudaSetDevice");
+    return TSRC_OK;
+}
+
+int ensure_scratch(tsrc_ctx* ctx, size_t bytes) {
+    if (bytes <= ctx->scratch_bytes) return TSRC_OK;
+    if (ctx->scratch) {
+        // the previous buffer may still be read by queued kernels
+        TSRC_CUDA(cudaDeviceSynchronize(), "cudaDeviceSynchronize");
+        cudaFree(ctx->scratch);
+        ctx->scratch = nullptr;
+        ctx->scratch_bytes = 0;
+    }
+    const size_t want = bytes < (1u << 20) ? (1u << 20) : bytes;
+    cudaError_t e = cudaMalloc(&ctx->scratch, want);
+    if (e != cudaSuccess) return fail(TSRC_E_NOMEM, "cudaMalloc of %zu scratch bytes: %s", want, cudaGetErrorString(e));
+    ctx->scratch_bytes = want;
+    return TSRC_OK;
+}
+
+const char* shape_reason(uint32_t fmt, uint64_t N, uint64_t K, uint64_t T) {
+    if (fmt != TSRC_FMT_Q8_0 && fmt != TSRC_FMT_Q4_K) return "MUL_MAT: the weight type has no device format (Q8_0 and Q4_K only)";
+    if (K == 0 || K % block_of(fmt) != 0) return "MUL_MAT: K is not a positive multiple of the block size (32 Q8_0, 256 Q4_K)";
+    if (K > kKMax) return "MUL_MAT: K exceeds 131072 (one token's quantized activation must fit shared memory)";
+    if (N == 0 || N > 0xFFFFFFFFull) return "MUL_MAT: N is 0 or does not fit 32 bits";
+    if (T > 0xFFFFFFFFull) return "MUL_MAT: too many tokens";
+    return nullptr;
+}
+
+int new_weight(tsrc_ctx* ctx, uint32_t fmt, uint32_t N, uint32_t K, uint32_t row0, uint32_t n_rows, tsrc_weight** out) {
+    if (!ctx || !out) return fail(TSRC_E_ARG, "NULL context or output handle");
+    if (const char* why = shape_reason(fmt, N, K, 1)) return fail(TSRC_E_SHAPE, "%s", why);
+    if (n_rows == 0 || (uint64_t)row0 + n_rows > N) return fail(TSRC_E_ARG, "row shard [%u, %u+%u) outside [0, %u)", row0, row0, n_rows, N);
+    int rc = use_device(ctx);
+    if (rc) return rc;
+    const size_t qb = align256(qs_row_bytes(fmt, K) * n_rows), mb = align256(meta_row_bytes(fmt, K) * n_rows);
+    uint8_t* mem = nullptr;
+    cudaError_t e = cudaMalloc(&mem, qb + mb);
+    if (e != cudaSuccess) return fail(TSRC_E_NOMEM, "cudaMalloc of %zu weight bytes: %s", qb + mb, cudaGetErrorString(e));
+    tsrc_weight* w = new tsrc_weight{ctx, fmt, N, K, row0, n_rows, mem, mem + qb, qb + mb};
+    ctx->weights.insert(w);
+    *out = w;
+    return TSRC_OK;
+}
+
+void drop_weight(tsrc_weight* w) {
+    if (!w) return;
+    cudaFree(w->qs);
+    w->ctx->weights.erase(w);
+    delete w;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* tsrc_last_error(void) { return g_err.c_str(); }
+
+const char* tsrc_version(void) { return "tsrc 0.1 sm_100a"; }
+
+int tsrc_open(int device, tsrc_ctx** out) {
+    if (!out) return fail(TSRC_E_ARG, "tsrc_open: NULL output handle");
+    *out = nullptr;
+    int n = 0;
+    cudaError_t e = cudaGetDeviceCount(&n);
+    if (e != cudaSuccess || n == 0) return fail(TSRC_E_NODEV, "no CUDA device (%s)", cudaGetErrorString(e));
+    if (device < 0 || device >= n) return fail(TSRC_E_NODEV, "device %d not in [0, %d)", device, n);
+    tsrc_ctx* ctx = new tsrc_ctx();
+    ctx->device = device;
+    e = cudaGetDeviceProperties(&ctx->prop, device);
+    if (e != cudaSuccess) {
+        delete ctx;
+        return cuda_fail(e, "cudaGetDeviceProperties");
+    }
+    if (ctx->prop.major != 10) {
+        const int maj = ctx->prop.major, mnr = ctx->prop.minor;
+        delete ctx;
+        return fail(TSRC_E_NODEV, "device %d is sm_%d%d; this library is built for sm_100a only", device, maj, mnr);
+    }
+    e = cudaSetDevice(device);
+    if (e != cudaSuccess) {
+        delete ctx;
+        return cuda_fail(e, "cudaSetDevice");
+    }
+    *out = ctx;
+    return TSRC_OK;
+}
+
+int tsrc_close(tsrc_ctx* ctx) {
+    if (!ctx) return fail(TSRC_E_ARG, "tsrc_close: NULL context");
+    use_device(ctx);
+    cudaDeviceSynchronize();
+    while (!ctx->weights.empty()) drop_weight(*ctx->weights.begin());
+    if (ctx->scratch) cudaFree(ctx->scratch);
+    delete ctx;
+    return TSRC_OK;
+}
+
+int tsrc_weight_upload_device(tsrc_ctx* ctx, uint32_t fmt, const void* ggml_rows_dev, uint32_t N, uint32_t K, uint32_t row0,
+                              uint32_t n_rows, void* stream, tsrc_weight** out) {
+    if (!ggml_rows_dev) return fail(TSRC_E_ARG, "tsrc_weight_upload_device: NULL rows");
+    if (fmt == TSRC_FMT_Q4_K && (reinterpret_cast<uintptr_t>(ggml_rows_dev) & 15u))
+        return fail(TSRC_E_ARG, "tsrc_weight_upload_device: Q4_K rows must be 16-byte aligned in device memory");
+    tsrc_weight* w = nullptr;
+    int rc = new_weight(ctx, fmt, N, K, row0, n_rows, &w);
+    if (rc) return rc;
+    cudaError_t e = tsrc::launch_repack(fmt, static_cast<const uint8_t*>(ggml_rows_dev), n_rows, K, w->qs, w->meta,
+                                        static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) {
+        drop_weight(w);
+        return cuda_fail(e, "repack launch");
+    }
+    *out = w;
+    return TSRC_OK;
+}
+
+int tsrc_weight_upload(tsrc_ctx* ctx, uint32_t fmt, const void* ggml_rows, uint32_t N, uint32_t K, uint32_t row0,
+                       uint32_t n_rows, tsrc_weight** out) {
+    if (!ctx || !ggml_rows || !out) return fail(TSRC_E_ARG, "tsrc_weight_upload: NULL argument");
+    if (const char* why = shape_reason(fmt, N, K, 1)) return fail(TSRC_E_SHAPE, "%s", why);
+    if (n_rows == 0 || (uint64_t)row0 + n_rows > N) return fail(TSRC_E_ARG, "row shard outside the tensor");
+    int rc = use_device(ctx);
+    if (rc) return rc;
+    tsrc_weight* w = nullptr;
+    rc = new_weight(ctx, fmt, N, K, row0, n_rows, &w);
+    if (rc) return rc;
+    // stage in pieces of at most 256 MiB of ggml rows
+    const size_t rb = ggml_row_bytes(fmt, K);
+    const uint32_t rows_per = (uint32_t)std::max<size_t>(1, (256u << 20) / rb);
+    uint8_t* stage = nullptr;
+    const size_t sb = (size_t)std::min<uint32_t>(rows_per, n_rows) * rb;
+    cudaError_t e = cudaMalloc(&stage, sb);
+    if (e != cudaSuccess) {
+        drop_weight(w);
+        return fail(TSRC_E_NOMEM, "cudaMalloc of %zu staging bytes: %s", sb, cudaGetErrorString(e));
+    }
+    for (uint32_t r = 0; r < n_rows && e == cudaSuccess; r += rows_per) {
+        const uint32_t nr = std::min(rows_per, n_rows - r);
+        e = cudaMemcpy(stage, static_cast<const uint8_t*>(ggml_rows) + (size_t)r * rb, (size_t)nr * rb, cudaMemcpyHostToDevice);
+        if (e == cudaSuccess)
+            e = tsrc::launch_repack(fmt, stage, nr, K, w->qs + qs_row_bytes(fmt, K) * r, w->meta + meta_row_bytes(fmt, K) * r, 0);
+        if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    }
+    cudaFree(stage);
+    if (e != cudaSuccess) {
+        drop_weight(w);
+        return cuda_fail(e, "weight upload");
+    }
+    *out = w;
+    return TSRC_OK;
+}
+
+int tsrc_weight_synth(tsrc_ctx* ctx, uint32_t fmt, uint32_t N, uint32_t K, uint32_t row0, uint32_t n_rows, uint64_t seed,
+                      float sigma, void* stream, tsrc_weight** out) {
+    tsrc_weight* w = nullptr;
+    int rc = new_weight(ctx, fmt, N, K, row0, n_rows, &w);
+    if (rc) return rc;
+    cudaError_t e = tsrc::launch_synth(fmt, K, row0, n_rows, seed, sigma, w->qs, w->meta, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) {
+        drop_weight(w);
+        return cuda_fail(e, "synth launch");
+    }
+    *out = w;
+    return TSRC_OK;
+}
+
+int tsrc_weight_download(const tsrc_weight* w, void* ggml_rows) {
+    if (!w || !ggml_rows) return fail(TSRC_E_ARG, "tsrc_weight_download: NULL argument");
+    int rc = use_device(w->ctx);
+    if (rc) return rc;
+    const size_t bytes = ggml_row_bytes(w->fmt, w->K) * w->n_rows;
+    uint8_t* stage = nullptr;
+    cudaError_t e = cudaMalloc(&stage, bytes);
+    if (e != cudaSuccess) return fail(TSRC_E_NOMEM, "cudaMalloc of %zu staging bytes", bytes);
+    e = tsrc::launch_unrepack(w->fmt, w->qs, w->meta, w->n_rows, w->K, stage, 0);
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    if (e == cudaSuccess) e = cudaMemcpy(ggml_rows, stage, bytes, cudaMemcpyDeviceToHost);
+    cudaFree(stage);
+    if (e != cudaSuccess) return cuda_fail(e, "weight download");
+    return TSRC_OK;
+}
+
+int tsrc_weight_info(const tsrc_weight* w, uint32_t* fmt, uint32_t* N, uint32_t* K, uint32_t* row0, uint32_t* n_rows,
+                     uint64_t* device_bytes) {
+    if (!w) return fail(TSRC_E_ARG, "tsrc_weight_info: NULL weight");
+    if (fmt) *fmt = w->fmt;
+    if (N) *N = w->N;
+    if (K) *K = w->K;
+    if (row0) *row0 = w->row0;
+    if (n_rows) *n_rows = w->n_rows;
+    if (device_bytes) *device_bytes = w->bytes;
+    return TSRC_OK;
+}
+
+int tsrc_weight_free(tsrc_weight* w) {
+    if (!w) return fail(TSRC_E_ARG, "tsrc_weight_free: NULL weight");
+    use_device(w->ctx);
+    cudaDeviceSynchronize();
+    drop_weight(w);
+    return TSRC_OK;
+}
+
+const char* tsrc_mul_mat_unsupported(uint32_t fmt, uint64_t N, uint64_t K, uint64_t T) { return shape_reason(fmt, N, K, T); }
+
+static int mul_mat_impl(tsrc_ctx* ctx, const tsrc_weight* w, const float* x, uint32_t T, uint32_t x_stride, float* y,
+                        uint32_t y_stride, const float* add, uint32_t add_stride, uint32_t flags, float s0, float s1,
+                        int32_t* isum_out, void* stream) {
+    if (!ctx || !w || !x || !y) return fail(TSRC_E_ARG, "tsrc_mul_mat: NULL argument");
+    if (w->ctx != ctx) return fail(TSRC_E_ARG, "tsrc_mul_mat: the weight belongs to another context");
+    if (T == 0) return TSRC_OK;
+    if (flags & ~(TSRC_MM_ADD | TSRC_MM_SCALE | TSRC_MM_SOFTCAP)) return fail(TSRC_E_ARG, "tsrc_mul_mat: undefined flag bits 0x%x", flags);
+    if ((flags & TSRC_MM_ADD) && (flags & (TSRC_MM_SCALE | TSRC_MM_SOFTCAP)))
+        return fail(TSRC_E_ARG, "tsrc_mul_mat: an addend cannot be combined with SCALE or SOFTCAP");
+    if ((flags & TSRC_MM_SCALE) && (flags & TSRC_MM_SOFTCAP)) return fail(TSRC_E_ARG, "tsrc_mul_mat: SCALE and SOFTCAP are exclusive");
+    if ((flags & TSRC_MM_ADD) && !add) return fail(TSRC_E_ARG, "tsrc_mul_mat: TSRC_MM_ADD without an addend");
+    const uint32_t K = w->K, fmt = w->fmt;
+    if (x_stride == 0) x_stride = K;
+    if (y_stride == 0) y_stride = w->n_rows;
+    if (x_stride < K || y_stride < w->n_rows) return fail(TSRC_E_ARG, "tsrc_mul_mat: a stride is shorter than its row");
+    if ((flags & TSRC_MM_ADD) && add_stride != 0 && add_stride < w->n_rows) return fail(TSRC_E_ARG, "tsrc_mul_mat: addend stride");
+    int rc = use_device(ctx);
+    if (rc) return rc;
+    const size_t per_tok = tsrc::mv_smem_bytes(fmt, K, 1) - (fmt == TSRC_FMT_Q4_K ? 8u * 32u * 16u : 0u) + 16u;
+    uint32_t tt = (uint32_t)std::min<size_t>(tsrc::kMvMaxT, std::max<size_t>(1, (kSmemBudget - 4096u) / per_tok));
+    tt = std::min(tt, T);
+    rc = ensure_scratch(ctx, qa_bytes(fmt, K, tt));
+    if (rc) return rc;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    int8_t* q = reinterpret_cast<int8_t*>(ctx->scratch);
+    float* d = reinterpret_cast<float*>(ctx->scratch + align256((size_t)tt * K));
+    int16_t* bs = reinterpret_cast<int16_t*>(ctx->scratch + align256((size_t)tt * K) + align256((size_t)tt * (K / block_of(fmt)) * 4u));
+    for (uint32_t t0 = 0; t0 < T; t0 += tt) {
+        const uint32_t n = std::min(tt, T - t0);
+        cudaError_t e = tsrc::launch_qact(fmt == TSRC_FMT_Q8_0 ? 0u : 1u, x + (size_t)t0 * x_stride, K, n, x_stride, q, d, bs, st);
+        if (e != cudaSuccess) return cuda_fail(e, "QACT launch");
+        tsrc::MvArgs a{};
+        a.qs = w->qs;
+        a.meta = w->meta;
+        a.n_rows = w->n_rows;
+        a.K = K;
+        a.qx = q;
+        a.dx = d;
+        a.bsx = bs;
+        a.T = n;
+        a.y = y + (size_t)t0 * y_stride;
+        a.y_stride = y_stride;
+        a.add = (flags & TSRC_MM_ADD) ? add + (size_t)t0 * add_stride : nullptr;
+        a.add_stride = add_stride;
+        a.flags = flags;
+        a.s0 = daz_host(s0);
+        a.s1 = daz_host(s1);
+        a.isum_out = t0 == 0 ? isum_out : nullptr;
+        e = tsrc::launch_matvec(fmt, a, st);
+        if (e != cudaSuccess) return cuda_fail(e, "matvec launch");
+    }
+    return TSRC_OK;
+}
+
+int tsrc_mvm(tsrc_ctx* ctx, const tsrc_weight* w, const int8_t* q, const float* d, const int16_t* bs, uint32_t T, float* y,
+             uint32_t y_stride, const float* add, uint32_t add_stride, uint32_t flags, float s0, float s1, void* stream) {
+    if (!ctx || !w || !q || !d || !y) return fail(TSRC_E_ARG, "tsrc_mvm: NULL argument");
+    if (w->ctx != ctx) return fail(TSRC_E_ARG, "tsrc_mvm: the weight belongs to another context");
+    if (w->fmt == TSRC_FMT_Q4_K && !bs) return fail(TSRC_E_ARG, "tsrc_mvm: Q4_K needs bs");
+    if (T == 0) return TSRC_OK;
+    if (T > tsrc::kMvMaxT) return fail(TSRC_E_ARG, "tsrc_mvm: T %u > %u", T, tsrc::kMvMaxT);
+    if (tsrc::mv_smem_bytes(w->fmt, w->K, T) > kSmemBudget) return fail(TSRC_E_SHAPE, "tsrc_mvm: T x K too large for one launch");
+    if (flags & ~(TSRC_MM_ADD | TSRC_MM_SCALE | TSRC_MM_SOFTCAP)) return fail(TSRC_E_ARG, "tsrc_mvm: undefined flag bits 0x%x", flags);
+    if ((flags & TSRC_MM_ADD) && ((flags & (TSRC_MM_SCALE | TSRC_MM_SOFTCAP)) || !add))
+        return fail(TSRC_E_ARG, "tsrc_mvm: ADD needs an addend and excludes SCALE / SOFTCAP");
+    if ((flags & TSRC_MM_SCALE) && (flags & TSRC_MM_SOFTCAP)) return fail(TSRC_E_ARG, "tsrc_mvm: SCALE and SOFTCAP are exclusive");
+    if (y_stride == 0) y_stride = w->n_rows;
+    int rc = use_device(ctx);
+    if (rc) return rc;
+    tsrc::MvArgs a{};
+    a.qs = w->qs;
+    a.meta = w->meta;
+    a.n_rows = w->n_rows;
+    a.K = w->K;
+    a.qx = q;
+    a.dx = d;
+    a.bsx = bs;
+    a.T = T;
+    a.y = y;
+    a.y_stride = y_stride;
+    a.add = (flags & TSRC_MM_ADD) ? add : nullptr;
+    a.add_stride = add_stride;
+    a.flags = flags;
+    a.s0 = daz_host(s0);
+    a.s1 = daz_host(s1);
+    cudaError_t e = tsrc::launch_matvec(w->fmt, a, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "matvec launch");
+    return TSRC_OK;
+}
+
+int tsrc_mul_mat(tsrc_ctx* ctx, const tsrc_weight* w, const float* x, uint32_t T, uint32_t x_stride, float* y, uint32_t y_stride,
+                 const float* add, uint32_t add_stride, uint32_t flags, float s0, float s1, void* stream) {
+    return mul_mat_impl(ctx, w, x, T, x_stride, y, y_stride, add, add_stride, flags, s0, s1, nullptr, stream);
+}
+
+int tsrc_mul_mat_isums(tsrc_ctx* ctx, const tsrc_weight* w, const float* x, float* y, int32_t* isum, void* stream) {
+    if (!isum) return fail(TSRC_E_ARG, "tsrc_mul_mat_isums: NULL isum");
+    return mul_mat_impl(ctx, w, x, 1, 0, y, 0, nullptr, 0, 0, 1.0f, 1.0f, isum, stream);
+}
+
+int tsrc_qact(tsrc_ctx* ctx, uint32_t kind, const float* x, uint32_t K, uint32_t T, uint32_t x_stride, int8_t* q, float* d,
+              int16_t* bs, void* stream) {
+    if (!ctx || !x || !q || !d) return fail(TSRC_E_ARG, "tsrc_qact: NULL argument");
+    if (kind > TSRC_QA_A256) return fail(TSRC_E_ARG, "tsrc_qact: kind %u", kind);
+    const uint32_t bsz = kind == TSRC_QA_A32 ? 32u : 256u;
+    if (K == 0 || K % bsz) return fail(TSRC_E_SHAPE, "tsrc_qact: K %u is not a positive multiple of %u", K, bsz);
+    if (kind == TSRC_QA_A256 && !bs) return fail(TSRC_E_ARG, "tsrc_qact: A256 needs bs");
+    if (x_stride == 0) x_stride = K;
+    if (x_stride < K) return fail(TSRC_E_ARG, "tsrc_qact: x_stride < K");
+    int rc = use_device(ctx);
+    if (rc) return rc;
+    cudaError_t e = tsrc::launch_qact(kind, x, K, T, x_stride, q, d, bs, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "QACT launch");
+    return TSRC_OK;
+}
+
+}  // extern "C"

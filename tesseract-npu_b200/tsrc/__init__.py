@@ -1,0 +1,227 @@
+"""Host-side binding of libtsrc.so (include/tsrc.h), the B200 hot path of the Tesseract stack.
+
+The classes mirror the ggml-tesseract backend's view of the path (jwkim04/tesseract-npu
+sw/ggml-tesseract/ggml-tesseract.cpp): a ``Device`` opened once per process and GPU
+(tsr_dev_open_locked, :463), ``Weight`` tensors uploaded into device memory in the device's own
+layout (the WEIGHTS buffer's set_tensor / get_tensor, :1905 / :1947), ``mul_mat`` with the MUL_MAT
+semantics (tsr_lower_mul_mat, :2790-2928, with the ADD / SCALE / softcap epilogues), and
+``mul_mat_unsupported`` for the supports_op refusals (:4199-4299).
+
+Device buffers are passed as torch CUDA tensors (or raw addresses); torch is only the allocator
+and stream provider here. There is no CPU path: if the library cannot be loaded, or no sm_100
+device is present, every call raises ``TsrcError``.
+"""
+from __future__ import annotations
+
+import ctypes as ct
+import os
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(os.path.dirname(HERE), "libtsrc.so")
+INCLUDE = os.path.join(os.path.dirname(os.path.dirname(HERE)), "include", "tsrc.h")
+
+FMT_Q8_0, FMT_Q4_K = 0, 1
+QA_A32, QA_A256 = 0, 1
+MM_ADD, MM_SCALE, MM_SOFTCAP = 0x1, 0x2, 0x4
+E_ARG, E_SHAPE, E_CUDA, E_NOMEM, E_NODEV = -1, -2, -3, -4, -5
+
+BLOCK = {FMT_Q8_0: 32, FMT_Q4_K: 256}
+BLOCK_BYTES = {FMT_Q8_0: 34, FMT_Q4_K: 144}
+
+
+class TsrcError(RuntimeError):
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"tsrc error {code}: {msg}")
+        self.code = code
+
+
+_p, _u32, _u64, _f32, _i = ct.c_void_p, ct.c_uint32, ct.c_uint64, ct.c_float, ct.c_int
+_lib = None
+
+# argtypes of every exported function (kept in the order of include/tsrc.h)
+_SIGS = {
+    "tsrc_last_error": (ct.c_char_p, []),
+    "tsrc_version": (ct.c_char_p, []),
+    "tsrc_open": (_i, [_i, ct.POINTER(_p)]),
+    "tsrc_close": (_i, [_p]),
+    "tsrc_weight_upload": (_i, [_p, _u32, _p, _u32, _u32, _u32, _u32, ct.POINTER(_p)]),
+    "tsrc_weight_upload_device": (_i, [_p, _u32, _p, _u32, _u32, _u32, _u32, _p, ct.POINTER(_p)]),
+    "tsrc_weight_synth": (_i, [_p, _u32, _u32, _u32, _u32, _u32, _u64, _f32, _p, ct.POINTER(_p)]),
+    "tsrc_weight_download": (_i, [_p, _p]),
+    "tsrc_weight_info": (_i, [_p] + [ct.POINTER(_u32)] * 5 + [ct.POINTER(_u64)]),
+    "tsrc_weight_free": (_i, [_p]),
+    "tsrc_mul_mat": (_i, [_p, _p, _p, _u32, _u32, _p, _u32, _p, _u32, _u32, _f32, _f32, _p]),
+    "tsrc_mvm": (_i, [_p, _p, _p, _p, _p, _u32, _p, _u32, _p, _u32, _u32, _f32, _f32, _p]),
+    "tsrc_mul_mat_unsupported": (ct.c_char_p, [_u32, _u64, _u64, _u64]),
+    "tsrc_qact": (_i, [_p, _u32, _p, _u32, _u32, _u32, _p, _p, _p, _p]),
+    "tsrc_mul_mat_isums": (_i, [_p, _p, _p, _p, _p, _p]),
+}
+
+
+def declared_symbols() -> list[str]:
+    """Function names include/tsrc.h declares (parsed from the header)."""
+    import re
+    with open(INCLUDE) as f:
+        return re.findall(r"^TSRC_API [^(]*?\b(tsrc_\w+)\(", f.read(), flags=re.M)
+
+
+def lib() -> ct.CDLL:
+    """Loads libtsrc.so (building it first if it is missing and nvcc is present)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        import importlib.util
+        spec = importlib.util.spec_from_file_location("tsrc_build", os.path.join(os.path.dirname(HERE), "build.py"))
+        mod = importlib.util.module_from_spec(spec)
+        spec.loader.exec_module(mod)
+        mod.build()
+    L = ct.CDLL(LIB_PATH)
+    for name, (res, args) in _SIGS.items():
+        fn = getattr(L, name)
+        fn.restype = res
+        fn.argtypes = args
+    _lib = L
+    return L
+
+
+def _check(rc: int) -> None:
+    if rc != 0:
+        raise TsrcError(rc, lib().tsrc_last_error().decode())
+
+
+def _addr(t) -> int | None:
+    """Device address of a torch tensor (or an int address, or None)."""
+    if t is None:
+        return None
+    if isinstance(t, int):
+        return t
+    return t.data_ptr()
+
+
+def _stream(stream) -> int | None:
+    if stream is None:
+        try:
+            import torch
+            return torch.cuda.current_stream().cuda_stream or None
+        except Exception:
+            return None
+    if isinstance(stream, int):
+        return stream or None
+    return stream.cuda_stream or None
+
+
+def ggml_row_bytes(fmt: int, K: int) -> int:
+    return K // BLOCK[fmt] * BLOCK_BYTES[fmt]
+
+
+def mul_mat_unsupported(fmt: int, N: int, K: int, T: int = 1) -> str | None:
+    r = lib().tsrc_mul_mat_unsupported(fmt, N, K, T)
+    return None if r is None else r.decode()
+
+
+class Device:
+    """One opened GPU (the backend device "Tesseract0" of the reference, now a B200)."""
+
+    def __init__(self, index: int = 0):
+        h = _p()
+        _check(lib().tsrc_open(index, ct.byref(h)))
+        self.handle = h
+        self.index = index
+
+    def close(self) -> None:
+        if self.handle:
+            _check(lib().tsrc_close(self.handle))
+            self.handle = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    # ---- weights ----
+    def upload(self, fmt: int, ggml_rows, N: int, K: int, row0: int = 0, n_rows: int | None = None) -> "Weight":
+        """ggml rows (numpy uint8 [n_rows, row_bytes], host) -> a device weight shard."""
+        import numpy as np
+        n_rows = N - row0 if n_rows is None else n_rows
+        a = np.ascontiguousarray(ggml_rows, dtype=np.uint8)
+        if a.size != n_rows * ggml_row_bytes(fmt, K):
+            raise TsrcError(E_ARG, f"upload: {a.size} bytes for {n_rows} rows of K={K}")
+        h = _p()
+        _check(lib().tsrc_weight_upload(self.handle, fmt, a.ctypes.data, N, K, row0, n_rows, ct.byref(h)))
+        return Weight(self, h)
+
+    def upload_device(self, fmt: int, rows_dev, N: int, K: int, row0: int = 0, n_rows: int | None = None,
+                      stream=None) -> "Weight":
+        n_rows = N - row0 if n_rows is None else n_rows
+        h = _p()
+        _check(lib().tsrc_weight_upload_device(self.handle, fmt, _addr(rows_dev), N, K, row0, n_rows,
+                                               _stream(stream), ct.byref(h)))
+        return Weight(self, h)
+
+    def synth(self, fmt: int, N: int, K: int, seed: int, sigma: float = 0.02, row0: int = 0,
+              n_rows: int | None = None, stream=None) -> "Weight":
+        n_rows = N - row0 if n_rows is None else n_rows
+        h = _p()
+        _check(lib().tsrc_weight_synth(self.handle, fmt, N, K, row0, n_rows, seed, sigma, _stream(stream),
+                                       ct.byref(h)))
+        return Weight(self, h)
+
+    # ---- MUL_MAT ----
+    def mul_mat(self, w: "Weight", x, y, T: int | None = None, add=None, add_stride: int | None = None,
+                flags: int = 0, s0: float = 1.0, s1: float = 1.0, x_stride: int = 0, y_stride: int = 0,
+                stream=None) -> None:
+        """y[t, n] = epilogue(W row n . QACT(x[t])) (torch CUDA tensors or addresses)."""
+        if T is None:
+            T = 1 if len(x.shape) == 1 else x.shape[0]
+        if add is not None:
+            flags |= MM_ADD
+            if add_stride is None:
+                add_stride = 0 if (len(add.shape) == 1 or add.shape[0] == 1) else w.n_rows
+        _check(lib().tsrc_mul_mat(self.handle, w.handle, _addr(x), T, x_stride, _addr(y), y_stride, _addr(add),
+                                  add_stride or 0, flags, s0, s1, _stream(stream)))
+
+    def mvm(self, w: "Weight", q, d, bs, y, T: int = 1, add=None, add_stride: int = 0, flags: int = 0,
+            s0: float = 1.0, s1: float = 1.0, y_stride: int = 0, stream=None) -> None:
+        """The MVM op alone on a QA image from qact()."""
+        if add is not None:
+            flags |= MM_ADD
+        _check(lib().tsrc_mvm(self.handle, w.handle, _addr(q), _addr(d), _addr(bs), T, _addr(y), y_stride, _addr(add),
+                              add_stride, flags, s0, s1, _stream(stream)))
+
+    def mul_mat_isums(self, w: "Weight", x, y, isum, stream=None) -> None:
+        _check(lib().tsrc_mul_mat_isums(self.handle, w.handle, _addr(x), _addr(y), _addr(isum), _stream(stream)))
+
+    def qact(self, kind: int, x, K: int, T: int, q, d, bs=None, x_stride: int = 0, stream=None) -> None:
+        _check(lib().tsrc_qact(self.handle, kind, _addr(x), K, T, x_stride, _addr(q), _addr(d), _addr(bs),
+                               _stream(stream)))
+
+
+class Weight:
+    """A weight shard resident in device memory."""
+
+    def __init__(self, dev: Device, handle):
+        self.dev, self.handle = dev, handle
+        f, n, k, r0, nr = (_u32() for _ in range(5))
+        b = _u64()
+        _check(lib().tsrc_weight_info(handle, ct.byref(f), ct.byref(n), ct.byref(k), ct.byref(r0), ct.byref(nr),
+                                      ct.byref(b)))
+        self.fmt, self.N, self.K, self.row0, self.n_rows = f.value, n.value, k.value, r0.value, nr.value
+        self.device_bytes = b.value
+
+    @property
+    def ggml_bytes(self) -> int:
+        return self.n_rows * ggml_row_bytes(self.fmt, self.K)
+
+    def download(self):
+        """The shard's ggml rows as numpy uint8 [n_rows, row_bytes]."""
+        import numpy as np
+        out = np.zeros((self.n_rows, ggml_row_bytes(self.fmt, self.K)), np.uint8)
+        _check(lib().tsrc_weight_download(self.handle, out.ctypes.data))
+        return out
+
+    def free(self) -> None:
+        if self.handle and self.dev.handle:
+            _check(lib().tsrc_weight_free(self.handle))
+        self.handle = None
