@@ -17,6 +17,7 @@
 
 #include "../../include/tsrc.h"
 #include "tsrc_internal.h"
+#include "tsrc_layout.cuh"
 
 namespace {
 
@@ -49,8 +50,8 @@ uint32_t block_of(uint32_t fmt) { return fmt == TSRC_FMT_Q8_0 ? 32u : 256u; }
 size_t ggml_row_bytes(uint32_t fmt, uint32_t K) {
     return fmt == TSRC_FMT_Q8_0 ? (size_t)(K / 32u) * 34u : (size_t)(K / 256u) * 144u;
 }
-size_t qs_row_bytes(uint32_t fmt, uint32_t K) { return fmt == TSRC_FMT_Q8_0 ? K : K / 2u; }
-size_t meta_row_bytes(uint32_t fmt, uint32_t K) { return fmt == TSRC_FMT_Q8_0 ? (size_t)(K / 32u) * 2u : (size_t)(K / 256u) * 16u; }
+size_t qs_row_bytes(uint32_t fmt, uint32_t K) { return tsrc::Layout{fmt, K}.qs_row_bytes(); }
+size_t meta_row_bytes(uint32_t fmt, uint32_t K) { return tsrc::Layout{fmt, K}.meta_row_bytes(); }
 size_t align256(size_t n) { return (n + 255u) & ~(size_t)255u; }
 
 // s0 / s1 enter the f32 rules as inputs: DAZ them once on the host.
@@ -130,6 +131,11 @@ int new_weight(tsrc_ctx* ctx, uint32_t fmt, uint32_t N, uint32_t K, uint32_t row
     uint8_t* mem = nullptr;
     cudaError_t e = cudaMalloc(&mem, qb + mb);
     if (e != cudaSuccess) return fail(TSRC_E_NOMEM, "cudaMalloc of %zu weight bytes: %s", qb + mb, cudaGetErrorString(e));
+    e = cudaMemset(mem, 0, qb + mb);      // the padding of partial tiles
+    if (e != cudaSuccess) {
+        cudaFree(mem);
+        return cuda_fail(e, "cudaMemset");
+    }
     tsrc_weight* w = new tsrc_weight{ctx, fmt, N, K, row0, n_rows, mem, mem + qb, qb + mb};
     ctx->weights.insert(w);
     *out = w;
@@ -313,12 +319,35 @@ static int mul_mat_impl(tsrc_ctx* ctx, const tsrc_weight* w, const float* x, uin
     if ((flags & TSRC_MM_ADD) && add_stride != 0 && add_stride < w->n_rows) return fail(TSRC_E_ARG, "tsrc_mul_mat: addend stride");
     int rc = use_device(ctx);
     if (rc) return rc;
-    const size_t per_tok = tsrc::mv_smem_bytes(fmt, K, 1) - (fmt == TSRC_FMT_Q4_K ? 8u * 32u * 16u : 0u) + 16u;
-    uint32_t tt = (uint32_t)std::min<size_t>(tsrc::kMvMaxT, std::max<size_t>(1, (kSmemBudget - 4096u) / per_tok));
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (T == 1) {
+        // decode: the matvec kernel quantizes the token itself (one launch, no scratch)
+        tsrc::MvArgs a{};
+        a.qs = w->qs;
+        a.meta = w->meta;
+        a.n_rows = w->n_rows;
+        a.K = K;
+        a.x = x;
+        a.x_stride = x_stride;
+        a.T = 1;
+        a.y = y;
+        a.y_stride = y_stride;
+        a.add = (flags & TSRC_MM_ADD) ? add : nullptr;
+        a.add_stride = add_stride;
+        a.flags = flags;
+        a.s0 = daz_host(s0);
+        a.s1 = daz_host(s1);
+        a.isum_out = isum_out;
+        cudaError_t e = tsrc::launch_matvec(fmt, a, st);
+        if (e != cudaSuccess) return cuda_fail(e, "matvec launch");
+        return TSRC_OK;
+    }
+    // several tokens: one QACT launch per tile of tokens into the scratch image, then the matvec
+    uint32_t tt = tsrc::kMvMaxT;
+    while (tt > 1 && tsrc::mv_smem_bytes(fmt, K, tt) > kSmemBudget) --tt;
     tt = std::min(tt, T);
     rc = ensure_scratch(ctx, qa_bytes(fmt, K, tt));
     if (rc) return rc;
-    cudaStream_t st = static_cast<cudaStream_t>(stream);
     int8_t* q = reinterpret_cast<int8_t*>(ctx->scratch);
     float* d = reinterpret_cast<float*>(ctx->scratch + align256((size_t)tt * K));
     int16_t* bs = reinterpret_cast<int16_t*>(ctx->scratch + align256((size_t)tt * K) + align256((size_t)tt * (K / block_of(fmt)) * 4u));

@@ -17,6 +17,8 @@ struct MvArgs {
     const uint8_t* qs;        // weight quants: Q8_0 [n_rows][K]; Q4_K [n_rows][K/2]
     const void* meta;         // Q8_0: fp16 d [n_rows][K/32]; Q4_K: 16 B {d, dmin, scales} [n_rows][K/256]
     uint32_t n_rows, K;
+    const float* x;           // f32 tokens (x[t * x_stride + k]): the kernel runs QACT itself; or NULL:
+    uint32_t x_stride;
     const int8_t* qx;         // QA of T tokens: q [T][K]
     const float* dx;          //                 d [T][K/bs]
     const int16_t* bsx;       //                 bs [T][K/16] (Q4_K)

@@ -15,6 +15,8 @@ namespace tsrc {
 __global__ void __launch_bounds__(256) qact_a32_kernel(const float* __restrict__ x, uint32_t K, uint32_t T,
                                                        uint32_t x_stride, int8_t* __restrict__ q,
                                                        float* __restrict__ d) {
+    // let the dependent matvec launch now; it reads this kernel's output only after completion
+    asm volatile("griddepcontrol.launch_dependents;");
     const uint32_t nb = K >> 5;
     const uint32_t gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const uint32_t lane = threadIdx.x & 31u;
@@ -31,6 +33,7 @@ __global__ void __launch_bounds__(256) qact_a32_kernel(const float* __restrict__
 __global__ void __launch_bounds__(256) qact_a256_kernel(const float* __restrict__ x, uint32_t K, uint32_t T,
                                                         uint32_t x_stride, int8_t* __restrict__ q,
                                                         float* __restrict__ d, int16_t* __restrict__ bs) {
+    asm volatile("griddepcontrol.launch_dependents;");
     const uint32_t nb = K >> 8;
     const uint32_t gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const uint32_t lane = threadIdx.x & 31u;

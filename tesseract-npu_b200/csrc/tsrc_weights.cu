@@ -1,14 +1,8 @@
 // tsrc_weights.cu -- weight layout on the device and seeded synthetic weights.
 //
-// Layout. ggml rows (Q8_0: K/32 blocks {fp16 d, int8 qs[32]} = 34 B; Q4_K: K/256 superblocks
-// {fp16 d, dmin, u8 scales[12], u8 qs[128]} = 144 B) are split on upload into two arrays so that
-// the matvec streams 16-byte-aligned quants with coalesced 128-bit loads:
-//   Q8_0: qs [n_rows][K] int8, meta [n_rows][K/32] fp16 d
-//   Q4_K: qs [n_rows][K/2] (each superblock's 128 qs bytes), meta [n_rows][K/256] 16 B
-//         {d, dmin, scales[12]} (the first 16 bytes of the ggml superblock, unchanged).
-// This plays the role of the reference's repack into its DRAM beat layout
-// (jwkim04/tesseract-npu sw/sim/tsr_ref.c:255-333): a pure byte permutation, inverted by
-// tsrc_weight_download (get_tensor).
+// Layout: ggml rows (Q8_0: K/32 blocks {fp16 d, int8 qs[32]} = 34 B; Q4_K: K/256 superblocks
+// {fp16 d, dmin, u8 scales[12], u8 qs[128]} = 144 B) <-> the tiled split layout of
+// tsrc_layout.cuh; tsrc_weight_download (get_tensor) inverts the upload exactly.
 //
 // Synthetic weights: value (row n, column k) is a normal N(0, sigma^2) draw from Philox4x32-10
 // (Salmon, Moraes, Dror, Shaw, SC'11) keyed by the seed, counter (n, k / 4), followed by the
@@ -17,87 +11,74 @@
 // test models (sw/ggml-tesseract/tests/gen_tiny_models.py:91-130). A row's values do not depend
 // on the shard it is generated in.
 #include "tsrc_internal.h"
+#include "tsrc_layout.cuh"
 #include "tsrc_numerics.cuh"
 
 namespace tsrc {
 
 // ---- layout ----------------------------------------------------------------------------------
-__global__ void repack_q8_0_kernel(const uint8_t* __restrict__ g, uint64_t nblk, uint8_t* __restrict__ qs,
-                                   uint16_t* __restrict__ d) {
+// One thread per block (Q8_0) / superblock (Q4_K); b = block index within the row.
+__global__ void repack_kernel(Layout L, const uint8_t* __restrict__ g, uint32_t n_rows, uint8_t* __restrict__ qs,
+                              uint8_t* __restrict__ meta) {
+    const uint32_t nb = L.blocks();
     const uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= nblk) return;
-    const uint8_t* b = g + i * 34u;
-    d[i] = (uint16_t)(b[0] | (b[1] << 8));
-    uint32_t w[8];
-#pragma unroll
-    for (int j = 0; j < 8; ++j)
-        w[j] = (uint32_t)b[2 + 4 * j] | ((uint32_t)b[3 + 4 * j] << 8) | ((uint32_t)b[4 + 4 * j] << 16) |
-               ((uint32_t)b[5 + 4 * j] << 24);
-    uint4* o = reinterpret_cast<uint4*>(qs + i * 32u);
-    o[0] = make_uint4(w[0], w[1], w[2], w[3]);
-    o[1] = make_uint4(w[4], w[5], w[6], w[7]);
+    if (i >= (uint64_t)n_rows * nb) return;
+    const uint32_t r = (uint32_t)(i / nb), b = (uint32_t)(i % nb);
+    if (L.fmt == 0) {
+        const uint8_t* src = g + i * 34u;
+        *reinterpret_cast<uint16_t*>(meta + L.meta_off(r, b)) = (uint16_t)(src[0] | (src[1] << 8));
+        for (uint32_t j = 0; j < 2; ++j) {
+            uint32_t w[4];
+            for (int e = 0; e < 4; ++e) {
+                const uint8_t* p = src + 2 + 16 * j + 4 * e;
+                w[e] = (uint32_t)p[0] | ((uint32_t)p[1] << 8) | ((uint32_t)p[2] << 16) | ((uint32_t)p[3] << 24);
+            }
+            *reinterpret_cast<uint4*>(qs + L.qs_off(r, b, j)) = make_uint4(w[0], w[1], w[2], w[3]);
+        }
+    } else {
+        const uint4* src = reinterpret_cast<const uint4*>(g) + i * 9u;    // 144 B, 16-byte aligned
+        *reinterpret_cast<uint4*>(meta + L.meta_off(r, b)) = src[0];
+        for (uint32_t j = 0; j < 8; ++j) *reinterpret_cast<uint4*>(qs + L.qs_off(r, b, j)) = src[1 + j];
+    }
 }
 
-__global__ void unrepack_q8_0_kernel(const uint8_t* __restrict__ qs, const uint16_t* __restrict__ d, uint64_t nblk,
-                                     uint8_t* __restrict__ g) {
+__global__ void unrepack_kernel(Layout L, const uint8_t* __restrict__ qs, const uint8_t* __restrict__ meta, uint32_t n_rows,
+                                uint8_t* __restrict__ g) {
+    const uint32_t nb = L.blocks();
     const uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= nblk) return;
-    uint8_t* b = g + i * 34u;
-    b[0] = (uint8_t)d[i];
-    b[1] = (uint8_t)(d[i] >> 8);
-    for (int j = 0; j < 32; ++j) b[2 + j] = qs[i * 32u + j];
-}
-
-// 144-byte superblocks: 9 uint4 each when the ggml buffer is 16-byte aligned (staging buffers are).
-__global__ void repack_q4_K_kernel(const uint4* __restrict__ g, uint64_t nsb, uint4* __restrict__ qs,
-                                   uint4* __restrict__ meta) {
-    const uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= nsb) return;
-    const uint4* b = g + i * 9u;
-    meta[i] = b[0];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) qs[i * 8u + j] = b[1 + j];
-}
-
-__global__ void unrepack_q4_K_kernel(const uint4* __restrict__ qs, const uint4* __restrict__ meta, uint64_t nsb,
-                                     uint4* __restrict__ g) {
-    const uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= nsb) return;
-    uint4* b = g + i * 9u;
-    b[0] = meta[i];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) b[1 + j] = qs[i * 8u + j];
+    if (i >= (uint64_t)n_rows * nb) return;
+    const uint32_t r = (uint32_t)(i / nb), b = (uint32_t)(i % nb);
+    if (L.fmt == 0) {
+        uint8_t* dst = g + i * 34u;
+        const uint16_t d = *reinterpret_cast<const uint16_t*>(meta + L.meta_off(r, b));
+        dst[0] = (uint8_t)d;
+        dst[1] = (uint8_t)(d >> 8);
+        for (uint32_t j = 0; j < 2; ++j) {
+            const uint8_t* c = qs + L.qs_off(r, b, j);
+            for (int e = 0; e < 16; ++e) dst[2 + 16 * j + e] = c[e];
+        }
+    } else {
+        uint4* dst = reinterpret_cast<uint4*>(g) + i * 9u;
+        dst[0] = *reinterpret_cast<const uint4*>(meta + L.meta_off(r, b));
+        for (uint32_t j = 0; j < 8; ++j) dst[1 + j] = *reinterpret_cast<const uint4*>(qs + L.qs_off(r, b, j));
+    }
 }
 
 static inline uint32_t grid_for(uint64_t n, uint32_t bs) { return (uint32_t)((n + bs - 1u) / bs); }
 
 cudaError_t launch_repack(uint32_t fmt, const uint8_t* ggml, uint32_t n_rows, uint32_t K, uint8_t* qs, uint8_t* meta,
                           cudaStream_t st) {
-    if (fmt == 0) {
-        const uint64_t nblk = (uint64_t)n_rows * (K / 32u);
-        if (nblk) repack_q8_0_kernel<<<grid_for(nblk, 256), 256, 0, st>>>(ggml, nblk, qs, reinterpret_cast<uint16_t*>(meta));
-    } else {
-        const uint64_t nsb = (uint64_t)n_rows * (K / 256u);
-        if (nsb)
-            repack_q4_K_kernel<<<grid_for(nsb, 256), 256, 0, st>>>(reinterpret_cast<const uint4*>(ggml), nsb,
-                                                                  reinterpret_cast<uint4*>(qs), reinterpret_cast<uint4*>(meta));
-    }
+    const Layout L{fmt, K};
+    const uint64_t n = (uint64_t)n_rows * L.blocks();
+    if (n) repack_kernel<<<grid_for(n, 256), 256, 0, st>>>(L, ggml, n_rows, qs, meta);
     return cudaGetLastError();
 }
 
 cudaError_t launch_unrepack(uint32_t fmt, const uint8_t* qs, const uint8_t* meta, uint32_t n_rows, uint32_t K,
                             uint8_t* ggml, cudaStream_t st) {
-    if (fmt == 0) {
-        const uint64_t nblk = (uint64_t)n_rows * (K / 32u);
-        if (nblk)
-            unrepack_q8_0_kernel<<<grid_for(nblk, 256), 256, 0, st>>>(qs, reinterpret_cast<const uint16_t*>(meta), nblk, ggml);
-    } else {
-        const uint64_t nsb = (uint64_t)n_rows * (K / 256u);
-        if (nsb)
-            unrepack_q4_K_kernel<<<grid_for(nsb, 256), 256, 0, st>>>(reinterpret_cast<const uint4*>(qs),
-                                                                    reinterpret_cast<const uint4*>(meta), nsb,
-                                                                    reinterpret_cast<uint4*>(ggml));
-    }
+    const Layout L{fmt, K};
+    const uint64_t n = (uint64_t)n_rows * L.blocks();
+    if (n) unrepack_kernel<<<grid_for(n, 256), 256, 0, st>>>(L, qs, meta, n_rows, ggml);
     return cudaGetLastError();
 }
 
@@ -135,7 +116,8 @@ __device__ __forceinline__ void normal4(uint64_t seed, uint32_t n, uint32_t q, f
 
 // One thread per Q8_0 block: A32 quantization of 32 normals (quantize_row_q8_0_ref).
 __global__ void synth_q8_0_kernel(uint32_t K, uint32_t row0, uint32_t n_rows, uint64_t seed, float sigma,
-                                  uint8_t* __restrict__ qs, uint16_t* __restrict__ d) {
+                                  uint8_t* __restrict__ qs, uint8_t* __restrict__ meta) {
+    const Layout L{0u, K};
     const uint32_t nb = K / 32u;
     const uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= (uint64_t)n_rows * nb) return;
@@ -156,15 +138,15 @@ __global__ void synth_q8_0_kernel(uint32_t K, uint32_t row0, uint32_t n_rows, ui
     uint32_t w[8] = {0, 0, 0, 0, 0, 0, 0, 0};
 #pragma unroll
     for (int j = 0; j < 32; ++j) w[j >> 2] |= ((uint32_t)round_sat8(fmul(daz(v[j]), id), false) & 0xFFu) << (8 * (j & 3));
-    uint4* o = reinterpret_cast<uint4*>(qs + i * 32u);
-    o[0] = make_uint4(w[0], w[1], w[2], w[3]);
-    o[1] = make_uint4(w[4], w[5], w[6], w[7]);
-    d[i] = f2h(db);
+    *reinterpret_cast<uint4*>(qs + L.qs_off(r, b, 0)) = make_uint4(w[0], w[1], w[2], w[3]);
+    *reinterpret_cast<uint4*>(qs + L.qs_off(r, b, 1)) = make_uint4(w[4], w[5], w[6], w[7]);
+    *reinterpret_cast<uint16_t*>(meta + L.meta_off(r, b)) = f2h(db);
 }
 
 // One thread per Q4_K superblock (gen_tiny_models.py quantize_q4_k, in f32).
 __global__ void synth_q4_K_kernel(uint32_t K, uint32_t row0, uint32_t n_rows, uint64_t seed, float sigma,
                                   uint8_t* __restrict__ qs, uint8_t* __restrict__ meta) {
+    const Layout L{1u, K};
     const uint32_t nsb = K / 256u;
     const uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= (uint64_t)n_rows * nsb) return;
@@ -197,14 +179,16 @@ __global__ void synth_q4_K_kernel(uint32_t K, uint32_t row0, uint32_t n_rows, ui
         sc[j] = (uint32_t)fminf(fmaxf(a, 0.0f), 63.0f);
         mn[j] = (uint32_t)fminf(fmaxf(b, 0.0f), 63.0f);
     }
-    uint8_t* m = meta + i * 16u;
+    uint8_t m[16];
     m[0] = (uint8_t)hd; m[1] = (uint8_t)(hd >> 8); m[2] = (uint8_t)hm; m[3] = (uint8_t)(hm >> 8);
     for (int j = 0; j < 4; ++j) {
         m[4 + j] = (uint8_t)((sc[j] & 63u) | ((sc[j + 4] >> 4) << 6));
         m[8 + j] = (uint8_t)((mn[j] & 63u) | ((mn[j + 4] >> 4) << 6));
         m[12 + j] = (uint8_t)((sc[j + 4] & 15u) | ((mn[j + 4] & 15u) << 4));
     }
-    uint8_t* qo = qs + i * 128u;
+    uint8_t* mo = meta + L.meta_off(r, s);
+    for (int j = 0; j < 16; ++j) mo[j] = m[j];
+    uint8_t qo[128];
     for (int c = 0; c < 4; ++c) {               // bytes 32c .. 32c+31: sub-block 2c low, 2c+1 high
         const float s0 = __fmul_rn(dd, (float)sc[2 * c]), o0 = __fmul_rn(dm, (float)mn[2 * c]);
         const float s1 = __fmul_rn(dd, (float)sc[2 * c + 1]), o1 = __fmul_rn(dm, (float)mn[2 * c + 1]);
@@ -220,13 +204,15 @@ __global__ void synth_q4_K_kernel(uint32_t K, uint32_t row0, uint32_t n_rows, ui
             }
         }
     }
+    for (uint32_t j = 0; j < 8; ++j)
+        for (int e = 0; e < 16; ++e) qs[L.qs_off(r, s, j) + e] = qo[16 * j + e];
 }
 
 cudaError_t launch_synth(uint32_t fmt, uint32_t K, uint32_t row0, uint32_t n_rows, uint64_t seed, float sigma,
                          uint8_t* qs, uint8_t* meta, cudaStream_t st) {
     if (fmt == 0) {
         const uint64_t n = (uint64_t)n_rows * (K / 32u);
-        if (n) synth_q8_0_kernel<<<grid_for(n, 128), 128, 0, st>>>(K, row0, n_rows, seed, sigma, qs, reinterpret_cast<uint16_t*>(meta));
+        if (n) synth_q8_0_kernel<<<grid_for(n, 128), 128, 0, st>>>(K, row0, n_rows, seed, sigma, qs, meta);
     } else {
         const uint64_t n = (uint64_t)n_rows * (K / 256u);
         if (n) synth_q4_K_kernel<<<grid_for(n, 128), 128, 0, st>>>(K, row0, n_rows, seed, sigma, qs, meta);
