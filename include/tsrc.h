@@ -38,6 +38,7 @@ extern "C" {
 #define TSRC_E_CUDA        (-3)   // a CUDA runtime error (message carries cudaGetErrorString)
 #define TSRC_E_NOMEM       (-4)   // device or host allocation failed
 #define TSRC_E_NODEV       (-5)   // no usable sm_100 device
+#define TSRC_E_DEVICE      (-6)   // a kernel reported an error (a bounded wait ran out)
 
 #define TSRC_FMT_Q8_0  0u         // ggml block_q8_0: {fp16 d; int8 qs[32]}, 34 B per 32 weights
 #define TSRC_FMT_Q4_K  1u         // ggml block_q4_K: {fp16 d, dmin; u8 scales[12]; u8 qs[128]}, 144 B per 256
@@ -66,6 +67,10 @@ TSRC_API const char * tsrc_version(void);
 TSRC_API int tsrc_open(int device, tsrc_ctx ** out);
 // Releases the context and every weight still attached to it (tsr_backend_free, :3799).
 TSRC_API int tsrc_close(tsrc_ctx * ctx);
+// Waits for the work queued on `stream` (NULL: the whole device) and reports a kernel-side error
+// (TSRC_E_DEVICE: a bounded wait inside a kernel ran out; the flag is cleared). The reference's
+// transport had launch timeouts for the same purpose (sw/transport/tsr_kdev.cpp:1452-1531).
+TSRC_API int tsrc_sync(tsrc_ctx * ctx, void * stream);
 
 // ---- weights (the WEIGHTS buffer's set_tensor / get_tensor, ggml-tesseract.cpp:1905, :1947) -----
 
@@ -77,12 +82,14 @@ TSRC_API int tsrc_close(tsrc_ctx * ctx);
 // sw/sim/tsr_ref.c:296-314).
 TSRC_API int tsrc_weight_upload(tsrc_ctx * ctx, uint32_t fmt, const void * ggml_rows, uint32_t N, uint32_t K,
                        uint32_t row0, uint32_t n_rows, tsrc_weight ** out);
-// The same from ggml rows already in device memory (e.g. a staging buffer); queued on `stream`.
+// The same from ggml rows already in device memory (e.g. a staging buffer); runs on `stream` and
+// returns when the weight is in place.
 TSRC_API int tsrc_weight_upload_device(tsrc_ctx * ctx, uint32_t fmt, const void * ggml_rows_dev, uint32_t N, uint32_t K,
                               uint32_t row0, uint32_t n_rows, void * stream, tsrc_weight ** out);
 // Seeded synthetic weight generated on the device (counter-based Philox4x32-10 normal values of
 // standard deviation sigma, quantized to fmt on the device); rows [row0, row0+n_rows) of an N x K
-// tensor, identical to the same rows of an unsharded generation. For benches and tests.
+// tensor, identical to the same rows of an unsharded generation. For benches and tests. Runs on
+// `stream` and returns when the weight is in place.
 TSRC_API int tsrc_weight_synth(tsrc_ctx * ctx, uint32_t fmt, uint32_t N, uint32_t K, uint32_t row0, uint32_t n_rows,
                       uint64_t seed, float sigma, void * stream, tsrc_weight ** out);
 // Reads the shard back as ggml rows (n_rows rows) into host memory (get_tensor; the inverse repack,

@@ -43,7 +43,7 @@ int cuda_fail(cudaError_t e, const char* what) {
         if (e_ != cudaSuccess) return cuda_fail(e_, what); \
     } while (0)
 
-constexpr uint32_t kKMax = 131072;            // shared-memory bound of one token's QA image
+constexpr uint32_t kKMax = 65536;             // shared-memory bound of one token's QA image
 constexpr size_t kSmemBudget = 200u * 1024u;  // dynamic shared memory one matvec CTA may use
 
 uint32_t block_of(uint32_t fmt) { return fmt == TSRC_FMT_Q8_0 ? 32u : 256u; }
@@ -115,7 +115,7 @@ int ensure_scratch(tsrc_ctx* ctx, size_t bytes) {
 const char* shape_reason(uint32_t fmt, uint64_t N, uint64_t K, uint64_t T) {
     if (fmt != TSRC_FMT_Q8_0 && fmt != TSRC_FMT_Q4_K) return "MUL_MAT: the weight type has no device format (Q8_0 and Q4_K only)";
     if (K == 0 || K % block_of(fmt) != 0) return "MUL_MAT: K is not a positive multiple of the block size (32 Q8_0, 256 Q4_K)";
-    if (K > kKMax) return "MUL_MAT: K exceeds 131072 (one token's quantized activation must fit shared memory)";
+    if (K > kKMax) return "MUL_MAT: K exceeds 65536 (one token's quantized activation must fit shared memory)";
     if (N == 0 || N > 0xFFFFFFFFull) return "MUL_MAT: N is 0 or does not fit 32 bits";
     if (T > 0xFFFFFFFFull) return "MUL_MAT: too many tokens";
     return nullptr;
@@ -195,6 +195,19 @@ int tsrc_close(tsrc_ctx* ctx) {
     return TSRC_OK;
 }
 
+int tsrc_sync(tsrc_ctx* ctx, void* stream) {
+    if (!ctx) return fail(TSRC_E_ARG, "tsrc_sync: NULL context");
+    int rc = use_device(ctx);
+    if (rc) return rc;
+    cudaError_t e = stream ? cudaStreamSynchronize(static_cast<cudaStream_t>(stream)) : cudaDeviceSynchronize();
+    if (e != cudaSuccess) return cuda_fail(e, "synchronize");
+    uint32_t code = 0;
+    e = tsrc::matvec_error(&code, true);
+    if (e != cudaSuccess) return cuda_fail(e, "reading the kernel error flag");
+    if (code) return fail(TSRC_E_DEVICE, "a matvec kernel gave up a bounded wait (code %u)", code);
+    return TSRC_OK;
+}
+
 int tsrc_weight_upload_device(tsrc_ctx* ctx, uint32_t fmt, const void* ggml_rows_dev, uint32_t N, uint32_t K, uint32_t row0,
                               uint32_t n_rows, void* stream, tsrc_weight** out) {
     if (!ggml_rows_dev) return fail(TSRC_E_ARG, "tsrc_weight_upload_device: NULL rows");
@@ -205,6 +218,8 @@ int tsrc_weight_upload_device(tsrc_ctx* ctx, uint32_t fmt, const void* ggml_rows
     if (rc) return rc;
     cudaError_t e = tsrc::launch_repack(fmt, static_cast<const uint8_t*>(ggml_rows_dev), n_rows, K, w->qs, w->meta,
                                         static_cast<cudaStream_t>(stream));
+    // the matvec streams weights before it waits on earlier kernels: the weight must be complete
+    if (e == cudaSuccess) e = cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) {
         drop_weight(w);
         return cuda_fail(e, "repack launch");
@@ -255,6 +270,7 @@ int tsrc_weight_synth(tsrc_ctx* ctx, uint32_t fmt, uint32_t N, uint32_t K, uint3
     int rc = new_weight(ctx, fmt, N, K, row0, n_rows, &w);
     if (rc) return rc;
     cudaError_t e = tsrc::launch_synth(fmt, K, row0, n_rows, seed, sigma, w->qs, w->meta, static_cast<cudaStream_t>(stream));
+    if (e == cudaSuccess) e = cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) {
         drop_weight(w);
         return cuda_fail(e, "synth launch");

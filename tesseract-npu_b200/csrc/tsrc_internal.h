@@ -36,6 +36,8 @@ cudaError_t launch_qact(uint32_t kind, const float* x, uint32_t K, uint32_t T, u
                         int16_t* bs, cudaStream_t st);
 cudaError_t launch_matvec(uint32_t fmt, const MvArgs& a, cudaStream_t st);
 size_t mv_smem_bytes(uint32_t fmt, uint32_t K, uint32_t T);
+// The first error code any matvec launch recorded on the current device (0 = none).
+cudaError_t matvec_error(uint32_t* code, bool clear);
 
 // Weight layout (tsrc_weights.cu): ggml rows <-> this library's split layout.
 cudaError_t launch_repack(uint32_t fmt, const uint8_t* ggml, uint32_t n_rows, uint32_t K, uint8_t* qs, uint8_t* meta,

@@ -23,7 +23,7 @@ INCLUDE = os.path.join(os.path.dirname(os.path.dirname(HERE)), "include", "tsrc.
 FMT_Q8_0, FMT_Q4_K = 0, 1
 QA_A32, QA_A256 = 0, 1
 MM_ADD, MM_SCALE, MM_SOFTCAP = 0x1, 0x2, 0x4
-E_ARG, E_SHAPE, E_CUDA, E_NOMEM, E_NODEV = -1, -2, -3, -4, -5
+E_ARG, E_SHAPE, E_CUDA, E_NOMEM, E_NODEV, E_DEVICE = -1, -2, -3, -4, -5, -6
 
 BLOCK = {FMT_Q8_0: 32, FMT_Q4_K: 256}
 BLOCK_BYTES = {FMT_Q8_0: 34, FMT_Q4_K: 144}
@@ -44,6 +44,7 @@ _SIGS = {
     "tsrc_version": (ct.c_char_p, []),
     "tsrc_open": (_i, [_i, ct.POINTER(_p)]),
     "tsrc_close": (_i, [_p]),
+    "tsrc_sync": (_i, [_p, _p]),
     "tsrc_weight_upload": (_i, [_p, _u32, _p, _u32, _u32, _u32, _u32, ct.POINTER(_p)]),
     "tsrc_weight_upload_device": (_i, [_p, _u32, _p, _u32, _u32, _u32, _u32, _p, ct.POINTER(_p)]),
     "tsrc_weight_synth": (_i, [_p, _u32, _u32, _u32, _u32, _u32, _u64, _f32, _p, ct.POINTER(_p)]),
@@ -139,6 +140,10 @@ class Device:
 
     def __exit__(self, *exc):
         self.close()
+
+    def sync(self, stream=None) -> None:
+        """Waits for queued work and raises if a kernel reported an error."""
+        _check(lib().tsrc_sync(self.handle, _stream(stream)))
 
     # ---- weights ----
     def upload(self, fmt: int, ggml_rows, N: int, K: int, row0: int = 0, n_rows: int | None = None) -> "Weight":

@@ -23,7 +23,7 @@ def test_version():
 
 @pytest.mark.parametrize("fmt,N,K,ok", [(0, 4864, 896, True), (1, 14336, 4096, True), (1, 10, 4000, False),
                                         (0, 10, 33, False), (2, 10, 32, False), (0, 0, 32, False),
-                                        (0, 10, 131072 + 32, False), (1, 1, 131072, True)])
+                                        (0, 10, 65536 + 32, False), (1, 1, 65536, True)])
 def test_mul_mat_refusals(fmt, N, K, ok):
     why = tsrc.mul_mat_unsupported(fmt, N, K, 1)
     assert (why is None) == ok, why

@@ -153,3 +153,28 @@ def test_argument_errors(dev, tsro):
             dev.synth(1, 10, 300, seed=1)
     finally:
         w.free()
+
+
+@pytest.mark.parametrize("fmt,N,K,T", [(1, 300, 4096, 1), (0, 129, 4864, 3), (1, 50, 14336, 2), (0, 64, 896, 8)])
+def test_mvm_prequantized(dev, tsro, fmt, N, K, T):
+    """The MVM op on a QA image from tsrc_qact (the kernel's staging path) equals MUL_MAT."""
+    import torch
+    w = H.weights(tsro, fmt, N, K, 90 + N)
+    x = H.special_acts(K, T, 91 + N)
+    wd = dev.upload(fmt, w, N, K)
+    try:
+        xd = torch.from_numpy(x).cuda()
+        q = torch.zeros((T, K), dtype=torch.int8, device="cuda")
+        d = torch.zeros((T, K // (32 if fmt == 0 else 256)), device="cuda")
+        bs = torch.zeros((T, K // 16), dtype=torch.int16, device="cuda") if fmt == 1 else None
+        dev.qact(fmt, xd, K, T, q, d, bs)
+        y = torch.zeros((T, N), device="cuda")
+        dev.mvm(wd, q, d, bs, y, T=T)
+        dev.sync()
+        np.testing.assert_array_equal(bits(y.cpu().numpy()), bits(tsro.matvec(fmt, w, K, x)))
+    finally:
+        wd.free()
+
+
+def test_sync_reports_no_error(dev):
+    dev.sync()
