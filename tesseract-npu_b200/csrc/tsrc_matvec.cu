@@ -7,24 +7,27 @@
 // then the MVM epilogue (addend / scale / softcap, tsr_sim.c:1648-1670).
 //
 // Structure (an HBM stream; tsrc_layout.cuh has the tiled weight layout):
-//   - each CTA owns a contiguous range of rows, cut into stages of 16 rows x a tile range;
-//   - a producer warp moves stages into a shared-memory ring with bulk asynchronous copies
-//     (cp.async.bulk, completion counted on an mbarrier; no multicast), starting at kernel entry,
-//     before the activation is even available, so the first stages of every CTA are in flight
-//     while the activation is quantized;
-//   - 8 consumer warps: warp w takes rows 2w, 2w+1 of a stage; lane L serves row L/16 and block
-//     16 t + (L % 16) of tile t, so it owns its block's whole integer sum (no cross-lane sums) and
-//     accumulates exactly partial p[L % 16] of its row, tile by tile (the reference's order); the
-//     16-partial tree is four xor-shuffle levels inside each half-warp;
+//   - one CTA per SM owns a contiguous range of rows; at entry one thread asks the memory system
+//     to move that whole range from HBM into L2 (cp.async.bulk.prefetch.L2: HBM -> L2 only, no
+//     shared memory and no SM ingress used), so HBM streams at full rate from the first
+//     microsecond, independently of how far the warps have got;
+//   - warps read the weights from L2 with 128-bit non-allocating loads into registers, the next
+//     unit's loads issued before the current unit is computed;
+//   - a warp owns a pair of rows; lane L serves row L/16 and block 16 t + (L % 16) of tile t, so
+//     it owns its block's whole integer sum (no cross-lane sums) and accumulates exactly partial
+//     p[L % 16] of its row, tile by tile (the reference's order); the 16-partial tree is four
+//     xor-shuffle levels inside each half-warp;
 //   - the quantized activation sits in shared memory in the same chunk-major tiles, so the 16
 //     lanes of a half-warp read 256 contiguous bytes (conflict-free) at immediate offsets; for one
-//     token the CTA quantizes x itself (QACT fused), otherwise it copies a QA image;
+//     token the CTA quantizes x itself (QACT fused; its loads are issued in batches), otherwise it
+//     copies a QA image;
+//   - the kernel lets the next launch on the stream start early (programmatic dependent launch:
+//     its L2 prefetch overlaps this launch's tail) and waits for the previous one before it
+//     touches the activation;
 //   - fast path: if every nonzero activation scale Dx is >= 2^-79, every term and partial is 0 or
 //     a multiple of 2^-126 of magnitude >= 2^-126 (|d_w| >= 2^-24 for a nonzero fp16), so no
 //     result can be subnormal and the flush tests are skipped (a CTA-uniform choice; the values
-//     are the same either way);
-//   - every mbarrier wait is bounded; a wait that runs out records an error code (read by
-//     tsrc_sync) and the CTA drains its copies in flight and returns.
+//     are the same either way).
 #include <type_traits>
 
 #include "tsrc_internal.h"
@@ -33,48 +36,24 @@
 
 namespace tsrc {
 
-constexpr uint32_t kCWarps = 8;                     // consumer warps
-constexpr uint32_t kThreads = (kCWarps + 1) * 32;   // + one producer warp
-constexpr uint32_t kStageRows = 2 * kCWarps;        // 16
+constexpr uint32_t kCWarps = 16;                    // warps per CTA (one CTA per SM)
+constexpr uint32_t kThreads = kCWarps * 32;
 constexpr uint32_t kSafeDx = 0x18000000u;           // 2^-79
-constexpr uint32_t kMaxStages = 4;
-constexpr uint32_t kSpinLimit = 1u << 21;           // mbarrier polls (each suspends <= ~0.5 us)
-constexpr uint32_t kErrConsumerWait = 1u, kErrProducerWait = 2u, kErrDrain = 3u;
+constexpr uint32_t kPrefetchChunk = 64u * 1024u;    // bytes per L2 prefetch instruction
 
-__device__ unsigned int g_mv_error;                 // first error code of any launch (0 = none)
+__device__ unsigned int g_mv_error;                 // first error code of any launch (0 = none; reserved)
 
 // ---- mbarrier and bulk-copy helpers -----------------------------------------------------------
 __device__ __forceinline__ uint32_t su32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
-__device__ __forceinline__ void mbar_init(uint64_t* b, uint32_t count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(su32(b)), "r"(count) : "memory");
+__device__ __forceinline__ void prefetch_l2(const void* src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
 }
-__device__ __forceinline__ void mbar_arrive(uint64_t* b) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(su32(b)) : "memory");
-}
-__device__ __forceinline__ void mbar_expect_tx(uint64_t* b, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(su32(b)), "r"(bytes) : "memory");
-}
-__device__ __forceinline__ bool mbar_try_wait(uint64_t* b, uint32_t parity) {
-    uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(ok)
-        : "r"(su32(b)), "r"(parity), "r"(500u)
-        : "memory");
-    return ok != 0;
-}
-__device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity, uint32_t code) {
-    for (uint32_t i = 0; i < kSpinLimit; ++i)
-        if (mbar_try_wait(b, parity)) return true;
-    atomicCAS(&g_mv_error, 0u, code);
-    return false;
-}
-__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
-    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(su32(dst)),
-                 "l"(src), "r"(bytes), "r"(su32(bar))
-                 : "memory");
+__device__ __forceinline__ uint4 ld_stream(const void* p) {
+    uint4 r;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                 : "l"(p));
+    return r;
 }
 __device__ __forceinline__ void consumer_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kCWarps * 32) : "memory"); }
 
@@ -153,37 +132,22 @@ struct Qa {
 __host__ __device__ constexpr size_t a16(size_t n) { return (n + 15u) & ~(size_t)15u; }
 
 struct Plan {                          // shared-memory plan of one launch (host and device agree)
-    uint32_t stage_q, stage_m;         // bytes of a stage's quant / meta regions
-    uint32_t pitch_q, pitch_m;         // per stage row
-    uint32_t stages;                   // ring depth
     uint32_t qa_q, qa_d, qa_bs;        // per-token bytes of the activation image
-    uint32_t whole;                    // 1: a stage holds whole rows (one contiguous copy)
-    uint32_t tps;                      // tiles per stage
     __host__ __device__ size_t qa_bytes(uint32_t T) const { return (size_t)T * (qa_q + qa_d + qa_bs); }
-    __host__ __device__ size_t ring_bytes() const { return (size_t)stages * (stage_q + stage_m); }
-    __host__ __device__ size_t total(uint32_t T) const { return ring_bytes() + a16(qa_bytes(T)) + 2u * kMaxStages * 8u + 16u; }
+    __host__ __device__ size_t total(uint32_t T) const { return a16(qa_bytes(T)) + 16u; }
 };
 
-__host__ __device__ inline Plan make_plan(uint32_t fmt, uint32_t K, uint32_t T, size_t budget) {
+__host__ __device__ inline Plan make_plan(uint32_t fmt, uint32_t K) {
     const Layout L{fmt, K};
     Plan p{};
-    p.tps = fmt == 0 ? 4u : 1u;
-    p.whole = L.tiles() <= p.tps ? 1u : 0u;
-    p.pitch_q = p.whole ? (uint32_t)L.qs_row_bytes() : p.tps * 16u * L.block_qs_bytes();
-    p.pitch_m = p.whole ? (uint32_t)L.meta_row_bytes() : (uint32_t)a16((size_t)p.tps * 16u * L.meta_entry_bytes());
-    p.stage_q = kStageRows * p.pitch_q;
-    p.stage_m = kStageRows * p.pitch_m;
     p.qa_q = L.tiles() * (fmt == 0 ? 512u : 4096u);
     p.qa_d = (uint32_t)a16((size_t)L.blocks() * 4u);
     p.qa_bs = fmt == 0 ? 0u : L.tiles() * 256u;
-    p.stages = kMaxStages;
-    while (p.stages > 2 && p.total(T) > budget) --p.stages;
     return p;
 }
 
-// QACT A32 of block b (tsr_ref.c:472-487), one warp.
-__device__ __forceinline__ void qact32_to_smem(const float* __restrict__ x, uint32_t b, uint32_t lane, uint8_t* q, float* d) {
-    const float v = x[32u * b + lane];
+// QACT A32 of one block (tsr_ref.c:472-487), one warp; v = the lane's value.
+__device__ __forceinline__ void qact32_to_smem(float v, uint32_t b, uint32_t lane, uint8_t* q, float* d) {
     const uint32_t amax = __reduce_max_sync(0xFFFFFFFFu, amax_key(v));
     const float db = fdiv(ffrom(amax), 127.0f);
     const float id = (fbits(db) & ~kSign) ? frecip(db) : 0.0f;
@@ -191,13 +155,8 @@ __device__ __forceinline__ void qact32_to_smem(const float* __restrict__ x, uint
     if (lane == 0) d[b] = h2f(f2h(db));
 }
 
-// QACT A256 of superblock s (tsr_ref.c:488-518), one warp; lane l holds values 8 l .. 8 l + 7.
-__device__ __forceinline__ void qact256_to_smem(const float* __restrict__ x, uint32_t s, uint32_t lane, uint8_t* q, float* d,
-                                                uint8_t* bs) {
-    const float* src = x + 256u * s + 8u * lane;
-    float v[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) v[i] = src[i];
+// QACT A256 of one superblock (tsr_ref.c:488-518), one warp; lane l holds values 8 l .. 8 l + 7.
+__device__ __forceinline__ void qact256_to_smem(const float (&v)[8], uint32_t s, uint32_t lane, uint8_t* q, float* d, uint8_t* bs) {
     uint32_t best = 0;
     float mine = 0.0f;
 #pragma unroll
@@ -243,17 +202,85 @@ __device__ __forceinline__ bool stage_qa(const MvArgs& a, const Qa& s, const Lay
     const uint32_t nb = L.blocks();
     if (tid == 0) *flag = 1u;
     if (a.x) {
-        for (uint32_t i = warp; i < T * nb; i += kCWarps) {
-            const uint32_t t = i / nb, b = i - t * nb;
-            const float* xt = a.x + (size_t)t * a.x_stride;
-            if (FMT == 0)
-                qact32_to_smem(xt, b, lane, s.q + (size_t)t * s.q_tok, reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(s.d) + (size_t)t * s.d_tok));
-            else
-                qact256_to_smem(xt, b, lane, s.q + (size_t)t * s.q_tok,
-                                reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(s.d) + (size_t)t * s.d_tok), s.bs + (size_t)t * s.bs_tok);
+        // each warp takes blocks i = warp + kCWarps j; the loads of a batch are all issued before
+        // any of them is used (one memory latency per batch, not per block)
+        if (FMT == 0) {
+            constexpr uint32_t B = 8;
+            for (uint32_t i0 = warp; i0 < T * nb; i0 += B * kCWarps) {
+                float v[B];
+#pragma unroll
+                for (uint32_t j = 0; j < B; ++j) {
+                    const uint32_t i = i0 + j * kCWarps;
+                    const uint32_t t = i / nb, b = i - t * nb;
+                    v[j] = i < T * nb ? a.x[(size_t)t * a.x_stride + 32u * b + lane] : 0.0f;
+                }
+#pragma unroll
+                for (uint32_t j = 0; j < B; ++j) {
+                    const uint32_t i = i0 + j * kCWarps;
+                    if (i < T * nb) {
+                        const uint32_t t = i / nb, b = i - t * nb;
+                        qact32_to_smem(v[j], b, lane, s.q + (size_t)t * s.q_tok,
+                                       reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(s.d) + (size_t)t * s.d_tok));
+                    }
+                }
+            }
+        } else {
+            constexpr uint32_t B = 2;
+            for (uint32_t i0 = warp; i0 < T * nb; i0 += B * kCWarps) {
+                float v[B][8];
+#pragma unroll
+                for (uint32_t j = 0; j < B; ++j) {
+                    const uint32_t i = i0 + j * kCWarps;
+                    const uint32_t t = i / nb, b = i - t * nb;
+                    const float* src = a.x + (size_t)t * a.x_stride + 256u * b + 8u * lane;
+                    if (i < T * nb && ((reinterpret_cast<uintptr_t>(src) & 15u) == 0)) {
+                        const float4 f0 = reinterpret_cast<const float4*>(src)[0], f1 = reinterpret_cast<const float4*>(src)[1];
+                        v[j][0] = f0.x; v[j][1] = f0.y; v[j][2] = f0.z; v[j][3] = f0.w;
+                        v[j][4] = f1.x; v[j][5] = f1.y; v[j][6] = f1.z; v[j][7] = f1.w;
+                    } else {
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) v[j][e] = i < T * nb ? src[e] : 0.0f;
+                    }
+                }
+#pragma unroll
+                for (uint32_t j = 0; j < B; ++j) {
+                    const uint32_t i = i0 + j * kCWarps;
+                    if (i < T * nb) {
+                        const uint32_t t = i / nb, b = i - t * nb;
+                        qact256_to_smem(v[j], b, lane, s.q + (size_t)t * s.q_tok,
+                                        reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(s.d) + (size_t)t * s.d_tok),
+                                        s.bs + (size_t)t * s.bs_tok);
+                    }
+                }
+            }
         }
     } else {
-        for (uint32_t i = tid; i < T * (K / 16u); i += kCWarps * 32u) {    // 16-byte chunks of q
+        // first batch: up to 4 chunks of q per thread, loaded before the arrive
+        constexpr uint32_t B = 4;
+        uint4 first[B];
+#pragma unroll
+        for (uint32_t j = 0; j < B; ++j) {
+            const uint32_t i = tid + j * kCWarps * 32u;
+            const uint32_t t = i / (K / 16u), c = i - t * (K / 16u);
+            first[j] = i < T * (K / 16u) ? reinterpret_cast<const uint4*>(a.qx + (size_t)t * K)[c] : make_uint4(0, 0, 0, 0);
+        }
+#pragma unroll
+        for (uint32_t j = 0; j < B; ++j) {
+            const uint32_t i = tid + j * kCWarps * 32u;
+            if (i < T * (K / 16u)) {
+                const uint32_t t = i / (K / 16u), c = i - t * (K / 16u);
+                uint32_t off;
+                if (FMT == 0) {
+                    const uint32_t b = c >> 1;
+                    off = (b >> 4) * 512u + 256u * (c & 1u) + 16u * (b & 15u);
+                } else {
+                    const uint32_t sb = c >> 4;
+                    off = (sb >> 4) * 4096u + 256u * (c & 15u) + 16u * (sb & 15u);
+                }
+                *reinterpret_cast<uint4*>(s.q + (size_t)t * s.q_tok + off) = first[j];
+            }
+        }
+        for (uint32_t i = tid + B * kCWarps * 32u; i < T * (K / 16u); i += kCWarps * 32u) {    // the rest
             const uint32_t t = i / (K / 16u), c = i - t * (K / 16u);
             const uint4 v = reinterpret_cast<const uint4*>(a.qx + (size_t)t * K)[c];
             uint32_t off;
@@ -291,25 +318,62 @@ __device__ __forceinline__ bool stage_qa(const MvArgs& a, const Qa& s, const Lay
     return *flag != 0u;
 }
 
-// ---- per-lane work on one stage -----------------------------------------------------------------
-// Q8_0: tiles [t0, t1) of the stage; row_q / row_m: this lane's row in the stage buffers.
-template <bool SAFE, int MAXT>
-__device__ __forceinline__ void q8_stage(const uint8_t* row_q, const uint8_t* row_m, const Qa& s, const Layout& L, uint32_t T,
-                                         uint32_t t0, uint32_t t1, bool whole, uint32_t k, float (&p)[MAXT], int32_t* isum_out) {
+// ---- per-lane units: loads into registers, then the math ----------------------------------------
+// Q8_0: a unit is up to 4 tiles of one row pair; per lane 2 x 16 B of quants and one fp16 scale
+// per tile. Q4_K: a unit is one tile; per lane its superblock's 8 x 16 B of quants and 16 B meta.
+constexpr uint32_t kQ8Tiles = 4;
+
+struct Q8Unit {
+    uint4 w[kQ8Tiles][2];
+    uint32_t d[kQ8Tiles];
+};
+struct Q4Unit {
+    uint4 w[8];
+    uint4 m;
+};
+
+__device__ __forceinline__ void load_unit(const MvArgs& a, const Layout& L, uint32_t row, bool rv, uint32_t t0, uint32_t k,
+                                          Q8Unit& u) {
     const uint32_t nb = L.blocks();
-    for (uint32_t t = t0; t < t1; ++t) {
-        const uint32_t b = 16u * t + k;
+    const uint8_t* meta = static_cast<const uint8_t*>(a.meta);
+#pragma unroll
+    for (uint32_t i = 0; i < kQ8Tiles; ++i) {
+        const uint32_t b = 16u * (t0 + i) + k;
+        if (rv && b < nb) {
+            const uint8_t* q = a.qs + L.qs_off(row, b, 0);
+            u.w[i][0] = ld_stream(q);
+            u.w[i][1] = ld_stream(q + 16u * L.tile_blocks(t0 + i));
+            u.d[i] = __ldg(reinterpret_cast<const uint16_t*>(meta + L.meta_off(row, b)));
+        }
+    }
+}
+
+__device__ __forceinline__ void load_unit(const MvArgs& a, const Layout& L, uint32_t row, bool rv, uint32_t t0, uint32_t k,
+                                          Q4Unit& u) {
+    const uint32_t sb = 16u * t0 + k;
+    if (rv && sb < L.blocks()) {
+        const uint8_t* q = a.qs + L.qs_off(row, sb, 0);
+        const uint32_t cs = 16u * L.tile_blocks(t0);
+#pragma unroll
+        for (uint32_t j = 0; j < 8; ++j) u.w[j] = ld_stream(q + (size_t)j * cs);
+        u.m = __ldg(reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(a.meta) + L.meta_off(row, sb)));
+    }
+}
+
+template <bool SAFE, int MAXT>
+__device__ __forceinline__ void compute_unit(const Q8Unit& u, const Qa& s, const Layout& L, uint32_t T, uint32_t t0, uint32_t k,
+                                             float (&p)[MAXT], int32_t* isum_out) {
+    const uint32_t nb = L.blocks();
+#pragma unroll
+    for (uint32_t i = 0; i < kQ8Tiles; ++i) {
+        const uint32_t t = t0 + i, b = 16u * t + k;
         if (b >= nb) break;
-        const uint32_t tl = whole ? t : t - t0;              // tile index inside the stage row
-        const uint32_t nv = L.tile_blocks(t);
-        const uint8_t* wq = row_q + (size_t)tl * 512u + 16u * k;
-        const uint4 w0 = lds<uint4>(wq), w1 = lds<uint4>(wq + 16u * nv);
-        const float dw = h2f(lds<uint16_t>(row_m + 2u * (16u * tl + k)));
+        const float dw = h2f((uint16_t)u.d[i]);
 #pragma unroll
         for (int tok = 0; tok < MAXT; ++tok) {
             if (tok < (int)T) {
                 const uint8_t* xq = s.q + (size_t)tok * s.q_tok + (size_t)t * 512u + 16u * k;
-                const int32_t isum = dot16s(w1, lds<uint4>(xq + 256u), dot16s(w0, lds<uint4>(xq), 0));
+                const int32_t isum = dot16s(u.w[i][1], lds<uint4>(xq + 256u), dot16s(u.w[i][0], lds<uint4>(xq), 0));
                 if (isum_out && tok == 0) isum_out[b] = isum;
                 const float Dx = reinterpret_cast<const float*>(reinterpret_cast<const uint8_t*>(s.d) + (size_t)tok * s.d_tok)[b];
                 p[tok] = add_<SAFE>(p[tok], mul_<SAFE>(mul_<SAFE>(dw, Dx), i2f(isum)));
@@ -318,179 +382,114 @@ __device__ __forceinline__ void q8_stage(const uint8_t* row_q, const uint8_t* ro
     }
 }
 
-// Q4_K: tile t of the stage (one per stage unless whole rows, then all tiles t0 .. t1).
 template <bool SAFE, int MAXT>
-__device__ __forceinline__ void q4_stage(const uint8_t* row_q, const uint8_t* row_m, const Qa& s, const Layout& L, uint32_t T,
-                                         uint32_t t0, uint32_t t1, bool whole, uint32_t k, float (&p)[MAXT], int32_t* isum_out) {
-    const uint32_t nsb = L.blocks();
-    for (uint32_t t = t0; t < t1; ++t) {
-        const uint32_t sb = 16u * t + k;
-        if (sb >= nsb) break;
-        const uint32_t tl = whole ? t : t - t0;
-        const uint32_t cs = 16u * L.tile_blocks(t);          // chunk stride in this tile
-        const uint8_t* wq = row_q + (size_t)tl * 2048u + 16u * k;
-        uint4 w[8];
+__device__ __forceinline__ void compute_unit(const Q4Unit& u, const Qa& s, const Layout& L, uint32_t T, uint32_t t0, uint32_t k,
+                                             float (&p)[MAXT], int32_t* isum_out) {
+    const uint32_t nsb = L.blocks(), t = t0, sb = 16u * t + k;
+    if (sb >= nsb) return;
+    const uint32_t sc_lo = u.m.y & 0x3F3F3F3Fu, mn_lo = u.m.z & 0x3F3F3F3Fu;
+    const uint32_t sc_hi = (u.m.w & 0x0F0F0F0Fu) | ((u.m.y >> 2) & 0x30303030u);
+    const uint32_t mn_hi = ((u.m.w >> 4) & 0x0F0F0F0Fu) | ((u.m.z >> 2) & 0x30303030u);
+    const float dw = h2f((uint16_t)(u.m.x & 0xFFFFu)), dmw = h2f((uint16_t)(u.m.x >> 16));
 #pragma unroll
-        for (int j = 0; j < 8; ++j) w[j] = lds<uint4>(wq + (size_t)j * cs);
-        const uint4 m = lds<uint4>(row_m + 16u * (16u * tl + k));
-        const uint32_t sc_lo = m.y & 0x3F3F3F3Fu, mn_lo = m.z & 0x3F3F3F3Fu;
-        const uint32_t sc_hi = (m.w & 0x0F0F0F0Fu) | ((m.y >> 2) & 0x30303030u);
-        const uint32_t mn_hi = ((m.w >> 4) & 0x0F0F0F0Fu) | ((m.z >> 2) & 0x30303030u);
-        const float dw = h2f((uint16_t)(m.x & 0xFFFFu)), dmw = h2f((uint16_t)(m.x >> 16));
+    for (int tok = 0; tok < MAXT; ++tok) {
+        if (tok < (int)T) {
+            const uint8_t* xq = s.q + (size_t)tok * s.q_tok + (size_t)t * 4096u + 16u * k;
+            int32_t S[8];
 #pragma unroll
-        for (int tok = 0; tok < MAXT; ++tok) {
-            if (tok < (int)T) {
-                const uint8_t* xq = s.q + (size_t)tok * s.q_tok + (size_t)t * 4096u + 16u * k;
-                int32_t S[8];
-#pragma unroll
-                for (int c = 0; c < 4; ++c) {      // qs bytes 32c .. 32c+31 = chunks 2c, 2c+1
-                    const uint4 a0 = w[2 * c], a1 = w[2 * c + 1];
-                    const uint4 l0 = make_uint4(a0.x & 0x0F0F0F0Fu, a0.y & 0x0F0F0F0Fu, a0.z & 0x0F0F0F0Fu, a0.w & 0x0F0F0F0Fu);
-                    const uint4 l1 = make_uint4(a1.x & 0x0F0F0F0Fu, a1.y & 0x0F0F0F0Fu, a1.z & 0x0F0F0F0Fu, a1.w & 0x0F0F0F0Fu);
-                    const uint4 h0 = make_uint4(a0.x & 0xF0F0F0F0u, a0.y & 0xF0F0F0F0u, a0.z & 0xF0F0F0F0u, a0.w & 0xF0F0F0F0u);
-                    const uint4 h1 = make_uint4(a1.x & 0xF0F0F0F0u, a1.y & 0xF0F0F0F0u, a1.z & 0xF0F0F0F0u, a1.w & 0xF0F0F0F0u);
-                    S[2 * c] = dot16s(l1, lds<uint4>(xq + 256u * (4 * c + 1)), dot16s(l0, lds<uint4>(xq + 256u * (4 * c)), 0));
-                    S[2 * c + 1] =
-                        dot16us(h1, lds<uint4>(xq + 256u * (4 * c + 3)), dot16us(h0, lds<uint4>(xq + 256u * (4 * c + 2)), 0)) >> 4;
-                }
-                int32_t isum = 0;
-#pragma unroll
-                for (uint32_t j = 0; j < 4; ++j) isum += ubyte(sc_lo, j) * S[j] + ubyte(sc_hi, j) * S[4 + j];
-                const uint4 B = lds<uint4>(s.bs + (size_t)tok * s.bs_tok + (size_t)t * 256u + 16u * k);
-                const int32_t msum = dp2a_hi(B.w, mn_hi, dp2a_lo(B.z, mn_hi, dp2a_hi(B.y, mn_lo, dp2a_lo(B.x, mn_lo, 0))));
-                if (isum_out && tok == 0) {
-                    isum_out[2u * sb] = isum;
-                    isum_out[2u * sb + 1u] = msum;
-                }
-                const float Dx = reinterpret_cast<const float*>(reinterpret_cast<const uint8_t*>(s.d) + (size_t)tok * s.d_tok)[sb];
-                const float t1v = mul_<SAFE>(mul_<SAFE>(dw, Dx), i2f(isum));
-                const float t2v = mul_<SAFE>(mul_<SAFE>(dmw, Dx), i2f(msum));
-                p[tok] = add_<SAFE>(p[tok], sub_<SAFE>(t1v, t2v));
+            for (int c = 0; c < 4; ++c) {          // qs bytes 32c .. 32c+31 = chunks 2c, 2c+1
+                const uint4 a0 = u.w[2 * c], a1 = u.w[2 * c + 1];
+                const uint4 l0 = make_uint4(a0.x & 0x0F0F0F0Fu, a0.y & 0x0F0F0F0Fu, a0.z & 0x0F0F0F0Fu, a0.w & 0x0F0F0F0Fu);
+                const uint4 l1 = make_uint4(a1.x & 0x0F0F0F0Fu, a1.y & 0x0F0F0F0Fu, a1.z & 0x0F0F0F0Fu, a1.w & 0x0F0F0F0Fu);
+                const uint4 h0 = make_uint4(a0.x & 0xF0F0F0F0u, a0.y & 0xF0F0F0F0u, a0.z & 0xF0F0F0F0u, a0.w & 0xF0F0F0F0u);
+                const uint4 h1 = make_uint4(a1.x & 0xF0F0F0F0u, a1.y & 0xF0F0F0F0u, a1.z & 0xF0F0F0F0u, a1.w & 0xF0F0F0F0u);
+                S[2 * c] = dot16s(l1, lds<uint4>(xq + 256u * (4 * c + 1)), dot16s(l0, lds<uint4>(xq + 256u * (4 * c)), 0));
+                S[2 * c + 1] =
+                    dot16us(h1, lds<uint4>(xq + 256u * (4 * c + 3)), dot16us(h0, lds<uint4>(xq + 256u * (4 * c + 2)), 0)) >> 4;
             }
+            int32_t isum = 0;
+#pragma unroll
+            for (uint32_t j = 0; j < 4; ++j) isum += ubyte(sc_lo, j) * S[j] + ubyte(sc_hi, j) * S[4 + j];
+            const uint4 B = lds<uint4>(s.bs + (size_t)tok * s.bs_tok + (size_t)t * 256u + 16u * k);
+            const int32_t msum = dp2a_hi(B.w, mn_hi, dp2a_lo(B.z, mn_hi, dp2a_hi(B.y, mn_lo, dp2a_lo(B.x, mn_lo, 0))));
+            if (isum_out && tok == 0) {
+                isum_out[2u * sb] = isum;
+                isum_out[2u * sb + 1u] = msum;
+            }
+            const float Dx = reinterpret_cast<const float*>(reinterpret_cast<const uint8_t*>(s.d) + (size_t)tok * s.d_tok)[sb];
+            const float t1v = mul_<SAFE>(mul_<SAFE>(dw, Dx), i2f(isum));
+            const float t2v = mul_<SAFE>(mul_<SAFE>(dmw, Dx), i2f(msum));
+            p[tok] = add_<SAFE>(p[tok], sub_<SAFE>(t1v, t2v));
         }
     }
 }
 
 // ---- the kernel ---------------------------------------------------------------------------------
 template <int FMT, int MAXT>
-__global__ void __launch_bounds__(kThreads, 2) matvec_kernel(MvArgs a, Plan P, uint32_t rows_per_cta) {
+__global__ void __launch_bounds__(kThreads, 1) matvec_kernel(MvArgs a, Plan P, uint32_t rows_per_cta) {
     extern __shared__ __align__(128) uint8_t smem[];
     const Layout L{(uint32_t)FMT, a.K};
     const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31u;
     const uint32_t r_begin = blockIdx.x * rows_per_cta;
     const uint32_t r_end = min(a.n_rows, r_begin + rows_per_cta);
     if (r_begin >= r_end) return;
-    const uint32_t tiles = L.tiles();
-    const uint32_t n_ranges = P.whole ? 1u : (tiles + P.tps - 1u) / P.tps;
-    const uint32_t n_groups = (r_end - r_begin + kStageRows - 1u) / kStageRows;
-    const uint32_t n_stages = n_groups * n_ranges;
-    const uint32_t NS = P.stages;
+    using Unit = typename std::conditional<FMT == 0, Q8Unit, Q4Unit>::type;
+    constexpr uint32_t TPU = FMT == 0 ? kQ8Tiles : 1u;      // tiles per unit
+    const uint32_t units = (L.tiles() + TPU - 1u) / TPU;
 
-    uint8_t* ring = smem;
+    // weights of this CTA: HBM -> L2 now (read-only data: safe before the previous kernel ends);
+    // the lanes of warp 0 issue the chunks in parallel, quants then meta
+    if (warp == 0) {
+        const uint8_t* q0 = a.qs + (size_t)r_begin * L.qs_row_bytes();
+        const uint8_t* m0 = static_cast<const uint8_t*>(a.meta) + (size_t)r_begin * L.meta_row_bytes();
+        const size_t qb = (size_t)(r_end - r_begin) * L.qs_row_bytes(), mb = (size_t)(r_end - r_begin) * L.meta_row_bytes();
+        const size_t nq = (qb + kPrefetchChunk - 1u) / kPrefetchChunk, nm = (mb + kPrefetchChunk - 1u) / kPrefetchChunk;
+        for (size_t c = lane; c < nq + nm; c += 32u) {
+            const bool isq = c < nq;
+            const size_t off = (isq ? c : c - nq) * kPrefetchChunk, tot = isq ? qb : mb;
+            prefetch_l2((isq ? q0 : m0) + off, (uint32_t)(tot - off < kPrefetchChunk ? tot - off : kPrefetchChunk));
+        }
+    }
+    asm volatile("griddepcontrol.launch_dependents;");
+    const uint32_t k = lane & 15u, half = lane >> 4;
+    const uint32_t n_pairs = (r_end - r_begin + 1u) / 2u;
+
+    // the activation (after the previous kernel on the stream has completed); no weight load is
+    // issued before it, so the activation's loads do not queue behind them
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     Qa qa;
-    qa.q = smem + P.ring_bytes();
+    qa.q = smem;
     qa.q_tok = P.qa_q;
-    qa.d = reinterpret_cast<float*>(qa.q + (size_t)a.T * P.qa_q);
+    qa.d = reinterpret_cast<float*>(smem + (size_t)a.T * P.qa_q);
     qa.d_tok = P.qa_d;
     qa.bs = reinterpret_cast<uint8_t*>(qa.d) + (size_t)a.T * P.qa_d;
     qa.bs_tok = P.qa_bs;
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + P.ring_bytes() + a16(P.qa_bytes(a.T)));
-    uint64_t* empty = full + kMaxStages;
-    uint32_t* flag = reinterpret_cast<uint32_t*>(empty + kMaxStages);
-
-    if (tid == 0) {
-        for (uint32_t s = 0; s < NS; ++s) {
-            mbar_init(&full[s], 1u);
-            mbar_init(&empty[s], kCWarps);
-        }
-        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    }
-    __syncthreads();
-
-    if (warp == kCWarps) {
-        // ===== producer: stages of 16 rows x a tile range into the ring (weights only) =====
-        uint32_t issued = 0;
-        bool ok = true;
-        for (uint32_t i = 0; i < n_stages && ok; ++i) {
-            const uint32_t s = i % NS;
-            if (i >= NS) ok = mbar_wait(&empty[s], ((i / NS) - 1u) & 1u, kErrProducerWait);
-            ok = __all_sync(0xFFFFFFFFu, ok);
-            if (!ok) break;
-            const uint32_t g = i / n_ranges, rng = i - g * n_ranges;
-            const uint32_t ra = r_begin + g * kStageRows, nr = min(kStageRows, r_end - ra);
-            uint8_t* sq = ring + (size_t)s * (P.stage_q + P.stage_m);
-            uint8_t* sm = sq + P.stage_q;
-            uint32_t qb, mb, bytes;
-            size_t qoff, moff;
-            if (P.whole) {
-                qb = nr * (uint32_t)L.qs_row_bytes();
-                mb = nr * (uint32_t)L.meta_row_bytes();
-                bytes = qb + mb;
-                qoff = (size_t)ra * L.qs_row_bytes();
-                moff = (size_t)ra * L.meta_row_bytes();
-            } else {
-                const uint32_t t0 = rng * P.tps, t1 = min(tiles, t0 + P.tps);
-                const uint32_t b0 = 16u * t0, b1 = min(L.blocks(), 16u * t1);
-                qb = (b1 - b0) * L.block_qs_bytes();
-                mb = (uint32_t)a16((size_t)(b1 - b0) * L.meta_entry_bytes());
-                bytes = nr * (qb + mb);
-                qoff = (size_t)t0 * 16u * L.block_qs_bytes();
-                moff = (size_t)b0 * L.meta_entry_bytes();
-            }
-            if (lane == 0) mbar_expect_tx(&full[s], bytes);
-            __syncwarp();
-            if (P.whole) {
-                if (lane == 0) bulk_g2s(sq, a.qs + qoff, qb, &full[s]);
-                if (lane == 1) bulk_g2s(sm, static_cast<const uint8_t*>(a.meta) + moff, mb, &full[s]);
-            } else {
-                if (lane < nr)
-                    bulk_g2s(sq + (size_t)lane * P.pitch_q, a.qs + (size_t)(ra + lane) * L.qs_row_bytes() + qoff, qb, &full[s]);
-                if (lane >= 16u && lane - 16u < nr)
-                    bulk_g2s(sm + (size_t)(lane - 16u) * P.pitch_m,
-                             static_cast<const uint8_t*>(a.meta) + (size_t)(ra + lane - 16u) * L.meta_row_bytes() + moff, mb, &full[s]);
-            }
-            issued = i + 1;
-        }
-        // drain: no copy of this CTA may still be in flight when it exits
-        if (lane == 0) {
-            const uint32_t first = issued > NS ? issued - NS : 0u;
-            for (uint32_t i = first; i < issued; ++i)
-                if (!mbar_wait(&full[i % NS], (i / NS) & 1u, kErrDrain)) break;
-        }
-        return;
-    }
-
-    // ===== consumers =====
-    asm volatile("griddepcontrol.wait;" ::: "memory");   // the activation is ready
+    uint32_t* flag = reinterpret_cast<uint32_t*>(smem + a16(P.qa_bytes(a.T)));
     const bool safe = stage_qa<FMT>(a, qa, L, flag);
-    const uint32_t k = lane & 15u, half = lane >> 4;
-    const uint32_t row_local = 2u * warp + half;
+    uint32_t pair = warp, ui = 0;
+    if (pair >= n_pairs) return;
+    Unit cur;
+    load_unit(a, L, r_begin + 2u * pair + half, r_begin + 2u * pair + half < r_end, 0, k, cur);
+
     float p[MAXT];
 #pragma unroll
     for (int t = 0; t < MAXT; ++t) p[t] = 0.0f;
-    for (uint32_t i = 0; i < n_stages; ++i) {
-        const uint32_t s = i % NS;
-        if (!__all_sync(0xFFFFFFFFu, mbar_wait(&full[s], (i / NS) & 1u, kErrConsumerWait))) break;
-        const uint32_t g = i / n_ranges, rng = i - g * n_ranges;
-        const uint32_t row = r_begin + g * kStageRows + row_local;
+    while (pair < n_pairs) {
+        const uint32_t row = r_begin + 2u * pair + half;
         const bool rv = row < r_end;
-        const uint32_t t0 = P.whole ? 0u : rng * P.tps, t1 = P.whole ? tiles : min(tiles, t0 + P.tps);
-        const uint8_t* sq = ring + (size_t)s * (P.stage_q + P.stage_m);
-        const uint8_t* row_q = sq + (size_t)row_local * P.pitch_q;
-        const uint8_t* row_m = sq + P.stage_q + (size_t)row_local * P.pitch_m;
-        int32_t* isum_out = (a.isum_out && rv) ? a.isum_out + (size_t)row * L.blocks() * (FMT == 0 ? 1u : 2u) : nullptr;
-        if (rv) {
-            if constexpr (FMT == 0) {
-                if (safe) q8_stage<true, MAXT>(row_q, row_m, qa, L, a.T, t0, t1, P.whole, k, p, isum_out);
-                else q8_stage<false, MAXT>(row_q, row_m, qa, L, a.T, t0, t1, P.whole, k, p, isum_out);
-            } else {
-                if (safe) q4_stage<true, MAXT>(row_q, row_m, qa, L, a.T, t0, t1, P.whole, k, p, isum_out);
-                else q4_stage<false, MAXT>(row_q, row_m, qa, L, a.T, t0, t1, P.whole, k, p, isum_out);
-            }
+        uint32_t npair = pair, nui = ui + 1u;
+        if (nui == units) { npair = pair + kCWarps; nui = 0; }
+        Unit nxt;
+        {
+            const uint32_t nrow = r_begin + 2u * npair + half;
+            load_unit(a, L, nrow, npair < n_pairs && nrow < r_end, nui * TPU, k, nxt);
         }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[s]);
-        if (rng == n_ranges - 1u) {            // the row pair is complete: tree, epilogue, store
+        if (rv) {
+            int32_t* isum_out = a.isum_out ? a.isum_out + (size_t)row * L.blocks() * (FMT == 0 ? 1u : 2u) : nullptr;
+            if (safe) compute_unit<true, MAXT>(cur, qa, L, a.T, ui * TPU, k, p, isum_out);
+            else compute_unit<false, MAXT>(cur, qa, L, a.T, ui * TPU, k, p, isum_out);
+        }
+        if (nui == 0) {                // the pair is complete: tree, epilogue, store
 #pragma unroll
             for (int t = 0; t < MAXT; ++t) {
                 if (t < (int)a.T) {
@@ -500,22 +499,25 @@ __global__ void __launch_bounds__(kThreads, 2) matvec_kernel(MvArgs a, Plan P, u
                 p[t] = 0.0f;
             }
         }
+        pair = npair;
+        ui = nui;
+        cur = nxt;
     }
 }
 
 // ---- host side ------------------------------------------------------------------------------------
-constexpr size_t kSmemPerCta = 113u * 1024u;      // two CTAs per SM (228 KB per SM)
+size_t mv_smem_bytes(uint32_t fmt, uint32_t K, uint32_t T) { return make_plan(fmt, K).total(T); }
 
-size_t mv_smem_bytes(uint32_t fmt, uint32_t K, uint32_t T) { return make_plan(fmt, K, T, kSmemPerCta).total(T); }
-
-template <typename F>
-static cudaError_t allow_smem(F* kernel) {
+// One flag set per kernel instance and device (the template arguments make each instance's
+// statics distinct).
+template <int FMT, int MAXT>
+static cudaError_t allow_smem() {
     static int done_dev[64];
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
     if (dev < 64 && done_dev[dev] == dev + 1) return cudaSuccess;
-    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(200u * 1024u));
+    e = cudaFuncSetAttribute(matvec_kernel<FMT, MAXT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(200u * 1024u));
     if (e == cudaSuccess && dev < 64) done_dev[dev] = dev + 1;
     return e;
 }
@@ -524,9 +526,9 @@ static int g_num_sms[64];
 
 template <int FMT, int MAXT>
 static cudaError_t launch_t(const MvArgs& a, cudaStream_t st) {
-    const Plan P = make_plan(FMT, a.K, a.T, kSmemPerCta);
+    const Plan P = make_plan(FMT, a.K);
     const size_t smem = P.total(a.T);
-    cudaError_t e = allow_smem(matvec_kernel<FMT, MAXT>);
+    cudaError_t e = allow_smem<FMT, MAXT>();
     if (e != cudaSuccess) return e;
     int dev = 0;
     if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
@@ -536,8 +538,8 @@ static cudaError_t launch_t(const MvArgs& a, cudaStream_t st) {
         g_num_sms[dev] = n > 0 ? n : 148;
     }
     const uint32_t sms = dev < 64 ? (uint32_t)g_num_sms[dev] : 148u;
-    // contiguous row ranges of even length, two CTAs per SM
-    uint32_t rpc = (a.n_rows + 2u * sms - 1u) / (2u * sms);
+    // contiguous row ranges of even length, one CTA per SM
+    uint32_t rpc = (a.n_rows + sms - 1u) / sms;
     rpc = (rpc + 1u) & ~1u;
     const uint32_t blocks = (a.n_rows + rpc - 1u) / rpc;
     cudaLaunchConfig_t cfg = {};
