@@ -119,6 +119,20 @@ TSRC_API int tsrc_mvm(tsrc_ctx * ctx, const tsrc_weight * w, const int8_t * q, c
                       uint32_t T, float * y, uint32_t y_stride, const float * add, uint32_t add_stride, uint32_t flags,
                       float s0, float s1, void * stream);
 
+// tsrc_mul_mat for callers that cannot allocate device memory (no counterpart in the reference,
+// whose device memory is planned by the backend). Same arguments, results and errors as
+// tsrc_mul_mat, but the quantized activations live in a fixed 1 MiB array compiled into this
+// library (present on every device that loads it until the process exits) instead of a scratch
+// buffer the context allocates: the call itself allocates nothing. The image of one token of K
+// values takes about 1.2 K bytes, so K up to 65536 works for any T (tokens are processed at most
+// 8 at a time); a larger image is refused with TSRC_E_SHAPE. The first call on a device looks up
+// the array's device address (cudaGetSymbolAddress): make it before any stream capture. All calls
+// share the array: calls that may run at the same time on one device (other streams, other
+// contexts) race and must be serialised by the caller; calls queued on one stream are ordered.
+TSRC_API int tsrc_mul_mat_noalloc(tsrc_ctx * ctx, const tsrc_weight * w, const float * x, uint32_t T, uint32_t x_stride,
+                                  float * y, uint32_t y_stride, const float * add, uint32_t add_stride, uint32_t flags,
+                                  float s0, float s1, void * stream);
+
 // Why a MUL_MAT of this weight shape could not run here (NULL if it can): the B200 counterpart of
 // the MUL_MAT branch of supports_op (ggml-tesseract.cpp:4199-4299).
 TSRC_API const char * tsrc_mul_mat_unsupported(uint32_t fmt, uint64_t N, uint64_t K, uint64_t T);

@@ -151,6 +151,46 @@ void drop_weight(tsrc_weight* w) {
 
 }  // namespace
 
+namespace tsrc {
+
+int set_error(int code, const char* msg) { return fail(code, "%s", msg); }
+
+// The argument checks of a MUL_MAT call (the same rules as tsrc_mul_mat) and the per-call launch
+// fields; for entry points that run the kernels with their own activation scratch.
+int mm_check(tsrc_ctx* ctx, const tsrc_weight* w, const float* x, uint32_t T, uint32_t* x_stride, float* y, uint32_t* y_stride,
+             const float* add, uint32_t add_stride, uint32_t flags, float s0, float s1, MvArgs* base, uint32_t* fmt,
+             const char* who) {
+    if (!ctx || !w || !x || !y) return fail(TSRC_E_ARG, "%s: NULL argument", who);
+    if (w->ctx != ctx) return fail(TSRC_E_ARG, "%s: the weight belongs to another context", who);
+    if (flags & ~(TSRC_MM_ADD | TSRC_MM_SCALE | TSRC_MM_SOFTCAP)) return fail(TSRC_E_ARG, "%s: undefined flag bits 0x%x", who, flags);
+    if ((flags & TSRC_MM_ADD) && (flags & (TSRC_MM_SCALE | TSRC_MM_SOFTCAP)))
+        return fail(TSRC_E_ARG, "%s: an addend cannot be combined with SCALE or SOFTCAP", who);
+    if ((flags & TSRC_MM_SCALE) && (flags & TSRC_MM_SOFTCAP)) return fail(TSRC_E_ARG, "%s: SCALE and SOFTCAP are exclusive", who);
+    if ((flags & TSRC_MM_ADD) && !add) return fail(TSRC_E_ARG, "%s: TSRC_MM_ADD without an addend", who);
+    if (*x_stride == 0) *x_stride = w->K;
+    if (*y_stride == 0) *y_stride = w->n_rows;
+    if (*x_stride < w->K || *y_stride < w->n_rows) return fail(TSRC_E_ARG, "%s: a stride is shorter than its row", who);
+    if ((flags & TSRC_MM_ADD) && add_stride != 0 && add_stride < w->n_rows) return fail(TSRC_E_ARG, "%s: addend stride", who);
+    (void)T;
+    int rc = use_device(ctx);
+    if (rc) return rc;
+    *fmt = w->fmt;
+    MvArgs a{};
+    a.qs = w->qs;
+    a.meta = w->meta;
+    a.n_rows = w->n_rows;
+    a.K = w->K;
+    a.y_stride = *y_stride;
+    a.add_stride = add_stride;
+    a.flags = flags;
+    a.s0 = daz_host(s0);
+    a.s1 = daz_host(s1);
+    *base = a;
+    return TSRC_OK;
+}
+
+}  // namespace tsrc
+
 extern "C" {
 
 const char* tsrc_last_error(void) { return g_err.c_str(); }

@@ -52,6 +52,7 @@ _SIGS = {
     "tsrc_weight_info": (_i, [_p] + [ct.POINTER(_u32)] * 5 + [ct.POINTER(_u64)]),
     "tsrc_weight_free": (_i, [_p]),
     "tsrc_mul_mat": (_i, [_p, _p, _p, _u32, _u32, _p, _u32, _p, _u32, _u32, _f32, _f32, _p]),
+    "tsrc_mul_mat_noalloc": (_i, [_p, _p, _p, _u32, _u32, _p, _u32, _p, _u32, _u32, _f32, _f32, _p]),
     "tsrc_mvm": (_i, [_p, _p, _p, _p, _p, _u32, _p, _u32, _p, _u32, _u32, _f32, _f32, _p]),
     "tsrc_mul_mat_unsupported": (ct.c_char_p, [_u32, _u64, _u64, _u64]),
     "tsrc_qact": (_i, [_p, _u32, _p, _u32, _u32, _u32, _p, _p, _p, _p]),
@@ -186,6 +187,20 @@ class Device:
                 add_stride = 0 if (len(add.shape) == 1 or add.shape[0] == 1) else w.n_rows
         _check(lib().tsrc_mul_mat(self.handle, w.handle, _addr(x), T, x_stride, _addr(y), y_stride, _addr(add),
                                   add_stride or 0, flags, s0, s1, _stream(stream)))
+
+    def mul_mat_noalloc(self, w: "Weight", x, y, T: int | None = None, add=None, add_stride: int | None = None,
+                        flags: int = 0, s0: float = 1.0, s1: float = 1.0, x_stride: int = 0, y_stride: int = 0,
+                        stream=None) -> None:
+        """mul_mat without any device allocation by the library (its scratch is a fixed array in the
+        library's device image); for hosts that plan all device memory themselves."""
+        if T is None:
+            T = 1 if len(x.shape) == 1 else x.shape[0]
+        if add is not None:
+            flags |= MM_ADD
+            if add_stride is None:
+                add_stride = 0 if (len(add.shape) == 1 or add.shape[0] == 1) else w.n_rows
+        _check(lib().tsrc_mul_mat_noalloc(self.handle, w.handle, _addr(x), T, x_stride, _addr(y), y_stride, _addr(add),
+                                          add_stride or 0, flags, s0, s1, _stream(stream)))
 
     def mvm(self, w: "Weight", q, d, bs, y, T: int = 1, add=None, add_stride: int = 0, flags: int = 0,
             s0: float = 1.0, s1: float = 1.0, y_stride: int = 0, stream=None) -> None:
