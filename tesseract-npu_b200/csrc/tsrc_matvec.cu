@@ -36,8 +36,15 @@
 
 namespace tsrc {
 
-constexpr uint32_t kCWarps = 16;                    // warps per CTA (one CTA per SM)
+#ifndef TSRC_MV_WARPS
+#define TSRC_MV_WARPS 16
+#endif
+// Warps per CTA. 16 warps, one CTA per SM: the bytes a warp keeps in flight from L2 (one unit
+// ahead) bound the stream rate, so more warps per SM beat co-residency of two launches (8 warps,
+// two CTAs an SM, measured 1.37x slower on the Q4_K 14336 x 4096 launch).
+constexpr uint32_t kCWarps = TSRC_MV_WARPS;
 constexpr uint32_t kThreads = kCWarps * 32;
+constexpr int kCtasPerSm = kCWarps <= 8 ? 2 : 1;
 constexpr uint32_t kSafeDx = 0x18000000u;           // 2^-79
 constexpr uint32_t kPrefetchChunk = 64u * 1024u;    // bytes per L2 prefetch instruction
 
@@ -134,7 +141,7 @@ __host__ __device__ constexpr size_t a16(size_t n) { return (n + 15u) & ~(size_t
 struct Plan {                          // shared-memory plan of one launch (host and device agree)
     uint32_t qa_q, qa_d, qa_bs;        // per-token bytes of the activation image
     __host__ __device__ size_t qa_bytes(uint32_t T) const { return (size_t)T * (qa_q + qa_d + qa_bs); }
-    __host__ __device__ size_t total(uint32_t T) const { return a16(qa_bytes(T)) + 16u; }
+    __host__ __device__ size_t total(uint32_t T) const { return a16(qa_bytes(T)) + 4u * kCWarps; }   // + a flag per warp
 };
 
 __host__ __device__ inline Plan make_plan(uint32_t fmt, uint32_t K) {
@@ -147,16 +154,21 @@ __host__ __device__ inline Plan make_plan(uint32_t fmt, uint32_t K) {
 }
 
 // QACT A32 of one block (tsr_ref.c:472-487), one warp; v = the lane's value.
-__device__ __forceinline__ void qact32_to_smem(float v, uint32_t b, uint32_t lane, uint8_t* q, float* d) {
+// Returns (uniform over the warp) whether the stored scale is 0 or >= 2^-79.
+__device__ __forceinline__ bool qact32_to_smem(float v, uint32_t b, uint32_t lane, uint8_t* q, float* d) {
     const uint32_t amax = __reduce_max_sync(0xFFFFFFFFu, amax_key(v));
     const float db = fdiv(ffrom(amax), 127.0f);
     const float id = (fbits(db) & ~kSign) ? frecip(db) : 0.0f;
-    q[(b >> 4) * 512u + 256u * (lane >> 4) + 16u * (b & 15u) + (lane & 15u)] = (uint8_t)round_sat8(fmul(daz(v), id), false);
-    if (lane == 0) d[b] = h2f(f2h(db));
+    q[(b >> 4) * 512u + 256u * (lane >> 4) + 16u * (b & 15u) + (lane & 15u)] = (uint8_t)round_away_sat8(fmul(daz(v), id));
+    const float ds = h2f(f2h(db));
+    if (lane == 0) d[b] = ds;
+    const uint32_t u = fbits(ds) & ~kSign;
+    return u == 0u || u >= kSafeDx;
 }
 
 // QACT A256 of one superblock (tsr_ref.c:488-518), one warp; lane l holds values 8 l .. 8 l + 7.
-__device__ __forceinline__ void qact256_to_smem(const float (&v)[8], uint32_t s, uint32_t lane, uint8_t* q, float* d, uint8_t* bs) {
+// Returns (uniform over the warp) whether the stored scale is 0 or >= 2^-79.
+__device__ __forceinline__ bool qact256_to_smem(const float (&v)[8], uint32_t s, uint32_t lane, uint8_t* q, float* d, uint8_t* bs) {
     uint32_t best = 0;
     float mine = 0.0f;
 #pragma unroll
@@ -172,7 +184,7 @@ __device__ __forceinline__ void qact256_to_smem(const float (&v)[8], uint32_t s,
     if (amax != 0u) {
         const float iscale = fdiv(-127.0f, mx);
 #pragma unroll
-        for (int i = 0; i < 8; ++i) qv[i] = round_sat8(fmul(iscale, daz(v[i])), true);
+        for (int i = 0; i < 8; ++i) qv[i] = round_even_sat8(fmul(iscale, daz(v[i])));
         db = frecip(iscale);
     } else {
 #pragma unroll
@@ -192,15 +204,18 @@ __device__ __forceinline__ void qact256_to_smem(const float (&v)[8], uint32_t s,
     if ((lane & 3u) == 0)
         *reinterpret_cast<int16_t*>(bs + (s >> 4) * 256u + 16u * (s & 15u) + 2u * (lane >> 2)) = (int16_t)sum;
     if (lane == 0) d[s] = db;
+    const uint32_t u = fbits(db) & ~kSign;
+    return u == 0u || u >= kSafeDx;
 }
 
-// Fills the activation image (consumer threads only). Returns (uniform over the consumers)
-// whether every nonzero scale is >= 2^-79.
+// Fills the activation image. Returns (uniform over the CTA) whether every nonzero scale is
+// >= 2^-79: each warp writes its own verdict to flags[warp] before the one barrier, and every
+// thread reads all of them after it.
 template <int FMT>
-__device__ __forceinline__ bool stage_qa(const MvArgs& a, const Qa& s, const Layout& L, uint32_t* flag) {
+__device__ __forceinline__ bool stage_qa(const MvArgs& a, const Qa& s, const Layout& L, uint32_t* flags) {
     const uint32_t K = a.K, T = a.T, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31u;
     const uint32_t nb = L.blocks();
-    if (tid == 0) *flag = 1u;
+    bool ok = true;
     if (a.x) {
         // each warp takes blocks i = warp + kCWarps j; the loads of a batch are all issued before
         // any of them is used (one memory latency per batch, not per block)
@@ -219,8 +234,8 @@ __device__ __forceinline__ bool stage_qa(const MvArgs& a, const Qa& s, const Lay
                     const uint32_t i = i0 + j * kCWarps;
                     if (i < T * nb) {
                         const uint32_t t = i / nb, b = i - t * nb;
-                        qact32_to_smem(v[j], b, lane, s.q + (size_t)t * s.q_tok,
-                                       reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(s.d) + (size_t)t * s.d_tok));
+                        ok &= qact32_to_smem(v[j], b, lane, s.q + (size_t)t * s.q_tok,
+                                             reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(s.d) + (size_t)t * s.d_tok));
                     }
                 }
             }
@@ -247,9 +262,9 @@ __device__ __forceinline__ bool stage_qa(const MvArgs& a, const Qa& s, const Lay
                     const uint32_t i = i0 + j * kCWarps;
                     if (i < T * nb) {
                         const uint32_t t = i / nb, b = i - t * nb;
-                        qact256_to_smem(v[j], b, lane, s.q + (size_t)t * s.q_tok,
-                                        reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(s.d) + (size_t)t * s.d_tok),
-                                        s.bs + (size_t)t * s.bs_tok);
+                        ok &= qact256_to_smem(v[j], b, lane, s.q + (size_t)t * s.q_tok,
+                                              reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(s.d) + (size_t)t * s.d_tok),
+                                              s.bs + (size_t)t * s.bs_tok);
                     }
                 }
             }
@@ -295,7 +310,10 @@ __device__ __forceinline__ bool stage_qa(const MvArgs& a, const Qa& s, const Lay
         }
         for (uint32_t i = tid; i < T * nb; i += kCWarps * 32u) {
             const uint32_t t = i / nb, b = i - t * nb;
-            reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(s.d) + (size_t)t * s.d_tok)[b] = a.dx[i];
+            const float dv = a.dx[i];
+            reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(s.d) + (size_t)t * s.d_tok)[b] = dv;
+            const uint32_t u = fbits(dv) & ~kSign;
+            ok = ok && (u == 0u || u >= kSafeDx);
         }
         if (FMT == 1) {
             for (uint32_t i = tid; i < T * nb * 8u; i += kCWarps * 32u) {
@@ -306,21 +324,23 @@ __device__ __forceinline__ bool stage_qa(const MvArgs& a, const Qa& s, const Lay
             }
         }
     }
+    const uint32_t bad = __any_sync(0xFFFFFFFFu, !ok);
+    if (lane == 0) flags[warp] = bad;
     consumer_sync();
-    bool ok = true;
-    for (uint32_t i = tid; i < T * nb; i += kCWarps * 32u) {
-        const uint32_t t = i / nb, b = i - t * nb;
-        const uint32_t u = fbits(reinterpret_cast<const float*>(reinterpret_cast<const uint8_t*>(s.d) + (size_t)t * s.d_tok)[b]) & ~kSign;
-        ok = ok && (u == 0u || u >= kSafeDx);
+    uint32_t any = 0;
+#pragma unroll
+    for (uint32_t w = 0; w < kCWarps; w += 4) {
+        const uint4 f = *reinterpret_cast<const uint4*>(flags + w);
+        any |= f.x | f.y | f.z | f.w;
     }
-    if (!ok) atomicAnd(flag, 0u);
-    consumer_sync();
-    return *flag != 0u;
+    return any == 0u;
 }
 
 // ---- per-lane units: loads into registers, then the math ----------------------------------------
 // Q8_0: a unit is up to 4 tiles of one row pair; per lane 2 x 16 B of quants and one fp16 scale
 // per tile. Q4_K: a unit is one tile; per lane its superblock's 8 x 16 B of quants and 16 B meta.
+// A lane's pointers qp / mp address its block k of tile 0 of its row (row base + 16 k, + 2 k or
+// 16 k in the meta row); tile t adds t x the tile's bytes, and a full tile's chunks are 256 B apart.
 constexpr uint32_t kQ8Tiles = 4;
 
 struct Q8Unit {
@@ -332,38 +352,40 @@ struct Q4Unit {
     uint4 m;
 };
 
-__device__ __forceinline__ void load_unit(const MvArgs& a, const Layout& L, uint32_t row, bool rv, uint32_t t0, uint32_t k,
-                                          Q8Unit& u) {
-    const uint32_t nb = L.blocks();
-    const uint8_t* meta = static_cast<const uint8_t*>(a.meta);
+__device__ __forceinline__ void load_unit(const uint8_t* qp, const uint8_t* mp, uint32_t nb, uint32_t t0, uint32_t k, Q8Unit& u) {
 #pragma unroll
     for (uint32_t i = 0; i < kQ8Tiles; ++i) {
-        const uint32_t b = 16u * (t0 + i) + k;
-        if (rv && b < nb) {
-            const uint8_t* q = a.qs + L.qs_off(row, b, 0);
+        const uint32_t t = t0 + i, b = 16u * t + k;
+        if (b < nb) {
+            const uint8_t* q = qp + (size_t)t * 512u;
+            const uint32_t rest = nb - 16u * t;
             u.w[i][0] = ld_stream(q);
-            u.w[i][1] = ld_stream(q + 16u * L.tile_blocks(t0 + i));
-            u.d[i] = __ldg(reinterpret_cast<const uint16_t*>(meta + L.meta_off(row, b)));
+            u.w[i][1] = ld_stream(q + (rest >= 16u ? 256u : 16u * rest));
+            u.d[i] = __ldg(reinterpret_cast<const uint16_t*>(mp + (size_t)t * 32u));
         }
     }
 }
 
-__device__ __forceinline__ void load_unit(const MvArgs& a, const Layout& L, uint32_t row, bool rv, uint32_t t0, uint32_t k,
-                                          Q4Unit& u) {
-    const uint32_t sb = 16u * t0 + k;
-    if (rv && sb < L.blocks()) {
-        const uint8_t* q = a.qs + L.qs_off(row, sb, 0);
-        const uint32_t cs = 16u * L.tile_blocks(t0);
+__device__ __forceinline__ void load_unit(const uint8_t* qp, const uint8_t* mp, uint32_t nsb, uint32_t t, uint32_t k, Q4Unit& u) {
+    const uint32_t sb = 16u * t + k;
+    if (sb < nsb) {
+        const uint8_t* q = qp + (size_t)t * 2048u;
+        const uint32_t rest = nsb - 16u * t;
+        if (rest >= 16u) {
 #pragma unroll
-        for (uint32_t j = 0; j < 8; ++j) u.w[j] = ld_stream(q + (size_t)j * cs);
-        u.m = __ldg(reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(a.meta) + L.meta_off(row, sb)));
+            for (uint32_t j = 0; j < 8; ++j) u.w[j] = ld_stream(q + 256u * j);
+        } else {
+            const uint32_t cs = 16u * rest;
+#pragma unroll
+            for (uint32_t j = 0; j < 8; ++j) u.w[j] = ld_stream(q + j * cs);
+        }
+        u.m = __ldg(reinterpret_cast<const uint4*>(mp + (size_t)t * 256u));
     }
 }
 
 template <bool SAFE, int MAXT>
-__device__ __forceinline__ void compute_unit(const Q8Unit& u, const Qa& s, const Layout& L, uint32_t T, uint32_t t0, uint32_t k,
+__device__ __forceinline__ void compute_unit(const Q8Unit& u, const Qa& s, uint32_t nb, uint32_t T, uint32_t t0, uint32_t k,
                                              float (&p)[MAXT], int32_t* isum_out) {
-    const uint32_t nb = L.blocks();
 #pragma unroll
     for (uint32_t i = 0; i < kQ8Tiles; ++i) {
         const uint32_t t = t0 + i, b = 16u * t + k;
@@ -383,9 +405,9 @@ __device__ __forceinline__ void compute_unit(const Q8Unit& u, const Qa& s, const
 }
 
 template <bool SAFE, int MAXT>
-__device__ __forceinline__ void compute_unit(const Q4Unit& u, const Qa& s, const Layout& L, uint32_t T, uint32_t t0, uint32_t k,
+__device__ __forceinline__ void compute_unit(const Q4Unit& u, const Qa& s, uint32_t nsb, uint32_t T, uint32_t t, uint32_t k,
                                              float (&p)[MAXT], int32_t* isum_out) {
-    const uint32_t nsb = L.blocks(), t = t0, sb = 16u * t + k;
+    const uint32_t sb = 16u * t + k;
     if (sb >= nsb) return;
     const uint32_t sc_lo = u.m.y & 0x3F3F3F3Fu, mn_lo = u.m.z & 0x3F3F3F3Fu;
     const uint32_t sc_hi = (u.m.w & 0x0F0F0F0Fu) | ((u.m.y >> 2) & 0x30303030u);
@@ -424,18 +446,70 @@ __device__ __forceinline__ void compute_unit(const Q4Unit& u, const Qa& s, const
     }
 }
 
+// The row pairs of one warp: pair = warp, warp + kCWarps, ...; per pair the units in order, each
+// unit's loads issued one unit ahead. Two unit buffers alternate roles (no register copies).
+template <int FMT, int MAXT, bool SAFE>
+__device__ __forceinline__ void stream_rows(const MvArgs& a, const Qa& qa, uint32_t r_begin, uint32_t r_end, uint32_t warp,
+                                            uint32_t lane) {
+    using Unit = typename std::conditional<FMT == 0, Q8Unit, Q4Unit>::type;
+    const Layout L{(uint32_t)FMT, a.K};
+    constexpr uint32_t TPU = FMT == 0 ? kQ8Tiles : 1u;      // tiles per unit
+    const uint32_t nb = L.blocks(), units = (L.tiles() + TPU - 1u) / TPU;
+    const uint32_t k = lane & 15u, half = lane >> 4;
+    const uint32_t n_pairs = (r_end - r_begin + 1u) / 2u;
+    const size_t qrow = L.qs_row_bytes(), mrow = L.meta_row_bytes();
+    const uint8_t* qbase = a.qs + 16u * k;
+    const uint8_t* mbase = static_cast<const uint8_t*>(a.meta) + (FMT == 0 ? 2u : 16u) * k;
+    const uint32_t isum_row = FMT == 0 ? nb : 2u * nb;
+
+    uint32_t pair = warp, ui = 0;
+    if (pair >= n_pairs) return;
+    float p[MAXT];
+#pragma unroll
+    for (int t = 0; t < MAXT; ++t) p[t] = 0.0f;
+
+    // loads unit ui of pair pr into u (nothing for a padding row)
+    auto load = [&](Unit& u, uint32_t pr, uint32_t uix) {
+        const uint32_t row = r_begin + 2u * pr + half;
+        if (row < r_end) load_unit(qbase + (size_t)row * qrow, mbase + (size_t)row * mrow, nb, uix * TPU, k, u);
+    };
+    // computes cur (unit ui of pair) and loads the next unit into nxt; false when the warp is done
+    auto step = [&](const Unit& cur, Unit& nxt) -> bool {
+        const uint32_t row = r_begin + 2u * pair + half;
+        const bool rv = row < r_end;
+        uint32_t npair = pair, nui = ui + 1u;
+        if (nui == units) { npair = pair + kCWarps; nui = 0; }
+        if (npair < n_pairs) load(nxt, npair, nui);
+        if (rv) compute_unit<SAFE, MAXT>(cur, qa, nb, a.T, ui * TPU, k, p, a.isum_out ? a.isum_out + (size_t)row * isum_row : nullptr);
+        if (nui == 0) {                // the pair is complete: tree, epilogue, store
+#pragma unroll
+            for (int t = 0; t < MAXT; ++t) {
+                if (t < (int)a.T) {
+                    const float v = tree16_lanes(p[t]);
+                    if (k == 0 && rv) a.y[(size_t)t * a.y_stride + row] = mm_epilogue(v, a, (uint32_t)t, row);
+                }
+                p[t] = 0.0f;
+            }
+        }
+        pair = npair;
+        ui = nui;
+        return pair < n_pairs;
+    };
+    Unit A, B;
+    load(A, pair, 0);
+    while (step(A, B) && step(B, A)) {
+    }
+}
+
 // ---- the kernel ---------------------------------------------------------------------------------
 template <int FMT, int MAXT>
-__global__ void __launch_bounds__(kThreads, 1) matvec_kernel(MvArgs a, Plan P, uint32_t rows_per_cta) {
+__global__ void __launch_bounds__(kThreads, kCtasPerSm) matvec_kernel(MvArgs a, Plan P, uint32_t rows_per_cta) {
     extern __shared__ __align__(128) uint8_t smem[];
     const Layout L{(uint32_t)FMT, a.K};
     const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31u;
     const uint32_t r_begin = blockIdx.x * rows_per_cta;
     const uint32_t r_end = min(a.n_rows, r_begin + rows_per_cta);
     if (r_begin >= r_end) return;
-    using Unit = typename std::conditional<FMT == 0, Q8Unit, Q4Unit>::type;
-    constexpr uint32_t TPU = FMT == 0 ? kQ8Tiles : 1u;      // tiles per unit
-    const uint32_t units = (L.tiles() + TPU - 1u) / TPU;
 
     // weights of this CTA: HBM -> L2 now (read-only data: safe before the previous kernel ends);
     // the lanes of warp 0 issue the chunks in parallel, quants then meta
@@ -451,8 +525,6 @@ __global__ void __launch_bounds__(kThreads, 1) matvec_kernel(MvArgs a, Plan P, u
         }
     }
     asm volatile("griddepcontrol.launch_dependents;");
-    const uint32_t k = lane & 15u, half = lane >> 4;
-    const uint32_t n_pairs = (r_end - r_begin + 1u) / 2u;
 
     // the activation (after the previous kernel on the stream has completed); no weight load is
     // issued before it, so the activation's loads do not queue behind them
@@ -464,45 +536,9 @@ __global__ void __launch_bounds__(kThreads, 1) matvec_kernel(MvArgs a, Plan P, u
     qa.d_tok = P.qa_d;
     qa.bs = reinterpret_cast<uint8_t*>(qa.d) + (size_t)a.T * P.qa_d;
     qa.bs_tok = P.qa_bs;
-    uint32_t* flag = reinterpret_cast<uint32_t*>(smem + a16(P.qa_bytes(a.T)));
-    const bool safe = stage_qa<FMT>(a, qa, L, flag);
-    uint32_t pair = warp, ui = 0;
-    if (pair >= n_pairs) return;
-    Unit cur;
-    load_unit(a, L, r_begin + 2u * pair + half, r_begin + 2u * pair + half < r_end, 0, k, cur);
-
-    float p[MAXT];
-#pragma unroll
-    for (int t = 0; t < MAXT; ++t) p[t] = 0.0f;
-    while (pair < n_pairs) {
-        const uint32_t row = r_begin + 2u * pair + half;
-        const bool rv = row < r_end;
-        uint32_t npair = pair, nui = ui + 1u;
-        if (nui == units) { npair = pair + kCWarps; nui = 0; }
-        Unit nxt;
-        {
-            const uint32_t nrow = r_begin + 2u * npair + half;
-            load_unit(a, L, nrow, npair < n_pairs && nrow < r_end, nui * TPU, k, nxt);
-        }
-        if (rv) {
-            int32_t* isum_out = a.isum_out ? a.isum_out + (size_t)row * L.blocks() * (FMT == 0 ? 1u : 2u) : nullptr;
-            if (safe) compute_unit<true, MAXT>(cur, qa, L, a.T, ui * TPU, k, p, isum_out);
-            else compute_unit<false, MAXT>(cur, qa, L, a.T, ui * TPU, k, p, isum_out);
-        }
-        if (nui == 0) {                // the pair is complete: tree, epilogue, store
-#pragma unroll
-            for (int t = 0; t < MAXT; ++t) {
-                if (t < (int)a.T) {
-                    const float v = tree16_lanes(p[t]);
-                    if (k == 0 && rv) a.y[(size_t)t * a.y_stride + row] = mm_epilogue(v, a, (uint32_t)t, row);
-                }
-                p[t] = 0.0f;
-            }
-        }
-        pair = npair;
-        ui = nui;
-        cur = nxt;
-    }
+    uint32_t* flags = reinterpret_cast<uint32_t*>(smem + a16(P.qa_bytes(a.T)));
+    if (stage_qa<FMT>(a, qa, L, flags)) stream_rows<FMT, MAXT, true>(a, qa, r_begin, r_end, warp, lane);
+    else stream_rows<FMT, MAXT, false>(a, qa, r_begin, r_end, warp, lane);
 }
 
 // ---- host side ------------------------------------------------------------------------------------

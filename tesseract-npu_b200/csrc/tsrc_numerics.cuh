@@ -70,6 +70,23 @@ __device__ __forceinline__ int32_t round_sat8(float v, bool half_even) {
     return ip < -128 ? -128 : (ip > 127 ? 127 : ip);
 }
 
+// The same conversions on the hardware's float-to-integer instructions (a NaN converts to 0 and an
+// out-of-range value saturates): half-even is one round-to-nearest-even conversion; half-away is a
+// truncation plus one step away from zero when the exact remainder is at least one half.
+__device__ __forceinline__ int32_t round_even_sat8(float v) {
+    int32_t r;
+    asm("cvt.rni.s32.f32 %0, %1;" : "=r"(r) : "f"(v));
+    return max(-128, min(127, r));
+}
+__device__ __forceinline__ int32_t round_away_sat8(float v) {
+    int32_t r;
+    asm("cvt.rzi.s32.f32 %0, %1;" : "=r"(r) : "f"(v));
+    r = max(-1024, min(1024, r));
+    const float f = __fsub_rn(v, __int2float_rn(r));      // the exact remainder for |v| < 2^24; NaN stays NaN
+    r += (fabsf(f) >= 0.5f) ? (v < 0.0f ? -1 : 1) : 0;
+    return max(-128, min(127, r));
+}
+
 // The amax key of QACT: |DAZ(x)| as bits for a non-NaN x (comparable as unsigned), 0 for NaN
 // (a NaN does not take part; 0 never wins a strict > against a real candidate).
 __device__ __forceinline__ uint32_t amax_key(float x) {

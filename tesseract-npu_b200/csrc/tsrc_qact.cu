@@ -26,7 +26,7 @@ __global__ void __launch_bounds__(256) qact_a32_kernel(const float* __restrict__
     const uint32_t amax = __reduce_max_sync(0xFFFFFFFFu, amax_key(v));
     const float db = fdiv(ffrom(amax), 127.0f);
     const float id = (fbits(db) & ~kSign) ? frecip(db) : 0.0f;
-    q[(size_t)t * K + 32u * b + lane] = (int8_t)round_sat8(fmul(daz(v), id), false);
+    q[(size_t)t * K + 32u * b + lane] = (int8_t)round_away_sat8(fmul(daz(v), id));
     if (lane == 0) d[(size_t)t * nb + b] = h2f(f2h(db));
 }
 
@@ -68,7 +68,7 @@ __global__ void __launch_bounds__(256) qact_a256_kernel(const float* __restrict_
     if (amax != 0u) {
         const float iscale = fdiv(-127.0f, mx);
 #pragma unroll
-        for (int i = 0; i < 8; ++i) qv[i] = round_sat8(fmul(iscale, daz(v[i])), true);
+        for (int i = 0; i < 8; ++i) qv[i] = round_even_sat8(fmul(iscale, daz(v[i])));
         db = frecip(iscale);
     } else {
 #pragma unroll
