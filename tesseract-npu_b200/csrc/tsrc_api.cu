@@ -79,12 +79,24 @@ struct tsrc_weight {
     size_t bytes;
 };
 
+struct tsrc_kv {
+    tsrc_ctx* ctx;
+    uint32_t n_head_kv, D, n_cells, n_alloc;   // n_alloc: n_cells rounded up to 16 (zero padding)
+    int8_t* q[2];                               // [K, V] quants [n_head_kv][n_alloc][D]
+    uint16_t* d[2];                             //        scales [n_head_kv][n_alloc][D/32]
+    uint8_t* mem;
+    size_t bytes;
+};
+
 struct tsrc_ctx {
     int device;
     cudaDeviceProp prop;
     uint8_t* scratch = nullptr;   // QA images of the tokens of one call
     size_t scratch_bytes = 0;
+    uint8_t* fa_scratch = nullptr;   // FA work items, channel partials, mask copies of one call
+    size_t fa_scratch_bytes = 0;
     std::set<tsrc_weight*> weights;
+    std::set<tsrc_kv*> kvs;
 };
 
 namespace {
@@ -147,6 +159,32 @@ void drop_weight(tsrc_weight* w) {
     cudaFree(w->qs);
     w->ctx->weights.erase(w);
     delete w;
+}
+
+void drop_kv(tsrc_kv* kv) {
+    if (!kv) return;
+    cudaFree(kv->mem);
+    kv->ctx->kvs.erase(kv);
+    delete kv;
+}
+
+int ensure_fa_scratch(tsrc_ctx* ctx, size_t bytes) {
+    if (bytes <= ctx->fa_scratch_bytes) return TSRC_OK;
+    if (ctx->fa_scratch) {
+        TSRC_CUDA(cudaDeviceSynchronize(), "cudaDeviceSynchronize");
+        cudaFree(ctx->fa_scratch);
+        ctx->fa_scratch = nullptr;
+        ctx->fa_scratch_bytes = 0;
+    }
+    const size_t want = std::max<size_t>(bytes, 4u << 20);
+    cudaError_t e = cudaMalloc(&ctx->fa_scratch, want);
+    if (e != cudaSuccess) return fail(TSRC_E_NOMEM, "cudaMalloc of %zu FA scratch bytes: %s", want, cudaGetErrorString(e));
+    ctx->fa_scratch_bytes = want;
+    return TSRC_OK;
+}
+
+bool kv_geometry_ok(uint32_t n_head_kv, uint32_t D) {
+    return (D == 64 || D == 128 || D == 256 || D == 512) && n_head_kv >= 1 && n_head_kv * D / 64u <= 511u;
 }
 
 }  // namespace
@@ -230,7 +268,9 @@ int tsrc_close(tsrc_ctx* ctx) {
     use_device(ctx);
     cudaDeviceSynchronize();
     while (!ctx->weights.empty()) drop_weight(*ctx->weights.begin());
+    while (!ctx->kvs.empty()) drop_kv(*ctx->kvs.begin());
     if (ctx->scratch) cudaFree(ctx->scratch);
+    if (ctx->fa_scratch) cudaFree(ctx->fa_scratch);
     delete ctx;
     return TSRC_OK;
 }
@@ -245,6 +285,9 @@ int tsrc_sync(tsrc_ctx* ctx, void* stream) {
     e = tsrc::matvec_error(&code, true);
     if (e != cudaSuccess) return cuda_fail(e, "reading the kernel error flag");
     if (code) return fail(TSRC_E_DEVICE, "a matvec kernel gave up a bounded wait (code %u)", code);
+    e = tsrc::kv_error(&code, true);
+    if (e != cudaSuccess) return cuda_fail(e, "reading the KV error flag");
+    if (code) return fail(TSRC_E_ARG, "tsrc_kv_set_rows: a cell index outside the cache (those rows were not stored)");
     return TSRC_OK;
 }
 
@@ -493,6 +536,208 @@ int tsrc_qact(tsrc_ctx* ctx, uint32_t kind, const float* x, uint32_t K, uint32_t
     if (rc) return rc;
     cudaError_t e = tsrc::launch_qact(kind, x, K, T, x_stride, q, d, bs, static_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) return cuda_fail(e, "QACT launch");
+    return TSRC_OK;
+}
+
+// ---- KV cache and flash attention -------------------------------------------------------------
+
+int tsrc_kv_create(tsrc_ctx* ctx, uint32_t n_head_kv, uint32_t D, uint32_t n_cells, tsrc_kv** out) {
+    if (!ctx || !out) return fail(TSRC_E_ARG, "tsrc_kv_create: NULL argument");
+    *out = nullptr;
+    if (!kv_geometry_ok(n_head_kv, D)) return fail(TSRC_E_SHAPE, "tsrc_kv_create: head_dim must be 64/128/256/512, E / 64 <= 511");
+    if (n_cells == 0 || n_cells > (1u << 30)) return fail(TSRC_E_SHAPE, "tsrc_kv_create: n_cells must be 1..2^30");
+    int rc = use_device(ctx);
+    if (rc) return rc;
+    const uint32_t n_alloc = (n_cells + 15u) & ~15u;
+    const size_t qb = align256((size_t)n_head_kv * n_alloc * D), db = align256((size_t)n_head_kv * n_alloc * (D / 32u) * 2u);
+    const size_t bytes = 2u * (qb + db);
+    uint8_t* mem = nullptr;
+    cudaError_t e = cudaMalloc(&mem, bytes);
+    if (e != cudaSuccess) return fail(TSRC_E_NOMEM, "cudaMalloc of %zu KV bytes: %s", bytes, cudaGetErrorString(e));
+    e = cudaMemset(mem, 0, bytes);
+    if (e != cudaSuccess) {
+        cudaFree(mem);
+        return cuda_fail(e, "cudaMemset");
+    }
+    tsrc_kv* kv = new tsrc_kv{};
+    kv->ctx = ctx;
+    kv->n_head_kv = n_head_kv;
+    kv->D = D;
+    kv->n_cells = n_cells;
+    kv->n_alloc = n_alloc;
+    kv->mem = mem;
+    kv->bytes = bytes;
+    for (int w = 0; w < 2; ++w) {
+        kv->q[w] = reinterpret_cast<int8_t*>(mem + (size_t)w * (qb + db));
+        kv->d[w] = reinterpret_cast<uint16_t*>(mem + (size_t)w * (qb + db) + qb);
+    }
+    ctx->kvs.insert(kv);
+    *out = kv;
+    return TSRC_OK;
+}
+
+int tsrc_kv_free(tsrc_kv* kv) {
+    if (!kv) return fail(TSRC_E_ARG, "tsrc_kv_free: NULL cache");
+    use_device(kv->ctx);
+    cudaDeviceSynchronize();
+    drop_kv(kv);
+    return TSRC_OK;
+}
+
+int tsrc_kv_set_rows(tsrc_ctx* ctx, tsrc_kv* kv, uint32_t which, const float* rows, uint32_t n, uint32_t row_stride,
+                     const int64_t* cells, uint32_t cell0, void* stream) {
+    if (!ctx || !kv || !rows) return fail(TSRC_E_ARG, "tsrc_kv_set_rows: NULL argument");
+    if (kv->ctx != ctx) return fail(TSRC_E_ARG, "tsrc_kv_set_rows: the cache belongs to another context");
+    if (which > TSRC_KV_V) return fail(TSRC_E_ARG, "tsrc_kv_set_rows: which must be TSRC_KV_K or TSRC_KV_V");
+    const uint32_t E = kv->n_head_kv * kv->D;
+    if (row_stride == 0) row_stride = E;
+    if (row_stride < E) return fail(TSRC_E_ARG, "tsrc_kv_set_rows: row_stride < E");
+    if (!cells && (uint64_t)cell0 + n > kv->n_cells) return fail(TSRC_E_ARG, "tsrc_kv_set_rows: cells [%u, %u+%u) outside the cache", cell0, cell0, n);
+    if (n == 0) return TSRC_OK;
+    int rc = use_device(ctx);
+    if (rc) return rc;
+    cudaError_t e = tsrc::launch_kv_store(rows, n, row_stride, cells, cell0, kv->n_head_kv, kv->D, kv->n_alloc, kv->q[which],
+                                          kv->d[which], static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "KVST launch");
+    return TSRC_OK;
+}
+
+static int kv_bytes_io(tsrc_kv* kv, uint32_t which, void* host, uint32_t cell0, uint32_t n, bool to_device) {
+    if (!kv || !host) return fail(TSRC_E_ARG, "tsrc_kv_%s_bytes: NULL argument", to_device ? "set" : "get");
+    if (which > TSRC_KV_V) return fail(TSRC_E_ARG, "tsrc_kv_*_bytes: which must be TSRC_KV_K or TSRC_KV_V");
+    if ((uint64_t)cell0 + n > kv->n_cells) return fail(TSRC_E_ARG, "tsrc_kv_*_bytes: cells outside the cache");
+    if (n == 0) return TSRC_OK;
+    int rc = use_device(kv->ctx);
+    if (rc) return rc;
+    const size_t bytes = (size_t)n * (kv->n_head_kv * kv->D / 32u) * 34u;
+    uint8_t* stage = nullptr;
+    cudaError_t e = cudaMalloc(&stage, bytes);
+    if (e != cudaSuccess) return fail(TSRC_E_NOMEM, "cudaMalloc of %zu staging bytes", bytes);
+    if (to_device) {
+        e = cudaMemcpy(stage, host, bytes, cudaMemcpyHostToDevice);
+        if (e == cudaSuccess)
+            e = tsrc::launch_kv_from_ggml(stage, n, cell0, kv->n_head_kv, kv->D, kv->n_alloc, kv->q[which], kv->d[which], 0);
+        if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    } else {
+        e = cudaDeviceSynchronize();
+        if (e == cudaSuccess)
+            e = tsrc::launch_kv_to_ggml(kv->q[which], kv->d[which], n, cell0, kv->n_head_kv, kv->D, kv->n_alloc, stage, 0);
+        if (e == cudaSuccess) e = cudaDeviceSynchronize();
+        if (e == cudaSuccess) e = cudaMemcpy(host, stage, bytes, cudaMemcpyDeviceToHost);
+    }
+    cudaFree(stage);
+    if (e != cudaSuccess) return cuda_fail(e, to_device ? "KV upload" : "KV download");
+    return TSRC_OK;
+}
+
+int tsrc_kv_set_bytes(tsrc_kv* kv, uint32_t which, const void* ggml_rows, uint32_t cell0, uint32_t n) {
+    return kv_bytes_io(kv, which, const_cast<void*>(ggml_rows), cell0, n, true);
+}
+
+int tsrc_kv_get_bytes(const tsrc_kv* kv, uint32_t which, void* ggml_rows, uint32_t cell0, uint32_t n) {
+    return kv_bytes_io(const_cast<tsrc_kv*>(kv), which, ggml_rows, cell0, n, false);
+}
+
+int tsrc_flash_attn(tsrc_ctx* ctx, const tsrc_kv* kv, const float* q, uint32_t T, uint32_t n_head, uint32_t n_kv,
+                    const uint16_t* mask, uint32_t mask_stride, float scale, uint32_t new_lo, uint32_t new_hi,
+                    const tsrc_fa_cfg* cfg, float* out, void* stream) {
+    if (!ctx || !kv || !q || !out) return fail(TSRC_E_ARG, "tsrc_flash_attn: NULL argument");
+    if (kv->ctx != ctx) return fail(TSRC_E_ARG, "tsrc_flash_attn: the cache belongs to another context");
+    if (n_kv > kv->n_cells) return fail(TSRC_E_ARG, "tsrc_flash_attn: n_kv %u exceeds the cache's %u cells", n_kv, kv->n_cells);
+    if (mask && mask_stride < n_kv) return fail(TSRC_E_ARG, "tsrc_flash_attn: mask_stride < n_kv");
+    uint32_t sb;
+    std::memcpy(&sb, &scale, 4);
+    if ((sb & 0x80000000u) || (sb & 0x7F800000u) == 0 || (sb & 0x7F800000u) == 0x7F800000u)
+        return fail(TSRC_E_SHAPE, "FLASH_ATTN: scale must be finite, normal and > 0");
+    const tsrc_fa_cfg def{4, 4, 9344, 32768};
+    const tsrc_fa_cfg& c = cfg ? *cfg : def;
+    tsrc::FaPlanIn in{};
+    in.C = c.C;
+    in.t_max = c.t_max;
+    in.pcap = c.pcap;
+    in.k_max = c.k_max;
+    in.T = T;
+    in.D = kv->D;
+    in.n_head = n_head;
+    in.n_head_kv = kv->n_head_kv;
+    in.n_kv = n_kv;
+    in.mask = mask;
+    in.mask_stride = mask_stride;
+    in.new_lo = new_lo;
+    in.new_hi = new_hi;
+    tsrc::FaPlanOut po{};
+    tsrc::FaItem* items = nullptr;
+    uint32_t* tiles = nullptr;
+    uint32_t n_items = 0;
+    const char* why = nullptr;
+    int rc = tsrc::fa_plan(in, &po, &items, &n_items, &tiles, &why);
+    if (rc != TSRC_OK) return fail(rc, "%s", why ? why : "FLASH_ATTN: planning failed");
+    if (tsrc::fa_smem_bytes(kv->D, po.n_max_groups, c.C) > 227u * 1024u) {
+        tsrc::fa_plan_free(items, tiles);
+        return fail(TSRC_E_SHAPE, "FLASH_ATTN: a chunk needs more shared memory than a CTA has");
+    }
+    rc = use_device(ctx);
+    if (rc) {
+        tsrc::fa_plan_free(items, tiles);
+        return rc;
+    }
+    const uint32_t rows_max = po.Tq0 * po.G;
+    const size_t b_items = align256((size_t)n_items * sizeof(tsrc::FaItem));
+    const size_t b_tiles = align256((size_t)(po.n_tiles + 1u) * 4u);
+    const size_t b_oc = align256((size_t)n_items * kv->n_head_kv * c.C * rows_max * kv->D * 4u);
+    const size_t b_lc = align256((size_t)n_items * kv->n_head_kv * c.C * rows_max * 4u);
+    const size_t b_mk = align256((size_t)n_items * kv->n_head_kv * rows_max * 4u);
+    const size_t b_m16 = po.general ? align256((size_t)T * mask_stride * 2u) : 0u;
+    const size_t b_mf = po.general ? align256((size_t)T * n_kv * 4u) : 0u;
+    rc = ensure_fa_scratch(ctx, b_items + b_tiles + b_oc + b_lc + b_mk + b_m16 + b_mf);
+    if (rc) {
+        tsrc::fa_plan_free(items, tiles);
+        return rc;
+    }
+    uint8_t* p = ctx->fa_scratch;
+    tsrc::FaLaunch a{};
+    a.items = reinterpret_cast<const tsrc::FaItem*>(p);
+    a.tile_items = reinterpret_cast<const uint32_t*>(p + b_items);
+    a.oc = reinterpret_cast<float*>(p + b_items + b_tiles);
+    a.lc = reinterpret_cast<float*>(p + b_items + b_tiles + b_oc);
+    a.mk = reinterpret_cast<float*>(p + b_items + b_tiles + b_oc + b_lc);
+    uint16_t* m16 = reinterpret_cast<uint16_t*>(p + b_items + b_tiles + b_oc + b_lc + b_mk);
+    float* mf = reinterpret_cast<float*>(p + b_items + b_tiles + b_oc + b_lc + b_mk + b_m16);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    // host -> device copies of the plan (and the mask of a GENERAL call): the sources are staged
+    // before cudaMemcpyAsync returns, so they may be released right after
+    cudaError_t e = cudaMemcpyAsync(const_cast<tsrc::FaItem*>(a.items), items, (size_t)n_items * sizeof(tsrc::FaItem),
+                                    cudaMemcpyHostToDevice, st);
+    if (e == cudaSuccess)
+        e = cudaMemcpyAsync(const_cast<uint32_t*>(a.tile_items), tiles, (size_t)(po.n_tiles + 1u) * 4u, cudaMemcpyHostToDevice, st);
+    tsrc::fa_plan_free(items, tiles);
+    if (e == cudaSuccess && po.general) {
+        e = cudaMemcpyAsync(m16, mask, (size_t)T * mask_stride * 2u, cudaMemcpyHostToDevice, st);
+        if (e == cudaSuccess) e = tsrc::launch_fa_maskf(m16, mask_stride, T, n_kv, scale, mf, st);
+    }
+    if (e != cudaSuccess) return cuda_fail(e, "FLASH_ATTN setup");
+    a.q = q;
+    a.T = T;
+    a.n_head = n_head;
+    a.n_head_kv = kv->n_head_kv;
+    a.D = kv->D;
+    a.G = po.G;
+    a.C = c.C;
+    a.n_kv = n_kv;
+    a.n_cells = kv->n_alloc;
+    a.kq = kv->q[0];
+    a.kd = kv->d[0];
+    a.vq = kv->q[1];
+    a.vd = kv->d[1];
+    a.maskf = po.general ? mf : nullptr;
+    a.maskf_stride = n_kv;
+    a.scale = scale;
+    a.n_items = n_items;
+    a.n_tiles = po.n_tiles;
+    a.Tq0 = po.Tq0;
+    a.out = out;
+    e = tsrc::launch_fa(a, po.n_max_groups, st);
+    if (e != cudaSuccess) return cuda_fail(e, "FLASH_ATTN launch");
     return TSRC_OK;
 }
 

@@ -1,0 +1,624 @@
+// tsrc_fa.cu -- flash attention over a q8_0 KV cache on sm_100a, bit-exact with the reference's
+// composite FA (jwkim04/tesseract-npu sw/sim/tsr_ref_at.c:774-860, design doc AT §6.6).
+//
+// The reference runs, per query tile and per chunk of cell groups (the chunk planner, rules 1-8 of
+// sw/sim/include/tsr_fa_plan.h; host side in tsrc_fa_plan.cu): ATTQK (scores, row max MAXOUT
+// floored at -2^100), ASMAX (EXP of the scaled difference), ATTPV + LSUM per channel (the groups
+// u = c mod C of the chunk) as block-floating-point sums per 64-cell segment, then AMERGE (channel
+// tree CTREE, online merge with the running max) and finally ANORM. Every f32 operation follows
+// the reference's rules (tsrc_numerics.cuh); every sum that the reference makes exact is an
+// integer sum here too, so the result does not depend on how the work is spread over threads.
+//
+// Work split (one launch of fa_chunk_kernel + one of fa_merge_kernel):
+//   - a thread-block cluster per (work item = query tile x chunk, KV head g), one CTA per channel
+//     (cluster rank = channel); the CTA prefetches its groups' K and V bytes into L2 on entry;
+//   - a CTA computes the scores of its channel's cells for RB rows (query heads of g x tokens of
+//     the tile) at a time, the cluster exchanges the per-channel row maxima through distributed
+//     shared memory (the chunk max is a max over all channels), then the CTA applies EXP and runs
+//     the channel's segments, one warp per segment, folding the segment results in order;
+//   - fa_merge_kernel reduces the C channel partials (CTREE), merges the chunks of a tile in
+//     execution order (AMERGE) and normalises (ANORM), one thread per output value.
+#include <cooperative_groups.h>
+
+#include "tsrc_internal.h"
+#include "tsrc_numerics.cuh"
+
+namespace cg = cooperative_groups;
+
+namespace tsrc {
+
+namespace {
+
+constexpr uint32_t kFaWarps = 8;
+constexpr uint32_t kFaThreads = kFaWarps * 32u;
+constexpr uint32_t kNegInf = 0xFF800000u;
+constexpr uint32_t kMFloor = 0xF1800000u;      // -2^100: MAXOUT's floor (sw/sim/include/tsr_tables.h:89)
+constexpr uint32_t kLFloor = 0x00800000u;      // 2^-126: ANORM's floor of the row sum (tsr_tables.h:90)
+constexpr uint32_t kFlCausal = 1u, kFlSlide = 2u;
+constexpr uint32_t kWPad = 65u;                 // int32 words per (row, slice, block) of a warp's W table
+
+// MAXT (VU §6.8; tsr_ref_at.c:318-325): NaN -> canonical NaN, else the larger value, -0 < +0.
+__device__ __forceinline__ float maxt(float a, float b) {
+    const uint32_t ua = fbits(daz(a)), ub = fbits(daz(b));
+    if ((ua & ~kSign) > kExp || (ub & ~kSign) > kExp) return ffrom(kCanonNaN);
+    const uint32_t ka = (ua & kSign) ? ~ua : (ua | kSign);
+    const uint32_t kb = (ub & kSign) ? ~ub : (ub | kSign);
+    return ffrom(ka >= kb ? ua : ub);
+}
+
+// Block floating point (tsr_ref_at.c:380-430): RNE_int(w * 2^(23 - es)) of a finite w whose
+// exponent is <= es (zero for a zero w), and RNE to 24 bits of A * 2^k with underflow to a signed
+// zero below 2^-126 and overflow to infinity.
+__device__ __forceinline__ int32_t bf_int(float w, int32_t es) {
+    const uint32_t u = fbits(w), a = u & ~kSign;
+    if ((a >> 23) == 0) return 0;
+    const int32_t sh = es - ((int32_t)(a >> 23) - 127);
+    const uint32_t m = 0x00800000u | (a & kMant);
+    uint32_t v;
+    if (sh == 0) {
+        v = m;
+    } else if (sh >= 26) {
+        v = 0;
+    } else {
+        v = m >> sh;
+        const uint32_t rem = m & ((1u << sh) - 1u), half = 1u << (sh - 1);
+        if (rem > half || (rem == half && (v & 1u))) v++;
+    }
+    return (u & kSign) ? -(int32_t)v : (int32_t)v;
+}
+
+__device__ __forceinline__ float bf_f(int64_t A, int32_t k) {
+    if (A == 0) return 0.0f;
+    const uint32_t s = A < 0 ? kSign : 0u;
+    uint64_t mag = A < 0 ? 0ull - (uint64_t)A : (uint64_t)A;
+    const int msb = 63 - __clzll((long long)mag);
+    int64_t e;
+    if (msb > 23) {
+        int sh = msb - 23;
+        uint64_t m = mag >> sh;
+        const uint64_t rem = mag & ((1ull << sh) - 1u), half = 1ull << (sh - 1);
+        if (rem > half || (rem == half && (m & 1u))) m++;
+        if (m == (1ull << 24)) {
+            m >>= 1;
+            sh++;
+        }
+        mag = m;
+        e = 23 + sh + (int64_t)k;
+    } else {
+        mag <<= (23 - msb);
+        e = msb + (int64_t)k;
+    }
+    if (e < -126) return ffrom(s);
+    if (e > 127) return ffrom(s | kExp);
+    return ffrom(s | ((uint32_t)(e + 127) << 23) | ((uint32_t)mag & kMant));
+}
+
+__device__ __forceinline__ bool nonfinite(uint32_t u) { return (u & kExp) == kExp; }
+
+// maxt over a warp (every lane gets the result)
+__device__ __forceinline__ float warp_maxt(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = maxt(v, __shfl_xor_sync(0xFFFFFFFFu, v, o));
+    return v;
+}
+
+__device__ __forceinline__ int32_t dot32(const uint4 a0, const uint4 a1, const uint4 b0, const uint4 b1) {
+    int32_t s = 0;
+    s = __dp4a((int)a0.x, (int)b0.x, s);
+    s = __dp4a((int)a0.y, (int)b0.y, s);
+    s = __dp4a((int)a0.z, (int)b0.z, s);
+    s = __dp4a((int)a0.w, (int)b0.w, s);
+    s = __dp4a((int)a1.x, (int)b1.x, s);
+    s = __dp4a((int)a1.y, (int)b1.y, s);
+    s = __dp4a((int)a1.z, (int)b1.z, s);
+    s = __dp4a((int)a1.w, (int)b1.w, s);
+    return s;
+}
+
+// The fixed 16-partial tree (tsr_ref.c:592-606) of ND terms p[b] = fadd(+0, term_b), zeros after.
+template <int ND>
+__device__ __forceinline__ float tree16_terms(const float (&t)[ND]) {
+    float v[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = i < ND ? fadd(0.0f, t[i]) : 0.0f;
+#pragma unroll
+    for (int n = 16; n > 1; n /= 2)
+#pragma unroll
+        for (int k = 0; k < n / 2; ++k) v[k] = fadd(v[2 * k], v[2 * k + 1]);
+    return v[0];
+}
+
+__device__ __forceinline__ void prefetch_l2(const void* src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
+// Shared-memory plan of fa_chunk_kernel (host and device agree).
+struct FaSmem {
+    uint32_t s_off, w_off, cv_off, misc_off, total;
+};
+
+__host__ __device__ inline uint32_t fa_a16(uint32_t n) { return (n + 15u) & ~15u; }
+
+__host__ __device__ inline FaSmem fa_smem(uint32_t D, uint32_t ncell_max) {
+    const uint32_t RB = 512u / D, ND = D / 32u, NSL = D / 64u;
+    FaSmem s{};
+    uint32_t o = 64u * 4u + 4u * 8u;                          // EXPK tables
+    o = fa_a16(o);
+    o += fa_a16(RB * D);                                        // qx [RB][D]
+    o += fa_a16(RB * ND * 4u);                                  // dx [RB][ND]
+    s.s_off = o;
+    o += fa_a16(RB * ncell_max * 4u);                           // S [RB][ncell_max]
+    s.w_off = o;
+    o += fa_a16(kFaWarps * RB * NSL * 2u * kWPad * 4u);         // W [warp][RB][NSL][2][kWPad]
+    s.cv_off = o;
+    o += fa_a16(kFaWarps * RB * D * 4u);                        // CV [warp][RB][D]
+    s.misc_off = o;
+    // mx [2][RB], mk [RB], wmax [warps][RB], ls [warps][RB], lacc [RB], es [warps][RB][NSL], fl [warps][RB][NSL]
+    o += 4u * (2u * RB + RB + kFaWarps * RB + kFaWarps * RB + RB + 2u * kFaWarps * RB * NSL);
+    s.total = fa_a16(o);
+    return s;
+}
+
+// ---------------------------------------------------------------------------------------------------
+template <int D>
+__global__ void __launch_bounds__(kFaThreads) fa_chunk_kernel(FaLaunch a) {
+    constexpr uint32_t ND = D / 32, NSL = D / 64, RB = 512 / D, NV = D / 32;
+    extern __shared__ __align__(16) uint8_t smem[];
+    cg::cluster_group cluster = cg::this_cluster();
+    const uint32_t C = a.C, cc = cluster.block_rank();
+    const uint32_t ig = blockIdx.x / C, item = ig / a.n_head_kv, g = ig - item * a.n_head_kv;
+    const FaItem it = a.items[item];
+    const uint32_t G = a.G, rows = it.Tq * G, rows_max = a.Tq0 * G;
+    const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31u;
+
+    // the channel's groups: u = ufirst + C k, k < nu
+    const uint32_t ufirst = it.u0 + (cc + C - it.u0 % C) % C;
+    const uint32_t nu = ufirst < it.u0 + it.n ? (it.u0 + it.n - ufirst + C - 1u) / C : 0u;
+    const uint32_t ncell = 16u * nu;
+    const uint32_t ncell_max = 16u * ((it.n + C - 1u) / C);
+    const FaSmem P = fa_smem(D, ncell_max);
+
+    const size_t head_cells = (size_t)g * a.n_cells;
+    // K and V of the channel's visible groups: HBM -> L2 now
+    for (uint32_t i = tid; i < 4u * nu; i += kFaThreads) {
+        const uint32_t k = i >> 2, which = i & 3u, u = ufirst + C * k;
+        if (16u * u >= a.n_kv) continue;
+        const size_t c0 = head_cells + 16u * u;
+        if (which == 0) prefetch_l2(a.kq + c0 * D, 16u * D);
+        else if (which == 1) prefetch_l2(a.vq + c0 * D, 16u * D);
+        else if (which == 2) prefetch_l2(a.kd + c0 * ND, 32u * ND);
+        else prefetch_l2(a.vd + c0 * ND, 32u * ND);
+    }
+
+    uint32_t* t64s = reinterpret_cast<uint32_t*>(smem);
+    uint64_t* lks = reinterpret_cast<uint64_t*>(smem + 256);
+    int8_t* qx = reinterpret_cast<int8_t*>(smem + fa_a16(64u * 4u + 4u * 8u));
+    float* dx = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(qx) + fa_a16(RB * D));
+    float* S = reinterpret_cast<float*>(smem + P.s_off);
+    int32_t* Wt = reinterpret_cast<int32_t*>(smem + P.w_off);
+    float* CV = reinterpret_cast<float*>(smem + P.cv_off);
+    float* mx = reinterpret_cast<float*>(smem + P.misc_off);   // [2][RB]
+    float* mk = mx + 2u * RB;                                    // [RB]
+    float* wmax = mk + RB;                                       // [warps][RB]
+    float* ls = wmax + kFaWarps * RB;                            // [warps][RB]
+    float* lacc = ls + kFaWarps * RB;                            // [RB]
+    int32_t* esw = reinterpret_cast<int32_t*>(lacc + RB);        // [warps][RB][NSL]
+    uint32_t* flw = reinterpret_cast<uint32_t*>(esw + kFaWarps * RB * NSL);
+    if (tid < 64) t64s[tid] = g_expk_t64[tid];
+    if (tid < 4) lks[tid] = g_expk_lk[tid];
+
+    const uint32_t nseg = (nu + 3u) / 4u;
+    const float scale = a.scale;
+    float* oc_base = a.oc + (((size_t)item * a.n_head_kv + g) * C + cc) * rows_max * D;
+    float* lc_base = a.lc + (((size_t)item * a.n_head_kv + g) * C + cc) * rows_max;
+
+    uint32_t pass = 0;
+    for (uint32_t r0 = 0; r0 < rows; r0 += RB, ++pass) {
+        const uint32_t nr = min(RB, rows - r0);
+        // ---- QACT A32 of the pass's query rows (tsr_ref.c:472-487): one warp per 32-block ----
+        for (uint32_t bi = warp; bi < nr * ND; bi += kFaWarps) {
+            const uint32_t r = bi / ND, b = bi - r * ND, ri = r0 + r;
+            const uint32_t t = ri / G, h = g * G + (ri - t * G);
+            const float v = a.q[((size_t)(it.q0 + t) * a.n_head + h) * D + 32u * b + lane];
+            const uint32_t amax = __reduce_max_sync(0xFFFFFFFFu, amax_key(v));
+            const float db = fdiv(ffrom(amax), 127.0f);
+            const float id = (fbits(db) & ~kSign) ? frecip(db) : 0.0f;
+            qx[r * D + 32u * b + lane] = (int8_t)round_away_sat8(fmul(daz(v), id));
+            if (lane == 0) dx[r * ND + b] = h2f(f2h(db));
+        }
+        __syncthreads();
+
+        // ---- ATTQK (+ AMASK for GENERAL chunks) and the CTA's row maxima ----
+        float rmax[RB];
+#pragma unroll
+        for (uint32_t r = 0; r < RB; ++r) rmax[r] = ffrom(kMFloor);
+        for (uint32_t j = tid; j < ncell; j += kFaThreads) {
+            const uint32_t k = j >> 4, u = ufirst + C * k, cell = 16u * u + (j & 15u);
+            const int64_t jr = (int64_t)cell - 16 * (int64_t)it.u0;         // cell within the chunk
+            const int8_t* kr = a.kq + (head_cells + cell) * D;
+            const uint16_t* kdr = a.kd + (head_cells + cell) * ND;
+            const bool live = cell < a.n_kv;
+            // D <= 128: the cell's K bytes stay in registers across the rows; larger D reads them
+            // per row (L1 hits after the first row)
+            constexpr uint32_t KW = D <= 128 ? 2 * ND : 1, KD = D <= 128 ? ND : 1;
+            uint4 kw[KW];
+            uint16_t kd[KD];
+            if constexpr (D <= 128) {
+                if (live) {
+#pragma unroll
+                    for (uint32_t i = 0; i < KW; ++i) kw[i] = reinterpret_cast<const uint4*>(kr)[i];
+#pragma unroll
+                    for (uint32_t i = 0; i < KD; ++i) kd[i] = kdr[i];
+                }
+            }
+#pragma unroll
+            for (uint32_t r = 0; r < RB; ++r) {
+                if (r >= nr) break;
+                const uint32_t ri = r0 + r, t = ri / G;
+                const int64_t dq = (int64_t)it.Tq - 1 - t;
+                float s = ffrom(kNegInf);
+                bool vis = true;
+                if (!it.general) {
+                    const int64_t lo = max((int64_t)0, (int64_t)it.c_lo - ((it.flags & kFlSlide) ? dq : 0));
+                    const int64_t hi = (int64_t)it.c_hi - ((it.flags & kFlCausal) ? dq : 0);
+                    vis = jr >= lo && jr < hi;
+                }
+                if (vis && live) {
+                    float terms[ND];
+#pragma unroll
+                    for (uint32_t b = 0; b < ND; ++b) {
+                        uint4 w0, w1;
+                        uint16_t dk;
+                        if constexpr (D <= 128) {
+                            w0 = kw[2 * b];
+                            w1 = kw[2 * b + 1];
+                            dk = kd[b];
+                        } else {
+                            w0 = reinterpret_cast<const uint4*>(kr)[2 * b];
+                            w1 = reinterpret_cast<const uint4*>(kr)[2 * b + 1];
+                            dk = kdr[b];
+                        }
+                        const uint4* xq = reinterpret_cast<const uint4*>(qx + r * D + 32u * b);
+                        const int32_t isum = dot32(w0, w1, xq[0], xq[1]);
+                        terms[b] = fmul(fmul(h2f(dk), dx[r * ND + b]), i2f(isum));
+                    }
+                    s = tree16_terms<ND>(terms);
+                }
+                if (it.general) {
+                    const float m = cell < a.n_kv ? a.maskf[(size_t)(it.q0 + t) * a.maskf_stride + cell] : ffrom(kNegInf);
+                    s = fbits(m) == kNegInf ? ffrom(kNegInf) : fadd(s, m);
+                }
+                S[r * ncell_max + j] = s;
+                rmax[r] = maxt(rmax[r], s);
+            }
+        }
+#pragma unroll
+        for (uint32_t r = 0; r < RB; ++r) {
+            const float m = warp_maxt(rmax[r]);
+            if (lane == 0) wmax[warp * RB + r] = m;
+        }
+        __syncthreads();
+        float* slot = mx + (pass & 1u) * RB;
+        if (tid < RB) {
+            float m = ffrom(kMFloor);
+            for (uint32_t w = 0; w < kFaWarps; ++w) m = maxt(m, wmax[w * RB + tid]);
+            slot[tid] = m;
+        }
+        // ---- the chunk maximum: MAXOUT over every channel of the chunk ----
+        cluster.sync();
+        if (tid < RB) {
+            float m = ffrom(kMFloor);
+            for (uint32_t c = 0; c < C; ++c) m = maxt(m, *cluster.map_shared_rank(slot + tid, c));
+            mk[tid] = m;
+            if (cc == 0 && tid < nr) a.mk[((size_t)item * a.n_head_kv + g) * rows_max + r0 + tid] = m;
+        }
+        __syncthreads();
+        // ---- ASMAX: p = EXP(fmul(fsub(s, m), scale)) ----
+        for (uint32_t i = tid; i < nr * ncell; i += kFaThreads) {
+            const uint32_t r = i / ncell, j = i - r * ncell;
+            float* sp = &S[r * ncell_max + j];
+            *sp = expk(fmul(fsub(*sp, mk[r]), scale), 0u, t64s, lks);
+        }
+        if (tid < RB) lacc[tid] = 0.0f;
+        __syncthreads();
+
+        // ---- ATTPV + LSUM: one warp per 64-cell segment, results folded in segment order ----
+        constexpr uint32_t kPer = RB * D / kFaThreads;        // (row, value) pairs folded per thread
+        float oacc[kPer];
+#pragma unroll
+        for (uint32_t i = 0; i < kPer; ++i) oacc[i] = 0.0f;
+        for (uint32_t sg0 = 0; sg0 < nseg; sg0 += kFaWarps) {
+            const uint32_t sg = sg0 + warp;
+            if (sg < nseg) {
+                const uint32_t ng = min(4u, nu - 4u * sg), nc = 16u * ng;
+                int32_t* W = Wt + warp * RB * NSL * 2u * kWPad;
+                // the two cells of this lane: i = lane, lane + 32
+                uint32_t cellv[2];
+                float dvv[2][NSL][2];
+#pragma unroll
+                for (uint32_t h = 0; h < 2; ++h) {
+                    const uint32_t i = lane + 32u * h, jl = 64u * sg + i;
+                    const uint32_t cell = 16u * (ufirst + C * (jl >> 4)) + (jl & 15u);
+                    cellv[h] = cell;
+#pragma unroll
+                    for (uint32_t sl = 0; sl < NSL; ++sl) {
+                        dvv[h][sl][0] = 0.0f;
+                        dvv[h][sl][1] = 0.0f;
+                        if (i < nc) {
+                            const uint32_t pr = *reinterpret_cast<const uint32_t*>(a.vd + (head_cells + cell) * ND + 2u * sl);
+                            dvv[h][sl][0] = h2f((uint16_t)(pr & 0xFFFFu));
+                            dvv[h][sl][1] = h2f((uint16_t)(pr >> 16));
+                        }
+                    }
+                }
+#pragma unroll
+                for (uint32_t r = 0; r < RB; ++r) {
+                    if (r >= nr) break;
+#pragma unroll
+                    for (uint32_t sl = 0; sl < NSL; ++sl) {
+                        float w[2][2];
+                        int32_t le = -1000;
+                        bool bad0 = false, bad1 = false, any = false;
+#pragma unroll
+                        for (uint32_t h = 0; h < 2; ++h) {
+                            const uint32_t i = lane + 32u * h;
+                            const float p = i < nc ? S[r * ncell_max + 64u * sg + i] : 0.0f;
+                            const bool pz = (fbits(p) & kExp) == 0;
+#pragma unroll
+                            for (uint32_t e = 0; e < 2; ++e) {
+                                const float wv = pz ? 0.0f : fmul(p, dvv[h][sl][e]);
+                                w[h][e] = wv;
+                                const uint32_t u = fbits(wv);
+                                if (nonfinite(u)) {
+                                    if (e == 0) bad0 = true;
+                                    else bad1 = true;
+                                } else if (u & ~kSign) {
+                                    le = max(le, (int32_t)((u >> 23) & 0xFFu) - 127);
+                                    any = true;
+                                }
+                            }
+                        }
+                        const int32_t es = (int32_t)__reduce_max_sync(0xFFFFFFFFu, (uint32_t)(le + 1000)) - 1000;
+                        bad0 = __any_sync(0xFFFFFFFFu, bad0);
+                        bad1 = __any_sync(0xFFFFFFFFu, bad1);
+                        any = __any_sync(0xFFFFFFFFu, any);
+#pragma unroll
+                        for (uint32_t h = 0; h < 2; ++h)
+#pragma unroll
+                            for (uint32_t e = 0; e < 2; ++e)
+                                W[((r * NSL + sl) * 2u + e) * kWPad + lane + 32u * h] =
+                                    (any && !(e ? bad1 : bad0)) ? bf_int(w[h][e], es) : 0;
+                        if (lane == 0) {
+                            esw[(warp * RB + r) * NSL + sl] = es;
+                            flw[(warp * RB + r) * NSL + sl] = (bad0 ? 1u : 0u) | (bad1 ? 2u : 0u) | (any ? 4u : 0u);
+                        }
+                    }
+                    // LSUM of the segment (tsr_ref_at.c:520-553)
+                    {
+                        int32_t le = -1000;
+                        bool bad = false, any = false;
+                        float pv[2];
+#pragma unroll
+                        for (uint32_t h = 0; h < 2; ++h) {
+                            const uint32_t i = lane + 32u * h;
+                            pv[h] = i < nc ? daz(S[r * ncell_max + 64u * sg + i]) : 0.0f;
+                            const uint32_t u = fbits(pv[h]);
+                            if (nonfinite(u)) bad = true;
+                            else if (u & ~kSign) {
+                                le = max(le, (int32_t)((u >> 23) & 0xFFu) - 127);
+                                any = true;
+                            }
+                        }
+                        const int32_t ep = (int32_t)__reduce_max_sync(0xFFFFFFFFu, (uint32_t)(le + 1000)) - 1000;
+                        bad = __any_sync(0xFFFFFFFFu, bad);
+                        any = __any_sync(0xFFFFFFFFu, any);
+                        int32_t part = 0;
+                        if (!bad && any) part = bf_int(pv[0], ep) + bf_int(pv[1], ep);
+                        const int32_t sum = __reduce_add_sync(0xFFFFFFFFu, part);
+                        if (lane == 0)
+                            ls[warp * RB + r] = bad ? ffrom(kCanonNaN) : !any ? 0.0f : bf_f((int64_t)sum, ep - 23);
+                    }
+                }
+                __syncwarp();
+                // exact sums A = sum_i W_i * qV_i for this lane's NV values
+                const uint32_t v0 = lane * NV, sl = v0 / 64u, e = (v0 % 64u) / 32u;
+                int64_t A[RB][NV];
+#pragma unroll
+                for (uint32_t r = 0; r < RB; ++r)
+#pragma unroll
+                    for (uint32_t i = 0; i < NV; ++i) A[r][i] = 0;
+                for (uint32_t i = 0; i < nc; ++i) {
+                    const uint32_t jl = 64u * sg + i;
+                    const uint32_t cell = 16u * (ufirst + C * (jl >> 4)) + (jl & 15u);
+                    const int8_t* vp = a.vq + (head_cells + cell) * D + v0;
+                    int8_t qv[NV];
+                    if (NV == 2) {
+                        const uint16_t x = *reinterpret_cast<const uint16_t*>(vp);
+#pragma unroll
+                        for (uint32_t k = 0; k < NV; ++k) qv[k] = (int8_t)(x >> (8 * k));
+                    } else if (NV == 4) {
+                        const uint32_t x = *reinterpret_cast<const uint32_t*>(vp);
+#pragma unroll
+                        for (uint32_t k = 0; k < NV; ++k) qv[k] = (int8_t)(x >> (8 * k));
+                    } else {
+#pragma unroll
+                        for (uint32_t k0 = 0; k0 < NV; k0 += 8) {
+                            const uint2 x = *reinterpret_cast<const uint2*>(vp + k0);
+#pragma unroll
+                            for (uint32_t k = 0; k < 8 && k0 + k < NV; ++k)
+                                qv[k0 + k] = (int8_t)((k < 4 ? x.x : x.y) >> (8 * (k & 3u)));
+                        }
+                    }
+#pragma unroll
+                    for (uint32_t r = 0; r < RB; ++r) {
+                        if (r >= nr) break;
+                        const int64_t Wv = W[((r * NSL + sl) * 2u + e) * kWPad + i];
+#pragma unroll
+                        for (uint32_t k = 0; k < NV; ++k) A[r][k] += Wv * (int64_t)qv[k];
+                    }
+                }
+                float* cvw = CV + warp * RB * D;
+#pragma unroll
+                for (uint32_t r = 0; r < RB; ++r) {
+                    if (r >= nr) break;
+                    const int32_t es = esw[(warp * RB + r) * NSL + sl];
+                    const uint32_t fl = flw[(warp * RB + r) * NSL + sl];
+                    const bool bad = (fl >> e) & 1u, any = (fl & 4u) != 0;
+#pragma unroll
+                    for (uint32_t k = 0; k < NV; ++k)
+                        cvw[r * D + v0 + k] = bad ? ffrom(kCanonNaN) : !any ? 0.0f : bf_f(A[r][k], es - 23);
+                }
+            }
+            __syncthreads();
+            // fold this round's segments in order: o = fadd(o, cv), l = fadd(l, v)
+            const uint32_t nw = min(kFaWarps, nseg - sg0);
+#pragma unroll
+            for (uint32_t i = 0; i < kPer; ++i) {
+                const uint32_t pidx = tid + i * kFaThreads, r = pidx / D;
+                if (r < nr)
+                    for (uint32_t w = 0; w < nw; ++w) oacc[i] = fadd(oacc[i], CV[w * RB * D + pidx]);
+            }
+            if (tid < nr) {
+                float l = lacc[tid];
+                for (uint32_t w = 0; w < nw; ++w) l = fadd(l, ls[w * RB + tid]);
+                lacc[tid] = l;
+            }
+            __syncthreads();
+        }
+        // the channel's partials of this pass
+#pragma unroll
+        for (uint32_t i = 0; i < kPer; ++i) {
+            const uint32_t pidx = tid + i * kFaThreads, r = pidx / D;
+            if (r < nr) oc_base[(size_t)(r0 + r) * D + (pidx - r * D)] = oacc[i];
+        }
+        if (tid < nr) lc_base[r0 + tid] = lacc[tid];
+        __syncthreads();
+    }
+    // no CTA of the cluster may leave while another can still read its shared memory
+    cluster.sync();
+}
+
+// CTREE (tsr_ref_at.c:588-598): pairwise by levels, an unpaired last element passes through.
+__device__ __forceinline__ float ctree(float (&v)[16], uint32_t n) {
+    while (n > 1) {
+        for (uint32_t k = 0; 2 * k + 1 < n; ++k) v[k] = fadd(v[2 * k], v[2 * k + 1]);
+        if (n & 1u) v[n / 2] = v[n - 1];
+        n = (n + 1) / 2;
+    }
+    return v[0];
+}
+
+// AMERGE over the chunks of each tile in execution order, then ANORM (tsr_ref_at.c:600-641).
+__global__ void __launch_bounds__(256) fa_merge_kernel(FaLaunch a) {
+    const uint32_t G = a.G, D = a.D, rows_max = a.Tq0 * G;
+    const size_t per_tile = (size_t)a.n_head_kv * rows_max * D;
+    const size_t idx = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (idx >= (size_t)a.n_tiles * per_tile) return;
+    const uint32_t tile = (uint32_t)(idx / per_tile);
+    size_t rem = idx - (size_t)tile * per_tile;
+    const uint32_t g = (uint32_t)(rem / ((size_t)rows_max * D));
+    rem -= (size_t)g * rows_max * D;
+    const uint32_t ri = (uint32_t)(rem / D), v = (uint32_t)(rem - (size_t)ri * D);
+    const uint32_t i0 = a.tile_items[tile], i1 = a.tile_items[tile + 1];
+    const FaItem first = a.items[i0];
+    if (ri >= first.Tq * G) return;
+    const uint32_t C = a.C;
+    const float scale = a.scale;
+    float O = 0.0f, lrun = 0.0f, mrun = 0.0f;
+    for (uint32_t k = i0; k < i1; ++k) {
+        float xo[16], xl[16];
+        for (uint32_t c = 0; c < C; ++c) {
+            const size_t base = ((size_t)k * a.n_head_kv + g) * C + c;
+            xo[c] = a.oc[(base * rows_max + ri) * D + v];
+            xl[c] = a.lc[base * rows_max + ri];
+        }
+        const float ok = ctree(xo, C), lk = ctree(xl, C);
+        const float mkk = a.mk[((size_t)k * a.n_head_kv + g) * rows_max + ri];
+        if (k == i0) {
+            O = ok;
+            lrun = lk;
+            mrun = mkk;
+        } else {
+            const float mn = maxt(mrun, mkk);
+            const float ea = expk(fmul(fsub(mrun, mn), scale), 0u, g_expk_t64, g_expk_lk);
+            const float eb = expk(fmul(fsub(mkk, mn), scale), 0u, g_expk_t64, g_expk_lk);
+            lrun = fadd(fmul(lrun, ea), fmul(lk, eb));
+            mrun = mn;
+            O = fadd(fmul(O, ea), fmul(ok, eb));
+        }
+    }
+    const float rinv = frecip(maxt(lrun, ffrom(kLFloor)));
+    const uint32_t t = ri / G, h = g * G + (ri - t * G);
+    a.out[((size_t)(first.q0 + t) * a.n_head + h) * D + v] = canon(fmul(O, rinv));
+}
+
+// f32 mask copy of the GENERAL path (tsr_ref_at.c:694-715): fdiv(f32(mask), scale), -inf kept.
+__global__ void fa_maskf_kernel(const uint16_t* m16, uint32_t stride, uint32_t T, uint32_t n_kv, float scale, float* out) {
+    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (size_t)T * n_kv) return;
+    const uint32_t t = (uint32_t)(i / n_kv), j = (uint32_t)(i - (size_t)t * n_kv);
+    const uint16_t h = m16[(size_t)t * stride + j];
+    out[(size_t)t * n_kv + j] = h == 0xFC00u ? ffrom(kNegInf) : fdiv(h2f(h), scale);
+}
+
+template <int D>
+cudaError_t launch_chunks(const FaLaunch& a, uint32_t ncell_max, cudaStream_t st) {
+    const FaSmem P = fa_smem(D, ncell_max);
+    cudaError_t e = cudaFuncSetAttribute(fa_chunk_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)P.total);
+    if (e != cudaSuccess) return e;
+    if (a.C > 8) {
+        e = cudaFuncSetAttribute(fa_chunk_kernel<D>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+        if (e != cudaSuccess) return e;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(a.n_items * a.n_head_kv * a.C);
+    cfg.blockDim = dim3(kFaThreads);
+    cfg.dynamicSmemBytes = P.total;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = a.C;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (a.C > 8) {        // a non-portable cluster size: make sure one cluster can be resident
+        int n = 0;
+        e = cudaOccupancyMaxActiveClusters(&n, (const void*)fa_chunk_kernel<D>, &cfg);
+        if (e != cudaSuccess) return e;
+        if (n == 0) return cudaErrorInvalidConfiguration;
+    }
+    return cudaLaunchKernelEx(&cfg, fa_chunk_kernel<D>, a);
+}
+
+}  // namespace
+
+size_t fa_smem_bytes(uint32_t D, uint32_t n_max_groups, uint32_t C) {
+    return fa_smem(D, 16u * ((n_max_groups + C - 1u) / C)).total;
+}
+
+cudaError_t launch_fa_maskf(const uint16_t* m16, uint32_t stride, uint32_t T, uint32_t n_kv, float scale, float* out,
+                            cudaStream_t st) {
+    const size_t n = (size_t)T * n_kv;
+    if (n == 0) return cudaSuccess;
+    fa_maskf_kernel<<<(unsigned)((n + 255u) / 256u), 256, 0, st>>>(m16, stride, T, n_kv, scale, out);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_fa(const FaLaunch& a, uint32_t n_max_groups, cudaStream_t st) {
+    const uint32_t ncell_max = 16u * ((n_max_groups + a.C - 1u) / a.C);
+    cudaError_t e;
+    switch (a.D) {
+        case 64: e = launch_chunks<64>(a, ncell_max, st); break;
+        case 128: e = launch_chunks<128>(a, ncell_max, st); break;
+        case 256: e = launch_chunks<256>(a, ncell_max, st); break;
+        case 512: e = launch_chunks<512>(a, ncell_max, st); break;
+        default: return cudaErrorInvalidValue;
+    }
+    if (e != cudaSuccess) return e;
+    const size_t n = (size_t)a.n_tiles * a.n_head_kv * a.Tq0 * a.G * a.D;
+    fa_merge_kernel<<<(unsigned)((n + 255u) / 256u), 256, 0, st>>>(a);
+    return cudaGetLastError();
+}
+
+}  // namespace tsrc

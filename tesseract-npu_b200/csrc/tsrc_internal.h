@@ -47,4 +47,64 @@ cudaError_t launch_unrepack(uint32_t fmt, const uint8_t* qs, const uint8_t* meta
 cudaError_t launch_synth(uint32_t fmt, uint32_t K, uint32_t row0, uint32_t n_rows, uint64_t seed, float sigma,
                          uint8_t* qs, uint8_t* meta, cudaStream_t st);
 
+// ---- flash attention (tsrc_fa.cu, tsrc_fa_plan.cu, tsrc_kv.cu) ----------------------------------
+// One work item: a query tile [q0, q0 + Tq) and one chunk of its plan (groups [u0, u0 + n) of 16
+// cells; c_lo / c_hi the ATTQK bounds relative to cell 16 u0; flags causal 1 / slide 2; general:
+// the chunk runs ATTQK without bounds and then adds the f32 mask copy).
+struct FaItem {
+    uint32_t q0, Tq, u0, n, c_lo, c_hi, flags, general;
+};
+
+struct FaLaunch {
+    const float* q;             // [T][n_head][D] f32
+    uint32_t T, n_head, n_head_kv, D, G, C, n_kv, n_cells;
+    const int8_t* kq;           // K quants [n_head_kv][n_cells][D]
+    const uint16_t* kd;         // K scales (fp16) [n_head_kv][n_cells][D/32]
+    const int8_t* vq;           // V, the same layout
+    const uint16_t* vd;
+    const float* maskf;         // f32 mask copy [T][maskf_stride] (GENERAL chunks only)
+    uint32_t maskf_stride;
+    float scale;
+    const FaItem* items;        // work items, tile by tile, chunks in execution order
+    uint32_t n_items;
+    const uint32_t* tile_items; // [n_tiles + 1]: items of tile i are [tile_items[i], tile_items[i + 1])
+    uint32_t n_tiles, Tq0;
+    float* oc;                  // channel partials [n_items][n_head_kv][C][Tq0 G][D]
+    float* lc;                  //                  [n_items][n_head_kv][C][Tq0 G]
+    float* mk;                  // chunk maxima     [n_items][n_head_kv][Tq0 G]
+    float* out;                 // [T][n_head][D] f32
+};
+
+cudaError_t launch_fa(const FaLaunch& a, uint32_t n_max_groups, cudaStream_t st);
+size_t fa_smem_bytes(uint32_t D, uint32_t n_max_groups, uint32_t C);
+cudaError_t launch_fa_maskf(const uint16_t* m16, uint32_t stride, uint32_t T, uint32_t n_kv, float scale, float* out,
+                            cudaStream_t st);
+
+// The host-side plan of one FA call (the reference's pass rule, mask summary and chunk planner).
+struct FaPlanIn {
+    uint32_t C, t_max, pcap, k_max;
+    uint32_t T, D, n_head, n_head_kv, n_kv;
+    const uint16_t* mask;       // host f16 mask [T][mask_stride], or NULL (every cell < n_kv visible)
+    size_t mask_stride;
+    uint32_t new_lo, new_hi;    // cells written by this launch: their chunks run last
+};
+struct FaPlanOut {
+    uint32_t Tq0, G, n_tiles, n_max_groups;
+    bool general;               // some chunk runs the GENERAL path (needs the f32 mask copy)
+};
+// 0, or a TSRC_E_* code with a message in *why.
+int fa_plan(const FaPlanIn& in, FaPlanOut* out, FaItem** items, uint32_t* n_items, uint32_t** tile_items, const char** why);
+void fa_plan_free(FaItem* items, uint32_t* tile_items);
+
+// KV cache planes (tsrc_kv.cu): KVST of f32 rows (QACT A32), and ggml q8_0 rows <-> planes.
+cudaError_t launch_kv_store(const float* rows, uint32_t n, uint32_t row_stride, const int64_t* cells, uint32_t cell0,
+                            uint32_t n_head_kv, uint32_t D, uint32_t n_cells, int8_t* q, uint16_t* d, cudaStream_t st);
+cudaError_t launch_kv_from_ggml(const uint8_t* ggml, uint32_t n, uint32_t cell0, uint32_t n_head_kv, uint32_t D,
+                                uint32_t n_cells, int8_t* q, uint16_t* d, cudaStream_t st);
+cudaError_t launch_kv_to_ggml(const int8_t* q, const uint16_t* d, uint32_t n, uint32_t cell0, uint32_t n_head_kv, uint32_t D,
+                              uint32_t n_cells, uint8_t* ggml, cudaStream_t st);
+// The first error a KVST launch recorded on the current device (0 = none, 1 = a cell index
+// outside the cache).
+cudaError_t kv_error(uint32_t* code, bool clear);
+
 }  // namespace tsrc

@@ -57,7 +57,22 @@ _SIGS = {
     "tsrc_mul_mat_unsupported": (ct.c_char_p, [_u32, _u64, _u64, _u64]),
     "tsrc_qact": (_i, [_p, _u32, _p, _u32, _u32, _u32, _p, _p, _p, _p]),
     "tsrc_mul_mat_isums": (_i, [_p, _p, _p, _p, _p, _p]),
+    "tsrc_kv_create": (_i, [_p, _u32, _u32, _u32, ct.POINTER(_p)]),
+    "tsrc_kv_free": (_i, [_p]),
+    "tsrc_kv_set_rows": (_i, [_p, _p, _u32, _p, _u32, _u32, _p, _u32, _p]),
+    "tsrc_kv_set_bytes": (_i, [_p, _u32, _p, _u32, _u32]),
+    "tsrc_kv_get_bytes": (_i, [_p, _u32, _p, _u32, _u32]),
+    "tsrc_flash_attn": (_i, [_p, _p, _p, _u32, _u32, _u32, _p, _u32, _f32, _u32, _u32, _p, _p, _p]),
 }
+
+
+class FaCfg(ct.Structure):
+    """tsrc_fa_cfg: the attention configuration (channels C, T_MAX, PCAP, K_MAX)."""
+    _fields_ = [("C", _u32), ("t_max", _u32), ("pcap", _u32), ("k_max", _u32)]
+
+
+KV_K, KV_V = 0, 1
+Q8_0_BLOCK_BYTES = 34
 
 
 def declared_symbols() -> list[str]:
@@ -217,6 +232,27 @@ class Device:
         _check(lib().tsrc_qact(self.handle, kind, _addr(x), K, T, x_stride, _addr(q), _addr(d), _addr(bs),
                                _stream(stream)))
 
+    # ---- KV cache and FLASH_ATTN_EXT ----
+    def kv_create(self, n_head_kv: int, head_dim: int, n_cells: int) -> "KvCache":
+        h = _p()
+        _check(lib().tsrc_kv_create(self.handle, n_head_kv, head_dim, n_cells, ct.byref(h)))
+        return KvCache(self, h, n_head_kv, head_dim, n_cells)
+
+    def flash_attn(self, kv: "KvCache", q, out, T: int, n_head: int, n_kv: int, scale: float, mask=None,
+                   new=(0, 0), cfg=None, stream=None) -> None:
+        """out[t][h] = the reference's composite FA of q[t][h] over cells [0, n_kv) of kv.
+        q / out: device f32 [T][n_head][head_dim]; mask: host numpy f16 [T][stride] or None;
+        cfg: (C, t_max, pcap, k_max) or None for the release values."""
+        import numpy as np
+        mptr, mstride, keep = None, 0, None
+        if mask is not None:
+            keep = np.ascontiguousarray(mask, dtype=np.float16)
+            mptr, mstride = keep.ctypes.data, keep.shape[-1]
+        c = None if cfg is None else FaCfg(*cfg)
+        _check(lib().tsrc_flash_attn(self.handle, kv.handle, _addr(q), T, n_head, n_kv, mptr, mstride, scale,
+                                     new[0], new[1], None if c is None else ct.byref(c), _addr(out),
+                                     _stream(stream)))
+
 
 class Weight:
     """A weight shard resident in device memory."""
@@ -244,4 +280,42 @@ class Weight:
     def free(self) -> None:
         if self.handle and self.dev.handle:
             _check(lib().tsrc_weight_free(self.handle))
+        self.handle = None
+
+
+class KvCache:
+    """One layer's q8_0 K and V cache resident in device memory."""
+
+    def __init__(self, dev: Device, handle, n_head_kv: int, head_dim: int, n_cells: int):
+        self.dev, self.handle = dev, handle
+        self.n_head_kv, self.head_dim, self.n_cells = n_head_kv, head_dim, n_cells
+        self.E = n_head_kv * head_dim
+
+    @property
+    def row_bytes(self) -> int:
+        return self.E // 32 * Q8_0_BLOCK_BYTES
+
+    def set_bytes(self, which: int, ggml_rows, cell0: int = 0) -> None:
+        """ggml q8_0 rows (numpy uint8 [n, row_bytes]) -> cells [cell0, cell0 + n)."""
+        import numpy as np
+        a = np.ascontiguousarray(ggml_rows, dtype=np.uint8).reshape(-1, self.row_bytes)
+        _check(lib().tsrc_kv_set_bytes(self.handle, which, a.ctypes.data, cell0, a.shape[0]))
+
+    def get_bytes(self, which: int, cell0: int = 0, n: int | None = None):
+        import numpy as np
+        n = self.n_cells - cell0 if n is None else n
+        out = np.zeros((n, self.row_bytes), np.uint8)
+        _check(lib().tsrc_kv_get_bytes(self.handle, which, out.ctypes.data, cell0, n))
+        return out
+
+    def set_rows(self, which: int, rows, n: int | None = None, cells=None, cell0: int = 0, row_stride: int = 0,
+                 stream=None) -> None:
+        """KVST of f32 device rows [n][E] (SET_ROWS): at cells (device int64) or cell0 + i."""
+        n = rows.shape[0] if n is None else n
+        _check(lib().tsrc_kv_set_rows(self.dev.handle, self.handle, which, _addr(rows), n, row_stride,
+                                      _addr(cells), cell0, _stream(stream)))
+
+    def free(self) -> None:
+        if self.handle and self.dev.handle:
+            _check(lib().tsrc_kv_free(self.handle))
         self.handle = None

@@ -38,6 +38,12 @@ def test_null_arguments_are_errors_not_crashes():
     assert L.tsrc_weight_free(None) == tsrc.E_ARG
     assert L.tsrc_mul_mat(None, None, None, 1, 0, None, 0, None, 0, 0, 1.0, 1.0, None) == tsrc.E_ARG
     assert L.tsrc_open(0, None) == tsrc.E_ARG
+    assert L.tsrc_kv_create(None, 1, 64, 16, None) == tsrc.E_ARG
+    assert L.tsrc_kv_free(None) == tsrc.E_ARG
+    assert L.tsrc_kv_set_rows(None, None, 0, None, 1, 0, None, 0, None) == tsrc.E_ARG
+    assert L.tsrc_kv_set_bytes(None, 0, None, 0, 1) == tsrc.E_ARG
+    assert L.tsrc_kv_get_bytes(None, 0, None, 0, 1) == tsrc.E_ARG
+    assert L.tsrc_flash_attn(None, None, None, 1, 4, 1, None, 0, 0.125, 0, 0, None, None, None) == tsrc.E_ARG
 
 
 def test_open_without_device():
