@@ -596,8 +596,8 @@ int tsrc_kv_set_rows(tsrc_ctx* ctx, tsrc_kv* kv, uint32_t which, const float* ro
     if (n == 0) return TSRC_OK;
     int rc = use_device(ctx);
     if (rc) return rc;
-    cudaError_t e = tsrc::launch_kv_store(rows, n, row_stride, cells, cell0, kv->n_head_kv, kv->D, kv->n_alloc, kv->q[which],
-                                          kv->d[which], static_cast<cudaStream_t>(stream));
+    cudaError_t e = tsrc::launch_kv_store(rows, n, row_stride, cells, cell0, kv->n_head_kv, kv->D, kv->n_alloc,
+                                          which == TSRC_KV_V, kv->q[which], kv->d[which], static_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) return cuda_fail(e, "KVST launch");
     return TSRC_OK;
 }
@@ -616,12 +616,14 @@ static int kv_bytes_io(tsrc_kv* kv, uint32_t which, void* host, uint32_t cell0, 
     if (to_device) {
         e = cudaMemcpy(stage, host, bytes, cudaMemcpyHostToDevice);
         if (e == cudaSuccess)
-            e = tsrc::launch_kv_from_ggml(stage, n, cell0, kv->n_head_kv, kv->D, kv->n_alloc, kv->q[which], kv->d[which], 0);
+            e = tsrc::launch_kv_from_ggml(stage, n, cell0, kv->n_head_kv, kv->D, kv->n_alloc, which == TSRC_KV_V, kv->q[which],
+                                          kv->d[which], 0);
         if (e == cudaSuccess) e = cudaDeviceSynchronize();
     } else {
         e = cudaDeviceSynchronize();
         if (e == cudaSuccess)
-            e = tsrc::launch_kv_to_ggml(kv->q[which], kv->d[which], n, cell0, kv->n_head_kv, kv->D, kv->n_alloc, stage, 0);
+            e = tsrc::launch_kv_to_ggml(kv->q[which], kv->d[which], n, cell0, kv->n_head_kv, kv->D, kv->n_alloc,
+                                        which == TSRC_KV_V, stage, 0);
         if (e == cudaSuccess) e = cudaDeviceSynchronize();
         if (e == cudaSuccess) e = cudaMemcpy(host, stage, bytes, cudaMemcpyDeviceToHost);
     }
@@ -684,8 +686,8 @@ int tsrc_flash_attn(tsrc_ctx* ctx, const tsrc_kv* kv, const float* q, uint32_t T
     const uint32_t rows_max = po.Tq0 * po.G;
     const size_t b_items = align256((size_t)n_items * sizeof(tsrc::FaItem));
     const size_t b_tiles = align256((size_t)(po.n_tiles + 1u) * 4u);
-    const size_t b_oc = align256((size_t)n_items * kv->n_head_kv * c.C * rows_max * kv->D * 4u);
-    const size_t b_lc = align256((size_t)n_items * kv->n_head_kv * c.C * rows_max * 4u);
+    const size_t b_oc = align256((size_t)n_items * kv->n_head_kv * rows_max * kv->D * 4u);
+    const size_t b_lc = align256((size_t)n_items * kv->n_head_kv * rows_max * 4u);
     const size_t b_mk = align256((size_t)n_items * kv->n_head_kv * rows_max * 4u);
     const size_t b_m16 = po.general ? align256((size_t)T * mask_stride * 2u) : 0u;
     const size_t b_mf = po.general ? align256((size_t)T * n_kv * 4u) : 0u;
@@ -698,18 +700,26 @@ int tsrc_flash_attn(tsrc_ctx* ctx, const tsrc_kv* kv, const float* q, uint32_t T
     tsrc::FaLaunch a{};
     a.items = reinterpret_cast<const tsrc::FaItem*>(p);
     a.tile_items = reinterpret_cast<const uint32_t*>(p + b_items);
-    a.oc = reinterpret_cast<float*>(p + b_items + b_tiles);
-    a.lc = reinterpret_cast<float*>(p + b_items + b_tiles + b_oc);
+    a.ok = reinterpret_cast<float*>(p + b_items + b_tiles);
+    a.lk = reinterpret_cast<float*>(p + b_items + b_tiles + b_oc);
     a.mk = reinterpret_cast<float*>(p + b_items + b_tiles + b_oc + b_lc);
     uint16_t* m16 = reinterpret_cast<uint16_t*>(p + b_items + b_tiles + b_oc + b_lc + b_mk);
     float* mf = reinterpret_cast<float*>(p + b_items + b_tiles + b_oc + b_lc + b_mk + b_m16);
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    // host -> device copies of the plan (and the mask of a GENERAL call): the sources are staged
-    // before cudaMemcpyAsync returns, so they may be released right after
-    cudaError_t e = cudaMemcpyAsync(const_cast<tsrc::FaItem*>(a.items), items, (size_t)n_items * sizeof(tsrc::FaItem),
-                                    cudaMemcpyHostToDevice, st);
-    if (e == cudaSuccess)
-        e = cudaMemcpyAsync(const_cast<uint32_t*>(a.tile_items), tiles, (size_t)(po.n_tiles + 1u) * 4u, cudaMemcpyHostToDevice, st);
+    cudaError_t e = cudaSuccess;
+    if (n_items <= tsrc::kFaInlineItems) {
+        // a small plan travels in the kernel parameters (no copy: the call can be graph-captured)
+        std::memcpy(a.inl_items, items, (size_t)n_items * sizeof(tsrc::FaItem));
+        std::memcpy(a.inl_tiles, tiles, (size_t)(po.n_tiles + 1u) * 4u);
+    } else {
+        // host -> device copies of the plan: the sources are staged before cudaMemcpyAsync
+        // returns, so they may be released right after
+        e = cudaMemcpyAsync(const_cast<tsrc::FaItem*>(a.items), items, (size_t)n_items * sizeof(tsrc::FaItem),
+                            cudaMemcpyHostToDevice, st);
+        if (e == cudaSuccess)
+            e = cudaMemcpyAsync(const_cast<uint32_t*>(a.tile_items), tiles, (size_t)(po.n_tiles + 1u) * 4u,
+                                cudaMemcpyHostToDevice, st);
+    }
     tsrc::fa_plan_free(items, tiles);
     if (e == cudaSuccess && po.general) {
         e = cudaMemcpyAsync(m16, mask, (size_t)T * mask_stride * 2u, cudaMemcpyHostToDevice, st);

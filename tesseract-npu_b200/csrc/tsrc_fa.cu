@@ -35,7 +35,7 @@ constexpr uint32_t kNegInf = 0xFF800000u;
 constexpr uint32_t kMFloor = 0xF1800000u;      // -2^100: MAXOUT's floor (sw/sim/include/tsr_tables.h:89)
 constexpr uint32_t kLFloor = 0x00800000u;      // 2^-126: ANORM's floor of the row sum (tsr_tables.h:90)
 constexpr uint32_t kFlCausal = 1u, kFlSlide = 2u;
-constexpr uint32_t kWPad = 65u;                 // int32 words per (row, slice, block) of a warp's W table
+constexpr uint32_t kWdStride = 80u;             // bytes per row of a W-digit table (64 cells + pad: no bank conflicts)
 
 // MAXT (VU §6.8; tsr_ref_at.c:318-325): NaN -> canonical NaN, else the larger value, -0 < +0.
 __device__ __forceinline__ float maxt(float a, float b) {
@@ -134,24 +134,34 @@ __device__ __forceinline__ void prefetch_l2(const void* src, uint32_t bytes) {
 
 // Shared-memory plan of fa_chunk_kernel (host and device agree).
 struct FaSmem {
-    uint32_t s_off, w_off, cv_off, misc_off, total;
+    uint32_t qx_off, dx_off, s_off, w_off, cv_off, vq_off, vs_off, misc_off, total;
 };
 
 __host__ __device__ inline uint32_t fa_a16(uint32_t n) { return (n + 15u) & ~15u; }
+// values of a 64-cell segment whose V quants one warp stages at a time (<= 8 KB a warp)
+__host__ __device__ inline uint32_t fa_vp(uint32_t D) { return D <= 128u ? D : 128u; }
+// rows of a W-digit table: RB rows x 4 digits (an 8-wide tensor-core tile wraps around a 4-row
+// table; the extra output columns are not used)
+__host__ __device__ inline uint32_t fa_wd_rows(uint32_t D) { return 4u * (512u / D); }
 
 __host__ __device__ inline FaSmem fa_smem(uint32_t D, uint32_t ncell_max) {
     const uint32_t RB = 512u / D, ND = D / 32u, NSL = D / 64u;
     FaSmem s{};
-    uint32_t o = 64u * 4u + 4u * 8u;                          // EXPK tables
-    o = fa_a16(o);
+    uint32_t o = fa_a16(64u * 4u + 4u * 8u);                    // EXPK tables
+    s.qx_off = o;
     o += fa_a16(RB * D);                                        // qx [RB][D]
+    s.dx_off = o;
     o += fa_a16(RB * ND * 4u);                                  // dx [RB][ND]
     s.s_off = o;
     o += fa_a16(RB * ncell_max * 4u);                           // S [RB][ncell_max]
     s.w_off = o;
-    o += fa_a16(kFaWarps * RB * NSL * 2u * kWPad * 4u);         // W [warp][RB][NSL][2][kWPad]
+    o += fa_a16(kFaWarps * NSL * 2u * fa_wd_rows(D) * kWdStride); // W digits [warp][NSL][2][rows][kWdStride]
     s.cv_off = o;
-    o += fa_a16(kFaWarps * RB * D * 4u);                        // CV [warp][RB][D]
+    o += fa_a16(kFaWarps * RB * D * 4u);                        // CV [warp][RB][D]; then the channel's O [RB][D]
+    s.vq_off = o;
+    o += fa_a16(kFaWarps * 64u * fa_vp(D));                     // V quants of a segment [warp][4 groups][VP][16]
+    s.vs_off = o;
+    o += fa_a16(kFaWarps * 64u * ND * 2u);                      // V scales of a segment [warp][64][ND]
     s.misc_off = o;
     // mx [2][RB], mk [RB], wmax [warps][RB], ls [warps][RB], lacc [RB], es [warps][RB][NSL], fl [warps][RB][NSL]
     o += 4u * (2u * RB + RB + kFaWarps * RB + kFaWarps * RB + RB + 2u * kFaWarps * RB * NSL);
@@ -159,15 +169,37 @@ __host__ __device__ inline FaSmem fa_smem(uint32_t D, uint32_t ncell_max) {
     return s;
 }
 
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(smem_dst)), "l"(gmem_src)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+
+// CTREE (tsr_ref_at.c:588-598) of n <= 16 values: pairwise by levels, an unpaired last element
+// passes through. Fully unrolled (static indices, values stay in registers).
+__device__ __forceinline__ float ctree16(float (&v)[16], uint32_t n) {
+#pragma unroll
+    for (int lvl = 0; lvl < 4; ++lvl) {
+#pragma unroll
+        for (uint32_t k = 0; k < 8; ++k) {
+            if (2u * k + 1u < n) v[k] = fadd(v[2 * k], v[2 * k + 1]);
+            else if (2u * k + 1u == n) v[k] = v[2 * k];
+        }
+        n = (n + 1u) / 2u;
+    }
+    return v[0];
+}
+
 // ---------------------------------------------------------------------------------------------------
 template <int D>
-__global__ void __launch_bounds__(kFaThreads) fa_chunk_kernel(FaLaunch a) {
+__global__ void __launch_bounds__(kFaThreads, 1) fa_chunk_kernel(FaLaunch a) {
     constexpr uint32_t ND = D / 32, NSL = D / 64, RB = 512 / D, NV = D / 32;
     extern __shared__ __align__(16) uint8_t smem[];
     cg::cluster_group cluster = cg::this_cluster();
     const uint32_t C = a.C, cc = cluster.block_rank();
     const uint32_t ig = blockIdx.x / C, item = ig / a.n_head_kv, g = ig - item * a.n_head_kv;
-    const FaItem it = a.items[item];
+    const FaItem it = a.n_items <= kFaInlineItems ? a.inl_items[item] : a.items[item];
     const uint32_t G = a.G, rows = it.Tq * G, rows_max = a.Tq0 * G;
     const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31u;
 
@@ -177,6 +209,10 @@ __global__ void __launch_bounds__(kFaThreads) fa_chunk_kernel(FaLaunch a) {
     const uint32_t ncell = 16u * nu;
     const uint32_t ncell_max = 16u * ((it.n + C - 1u) / C);
     const FaSmem P = fa_smem(D, ncell_max);
+    constexpr uint32_t VP = D <= 128 ? D : 128u;               // fa_vp(D)
+    constexpr uint32_t kWdRows = 4u * RB;                      // fa_wd_rows(D)
+    constexpr uint32_t kNT = kWdRows < 8u ? 1u : kWdRows / 8u; // 8-wide tensor-core tiles of the W digits
+    constexpr uint32_t kWdWarp = NSL * 2u * kWdRows * kWdStride;
 
     const size_t head_cells = (size_t)g * a.n_cells;
     // K and V of the channel's visible groups: HBM -> L2 now
@@ -192,11 +228,13 @@ __global__ void __launch_bounds__(kFaThreads) fa_chunk_kernel(FaLaunch a) {
 
     uint32_t* t64s = reinterpret_cast<uint32_t*>(smem);
     uint64_t* lks = reinterpret_cast<uint64_t*>(smem + 256);
-    int8_t* qx = reinterpret_cast<int8_t*>(smem + fa_a16(64u * 4u + 4u * 8u));
-    float* dx = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(qx) + fa_a16(RB * D));
+    int8_t* qx = reinterpret_cast<int8_t*>(smem + P.qx_off);
+    float* dx = reinterpret_cast<float*>(smem + P.dx_off);
     float* S = reinterpret_cast<float*>(smem + P.s_off);
-    int32_t* Wt = reinterpret_cast<int32_t*>(smem + P.w_off);
+    uint8_t* Wbase = smem + P.w_off;
     float* CV = reinterpret_cast<float*>(smem + P.cv_off);
+    int8_t* vqs = reinterpret_cast<int8_t*>(smem + P.vq_off) + warp * 64u * VP;
+    uint16_t* vss = reinterpret_cast<uint16_t*>(smem + P.vs_off) + warp * 64u * ND;
     float* mx = reinterpret_cast<float*>(smem + P.misc_off);   // [2][RB]
     float* mk = mx + 2u * RB;                                    // [RB]
     float* wmax = mk + RB;                                       // [warps][RB]
@@ -209,12 +247,33 @@ __global__ void __launch_bounds__(kFaThreads) fa_chunk_kernel(FaLaunch a) {
 
     const uint32_t nseg = (nu + 3u) / 4u;
     const float scale = a.scale;
-    float* oc_base = a.oc + (((size_t)item * a.n_head_kv + g) * C + cc) * rows_max * D;
-    float* lc_base = a.lc + (((size_t)item * a.n_head_kv + g) * C + cc) * rows_max;
+
+    // cell of the channel's local index j (cells of group k are 16 k .. 16 k + 15)
+    auto cell_of = [&](uint32_t j) { return 16u * (ufirst + C * (j >> 4)) + (j & 15u); };
+    // this warp's copies of segment sg into shared memory: of each of its groups the quants of
+    // values [ph VP, ph VP + VP) (16 cells each, value-major), and (with scales) the fp16 scales of
+    // all its cells; one commit group
+    auto stage_v = [&](uint32_t sg, uint32_t ph, bool scales) {
+        const uint32_t ng = min(4u, nu - 4u * sg);
+        for (uint32_t c = lane; c < ng * VP; c += 32u) {         // VP 16-byte chunks per group
+            const uint32_t kk = c / VP, off = (c % VP) * 16u;
+            const int8_t* src = a.vq + (head_cells + 16u * (ufirst + C * (4u * sg + kk))) * D + (size_t)ph * VP * 16u;
+            cp_async16(vqs + kk * VP * 16u + off, src + off);
+        }
+        if (scales) {
+            for (uint32_t c = lane; c < ng * 2u * ND; c += 32u) {    // a group's scales: 32 ND bytes
+                const uint32_t kk = c / (2u * ND), off = (c % (2u * ND)) * 16u;
+                const uint8_t* src = reinterpret_cast<const uint8_t*>(a.vd + (head_cells + 16u * (ufirst + C * (4u * sg + kk))) * ND);
+                cp_async16(reinterpret_cast<uint8_t*>(vss) + kk * 32u * ND + off, src + off);
+            }
+        }
+        cp_async_commit();
+    };
 
     uint32_t pass = 0;
     for (uint32_t r0 = 0; r0 < rows; r0 += RB, ++pass) {
         const uint32_t nr = min(RB, rows - r0);
+        if (warp < nseg) stage_v(warp, 0, true);                 // round 0's V, in flight during ATTQK
         // ---- QACT A32 of the pass's query rows (tsr_ref.c:472-487): one warp per 32-block ----
         for (uint32_t bi = warp; bi < nr * ND; bi += kFaWarps) {
             const uint32_t r = bi / ND, b = bi - r * ND, ri = r0 + r;
@@ -233,7 +292,7 @@ __global__ void __launch_bounds__(kFaThreads) fa_chunk_kernel(FaLaunch a) {
 #pragma unroll
         for (uint32_t r = 0; r < RB; ++r) rmax[r] = ffrom(kMFloor);
         for (uint32_t j = tid; j < ncell; j += kFaThreads) {
-            const uint32_t k = j >> 4, u = ufirst + C * k, cell = 16u * u + (j & 15u);
+            const uint32_t cell = cell_of(j);
             const int64_t jr = (int64_t)cell - 16 * (int64_t)it.u0;         // cell within the chunk
             const int8_t* kr = a.kq + (head_cells + cell) * D;
             const uint16_t* kdr = a.kd + (head_cells + cell) * ND;
@@ -331,31 +390,16 @@ __global__ void __launch_bounds__(kFaThreads) fa_chunk_kernel(FaLaunch a) {
             const uint32_t sg = sg0 + warp;
             if (sg < nseg) {
                 const uint32_t ng = min(4u, nu - 4u * sg), nc = 16u * ng;
-                int32_t* W = Wt + warp * RB * NSL * 2u * kWPad;
-                // the two cells of this lane: i = lane, lane + 32
-                uint32_t cellv[2];
-                float dvv[2][NSL][2];
-#pragma unroll
-                for (uint32_t h = 0; h < 2; ++h) {
-                    const uint32_t i = lane + 32u * h, jl = 64u * sg + i;
-                    const uint32_t cell = 16u * (ufirst + C * (jl >> 4)) + (jl & 15u);
-                    cellv[h] = cell;
-#pragma unroll
-                    for (uint32_t sl = 0; sl < NSL; ++sl) {
-                        dvv[h][sl][0] = 0.0f;
-                        dvv[h][sl][1] = 0.0f;
-                        if (i < nc) {
-                            const uint32_t pr = *reinterpret_cast<const uint32_t*>(a.vd + (head_cells + cell) * ND + 2u * sl);
-                            dvv[h][sl][0] = h2f((uint16_t)(pr & 0xFFFFu));
-                            dvv[h][sl][1] = h2f((uint16_t)(pr >> 16));
-                        }
-                    }
-                }
+                uint8_t* Wd = Wbase + warp * kWdWarp;
+                if (sg0 > 0) stage_v(sg, 0, true);
+                cp_async_wait_all();
+                __syncwarp();
 #pragma unroll
                 for (uint32_t r = 0; r < RB; ++r) {
                     if (r >= nr) break;
 #pragma unroll
                     for (uint32_t sl = 0; sl < NSL; ++sl) {
+                        // w = p (*) dV of the lane's two cells and the slice's two blocks
                         float w[2][2];
                         int32_t le = -1000;
                         bool bad0 = false, bad1 = false, any = false;
@@ -364,9 +408,10 @@ __global__ void __launch_bounds__(kFaThreads) fa_chunk_kernel(FaLaunch a) {
                             const uint32_t i = lane + 32u * h;
                             const float p = i < nc ? S[r * ncell_max + 64u * sg + i] : 0.0f;
                             const bool pz = (fbits(p) & kExp) == 0;
+                            const uint32_t pr = i < nc ? *reinterpret_cast<const uint32_t*>(vss + i * ND + 2u * sl) : 0u;
 #pragma unroll
                             for (uint32_t e = 0; e < 2; ++e) {
-                                const float wv = pz ? 0.0f : fmul(p, dvv[h][sl][e]);
+                                const float wv = pz ? 0.0f : fmul(p, h2f((uint16_t)(e ? pr >> 16 : pr & 0xFFFFu)));
                                 w[h][e] = wv;
                                 const uint32_t u = fbits(wv);
                                 if (nonfinite(u)) {
@@ -382,12 +427,22 @@ __global__ void __launch_bounds__(kFaThreads) fa_chunk_kernel(FaLaunch a) {
                         bad0 = __any_sync(0xFFFFFFFFu, bad0);
                         bad1 = __any_sync(0xFFFFFFFFu, bad1);
                         any = __any_sync(0xFFFFFFFFu, any);
+                        // W = RNE_int(w 2^(23 - es)) (|W| <= 2^24) as four balanced base-256 digits,
+                        // the B operand of the int8 tensor-core products: table (sl, e), row r*4 + digit
 #pragma unroll
                         for (uint32_t h = 0; h < 2; ++h)
 #pragma unroll
-                            for (uint32_t e = 0; e < 2; ++e)
-                                W[((r * NSL + sl) * 2u + e) * kWPad + lane + 32u * h] =
-                                    (any && !(e ? bad1 : bad0)) ? bf_int(w[h][e], es) : 0;
+                            for (uint32_t e = 0; e < 2; ++e) {
+                                const int32_t Wv = (any && !(e ? bad1 : bad0)) ? bf_int(w[h][e], es) : 0;
+                                const int32_t d0 = (int8_t)(Wv & 0xFF), W1 = (Wv - d0) >> 8;
+                                const int32_t d1 = (int8_t)(W1 & 0xFF), W2 = (W1 - d1) >> 8;
+                                const int32_t d2 = (int8_t)(W2 & 0xFF), d3 = (W2 - d2) >> 8;
+                                uint8_t* col = Wd + ((sl * 2u + e) * kWdRows + r * 4u) * kWdStride + lane + 32u * h;
+                                col[0] = (uint8_t)d0;
+                                col[kWdStride] = (uint8_t)d1;
+                                col[2u * kWdStride] = (uint8_t)d2;
+                                col[3u * kWdStride] = (uint8_t)d3;
+                            }
                         if (lane == 0) {
                             esw[(warp * RB + r) * NSL + sl] = es;
                             flw[(warp * RB + r) * NSL + sl] = (bad0 ? 1u : 0u) | (bad1 ? 2u : 0u) | (any ? 4u : 0u);
@@ -420,53 +475,65 @@ __global__ void __launch_bounds__(kFaThreads) fa_chunk_kernel(FaLaunch a) {
                     }
                 }
                 __syncwarp();
-                // exact sums A = sum_i W_i * qV_i for this lane's NV values
-                const uint32_t v0 = lane * NV, sl = v0 / 64u, e = (v0 % 64u) / 32u;
-                int64_t A[RB][NV];
+                // exact sums A[r][v] = sum_cells W * qV on the int8 tensor cores (m16n8k32): A operand
+                // = V^T (16 values x 32 cells, from the value-major groups), B operand = the W digits
+                // (32 cells x 8 = 2 rows x 4 digits); digit sums are exact in int32 (|.| <= 2^20)
+                const uint32_t gid = lane >> 2, tig = lane & 3u;
+                const uint32_t nks = (ng + 1u) / 2u;
+                float* cvw = CV + warp * RB * D;
+                for (uint32_t ph = 0; ph < D / VP; ++ph) {
+                    if (ph > 0) {                          // the next values of the segment (D = 512)
+                        __syncwarp();
+                        stage_v(sg, ph, false);
+                        cp_async_wait_all();
+                        __syncwarp();
+                    }
+#pragma unroll 1
+                    for (uint32_t mt = 0; mt < VP / 16u; ++mt) {
+                        const uint32_t v0 = ph * VP + 16u * mt, sl = v0 / 64u, e = (v0 % 64u) / 32u;
+                        const uint8_t* Wt_se = Wd + (sl * 2u + e) * kWdRows * kWdStride;
+                        int32_t acc[kNT][4];
 #pragma unroll
-                for (uint32_t r = 0; r < RB; ++r)
+                        for (uint32_t nt = 0; nt < kNT; ++nt)
 #pragma unroll
-                    for (uint32_t i = 0; i < NV; ++i) A[r][i] = 0;
-                for (uint32_t i = 0; i < nc; ++i) {
-                    const uint32_t jl = 64u * sg + i;
-                    const uint32_t cell = 16u * (ufirst + C * (jl >> 4)) + (jl & 15u);
-                    const int8_t* vp = a.vq + (head_cells + cell) * D + v0;
-                    int8_t qv[NV];
-                    if (NV == 2) {
-                        const uint16_t x = *reinterpret_cast<const uint16_t*>(vp);
+                            for (uint32_t j = 0; j < 4; ++j) acc[nt][j] = 0;
+                        for (uint32_t ks = 0; ks < nks; ++ks) {
+                            const uint8_t* va = reinterpret_cast<const uint8_t*>(vqs) + ((2u * ks) * VP + 16u * mt + gid) * 16u + tig * 4u;
+                            const uint32_t a0 = *reinterpret_cast<const uint32_t*>(va);
+                            const uint32_t a1 = *reinterpret_cast<const uint32_t*>(va + 8u * 16u);
+                            const uint32_t a2 = *reinterpret_cast<const uint32_t*>(va + VP * 16u);
+                            const uint32_t a3 = *reinterpret_cast<const uint32_t*>(va + VP * 16u + 8u * 16u);
 #pragma unroll
-                        for (uint32_t k = 0; k < NV; ++k) qv[k] = (int8_t)(x >> (8 * k));
-                    } else if (NV == 4) {
-                        const uint32_t x = *reinterpret_cast<const uint32_t*>(vp);
+                            for (uint32_t nt = 0; nt < kNT; ++nt) {
+                                const uint8_t* wb = Wt_se + ((nt * 8u + gid) % kWdRows) * kWdStride + 32u * ks + tig * 4u;
+                                const uint32_t b0 = *reinterpret_cast<const uint32_t*>(wb);
+                                const uint32_t b1 = *reinterpret_cast<const uint32_t*>(wb + 16u);
+                                asm volatile(
+                                    "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+                                    "{%0,%1,%2,%3};"
+                                    : "+r"(acc[nt][0]), "+r"(acc[nt][1]), "+r"(acc[nt][2]), "+r"(acc[nt][3])
+                                    : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+                            }
+                        }
+                        // digits 0,1 sit in even lanes (tig even), 2,3 in the odd neighbour: even lanes
+                        // finish value gid, odd lanes value gid + 8
+                        const bool odd = (tig & 1u) != 0;
 #pragma unroll
-                        for (uint32_t k = 0; k < NV; ++k) qv[k] = (int8_t)(x >> (8 * k));
-                    } else {
-#pragma unroll
-                        for (uint32_t k0 = 0; k0 < NV; k0 += 8) {
-                            const uint2 x = *reinterpret_cast<const uint2*>(vp + k0);
-#pragma unroll
-                            for (uint32_t k = 0; k < 8 && k0 + k < NV; ++k)
-                                qv[k0 + k] = (int8_t)((k < 4 ? x.x : x.y) >> (8 * (k & 3u)));
+                        for (uint32_t nt = 0; nt < kNT; ++nt) {
+                            const int32_t s0 = odd ? acc[nt][0] : acc[nt][2], s1 = odd ? acc[nt][1] : acc[nt][3];
+                            const int32_t o0 = __shfl_xor_sync(0xFFFFFFFFu, s0, 1), o1 = __shfl_xor_sync(0xFFFFFFFFu, s1, 1);
+                            int64_t Av;
+                            if (!odd) Av = (int64_t)acc[nt][0] + ((int64_t)acc[nt][1] << 8) + ((int64_t)o0 << 16) + ((int64_t)o1 << 24);
+                            else Av = (int64_t)o0 + ((int64_t)o1 << 8) + ((int64_t)acc[nt][2] << 16) + ((int64_t)acc[nt][3] << 24);
+                            const uint32_t r = nt * 2u + (tig >> 1), v = v0 + gid + (odd ? 8u : 0u);
+                            if (r < nr) {
+                                const int32_t es = esw[(warp * RB + r) * NSL + sl];
+                                const uint32_t fl = flw[(warp * RB + r) * NSL + sl];
+                                const bool bad = (fl >> e) & 1u, any = (fl & 4u) != 0;
+                                cvw[r * D + v] = bad ? ffrom(kCanonNaN) : !any ? 0.0f : bf_f(Av, es - 23);
+                            }
                         }
                     }
-#pragma unroll
-                    for (uint32_t r = 0; r < RB; ++r) {
-                        if (r >= nr) break;
-                        const int64_t Wv = W[((r * NSL + sl) * 2u + e) * kWPad + i];
-#pragma unroll
-                        for (uint32_t k = 0; k < NV; ++k) A[r][k] += Wv * (int64_t)qv[k];
-                    }
-                }
-                float* cvw = CV + warp * RB * D;
-#pragma unroll
-                for (uint32_t r = 0; r < RB; ++r) {
-                    if (r >= nr) break;
-                    const int32_t es = esw[(warp * RB + r) * NSL + sl];
-                    const uint32_t fl = flw[(warp * RB + r) * NSL + sl];
-                    const bool bad = (fl >> e) & 1u, any = (fl & 4u) != 0;
-#pragma unroll
-                    for (uint32_t k = 0; k < NV; ++k)
-                        cvw[r * D + v0 + k] = bad ? ffrom(kCanonNaN) : !any ? 0.0f : bf_f(A[r][k], es - 23);
                 }
             }
             __syncthreads();
@@ -485,30 +552,30 @@ __global__ void __launch_bounds__(kFaThreads) fa_chunk_kernel(FaLaunch a) {
             }
             __syncthreads();
         }
-        // the channel's partials of this pass
+        // ---- CTREE over the cluster's channels; CTA cc writes every C-th (row, value) ----
 #pragma unroll
-        for (uint32_t i = 0; i < kPer; ++i) {
-            const uint32_t pidx = tid + i * kFaThreads, r = pidx / D;
-            if (r < nr) oc_base[(size_t)(r0 + r) * D + (pidx - r * D)] = oacc[i];
+        for (uint32_t i = 0; i < kPer; ++i) CV[tid + i * kFaThreads] = oacc[i];
+        cluster.sync();
+        float* ok_base = a.ok + ((size_t)item * a.n_head_kv + g) * rows_max * D + (size_t)r0 * D;
+        for (uint32_t pidx = cc * kFaThreads + tid; pidx < nr * D; pidx += C * kFaThreads) {
+            float xv[16];
+#pragma unroll
+            for (uint32_t c = 0; c < 16; ++c) xv[c] = c < C ? *cluster.map_shared_rank(CV + pidx, c) : 0.0f;
+            ok_base[pidx] = ctree16(xv, C);
         }
-        if (tid < nr) lc_base[r0 + tid] = lacc[tid];
-        __syncthreads();
+        if (tid < nr && tid % C == cc) {
+            float xv[16];
+#pragma unroll
+            for (uint32_t c = 0; c < 16; ++c) xv[c] = c < C ? *cluster.map_shared_rank(lacc + tid, c) : 0.0f;
+            a.lk[((size_t)item * a.n_head_kv + g) * rows_max + r0 + tid] = ctree16(xv, C);
+        }
+        // no CTA may overwrite (next pass) or release (exit) what another still reads
+        cluster.sync();
     }
-    // no CTA of the cluster may leave while another can still read its shared memory
-    cluster.sync();
-}
-
-// CTREE (tsr_ref_at.c:588-598): pairwise by levels, an unpaired last element passes through.
-__device__ __forceinline__ float ctree(float (&v)[16], uint32_t n) {
-    while (n > 1) {
-        for (uint32_t k = 0; 2 * k + 1 < n; ++k) v[k] = fadd(v[2 * k], v[2 * k + 1]);
-        if (n & 1u) v[n / 2] = v[n - 1];
-        n = (n + 1) / 2;
-    }
-    return v[0];
 }
 
 // AMERGE over the chunks of each tile in execution order, then ANORM (tsr_ref_at.c:600-641).
+// One thread per output value; the chunk values of 4 items are loaded before they are folded.
 __global__ void __launch_bounds__(256) fa_merge_kernel(FaLaunch a) {
     const uint32_t G = a.G, D = a.D, rows_max = a.Tq0 * G;
     const size_t per_tile = (size_t)a.n_head_kv * rows_max * D;
@@ -519,32 +586,39 @@ __global__ void __launch_bounds__(256) fa_merge_kernel(FaLaunch a) {
     const uint32_t g = (uint32_t)(rem / ((size_t)rows_max * D));
     rem -= (size_t)g * rows_max * D;
     const uint32_t ri = (uint32_t)(rem / D), v = (uint32_t)(rem - (size_t)ri * D);
-    const uint32_t i0 = a.tile_items[tile], i1 = a.tile_items[tile + 1];
-    const FaItem first = a.items[i0];
+    const bool inl = a.n_items <= kFaInlineItems;
+    const uint32_t i0 = inl ? a.inl_tiles[tile] : a.tile_items[tile], i1 = inl ? a.inl_tiles[tile + 1] : a.tile_items[tile + 1];
+    const FaItem first = inl ? a.inl_items[i0] : a.items[i0];
     if (ri >= first.Tq * G) return;
-    const uint32_t C = a.C;
     const float scale = a.scale;
     float O = 0.0f, lrun = 0.0f, mrun = 0.0f;
-    for (uint32_t k = i0; k < i1; ++k) {
-        float xo[16], xl[16];
-        for (uint32_t c = 0; c < C; ++c) {
-            const size_t base = ((size_t)k * a.n_head_kv + g) * C + c;
-            xo[c] = a.oc[(base * rows_max + ri) * D + v];
-            xl[c] = a.lc[base * rows_max + ri];
+    constexpr uint32_t kB = 4;
+    for (uint32_t k0 = i0; k0 < i1; k0 += kB) {
+        float ok[kB], lk[kB], mkk[kB];
+#pragma unroll
+        for (uint32_t j = 0; j < kB; ++j) {
+            if (k0 + j < i1) {
+                const size_t base = (size_t)(k0 + j) * a.n_head_kv + g;
+                ok[j] = a.ok[(base * rows_max + ri) * D + v];
+                lk[j] = a.lk[base * rows_max + ri];
+                mkk[j] = a.mk[base * rows_max + ri];
+            }
         }
-        const float ok = ctree(xo, C), lk = ctree(xl, C);
-        const float mkk = a.mk[((size_t)k * a.n_head_kv + g) * rows_max + ri];
-        if (k == i0) {
-            O = ok;
-            lrun = lk;
-            mrun = mkk;
-        } else {
-            const float mn = maxt(mrun, mkk);
-            const float ea = expk(fmul(fsub(mrun, mn), scale), 0u, g_expk_t64, g_expk_lk);
-            const float eb = expk(fmul(fsub(mkk, mn), scale), 0u, g_expk_t64, g_expk_lk);
-            lrun = fadd(fmul(lrun, ea), fmul(lk, eb));
-            mrun = mn;
-            O = fadd(fmul(O, ea), fmul(ok, eb));
+#pragma unroll
+        for (uint32_t j = 0; j < kB; ++j) {
+            if (k0 + j >= i1) break;
+            if (k0 + j == i0) {
+                O = ok[j];
+                lrun = lk[j];
+                mrun = mkk[j];
+            } else {
+                const float mn = maxt(mrun, mkk[j]);
+                const float ea = expk(fmul(fsub(mrun, mn), scale), 0u, g_expk_t64, g_expk_lk);
+                const float eb = expk(fmul(fsub(mkk[j], mn), scale), 0u, g_expk_t64, g_expk_lk);
+                lrun = fadd(fmul(lrun, ea), fmul(lk[j], eb));
+                mrun = mn;
+                O = fadd(fmul(O, ea), fmul(ok[j], eb));
+            }
         }
     }
     const float rinv = frecip(maxt(lrun, ffrom(kLFloor)));
@@ -561,15 +635,26 @@ __global__ void fa_maskf_kernel(const uint16_t* m16, uint32_t stride, uint32_t T
     out[(size_t)t * n_kv + j] = h == 0xFC00u ? ffrom(kNegInf) : fdiv(h2f(h), scale);
 }
 
+// The kernel's attributes, set once per device: the largest shared-memory plan any call can need
+// and non-portable cluster sizes (C up to 16).
+template <int D>
+cudaError_t fa_attributes() {
+    static int done_dev[64];
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 64 && done_dev[dev] == dev + 1) return cudaSuccess;
+    e = cudaFuncSetAttribute(fa_chunk_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(227u * 1024u));
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(fa_chunk_kernel<D>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    if (e == cudaSuccess && dev < 64) done_dev[dev] = dev + 1;
+    return e;
+}
+
 template <int D>
 cudaError_t launch_chunks(const FaLaunch& a, uint32_t ncell_max, cudaStream_t st) {
     const FaSmem P = fa_smem(D, ncell_max);
-    cudaError_t e = cudaFuncSetAttribute(fa_chunk_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)P.total);
+    cudaError_t e = fa_attributes<D>();
     if (e != cudaSuccess) return e;
-    if (a.C > 8) {
-        e = cudaFuncSetAttribute(fa_chunk_kernel<D>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
-        if (e != cudaSuccess) return e;
-    }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(a.n_items * a.n_head_kv * a.C);
     cfg.blockDim = dim3(kFaThreads);

@@ -55,13 +55,15 @@ struct FaItem {
     uint32_t q0, Tq, u0, n, c_lo, c_hi, flags, general;
 };
 
+constexpr uint32_t kFaInlineItems = 32;   // plans up to this size travel in the kernel parameters
+
 struct FaLaunch {
     const float* q;             // [T][n_head][D] f32
     uint32_t T, n_head, n_head_kv, D, G, C, n_kv, n_cells;
     const int8_t* kq;           // K quants [n_head_kv][n_cells][D]
     const uint16_t* kd;         // K scales (fp16) [n_head_kv][n_cells][D/32]
-    const int8_t* vq;           // V, the same layout
-    const uint16_t* vd;
+    const int8_t* vq;           // V quants [n_head_kv][n_cells / 16][D][16] (value-major per group)
+    const uint16_t* vd;         // V scales, as K
     const float* maskf;         // f32 mask copy [T][maskf_stride] (GENERAL chunks only)
     uint32_t maskf_stride;
     float scale;
@@ -69,10 +71,14 @@ struct FaLaunch {
     uint32_t n_items;
     const uint32_t* tile_items; // [n_tiles + 1]: items of tile i are [tile_items[i], tile_items[i + 1])
     uint32_t n_tiles, Tq0;
-    float* oc;                  // channel partials [n_items][n_head_kv][C][Tq0 G][D]
-    float* lc;                  //                  [n_items][n_head_kv][C][Tq0 G]
-    float* mk;                  // chunk maxima     [n_items][n_head_kv][Tq0 G]
+    float* ok;                  // chunk results (channel tree done) [n_items][n_head_kv][Tq0 G][D]
+    float* lk;                  // chunk row sums                    [n_items][n_head_kv][Tq0 G]
+    float* mk;                  // chunk maxima                      [n_items][n_head_kv][Tq0 G]
     float* out;                 // [T][n_head][D] f32
+    // small plans: the items and tile offsets themselves (no host -> device copy, so a call can be
+    // captured in a CUDA graph); used when n_items <= kFaInlineItems
+    FaItem inl_items[kFaInlineItems];
+    uint32_t inl_tiles[kFaInlineItems + 1];
 };
 
 cudaError_t launch_fa(const FaLaunch& a, uint32_t n_max_groups, cudaStream_t st);
@@ -97,12 +103,13 @@ int fa_plan(const FaPlanIn& in, FaPlanOut* out, FaItem** items, uint32_t* n_item
 void fa_plan_free(FaItem* items, uint32_t* tile_items);
 
 // KV cache planes (tsrc_kv.cu): KVST of f32 rows (QACT A32), and ggml q8_0 rows <-> planes.
+// vt: the V plane (value-major inside each 16-cell group); K is cell-major.
 cudaError_t launch_kv_store(const float* rows, uint32_t n, uint32_t row_stride, const int64_t* cells, uint32_t cell0,
-                            uint32_t n_head_kv, uint32_t D, uint32_t n_cells, int8_t* q, uint16_t* d, cudaStream_t st);
+                            uint32_t n_head_kv, uint32_t D, uint32_t n_cells, bool vt, int8_t* q, uint16_t* d, cudaStream_t st);
 cudaError_t launch_kv_from_ggml(const uint8_t* ggml, uint32_t n, uint32_t cell0, uint32_t n_head_kv, uint32_t D,
-                                uint32_t n_cells, int8_t* q, uint16_t* d, cudaStream_t st);
+                                uint32_t n_cells, bool vt, int8_t* q, uint16_t* d, cudaStream_t st);
 cudaError_t launch_kv_to_ggml(const int8_t* q, const uint16_t* d, uint32_t n, uint32_t cell0, uint32_t n_head_kv, uint32_t D,
-                              uint32_t n_cells, uint8_t* ggml, cudaStream_t st);
+                              uint32_t n_cells, bool vt, uint8_t* ggml, cudaStream_t st);
 // The first error a KVST launch recorded on the current device (0 = none, 1 = a cell index
 // outside the cache).
 cudaError_t kv_error(uint32_t* code, bool clear);

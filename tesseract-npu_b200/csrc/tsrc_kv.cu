@@ -4,8 +4,12 @@
 // interleaved over channels; jwkim04/tesseract-npu sw/sim/tsr_ref_at.c:91-212) and converts
 // ggml's q8_0 cache rows into them in the backend's set_tensor. Here a plane is split per KV
 // head, head-major, so that a 16-cell group of one head is one contiguous run of bytes:
-//   quants  q[head][cell][D]      (int8, the ggml block's qs in order)
-//   scales  d[head][cell][D / 32] (the ggml block's fp16 d)
+//   K quants  q[head][cell][D]                  (cell-major: a cell's D values contiguous, the
+//                                                row operand of the QK products)
+//   V quants  q[head][group][D][16]             (value-major inside a 16-cell group: 16 cells of
+//                                                one value contiguous, the tensor-core A operand
+//                                                of the P.V products)
+//   scales    d[head][cell][D / 32]             (the ggml block's fp16 d, K and V alike)
 // The planes hold exactly the bytes of the ggml image (get / set round-trip them); the cell count
 // is padded to a multiple of 16 with zeros so that a group never runs past the allocation.
 //
@@ -19,9 +23,16 @@ namespace tsrc {
 
 namespace {
 
+// Byte offset of (cell, value k of head g) in a quant plane; vt: the V plane's value-major groups.
+__device__ __forceinline__ size_t qoff(bool vt, uint32_t g, uint32_t n_cells, uint32_t D, size_t cell, uint32_t k) {
+    const size_t hc = (size_t)g * n_cells + cell;
+    return vt ? (hc - (cell & 15u)) * D + (size_t)k * 16u + (cell & 15u) : hc * D + k;
+}
+
 // one warp per 32-value block of a row
 __global__ void kv_store_kernel(const float* rows, uint32_t n, uint32_t row_stride, const int64_t* cells, uint32_t cell0,
-                                uint32_t n_head_kv, uint32_t D, uint32_t n_cells, int8_t* q, uint16_t* d, unsigned int* err) {
+                                uint32_t n_head_kv, uint32_t D, uint32_t n_cells, bool vt, int8_t* q, uint16_t* d,
+                                unsigned int* err) {
     const uint32_t nb = n_head_kv * D / 32u;
     const size_t wi = ((size_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const uint32_t lane = threadIdx.x & 31u;
@@ -38,13 +49,13 @@ __global__ void kv_store_kernel(const float* rows, uint32_t n, uint32_t row_stri
     const float id = (fbits(db) & ~kSign) ? frecip(db) : 0.0f;
     const uint32_t g = 32u * b / D, k = 32u * b - g * D;
     const size_t hc = (size_t)g * n_cells + (size_t)cell;
-    q[hc * D + k + lane] = (int8_t)round_away_sat8(fmul(daz(v), id));
+    q[qoff(vt, g, n_cells, D, (size_t)cell, k + lane)] = (int8_t)round_away_sat8(fmul(daz(v), id));
     if (lane == 0) d[hc * (D / 32u) + k / 32u] = f2h(db);
 }
 
 // one thread per (cell, block): ggml block {fp16 d; int8 qs[32]} (34 bytes) <-> planes
 __global__ void kv_from_ggml_kernel(const uint8_t* ggml, uint32_t n, uint32_t cell0, uint32_t n_head_kv, uint32_t D,
-                                    uint32_t n_cells, int8_t* q, uint16_t* d) {
+                                    uint32_t n_cells, bool vt, int8_t* q, uint16_t* d) {
     const uint32_t nb = n_head_kv * D / 32u;
     const size_t t = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (t >= (size_t)n * nb) return;
@@ -53,6 +64,10 @@ __global__ void kv_from_ggml_kernel(const uint8_t* ggml, uint32_t n, uint32_t ce
     const uint32_t g = 32u * b / D, k = 32u * b - g * D;
     const size_t hc = (size_t)g * n_cells + cell0 + i;
     d[hc * (D / 32u) + k / 32u] = (uint16_t)(src[0] | (src[1] << 8));
+    if (vt) {
+        for (uint32_t j = 0; j < 32; ++j) q[qoff(true, g, n_cells, D, (size_t)cell0 + i, k + j)] = (int8_t)src[2 + j];
+        return;
+    }
     uint32_t w[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j)
@@ -64,7 +79,7 @@ __global__ void kv_from_ggml_kernel(const uint8_t* ggml, uint32_t n, uint32_t ce
 }
 
 __global__ void kv_to_ggml_kernel(const int8_t* q, const uint16_t* d, uint32_t n, uint32_t cell0, uint32_t n_head_kv, uint32_t D,
-                                  uint32_t n_cells, uint8_t* ggml) {
+                                  uint32_t n_cells, bool vt, uint8_t* ggml) {
     const uint32_t nb = n_head_kv * D / 32u;
     const size_t t = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (t >= (size_t)n * nb) return;
@@ -75,6 +90,10 @@ __global__ void kv_to_ggml_kernel(const int8_t* q, const uint16_t* d, uint32_t n
     const uint16_t h = d[hc * (D / 32u) + k / 32u];
     dst[0] = (uint8_t)(h & 0xFFu);
     dst[1] = (uint8_t)(h >> 8);
+    if (vt) {
+        for (uint32_t j = 0; j < 32; ++j) dst[2 + j] = (uint8_t)q[qoff(true, g, n_cells, D, (size_t)cell0 + i, k + j)];
+        return;
+    }
     const uint4* src = reinterpret_cast<const uint4*>(q + hc * D + k);
     const uint4 a = src[0], c = src[1];
     const uint32_t w[8] = {a.x, a.y, a.z, a.w, c.x, c.y, c.z, c.w};
@@ -89,14 +108,14 @@ __device__ unsigned int g_kv_error;
 }  // namespace
 
 cudaError_t launch_kv_store(const float* rows, uint32_t n, uint32_t row_stride, const int64_t* cells, uint32_t cell0,
-                            uint32_t n_head_kv, uint32_t D, uint32_t n_cells, int8_t* q, uint16_t* d, cudaStream_t st) {
+                            uint32_t n_head_kv, uint32_t D, uint32_t n_cells, bool vt, int8_t* q, uint16_t* d, cudaStream_t st) {
     const size_t threads = (size_t)n * (n_head_kv * D / 32u) * 32u;
     if (threads == 0) return cudaSuccess;
     unsigned int* err = nullptr;
     cudaError_t e = cudaGetSymbolAddress(reinterpret_cast<void**>(&err), g_kv_error);
     if (e != cudaSuccess) return e;
     kv_store_kernel<<<(unsigned)((threads + 255u) / 256u), 256, 0, st>>>(rows, n, row_stride, cells, cell0, n_head_kv, D, n_cells,
-                                                                         q, d, err);
+                                                                         vt, q, d, err);
     return cudaGetLastError();
 }
 
@@ -112,18 +131,18 @@ cudaError_t kv_error(uint32_t* code, bool clear) {
 }
 
 cudaError_t launch_kv_from_ggml(const uint8_t* ggml, uint32_t n, uint32_t cell0, uint32_t n_head_kv, uint32_t D,
-                                uint32_t n_cells, int8_t* q, uint16_t* d, cudaStream_t st) {
+                                uint32_t n_cells, bool vt, int8_t* q, uint16_t* d, cudaStream_t st) {
     const size_t t = (size_t)n * (n_head_kv * D / 32u);
     if (t == 0) return cudaSuccess;
-    kv_from_ggml_kernel<<<(unsigned)((t + 255u) / 256u), 256, 0, st>>>(ggml, n, cell0, n_head_kv, D, n_cells, q, d);
+    kv_from_ggml_kernel<<<(unsigned)((t + 255u) / 256u), 256, 0, st>>>(ggml, n, cell0, n_head_kv, D, n_cells, vt, q, d);
     return cudaGetLastError();
 }
 
 cudaError_t launch_kv_to_ggml(const int8_t* q, const uint16_t* d, uint32_t n, uint32_t cell0, uint32_t n_head_kv, uint32_t D,
-                              uint32_t n_cells, uint8_t* ggml, cudaStream_t st) {
+                              uint32_t n_cells, bool vt, uint8_t* ggml, cudaStream_t st) {
     const size_t t = (size_t)n * (n_head_kv * D / 32u);
     if (t == 0) return cudaSuccess;
-    kv_to_ggml_kernel<<<(unsigned)((t + 255u) / 256u), 256, 0, st>>>(q, d, n, cell0, n_head_kv, D, n_cells, ggml);
+    kv_to_ggml_kernel<<<(unsigned)((t + 255u) / 256u), 256, 0, st>>>(q, d, n, cell0, n_head_kv, D, n_cells, vt, ggml);
     return cudaGetLastError();
 }
 
