@@ -35,8 +35,110 @@ CONFIGS = {
     # name: (fmt, N, K, weight seed, x seed, description)
     "cfg2": (1, 14336, 4096, 201, 202, "BASELINE config 2: Q4_K matvec 14336x4096, one token (decode)"),
     "cfg1": (0, 4864, 896, 101, 102, "BASELINE config 1: Q8_0 matvec 4864x896, one token (decode)"),
+    "cfg3": (None, None, None, 301, 303, "BASELINE config 3: flash-attention decode over a q8_0 KV cache, "
+             "32 q / 8 kv heads, head_dim 128, 8192 cells, one token"),
 }
 METRIC = "Q8_0/Q4_K matvec HBM GB/s"
+FA = dict(D=128, n_head_kv=8, G=4, n_kv=8192)
+
+
+def fa_algo_bytes(n_head_kv, D, G, n_kv):
+    """K and V q8_0 bytes of the visible cells + f32 q in + f32 out (per call)."""
+    E = n_head_kv * D
+    return 2 * n_kv * (E // 32) * 34 + 2 * 4 * n_head_kv * G * D
+
+
+def fa_measure(dev, tsrc, torch, steps, warmup, world=1, rank=0, dist=None):
+    """FA decode (config 3) on this rank's KV heads (8 / world of them): a ring of caches larger
+    than 4x L2, each step one tsrc_flash_attn (plus the all-gather of out on N > 1 GPUs).
+    Returns (device ms for `steps` steps, e2e ms for min(steps, 2000) steps, info)."""
+    import numpy as np
+    D, H, G, n_kv = FA["D"], FA["n_head_kv"], FA["G"], FA["n_kv"]
+    h_loc = H // world
+    E = h_loc * D
+    local = torch.cuda.current_device()
+    l2 = torch.cuda.get_device_properties(local).L2_cache_size
+    cache_bytes = 2 * n_kv * (E // 32) * 34
+    n_ring = max(2, math.ceil(4 * l2 / cache_bytes))
+    gen = torch.Generator(device="cuda").manual_seed(301 + rank)
+    kvs = []
+    for _ in range(n_ring):
+        kv = dev.kv_create(h_loc, D, n_kv)
+        for which in (0, 1):
+            kv.set_rows(which, torch.randn((n_kv, E), device="cuda", generator=gen))
+        kvs.append(kv)
+    torch.cuda.synchronize()
+    q = torch.randn((1, h_loc * G, D), device="cuda", generator=torch.Generator(device="cuda").manual_seed(303 + rank))
+    out = torch.empty_like(q)
+    out_all = torch.empty((world, h_loc * G, D), device="cuda")
+    scale = float(np.float32(1.0 / np.sqrt(D)))
+
+    def step(i):
+        dev.flash_attn(kvs[i % n_ring], q, out, T=1, n_head=h_loc * G, n_kv=n_kv, scale=scale, new=(n_kv - 1, n_kv))
+        if world > 1:
+            dist.all_gather_into_tensor(out_all, out)
+
+    for i in range(warmup):
+        step(i)
+    torch.cuda.synchronize()
+    graph = None
+    if world == 1:
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for i in range(n_ring):
+                step(i)
+        graph.replay()
+        torch.cuda.synchronize()
+
+    def loop(n):
+        if graph is not None:
+            reps, rem = divmod(n, n_ring)
+            for _ in range(reps):
+                graph.replay()
+            for i in range(rem):
+                step(i)
+        else:
+            for i in range(n):
+                step(i)
+
+    q_host = q.cpu().pin_memory()
+    o_host = torch.empty((world, h_loc * G, D)).pin_memory()
+    n_e2e = min(steps, 2000)
+
+    def e2e(n):
+        for i in range(n):
+            q.copy_(q_host, non_blocking=True)
+            step(i)
+            o_host.copy_(out_all if world > 1 else out.view(1, h_loc * G, D), non_blocking=True)
+
+    def timed(fn, n):
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        fn(n)
+        e1.record()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1)
+        if world > 1:
+            t = torch.tensor([ms], dtype=torch.float64, device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        return ms
+
+    ms = timed(loop, steps)
+    ms_e2e = timed(e2e, n_e2e)
+    used_graph = graph is not None
+    del graph
+    for kv in kvs:
+        kv.free()
+    info = {"ring": n_ring, "ring_mb_per_gpu": round(n_ring * cache_bytes / 1e6, 1), "heads_kv_per_gpu": h_loc,
+            "h2d_bytes_per_step": 4 * h_loc * G * D, "d2h_bytes_per_step": 4 * world * h_loc * G * D, "e2e_steps": n_e2e,
+            "cuda_graph": used_graph}
+    return ms, ms_e2e, info
 
 
 def row_bytes(fmt, K):
@@ -146,11 +248,132 @@ def cpu_reference_matvec(fmt, N, K, x, seconds, threads):
     return gbs, kind, f"{n} full {N}x{K} matvecs in {el:.1f} s ({threads} threads)", el / n
 
 
+def cpu_reference_fa(seconds, threads, calls=None):
+    """The reference's tsr_ref_fa (oracle/_ref) -- else the restatement -- on config 3, one full call
+    per worker thread at a time, for about `seconds` (or exactly `calls` calls per thread).
+    Returns (GB/s of algorithmic bytes, kind, sample text, seconds per call)."""
+    import threading
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    import oracle
+    import helpers as H
+    tsro = oracle.Tsro()
+    q, k, v, kw = H.fa_inputs(tsro, H.FA_CONFIGS["cfg3"])
+    kw = dict(kw, new=(kw["n_kv"] - 1, kw["n_kv"]))
+    kind = "reference" if oracle.Ref.available() else "port"
+    if kind == "reference":
+        ref = oracle.Ref()
+        hs = [ref.fa_prepare(k, v, T=1, **kw) for _ in range(threads)]
+        run = lambda i: ref.fa_run(hs[i], q)  # noqa: E731
+    else:
+        run = lambda i: tsro.fa(q, k, v, **kw)  # noqa: E731
+    t0 = time.perf_counter()
+    run(0)
+    per = time.perf_counter() - t0
+    n_each = calls if calls is not None else max(1, int(seconds / per / 1.0))
+    done = [0] * threads
+
+    def worker(i):
+        for _ in range(n_each):
+            run(i)
+            done[i] += 1
+
+    t0 = time.perf_counter()
+    ths = [threading.Thread(target=worker, args=(i,)) for i in range(threads)]
+    for t in ths:
+        t.start()
+    for t in ths:
+        t.join()
+    el = time.perf_counter() - t0
+    if kind == "reference":
+        for h in hs:
+            ref.fa_free(h)
+    n = sum(done)
+    gbs = n * fa_algo_bytes(FA["n_head_kv"], FA["D"], FA["G"], FA["n_kv"]) / el / 1e9
+    return gbs, kind, f"{n} full config-3 FA calls in {el:.1f} s ({threads} threads, one call per thread at a time)", el / max(1, n_each)
+
+
+def run_fa(args):
+    """--config cfg3: FA decode over the q8_0 KV cache; KV heads sharded over the ranks."""
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    import tsrc
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+    if FA["n_head_kv"] % world:
+        raise SystemExit(f"cfg3 shards 8 KV heads: --gpus must divide 8, not {world}")
+    dev = tsrc.Device(local)
+    steps = args.steps if args.steps != 50000 else 5000
+    with Clocks(local) as clk:
+        ms, ms_e2e, info = fa_measure(dev, tsrc, torch, steps, args.warmup, world, rank, dist)
+    total = fa_algo_bytes(FA["n_head_kv"], FA["D"], FA["G"], FA["n_kv"])
+    shard = fa_algo_bytes(FA["n_head_kv"] // world, FA["D"], FA["G"], FA["n_kv"])
+    us = ms * 1e3 / steps
+    peak, peak_kind = peaks()
+    cpu = None
+    if rank == 0 and world == 1 and args.cpu_seconds > 0:
+        threads = len(os.sched_getaffinity(0))
+        gbs, kind, sample, _ = cpu_reference_fa(args.cpu_seconds, threads)
+        cpu = {"value": round(gbs, 4), "unit": "GB/s", "cores": threads, "kind": kind, "sample": sample}
+    traffic = None
+    prof = os.path.join(ROOT, "profiles", "traffic_cfg3.json")
+    if os.path.exists(prof):
+        with open(prof) as f:
+            t = json.load(f).get("dram_bytes_per_launch")
+        traffic = None if t is None else int(t // world)        # measured on one GPU (8 KV heads)
+    line = {
+        "metric": "FA decode HBM GB/s (q8_0 KV cache)", "value": round(steps * total / (ms * 1e-3) / 1e9, 2), "unit": "GB/s",
+        "n_gpus": world, "steps": steps, "warmup": args.warmup, "ms_per_step": round(ms / steps, 6),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int8",
+        "data": "synthetic (seeded N(0,1) K, V through KVST, N(0,1) q)",
+        "config": {"workload": CONFIGS["cfg3"][5], "parallelism": f"kv-head split x{world}" if world > 1 else "single",
+                   "l2": f"inputs larger than L2: ring of {info['ring']} caches, {info['ring_mb_per_gpu']} MB per GPU",
+                   "cuda_graph": world == 1, "collective": "NCCL all_gather of out" if world > 1 else None},
+        "roofline": {"bound": "hbm", "achieved": round(shard / (us * 1e-6) / 1e9, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(shard / (us * 1e-6) / 1e9 / peak, 4), "traffic": traffic, "peak_kind": peak_kind,
+                     "kernel": "fa_chunk_kernel<128> + fa_merge_kernel (one step)", "us_per_launch": round(us, 3),
+                     "algorithmic_bytes_per_launch": shard},
+        "e2e": {"value": round(info["e2e_steps"] * total / (ms_e2e * 1e-3) / 1e9, 2), "unit": "GB/s",
+                "h2d_bytes_per_step": info["h2d_bytes_per_step"], "d2h_bytes_per_step": info["d2h_bytes_per_step"],
+                "ms_per_step": round(ms_e2e / info["e2e_steps"], 6)},
+        "gpu_launches": 2 * steps,
+        "clocks": clk.summary(),
+        "cpu_baseline": cpu,
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    dev.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
 def run_reference(args, cfg):
     """--impl reference: the reference's own CPU implementation of the path, rank 0 only."""
     import numpy as np
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
+        return 0
+    if args.config == "cfg3":
+        threads = len(os.sched_getaffinity(0))
+        n_each = max(1, min(args.steps, 3))
+        gbs, kind, sample, per = cpu_reference_fa(0, threads, calls=n_each)
+        line = {
+            "impl": "reference", "metric": "FA decode HBM GB/s (q8_0 KV cache)", "value": round(gbs, 4), "unit": "GB/s",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": 0, "ms_per_step": round(per * 1e3, 3),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int8",
+            "data": "synthetic (seeded N(0,1) K, V, q)", "config": {"workload": CONFIGS["cfg3"][5], "host_threads": threads},
+            "cpu_baseline": {"value": round(gbs, 4), "unit": "GB/s", "cores": threads, "kind": kind, "sample": sample},
+            "e2e": {"value": round(gbs, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        }
+        print(json.dumps(line), flush=True)
         return 0
     fmt, N, K, ws, xs, desc = cfg
     threads = len(os.sched_getaffinity(0))
@@ -205,11 +428,14 @@ def main():
     ap.add_argument("--config", default="cfg2", choices=list(CONFIGS))
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-graph", action="store_true")
+    ap.add_argument("--no-fa", action="store_true", help="skip the config-3 FA summary in the default line")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     cfg = CONFIGS[args.config]
     if args.impl == "reference":
         return run_reference(args, cfg)
+    if args.config == "cfg3":
+        return run_fa(args)
 
     import numpy as np
     import torch
@@ -341,6 +567,18 @@ def main():
         gbs, kind, sample, _ = cpu_reference_matvec(fmt, N, K, xn, args.cpu_seconds, threads)
         cpu = {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": kind, "sample": sample}
 
+    also = {}
+    if world == 1 and not args.no_fa:
+        ms_fa, ms_fa_e2e, info = fa_measure(dev, tsrc, torch, 2000, 20)
+        fa_b = fa_algo_bytes(FA["n_head_kv"], FA["D"], FA["G"], FA["n_kv"])
+        fa_us = ms_fa * 1e3 / 2000
+        also["fa_cfg3"] = {"metric": "FA decode HBM GB/s (q8_0 KV cache)", "workload": CONFIGS["cfg3"][5],
+                           "value": round(fa_b / (fa_us * 1e-6) / 1e9, 1), "unit": "GB/s", "us_per_step": round(fa_us, 3),
+                           "frac": round(fa_b / (fa_us * 1e-6) / 1e9 / peak, 4),
+                           "e2e_us_per_step": round(ms_fa_e2e * 1e3 / info["e2e_steps"], 3),
+                           "l2": f"ring of {info['ring']} caches ({info['ring_mb_per_gpu']} MB)", "cuda_graph": True,
+                           "full_line": "python bench.py --config cfg3"}
+
     traffic = None
     prof = os.path.join(ROOT, "profiles", f"traffic_{args.config}.json")
     if os.path.exists(prof):
@@ -366,6 +604,8 @@ def main():
         "clocks": clocks,
         "cpu_baseline": cpu,
     }
+    if also:
+        line["also"] = also
     if rank == 0:
         print(json.dumps(line), flush=True)
     del graph, kgraph
