@@ -73,8 +73,11 @@ def fa_measure(dev, tsrc, torch, steps, warmup, world=1, rank=0, dist=None):
     out_all = torch.empty((world, h_loc * G, D), device="cuda")
     scale = float(np.float32(1.0 / np.sqrt(D)))
 
+    cfg = (4, 4, 9344, 32768, H)          # release configuration; shards plan with the model's 8 KV heads
+
     def step(i):
-        dev.flash_attn(kvs[i % n_ring], q, out, T=1, n_head=h_loc * G, n_kv=n_kv, scale=scale, new=(n_kv - 1, n_kv))
+        dev.flash_attn(kvs[i % n_ring], q, out, T=1, n_head=h_loc * G, n_kv=n_kv, scale=scale, new=(n_kv - 1, n_kv),
+                       cfg=cfg)
         if world > 1:
             dist.all_gather_into_tensor(out_all, out)
 
@@ -454,8 +457,9 @@ def main():
     stream = torch.cuda.current_stream()
 
     # row shard of this rank (symmetric split R = ceil(N / world), sw/sim/tsr_ref.c:335-357)
+    from tsrc import parallel
     R = (N + world - 1) // world
-    row0, n_rows = rank * R, max(0, min(R, N - rank * R))
+    row0, n_rows = parallel.row_shard(N, world, rank)
     shard_bytes = n_rows * row_bytes(fmt, K)
     l2 = torch.cuda.get_device_properties(local).L2_cache_size
     n_copies = max(2, math.ceil(4 * l2 / max(1, shard_bytes)))

@@ -651,13 +651,17 @@ int tsrc_flash_attn(tsrc_ctx* ctx, const tsrc_kv* kv, const float* q, uint32_t T
     std::memcpy(&sb, &scale, 4);
     if ((sb & 0x80000000u) || (sb & 0x7F800000u) == 0 || (sb & 0x7F800000u) == 0x7F800000u)
         return fail(TSRC_E_SHAPE, "FLASH_ATTN: scale must be finite, normal and > 0");
-    const tsrc_fa_cfg def{4, 4, 9344, 32768};
+    const tsrc_fa_cfg def{4, 4, 9344, 32768, 0};
     const tsrc_fa_cfg& c = cfg ? *cfg : def;
     tsrc::FaPlanIn in{};
     in.C = c.C;
     in.t_max = c.t_max;
     in.pcap = c.pcap;
     in.k_max = c.k_max;
+    if (c.plan_n_head_kv && (c.plan_n_head_kv < kv->n_head_kv || c.plan_n_head_kv % kv->n_head_kv))
+        return fail(TSRC_E_ARG, "tsrc_flash_attn: plan_n_head_kv %u is not a multiple of the cache's %u KV heads",
+                    c.plan_n_head_kv, kv->n_head_kv);
+    in.plan_n_head_kv = c.plan_n_head_kv ? c.plan_n_head_kv : kv->n_head_kv;
     in.T = T;
     in.D = kv->D;
     in.n_head = n_head;

@@ -297,7 +297,9 @@ int fa_plan(const FaPlanIn& in, FaPlanOut* po, FaItem** items, uint32_t* n_items
         *why = "FLASH_ATTN: head_dim must be 64/128/256/512 and n_head a multiple of n_head_kv";
         return TSRC_E_SHAPE;
     }
-    const uint32_t G = in.n_head / in.n_head_kv, E = in.n_head_kv * in.D;
+    // E of the whole model (a shard of the KV heads plans as the single device does)
+    const uint32_t plan_h = in.plan_n_head_kv ? in.plan_n_head_kv : in.n_head_kv;
+    const uint32_t G = in.n_head / in.n_head_kv, E = plan_h * in.D;
     if (G == 0 || G > 64 || E / 64u > 511u) {
         *why = "FLASH_ATTN: G must be 1..64 and E / 64 at most 511";
         return TSRC_E_SHAPE;
@@ -307,7 +309,7 @@ int fa_plan(const FaPlanIn& in, FaPlanOut* po, FaItem** items, uint32_t* n_items
         return TSRC_E_SHAPE;
     }
     const uint32_t GS0 = std::min(G, in.t_max), Tq0 = in.t_max / GS0;
-    if (in.n_head_kv * GS0 * Tq0 > 128u || Tq0 * in.n_head > 1024u) {
+    if (plan_h * GS0 * Tq0 > 128u || Tq0 * G * plan_h > 1024u) {
         *why = "FLASH_ATTN: a tile has more than 128 head rows or 1024 query rows";
         return TSRC_E_SHAPE;
     }

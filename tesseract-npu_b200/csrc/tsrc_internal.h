@@ -90,6 +90,7 @@ cudaError_t launch_fa_maskf(const uint16_t* m16, uint32_t stride, uint32_t T, ui
 struct FaPlanIn {
     uint32_t C, t_max, pcap, k_max;
     uint32_t T, D, n_head, n_head_kv, n_kv;
+    uint32_t plan_n_head_kv;    // KV heads of the whole model (E of the plan and the shape checks)
     const uint16_t* mask;       // host f16 mask [T][mask_stride], or NULL (every cell < n_kv visible)
     size_t mask_stride;
     uint32_t new_lo, new_hi;    // cells written by this launch: their chunks run last

@@ -67,8 +67,9 @@ _SIGS = {
 
 
 class FaCfg(ct.Structure):
-    """tsrc_fa_cfg: the attention configuration (channels C, T_MAX, PCAP, K_MAX)."""
-    _fields_ = [("C", _u32), ("t_max", _u32), ("pcap", _u32), ("k_max", _u32)]
+    """tsrc_fa_cfg: the attention configuration (channels C, T_MAX, PCAP, K_MAX) and the model's KV
+    heads when a cache holds a shard of them (0: the cache's own)."""
+    _fields_ = [("C", _u32), ("t_max", _u32), ("pcap", _u32), ("k_max", _u32), ("plan_n_head_kv", _u32)]
 
 
 KV_K, KV_V = 0, 1
@@ -242,13 +243,13 @@ class Device:
                    new=(0, 0), cfg=None, stream=None) -> None:
         """out[t][h] = the reference's composite FA of q[t][h] over cells [0, n_kv) of kv.
         q / out: device f32 [T][n_head][head_dim]; mask: host numpy f16 [T][stride] or None;
-        cfg: (C, t_max, pcap, k_max) or None for the release values."""
+        cfg: (C, t_max, pcap, k_max[, plan_n_head_kv]) or None for the release values."""
         import numpy as np
         mptr, mstride, keep = None, 0, None
         if mask is not None:
             keep = np.ascontiguousarray(mask, dtype=np.float16)
             mptr, mstride = keep.ctypes.data, keep.shape[-1]
-        c = None if cfg is None else FaCfg(*cfg)
+        c = None if cfg is None else FaCfg(*(tuple(cfg) + (0,) * (5 - len(cfg))))
         _check(lib().tsrc_flash_attn(self.handle, kv.handle, _addr(q), T, n_head, n_kv, mptr, mstride, scale,
                                      new[0], new[1], None if c is None else ct.byref(c), _addr(out),
                                      _stream(stream)))

@@ -166,3 +166,38 @@ def test_fa_rejects(dev):
             dev.kv_create(2, 96, 10)                # head_dim 96
     finally:
         kv.free()
+
+
+def test_fa_kv_head_shards_plan_as_one_device(dev, tsro):
+    """Tensor parallelism by KV heads, emulated with one cache per shard on one GPU: with the
+    model's KV heads as plan_n_head_kv every shard chunks as the single device does (PCAP binds
+    the chunk size here, and it depends on E), so the concatenated heads are the single-device
+    output bit for bit; planning with the shard's own E would not be."""
+    import torch
+    from tsrc import parallel as P
+    D, nkvh, G = 128, 8, 4
+    case = (D, nkvh, G, 1, 3000, 2999, "causal", 4, 4, 2048, 0.0883883, 1.0, 2999, 3000, 81)
+    q, k, v, kw = H.fa_inputs(tsro, case)
+    rc, want = tsro.fa(q, k, v, **kw)
+    assert rc == 0
+    rb = D // 32 * 34
+    for world in (2, 4):
+        outs, outs_own = [], []
+        for r in range(world):
+            h0, hn = P.kv_head_shard(nkvh, world, r)
+            kv = dev.kv_create(hn, D, kw["n_kv"])
+            try:
+                kv.set_bytes(tsrc.KV_K, np.ascontiguousarray(k[:, h0 * rb:(h0 + hn) * rb]))
+                kv.set_bytes(tsrc.KV_V, np.ascontiguousarray(v[:, h0 * rb:(h0 + hn) * rb]))
+                qd = torch.from_numpy(np.ascontiguousarray(q[:, h0 * G:(h0 + hn) * G])).cuda()
+                for plan, dst in ((nkvh, outs), (0, outs_own)):
+                    out = torch.full_like(qd, float("nan"))
+                    dev.flash_attn(kv, qd, out, T=1, n_head=hn * G, n_kv=kw["n_kv"], scale=kw["scale"], mask=kw["mask"],
+                                   new=kw["new"], cfg=(kw["C"], kw["t_max"], kw["pcap"], 32768, plan))
+                    dev.sync()
+                    dst.append(out.cpu().numpy())
+            finally:
+                kv.free()
+        got = np.concatenate(outs, axis=1)
+        np.testing.assert_array_equal(got.view(np.uint32), want.view(np.uint32))
+        assert not np.array_equal(np.concatenate(outs_own, axis=1).view(np.uint32), want.view(np.uint32))
