@@ -42,6 +42,23 @@ METRIC = "Q8_0/Q4_K matvec HBM GB/s"
 FA = dict(D=128, n_head_kv=8, G=4, n_kv=8192)
 
 
+def capture(torch, body, sync):
+    """A CUDA graph of body() (NCCL collectives included), replayed once; None if capture fails
+    (the loops then run eagerly)."""
+    try:
+        sync()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            body()
+        g.replay()
+        sync()
+        return g
+    except Exception as e:  # noqa: BLE001
+        print(f"bench: CUDA graph capture failed ({e}); timing eager launches", file=sys.stderr)
+        sync()
+        return None
+
+
 def fa_algo_bytes(n_head_kv, D, G, n_kv):
     """K and V q8_0 bytes of the visible cells + f32 q in + f32 out (per call)."""
     E = n_head_kv * D
@@ -84,14 +101,12 @@ def fa_measure(dev, tsrc, torch, steps, warmup, world=1, rank=0, dist=None):
     for i in range(warmup):
         step(i)
     torch.cuda.synchronize()
-    graph = None
-    if world == 1:
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph):
-            for i in range(n_ring):
-                step(i)
-        graph.replay()
+    def sync_all():
+        if world > 1:
+            dist.barrier()
         torch.cuda.synchronize()
+
+    graph = capture(torch, lambda: [step(i) for i in range(n_ring)], sync_all)
 
     def loop(n):
         if graph is not None:
@@ -337,7 +352,7 @@ def run_fa(args):
         "data": "synthetic (seeded N(0,1) K, V through KVST, N(0,1) q)",
         "config": {"workload": CONFIGS["cfg3"][5], "parallelism": f"kv-head split x{world}" if world > 1 else "single",
                    "l2": f"inputs larger than L2: ring of {info['ring']} caches, {info['ring_mb_per_gpu']} MB per GPU",
-                   "cuda_graph": world == 1, "collective": "NCCL all_gather of out" if world > 1 else None},
+                   "cuda_graph": info["cuda_graph"], "collective": "NCCL all_gather of out" if world > 1 else None},
         "roofline": {"bound": "hbm", "achieved": round(shard / (us * 1e-6) / 1e9, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(shard / (us * 1e-6) / 1e9 / peak, 4), "traffic": traffic, "peak_kind": peak_kind,
                      "kernel": "fa_chunk_kernel<128> + fa_merge_kernel (one step)", "us_per_launch": round(us, 3),
@@ -432,6 +447,8 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-graph", action="store_true")
     ap.add_argument("--no-fa", action="store_true", help="skip the config-3 FA summary in the default line")
+    ap.add_argument("--collective", default="p2p", choices=["p2p", "nccl"],
+                    help="N > 1 matvec: all-gather fused into the kernel (P2P stores) or an NCCL all_gather")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     cfg = CONFIGS[args.config]
@@ -469,8 +486,18 @@ def main():
     x = torch.from_numpy(np.random.default_rng(xs).standard_normal(K, dtype=np.float32)).cuda()
     y_loc = torch.zeros(n_rows, device="cuda")
     y_full = torch.zeros(R * world, device="cuda")
+    team = None
+    if world > 1 and args.collective == "p2p":
+        # MUL_MAT with the all-gather fused in: rows stored into every rank's buffer over NVLink
+        team = dev.team_create(rank, world, N)
+        hs = [None] * world
+        dist.all_gather_object(hs, team.ipc_handle)
+        team.connect(b"".join(hs))
 
     def step(i):
+        if team is not None:
+            dev.mul_mat_allgather(team, weights[i % n_copies], x, y_full)
+            return
         dev.mul_mat(weights[i % n_copies], x, y_loc, T=1)
         if world > 1:
             dist.all_gather_into_tensor(y_full, torch.nn.functional.pad(y_loc, (0, R - n_rows)))
@@ -500,16 +527,12 @@ def main():
         step(i)
     torch.cuda.synchronize()
 
-    use_graph = world == 1 and not args.no_graph
+    # one CUDA graph of the ring of steps (on N > 1 GPUs the NCCL all-gathers are captured too)
+    use_graph = not args.no_graph
     graph = None
     if use_graph:
-        g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g):
-            for i in range(n_copies):
-                step(i)
-        graph = g
-        graph.replay()
-        torch.cuda.synchronize()
+        graph = capture(torch, lambda: [step(i) for i in range(n_copies)], barrier)
+        use_graph = graph is not None
 
     def value_loop(n):
         if graph is not None:
@@ -596,7 +619,9 @@ def main():
         "data": "synthetic (seeded N(0,0.02) weights quantized on device, N(0,1) activation)",
         "config": {"workload": desc, "rows_per_gpu": n_rows, "parallelism": f"row-split tp{world}" if world > 1 else "single",
                    "l2": f"inputs larger than L2: ring of {n_copies} weight copies, {n_copies * shard_bytes / 1e6:.0f} MB per GPU",
-                   "cuda_graph": use_graph, "collective": "NCCL all_gather of y" if world > 1 else None},
+                   "cuda_graph": use_graph,
+                   "collective": None if world == 1 else ("all-gather fused in the matvec kernel (P2P stores over NVLink)"
+                                                           if team is not None else "NCCL all_gather of y")},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "traffic": traffic, "peak_kind": peak_kind,
                      "kernel": f"matvec_kernel<{fmt},1> (QACT fused)", "us_per_launch": round(kern_us, 3),
@@ -613,6 +638,10 @@ def main():
     if rank == 0:
         print(json.dumps(line), flush=True)
     del graph, kgraph
+    if world > 1:
+        dist.barrier()
+    if team is not None:
+        team.free()
     for w in weights:
         w.free()
     dev.close()

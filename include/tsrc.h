@@ -54,6 +54,7 @@ extern "C" {
 
 typedef struct tsrc_ctx tsrc_ctx;
 typedef struct tsrc_weight tsrc_weight;
+typedef struct tsrc_team tsrc_team;
 
 // Last error message of the calling thread ("" if none). Replaces the reference's GGML_ABORT text
 // (ggml-tesseract.cpp:2260-2271) as a returned status.
@@ -150,6 +151,32 @@ TSRC_API int tsrc_qact(tsrc_ctx * ctx, uint32_t kind, const float * x, uint32_t 
 // check them bit for bit. Device pointers, queued on `stream`.
 TSRC_API int tsrc_mul_mat_isums(tsrc_ctx * ctx, const tsrc_weight * w, const float * x, float * y, int32_t * isum,
                        void * stream);
+// Connects a team with other teams of the same process and GPU (members[r] = rank r's team, this
+// one included) instead of IPC handles: for tests of the team's flag protocol on one GPU (only
+// one rank's launches may run there: ranks wait for each other, and two of them on one GPU are
+// not guaranteed to run at the same time).
+TSRC_API int tsrc_team_connect_local(tsrc_team * team, const tsrc_team * const * members);
+
+// ---- tensor parallelism: MUL_MAT with the all-gather fused in (no counterpart in the reference,
+// whose channels live on one card) ------------------------------------------------------------------
+// A team is one rank's side of a group of `world` GPUs of one box (one process per GPU). Each rank
+// creates its buffer (writing a TSRC_TEAM_HANDLE_BYTES CUDA IPC handle), the ranks exchange the
+// handles (e.g. an all-gather over torch.distributed), and each rank connects with all of them
+// (world x TSRC_TEAM_HANDLE_BYTES bytes in rank order).
+#define TSRC_TEAM_HANDLE_BYTES 64
+TSRC_API int tsrc_team_create(tsrc_ctx * ctx, uint32_t rank, uint32_t world, uint32_t n_max, void * handle_out,
+                              tsrc_team ** out);
+TSRC_API int tsrc_team_connect(tsrc_team * team, const void * handles);
+TSRC_API int tsrc_team_free(tsrc_team * team);
+// MUL_MAT of one token over this rank's row shard of an N-row weight (N <= n_max) whose rows go
+// to every rank: y (device, N floats) receives the whole vector on every rank, bit for bit the
+// single-GPU result. The shard's rows are stored into every rank's buffer by the matvec kernel
+// itself (P2P stores over NVLink); its last CTA exchanges step flags with the peers (a bounded
+// wait: a rank that does not take part makes tsrc_sync return TSRC_E_DEVICE) and copies the vector
+// out. Every rank must make the same sequence of calls; queued on `stream`, no host sync. (The
+// reference's row split: sw/sim/tsr_ref.c:335-357; its host then had all rows in one memory.)
+TSRC_API int tsrc_mul_mat_allgather(tsrc_ctx * ctx, tsrc_team * team, const tsrc_weight * w, const float * x, float * y,
+                                    void * stream);
 
 // ---- q8_0 KV cache (one layer) -------------------------------------------------------------------
 // A cache holds n_cells cells of E = n_head_kv * head_dim values for K and for V, each value stored

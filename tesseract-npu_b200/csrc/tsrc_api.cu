@@ -193,6 +193,13 @@ namespace tsrc {
 
 int set_error(int code, const char* msg) { return fail(code, "%s", msg); }
 
+int weight_rows(const tsrc_weight* w, uint32_t* N, uint32_t* row0, uint32_t* n_rows) {
+    *N = w->N;
+    *row0 = w->row0;
+    *n_rows = w->n_rows;
+    return TSRC_OK;
+}
+
 // The argument checks of a MUL_MAT call (the same rules as tsrc_mul_mat) and the per-call launch
 // fields; for entry points that run the kernels with their own activation scratch.
 int mm_check(tsrc_ctx* ctx, const tsrc_weight* w, const float* x, uint32_t T, uint32_t* x_stride, float* y, uint32_t* y_stride,
@@ -284,7 +291,8 @@ int tsrc_sync(tsrc_ctx* ctx, void* stream) {
     uint32_t code = 0;
     e = tsrc::matvec_error(&code, true);
     if (e != cudaSuccess) return cuda_fail(e, "reading the kernel error flag");
-    if (code) return fail(TSRC_E_DEVICE, "a matvec kernel gave up a bounded wait (code %u)", code);
+    if (code) return fail(TSRC_E_DEVICE, "a matvec kernel gave up a bounded wait (code %u%s)", code,
+                          code == 2 ? ": a team peer did not signal its step" : "");
     e = tsrc::kv_error(&code, true);
     if (e != cudaSuccess) return cuda_fail(e, "reading the KV error flag");
     if (code) return fail(TSRC_E_ARG, "tsrc_kv_set_rows: a cell index outside the cache (those rows were not stored)");

@@ -450,7 +450,7 @@ __device__ __forceinline__ void compute_unit(const Q4Unit& u, const Qa& s, uint3
 // unit's loads issued one unit ahead. Two unit buffers alternate roles (no register copies).
 template <int FMT, int MAXT, bool SAFE>
 __device__ __forceinline__ void stream_rows(const MvArgs& a, const Qa& qa, uint32_t r_begin, uint32_t r_end, uint32_t warp,
-                                            uint32_t lane) {
+                                            uint32_t lane, float* team_rows) {
     using Unit = typename std::conditional<FMT == 0, Q8Unit, Q4Unit>::type;
     const Layout L{(uint32_t)FMT, a.K};
     constexpr uint32_t TPU = FMT == 0 ? kQ8Tiles : 1u;      // tiles per unit
@@ -486,7 +486,14 @@ __device__ __forceinline__ void stream_rows(const MvArgs& a, const Qa& qa, uint3
             for (int t = 0; t < MAXT; ++t) {
                 if (t < (int)a.T) {
                     const float v = tree16_lanes(p[t]);
-                    if (k == 0 && rv) a.y[(size_t)t * a.y_stride + row] = mm_epilogue(v, a, (uint32_t)t, row);
+                    if (k == 0 && rv) {
+                        const float yv = mm_epilogue(v, a, (uint32_t)t, row);
+                        if (a.team_world) {                 // collected per CTA, sent in team_finish
+                            team_rows[row - r_begin] = yv;
+                        } else {
+                            a.y[(size_t)t * a.y_stride + row] = yv;
+                        }
+                    }
                 }
                 p[t] = 0.0f;
             }
@@ -499,6 +506,71 @@ __device__ __forceinline__ void stream_rows(const MvArgs& a, const Qa& qa, uint3
     load(A, pair, 0);
     while (step(A, B) && step(B, A)) {
     }
+}
+
+// ---- fused all-gather: the end of a team launch ----------------------------------------------------
+// Every CTA's P2P stores are ordered (system scope) before it counts itself done; the last CTA
+// releases this step's flag to every rank, waits (bounded) until every rank's flag has arrived,
+// then copies the full vector from its own staging buffer into y and advances the step counter.
+// Double buffering by step parity keeps a rank that runs one step ahead from overwriting a half
+// that a slower rank still copies. A wait that runs out records error code 2 (tsrc_sync reports
+// it) and the launch ends; nothing else spins.
+constexpr uint32_t kTeamSpin = 1u << 22;             // x ~100 ns: a peer absent for ~0.4 s is an error
+
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ void team_finish(const MvArgs& a, uint32_t step, uint32_t* sflag, const float* rows,
+                                            uint32_t r_begin, uint32_t r_end) {
+    // this CTA's rows (contiguous) go to every rank's staging half as coalesced P2P stores
+    __syncthreads();
+    const size_t o = (size_t)(step & 1u) * a.team_n + a.team_row0 + r_begin;
+    for (uint32_t r = 0; r < a.team_world; ++r)
+        for (uint32_t i = threadIdx.x; i < r_end - r_begin; i += blockDim.x) a.team_y[r][o + i] = rows[i];
+    // the CTA's stores happen before thread 0's system-scope fence (barrier, then a cumulative
+    // fence), which orders them before the count and, through it, before the flags
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence_system();
+        *sflag = atomicAdd(a.team_state + 1, 1u) + 1u == gridDim.x ? 1u : 0u;
+    }
+    __syncthreads();
+    if (*sflag == 0u) return;
+    const uint32_t target = step + 1u;
+    if (threadIdx.x == 0) {
+        a.team_state[1] = 0u;
+        __threadfence_system();
+    }
+    __syncthreads();
+    // thread r releases this rank's flag to rank r, then waits for rank r's flag here
+    for (uint32_t r = threadIdx.x; r < a.team_world; r += blockDim.x) {
+        st_release_sys(a.team_flags[r] + a.team_rank, target);
+        const uint32_t* f = a.team_flags[a.team_rank] + r;
+        uint32_t it = 0;
+        while (ld_acquire_sys(f) < target && ++it < kTeamSpin) __nanosleep(64);
+        if (it >= kTeamSpin) atomicCAS(&g_mv_error, 0u, 2u);
+    }
+    __syncthreads();
+    // the gathered vector: L2 loads (the peers wrote it through L2; no stale L1 lines), eight in
+    // flight per thread
+    const float* src = a.team_y[a.team_rank] + (size_t)(step & 1u) * a.team_n;
+    const uint32_t n = a.team_n, stride = blockDim.x;
+    for (uint32_t i0 = threadIdx.x; i0 < n; i0 += 8u * stride) {
+        float v[8];
+#pragma unroll
+        for (uint32_t q = 0; q < 8; ++q) v[q] = i0 + q * stride < n ? __ldcg(src + i0 + q * stride) : 0.0f;
+#pragma unroll
+        for (uint32_t q = 0; q < 8; ++q)
+            if (i0 + q * stride < n) a.y[i0 + q * stride] = v[q];
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) a.team_state[0] = target;
 }
 
 // ---- the kernel ---------------------------------------------------------------------------------
@@ -537,8 +609,12 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) matvec_kernel(MvArgs a, 
     qa.bs = reinterpret_cast<uint8_t*>(qa.d) + (size_t)a.T * P.qa_d;
     qa.bs_tok = P.qa_bs;
     uint32_t* flags = reinterpret_cast<uint32_t*>(smem + a16(P.qa_bytes(a.T)));
-    if (stage_qa<FMT>(a, qa, L, flags)) stream_rows<FMT, MAXT, true>(a, qa, r_begin, r_end, warp, lane);
-    else stream_rows<FMT, MAXT, false>(a, qa, r_begin, r_end, warp, lane);
+    const uint32_t team_step = a.team_world ? *reinterpret_cast<volatile uint32_t*>(a.team_state) : 0u;
+    float* team_rows = reinterpret_cast<float*>(smem + a16(P.qa_bytes(a.T)) + 4u * kCWarps);   // [rows_per_cta]
+    if (stage_qa<FMT>(a, qa, L, flags)) stream_rows<FMT, MAXT, true>(a, qa, r_begin, r_end, warp, lane, team_rows);
+    else stream_rows<FMT, MAXT, false>(a, qa, r_begin, r_end, warp, lane, team_rows);
+    if (a.team_world)
+        team_finish(a, team_step, reinterpret_cast<uint32_t*>(smem + a16(P.qa_bytes(a.T))), team_rows, r_begin, r_end);
 }
 
 // ---- host side ------------------------------------------------------------------------------------
@@ -563,7 +639,7 @@ static int g_num_sms[64];
 template <int FMT, int MAXT>
 static cudaError_t launch_t(const MvArgs& a, cudaStream_t st) {
     const Plan P = make_plan(FMT, a.K);
-    const size_t smem = P.total(a.T);
+    size_t smem = P.total(a.T);
     cudaError_t e = allow_smem<FMT, MAXT>();
     if (e != cudaSuccess) return e;
     int dev = 0;
@@ -578,6 +654,7 @@ static cudaError_t launch_t(const MvArgs& a, cudaStream_t st) {
     uint32_t rpc = (a.n_rows + sms - 1u) / sms;
     rpc = (rpc + 1u) & ~1u;
     const uint32_t blocks = (a.n_rows + rpc - 1u) / rpc;
+    if (a.team_world) smem += 4u * rpc;                       // the CTA's rows before they are sent
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(blocks);
     cfg.blockDim = dim3(kThreads);

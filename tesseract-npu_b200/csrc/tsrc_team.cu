@@ -1,0 +1,182 @@
+// tsrc_team.cu -- MUL_MAT with the all-gather of its rows fused in, over the GPUs of one box.
+//
+// Tensor parallelism splits a weight's rows over the ranks (the reference's symmetric row split,
+// jwkim04/tesseract-npu sw/sim/tsr_ref.c:335-357); every rank then needs every row of y for the
+// next layer. Instead of a matvec followed by a collective, the matvec kernel itself stores each
+// finished row into every rank's staging buffer over NVLink (CUDA IPC mappings of the peers'
+// buffers: plain P2P stores, no multicast) and its last CTA exchanges per-step flags with the
+// peers (release / acquire at system scope, a bounded wait) before it copies the gathered vector
+// out. The reference has no counterpart (its channels live on one card).
+//
+// A team's buffer on each rank: staging [2][n_max] f32 (double-buffered by step parity) | flags
+// [world] u32 (the last step each rank has completed) | state [2] u32 (this rank's steps, CTAs
+// finished in the current launch). All start at zero; every rank must run the same sequence of
+// tsrc_mul_mat_allgather calls (one step each).
+#include <cuda_runtime.h>
+
+#include <cstdio>
+#include <cstring>
+
+#include "../../include/tsrc.h"
+#include "tsrc_internal.h"
+
+namespace tsrc {
+int set_error(int code, const char* msg);
+int mm_check(tsrc_ctx* ctx, const tsrc_weight* w, const float* x, uint32_t T, uint32_t* x_stride, float* y, uint32_t* y_stride,
+             const float* add, uint32_t add_stride, uint32_t flags, float s0, float s1, MvArgs* base, uint32_t* fmt,
+             const char* who);
+int weight_rows(const tsrc_weight* w, uint32_t* N, uint32_t* row0, uint32_t* n_rows);
+}  // namespace tsrc
+
+struct tsrc_team {
+    tsrc_ctx* ctx;
+    int device;
+    uint32_t rank, world, n_max;
+    size_t staging_bytes, bytes;
+    uint8_t* local;             // this rank's buffer
+    uint8_t* peer[64];          // every rank's buffer (this rank's is `local`)
+    bool opened[64];
+    bool connected;
+    float** dev_y;              // device arrays of the staging / flag pointers of every rank
+    uint32_t** dev_flags;
+};
+
+namespace {
+
+size_t a256(size_t n) { return (n + 255u) & ~(size_t)255u; }
+
+int cuda_err(cudaError_t e, const char* what) {
+    char msg[256];
+    snprintf(msg, sizeof msg, "%s: %s", what, cudaGetErrorString(e));
+    return tsrc::set_error(TSRC_E_CUDA, msg);
+}
+
+}  // namespace
+
+extern "C" {
+
+int tsrc_team_create(tsrc_ctx* ctx, uint32_t rank, uint32_t world, uint32_t n_max, void* handle_out, tsrc_team** out) {
+    if (!ctx || !handle_out || !out) return tsrc::set_error(TSRC_E_ARG, "tsrc_team_create: NULL argument");
+    *out = nullptr;
+    if (world < 1 || world > 64 || rank >= world) return tsrc::set_error(TSRC_E_ARG, "tsrc_team_create: rank / world out of range");
+    if (n_max == 0) return tsrc::set_error(TSRC_E_ARG, "tsrc_team_create: n_max is 0");
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_err(e, "cudaGetDevice");
+    tsrc_team* t = new tsrc_team{};
+    t->ctx = ctx;
+    t->device = dev;
+    t->rank = rank;
+    t->world = world;
+    t->n_max = n_max;
+    t->staging_bytes = a256((size_t)2 * n_max * 4u);
+    t->bytes = t->staging_bytes + a256((size_t)world * 4u) + 256u;
+    e = cudaMalloc(&t->local, t->bytes);
+    if (e == cudaSuccess) e = cudaMemset(t->local, 0, t->bytes);
+    if (e == cudaSuccess) e = cudaMalloc(&t->dev_y, sizeof(float*) * world);
+    if (e == cudaSuccess) e = cudaMalloc(&t->dev_flags, sizeof(uint32_t*) * world);
+    cudaIpcMemHandle_t h;
+    if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, t->local);
+    if (e != cudaSuccess) {
+        cudaFree(t->local);
+        cudaFree(t->dev_y);
+        cudaFree(t->dev_flags);
+        delete t;
+        return cuda_err(e, "tsrc_team_create");
+    }
+    static_assert(sizeof(cudaIpcMemHandle_t) == TSRC_TEAM_HANDLE_BYTES, "IPC handle size");
+    std::memcpy(handle_out, &h, sizeof h);
+    t->peer[rank] = t->local;
+    *out = t;
+    return TSRC_OK;
+}
+
+int tsrc_team_connect(tsrc_team* t, const void* handles) {
+    if (!t || !handles) return tsrc::set_error(TSRC_E_ARG, "tsrc_team_connect: NULL argument");
+    if (t->connected) return tsrc::set_error(TSRC_E_ARG, "tsrc_team_connect: already connected");
+    for (uint32_t r = 0; r < t->world; ++r) {
+        if (r == t->rank) continue;
+        cudaIpcMemHandle_t h;
+        std::memcpy(&h, static_cast<const uint8_t*>(handles) + (size_t)r * TSRC_TEAM_HANDLE_BYTES, sizeof h);
+        void* p = nullptr;
+        cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+        if (e != cudaSuccess) {
+            char msg[160];
+            snprintf(msg, sizeof msg, "tsrc_team_connect: opening rank %u's buffer", r);
+            return cuda_err(e, msg);
+        }
+        t->peer[r] = static_cast<uint8_t*>(p);
+        t->opened[r] = true;
+    }
+    float* ys[64];
+    uint32_t* fs[64];
+    for (uint32_t r = 0; r < t->world; ++r) {
+        ys[r] = reinterpret_cast<float*>(t->peer[r]);
+        fs[r] = reinterpret_cast<uint32_t*>(t->peer[r] + t->staging_bytes);
+    }
+    cudaError_t e = cudaMemcpy(t->dev_y, ys, sizeof(float*) * t->world, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMemcpy(t->dev_flags, fs, sizeof(uint32_t*) * t->world, cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) return cuda_err(e, "tsrc_team_connect");
+    t->connected = true;
+    return TSRC_OK;
+}
+
+int tsrc_team_connect_local(tsrc_team* t, const tsrc_team* const* members) {
+    if (!t || !members) return tsrc::set_error(TSRC_E_ARG, "tsrc_team_connect_local: NULL argument");
+    if (t->connected) return tsrc::set_error(TSRC_E_ARG, "tsrc_team_connect_local: already connected");
+    float* ys[64];
+    uint32_t* fs[64];
+    for (uint32_t r = 0; r < t->world; ++r) {
+        const tsrc_team* m = members[r];
+        if (!m || m->world != t->world || m->rank != r || m->n_max != t->n_max)
+            return tsrc::set_error(TSRC_E_ARG, "tsrc_team_connect_local: members must be ranks 0..world-1 of equal teams");
+        t->peer[r] = m->local;
+        ys[r] = reinterpret_cast<float*>(m->local);
+        fs[r] = reinterpret_cast<uint32_t*>(m->local + m->staging_bytes);
+    }
+    cudaError_t e = cudaMemcpy(t->dev_y, ys, sizeof(float*) * t->world, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMemcpy(t->dev_flags, fs, sizeof(uint32_t*) * t->world, cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) return cuda_err(e, "tsrc_team_connect_local");
+    t->connected = true;
+    return TSRC_OK;
+}
+
+int tsrc_team_free(tsrc_team* t) {
+    if (!t) return tsrc::set_error(TSRC_E_ARG, "tsrc_team_free: NULL team");
+    cudaDeviceSynchronize();
+    for (uint32_t r = 0; r < t->world; ++r)
+        if (t->opened[r]) cudaIpcCloseMemHandle(t->peer[r]);
+    cudaFree(t->local);
+    cudaFree(t->dev_y);
+    cudaFree(t->dev_flags);
+    delete t;
+    return TSRC_OK;
+}
+
+int tsrc_mul_mat_allgather(tsrc_ctx* ctx, tsrc_team* t, const tsrc_weight* w, const float* x, float* y, void* stream) {
+    if (!t || !t->connected) return tsrc::set_error(TSRC_E_ARG, "tsrc_mul_mat_allgather: team missing or not connected");
+    tsrc::MvArgs a{};
+    uint32_t fmt = 0, x_stride = 0, y_stride = 0;
+    int rc = tsrc::mm_check(ctx, w, x, 1, &x_stride, y, &y_stride, nullptr, 0, 0, 1.0f, 1.0f, &a, &fmt,
+                            "tsrc_mul_mat_allgather");
+    if (rc != TSRC_OK) return rc;
+    uint32_t N = 0, row0 = 0, n_rows = 0;
+    tsrc::weight_rows(w, &N, &row0, &n_rows);
+    if (N > t->n_max) return tsrc::set_error(TSRC_E_ARG, "tsrc_mul_mat_allgather: N exceeds the team's n_max");
+    a.x = x;
+    a.x_stride = x_stride;
+    a.T = 1;
+    a.y = y;
+    a.team_y = t->dev_y;
+    a.team_flags = t->dev_flags;
+    a.team_state = reinterpret_cast<uint32_t*>(t->local + t->staging_bytes + a256((size_t)t->world * 4u));
+    a.team_world = t->world;
+    a.team_rank = t->rank;
+    a.team_row0 = row0;
+    a.team_n = N;
+    cudaError_t e = tsrc::launch_matvec(fmt, a, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_err(e, "tsrc_mul_mat_allgather launch");
+    return TSRC_OK;
+}
+
+}  // extern "C"

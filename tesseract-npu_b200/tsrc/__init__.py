@@ -57,6 +57,11 @@ _SIGS = {
     "tsrc_mul_mat_unsupported": (ct.c_char_p, [_u32, _u64, _u64, _u64]),
     "tsrc_qact": (_i, [_p, _u32, _p, _u32, _u32, _u32, _p, _p, _p, _p]),
     "tsrc_mul_mat_isums": (_i, [_p, _p, _p, _p, _p, _p]),
+    "tsrc_team_connect_local": (_i, [_p, _p]),
+    "tsrc_team_create": (_i, [_p, _u32, _u32, _u32, _p, ct.POINTER(_p)]),
+    "tsrc_team_connect": (_i, [_p, _p]),
+    "tsrc_team_free": (_i, [_p]),
+    "tsrc_mul_mat_allgather": (_i, [_p, _p, _p, _p, _p, _p]),
     "tsrc_kv_create": (_i, [_p, _u32, _u32, _u32, ct.POINTER(_p)]),
     "tsrc_kv_free": (_i, [_p]),
     "tsrc_kv_set_rows": (_i, [_p, _p, _u32, _p, _u32, _u32, _p, _u32, _p]),
@@ -73,6 +78,7 @@ class FaCfg(ct.Structure):
 
 
 KV_K, KV_V = 0, 1
+TEAM_HANDLE_BYTES = 64
 Q8_0_BLOCK_BYTES = 34
 
 
@@ -233,6 +239,19 @@ class Device:
         _check(lib().tsrc_qact(self.handle, kind, _addr(x), K, T, x_stride, _addr(q), _addr(d), _addr(bs),
                                _stream(stream)))
 
+    # ---- tensor parallelism: MUL_MAT with the all-gather fused in ----
+    def team_create(self, rank: int, world: int, n_max: int) -> "Team":
+        """This rank's side of a team of `world` GPUs; exchange `team.handle` (bytes) with the other
+        ranks and call team.connect(all handles in rank order)."""
+        h = _p()
+        buf = ct.create_string_buffer(TEAM_HANDLE_BYTES)
+        _check(lib().tsrc_team_create(self.handle, rank, world, n_max, buf, ct.byref(h)))
+        return Team(self, h, rank, world, bytes(buf.raw))
+
+    def mul_mat_allgather(self, team: "Team", w: "Weight", x, y, stream=None) -> None:
+        """y (all N rows, device) = this rank's row shard of W . QACT(x) gathered from every rank."""
+        _check(lib().tsrc_mul_mat_allgather(self.handle, team.handle, w.handle, _addr(x), _addr(y), _stream(stream)))
+
     # ---- KV cache and FLASH_ATTN_EXT ----
     def kv_create(self, n_head_kv: int, head_dim: int, n_cells: int) -> "KvCache":
         h = _p()
@@ -319,4 +338,26 @@ class KvCache:
     def free(self) -> None:
         if self.handle and self.dev.handle:
             _check(lib().tsrc_kv_free(self.handle))
+        self.handle = None
+
+
+class Team:
+    """One rank's side of a tensor-parallel team (CUDA IPC buffers of every rank)."""
+
+    def __init__(self, dev: Device, handle, rank: int, world: int, ipc_handle: bytes):
+        self.dev, self.handle, self.rank, self.world, self.ipc_handle = dev, handle, rank, world, ipc_handle
+
+    def connect(self, handles: bytes) -> None:
+        """handles: world x TEAM_HANDLE_BYTES bytes, rank order."""
+        buf = ct.create_string_buffer(bytes(handles), len(handles))
+        _check(lib().tsrc_team_connect(self.handle, buf))
+
+    def connect_local(self, members: list) -> None:
+        """Test hook: members = the teams of ranks 0..world-1 in this process (this one included)."""
+        arr = (_p * len(members))(*[m.handle.value for m in members])
+        _check(lib().tsrc_team_connect_local(self.handle, arr))
+
+    def free(self) -> None:
+        if self.handle and self.dev.handle:
+            _check(lib().tsrc_team_free(self.handle))
         self.handle = None
