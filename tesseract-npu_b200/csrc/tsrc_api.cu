@@ -10,6 +10,7 @@
 #include <algorithm>
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <set>
@@ -53,6 +54,13 @@ size_t ggml_row_bytes(uint32_t fmt, uint32_t K) {
 size_t qs_row_bytes(uint32_t fmt, uint32_t K) { return tsrc::Layout{fmt, K}.qs_row_bytes(); }
 size_t meta_row_bytes(uint32_t fmt, uint32_t K) { return tsrc::Layout{fmt, K}.meta_row_bytes(); }
 size_t align256(size_t n) { return (n + 255u) & ~(size_t)255u; }
+
+// The tensor-core prefill path is on unless TSRC_NO_TC is set (then many tokens run through the
+// matvec kernel, eight per launch; both give the same bits).
+bool tc_enabled() {
+    static const bool on = std::getenv("TSRC_NO_TC") == nullptr;
+    return on;
+}
 
 // s0 / s1 enter the f32 rules as inputs: DAZ them once on the host.
 float daz_host(float v) {
@@ -293,6 +301,9 @@ int tsrc_sync(tsrc_ctx* ctx, void* stream) {
     if (e != cudaSuccess) return cuda_fail(e, "reading the kernel error flag");
     if (code) return fail(TSRC_E_DEVICE, "a matvec kernel gave up a bounded wait (code %u%s)", code,
                           code == 2 ? ": a team peer did not signal its step" : "");
+    e = tsrc::tc_error(&code, true);
+    if (e != cudaSuccess) return cuda_fail(e, "reading the tensor-core kernel error flag");
+    if (code) return fail(TSRC_E_DEVICE, "a tensor-core MUL_MAT kernel gave up waiting for its MMA (code %u)", code);
     e = tsrc::kv_error(&code, true);
     if (e != cudaSuccess) return cuda_fail(e, "reading the KV error flag");
     if (code) return fail(TSRC_E_ARG, "tsrc_kv_set_rows: a cell index outside the cache (those rows were not stored)");
@@ -447,6 +458,33 @@ static int mul_mat_impl(tsrc_ctx* ctx, const tsrc_weight* w, const float* x, uin
         a.isum_out = isum_out;
         cudaError_t e = tsrc::launch_matvec(fmt, a, st);
         if (e != cudaSuccess) return cuda_fail(e, "matvec launch");
+        return TSRC_OK;
+    }
+    if (fmt == TSRC_FMT_Q8_0 && T > tsrc::kMvMaxT && tc_enabled()) {
+        // prefill: QACT of every token, then one tensor-core MUL_MAT over all of them
+        rc = ensure_scratch(ctx, qa_bytes(fmt, K, T));
+        if (rc) return rc;
+        int8_t* q = reinterpret_cast<int8_t*>(ctx->scratch);
+        float* d = reinterpret_cast<float*>(ctx->scratch + align256((size_t)T * K));
+        cudaError_t e = tsrc::launch_qact(0u, x, K, T, x_stride, q, d, nullptr, st);
+        if (e != cudaSuccess) return cuda_fail(e, "QACT launch");
+        tsrc::MvArgs a{};
+        a.qs = w->qs;
+        a.meta = w->meta;
+        a.n_rows = w->n_rows;
+        a.K = K;
+        a.qx = q;
+        a.dx = d;
+        a.T = T;
+        a.y = y;
+        a.y_stride = y_stride;
+        a.add = (flags & TSRC_MM_ADD) ? add : nullptr;
+        a.add_stride = add_stride;
+        a.flags = flags;
+        a.s0 = daz_host(s0);
+        a.s1 = daz_host(s1);
+        e = tsrc::launch_mm_tc(fmt, a, st);
+        if (e != cudaSuccess) return cuda_fail(e, "tensor-core MUL_MAT launch");
         return TSRC_OK;
     }
     // several tokens: one QACT launch per tile of tokens into the scratch image, then the matvec

@@ -42,6 +42,9 @@ struct MvArgs {
 cudaError_t launch_qact(uint32_t kind, const float* x, uint32_t K, uint32_t T, uint32_t x_stride, int8_t* q, float* d,
                         int16_t* bs, cudaStream_t st);
 cudaError_t launch_matvec(uint32_t fmt, const MvArgs& a, cudaStream_t st);
+// Many-token MUL_MAT on the tcgen05 tensor cores (Q8_0; the QA image in qx / dx, any T).
+cudaError_t launch_mm_tc(uint32_t fmt, const MvArgs& a, cudaStream_t st);
+cudaError_t tc_error(uint32_t* code, bool clear);
 size_t mv_smem_bytes(uint32_t fmt, uint32_t K, uint32_t T);
 // The first error code any matvec launch recorded on the current device (0 = none).
 cudaError_t matvec_error(uint32_t* code, bool clear);

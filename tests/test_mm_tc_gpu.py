@@ -1,0 +1,56 @@
+"""Prefill MUL_MAT (many tokens) on the tcgen05 tensor cores, through the C ABI, against the oracle.
+
+Q8_0 calls with more than eight tokens run one tensor-core kernel over all tokens (the exact int32
+block sums from tcgen05.mma kind::i8, the f32 row rule in registers). The results must be the
+reference's bit for bit, as for the matvec kernel: same tolerance (exact equality of the f32 bits).
+"""
+import numpy as np
+import pytest
+
+import helpers as H
+import tsrc
+
+pytestmark = pytest.mark.gpu
+
+
+def _mul_mat(dev, wd, x, T, flags=0, add=None, s0=1.0, s1=1.0):
+    import torch
+    y = torch.full((T, wd.n_rows), float("nan"), device="cuda")
+    xd = torch.from_numpy(np.ascontiguousarray(x)).cuda()
+    ad = None if add is None else torch.from_numpy(np.ascontiguousarray(add)).cuda()
+    dev.mul_mat(wd, xd, y, T=T, flags=flags, add=ad, add_stride=None if add is None else wd.n_rows, s0=s0, s1=s1)
+    dev.sync()
+    return y.cpu().numpy()
+
+
+@pytest.mark.parametrize("N,K,T,seed", [(300, 896, 9, 1), (1000, 4096, 64, 2), (257, 512, 33, 3), (129, 96, 100, 4),
+                                        (4864, 896, 17, 5), (130, 1024, 300, 6), (64, 8192, 48, 7)])
+def test_prefill_q8_0_bit_exact(dev, tsro, N, K, T, seed):
+    w = H.weights(tsro, 0, N, K, seed)
+    x = H.acts(K, T, seed + 100)
+    wd = dev.upload(0, w, N, K)
+    try:
+        got = _mul_mat(dev, wd, x, T)
+        want = tsro.matvec(0, w, K, x)
+        np.testing.assert_array_equal(got.view(np.uint32), want.view(np.uint32))
+    finally:
+        wd.free()
+
+
+def test_prefill_q8_0_special_values_and_epilogues(dev, tsro):
+    N, K, T = 200, 640, 40
+    w = H.weights(tsro, 0, N, K, 11)
+    x = H.special_acts(K, T, 12)
+    wd = dev.upload(0, w, N, K)
+    try:
+        want = tsro.matvec(0, w, K, x)
+        np.testing.assert_array_equal(_mul_mat(dev, wd, x, T).view(np.uint32), want.view(np.uint32))
+        add = np.random.default_rng(13).standard_normal((T, N)).astype(np.float32)
+        got = _mul_mat(dev, wd, x, T, add=add)
+        want_add = tsro.matvec(0, w, K, x, flags=tsrc.MM_ADD, add=add)
+        np.testing.assert_array_equal(got.view(np.uint32), want_add.view(np.uint32))
+        got = _mul_mat(dev, wd, x, T, flags=tsrc.MM_SOFTCAP, s0=0.03, s1=30.0)
+        want_sc = tsro.matvec(0, w, K, x, flags=tsrc.MM_SOFTCAP, s0=0.03, s1=30.0)
+        np.testing.assert_array_equal(got.view(np.uint32), want_sc.view(np.uint32))
+    finally:
+        wd.free()
