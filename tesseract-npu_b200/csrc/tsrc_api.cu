@@ -460,13 +460,14 @@ static int mul_mat_impl(tsrc_ctx* ctx, const tsrc_weight* w, const float* x, uin
         if (e != cudaSuccess) return cuda_fail(e, "matvec launch");
         return TSRC_OK;
     }
-    if (fmt == TSRC_FMT_Q8_0 && T > tsrc::kMvMaxT && tc_enabled()) {
+    if (T > tsrc::kMvMaxT && !isum_out && tc_enabled()) {
         // prefill: QACT of every token, then one tensor-core MUL_MAT over all of them
         rc = ensure_scratch(ctx, qa_bytes(fmt, K, T));
         if (rc) return rc;
         int8_t* q = reinterpret_cast<int8_t*>(ctx->scratch);
         float* d = reinterpret_cast<float*>(ctx->scratch + align256((size_t)T * K));
-        cudaError_t e = tsrc::launch_qact(0u, x, K, T, x_stride, q, d, nullptr, st);
+        int16_t* bs = reinterpret_cast<int16_t*>(ctx->scratch + align256((size_t)T * K) + align256((size_t)T * (K / block_of(fmt)) * 4u));
+        cudaError_t e = tsrc::launch_qact(fmt == TSRC_FMT_Q8_0 ? 0u : 1u, x, K, T, x_stride, q, d, bs, st);
         if (e != cudaSuccess) return cuda_fail(e, "QACT launch");
         tsrc::MvArgs a{};
         a.qs = w->qs;
@@ -475,6 +476,7 @@ static int mul_mat_impl(tsrc_ctx* ctx, const tsrc_weight* w, const float* x, uin
         a.K = K;
         a.qx = q;
         a.dx = d;
+        a.bsx = bs;
         a.T = T;
         a.y = y;
         a.y_stride = y_stride;

@@ -1,8 +1,9 @@
 """Prefill MUL_MAT (many tokens) on the tcgen05 tensor cores, through the C ABI, against the oracle.
 
-Q8_0 calls with more than eight tokens run one tensor-core kernel over all tokens (the exact int32
-block sums from tcgen05.mma kind::i8, the f32 row rule in registers). The results must be the
-reference's bit for bit, as for the matvec kernel: same tolerance (exact equality of the f32 bits).
+Q8_0 and Q4_K calls with more than eight tokens run one QACT over all tokens and one tensor-core
+kernel (the exact int32 block / sub-block sums from tcgen05.mma kind::i8, the f32 row rule in
+registers). The results must be the reference's bit for bit, as for the matvec kernel: same
+tolerance (exact equality of the f32 bits).
 """
 import numpy as np
 import pytest
@@ -37,20 +38,56 @@ def test_prefill_q8_0_bit_exact(dev, tsro, N, K, T, seed):
         wd.free()
 
 
-def test_prefill_q8_0_special_values_and_epilogues(dev, tsro):
-    N, K, T = 200, 640, 40
-    w = H.weights(tsro, 0, N, K, 11)
-    x = H.special_acts(K, T, 12)
-    wd = dev.upload(0, w, N, K)
+@pytest.mark.parametrize("N,K,T,seed", [(300, 1024, 9, 21), (1000, 4096, 64, 22), (257, 256, 33, 23), (129, 512, 100, 24),
+                                        (896, 4864, 17, 25), (130, 2048, 300, 26), (64, 8192, 20, 27)])
+def test_prefill_q4_k_bit_exact(dev, tsro, N, K, T, seed):
+    w = H.weights(tsro, 1, N, K, seed)
+    x = H.acts(K, T, seed + 100)
+    wd = dev.upload(1, w, N, K)
     try:
-        want = tsro.matvec(0, w, K, x)
+        got = _mul_mat(dev, wd, x, T)
+        want = tsro.matvec(1, w, K, x)
+        np.testing.assert_array_equal(got.view(np.uint32), want.view(np.uint32))
+    finally:
+        wd.free()
+
+
+@pytest.mark.parametrize("fmt", [0, 1])
+def test_prefill_tiny_activations(dev, tsro, fmt):
+    """Blocks scaled down to 1e-20 .. 1e-37: activation scales far below 2^-79, so products and
+    sums go subnormal and the reference's flush rule decides the low bits."""
+    N, K, T = 160, 1024, 24
+    w = H.weights(tsro, fmt, N, K, 31 + fmt)
+    x = H.acts(K, T, 32 + fmt)
+    rng = np.random.default_rng(33 + fmt)
+    for t in range(T):
+        for b in range(K // 32):
+            if rng.integers(0, 3) == 0:
+                x[t, 32 * b:32 * b + 32] *= np.float32(10.0 ** -rng.integers(20, 38))
+    wd = dev.upload(fmt, w, N, K)
+    try:
+        got = _mul_mat(dev, wd, x, T)
+        want = tsro.matvec(fmt, w, K, x)
+        np.testing.assert_array_equal(got.view(np.uint32), want.view(np.uint32))
+    finally:
+        wd.free()
+
+
+@pytest.mark.parametrize("fmt", [0, 1])
+def test_prefill_special_values_and_epilogues(dev, tsro, fmt):
+    N, K, T = 200, 1024 if fmt else 640, 40
+    w = H.weights(tsro, fmt, N, K, 11)
+    x = H.special_acts(K, T, 12)
+    wd = dev.upload(fmt, w, N, K)
+    try:
+        want = tsro.matvec(fmt, w, K, x)
         np.testing.assert_array_equal(_mul_mat(dev, wd, x, T).view(np.uint32), want.view(np.uint32))
         add = np.random.default_rng(13).standard_normal((T, N)).astype(np.float32)
         got = _mul_mat(dev, wd, x, T, add=add)
-        want_add = tsro.matvec(0, w, K, x, flags=tsrc.MM_ADD, add=add)
+        want_add = tsro.matvec(fmt, w, K, x, flags=tsrc.MM_ADD, add=add)
         np.testing.assert_array_equal(got.view(np.uint32), want_add.view(np.uint32))
         got = _mul_mat(dev, wd, x, T, flags=tsrc.MM_SOFTCAP, s0=0.03, s1=30.0)
-        want_sc = tsro.matvec(0, w, K, x, flags=tsrc.MM_SOFTCAP, s0=0.03, s1=30.0)
+        want_sc = tsro.matvec(fmt, w, K, x, flags=tsrc.MM_SOFTCAP, s0=0.03, s1=30.0)
         np.testing.assert_array_equal(got.view(np.uint32), want_sc.view(np.uint32))
     finally:
         wd.free()
