@@ -84,17 +84,6 @@ __device__ __forceinline__ int32_t dot16us(const uint4 w, const uint4 x, int32_t
     acc = dp4a_us(w.w, x.w, acc);
     return acc;
 }
-// two signed 16-bit values of a times unsigned bytes 0,1 (lo) or 2,3 (hi) of b, plus c
-__device__ __forceinline__ int32_t dp2a_lo(uint32_t a, uint32_t b, int32_t c) {
-    int32_t d;
-    asm("dp2a.lo.s32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
-    return d;
-}
-__device__ __forceinline__ int32_t dp2a_hi(uint32_t a, uint32_t b, int32_t c) {
-    int32_t d;
-    asm("dp2a.hi.s32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
-    return d;
-}
 __device__ __forceinline__ int32_t ubyte(uint32_t w, uint32_t i) { return (int32_t)__byte_perm(w, 0u, 0x4440u | i); }
 
 template <class T>

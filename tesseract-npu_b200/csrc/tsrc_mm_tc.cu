@@ -3,21 +3,23 @@
 // Numerics: the reference's MVM row rule bit for bit (jwkim04/tesseract-npu sw/sim/tsr_ref.c:
 // 533-635): for each token and row, block i contributes t_i = (d_w (*) Dx_i) (*) f32(isum_i) to
 // partial p[i mod 16] (in order of i, from +0), then the fixed 16-partial tree. The exact int32
-// block sums isum_i come from one tcgen05.mma (kind::i8, K = 32: one block) per block, written to
-// a fresh TMEM tile (no accumulation across blocks: each block has its own scales). The f32 part
-// runs in registers: blocks are visited partial by partial (i = j, j + 16, j + 32, ... for j = 0..15),
-// so a thread needs one running partial per output plus a four-deep stack that folds the partials
-// into the tree as they complete (((p0 + p1) + (p2 + p3)) + ...). Every factor is a multiple of
-// 2^-24 (fp16 weight scales, the A32 activation scale stored as fp16, integer sums), so every
-// product and sum is a multiple of 2^-48 and never subnormal: the flush tests are not needed.
+// block sums isum_i come from tcgen05.mma (kind::i8, K = 32: one block or Q4_K sub-block per MMA)
+// into fresh TMEM tiles (no accumulation across blocks: each block has its own scales). The f32
+// part runs on the CUDA cores: blocks are visited partial by partial (i = j, j + 16, j + 32, ... for
+// j = 0..15), so a thread keeps one running partial per output and folds the partials into the
+// tree as they complete (((p0 + p1) + (p2 + p3)) + ...) through a four-level stack in shared memory.
+// Q8_0: every factor is a multiple of 2^-24 (fp16 weight scales, the A32 activation scale stored as
+// fp16, integer sums), so every product and sum is a multiple of 2^-48 and never subnormal: the
+// flush tests are not needed.
 //
-// Work split: a CTA computes 128 rows x NT tokens; TMEM holds two 128 x NT int32 tiles (block s
-// and block s + 1 alternate); warp w reads TMEM lanes 32 (w mod 4) .. + 31 (its rows) and columns
-// 16 (w / 4) .. + 15 (its tokens). Operands go through a ring of kStages shared-memory stages,
-// copied with cp.async into the canonical K-major, no-swizzle layout of the UMMA descriptors (8-row
-// x 16-byte core matrices; the two 16-byte halves of a block 128 bytes apart, 8-row groups 256 bytes
-// apart). One thread issues each MMA and commits it to an mbarrier; every wait on an mbarrier is
-// bounded (error code 3 in the matvec error flag, reported by tsrc_sync).
+// Work split: a CTA computes 128 rows x NT tokens with warp-specialised roles (producer warps
+// copying operands with cp.async into a ring of shared-memory stages in the canonical K-major,
+// no-swizzle layout of the UMMA descriptors -- 8-row x 16-byte core matrices, the two 16-byte
+// halves of a block 128 bytes apart, 8-row groups 256 bytes apart --, one thread issuing the MMAs,
+// epilogue warps reading TMEM lanes 32 (w mod 4) .. + 31 and token columns 16 (w / 4) .. + 15),
+// handing work over through mbarriers. Every wait is bounded by the SM clock (~1 s); a wait that
+// runs out sets a CTA-wide abort flag that ends every role's loop, and error code 3, reported by
+// tsrc_sync.
 #include "tsrc_internal.h"
 #include "tsrc_layout.cuh"
 #include "tsrc_numerics.cuh"
@@ -28,9 +30,7 @@ namespace {
 
 __device__ unsigned int g_tc_error;                // first error code of any launch (3: an MMA wait ran out)
 
-constexpr uint32_t kStages = 6;                    // operand ring (blocks in flight: kStages - 2)
 constexpr uint32_t kTileM = 128;
-constexpr uint32_t kSpin = 1u << 22;               // mbarrier polls (~30 ns apart) before giving up
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
@@ -53,22 +53,6 @@ __device__ __forceinline__ uint32_t umma_idesc() {
     return (2u << 4) | (1u << 7) | (1u << 10) | ((NT >> 3) << 17) | ((kTileM >> 4) << 24);
 }
 
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
-    for (uint32_t it = 0; it < kSpin; ++it) {
-        uint32_t ok;
-        asm volatile(
-            "{\n\t.reg .pred p;\n\t"
-            "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-            "selp.u32 %0, 1, 0, p;\n\t}"
-            : "=r"(ok)
-            : "r"(bar), "r"(parity)
-            : "memory");
-        if (ok) return true;
-        __nanosleep(20);
-    }
-    return false;
-}
-
 // block of sequence position s in partial-major order (j = 0..15, then i = j, j + 16, ...)
 struct Seq {
     uint32_t nb, q, rem;      // q = nb / 16, rem = nb % 16
@@ -89,19 +73,6 @@ struct Seq {
         return jj + 16u * ii;
     }
 };
-
-// folds partial j (value v) into the 16-partial tree kept as a four-level stack; after partial 15
-// the tree's value is in L0
-__device__ __forceinline__ void tree_push(float& L0, float& L1, float& L2, float& L3, uint32_t j, float v) {
-    if ((j & 1u) == 0) { L0 = v; return; }
-    v = fadd(L0, v);
-    if ((j & 2u) == 0) { L1 = v; return; }
-    v = fadd(L1, v);
-    if ((j & 4u) == 0) { L2 = v; return; }
-    v = fadd(L2, v);
-    if ((j & 8u) == 0) { L3 = v; return; }
-    L0 = fadd(L3, v);
-}
 
 // ---- pipeline primitives (warp-specialised kernels) --------------------------------------------
 constexpr long long kWaitCycles = 1ll << 31;       // a wait gives up after ~1 s of SM clock
@@ -155,68 +126,78 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
         : "r"(taddr));
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
-__device__ __forceinline__ void tmem_st16(uint32_t taddr, const float (&v)[16]) {
-    asm volatile(
-        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};"
-        ::"r"(taddr), "f"(v[0]), "f"(v[1]), "f"(v[2]), "f"(v[3]), "f"(v[4]), "f"(v[5]), "f"(v[6]), "f"(v[7]), "f"(v[8]),
-          "f"(v[9]), "f"(v[10]), "f"(v[11]), "f"(v[12]), "f"(v[13]), "f"(v[14]), "f"(v[15])
-        : "memory");
-    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
-}
-
 // Folds partial j (16 values, one per token of the thread) into the 16-partial tree whose four
-// stack levels live in TMEM columns lv, lv + NT, lv + 2 NT, lv + 3 NT (the thread's lane); after
+// stack levels live in shared memory (level l of token i at s[l * lstride + i * kTileM]); after
 // partial 15 the tree's value is level 0. FLUSH: the reference's flush test on every sum.
-template <bool FLUSH, uint32_t NT>
-__device__ __forceinline__ void tree_push_tmem(uint32_t lv, uint32_t j, float (&v)[16]) {
-    uint32_t w[16];
+template <bool FLUSH>
+__device__ __forceinline__ void tree_push_smem(float* s, uint32_t lstride, uint32_t j, float (&v)[16]) {
 #pragma unroll
     for (uint32_t lvl = 0; lvl < 4; ++lvl) {
+        float* p = s + lvl * lstride;
         if (((j >> lvl) & 1u) == 0u) {
-            tmem_st16(lv + lvl * NT, v);
+#pragma unroll
+            for (uint32_t i = 0; i < 16; ++i) p[i * kTileM] = v[i];
             return;
         }
-        tmem_ld16(lv + lvl * NT, w);
 #pragma unroll
-        for (uint32_t i = 0; i < 16; ++i) v[i] = FLUSH ? fadd(__uint_as_float(w[i]), v[i]) : __fadd_rn(__uint_as_float(w[i]), v[i]);
+        for (uint32_t i = 0; i < 16; ++i) v[i] = FLUSH ? fadd(p[i * kTileM], v[i]) : __fadd_rn(p[i * kTileM], v[i]);
     }
-    tmem_st16(lv, v);
-}
-
-// exact int32 -> f32 for |v| < 2^22 (block sums of Q8_0: |v| <= 32 * 128 * 128 = 2^19)
-__device__ __forceinline__ float small_i2f(int32_t v) {
-    return __fsub_rn(__int_as_float(v + 0x4B400000), 12582912.0f);
+#pragma unroll
+    for (uint32_t i = 0; i < 16; ++i) s[i * kTileM] = v[i];
 }
 
 // ---- Q8_0 ---------------------------------------------------------------------------------------
 // Warp roles: E epilogue warps (warp w: TMEM lanes 32 (w mod 4) .., tokens 16 (w / 4) ..), P producer
-// warps (cp.async of the block's A / B operand tiles, activation scales and weight scales into a
-// ring of S stages; a stage is published when the producer's copies of it have landed), one MMA
-// warp (TMEM allocation; one thread issues each block's MMA into one of NB accumulator tiles).
+// warps (cp.async of the operand tiles, activation scales and weight scales of BPS consecutive
+// blocks of the sequence into one of S ring stages; a stage is published when the producer's
+// copies of it have landed), one MMA warp (TMEM allocation; one thread issues the stage's MMAs into
+// one of NB accumulator groups of BPS tiles, all of TMEM). The partial trees' stacks live in shared
+// memory. Grouping blocks per stage divides the barrier work per output element by BPS.
 // mbarriers: full[S] (producers -> MMA, epilogue), empty[S] (MMA commit + epilogue warps ->
 // producers), tfull[NB] (MMA commit -> epilogue), tempty[NB] (epilogue warps -> MMA).
+// pipeline shape (compile-time tuning knobs)
+#ifndef TSRC_Q8TC_P
+#define TSRC_Q8TC_P 2u
+#endif
+#ifndef TSRC_Q8TC_BPS
+#define TSRC_Q8TC_BPS 2u
+#endif
+#ifndef TSRC_Q8TC_S
+#define TSRC_Q8TC_S 6u
+#endif
+#ifndef TSRC_Q8TC_LAG
+#define TSRC_Q8TC_LAG 2u
+#endif
+#ifndef TSRC_Q8TC_NB
+#define TSRC_Q8TC_NB 4u
+#endif
 template <uint32_t NT>
 struct Q8Cfg {
     static constexpr uint32_t E = 4u * (NT / 16u);
-    static constexpr uint32_t P = 2u;
+    static constexpr uint32_t P = TSRC_Q8TC_P;
     static constexpr uint32_t WARPS = E + P + 1u;
-    static constexpr uint32_t S = 16u;
-    static constexpr uint32_t LAG = 8u;                // producer: stages in flight before publishing
-    static constexpr uint32_t NB = 4u;
+    static constexpr uint32_t BPS = TSRC_Q8TC_BPS;     // blocks per stage
+    static constexpr uint32_t S = TSRC_Q8TC_S;
+    static constexpr uint32_t LAG = TSRC_Q8TC_LAG;     // producer: stages in flight before publishing
+    static constexpr uint32_t NB = TSRC_Q8TC_NB;
     static constexpr uint32_t A_BYTES = kTileM * 32u, B_BYTES = NT * 32u;
-    static constexpr uint32_t DX_OFF = A_BYTES + B_BYTES, DW_OFF = DX_OFF + NT * 4u;
-    static constexpr uint32_t STAGE = DW_OFF + kTileM * 4u;
-    static constexpr uint32_t TCOLS = 8u * NT;         // NB accumulator tiles + 4 tree levels
-    static constexpr size_t BAR_OFF = (size_t)S * STAGE;
-    static constexpr size_t NEED = BAR_OFF + (2u * S + 2u * NB) * 8u + 16u;
-    // 512 TMEM columns: one CTA per SM (more shared memory than half the SM's)
-    static constexpr size_t SMEM = (TCOLS == 512u && NEED < 120u * 1024u) ? 120u * 1024u : NEED;
+    static constexpr uint32_t B_OFF = BPS * A_BYTES;
+    static constexpr uint32_t DX_OFF = B_OFF + BPS * B_BYTES, DW_OFF = DX_OFF + BPS * NT * 4u;
+    static constexpr uint32_t STAGE = DW_OFF + BPS * kTileM * 4u;
+    static constexpr uint32_t TCOLS = NB * BPS * NT;
+    static constexpr size_t STACK_OFF = (size_t)S * STAGE;
+    static constexpr uint32_t LSTRIDE = NT * kTileM;   // floats per stack level
+    static constexpr size_t BAR_OFF = STACK_OFF + 4u * LSTRIDE * 4u;
+    static constexpr size_t SMEM = BAR_OFF + (2u * S + 2u * NB) * 8u + 16u;
+    static_assert(TCOLS == 128u || TCOLS == 256u || TCOLS == 512u, "TMEM allocation is a power of two");
+    static_assert(SMEM <= 227u * 1024u, "shared memory");
 };
 
 template <uint32_t NT>
 __global__ void __launch_bounds__(32 * Q8Cfg<NT>::WARPS, 1) mm_q8_tc_kernel(MvArgs a) {
     using C = Q8Cfg<NT>;
     extern __shared__ __align__(128) uint8_t smem[];
+    float* stack = reinterpret_cast<float*>(smem + C::STACK_OFF);
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::BAR_OFF);
     uint64_t* empty = full + C::S;
     uint64_t* tfull = empty + C::S;
@@ -227,6 +208,7 @@ __global__ void __launch_bounds__(32 * Q8Cfg<NT>::WARPS, 1) mm_q8_tc_kernel(MvAr
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
     const uint32_t row0 = blockIdx.x * kTileM, tok0 = blockIdx.y * NT;
     const uint32_t K = a.K, nb = K / 32u, q = nb >> 4, rem = nb & 15u;
+    const uint32_t nst = (nb + C::BPS - 1u) / C::BPS;      // stage uses
     const Layout L{0u, K};
 
     if (warp == C::E + C::P) {
@@ -250,7 +232,6 @@ __global__ void __launch_bounds__(32 * Q8Cfg<NT>::WARPS, 1) mm_q8_tc_kernel(MvAr
     __syncthreads();
     asm volatile("tcgen05.fence::after_thread_sync;");
     const uint32_t tmem = *tslot;
-    bool aborted = false;
 
     if (warp >= C::E && warp < C::E + C::P) {
         // ---- producers: lane pl copies A chunks of rows (pl / 2) + 32 P k, half pl & 1, ...
@@ -270,7 +251,7 @@ __global__ void __launch_bounds__(32 * Q8Cfg<NT>::WARPS, 1) mm_q8_tc_kernel(MvAr
         for (uint32_t k = 0; k < BR; ++k) {
             const uint32_t t = (pl >> 1) + (LN / 2u) * k;
             brow[k] = a.qx + (size_t)min(tok0 + t, a.T - 1u) * K + 16u * h;
-            bdst[k] = t < NT ? C::A_BYTES + (t >> 3) * 256u + h * 128u + (t & 7u) * 16u : 0xFFFFFFFFu;
+            bdst[k] = t < NT ? C::B_OFF + (t >> 3) * 256u + h * 128u + (t & 7u) * 16u : 0xFFFFFFFFu;
         }
         const float* dxrow = a.dx + (size_t)min(tok0 + (pl < NT ? pl : 0u), a.T - 1u) * nb;
         const uint8_t* wrow[WR];
@@ -278,57 +259,67 @@ __global__ void __launch_bounds__(32 * Q8Cfg<NT>::WARPS, 1) mm_q8_tc_kernel(MvAr
         for (uint32_t k = 0; k < WR; ++k)
             wrow[k] = static_cast<const uint8_t*>(a.meta) + (size_t)min(row0 + pl + LN * k, a.n_rows - 1u) * L.meta_row_bytes();
         uint32_t j = 0, ii = 0, cnt = q + (rem > 0u ? 1u : 0u), issued = 0;
-        for (uint32_t s = 0; s < nb; ++s) {
-            const uint32_t st = s % C::S;
-            if (s >= C::S && !mbar_wait_ab(&empty[st], ((s / C::S) - 1u) & 1u, abort_flag)) { aborted = true; break; }
-            const uint32_t b = j + 16u * ii;
+        for (uint32_t u = 0; u < nst; ++u) {
+            const uint32_t st = u % C::S;
+            if (u >= C::S && !mbar_wait_ab(&empty[st], ((u / C::S) - 1u) & 1u, abort_flag)) break;
             uint8_t* sb = smem + (size_t)st * C::STAGE;
-            const size_t aoff = L.qs_off(0u, b, h);
 #pragma unroll
-            for (uint32_t k = 0; k < AR; ++k) cp_async16(sb + adst[k], arow[k] + aoff);
+            for (uint32_t x = 0; x < C::BPS; ++x) {
+                if (u * C::BPS + x < nb) {
+                    const uint32_t b = j + 16u * ii;
+                    const size_t aoff = L.qs_off(0u, b, h);
 #pragma unroll
-            for (uint32_t k = 0; k < BR; ++k)
-                if (bdst[k] != 0xFFFFFFFFu) cp_async16(sb + bdst[k], brow[k] + 32u * b);
-            if (pl < NT) cp_async4(sb + C::DX_OFF + 4u * pl, dxrow + b);
+                    for (uint32_t k = 0; k < AR; ++k) cp_async16(sb + x * C::A_BYTES + adst[k], arow[k] + aoff);
 #pragma unroll
-            for (uint32_t k = 0; k < WR; ++k) cp_async4(sb + C::DW_OFF + 4u * (pl + LN * k), wrow[k] + 2u * (b & ~1u));
+                    for (uint32_t k = 0; k < BR; ++k)
+                        if (bdst[k] != 0xFFFFFFFFu) cp_async16(sb + x * C::B_BYTES + bdst[k], brow[k] + 32u * b);
+                    if (pl < NT) cp_async4(sb + C::DX_OFF + x * NT * 4u + 4u * pl, dxrow + b);
+#pragma unroll
+                    for (uint32_t k = 0; k < WR; ++k)
+                        cp_async4(sb + C::DW_OFF + x * kTileM * 4u + 4u * (pl + LN * k), wrow[k] + 2u * (b & ~1u));
+                    if (++ii == cnt) {
+                        ++j;
+                        ii = 0;
+                        cnt = q + (j < rem ? 1u : 0u);
+                    }
+                }
+            }
             cp_async_commit();
             ++issued;
-            if (s >= C::LAG) {
+            if (u >= C::LAG) {
                 cp_async_wait<C::LAG>();
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&full[(s - C::LAG) % C::S]);
-            }
-            if (++ii == cnt) {
-                ++j;
-                ii = 0;
-                cnt = q + (j < rem ? 1u : 0u);
+                if (lane == 0) mbar_arrive(&full[(u - C::LAG) % C::S]);
             }
         }
         cp_async_wait<0>();
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         __syncwarp();
         if (lane == 0)
-            for (uint32_t s = issued > C::LAG ? issued - C::LAG : 0u; s < issued; ++s) mbar_arrive(&full[s % C::S]);
+            for (uint32_t u = issued > C::LAG ? issued - C::LAG : 0u; u < issued; ++u) mbar_arrive(&full[u % C::S]);
     } else if (warp == C::E + C::P) {
         // ---- MMA issuer
         if (lane == 0) {
             uint32_t issued = 0;
-            for (uint32_t s = 0; s < nb; ++s) {
-                const uint32_t st = s % C::S, buf = s % C::NB;
-                if (!mbar_wait_ab(&full[st], (s / C::S) & 1u, abort_flag)) break;
-                if (s >= C::NB && !mbar_wait_ab(&tempty[buf], ((s / C::NB) - 1u) & 1u, abort_flag)) break;
+            for (uint32_t u = 0; u < nst; ++u) {
+                const uint32_t st = u % C::S, buf = u % C::NB;
+                if (!mbar_wait_ab(&full[st], (u / C::S) & 1u, abort_flag)) break;
+                if (u >= C::NB && !mbar_wait_ab(&tempty[buf], ((u / C::NB) - 1u) & 1u, abort_flag)) break;
                 asm volatile("tcgen05.fence::after_thread_sync;");
                 uint8_t* sb = smem + (size_t)st * C::STAGE;
-                mma_i8(tmem + buf * NT, umma_desc(sb), umma_desc(sb + C::A_BYTES), umma_idesc<NT>(), 0u);
+#pragma unroll
+                for (uint32_t x = 0; x < C::BPS; ++x)
+                    if (u * C::BPS + x < nb)
+                        mma_i8(tmem + (buf * C::BPS + x) * NT, umma_desc(sb + x * C::A_BYTES),
+                               umma_desc(sb + C::B_OFF + x * C::B_BYTES), umma_idesc<NT>(), 0u);
                 mma_commit(&tfull[buf]);
                 mma_commit(&empty[st]);
                 ++issued;
             }
             if (issued) {     // the last MMA (and with it every earlier one) has completed
-                const uint32_t s = issued - 1u;
-                mbar_wait_ab(&tfull[s % C::NB], (s / C::NB) & 1u, abort_flag);
+                const uint32_t u = issued - 1u;
+                mbar_wait_ab(&tfull[u % C::NB], (u / C::NB) & 1u, abort_flag);
             }
         }
         __syncwarp();
@@ -336,58 +327,69 @@ __global__ void __launch_bounds__(32 * Q8Cfg<NT>::WARPS, 1) mm_q8_tc_kernel(MvAr
         // ---- epilogue: row = row0 + 32 rq + lane, tokens tok0 + 16 cq + i
         const uint32_t rq = warp & 3u, cq = warp >> 2;
         const uint32_t row = row0 + 32u * rq + lane;
-        const uint32_t tl = tmem + ((32u * rq) << 16);
-        const uint32_t lv = tl + C::NB * NT + 16u * cq;
+        const uint32_t tl = tmem + ((32u * rq) << 16) + 16u * cq;
+        float* stk = stack + 16u * cq * kTileM + 32u * rq + lane;
         float acc[16];
 #pragma unroll
         for (uint32_t i = 0; i < 16; ++i) acc[i] = 0.0f;
         uint32_t j = 0, ii = 0, cnt = q + (rem > 0u ? 1u : 0u);
-        for (uint32_t s = 0; s < nb; ++s) {
-            const uint32_t st = s % C::S, buf = s % C::NB;
-            if (!mbar_wait_ab(&tfull[buf], (s / C::NB) & 1u, abort_flag)) { aborted = true; break; }
+        bool aborted = false;
+        for (uint32_t u = 0; u < nst; ++u) {
+            const uint32_t st = u % C::S, buf = u % C::NB;
+            if (!mbar_wait_ab(&tfull[buf], (u / C::NB) & 1u, abort_flag)) { aborted = true; break; }
+            if (!mbar_wait_ab(&full[st], (u / C::S) & 1u, abort_flag)) { aborted = true; break; }
             asm volatile("tcgen05.fence::after_thread_sync;");
-            uint32_t v[16];
-            tmem_ld16(tl + buf * NT + 16u * cq, v);
-            asm volatile("tcgen05.fence::before_thread_sync;");
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&tempty[buf]);
-            if (!mbar_wait_ab(&full[st], (s / C::S) & 1u, abort_flag)) { aborted = true; break; }
             const uint8_t* sb = smem + (size_t)st * C::STAGE;
-            const float4* dx4 = reinterpret_cast<const float4*>(sb + C::DX_OFF + 64u * cq);
-            const float4 x0 = dx4[0], x1 = dx4[1], x2 = dx4[2], x3 = dx4[3];
-            const uint32_t dwp = reinterpret_cast<const uint32_t*>(sb + C::DW_OFF)[32u * rq + lane];
+#pragma unroll
+            for (uint32_t x = 0; x < C::BPS; ++x) {
+                uint32_t v[16];
+                tmem_ld16(tl + (buf * C::BPS + x) * NT, v);
+                if (x + 1u == C::BPS) {                          // the accumulator group is free again
+                    asm volatile("tcgen05.fence::before_thread_sync;");
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&tempty[buf]);
+                }
+                if (u * C::BPS + x < nb) {
+                    const float4* dx4 = reinterpret_cast<const float4*>(sb + C::DX_OFF + x * NT * 4u + 64u * cq);
+                    const uint32_t dwp = reinterpret_cast<const uint32_t*>(sb + C::DW_OFF + x * kTileM * 4u)[32u * rq + lane];
+                    const uint32_t b = j + 16u * ii;
+                    const float dw = h2f((uint16_t)((b & 1u) ? (dwp >> 16) : (dwp & 0xFFFFu)));
+#pragma unroll
+                    for (uint32_t k = 0; k < 4; ++k) {
+                        const float4 f = dx4[k];
+                        const float d4[4] = {f.x, f.y, f.z, f.w};
+#pragma unroll
+                        for (uint32_t e = 0; e < 4; ++e) {
+                            const uint32_t i = 4u * k + e;
+                            acc[i] = __fadd_rn(acc[i], __fmul_rn(__fmul_rn(dw, d4[e]), __int2float_rn((int32_t)v[i])));
+                        }
+                    }
+                    if (++ii == cnt) {                           // partial j is complete
+                        tree_push_smem<false>(stk, C::LSTRIDE, j, acc);
+#pragma unroll
+                        for (uint32_t i = 0; i < 16; ++i) acc[i] = 0.0f;
+                        ++j;
+                        ii = 0;
+                        cnt = q + (j < rem ? 1u : 0u);
+                    }
+                }
+            }
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[st]);
-            const uint32_t b = j + 16u * ii;
-            const float dw = h2f((uint16_t)((b & 1u) ? (dwp >> 16) : (dwp & 0xFFFFu)));
-            const float dx[16] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w, x2.x, x2.y, x2.z, x2.w, x3.x, x3.y, x3.z, x3.w};
-#pragma unroll
-            for (uint32_t i = 0; i < 16; ++i)
-                acc[i] = __fadd_rn(acc[i], __fmul_rn(__fmul_rn(dw, dx[i]), small_i2f((int32_t)v[i])));
-            if (++ii == cnt) {                                   // partial j is complete
-                tree_push_tmem<false, NT>(lv, j, acc);
-#pragma unroll
-                for (uint32_t i = 0; i < 16; ++i) acc[i] = 0.0f;
-                ++j;
-                ii = 0;
-                cnt = q + (j < rem ? 1u : 0u);
-            }
         }
         if (!aborted) {
             for (; j < 16u; ++j) {                               // partials nb .. 15 (fewer than 16 blocks) are +0
                 float z[16];
 #pragma unroll
                 for (uint32_t i = 0; i < 16; ++i) z[i] = 0.0f;
-                tree_push_tmem<false, NT>(lv, j, z);
+                tree_push_smem<false>(stk, C::LSTRIDE, j, z);
             }
-            uint32_t r[16];
-            tmem_ld16(lv, r);
             if (row < a.n_rows) {
 #pragma unroll
                 for (uint32_t i = 0; i < 16; ++i) {
                     const uint32_t tok = tok0 + 16u * cq + i;
                     if (tok < a.T) {
-                        float y = __uint_as_float(r[i]);
+                        float y = stk[i * kTileM];
                         if (a.flags & kMmAdd) y = fadd(daz(a.add[(size_t)tok * a.add_stride + row]), y);
                         if (a.flags & kMmSoftcap) y = fmul(tanh_vu(fmul(y, a.s0), g_expk_t64, g_expk_lk), a.s1);
                         else if (a.flags & kMmScale) y = fmul(y, a.s1);
@@ -397,7 +399,6 @@ __global__ void __launch_bounds__(32 * Q8Cfg<NT>::WARPS, 1) mm_q8_tc_kernel(MvAr
             }
         }
     }
-    (void)aborted;
     asm volatile("tcgen05.fence::before_thread_sync;");
     __syncthreads();
     if (warp == C::E + C::P) {
@@ -437,236 +438,326 @@ cudaError_t launch_nt(const MvArgs& a, cudaStream_t st) {
 // expanded to int8 (0..15) in shared memory, B = the tokens' quantized activation of the same 32
 // values; D = S_j[row][token] exactly. Then isum = sum_j sc_j S_j and msum = sum_j m_j (BS_2j +
 // BS_2j+1) in int32 (exact, as tsr_ref.c:540-567), and the term d Dx isum - dmin Dx msum with the
-// f32 rules (the A256 scale Dx is an arbitrary f32, so the flush tests stay).
+// f32 rules. The A256 scale Dx is an arbitrary f32: when every Dx of the CTA's tokens is 0 or at
+// least 2^-79 in magnitude, every product and sum is a multiple of 2^-126 and the flush tests are
+// skipped (SAFE); otherwise they run.
+//
+// Warp roles: E epilogue warps (32 rows x 16 tokens each), P producer warps (cp.async of the raw
+// quants, with the 16-byte chunks of a row rotated by the row so that the expanders read without
+// bank conflicts, the B tiles, Dx, the pair sums BS_2j + BS_2j+1 and the 16-byte row metadata into
+// a ring of S stages), X expander warps (one row per thread: nibbles -> two int8 A tiles, into one
+// of NA expanded slots), one MMA warp. mbarriers: full/empty[S], afull/aempty[NA], tfull/tempty[NB].
+constexpr uint32_t kSafeDxQ4 = 0x18000000u;            // 2^-79
+
 template <uint32_t NT>
-__global__ void __launch_bounds__(128 * (NT / 16), 1) mm_q4k_tc_kernel(MvArgs a) {
-    constexpr uint32_t WARPS = 4 * (NT / 16), THREADS = 32 * WARPS;
-    constexpr uint32_t RING = 4;
-    constexpr uint32_t RAW = kTileM * 128u;            // the superblock's quants of 128 rows (16 KB)
-    constexpr uint32_t ATILE = kTileM * 32u;           // one sub-block's expanded A tile
-    constexpr uint32_t BTILE = NT * 32u;
-    constexpr uint32_t TCOLS = 16 * NT <= 256 ? 256 : 512;   // two superblocks x 8 tiles
-    extern __shared__ __align__(128) uint8_t smem[];
-    uint8_t* Raw = smem;                                                   // [RING][RAW]
-    uint8_t* Ax = Raw + RING * RAW;                                        // [2][8][ATILE]
-    uint8_t* Bs = Ax + 2u * 8u * ATILE;                                    // [RING][8][BTILE]
-    float* DX = reinterpret_cast<float*>(Bs + RING * 8u * BTILE);          // [RING][NT]
-    int32_t* BSS = reinterpret_cast<int32_t*>(DX + RING * NT);             // [RING][NT][8]
-    uint64_t* bars = reinterpret_cast<uint64_t*>(BSS + RING * NT * 8u);    // [2]
-    uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 2);
+struct Q4Cfg {
+    static constexpr uint32_t E = 4u * (NT / 16u), P = 2u, X = 4u;
+    static constexpr uint32_t WARPS = E + P + X + 1u, MMA_WARP = E + P + X;
+    static constexpr uint32_t S = 3u, LAG = 2u, NB = 2u, NA = 2u;
+    static constexpr uint32_t RAW = kTileM * 128u, BT = NT * 32u, ATILE = kTileM * 32u;
+    static constexpr uint32_t B_OFF = RAW, DX_OFF = B_OFF + 8u * BT, BS_OFF = DX_OFF + NT * 4u;
+    static constexpr uint32_t META_OFF = BS_OFF + NT * 16u, STAGE = META_OFF + kTileM * 16u;
+    static constexpr size_t AX_OFF = (size_t)S * STAGE, ASLOT = 8u * ATILE;
+    static constexpr size_t STACK_OFF = AX_OFF + NA * ASLOT;
+    static constexpr uint32_t LSTRIDE = NT * kTileM;
+    static constexpr size_t BAR_OFF = STACK_OFF + 4u * LSTRIDE * 4u;
+    static constexpr size_t SMEM = BAR_OFF + (2u * S + 2u * NA + 2u * NB) * 8u + 16u;
+    static constexpr uint32_t TCOLS = NB * 8u * NT;
+    static_assert(TCOLS == 256u || TCOLS == 512u, "TMEM allocation is a power of two");
+    static_assert(SMEM <= 227u * 1024u, "shared memory");
+};
 
-    const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31u;
-    const uint32_t row0 = blockIdx.x * kTileM, tok0 = blockIdx.y * NT;
-    const uint32_t K = a.K, nsb = K / 256u;
-    const Layout L{1u, K};
-    const Seq seq{nsb, nsb / 16u, nsb % 16u};
-
-    if (warp == 0) {
-        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tslot)), "r"(TCOLS));
-        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
-    }
-    if (tid == 0) {
-        asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(&bars[0])));
-        asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(&bars[1])));
-        asm volatile("fence.mbarrier_init.release.cluster;");
-    }
-    asm volatile("griddepcontrol.wait;" ::: "memory");
-    __syncthreads();
-    asm volatile("tcgen05.fence::after_thread_sync;");
-    const uint32_t tmem = *tslot;
-
-    auto fill = [&](uint32_t s) {
-        if (s < nsb) {
-            uint32_t j;
-            bool last;
-            const uint32_t sb = seq.block(s, &j, &last), st = s % RING;
-            for (uint32_t c = tid; c < kTileM * 8u; c += THREADS) {          // 8 chunks of 16 B per row
-                const uint32_t r = c >> 3, k = c & 7u, row = row0 + r;
-                if (row < a.n_rows) cp_async16(Raw + st * RAW + r * 128u + k * 16u, a.qs + L.qs_off(row, sb, k));
-            }
-            for (uint32_t c = tid; c < 8u * NT * 2u; c += THREADS) {         // 8 sub-blocks x NT tokens x 2 halves
-                const uint32_t jj = c / (2u * NT), rem = c - jj * 2u * NT, t = rem >> 1, h = rem & 1u, tok = tok0 + t;
-                if (tok < a.T)
-                    cp_async16(Bs + (st * 8u + jj) * BTILE + (t >> 3) * 256u + h * 128u + (t & 7u) * 16u,
-                               a.qx + (size_t)tok * K + 256u * sb + 32u * jj + 16u * h);
-            }
-            for (uint32_t t = tid; t < NT; t += THREADS) {
-                const uint32_t tok = tok0 + t;
-                DX[st * NT + t] = tok < a.T ? a.dx[(size_t)tok * nsb + sb] : 0.0f;
-#pragma unroll
-                for (uint32_t jj = 0; jj < 8; ++jj) {
-                    int32_t v = 0;
-                    if (tok < a.T) {
-                        const int16_t* b16 = a.bsx + (size_t)tok * (K / 16u) + 16u * sb + 2u * jj;
-                        v = (int32_t)b16[0] + (int32_t)b16[1];
-                    }
-                    BSS[(st * NT + t) * 8u + jj] = v;
-                }
-            }
-        }
-        cp_async_commit();
-    };
-    // the raw quants of superblock s -> the eight expanded A tiles (low nibbles: sub-block 2c, high: 2c + 1)
-    auto expand = [&](uint32_t s) {
-        const uint32_t st = s % RING;
-        uint8_t* A = Ax + (s & 1u) * 8u * ATILE;
-        for (uint32_t c = tid; c < kTileM * 8u; c += THREADS) {
-            const uint32_t r = c >> 3, k = c & 7u, cc = k >> 1, h = k & 1u;
-            const uint4 w = *reinterpret_cast<const uint4*>(Raw + st * RAW + r * 128u + k * 16u);
-            const uint4 lo = make_uint4(w.x & 0x0F0F0F0Fu, w.y & 0x0F0F0F0Fu, w.z & 0x0F0F0F0Fu, w.w & 0x0F0F0F0Fu);
-            const uint4 hi = make_uint4((w.x >> 4) & 0x0F0F0F0Fu, (w.y >> 4) & 0x0F0F0F0Fu, (w.z >> 4) & 0x0F0F0F0Fu,
-                                        (w.w >> 4) & 0x0F0F0F0Fu);
-            const uint32_t off = (r >> 3) * 256u + h * 128u + (r & 7u) * 16u;
-            *reinterpret_cast<uint4*>(A + (2u * cc) * ATILE + off) = lo;
-            *reinterpret_cast<uint4*>(A + (2u * cc + 1u) * ATILE + off) = hi;
-        }
-    };
-
+template <uint32_t NT, bool SAFE>
+__device__ __forceinline__ void q4k_epilogue(const MvArgs& a, uint8_t* smem, uint64_t* full, uint64_t* empty,
+                                             uint64_t* tfull, uint64_t* tempty, volatile uint32_t* abort_flag, uint32_t tmem,
+                                             uint32_t warp, uint32_t lane) {
+    using C = Q4Cfg<NT>;
+    const uint32_t nsb = a.K / 256u, q = nsb >> 4, rem = nsb & 15u;
     const uint32_t rq = warp & 3u, cq = warp >> 2;
-    const uint32_t row = row0 + 32u * rq + lane;
-    const uint8_t* meta = static_cast<const uint8_t*>(a.meta);
-    float acc[16], L0[16], L1[16], L2[16], L3[16];
+    const uint32_t row = blockIdx.x * kTileM + 32u * rq + lane, tok0 = blockIdx.y * NT;
+    const uint32_t tl = tmem + ((32u * rq) << 16) + 16u * cq;
+    float* stk = reinterpret_cast<float*>(smem + C::STACK_OFF) + 16u * cq * kTileM + 32u * rq + lane;
+    float acc[16];
 #pragma unroll
-    for (uint32_t i = 0; i < 16; ++i) acc[i] = L0[i] = L1[i] = L2[i] = L3[i] = 0.0f;
-
-    for (uint32_t s = 0; s + 2u < RING; ++s) fill(s);
-    uint32_t phase[2] = {0u, 0u};
-    uint32_t jcur = 0;
-    uint4 m_next = make_uint4(0, 0, 0, 0);
-    if (nsb) {
-        uint32_t j0;
-        bool l0;
-        const uint32_t sb0 = seq.block(0, &j0, &l0);
-        if (row < a.n_rows) m_next = *reinterpret_cast<const uint4*>(meta + L.meta_off(row, sb0));
-    }
-    bool failed = false;
-    for (uint32_t s = 0; s <= nsb; ++s) {
-        if (s < nsb) {
-            cp_async_wait<RING - 3>();
-            __syncthreads();
-            expand(s);
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    for (uint32_t i = 0; i < 16; ++i) acc[i] = 0.0f;
+    uint32_t j = 0, ii = 0, cnt = q + (rem > 0u ? 1u : 0u);
+    bool aborted = false;
+    for (uint32_t u = 0; u < nsb; ++u) {
+        const uint32_t st = u % C::S, buf = u % C::NB;
+        if (!mbar_wait_ab(&tfull[buf], (u / C::NB) & 1u, abort_flag)) { aborted = true; break; }
+        if (!mbar_wait_ab(&full[st], (u / C::S) & 1u, abort_flag)) { aborted = true; break; }
+        asm volatile("tcgen05.fence::after_thread_sync;");
+        const uint8_t* sb = smem + (size_t)st * C::STAGE;
+        const uint4 m = reinterpret_cast<const uint4*>(sb + C::META_OFF)[32u * rq + lane];
+        const uint32_t sc_lo = m.y & 0x3F3F3F3Fu, mn_lo = m.z & 0x3F3F3F3Fu;
+        const uint32_t sc_hi = (m.w & 0x0F0F0F0Fu) | ((m.y >> 2) & 0x30303030u);
+        const uint32_t mn_hi = ((m.w >> 4) & 0x0F0F0F0Fu) | ((m.z >> 2) & 0x30303030u);
+        int32_t isum[16];
+#pragma unroll
+        for (uint32_t i = 0; i < 16; ++i) isum[i] = 0;
+#pragma unroll
+        for (uint32_t jj = 0; jj < 8u; ++jj) {
+            uint32_t v[16];
+            tmem_ld16(tl + (buf * 8u + jj) * NT, v);
+            const int32_t sc = (int32_t)__byte_perm(jj < 4u ? sc_lo : sc_hi, 0u, 0x4440u | (jj & 3u));
+#pragma unroll
+            for (uint32_t i = 0; i < 16; ++i) isum[i] += sc * (int32_t)v[i];
         }
         asm volatile("tcgen05.fence::before_thread_sync;");
-        __syncthreads();
-        asm volatile("tcgen05.fence::after_thread_sync;");
-        fill(s + RING - 2u);
-        if (s < nsb && tid == 0) {
-            const uint32_t st = s % RING;
-#pragma unroll 1
-            for (uint32_t jj = 0; jj < 8u; ++jj) {
-                const uint64_t da = umma_desc(Ax + ((s & 1u) * 8u + jj) * ATILE);
-                const uint64_t db = umma_desc(Bs + (st * 8u + jj) * BTILE);
-                const uint32_t d = tmem + (s & 1u) * 8u * NT + jj * NT;
-                asm volatile(
-                    "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-                    "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}"
-                    ::"r"(d), "l"(da), "l"(db), "r"(umma_idesc<NT>()), "r"(0u));
-            }
-            asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
-                         ::"r"(smem_u32(&bars[s & 1u])) : "memory");
-        }
-        if (s >= 1u) {
-            const uint32_t sp = s - 1u, buf = sp & 1u, st = sp % RING;
-            if (!mbar_wait(smem_u32(&bars[buf]), phase[buf])) failed = true;
-            phase[buf] ^= 1u;
-            asm volatile("tcgen05.fence::after_thread_sync;");
-            const uint4 m = m_next;
-            if (sp + 1u < nsb) {
-                uint32_t jn;
-                bool ln;
-                const uint32_t sbn = seq.block(sp + 1u, &jn, &ln);
-                if (row < a.n_rows) m_next = *reinterpret_cast<const uint4*>(meta + L.meta_off(row, sbn));
-            }
-            const uint32_t sc_lo = m.y & 0x3F3F3F3Fu, mn_lo = m.z & 0x3F3F3F3Fu;
-            const uint32_t sc_hi = (m.w & 0x0F0F0F0Fu) | ((m.y >> 2) & 0x30303030u);
-            const uint32_t mn_hi = ((m.w >> 4) & 0x0F0F0F0Fu) | ((m.z >> 2) & 0x30303030u);
-            int32_t isum[16];
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty[buf]);
+        const float dw = h2f((uint16_t)(m.x & 0xFFFFu)), dmw = h2f((uint16_t)(m.x >> 16));
+        const float4* dx4 = reinterpret_cast<const float4*>(sb + C::DX_OFF + 64u * cq);
+        const uint4* bs4 = reinterpret_cast<const uint4*>(sb + C::BS_OFF) + 16u * cq;
 #pragma unroll
-            for (uint32_t i = 0; i < 16; ++i) isum[i] = 0;
+        for (uint32_t k = 0; k < 4; ++k) {
+            const float4 f = dx4[k];
+            const float d4[4] = {f.x, f.y, f.z, f.w};
 #pragma unroll
-            for (uint32_t jj = 0; jj < 8u; ++jj) {
-                uint32_t v[16];
-                asm volatile(
-                    "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-                    : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
-                      "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
-                    : "r"(tmem + ((32u * rq) << 16) + buf * 8u * NT + jj * NT + 16u * cq));
-                asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-                const int32_t sc = (int32_t)__byte_perm(jj < 4u ? sc_lo : sc_hi, 0u, 0x4440u | (jj & 3u));
-#pragma unroll
-                for (uint32_t i = 0; i < 16; ++i) isum[i] += sc * (int32_t)v[i];
-            }
-            uint32_t j;
-            bool last;
-            seq.block(sp, &j, &last);
-            const float dw = h2f((uint16_t)(m.x & 0xFFFFu)), dmw = h2f((uint16_t)(m.x >> 16));
-#pragma unroll
-            for (uint32_t i = 0; i < 16; ++i) {
-                const int32_t* bsv = BSS + (st * NT + 16u * cq + i) * 8u;
-                int32_t msum = 0;
-#pragma unroll
-                for (uint32_t jj = 0; jj < 8u; ++jj)
-                    msum += (int32_t)__byte_perm(jj < 4u ? mn_lo : mn_hi, 0u, 0x4440u | (jj & 3u)) * bsv[jj];
-                const float Dx = DX[st * NT + 16u * cq + i];
-                const float t1 = fmul(fmul(dw, Dx), i2f(isum[i]));
-                const float t2 = fmul(fmul(dmw, Dx), i2f(msum));
-                acc[i] = fadd(acc[i], fsub(t1, t2));
-            }
-            if (last) {
-#pragma unroll
-                for (uint32_t i = 0; i < 16; ++i) {
-                    tree_push(L0[i], L1[i], L2[i], L3[i], j, acc[i]);
-                    acc[i] = 0.0f;
+            for (uint32_t e = 0; e < 4; ++e) {
+                const uint32_t i = 4u * k + e;
+                const uint4 B = bs4[i];
+                const int32_t msum = dp2a_hi(B.w, mn_hi, dp2a_lo(B.z, mn_hi, dp2a_hi(B.y, mn_lo, dp2a_lo(B.x, mn_lo, 0))));
+                const float Dx = d4[e];
+                if (SAFE) {
+                    const float t1 = __fmul_rn(__fmul_rn(dw, Dx), __int2float_rn(isum[i]));
+                    const float t2 = __fmul_rn(__fmul_rn(dmw, Dx), __int2float_rn(msum));
+                    acc[i] = __fadd_rn(acc[i], __fsub_rn(t1, t2));
+                } else {
+                    const float t1 = fmul(fmul(dw, Dx), i2f(isum[i]));
+                    const float t2 = fmul(fmul(dmw, Dx), i2f(msum));
+                    acc[i] = fadd(acc[i], fsub(t1, t2));
                 }
-                jcur = j + 1u;
             }
         }
-    }
-    for (uint32_t j = jcur; j < 16u; ++j) {
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[st]);
+        if (++ii == cnt) {                                       // partial j is complete
+            tree_push_smem<!SAFE>(stk, C::LSTRIDE, j, acc);
 #pragma unroll
-        for (uint32_t i = 0; i < 16; ++i) tree_push(L0[i], L1[i], L2[i], L3[i], j, 0.0f);
+            for (uint32_t i = 0; i < 16; ++i) acc[i] = 0.0f;
+            ++j;
+            ii = 0;
+            cnt = q + (j < rem ? 1u : 0u);
+        }
     }
-    if (failed && lane == 0) atomicCAS(&g_tc_error, 0u, 3u);
+    if (aborted) return;
+    for (; j < 16u; ++j) {                                       // partials nsb .. 15 are +0
+        float z[16];
+#pragma unroll
+        for (uint32_t i = 0; i < 16; ++i) z[i] = 0.0f;
+        tree_push_smem<!SAFE>(stk, C::LSTRIDE, j, z);
+    }
     if (row < a.n_rows) {
 #pragma unroll
         for (uint32_t i = 0; i < 16; ++i) {
             const uint32_t tok = tok0 + 16u * cq + i;
             if (tok < a.T) {
-                float v = L0[i];
-                if (a.flags & kMmAdd) v = fadd(daz(a.add[(size_t)tok * a.add_stride + row]), v);
-                if (a.flags & kMmSoftcap) v = fmul(tanh_vu(fmul(v, a.s0), g_expk_t64, g_expk_lk), a.s1);
-                else if (a.flags & kMmScale) v = fmul(v, a.s1);
-                a.y[(size_t)tok * a.y_stride + row] = canon(v);
+                float y = stk[i * kTileM];
+                if (a.flags & kMmAdd) y = fadd(daz(a.add[(size_t)tok * a.add_stride + row]), y);
+                if (a.flags & kMmSoftcap) y = fmul(tanh_vu(fmul(y, a.s0), g_expk_t64, g_expk_lk), a.s1);
+                else if (a.flags & kMmScale) y = fmul(y, a.s1);
+                a.y[(size_t)tok * a.y_stride + row] = canon(y);
             }
         }
     }
-    asm volatile("tcgen05.fence::before_thread_sync;");
-    __syncthreads();
-    if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TCOLS));
 }
 
 template <uint32_t NT>
-size_t q4k_smem() {
-    return 4u * kTileM * 128u + 2u * 8u * kTileM * 32u + 4u * 8u * NT * 32u + 4u * NT * 4u + 4u * NT * 8u * 4u + 2u * 8u + 16u;
+__global__ void __launch_bounds__(32 * Q4Cfg<NT>::WARPS, 1) mm_q4k_tc_kernel(MvArgs a) {
+    using C = Q4Cfg<NT>;
+    extern __shared__ __align__(128) uint8_t smem[];
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::BAR_OFF);
+    uint64_t* empty = full + C::S;
+    uint64_t* afull = empty + C::S;
+    uint64_t* aempty = afull + C::NA;
+    uint64_t* tfull = aempty + C::NA;
+    uint64_t* tempty = tfull + C::NB;
+    uint32_t* tslot = reinterpret_cast<uint32_t*>(tempty + C::NB);
+    volatile uint32_t* abort_flag = tslot + 1;
+
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+    const uint32_t row0 = blockIdx.x * kTileM, tok0 = blockIdx.y * NT;
+    const uint32_t K = a.K, nsb = K / 256u, q = nsb >> 4, rem = nsb & 15u;
+    const Layout L{1u, K};
+
+    if (warp == C::MMA_WARP) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tslot)), "r"(C::TCOLS));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    if (threadIdx.x == 0) {
+        for (uint32_t i = 0; i < C::S; ++i) {
+            mbar_init(&full[i], C::P);
+            mbar_init(&empty[i], 1u + C::X + C::E);
+        }
+        for (uint32_t i = 0; i < C::NA; ++i) {
+            mbar_init(&afull[i], C::X);
+            mbar_init(&aempty[i], 1u);
+        }
+        for (uint32_t i = 0; i < C::NB; ++i) {
+            mbar_init(&tfull[i], 1u);
+            mbar_init(&tempty[i], C::E);
+        }
+        *abort_flag = 0u;
+        asm volatile("fence.mbarrier_init.release.cluster;");
+    }
+    asm volatile("griddepcontrol.wait;" ::: "memory");     // the QA image comes from the previous kernels
+    // SAFE: every activation scale of this CTA's tokens is 0 or at least 2^-79 in magnitude
+    bool ok = true;
+    for (uint32_t i = threadIdx.x; i < NT * nsb; i += 32u * C::WARPS) {
+        const uint32_t t = i / nsb, tok = tok0 + t;
+        if (tok < a.T) {
+            const uint32_t u = __float_as_uint(a.dx[(size_t)tok * nsb + (i - t * nsb)]) & 0x7FFFFFFFu;
+            ok = ok && (u == 0u || u >= kSafeDxQ4);
+        }
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;");
+    const bool safe = __syncthreads_and(ok) != 0;
+    asm volatile("tcgen05.fence::after_thread_sync;");
+    const uint32_t tmem = *tslot;
+
+    if (warp >= C::E && warp < C::E + C::P) {
+        // ---- producers
+        constexpr uint32_t LN = 32u * C::P;
+        const uint32_t pl = (warp - C::E) * 32u + lane, kk = pl & 7u;
+        const size_t qrow = L.qs_row_bytes(), mrow = L.meta_row_bytes();
+        uint32_t issued = 0;
+        for (uint32_t u = 0; u < nsb; ++u) {
+            const uint32_t st = u % C::S;
+            if (u >= C::S && !mbar_wait_ab(&empty[st], ((u / C::S) - 1u) & 1u, abort_flag)) break;
+            uint32_t jb;
+            bool lb;
+            const uint32_t sbk = Seq{nsb, q, rem}.block(u, &jb, &lb);
+            uint8_t* sb = smem + (size_t)st * C::STAGE;
+            const size_t qoff = L.qs_off(0u, sbk, kk);
+#pragma unroll 4
+            for (uint32_t k = 0; k < 1024u / LN; ++k) {          // raw quants: row (pl / 8) + 8 k, chunk pl & 7
+                const uint32_t r = (pl >> 3) + (LN / 8u) * k;
+                cp_async16(sb + r * 128u + ((kk ^ (r & 7u)) * 16u), a.qs + (size_t)min(row0 + r, a.n_rows - 1u) * qrow + qoff);
+            }
+#pragma unroll
+            for (uint32_t k = 0; k < 16u * NT / LN; ++k) {       // B tiles: (sub-block, token, half)
+                const uint32_t idx = pl + LN * k, h = idx & 1u, t = (idx >> 1) % NT, jj = (idx >> 1) / NT;
+                cp_async16(sb + C::B_OFF + jj * C::BT + (t >> 3) * 256u + h * 128u + (t & 7u) * 16u,
+                           a.qx + (size_t)min(tok0 + t, a.T - 1u) * K + 256u * sbk + 32u * jj + 16u * h);
+            }
+            if (pl < NT) {
+                const uint32_t tok = min(tok0 + pl, a.T - 1u);
+                cp_async4(sb + C::DX_OFF + 4u * pl, a.dx + (size_t)tok * nsb + sbk);
+                cp_async16(sb + C::BS_OFF + 16u * pl, a.bs2x + (size_t)tok * (K / 32u) + 8u * sbk);
+            }
+#pragma unroll
+            for (uint32_t k = 0; k < kTileM / LN; ++k) {
+                const uint32_t r = pl + LN * k;
+                cp_async16(sb + C::META_OFF + 16u * r,
+                           static_cast<const uint8_t*>(a.meta) + (size_t)min(row0 + r, a.n_rows - 1u) * mrow + 16u * sbk);
+            }
+            cp_async_commit();
+            ++issued;
+            if (u >= C::LAG) {
+                cp_async_wait<C::LAG>();
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&full[(u - C::LAG) % C::S]);
+            }
+        }
+        cp_async_wait<0>();
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        __syncwarp();
+        if (lane == 0)
+            for (uint32_t u = issued > C::LAG ? issued - C::LAG : 0u; u < issued; ++u) mbar_arrive(&full[u % C::S]);
+    } else if (warp >= C::E + C::P && warp < C::MMA_WARP) {
+        // ---- expanders: thread r owns row r of the tile
+        const uint32_t r = (warp - C::E - C::P) * 32u + lane;
+        const uint32_t off = (r >> 3) * 256u + (r & 7u) * 16u;
+        for (uint32_t u = 0; u < nsb; ++u) {
+            const uint32_t st = u % C::S, slot = u % C::NA;
+            if (!mbar_wait_ab(&full[st], (u / C::S) & 1u, abort_flag)) break;
+            if (u >= C::NA && !mbar_wait_ab(&aempty[slot], ((u / C::NA) - 1u) & 1u, abort_flag)) break;
+            const uint8_t* raw = smem + (size_t)st * C::STAGE + r * 128u;
+            uint8_t* ax = smem + C::AX_OFF + slot * C::ASLOT + off;
+#pragma unroll
+            for (uint32_t k = 0; k < 8u; ++k) {                  // chunk k: low nibbles -> sub-block 2 (k / 2), high -> +1
+                const uint4 w = *reinterpret_cast<const uint4*>(raw + ((k ^ (r & 7u)) * 16u));
+                const uint4 lo = make_uint4(w.x & 0x0F0F0F0Fu, w.y & 0x0F0F0F0Fu, w.z & 0x0F0F0F0Fu, w.w & 0x0F0F0F0Fu);
+                const uint4 hi = make_uint4((w.x >> 4) & 0x0F0F0F0Fu, (w.y >> 4) & 0x0F0F0F0Fu, (w.z >> 4) & 0x0F0F0F0Fu,
+                                            (w.w >> 4) & 0x0F0F0F0Fu);
+                const uint32_t c = k >> 1, h = k & 1u;
+                *reinterpret_cast<uint4*>(ax + (2u * c) * C::ATILE + h * 128u) = lo;
+                *reinterpret_cast<uint4*>(ax + (2u * c + 1u) * C::ATILE + h * 128u) = hi;
+            }
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(&afull[slot]);
+                mbar_arrive(&empty[st]);
+            }
+        }
+    } else if (warp == C::MMA_WARP) {
+        if (lane == 0) {
+            uint32_t issued = 0;
+            for (uint32_t u = 0; u < nsb; ++u) {
+                const uint32_t st = u % C::S, slot = u % C::NA, buf = u % C::NB;
+                if (!mbar_wait_ab(&full[st], (u / C::S) & 1u, abort_flag)) break;
+                if (!mbar_wait_ab(&afull[slot], (u / C::NA) & 1u, abort_flag)) break;
+                if (u >= C::NB && !mbar_wait_ab(&tempty[buf], ((u / C::NB) - 1u) & 1u, abort_flag)) break;
+                asm volatile("tcgen05.fence::after_thread_sync;");
+                uint8_t* sb = smem + (size_t)st * C::STAGE;
+                uint8_t* ax = smem + C::AX_OFF + slot * C::ASLOT;
+#pragma unroll
+                for (uint32_t jj = 0; jj < 8u; ++jj)
+                    mma_i8(tmem + (buf * 8u + jj) * NT, umma_desc(ax + jj * C::ATILE), umma_desc(sb + C::B_OFF + jj * C::BT),
+                           umma_idesc<NT>(), 0u);
+                mma_commit(&tfull[buf]);
+                mma_commit(&aempty[slot]);
+                mma_commit(&empty[st]);
+                ++issued;
+            }
+            if (issued) {
+                const uint32_t u = issued - 1u;
+                mbar_wait_ab(&tfull[u % C::NB], (u / C::NB) & 1u, abort_flag);
+            }
+        }
+        __syncwarp();
+    } else if (safe) {
+        q4k_epilogue<NT, true>(a, smem, full, empty, tfull, tempty, abort_flag, tmem, warp, lane);
+    } else {
+        q4k_epilogue<NT, false>(a, smem, full, empty, tfull, tempty, abort_flag, tmem, warp, lane);
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;");
+    __syncthreads();
+    if (warp == C::MMA_WARP) {
+        asm volatile("tcgen05.fence::after_thread_sync;");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(C::TCOLS));
+    }
+}
+
+// BS_2j + BS_2j+1 of every token (the Q4_K min sums' activation side), int16 exact (|sum| <= 4064)
+__global__ void bs_pairs_kernel(const int16_t* __restrict__ bs, int16_t* __restrict__ bs2, uint32_t n) {
+    const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) bs2[i] = (int16_t)((int32_t)bs[2u * i] + (int32_t)bs[2u * i + 1u]);
 }
 
 template <uint32_t NT>
 cudaError_t launch_q4k_nt(const MvArgs& a, cudaStream_t st) {
+    using C = Q4Cfg<NT>;
     static int done_dev[64];
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
-    const size_t smem = q4k_smem<NT>();
     if (dev < 64 && done_dev[dev] != dev + 1) {
-        e = cudaFuncSetAttribute(mm_q4k_tc_kernel<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        e = cudaFuncSetAttribute(mm_q4k_tc_kernel<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM);
         if (e != cudaSuccess) return e;
         done_dev[dev] = dev + 1;
     }
+    const uint32_t n = a.T * (a.K / 32u);
+    bs_pairs_kernel<<<(n + 255u) / 256u, 256, 0, st>>>(a.bsx, const_cast<int16_t*>(a.bs2x), n);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((a.n_rows + kTileM - 1u) / kTileM, (a.T + NT - 1u) / NT);
-    cfg.blockDim = dim3(128u * (NT / 16u));
-    cfg.dynamicSmemBytes = smem;
+    cfg.blockDim = dim3(32u * C::WARPS);
+    cfg.dynamicSmemBytes = C::SMEM;
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;

@@ -53,6 +53,18 @@ __device__ __forceinline__ float i2f(int32_t v) { return __int2float_rn(v); }
 __device__ __forceinline__ float h2f(uint16_t h) { return __half2float(__ushort_as_half(h)); }
 __device__ __forceinline__ uint16_t f2h(float f) { return __half_as_ushort(__float2half_rn(f)); }
 
+// two signed 16-bit values of a times unsigned bytes 0,1 (lo) or 2,3 (hi) of b, plus c
+__device__ __forceinline__ int32_t dp2a_lo(uint32_t a, uint32_t b, int32_t c) {
+    int32_t d;
+    asm("dp2a.lo.s32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+__device__ __forceinline__ int32_t dp2a_hi(uint32_t a, uint32_t b, int32_t c) {
+    int32_t d;
+    asm("dp2a.hi.s32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+
 // QACT's f32 -> int8 conversion (sw/sim/tsr_ref.c:202-229): NaN -> 0, the rounded value
 // saturated to [-128, 127]; half_even: ties to even (A256), else ties away from zero (A32).
 __device__ __forceinline__ int32_t round_sat8(float v, bool half_even) {
