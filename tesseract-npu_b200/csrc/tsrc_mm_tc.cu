@@ -80,6 +80,10 @@ constexpr long long kWaitCycles = 1ll << 31;       // a wait gives up after ~1 s
 __device__ __forceinline__ void cp_async4(void* dst, const void* src) {
     asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
 }
+// arrive on b once every cp.async this thread has issued so far has landed (counted in the init count)
+__device__ __forceinline__ void cp_async_arrive(uint64_t* b) {
+    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(b)) : "memory");
+}
 __device__ __forceinline__ void mbar_init(uint64_t* b, uint32_t count) {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(b)), "r"(count));
 }
@@ -124,8 +128,9 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
         : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
           "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
         : "r"(taddr));
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
+// waits for every tcgen05.ld of the thread: their registers are valid after it, not before
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 // Folds partial j (16 values, one per token of the thread) into the 16-partial tree whose four
 // stack levels live in shared memory (level l of token i at s[l * lstride + i * kTileM]); after
 // partial 15 the tree's value is level 0. FLUSH: the reference's flush test on every sum.
@@ -149,8 +154,8 @@ __device__ __forceinline__ void tree_push_smem(float* s, uint32_t lstride, uint3
 // ---- Q8_0 ---------------------------------------------------------------------------------------
 // Warp roles: E epilogue warps (warp w: TMEM lanes 32 (w mod 4) .., tokens 16 (w / 4) ..), P producer
 // warps (cp.async of the operand tiles, activation scales and weight scales of BPS consecutive
-// blocks of the sequence into one of S ring stages; a stage is published when the producer's
-// copies of it have landed), one MMA warp (TMEM allocation; one thread issues the stage's MMAs into
+// blocks of the sequence into one of S ring stages; each copying thread arrives on the stage's
+// full barrier when its copies have landed, cp.async.mbarrier.arrive), one MMA warp (TMEM allocation; one thread issues the stage's MMAs into
 // one of NB accumulator groups of BPS tiles, all of TMEM). The partial trees' stacks live in shared
 // memory. Grouping blocks per stage divides the barrier work per output element by BPS.
 // mbarriers: full[S] (producers -> MMA, epilogue), empty[S] (MMA commit + epilogue warps ->
@@ -165,9 +170,6 @@ __device__ __forceinline__ void tree_push_smem(float* s, uint32_t lstride, uint3
 #ifndef TSRC_Q8TC_S
 #define TSRC_Q8TC_S 6u
 #endif
-#ifndef TSRC_Q8TC_LAG
-#define TSRC_Q8TC_LAG 2u
-#endif
 #ifndef TSRC_Q8TC_NB
 #define TSRC_Q8TC_NB 4u
 #endif
@@ -178,7 +180,6 @@ struct Q8Cfg {
     static constexpr uint32_t WARPS = E + P + 1u;
     static constexpr uint32_t BPS = TSRC_Q8TC_BPS;     // blocks per stage
     static constexpr uint32_t S = TSRC_Q8TC_S;
-    static constexpr uint32_t LAG = TSRC_Q8TC_LAG;     // producer: stages in flight before publishing
     static constexpr uint32_t NB = TSRC_Q8TC_NB;
     static constexpr uint32_t A_BYTES = kTileM * 32u, B_BYTES = NT * 32u;
     static constexpr uint32_t B_OFF = BPS * A_BYTES;
@@ -217,7 +218,7 @@ __global__ void __launch_bounds__(32 * Q8Cfg<NT>::WARPS, 1) mm_q8_tc_kernel(MvAr
     }
     if (threadIdx.x == 0) {
         for (uint32_t i = 0; i < C::S; ++i) {
-            mbar_init(&full[i], C::P);
+            mbar_init(&full[i], 32u * C::P);
             mbar_init(&empty[i], 1u + C::E);
         }
         for (uint32_t i = 0; i < C::NB; ++i) {
@@ -258,7 +259,7 @@ __global__ void __launch_bounds__(32 * Q8Cfg<NT>::WARPS, 1) mm_q8_tc_kernel(MvAr
 #pragma unroll
         for (uint32_t k = 0; k < WR; ++k)
             wrow[k] = static_cast<const uint8_t*>(a.meta) + (size_t)min(row0 + pl + LN * k, a.n_rows - 1u) * L.meta_row_bytes();
-        uint32_t j = 0, ii = 0, cnt = q + (rem > 0u ? 1u : 0u), issued = 0;
+        uint32_t j = 0, ii = 0, cnt = q + (rem > 0u ? 1u : 0u);
         for (uint32_t u = 0; u < nst; ++u) {
             const uint32_t st = u % C::S;
             if (u >= C::S && !mbar_wait_ab(&empty[st], ((u / C::S) - 1u) & 1u, abort_flag)) break;
@@ -284,20 +285,9 @@ __global__ void __launch_bounds__(32 * Q8Cfg<NT>::WARPS, 1) mm_q8_tc_kernel(MvAr
                     }
                 }
             }
-            cp_async_commit();
-            ++issued;
-            if (u >= C::LAG) {
-                cp_async_wait<C::LAG>();
-                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&full[(u - C::LAG) % C::S]);
-            }
+            cp_async_arrive(&full[st]);                          // the stage is published when its copies land
         }
         cp_async_wait<0>();
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        __syncwarp();
-        if (lane == 0)
-            for (uint32_t u = issued > C::LAG ? issued - C::LAG : 0u; u < issued; ++u) mbar_arrive(&full[u % C::S]);
     } else if (warp == C::E + C::P) {
         // ---- MMA issuer
         if (lane == 0) {
@@ -340,15 +330,15 @@ __global__ void __launch_bounds__(32 * Q8Cfg<NT>::WARPS, 1) mm_q8_tc_kernel(MvAr
             if (!mbar_wait_ab(&full[st], (u / C::S) & 1u, abort_flag)) { aborted = true; break; }
             asm volatile("tcgen05.fence::after_thread_sync;");
             const uint8_t* sb = smem + (size_t)st * C::STAGE;
+            uint32_t v[C::BPS][16];
+#pragma unroll
+            for (uint32_t x = 0; x < C::BPS; ++x) tmem_ld16(tl + (buf * C::BPS + x) * NT, v[x]);
+            tmem_wait_ld();
+            asm volatile("tcgen05.fence::before_thread_sync;");
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tempty[buf]);          // the accumulator group is free again
 #pragma unroll
             for (uint32_t x = 0; x < C::BPS; ++x) {
-                uint32_t v[16];
-                tmem_ld16(tl + (buf * C::BPS + x) * NT, v);
-                if (x + 1u == C::BPS) {                          // the accumulator group is free again
-                    asm volatile("tcgen05.fence::before_thread_sync;");
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(&tempty[buf]);
-                }
                 if (u * C::BPS + x < nb) {
                     const float4* dx4 = reinterpret_cast<const float4*>(sb + C::DX_OFF + x * NT * 4u + 64u * cq);
                     const uint32_t dwp = reinterpret_cast<const uint32_t*>(sb + C::DW_OFF + x * kTileM * 4u)[32u * rq + lane];
@@ -361,7 +351,7 @@ __global__ void __launch_bounds__(32 * Q8Cfg<NT>::WARPS, 1) mm_q8_tc_kernel(MvAr
 #pragma unroll
                         for (uint32_t e = 0; e < 4; ++e) {
                             const uint32_t i = 4u * k + e;
-                            acc[i] = __fadd_rn(acc[i], __fmul_rn(__fmul_rn(dw, d4[e]), __int2float_rn((int32_t)v[i])));
+                            acc[i] = __fadd_rn(acc[i], __fmul_rn(__fmul_rn(dw, d4[e]), __int2float_rn((int32_t)v[x][i])));
                         }
                     }
                     if (++ii == cnt) {                           // partial j is complete
@@ -453,7 +443,7 @@ template <uint32_t NT>
 struct Q4Cfg {
     static constexpr uint32_t E = 4u * (NT / 16u), P = 2u, X = 4u;
     static constexpr uint32_t WARPS = E + P + X + 1u, MMA_WARP = E + P + X;
-    static constexpr uint32_t S = 3u, LAG = 2u, NB = 2u, NA = 2u;
+    static constexpr uint32_t S = 3u, NB = 2u, NA = 2u;
     static constexpr uint32_t RAW = kTileM * 128u, BT = NT * 32u, ATILE = kTileM * 32u;
     static constexpr uint32_t B_OFF = RAW, DX_OFF = B_OFF + 8u * BT, BS_OFF = DX_OFF + NT * 4u;
     static constexpr uint32_t META_OFF = BS_OFF + NT * 16u, STAGE = META_OFF + kTileM * 16u;
@@ -496,12 +486,18 @@ __device__ __forceinline__ void q4k_epilogue(const MvArgs& a, uint8_t* smem, uin
 #pragma unroll
         for (uint32_t i = 0; i < 16; ++i) isum[i] = 0;
 #pragma unroll
-        for (uint32_t jj = 0; jj < 8u; ++jj) {
-            uint32_t v[16];
-            tmem_ld16(tl + (buf * 8u + jj) * NT, v);
-            const int32_t sc = (int32_t)__byte_perm(jj < 4u ? sc_lo : sc_hi, 0u, 0x4440u | (jj & 3u));
+        for (uint32_t g = 0; g < 2u; ++g) {                      // sub-blocks 4 g .. 4 g + 3: four loads, one wait
+            uint32_t v[4][16];
 #pragma unroll
-            for (uint32_t i = 0; i < 16; ++i) isum[i] += sc * (int32_t)v[i];
+            for (uint32_t x = 0; x < 4u; ++x) tmem_ld16(tl + (buf * 8u + 4u * g + x) * NT, v[x]);
+            tmem_wait_ld();
+            const uint32_t scw = g ? sc_hi : sc_lo;
+#pragma unroll
+            for (uint32_t x = 0; x < 4u; ++x) {
+                const int32_t sc = (int32_t)__byte_perm(scw, 0u, 0x4440u | x);
+#pragma unroll
+                for (uint32_t i = 0; i < 16; ++i) isum[i] += sc * (int32_t)v[x][i];
+            }
         }
         asm volatile("tcgen05.fence::before_thread_sync;");
         __syncwarp();
@@ -587,7 +583,7 @@ __global__ void __launch_bounds__(32 * Q4Cfg<NT>::WARPS, 1) mm_q4k_tc_kernel(MvA
     }
     if (threadIdx.x == 0) {
         for (uint32_t i = 0; i < C::S; ++i) {
-            mbar_init(&full[i], C::P);
+            mbar_init(&full[i], 32u * C::P);
             mbar_init(&empty[i], 1u + C::X + C::E);
         }
         for (uint32_t i = 0; i < C::NA; ++i) {
@@ -621,7 +617,6 @@ __global__ void __launch_bounds__(32 * Q4Cfg<NT>::WARPS, 1) mm_q4k_tc_kernel(MvA
         constexpr uint32_t LN = 32u * C::P;
         const uint32_t pl = (warp - C::E) * 32u + lane, kk = pl & 7u;
         const size_t qrow = L.qs_row_bytes(), mrow = L.meta_row_bytes();
-        uint32_t issued = 0;
         for (uint32_t u = 0; u < nsb; ++u) {
             const uint32_t st = u % C::S;
             if (u >= C::S && !mbar_wait_ab(&empty[st], ((u / C::S) - 1u) & 1u, abort_flag)) break;
@@ -652,20 +647,9 @@ __global__ void __launch_bounds__(32 * Q4Cfg<NT>::WARPS, 1) mm_q4k_tc_kernel(MvA
                 cp_async16(sb + C::META_OFF + 16u * r,
                            static_cast<const uint8_t*>(a.meta) + (size_t)min(row0 + r, a.n_rows - 1u) * mrow + 16u * sbk);
             }
-            cp_async_commit();
-            ++issued;
-            if (u >= C::LAG) {
-                cp_async_wait<C::LAG>();
-                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&full[(u - C::LAG) % C::S]);
-            }
+            cp_async_arrive(&full[st]);                          // the stage is published when its copies land
         }
         cp_async_wait<0>();
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        __syncwarp();
-        if (lane == 0)
-            for (uint32_t u = issued > C::LAG ? issued - C::LAG : 0u; u < issued; ++u) mbar_arrive(&full[u % C::S]);
     } else if (warp >= C::E + C::P && warp < C::MMA_WARP) {
         // ---- expanders: thread r owns row r of the tile
         const uint32_t r = (warp - C::E - C::P) * 32u + lane;
