@@ -237,6 +237,7 @@ __global__ void __launch_bounds__(32 * Q8Cfg<NT>::WARPS, 1) mm_q8_tc_kernel(MvAr
     if (warp >= C::E && warp < C::E + C::P) {
         // ---- producers: lane pl copies A chunks of rows (pl / 2) + 32 P k, half pl & 1, ...
         constexpr uint32_t LN = 32u * C::P, AR = 256u / LN, BR = (2u * NT + LN - 1u) / LN, WR = kTileM / LN;
+        constexpr uint32_t DR = (NT + LN - 1u) / LN;
         const uint32_t pl = (warp - C::E) * 32u + lane, h = pl & 1u;
         const uint8_t* arow[AR];
         uint32_t adst[AR];
@@ -254,7 +255,9 @@ __global__ void __launch_bounds__(32 * Q8Cfg<NT>::WARPS, 1) mm_q8_tc_kernel(MvAr
             brow[k] = a.qx + (size_t)min(tok0 + t, a.T - 1u) * K + 16u * h;
             bdst[k] = t < NT ? C::B_OFF + (t >> 3) * 256u + h * 128u + (t & 7u) * 16u : 0xFFFFFFFFu;
         }
-        const float* dxrow = a.dx + (size_t)min(tok0 + (pl < NT ? pl : 0u), a.T - 1u) * nb;
+        const float* dxrow[DR];
+#pragma unroll
+        for (uint32_t k = 0; k < DR; ++k) dxrow[k] = a.dx + (size_t)min(tok0 + pl + LN * k, a.T - 1u) * nb;
         const uint8_t* wrow[WR];
 #pragma unroll
         for (uint32_t k = 0; k < WR; ++k)
@@ -274,7 +277,9 @@ __global__ void __launch_bounds__(32 * Q8Cfg<NT>::WARPS, 1) mm_q8_tc_kernel(MvAr
 #pragma unroll
                     for (uint32_t k = 0; k < BR; ++k)
                         if (bdst[k] != 0xFFFFFFFFu) cp_async16(sb + x * C::B_BYTES + bdst[k], brow[k] + 32u * b);
-                    if (pl < NT) cp_async4(sb + C::DX_OFF + x * NT * 4u + 4u * pl, dxrow + b);
+#pragma unroll
+                    for (uint32_t k = 0; k < DR; ++k)
+                        if (pl + LN * k < NT) cp_async4(sb + C::DX_OFF + x * NT * 4u + 4u * (pl + LN * k), dxrow[k] + b);
 #pragma unroll
                     for (uint32_t k = 0; k < WR; ++k)
                         cp_async4(sb + C::DW_OFF + x * kTileM * 4u + 4u * (pl + LN * k), wrow[k] + 2u * (b & ~1u));
@@ -615,6 +620,7 @@ __global__ void __launch_bounds__(32 * Q4Cfg<NT>::WARPS, 1) mm_q4k_tc_kernel(MvA
     if (warp >= C::E && warp < C::E + C::P) {
         // ---- producers
         constexpr uint32_t LN = 32u * C::P;
+        static_assert(LN >= NT && LN <= kTileM && LN % 8u == 0u, "one Dx / pair-sum copy per token, META rows by LN");
         const uint32_t pl = (warp - C::E) * 32u + lane, kk = pl & 7u;
         const size_t qrow = L.qs_row_bytes(), mrow = L.meta_row_bytes();
         for (uint32_t u = 0; u < nsb; ++u) {
