@@ -59,6 +59,49 @@ def capture(torch, body, sync):
         return None
 
 
+# prefill MUL_MAT on the tensor cores (many tokens): BASELINE configs 5 and 4 FFN shapes
+PREFILL = [
+    (1, 14336, 4096, 2048, 501, "cfg5 FFN gate/up: Q4_K 14336x4096, 2048-token prefill"),
+    (0, 4864, 896, 512, 401, "cfg4 FFN gate/up: Q8_0 4864x896, 512-token prefill"),
+]
+
+
+def prefill_measure(dev, tsrc, torch, reps=10, warmup=3):
+    """tsrc_mul_mat over T tokens (QACT of every token + the tcgen05 kernel), inputs resident in
+    HBM; int8 ops = 2 N K T. Compute-bound, so L2 residency of the weights does not matter."""
+    peak = None
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            peak = 2.0 * float(json.load(f)["bf16_tflops"])     # int8 dense = 2x bf16 dense on this tensor pipe
+    res = []
+    for fmt, N, K, T, seed, desc in PREFILL:
+        w = dev.synth(fmt, N, K, seed=seed)
+        g = torch.Generator(device="cuda")
+        g.manual_seed(seed + 1)
+        x = torch.randn(T, K, device="cuda", generator=g)
+        y = torch.empty(T, N, device="cuda")
+        for _ in range(warmup):
+            dev.mul_mat(w, x, y, T=T)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            dev.mul_mat(w, x, y, T=T)
+        e1.record()
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) * 1e3 / reps
+        tops = 2.0 * N * K * T / (us * 1e-6) / 1e12
+        res.append({"workload": desc, "us_per_call": round(us, 1), "TOPS": round(tops, 1),
+                    "frac_of_int8_peak": round(tops / peak, 4) if peak else None,
+                    "int8_peak_TOPS": round(peak, 1) if peak else None})
+        w.free()
+    return {"metric": "prefill MUL_MAT int8 TOPS (tcgen05 kind::i8, bit-exact f32 block scaling)", "runs": res,
+            "peak_kind": "2x measured bf16 dense (MEASURED_PEAKS.json)" if peak else None,
+            "note": "the reference's per-32-value f32 scale-and-accumulate runs on the CUDA cores; ncu tensor-pipe "
+                    "activity in profiles/mm_tc_prefill.md"}
+
+
 def fa_algo_bytes(n_head_kv, D, G, n_kv):
     """K and V q8_0 bytes of the visible cells + f32 q in + f32 out (per call)."""
     E = n_head_kv * D
@@ -447,6 +490,7 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-graph", action="store_true")
     ap.add_argument("--no-fa", action="store_true", help="skip the config-3 FA summary in the default line")
+    ap.add_argument("--no-prefill", action="store_true", help="skip the tensor-core prefill summary in the default line")
     ap.add_argument("--collective", default="p2p", choices=["p2p", "nccl"],
                     help="N > 1 matvec: all-gather fused into the kernel (P2P stores) or an NCCL all_gather")
     args = ap.parse_args()
@@ -605,6 +649,9 @@ def main():
                            "e2e_us_per_step": round(ms_fa_e2e * 1e3 / info["e2e_steps"], 3),
                            "l2": f"ring of {info['ring']} caches ({info['ring_mb_per_gpu']} MB)", "cuda_graph": True,
                            "full_line": "python bench.py --config cfg3"}
+
+    if world == 1 and not args.no_prefill:
+        also["prefill"] = prefill_measure(dev, tsrc, torch)
 
     traffic = None
     prof = os.path.join(ROOT, "profiles", f"traffic_{args.config}.json")
