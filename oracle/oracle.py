@@ -77,6 +77,11 @@ class Tsro:
         L.tsro_fa_qk_isums.argtypes = [ct.POINTER(FaParams), _p, _p, _p]
         L.tsro_quantize_q8_0.argtypes = [_p, _u32, _p]
         L.tsro_quantize_q4_K.argtypes = [_p, _u32, _p]
+        L.tsro_rms_norm.argtypes = [_p, _p, _p, _u32, _u32, _f32, _f32]
+        L.tsro_sincos.argtypes = [_f32, _p, _p]
+        L.tsro_rope.argtypes = [_p, _p, _p, _u32, _u32, _u32, _u32, _u32, _f32, _f32]
+        L.tsro_vop.argtypes = [_u32, _p, _p, _p, _sz]
+        L.tsro_dequant_row.argtypes = [_u32, _p, _u32, _p]
 
     # -- scalar rules, vectorised by a Python loop (small inputs only) --
     def fp(self, op: str, a, b=None):
@@ -179,6 +184,60 @@ class Tsro:
         return out
 
 
+    # -- decoder-layer vector kinds (tsro_vu.c) --
+    def rms_norm(self, x, w=None, eps=1e-5, inv_n=None):
+        """RMS_NORM + MUL of rows of x [rows, n] (w [n] or None); inv_n defaults to f32(1/n)."""
+        x = np.ascontiguousarray(np.atleast_2d(x), np.float32)
+        rows, n = x.shape
+        inv_n = np.float32(1.0) / np.float32(n) if inv_n is None else inv_n
+        y = np.empty_like(x)
+        w = None if w is None else np.ascontiguousarray(w, np.float32)
+        self.lib.tsro_rms_norm(_ptr(x), _ptr(y), _ptr(w), n, rows, float(np.float32(eps)), float(np.float32(inv_n)))
+        return y
+
+    def sincos(self, t):
+        t = np.ascontiguousarray(t, np.float32).ravel()
+        s, c = np.empty_like(t), np.empty_like(t)
+        sv, cv = ct.c_float(), ct.c_float()
+        for i, v in enumerate(t):
+            self.lib.tsro_sincos(float(v), ct.byref(sv), ct.byref(cv))
+            s[i], c[i] = sv.value, cv.value
+        return s, c
+
+    def rope(self, x, pos, *, n_heads, head_dim, n_dims, mode, ts, attn_factor=1.0):
+        """x [T, n_heads * head_dim] f32, pos [T] int32 -> rotated copy."""
+        x = np.ascontiguousarray(np.atleast_2d(x), np.float32)
+        pos = np.ascontiguousarray(pos, np.int32)
+        y = np.empty_like(x)
+        self.lib.tsro_rope(_ptr(x), _ptr(y), _ptr(pos), x.shape[0], n_heads, head_dim, n_dims, mode, float(np.float32(ts)),
+                           float(np.float32(attn_factor)))
+        return y
+
+    def vop(self, func: int, a, b=None):
+        a = np.ascontiguousarray(a, np.float32)
+        b = a if b is None else np.ascontiguousarray(b, np.float32)
+        y = np.empty_like(a)
+        self.lib.tsro_vop(func, _ptr(a), _ptr(b), _ptr(y), a.size)
+        return y
+
+    def dequant(self, fmt: int, w, K: int):
+        """ggml rows [N, row bytes] -> f32 [N, K]."""
+        w = np.ascontiguousarray(np.atleast_2d(w), np.uint8)
+        y = np.empty((w.shape[0], K), np.float32)
+        for r in range(w.shape[0]):
+            self.lib.tsro_dequant_row(fmt, _ptr(w[r]), K, _ptr(y[r]))
+        return y
+
+
+class RopeCfg(ct.Structure):
+    """tsr_ref_rope_cfg (sw/sim/include/tsr_ref_vu.h:111-123)."""
+    _fields_ = [(n, _u32) for n in ("mode", "ff", "fs", "atab", "m", "ts", "freq_scale", "head_dim", "n_dims", "n_heads", "T")]
+
+
+def _bits(v) -> int:
+    return int(np.float32(v).view(np.uint32))
+
+
 class Ref:
     """The reference's own library (oracle/_ref/libtsr_refdrv.so), when it was built."""
 
@@ -203,6 +262,12 @@ class Ref:
         L.refdrv_fa_run.restype = ct.c_int
         L.refdrv_fa_run.argtypes = [_p, _p, _p]
         L.refdrv_fa_free.argtypes = [_p]
+        L.tsr_ref_red_row.restype = _u32
+        L.tsr_ref_red_row.argtypes = [_u32, _u32, _p, _u32, _u32, _u32]
+        L.tsr_ref_vop.argtypes = [_u32, _u32, _u32, _u32, _p, _u32, _p, _u32, _p, _u32, _p]
+        L.tsr_m_sincos.argtypes = [_f32, _p, _p]
+        L.tsr_ref_rope.argtypes = [ct.POINTER(RopeCfg), _p, _u32, _p, _u32, _p, _p]
+        L.tsr_dequant_row.argtypes = [_u32, _p, _u32, _p]
 
     def expk(self, v, kappa=0):
         v = np.ascontiguousarray(v, np.float32).ravel()
@@ -293,3 +358,60 @@ class Ref:
             return self.fa_run(h, q)
         finally:
             self.fa_free(h)
+
+    # -- the reference's vector unit (tsr_ref_vu.c, tsr_ref_math.c, tsr_ref.c) --
+    def rms_norm(self, x, w=None, eps=1e-5, inv_n=None):
+        """RED.SUMSQ post RMS per row, then VOP.MULCB (MULC without w), as rmsnorm_ref_rows does."""
+        x = np.ascontiguousarray(np.atleast_2d(x), np.float32)
+        rows, n = x.shape
+        inv_n = np.float32(1.0) / np.float32(n) if inv_n is None else inv_n
+        L = -(-n // 16) * 16
+        y = np.zeros((rows, n), np.float32)
+        wp = None if w is None else np.ascontiguousarray(np.pad(np.asarray(w, np.float32), (0, L - n)), np.float32)
+        for r in range(rows):
+            xr = np.ascontiguousarray(np.pad(x[r], (0, L - n)), np.float32)
+            s = self.lib.tsr_ref_red_row(1, 2, _ptr(xr), n, _bits(inv_n), _bits(eps))
+            c = np.array([s], np.uint32)
+            out = np.zeros(L, np.float32)
+            if wp is None:
+                self.lib.tsr_ref_vop(4, 1, 1, n, _ptr(out), 0, _ptr(xr), 0, None, 0, _ptr(c))
+            else:
+                self.lib.tsr_ref_vop(12, 1, 1, n, _ptr(out), 0, _ptr(xr), 0, _ptr(wp), 0, _ptr(c))
+            y[r] = out[:n]
+        return y
+
+    def sincos(self, t):
+        t = np.ascontiguousarray(t, np.float32).ravel()
+        s, c = np.empty_like(t), np.empty_like(t)
+        sv, cv = ct.c_float(), ct.c_float()
+        for i, v in enumerate(t):
+            self.lib.tsr_m_sincos(float(v), ct.byref(sv), ct.byref(cv))
+            s[i], c[i] = sv.value, cv.value
+        return s, c
+
+    def rope(self, x, pos, *, n_heads, head_dim, n_dims, mode, ts, attn_factor=1.0):
+        x = np.ascontiguousarray(np.atleast_2d(x), np.float32)
+        T = x.shape[0]
+        cfg = RopeCfg(mode, 0, 0, 0, _bits(attn_factor), _bits(ts), 0, head_dim, n_dims, n_heads, T)
+        y = np.zeros_like(x)
+        pos = np.ascontiguousarray(np.asarray(pos, np.int32).view(np.uint32))
+        self.lib.tsr_ref_rope(ct.byref(cfg), _ptr(y), 0, _ptr(x), 0, _ptr(pos), None)
+        return y
+
+    def vop(self, func: int, a, b=None):
+        a = np.ascontiguousarray(a, np.float32).ravel()
+        n = a.size
+        L = -(-n // 16) * 16
+        ap = np.ascontiguousarray(np.pad(a, (0, L - n)), np.float32)
+        bp = None if b is None else np.ascontiguousarray(np.pad(np.asarray(b, np.float32).ravel(), (0, L - n)), np.float32)
+        out = np.zeros(L, np.float32)
+        self.lib.tsr_ref_vop(func, 0, 1, n, _ptr(out), 0, _ptr(ap), 0, _ptr(bp), 0, None)
+        return out[:n]
+
+    def dequant(self, fmt: int, w, K: int):
+        w = np.ascontiguousarray(np.atleast_2d(w), np.uint8)
+        rows = self.repack(fmt, w, K)
+        y = np.empty((w.shape[0], K), np.float32)
+        for r in range(w.shape[0]):
+            self.lib.tsr_dequant_row(fmt, _ptr(rows[r]), K, _ptr(y[r]))
+        return y

@@ -45,6 +45,19 @@ float    tsro_expk(float v, unsigned kappa);   // kappa: 0 P1 (+1), 1 N1 (-1), 2
 float    tsro_exp(float x);
 float    tsro_tanh(float x);
 
+// ---- decoder-layer vector kinds (tsro_vu.c; tsr_ref_vu.c, tsr_ref_math.c, tsr_ref.c) ------------
+float    tsro_fsqrt(float a);
+// RMS_NORM + MUL on rows x n (contiguous rows): RED.SUMSQ post RMS then FM(FM(x, s), w) (w may be NULL)
+void     tsro_rms_norm(const float * x, float * y, const float * w, uint32_t n, uint32_t rows, float eps, float inv_n);
+void     tsro_sincos(float t, float * s, float * c);
+// ROPE recurrence form; mode 0 NORM, 1 NEOX; x, y: [T][n_heads][hd] (y may be x)
+void     tsro_rope(const float * x, float * y, const int32_t * pos, uint32_t T, uint32_t n_heads, uint32_t hd, uint32_t nd,
+                   uint32_t mode, float ts, float m);
+// VOP: func 0 ADD, 2 MUL, 6 SILU (b unused), 7 SWIGLU
+void     tsro_vop(uint32_t func, const float * a, const float * b, float * y, size_t n);
+// one ggml row (K/32 block_q8_0 or K/256 block_q4_K) -> K f32 values
+void     tsro_dequant_row(uint32_t fmt, const uint8_t * row, uint32_t K, float * y);
+
 // ---- QACT (tsr_ref.c:456-518) ----------------------------------------------------------------
 // A32: q[K], d[K/32] (d = f32(fp16(amax/127))). A256: q[K], d[K/256], bs[K/16].
 void     tsro_qact_a32(const float * x, uint32_t K, int8_t * q, float * d);

@@ -307,7 +307,75 @@ int tsrc_sync(tsrc_ctx* ctx, void* stream) {
     e = tsrc::kv_error(&code, true);
     if (e != cudaSuccess) return cuda_fail(e, "reading the KV error flag");
     if (code) return fail(TSRC_E_ARG, "tsrc_kv_set_rows: a cell index outside the cache (those rows were not stored)");
+    e = tsrc::vu_error(&code, true);
+    if (e != cudaSuccess) return cuda_fail(e, "reading the vector-kind error flag");
+    if (code) return fail(TSRC_E_ARG, "tsrc_get_rows: a token id outside the weight (that row was not written)");
     return TSRC_OK;
+}
+
+// ---- vector kinds ---------------------------------------------------------------------------------
+int tsrc_rms_norm(tsrc_ctx* ctx, const float* x, uint32_t x_stride, float* y, uint32_t y_stride, const float* w, uint32_t n,
+                  uint32_t rows, float eps, float inv_n, void* stream) {
+    if (!ctx || !x || !y) return fail(TSRC_E_ARG, "tsrc_rms_norm: NULL argument");
+    if (n == 0 || rows == 0) return TSRC_OK;
+    if (x_stride == 0) x_stride = n;
+    if (y_stride == 0) y_stride = n;
+    if (x_stride < n || y_stride < n) return fail(TSRC_E_ARG, "tsrc_rms_norm: stride below n");
+    int rc = use_device(ctx);
+    if (rc) return rc;
+    cudaError_t e = tsrc::launch_rms_norm(x, x_stride, y, y_stride, w, n, rows, daz_host(eps), daz_host(inv_n),
+                                          static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? TSRC_OK : cuda_fail(e, "rms_norm launch");
+}
+
+int tsrc_rope(tsrc_ctx* ctx, const float* x, uint32_t x_stride, float* y, uint32_t y_stride, const int32_t* pos, uint32_t T,
+              uint32_t n_heads, uint32_t head_dim, uint32_t n_dims, uint32_t mode, float ts, float attn_factor, void* stream) {
+    if (!ctx || !x || !y || !pos) return fail(TSRC_E_ARG, "tsrc_rope: NULL argument");
+    if (mode > TSRC_ROPE_NEOX) return fail(TSRC_E_ARG, "tsrc_rope: undefined mode %u", mode);
+    if (head_dim == 0 || (head_dim & 15u) || head_dim > 1024u) return fail(TSRC_E_ARG, "tsrc_rope: head_dim %u", head_dim);
+    if (n_dims == 0 || n_dims > head_dim || n_dims % (mode == TSRC_ROPE_NEOX ? 32u : 16u))
+        return fail(TSRC_E_ARG, "tsrc_rope: n_dims %u", n_dims);
+    if (T == 0 || n_heads == 0) return TSRC_OK;
+    const uint32_t row = n_heads * head_dim;
+    if (x_stride == 0) x_stride = row;
+    if (y_stride == 0) y_stride = row;
+    if (x_stride < row || y_stride < row) return fail(TSRC_E_ARG, "tsrc_rope: stride below n_heads * head_dim");
+    int rc = use_device(ctx);
+    if (rc) return rc;
+    cudaError_t e = tsrc::launch_rope(x, x_stride, y, y_stride, pos, T, n_heads, head_dim, n_dims, mode, daz_host(ts),
+                                      daz_host(attn_factor), static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? TSRC_OK : cuda_fail(e, "rope launch");
+}
+
+int tsrc_vop(tsrc_ctx* ctx, uint32_t func, const float* a, uint32_t a_stride, const float* b, uint32_t b_stride, float* y,
+             uint32_t y_stride, uint32_t n, uint32_t rows, void* stream) {
+    if (!ctx || !a || !y) return fail(TSRC_E_ARG, "tsrc_vop: NULL argument");
+    if (func != TSRC_VOP_ADD && func != TSRC_VOP_MUL && func != TSRC_VOP_SILU && func != TSRC_VOP_SWIGLU)
+        return fail(TSRC_E_ARG, "tsrc_vop: function %u not supported", func);
+    if (func != TSRC_VOP_SILU && !b) return fail(TSRC_E_ARG, "tsrc_vop: function %u reads b", func);
+    if (n == 0 || rows == 0) return TSRC_OK;
+    if (a_stride == 0) a_stride = n;
+    if (b_stride == 0) b_stride = n;
+    if (y_stride == 0) y_stride = n;
+    if (a_stride < n || y_stride < n || (b && b_stride < n)) return fail(TSRC_E_ARG, "tsrc_vop: stride below n");
+    int rc = use_device(ctx);
+    if (rc) return rc;
+    cudaError_t e = tsrc::launch_vop(func, a, a_stride, func == TSRC_VOP_SILU ? nullptr : b, b_stride, y, y_stride, n, rows,
+                                     static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? TSRC_OK : cuda_fail(e, "vop launch");
+}
+
+int tsrc_get_rows(tsrc_ctx* ctx, const tsrc_weight* w, const int32_t* ids, uint32_t T, float* y, uint32_t y_stride, void* stream) {
+    if (!ctx || !w || !ids || !y) return fail(TSRC_E_ARG, "tsrc_get_rows: NULL argument");
+    if (w->ctx != ctx) return fail(TSRC_E_ARG, "tsrc_get_rows: the weight belongs to another context");
+    if (T == 0) return TSRC_OK;
+    if (y_stride == 0) y_stride = w->K;
+    if (y_stride < w->K) return fail(TSRC_E_ARG, "tsrc_get_rows: stride below K");
+    int rc = use_device(ctx);
+    if (rc) return rc;
+    cudaError_t e = tsrc::launch_get_rows(w->fmt, w->qs, w->meta, w->n_rows, w->K, ids, T, y, y_stride,
+                                          static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? TSRC_OK : cuda_fail(e, "get_rows launch");
 }
 
 int tsrc_weight_upload_device(tsrc_ctx* ctx, uint32_t fmt, const void* ggml_rows_dev, uint32_t N, uint32_t K, uint32_t row0,

@@ -45,6 +45,17 @@ cudaError_t launch_qact(uint32_t kind, const float* x, uint32_t K, uint32_t T, u
 cudaError_t launch_matvec(uint32_t fmt, const MvArgs& a, cudaStream_t st);
 // Many-token MUL_MAT on the tcgen05 tensor cores (Q8_0; the QA image in qx / dx, any T).
 cudaError_t launch_mm_tc(uint32_t fmt, const MvArgs& a, cudaStream_t st);
+
+// tsrc_vu.cu: RMS_NORM, ROPE, VOP, GET_ROWS
+cudaError_t launch_rms_norm(const float* x, uint32_t xs, float* y, uint32_t ys, const float* w, uint32_t n, uint32_t rows,
+                            float eps, float inv_n, cudaStream_t st);
+cudaError_t launch_rope(const float* x, uint32_t xs, float* y, uint32_t ys, const int32_t* pos, uint32_t T, uint32_t n_heads,
+                        uint32_t hd, uint32_t nd, uint32_t neox, float ts, float m, cudaStream_t st);
+cudaError_t launch_vop(uint32_t func, const float* a, uint32_t as, const float* b, uint32_t bs, float* y, uint32_t ys,
+                       uint32_t n, uint32_t rows, cudaStream_t st);
+cudaError_t launch_get_rows(uint32_t fmt, const uint8_t* qs, const void* meta, uint32_t n_rows, uint32_t K, const int32_t* ids,
+                            uint32_t T, float* y, uint32_t ys, cudaStream_t st);
+cudaError_t vu_error(uint32_t* code, bool clear);
 cudaError_t tc_error(uint32_t* code, bool clear);
 size_t mv_smem_bytes(uint32_t fmt, uint32_t K, uint32_t T);
 // The first error code any matvec launch recorded on the current device (0 = none).

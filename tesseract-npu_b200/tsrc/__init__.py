@@ -16,6 +16,8 @@ from __future__ import annotations
 import ctypes as ct
 import os
 
+import numpy as np
+
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(os.path.dirname(HERE), "libtsrc.so")
 INCLUDE = os.path.join(os.path.dirname(os.path.dirname(HERE)), "include", "tsrc.h")
@@ -23,6 +25,8 @@ INCLUDE = os.path.join(os.path.dirname(os.path.dirname(HERE)), "include", "tsrc.
 FMT_Q8_0, FMT_Q4_K = 0, 1
 QA_A32, QA_A256 = 0, 1
 MM_ADD, MM_SCALE, MM_SOFTCAP = 0x1, 0x2, 0x4
+ROPE_NORM, ROPE_NEOX = 0, 1
+VOP_ADD, VOP_MUL, VOP_SILU, VOP_SWIGLU = 0, 2, 6, 7
 E_ARG, E_SHAPE, E_CUDA, E_NOMEM, E_NODEV, E_DEVICE = -1, -2, -3, -4, -5, -6
 
 BLOCK = {FMT_Q8_0: 32, FMT_Q4_K: 256}
@@ -52,6 +56,10 @@ _SIGS = {
     "tsrc_weight_info": (_i, [_p] + [ct.POINTER(_u32)] * 5 + [ct.POINTER(_u64)]),
     "tsrc_weight_free": (_i, [_p]),
     "tsrc_mul_mat": (_i, [_p, _p, _p, _u32, _u32, _p, _u32, _p, _u32, _u32, _f32, _f32, _p]),
+    "tsrc_rms_norm": (_i, [_p, _p, _u32, _p, _u32, _p, _u32, _u32, _f32, _f32, _p]),
+    "tsrc_rope": (_i, [_p, _p, _u32, _p, _u32, _p, _u32, _u32, _u32, _u32, _u32, _f32, _f32, _p]),
+    "tsrc_vop": (_i, [_p, _u32, _p, _u32, _p, _u32, _p, _u32, _u32, _u32, _p]),
+    "tsrc_get_rows": (_i, [_p, _p, _p, _u32, _p, _u32, _p]),
     "tsrc_mul_mat_noalloc": (_i, [_p, _p, _p, _u32, _u32, _p, _u32, _p, _u32, _u32, _f32, _f32, _p]),
     "tsrc_mvm": (_i, [_p, _p, _p, _p, _p, _u32, _p, _u32, _p, _u32, _u32, _f32, _f32, _p]),
     "tsrc_mul_mat_unsupported": (ct.c_char_p, [_u32, _u64, _u64, _u64]),
@@ -197,6 +205,26 @@ class Device:
         return Weight(self, h)
 
     # ---- MUL_MAT ----
+    # ---- the decoder layer's vector kinds ----
+    def rms_norm(self, x, y, n: int, rows: int, w=None, eps: float = 1e-5, inv_n: float | None = None,
+                 x_stride: int = 0, y_stride: int = 0, stream=None) -> None:
+        inv_n = float(np.float32(1.0) / np.float32(n)) if inv_n is None else inv_n
+        _check(lib().tsrc_rms_norm(self.handle, _addr(x), x_stride, _addr(y), y_stride, _addr(w), n, rows, eps, inv_n,
+                                   _stream(stream)))
+
+    def rope(self, x, y, pos, T: int, n_heads: int, head_dim: int, n_dims: int, mode: int, ts: float,
+             attn_factor: float = 1.0, x_stride: int = 0, y_stride: int = 0, stream=None) -> None:
+        _check(lib().tsrc_rope(self.handle, _addr(x), x_stride, _addr(y), y_stride, _addr(pos), T, n_heads, head_dim,
+                               n_dims, mode, ts, attn_factor, _stream(stream)))
+
+    def vop(self, func: int, a, b, y, n: int, rows: int = 1, a_stride: int = 0, b_stride: int = 0, y_stride: int = 0,
+            stream=None) -> None:
+        _check(lib().tsrc_vop(self.handle, func, _addr(a), a_stride, _addr(b), b_stride, _addr(y), y_stride, n, rows,
+                              _stream(stream)))
+
+    def get_rows(self, w: "Weight", ids, T: int, y, y_stride: int = 0, stream=None) -> None:
+        _check(lib().tsrc_get_rows(self.handle, w.handle, _addr(ids), T, _addr(y), y_stride, _stream(stream)))
+
     def mul_mat(self, w: "Weight", x, y, T: int | None = None, add=None, add_stride: int | None = None,
                 flags: int = 0, s0: float = 1.0, s1: float = 1.0, x_stride: int = 0, y_stride: int = 0,
                 stream=None) -> None:
