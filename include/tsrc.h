@@ -267,6 +267,46 @@ TSRC_API int tsrc_vop(tsrc_ctx * ctx, uint32_t func, const float * a, uint32_t a
 TSRC_API int tsrc_get_rows(tsrc_ctx * ctx, const tsrc_weight * w, const int32_t * ids, uint32_t T, float * y,
                            uint32_t y_stride, void * stream);
 
+// ---- an end-to-end decoder model through the kinds above (llama.cpp's llama / qwen2 graphs) --------
+// A random-init model of the given shape, every matrix quantized to fmt, run layer by layer through
+// GET_ROWS, RMS_NORM + MUL, MUL_MAT (+ bias), ROPE, SET_ROWS into a per-layer q8_0 KV cache,
+// FLASH_ATTN_EXT, MUL_MAT + residual, SWIGLU, MUL_MAT + residual, the output norm and head. It is
+// the device-side counterpart of llama.cpp with -ngl all on the reference backend (the model's
+// graph_compute of every node, ggml-tesseract.cpp:3929-3966), for the decode tokens/s measurement.
+typedef struct tsrc_model tsrc_model;
+typedef struct tsrc_model_cfg {
+    uint32_t n_layer, n_embd, n_ff, n_head, n_head_kv, head_dim, n_vocab;
+    uint32_t fmt;            // TSRC_FMT_Q8_0 or TSRC_FMT_Q4_K for every matrix (K multiples of 256 for Q4_K)
+    uint32_t rope_mode;      // TSRC_ROPE_NORM (llama) or TSRC_ROPE_NEOX (qwen2); n_dims = head_dim
+    float rope_base;         // freq_base; ts = powf(freq_base, -2 / head_dim) on the host
+    float rms_eps;
+    uint32_t qkv_bias;       // f32 biases on q, k, v (qwen2)
+    uint32_t tied_head;      // the head is the token embedding (qwen2.5-0.5B)
+    uint32_t n_ctx;          // KV cells per layer
+    tsrc_fa_cfg fa;          // C = 0: the release image's {4, 4, 9344, 32768, 0}
+} tsrc_model_cfg;
+#define TSRC_MODEL_GLOBAL 0xFFFFFFFFu   // tsrc_model_weight layer: which 0 = token embedding, 1 = head
+
+// Weights from tsrc_weight_synth(seed * 1000 + 1 / + 2 for the embedding / head; seed * 1000 +
+// 16 (l + 1) + i for layer l's q, k, v, o, gate, up, down, sigma 0.02); f32 vectors from
+// tsrc_model_f32_value.
+TSRC_API int tsrc_model_create(tsrc_ctx * ctx, const tsrc_model_cfg * cfg, uint64_t seed, tsrc_model ** out);
+TSRC_API int tsrc_model_free(tsrc_model * m);
+// Runs tokens ids[0..T) (device int32) at positions pos0 .. pos0 + T - 1: their K / V rows are stored
+// at cells pos0 .. and attention is causal over cells [0, pos0 + t]. logits (device f32 [n_vocab])
+// receives the head output of the last token. Queued on `stream`.
+TSRC_API int tsrc_model_forward(tsrc_model * m, const int32_t * ids, uint32_t T, uint32_t pos0, float * logits,
+                                void * stream);
+// The model's weight handles (owned by the model): layer < n_layer, which 0..6 = q, k, v, o, gate,
+// up, down; or TSRC_MODEL_GLOBAL.
+TSRC_API int tsrc_model_weight(const tsrc_model * m, uint32_t layer, uint32_t which, tsrc_weight ** out);
+// The host-computed ROPE theta scale and attention scale the model passes to the kinds.
+TSRC_API int tsrc_model_params(const tsrc_model * m, float * ts, float * kq_scale);
+// f32 vector element i of the model: which 0 attn_norm, 1 ffn_norm, 2 / 3 / 4 q / k / v bias (layer
+// l), 5 output norm (layer = n_layer): splitmix64 of (seed, layer, which, i) -> 1 + 0.25 u for the
+// norms, 0.1 u for the biases, u uniform in [-1, 1) on 24 bits.
+TSRC_API float tsrc_model_f32_value(uint64_t seed, uint32_t layer, uint32_t which, uint32_t i);
+
 #ifdef __cplusplus
 }
 #endif

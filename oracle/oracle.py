@@ -415,3 +415,57 @@ class Ref:
         for r in range(w.shape[0]):
             self.lib.tsr_dequant_row(fmt, _ptr(rows[r]), K, _ptr(y[r]))
         return y
+
+
+class OracleModel:
+    """CPU composition of the decoder graph (llama / qwen2 layers) over the oracle's kinds, in the
+    order tsrc_model_forward runs them: GET_ROWS, RMS_NORM + MUL, MUL_MAT (+ bias), ROPE, KVST into
+    ggml q8_0 cache rows, FA, MUL_MAT + residual, RMS_NORM + MUL, gate / up, SWIGLU, down + residual,
+    output norm and head of the last token. Test and baseline infrastructure only."""
+
+    def __init__(self, tsro: "Tsro", cfg: dict, layers: list, emb, head, out_norm, ts: float, kq_scale: float,
+                 threads: int | None = None):
+        self.o, self.c, self.layers = tsro, cfg, layers
+        self.emb, self.head, self.out_norm = emb, head, out_norm
+        self.ts, self.kq_scale, self.threads = ts, kq_scale, threads
+        E = cfg["n_head_kv"] * cfg["head_dim"]
+        self.kc = [np.zeros((cfg["n_ctx"], E // 32 * 34), np.uint8) for _ in layers]
+        self.vc = [np.zeros((cfg["n_ctx"], E // 32 * 34), np.uint8) for _ in layers]
+
+    def forward(self, ids, pos0: int):
+        o, c = self.o, self.c
+        ids = np.asarray(ids, np.int64)
+        T = ids.size
+        E, D, nh, nkv, F, fmt = c["n_embd"], c["head_dim"], c["n_head"], c["n_head_kv"], c["n_ff"], c["fmt"]
+        Hq, n_kv = nh * D, pos0 + T
+        inv_n = np.float32(1.0) / np.float32(E)
+        pos = np.arange(pos0, pos0 + T, dtype=np.int32)
+        mask = None
+        if T > 1:
+            mask = np.full((T, n_kv), -np.inf, np.float16)
+            for t in range(T):
+                mask[t, :pos0 + t + 1] = 0
+        x = o.dequant(fmt, self.emb[ids], E)
+        th = self.threads
+        rope = dict(head_dim=D, n_dims=D, mode=c["rope_mode"], ts=self.ts)
+        for li, L in enumerate(self.layers):
+            h = o.rms_norm(x, L["attn_norm"], c["rms_eps"], inv_n)
+            q = o.matvec(fmt, L["wq"], E, h, add=None if L.get("bq") is None else L["bq"][None, :], add_stride=0, threads=th)
+            k = o.matvec(fmt, L["wk"], E, h, add=None if L.get("bk") is None else L["bk"][None, :], add_stride=0, threads=th)
+            v = o.matvec(fmt, L["wv"], E, h, add=None if L.get("bv") is None else L["bv"][None, :], add_stride=0, threads=th)
+            q = o.rope(q, pos, n_heads=nh, **rope)
+            k = o.rope(k, pos, n_heads=nkv, **rope)
+            self.kc[li][pos0:n_kv] = o.quantize(FMT_Q8_0, k)
+            self.vc[li][pos0:n_kv] = o.quantize(FMT_Q8_0, v)
+            rc, att = o.fa(q.reshape(T, nh, D), self.kc[li], self.vc[li], D=D, n_head=nh, n_head_kv=nkv, n_kv=n_kv,
+                           scale=self.kq_scale, mask=mask, new=(pos0, n_kv))
+            if rc != 0:
+                raise RuntimeError(f"tsro_fa returned {rc}")
+            x = o.matvec(fmt, L["wo"], Hq, att.reshape(T, Hq), add=x, add_stride=E, threads=th)
+            h = o.rms_norm(x, L["ffn_norm"], c["rms_eps"], inv_n)
+            g = o.matvec(fmt, L["wg"], E, h, threads=th)
+            u = o.matvec(fmt, L["wu"], E, h, threads=th)
+            s = o.vop(7, g, u)
+            x = o.matvec(fmt, L["wd"], F, s, add=x, add_stride=E, threads=th)
+        h = o.rms_norm(x[-1:], self.out_norm, c["rms_eps"], inv_n)
+        return o.matvec(fmt, self.head, E, h, threads=th)[0]

@@ -194,7 +194,7 @@ __device__ __forceinline__ float ctree16(float (&v)[16], uint32_t n) {
 // ---------------------------------------------------------------------------------------------------
 template <int D>
 __global__ void __launch_bounds__(kFaThreads, 1) fa_chunk_kernel(FaLaunch a) {
-    constexpr uint32_t ND = D / 32, NSL = D / 64, RB = 512 / D, NV = D / 32;
+    constexpr uint32_t ND = D / 32, NSL = D / 64, RB = 512 / D;
     extern __shared__ __align__(16) uint8_t smem[];
     cg::cluster_group cluster = cg::this_cluster();
     const uint32_t C = a.C, cc = cluster.block_rank();

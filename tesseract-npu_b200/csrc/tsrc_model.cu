@@ -1,0 +1,241 @@
+// tsrc_model.cu -- a random-init decoder-only transformer (Llama / Qwen2 layer graph) run through the
+// C ABI's kinds, for end-to-end prefill and decode: the graph llama.cpp builds for these
+// architectures (llm_build_llama / llm_build_qwen2 of the pinned llama.cpp) with every node on the
+// device: GET_ROWS, RMS_NORM + MUL, MUL_MAT (+ bias ADD), ROPE, SET_ROWS into the q8_0 KV cache,
+// FLASH_ATTN_EXT, MUL_MAT + residual ADD, RMS_NORM + MUL, MUL_MAT gate / up, SWIGLU, MUL_MAT down +
+// residual ADD; then the output RMS_NORM + MUL and the head MUL_MAT of the last token.
+//
+// Each residual ADD is the MUL_MAT's addend epilogue (fadd(x, dot): the same value as the ADD
+// node). Weights come from tsrc_weight_synth (seeded); the f32 vectors (norm weights, biases) from
+// splitmix64 (tsrc_model_f32_value), so a checker can rebuild them.
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <vector>
+
+#include "tsrc_internal.h"
+#include "../../include/tsrc.h"
+
+struct tsrc_model {
+    tsrc_ctx* ctx;
+    tsrc_model_cfg c;
+    float ts, kq_scale;
+    tsrc_weight* tok_embd = nullptr;
+    tsrc_weight* output = nullptr;                       // NULL with a tied head
+    float* f32 = nullptr;                                // every f32 vector, one allocation
+    float* out_norm = nullptr;
+    struct Layer {
+        tsrc_weight *wq, *wk, *wv, *wo, *wg, *wu, *wd;
+        float *attn_norm, *ffn_norm, *bq, *bk, *bv;
+        tsrc_kv* kv;
+    };
+    std::vector<Layer> layers;
+    int32_t* pos = nullptr;                              // 0 .. n_ctx - 1 (device)
+    float* buf = nullptr;                                // activations for t_alloc tokens
+    uint32_t t_alloc = 0;
+    float *x, *h, *q, *k, *v, *att, *g, *u;
+    std::vector<uint16_t> mask;                          // host causal mask of a multi-token call
+};
+
+namespace {
+
+uint64_t splitmix64(uint64_t z) {
+    z += 0x9E3779B97F4A7C15ull;
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+}
+
+int set_err(int rc) { return rc; }
+
+// f32 vector kinds of the model (tsrc_model_f32_value)
+constexpr uint32_t kVecAttnNorm = 0, kVecFfnNorm = 1, kVecBq = 2, kVecBk = 3, kVecBv = 4, kVecOutNorm = 5;
+
+}  // namespace
+
+extern "C" {
+
+float tsrc_model_f32_value(uint64_t seed, uint32_t layer, uint32_t which, uint32_t i) {
+    const uint64_t z = splitmix64(seed ^ ((uint64_t)layer << 40) ^ ((uint64_t)which << 32) ^ i);
+    const float u = (float)(z >> 40) * (1.0f / 16777216.0f) * 2.0f - 1.0f;   // [-1, 1), 24 random bits
+    return (which == kVecAttnNorm || which == kVecFfnNorm || which == kVecOutNorm) ? 1.0f + 0.25f * u : 0.1f * u;
+}
+
+int tsrc_model_free(tsrc_model* m) {
+    if (!m) return TSRC_OK;
+    cudaDeviceSynchronize();
+    for (auto& L : m->layers) {
+        tsrc_weight* ws[] = {L.wq, L.wk, L.wv, L.wo, L.wg, L.wu, L.wd};
+        for (tsrc_weight* w : ws)
+            if (w) tsrc_weight_free(w);
+        if (L.kv) tsrc_kv_free(L.kv);
+    }
+    if (m->tok_embd) tsrc_weight_free(m->tok_embd);
+    if (m->output) tsrc_weight_free(m->output);
+    cudaFree(m->f32);
+    cudaFree(m->pos);
+    cudaFree(m->buf);
+    delete m;
+    return TSRC_OK;
+}
+
+int tsrc_model_create(tsrc_ctx* ctx, const tsrc_model_cfg* cfg, uint64_t seed, tsrc_model** out) {
+    if (!ctx || !cfg || !out) return TSRC_E_ARG;
+    *out = nullptr;
+    const tsrc_model_cfg& c = *cfg;
+    if (c.n_layer == 0 || c.n_embd == 0 || c.n_ff == 0 || c.n_head == 0 || c.n_head_kv == 0 || c.n_head % c.n_head_kv ||
+        c.n_vocab == 0 || c.n_ctx == 0 || (c.fmt != TSRC_FMT_Q8_0 && c.fmt != TSRC_FMT_Q4_K) || c.rope_mode > TSRC_ROPE_NEOX)
+        return TSRC_E_ARG;
+    tsrc_model* m = new tsrc_model();
+    m->ctx = ctx;
+    m->c = c;
+    m->ts = powf(c.rope_base, -2.0f / (float)c.head_dim);       // the backend's theta scale (host libm)
+    m->kq_scale = 1.0f / sqrtf((float)c.head_dim);              // llama.cpp's kq_scale
+    const uint32_t E = c.n_embd, D = c.head_dim, Hq = c.n_head * D, Hkv = c.n_head_kv * D, F = c.n_ff;
+    const float sigma = 0.02f;
+    int rc = TSRC_OK;
+    auto synth = [&](uint32_t N, uint32_t K, uint64_t s, tsrc_weight** w) {
+        if (rc == TSRC_OK) rc = tsrc_weight_synth(ctx, c.fmt, N, K, 0, N, s, sigma, nullptr, w);
+    };
+    synth(c.n_vocab, E, seed * 1000u + 1u, &m->tok_embd);
+    if (!c.tied_head) synth(c.n_vocab, E, seed * 1000u + 2u, &m->output);
+    // f32 vectors: per layer attn_norm, ffn_norm (E) and the biases (Hq, Hkv, Hkv); out_norm (E)
+    const size_t per_layer = 2u * E + (c.qkv_bias ? (size_t)Hq + 2u * Hkv : 0u);
+    const size_t n_f32 = per_layer * c.n_layer + E;
+    std::vector<float> host(n_f32);
+    m->layers.resize(c.n_layer);
+    if (rc == TSRC_OK && cudaMalloc(&m->f32, n_f32 * sizeof(float)) != cudaSuccess) rc = TSRC_E_NOMEM;
+    size_t o = 0;
+    auto vec = [&](uint32_t layer, uint32_t which, uint32_t n) {
+        float* p = m->f32 + o;
+        for (uint32_t i = 0; i < n; ++i) host[o + i] = tsrc_model_f32_value(seed, layer, which, i);
+        o += n;
+        return p;
+    };
+    for (uint32_t l = 0; l < c.n_layer && rc == TSRC_OK; ++l) {
+        tsrc_model::Layer& L = m->layers[l];
+        std::memset(&L, 0, sizeof L);
+        const uint64_t s = seed * 1000u + 16u * (l + 1u);
+        synth(Hq, E, s + 0, &L.wq);
+        synth(Hkv, E, s + 1, &L.wk);
+        synth(Hkv, E, s + 2, &L.wv);
+        synth(E, Hq, s + 3, &L.wo);
+        synth(F, E, s + 4, &L.wg);
+        synth(F, E, s + 5, &L.wu);
+        synth(E, F, s + 6, &L.wd);
+        L.attn_norm = vec(l, kVecAttnNorm, E);
+        L.ffn_norm = vec(l, kVecFfnNorm, E);
+        if (c.qkv_bias) {
+            L.bq = vec(l, kVecBq, Hq);
+            L.bk = vec(l, kVecBk, Hkv);
+            L.bv = vec(l, kVecBv, Hkv);
+        }
+        if (rc == TSRC_OK) rc = tsrc_kv_create(ctx, c.n_head_kv, D, c.n_ctx, &L.kv);
+    }
+    m->out_norm = vec(c.n_layer, kVecOutNorm, E);
+    if (rc == TSRC_OK && cudaMemcpy(m->f32, host.data(), n_f32 * sizeof(float), cudaMemcpyHostToDevice) != cudaSuccess)
+        rc = TSRC_E_CUDA;
+    std::vector<int32_t> pos(c.n_ctx);
+    for (uint32_t i = 0; i < c.n_ctx; ++i) pos[i] = (int32_t)i;
+    if (rc == TSRC_OK && (cudaMalloc(&m->pos, c.n_ctx * sizeof(int32_t)) != cudaSuccess ||
+                          cudaMemcpy(m->pos, pos.data(), c.n_ctx * sizeof(int32_t), cudaMemcpyHostToDevice) != cudaSuccess))
+        rc = TSRC_E_NOMEM;
+    if (rc != TSRC_OK) {
+        tsrc_model_free(m);
+        return rc;
+    }
+    *out = m;
+    return TSRC_OK;
+}
+
+int tsrc_model_weight(const tsrc_model* m, uint32_t layer, uint32_t which, tsrc_weight** out) {
+    if (!m || !out) return TSRC_E_ARG;
+    *out = nullptr;
+    if (layer == TSRC_MODEL_GLOBAL) {
+        if (which == 0u) *out = m->tok_embd;
+        else if (which == 1u) *out = m->c.tied_head ? m->tok_embd : m->output;
+        return *out ? TSRC_OK : TSRC_E_ARG;
+    }
+    if (layer >= m->c.n_layer || which > 6u) return TSRC_E_ARG;
+    const tsrc_model::Layer& L = m->layers[layer];
+    tsrc_weight* ws[] = {L.wq, L.wk, L.wv, L.wo, L.wg, L.wu, L.wd};
+    *out = ws[which];
+    return TSRC_OK;
+}
+
+int tsrc_model_params(const tsrc_model* m, float* ts, float* kq_scale) {
+    if (!m) return TSRC_E_ARG;
+    if (ts) *ts = m->ts;
+    if (kq_scale) *kq_scale = m->kq_scale;
+    return TSRC_OK;
+}
+
+int tsrc_model_forward(tsrc_model* m, const int32_t* ids, uint32_t T, uint32_t pos0, float* logits, void* stream) {
+    if (!m || !ids || !logits || T == 0) return TSRC_E_ARG;
+    const tsrc_model_cfg& c = m->c;
+    if ((uint64_t)pos0 + T > c.n_ctx) return TSRC_E_ARG;
+    tsrc_ctx* ctx = m->ctx;
+    const uint32_t E = c.n_embd, D = c.head_dim, Hq = c.n_head * D, Hkv = c.n_head_kv * D, F = c.n_ff;
+    if (T > m->t_alloc) {
+        cudaDeviceSynchronize();
+        cudaFree(m->buf);
+        m->buf = nullptr;
+        const size_t per = 2u * E + Hq + 2u * Hkv + Hq + 2u * F;
+        if (cudaMalloc(&m->buf, per * T * sizeof(float)) != cudaSuccess) {
+            m->t_alloc = 0;
+            return TSRC_E_NOMEM;
+        }
+        m->t_alloc = T;
+        float* p = m->buf;
+        m->x = p; p += (size_t)E * T;
+        m->h = p; p += (size_t)E * T;
+        m->q = p; p += (size_t)Hq * T;
+        m->k = p; p += (size_t)Hkv * T;
+        m->v = p; p += (size_t)Hkv * T;
+        m->att = p; p += (size_t)Hq * T;
+        m->g = p; p += (size_t)F * T;
+        m->u = p;
+    }
+    const uint32_t n_kv = pos0 + T;
+    const uint16_t* mask = nullptr;
+    if (T > 1) {                                          // causal: token t sees cells [0, pos0 + t]
+        m->mask.assign((size_t)T * n_kv, 0xFC00u);
+        for (uint32_t t = 0; t < T; ++t)
+            std::fill(m->mask.begin() + (size_t)t * n_kv, m->mask.begin() + (size_t)t * n_kv + pos0 + t + 1u, (uint16_t)0u);
+        mask = m->mask.data();
+    }
+    const float inv_n = 1.0f / (float)E;
+    const int32_t* pos = m->pos + pos0;
+    tsrc_fa_cfg fa = c.fa;
+    if (fa.C == 0) fa = tsrc_fa_cfg{4u, 4u, 9344u, 32768u, 0u};
+    int rc = tsrc_get_rows(ctx, m->tok_embd, ids, T, m->x, E, stream);
+#define TSRC_M(call) \
+    if (rc == TSRC_OK) rc = (call)
+    for (uint32_t l = 0; l < c.n_layer; ++l) {
+        const tsrc_model::Layer& L = m->layers[l];
+        TSRC_M(tsrc_rms_norm(ctx, m->x, E, m->h, E, L.attn_norm, E, T, c.rms_eps, inv_n, stream));
+        TSRC_M(tsrc_mul_mat(ctx, L.wq, m->h, T, E, m->q, Hq, L.bq, 0, L.bq ? TSRC_MM_ADD : 0u, 1.0f, 1.0f, stream));
+        TSRC_M(tsrc_mul_mat(ctx, L.wk, m->h, T, E, m->k, Hkv, L.bk, 0, L.bk ? TSRC_MM_ADD : 0u, 1.0f, 1.0f, stream));
+        TSRC_M(tsrc_mul_mat(ctx, L.wv, m->h, T, E, m->v, Hkv, L.bv, 0, L.bv ? TSRC_MM_ADD : 0u, 1.0f, 1.0f, stream));
+        TSRC_M(tsrc_rope(ctx, m->q, Hq, m->q, Hq, pos, T, c.n_head, D, D, c.rope_mode, m->ts, 1.0f, stream));
+        TSRC_M(tsrc_rope(ctx, m->k, Hkv, m->k, Hkv, pos, T, c.n_head_kv, D, D, c.rope_mode, m->ts, 1.0f, stream));
+        TSRC_M(tsrc_kv_set_rows(ctx, L.kv, TSRC_KV_K, m->k, T, Hkv, nullptr, pos0, stream));
+        TSRC_M(tsrc_kv_set_rows(ctx, L.kv, TSRC_KV_V, m->v, T, Hkv, nullptr, pos0, stream));
+        TSRC_M(tsrc_flash_attn(ctx, L.kv, m->q, T, c.n_head, n_kv, mask, n_kv, m->kq_scale, pos0, n_kv, &fa, m->att, stream));
+        TSRC_M(tsrc_mul_mat(ctx, L.wo, m->att, T, Hq, m->x, E, m->x, E, TSRC_MM_ADD, 1.0f, 1.0f, stream));
+        TSRC_M(tsrc_rms_norm(ctx, m->x, E, m->h, E, L.ffn_norm, E, T, c.rms_eps, inv_n, stream));
+        TSRC_M(tsrc_mul_mat(ctx, L.wg, m->h, T, E, m->g, F, nullptr, 0, 0u, 1.0f, 1.0f, stream));
+        TSRC_M(tsrc_mul_mat(ctx, L.wu, m->h, T, E, m->u, F, nullptr, 0, 0u, 1.0f, 1.0f, stream));
+        TSRC_M(tsrc_vop(ctx, TSRC_VOP_SWIGLU, m->g, F, m->u, F, m->g, F, F, T, stream));
+        TSRC_M(tsrc_mul_mat(ctx, L.wd, m->g, T, F, m->x, E, m->x, E, TSRC_MM_ADD, 1.0f, 1.0f, stream));
+    }
+    // the last token: output norm and head
+    const float* xl = m->x + (size_t)(T - 1u) * E;
+    TSRC_M(tsrc_rms_norm(ctx, xl, E, m->h, E, m->out_norm, E, 1, c.rms_eps, inv_n, stream));
+    TSRC_M(tsrc_mul_mat(ctx, c.tied_head ? m->tok_embd : m->output, m->h, 1, E, logits, c.n_vocab, nullptr, 0, 0u, 1.0f, 1.0f,
+                        stream));
+#undef TSRC_M
+    return set_err(rc);
+}
+
+}  // extern "C"

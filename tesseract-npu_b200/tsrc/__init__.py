@@ -57,6 +57,12 @@ _SIGS = {
     "tsrc_weight_free": (_i, [_p]),
     "tsrc_mul_mat": (_i, [_p, _p, _p, _u32, _u32, _p, _u32, _p, _u32, _u32, _f32, _f32, _p]),
     "tsrc_rms_norm": (_i, [_p, _p, _u32, _p, _u32, _p, _u32, _u32, _f32, _f32, _p]),
+    "tsrc_model_create": (_i, [_p, _p, _u64, ct.POINTER(_p)]),
+    "tsrc_model_free": (_i, [_p]),
+    "tsrc_model_forward": (_i, [_p, _p, _u32, _u32, _p, _p]),
+    "tsrc_model_weight": (_i, [_p, _u32, _u32, ct.POINTER(_p)]),
+    "tsrc_model_params": (_i, [_p, ct.POINTER(_f32), ct.POINTER(_f32)]),
+    "tsrc_model_f32_value": (_f32, [_u64, _u32, _u32, _u32]),
     "tsrc_rope": (_i, [_p, _p, _u32, _p, _u32, _p, _u32, _u32, _u32, _u32, _u32, _f32, _f32, _p]),
     "tsrc_vop": (_i, [_p, _u32, _p, _u32, _p, _u32, _p, _u32, _u32, _u32, _p]),
     "tsrc_get_rows": (_i, [_p, _p, _p, _u32, _p, _u32, _p]),
@@ -85,6 +91,14 @@ class FaCfg(ct.Structure):
     _fields_ = [("C", _u32), ("t_max", _u32), ("pcap", _u32), ("k_max", _u32), ("plan_n_head_kv", _u32)]
 
 
+class ModelCfg(ct.Structure):
+    """tsrc_model_cfg: the shape of a random-init decoder (llama / qwen2 graph)."""
+    _fields_ = [(n, _u32) for n in ("n_layer", "n_embd", "n_ff", "n_head", "n_head_kv", "head_dim", "n_vocab", "fmt",
+                                   "rope_mode")] + [("rope_base", _f32), ("rms_eps", _f32)] + \
+               [(n, _u32) for n in ("qkv_bias", "tied_head", "n_ctx")] + [("fa", FaCfg)]
+
+
+MODEL_GLOBAL = 0xFFFFFFFF
 KV_K, KV_V = 0, 1
 TEAM_HANDLE_BYTES = 64
 Q8_0_BLOCK_BYTES = 34
@@ -328,6 +342,38 @@ class Weight:
     def free(self) -> None:
         if self.handle and self.dev.handle:
             _check(lib().tsrc_weight_free(self.handle))
+        self.handle = None
+
+
+class Model:
+    """A random-init decoder on the device (tsrc_model_*)."""
+
+    def __init__(self, dev: Device, cfg: ModelCfg, seed: int):
+        h = _p()
+        self.dev, self.cfg, self.seed = dev, cfg, seed
+        _check(lib().tsrc_model_create(dev.handle, ct.byref(cfg), seed, ct.byref(h)))
+        self.handle = h
+        ts, ks = _f32(), _f32()
+        _check(lib().tsrc_model_params(h, ct.byref(ts), ct.byref(ks)))
+        self.ts, self.kq_scale = ts.value, ks.value
+
+    def forward(self, ids, T: int, pos0: int, logits, stream=None) -> None:
+        _check(lib().tsrc_model_forward(self.handle, _addr(ids), T, pos0, _addr(logits), _stream(stream)))
+
+    def weight(self, layer: int, which: int) -> "Weight":
+        h = _p()
+        _check(lib().tsrc_model_weight(self.handle, layer, which, ct.byref(h)))
+        w = Weight(self.dev, h)
+        w.free = lambda: None                       # owned by the model
+        return w
+
+    def f32_vector(self, layer: int, which: int, n: int):
+        f = lib().tsrc_model_f32_value
+        return np.array([f(self.seed, layer, which, i) for i in range(n)], np.float32)
+
+    def free(self) -> None:
+        if self.handle and self.dev.handle:
+            _check(lib().tsrc_model_free(self.handle))
         self.handle = None
 
 
