@@ -38,6 +38,8 @@ CONFIGS = {
     "cfg3": (None, None, None, 301, 303, "BASELINE config 3: flash-attention decode over a q8_0 KV cache, "
              "32 q / 8 kv heads, head_dim 128, 8192 cells, one token"),
 }
+CONFIGS["cfg4"] = (None, None, None, 41, 42, "BASELINE config 4: Qwen2.5-0.5B architecture (random-init, Q8_0), decode")
+CONFIGS["cfg5"] = (None, None, None, 51, 52, "BASELINE config 5: Llama-3-8B architecture (random-init, Q4_K), decode")
 METRIC = "Q8_0/Q4_K matvec HBM GB/s"
 FA = dict(D=128, n_head_kv=8, G=4, n_kv=8192)
 
@@ -100,6 +102,140 @@ def prefill_measure(dev, tsrc, torch, reps=10, warmup=3):
             "peak_kind": "2x measured bf16 dense (MEASURED_PEAKS.json)" if peak else None,
             "note": "the reference's per-32-value f32 scale-and-accumulate runs on the CUDA cores; ncu tensor-pipe "
                     "activity in profiles/mm_tc_prefill.md"}
+
+
+# end-to-end random-init models (BASELINE configs 4 and 5): decode tokens/s
+MODELS = {
+    "cfg4": dict(desc="BASELINE config 4: Qwen2.5-0.5B architecture, random-init, all Q8_0, 512-token prefill then decode",
+                 shape=dict(n_layer=24, n_embd=896, n_ff=4864, n_head=14, n_head_kv=2, head_dim=64, n_vocab=151936, fmt=0,
+                            rope_mode=1, rope_base=1e6, rms_eps=1e-6, qkv_bias=1, tied_head=1),
+                 prompt=512, decode=128, seed=41),
+    "cfg5": dict(desc="BASELINE config 5: Llama-3-8B architecture, random-init, all Q4_K, 2048-token prefill then decode",
+                 shape=dict(n_layer=32, n_embd=4096, n_ff=14336, n_head=32, n_head_kv=8, head_dim=128, n_vocab=128256, fmt=1,
+                            rope_mode=0, rope_base=500000.0, rms_eps=1e-5, qkv_bias=0, tied_head=0),
+                 prompt=2048, decode=256, seed=51),
+}
+
+
+def model_row_bytes(fmt, N, K):
+    return N * (K // 32 * 34 if fmt == 0 else K // 256 * 144)
+
+
+def model_algo_bytes(s, n_kv):
+    """Bytes one decode token must read: every layer's seven matrices, the K / V cells it attends
+    (q8_0, 34 B per 32 values), the head, and the token's embedding row."""
+    fmt, E, D, F = s["fmt"], s["n_embd"], s["head_dim"], s["n_ff"]
+    Hq, Hkv = s["n_head"] * D, s["n_head_kv"] * D
+    layer = (model_row_bytes(fmt, Hq, E) + 2 * model_row_bytes(fmt, Hkv, E) + model_row_bytes(fmt, E, Hq)
+             + 2 * model_row_bytes(fmt, F, E) + model_row_bytes(fmt, E, F))
+    kv = 2 * n_kv * (Hkv // 32) * 34
+    return s["n_layer"] * (layer + kv) + model_row_bytes(fmt, s["n_vocab"], E) + model_row_bytes(fmt, 1, E)
+
+
+def model_measure(dev, tsrc, torch, name, steps, warmup, e2e_steps=32):
+    """Prefill of the config's prompt, then `warmup` + `steps` timed decode tokens (CUDA events on
+    the stream, inputs resident) and `e2e_steps` decode tokens with the token id copied in from
+    pinned host memory and the logits read back every step. Returns a dict and the model (for the
+    CPU sample's weights); the caller frees the model."""
+    spec = MODELS[name]
+    prompt = spec["prompt"]
+    n_ctx = prompt + warmup + steps + e2e_steps
+    s = dict(spec["shape"], n_ctx=n_ctx)
+    model = tsrc.Model(dev, tsrc.ModelCfg(**s), seed=spec["seed"])
+    g = torch.Generator(device="cuda")
+    g.manual_seed(spec["seed"])
+    ids = torch.randint(0, s["n_vocab"], (n_ctx,), dtype=torch.int32, device="cuda", generator=g)
+    logits = torch.empty(s["n_vocab"], device="cuda")
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record()
+    model.forward(ids, prompt, 0, logits)
+    e1.record()
+    torch.cuda.synchronize()
+    prefill_ms = e0.elapsed_time(e1)
+    pos = prompt
+    for _ in range(warmup):
+        model.forward(ids[pos:], 1, pos, logits)
+        pos += 1
+    torch.cuda.synchronize()
+    kv0 = pos
+    e0.record()
+    for _ in range(steps):
+        model.forward(ids[pos:], 1, pos, logits)
+        pos += 1
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    host_ids = ids[pos:pos + e2e_steps].cpu().pin_memory()
+    host_logits = torch.empty(s["n_vocab"], pin_memory=True)
+    one = torch.empty(1, dtype=torch.int32, device="cuda")
+    torch.cuda.synchronize()
+    e0.record()
+    for i in range(e2e_steps):
+        one.copy_(host_ids[i:i + 1], non_blocking=True)
+        model.forward(one, 1, pos, logits)
+        host_logits.copy_(logits, non_blocking=True)
+        pos += 1
+    e1.record()
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / e2e_steps
+    algo = model_algo_bytes(s, kv0 + steps // 2)
+    launches = 3 + 16 * s["n_layer"]
+    return dict(shape=s, prefill_ms=prefill_ms, ms=ms, e2e_ms=e2e_ms, algo_bytes=algo, launches=launches,
+                n_kv=(kv0, pos)), model
+
+
+def cpu_reference_model(name, threads, model=None):
+    """One decode token of the config on the host cores with the oracle's composition of the graph
+    (the reference's kinds): one layer at the config's KV length (synthetic q8_0 cache rows) plus
+    the head, the layer time scaled to all layers. Weights: the device model's rows when given, else
+    quantized on the host from seeded normals. Returns (tokens/s, kind, sample text)."""
+    import numpy as np
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle
+    tsro = oracle.Tsro()
+    spec = MODELS[name]
+    prompt = spec["prompt"]
+    s = dict(spec["shape"], n_ctx=prompt + 1)
+    fmt, E, D, F, V = s["fmt"], s["n_embd"], s["head_dim"], s["n_ff"], s["n_vocab"]
+    Hq, Hkv = s["n_head"] * D, s["n_head_kv"] * D
+    rng = np.random.default_rng(spec["seed"])
+    names = ("wq", "wk", "wv", "wo", "wg", "wu", "wd")
+    shapes = ((Hq, E), (Hkv, E), (Hkv, E), (E, Hq), (F, E), (F, E), (E, F))
+    if model is not None:
+        L = {n: model.weight(0, i).download() for i, n in enumerate(names)}
+        head = model.weight(0xFFFFFFFF, 1).download()
+        emb = model.weight(0xFFFFFFFF, 0).download()[:16]
+        src = "the device model's layer-0 and head rows"
+    else:
+        L = {n: tsro.quantize(fmt, (rng.standard_normal(sh, dtype=np.float32) * np.float32(0.02))) for n, sh in zip(names, shapes)}
+        head = tsro.quantize(fmt, rng.standard_normal((V, E), dtype=np.float32) * np.float32(0.02))
+        emb = head[:16]
+        src = "host-quantized seeded N(0, 0.02) rows"
+    L["attn_norm"] = np.ones(E, np.float32)
+    L["ffn_norm"] = np.ones(E, np.float32)
+    if s["qkv_bias"]:
+        L["bq"], L["bk"], L["bv"] = np.zeros(Hq, np.float32), np.zeros(Hkv, np.float32), np.zeros(Hkv, np.float32)
+    ts = float(np.power(np.float32(s["rope_base"]), np.float32(-2.0) / np.float32(D), dtype=np.float32))
+    om = oracle.OracleModel(tsro, dict(s, n_layer=1), [L], emb, head, np.ones(E, np.float32), ts,
+                            float(np.float32(1.0) / np.sqrt(np.float32(D))), threads=threads)
+    kv = tsro.quantize(0, rng.standard_normal((prompt, Hkv), dtype=np.float32))
+    om.kc[0][:prompt] = kv
+    om.vc[0][:prompt] = kv[::-1]
+    x1 = np.zeros((1, E), np.float32)
+    t0 = time.perf_counter()
+    om.forward(np.array([3], np.int32), prompt)
+    t_fwd = time.perf_counter() - t0
+    t0 = time.perf_counter()
+    tsro.matvec(fmt, head, E, x1, threads=threads)
+    t_head = time.perf_counter() - t0
+    t_layer = max(t_fwd - t_head, 1e-9)
+    t_tok = s["n_layer"] * t_layer + t_head
+    kind = "port"
+    sample = (f"one decode token at KV length {prompt}: layer 0 timed ({t_layer * 1e3:.1f} ms) x {s['n_layer']} layers "
+              f"+ head ({t_head * 1e3:.1f} ms); {src}; oracle composition of the reference's kinds, {threads} host threads "
+              f"for the MUL_MATs")
+    return 1.0 / t_tok, kind, sample
 
 
 def fa_algo_bytes(n_head_kv, D, G, n_kv):
@@ -416,11 +552,76 @@ def run_fa(args):
     return 0
 
 
+def run_model(args):
+    """--config cfg4 / cfg5: end-to-end decode tokens/s of the random-init model on one GPU."""
+    import torch
+    import tsrc
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if world > 1:
+        if rank == 0:
+            print(json.dumps({"metric": "decode tokens/s", "unavailable": "the model runner is single-GPU (tensor-parallel "
+                              "model not built); the matvec and FA configs shard across GPUs"}), flush=True)
+        return 0
+    spec = MODELS[args.config]
+    args.warmup = min(args.warmup, 8)                      # decode tokens before timing (>= 3)
+    steps = max(1, min(args.steps, spec["decode"] - args.warmup))
+    torch.cuda.set_device(0)
+    dev = tsrc.Device(0)
+    with Clocks(0) as clk:
+        r, model = model_measure(dev, tsrc, torch, args.config, steps, args.warmup)
+    clocks = clk.summary()
+    cpu = None
+    if args.cpu_seconds > 0:
+        threads = len(os.sched_getaffinity(0))
+        tps, kind, sample = cpu_reference_model(args.config, threads, model)
+        cpu = {"value": round(tps, 4), "unit": "tokens/s", "cores": threads, "kind": kind, "sample": sample}
+    model.free()
+    dev.close()
+    peak, peak_kind = peaks()
+    s = r["shape"]
+    achieved = r["algo_bytes"] / (r["ms"] * 1e-3) / 1e9
+    line = {
+        "metric": "decode tokens/s", "value": round(1e3 / r["ms"], 2), "unit": "tokens/s", "n_gpus": 1, "steps": steps,
+        "warmup": args.warmup, "ms_per_step": round(r["ms"], 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "int8",
+        "data": "synthetic (random-init weights quantized on device, random token ids)",
+        "config": {"workload": spec["desc"], "prompt_tokens": spec["prompt"], "kv_cells_during_timing": list(r["n_kv"]),
+                   "l2": "inputs larger than L2 (every decode token reads all weights: "
+                         f"{r['algo_bytes'] / 1e6:.0f} MB)", "cuda_graph": False,
+                   "prefill_ms": round(r["prefill_ms"], 2),
+                   "prefill_tokens_per_s": round(spec["prompt"] / (r["prefill_ms"] * 1e-3), 1)},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4),
+                     "traffic": None, "peak_kind": peak_kind, "kernel": "whole decode step (all kernels)",
+                     "algorithmic_bytes_per_step": r["algo_bytes"]},
+        "e2e": {"value": round(1e3 / r["e2e_ms"], 2), "unit": "tokens/s", "h2d_bytes_per_step": 4,
+                "d2h_bytes_per_step": 4 * s["n_vocab"], "ms_per_step": round(r["e2e_ms"], 4)},
+        "gpu_launches": r["launches"] * steps,
+        "clocks": clocks,
+        "cpu_baseline": cpu,
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def run_reference(args, cfg):
     """--impl reference: the reference's own CPU implementation of the path, rank 0 only."""
     import numpy as np
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
+        return 0
+    if args.config in MODELS:
+        threads = len(os.sched_getaffinity(0))
+        tps, kind, sample = cpu_reference_model(args.config, threads)
+        line = {
+            "impl": "reference", "metric": "decode tokens/s", "value": round(tps, 4), "unit": "tokens/s", "n_gpus": args.gpus,
+            "steps": 1, "warmup": 0, "ms_per_step": round(1e3 / tps, 2), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "int8", "data": "synthetic (seeded weights quantized on the host)",
+            "config": {"workload": MODELS[args.config]["desc"], "host_threads": threads},
+            "cpu_baseline": {"value": round(tps, 4), "unit": "tokens/s", "cores": threads, "kind": kind, "sample": sample},
+            "e2e": {"value": round(tps, 4), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        }
+        print(json.dumps(line), flush=True)
         return 0
     if args.config == "cfg3":
         threads = len(os.sched_getaffinity(0))
@@ -491,6 +692,7 @@ def main():
     ap.add_argument("--no-graph", action="store_true")
     ap.add_argument("--no-fa", action="store_true", help="skip the config-3 FA summary in the default line")
     ap.add_argument("--no-prefill", action="store_true", help="skip the tensor-core prefill summary in the default line")
+    ap.add_argument("--no-model", action="store_true", help="skip the config 4 / 5 decode summaries in the default line")
     ap.add_argument("--collective", default="p2p", choices=["p2p", "nccl"],
                     help="N > 1 matvec: all-gather fused into the kernel (P2P stores) or an NCCL all_gather")
     args = ap.parse_args()
@@ -500,6 +702,8 @@ def main():
         return run_reference(args, cfg)
     if args.config == "cfg3":
         return run_fa(args)
+    if args.config in MODELS:
+        return run_model(args)
 
     import numpy as np
     import torch
@@ -652,6 +856,23 @@ def main():
 
     if world == 1 and not args.no_prefill:
         also["prefill"] = prefill_measure(dev, tsrc, torch)
+    if world == 1 and not args.no_model:
+        for name in ("cfg5", "cfg4"):
+            try:
+                r, model = model_measure(dev, tsrc, torch, name, 64, 3, e2e_steps=16)
+                entry = {"metric": "decode tokens/s", "workload": MODELS[name]["desc"], "value": round(1e3 / r["ms"], 2),
+                         "unit": "tokens/s", "ms_per_token": round(r["ms"], 4), "steps": 64,
+                         "e2e_tokens_per_s": round(1e3 / r["e2e_ms"], 2),
+                         "prefill_tokens_per_s": round(MODELS[name]["prompt"] / (r["prefill_ms"] * 1e-3), 1),
+                         "hbm_frac": round(r["algo_bytes"] / (r["ms"] * 1e-3) / 1e9 / peaks()[0], 4),
+                         "full_line": f"python bench.py --config {name}"}
+                if rank == 0 and args.cpu_seconds > 0:
+                    tps, kind, sample = cpu_reference_model(name, len(os.sched_getaffinity(0)), model)
+                    entry["cpu_baseline"] = {"value": round(tps, 4), "unit": "tokens/s", "kind": kind, "sample": sample}
+                model.free()
+            except Exception as e:  # noqa: BLE001
+                entry = {"error": str(e)[:300]}
+            also[f"decode_{name}"] = entry
 
     traffic = None
     prof = os.path.join(ROOT, "profiles", f"traffic_{args.config}.json")

@@ -34,6 +34,18 @@ int fail(int code, const char* fmt, ...) {
     return code;
 }
 
+}  // namespace
+
+namespace tsrc {
+// the C ABI's error record, for the library's other translation units (the model runner)
+int api_fail(int code, const char* msg) {
+    g_err = msg;
+    return code;
+}
+}  // namespace tsrc
+
+namespace {
+
 int cuda_fail(cudaError_t e, const char* what) {
     return fail(TSRC_E_CUDA, "%s: %s (%s)", what, cudaGetErrorString(e), cudaGetErrorName(e));
 }

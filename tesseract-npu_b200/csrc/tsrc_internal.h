@@ -56,6 +56,9 @@ cudaError_t launch_vop(uint32_t func, const float* a, uint32_t as, const float* 
 cudaError_t launch_get_rows(uint32_t fmt, const uint8_t* qs, const void* meta, uint32_t n_rows, uint32_t K, const int32_t* ids,
                             uint32_t T, float* y, uint32_t ys, cudaStream_t st);
 cudaError_t vu_error(uint32_t* code, bool clear);
+
+// records msg as the C ABI's last error and returns code (tsrc_api.cu)
+int api_fail(int code, const char* msg);
 cudaError_t tc_error(uint32_t* code, bool clear);
 size_t mv_smem_bytes(uint32_t fmt, uint32_t K, uint32_t T);
 // The first error code any matvec launch recorded on the current device (0 = none).

@@ -46,7 +46,6 @@ uint64_t splitmix64(uint64_t z) {
     return z ^ (z >> 31);
 }
 
-int set_err(int rc) { return rc; }
 
 // f32 vector kinds of the model (tsrc_model_f32_value)
 constexpr uint32_t kVecAttnNorm = 0, kVecFfnNorm = 1, kVecBq = 2, kVecBk = 3, kVecBv = 4, kVecOutNorm = 5;
@@ -80,12 +79,12 @@ int tsrc_model_free(tsrc_model* m) {
 }
 
 int tsrc_model_create(tsrc_ctx* ctx, const tsrc_model_cfg* cfg, uint64_t seed, tsrc_model** out) {
-    if (!ctx || !cfg || !out) return TSRC_E_ARG;
+    if (!ctx || !cfg || !out) return tsrc::api_fail(TSRC_E_ARG, "tsrc_model_create: NULL argument");
     *out = nullptr;
     const tsrc_model_cfg& c = *cfg;
     if (c.n_layer == 0 || c.n_embd == 0 || c.n_ff == 0 || c.n_head == 0 || c.n_head_kv == 0 || c.n_head % c.n_head_kv ||
         c.n_vocab == 0 || c.n_ctx == 0 || (c.fmt != TSRC_FMT_Q8_0 && c.fmt != TSRC_FMT_Q4_K) || c.rope_mode > TSRC_ROPE_NEOX)
-        return TSRC_E_ARG;
+        return tsrc::api_fail(TSRC_E_ARG, "tsrc_model_create: a shape field is zero or out of range");
     tsrc_model* m = new tsrc_model();
     m->ctx = ctx;
     m->c = c;
@@ -149,14 +148,14 @@ int tsrc_model_create(tsrc_ctx* ctx, const tsrc_model_cfg* cfg, uint64_t seed, t
 }
 
 int tsrc_model_weight(const tsrc_model* m, uint32_t layer, uint32_t which, tsrc_weight** out) {
-    if (!m || !out) return TSRC_E_ARG;
+    if (!m || !out) return tsrc::api_fail(TSRC_E_ARG, "tsrc_model_weight: NULL argument");
     *out = nullptr;
     if (layer == TSRC_MODEL_GLOBAL) {
         if (which == 0u) *out = m->tok_embd;
         else if (which == 1u) *out = m->c.tied_head ? m->tok_embd : m->output;
         return *out ? TSRC_OK : TSRC_E_ARG;
     }
-    if (layer >= m->c.n_layer || which > 6u) return TSRC_E_ARG;
+    if (layer >= m->c.n_layer || which > 6u) return tsrc::api_fail(TSRC_E_ARG, "tsrc_model_weight: no such weight");
     const tsrc_model::Layer& L = m->layers[layer];
     tsrc_weight* ws[] = {L.wq, L.wk, L.wv, L.wo, L.wg, L.wu, L.wd};
     *out = ws[which];
@@ -171,9 +170,9 @@ int tsrc_model_params(const tsrc_model* m, float* ts, float* kq_scale) {
 }
 
 int tsrc_model_forward(tsrc_model* m, const int32_t* ids, uint32_t T, uint32_t pos0, float* logits, void* stream) {
-    if (!m || !ids || !logits || T == 0) return TSRC_E_ARG;
+    if (!m || !ids || !logits || T == 0) return tsrc::api_fail(TSRC_E_ARG, "tsrc_model_forward: NULL argument or T = 0");
     const tsrc_model_cfg& c = m->c;
-    if ((uint64_t)pos0 + T > c.n_ctx) return TSRC_E_ARG;
+    if ((uint64_t)pos0 + T > c.n_ctx) return tsrc::api_fail(TSRC_E_ARG, "tsrc_model_forward: positions beyond n_ctx");
     tsrc_ctx* ctx = m->ctx;
     const uint32_t E = c.n_embd, D = c.head_dim, Hq = c.n_head * D, Hkv = c.n_head_kv * D, F = c.n_ff;
     if (T > m->t_alloc) {
@@ -183,7 +182,7 @@ int tsrc_model_forward(tsrc_model* m, const int32_t* ids, uint32_t T, uint32_t p
         const size_t per = 2u * E + Hq + 2u * Hkv + Hq + 2u * F;
         if (cudaMalloc(&m->buf, per * T * sizeof(float)) != cudaSuccess) {
             m->t_alloc = 0;
-            return TSRC_E_NOMEM;
+            return tsrc::api_fail(TSRC_E_NOMEM, "tsrc_model_forward: activation buffers");
         }
         m->t_alloc = T;
         float* p = m->buf;
@@ -235,7 +234,7 @@ int tsrc_model_forward(tsrc_model* m, const int32_t* ids, uint32_t T, uint32_t p
     TSRC_M(tsrc_mul_mat(ctx, c.tied_head ? m->tok_embd : m->output, m->h, 1, E, logits, c.n_vocab, nullptr, 0, 0u, 1.0f, 1.0f,
                         stream));
 #undef TSRC_M
-    return set_err(rc);
+    return rc;
 }
 
 }  // extern "C"
