@@ -180,7 +180,7 @@ def model_measure(dev, tsrc, torch, name, steps, warmup, e2e_steps=32):
     torch.cuda.synchronize()
     e2e_ms = e0.elapsed_time(e1) / e2e_steps
     algo = model_algo_bytes(s, kv0 + steps // 2)
-    launches = 3 + 16 * s["n_layer"]
+    launches = 3 + 11 * s["n_layer"]
     return dict(shape=s, prefill_ms=prefill_ms, ms=ms, e2e_ms=e2e_ms, algo_bytes=algo, launches=launches,
                 n_kv=(kv0, pos)), model
 
@@ -200,8 +200,8 @@ def cpu_reference_model(name, threads, model=None):
     fmt, E, D, F, V = s["fmt"], s["n_embd"], s["head_dim"], s["n_ff"], s["n_vocab"]
     Hq, Hkv = s["n_head"] * D, s["n_head_kv"] * D
     rng = np.random.default_rng(spec["seed"])
-    names = ("wq", "wk", "wv", "wo", "wg", "wu", "wd")
-    shapes = ((Hq, E), (Hkv, E), (Hkv, E), (E, Hq), (F, E), (F, E), (E, F))
+    names = ("wqkv", "wo", "wgu", "wd")
+    shapes = ((Hq + 2 * Hkv, E), (E, Hq), (2 * F, E), (E, F))
     if model is not None:
         L = {n: model.weight(0, i).download() for i, n in enumerate(names)}
         head = model.weight(0xFFFFFFFF, 1).download()
@@ -215,7 +215,7 @@ def cpu_reference_model(name, threads, model=None):
     L["attn_norm"] = np.ones(E, np.float32)
     L["ffn_norm"] = np.ones(E, np.float32)
     if s["qkv_bias"]:
-        L["bq"], L["bk"], L["bv"] = np.zeros(Hq, np.float32), np.zeros(Hkv, np.float32), np.zeros(Hkv, np.float32)
+        L["bqkv"] = np.zeros(Hq + 2 * Hkv, np.float32)
     ts = float(np.power(np.float32(s["rope_base"]), np.float32(-2.0) / np.float32(D), dtype=np.float32))
     om = oracle.OracleModel(tsro, dict(s, n_layer=1), [L], emb, head, np.ones(E, np.float32), ts,
                             float(np.float32(1.0) / np.sqrt(np.float32(D))), threads=threads)

@@ -288,8 +288,8 @@ typedef struct tsrc_model_cfg {
 #define TSRC_MODEL_GLOBAL 0xFFFFFFFFu   // tsrc_model_weight layer: which 0 = token embedding, 1 = head
 
 // Weights from tsrc_weight_synth(seed * 1000 + 1 / + 2 for the embedding / head; seed * 1000 +
-// 16 (l + 1) + i for layer l's q, k, v, o, gate, up, down, sigma 0.02); f32 vectors from
-// tsrc_model_f32_value.
+// 16 (l + 1) + i for layer l's i = 0 [q | k | v] rows, 1 o, 2 [gate | up] rows, 3 down; sigma 0.02);
+// f32 vectors from tsrc_model_f32_value.
 TSRC_API int tsrc_model_create(tsrc_ctx * ctx, const tsrc_model_cfg * cfg, uint64_t seed, tsrc_model ** out);
 TSRC_API int tsrc_model_free(tsrc_model * m);
 // Runs tokens ids[0..T) (device int32) at positions pos0 .. pos0 + T - 1: their K / V rows are stored
@@ -297,13 +297,14 @@ TSRC_API int tsrc_model_free(tsrc_model * m);
 // receives the head output of the last token. Queued on `stream`.
 TSRC_API int tsrc_model_forward(tsrc_model * m, const int32_t * ids, uint32_t T, uint32_t pos0, float * logits,
                                 void * stream);
-// The model's weight handles (owned by the model): layer < n_layer, which 0..6 = q, k, v, o, gate,
-// up, down; or TSRC_MODEL_GLOBAL.
+// The model's weight handles (owned by the model): layer < n_layer, which 0 = the q, k, v rows
+// stacked (n_head + 2 n_head_kv heads), 1 = o, 2 = the gate and up rows stacked (2 n_ff), 3 = down;
+// or TSRC_MODEL_GLOBAL.
 TSRC_API int tsrc_model_weight(const tsrc_model * m, uint32_t layer, uint32_t which, tsrc_weight ** out);
 // The host-computed ROPE theta scale and attention scale the model passes to the kinds.
 TSRC_API int tsrc_model_params(const tsrc_model * m, float * ts, float * kq_scale);
-// f32 vector element i of the model: which 0 attn_norm, 1 ffn_norm, 2 / 3 / 4 q / k / v bias (layer
-// l), 5 output norm (layer = n_layer): splitmix64 of (seed, layer, which, i) -> 1 + 0.25 u for the
+// f32 vector element i of the model: which 0 attn_norm, 1 ffn_norm, 2 the q | k | v bias (layer l),
+// 5 output norm (layer = n_layer): splitmix64 of (seed, layer, which, i) -> 1 + 0.25 u for the
 // norms, 0.1 u for the biases, u uniform in [-1, 1) on 24 bits.
 TSRC_API float tsrc_model_f32_value(uint64_t seed, uint32_t layer, uint32_t which, uint32_t i);
 

@@ -419,9 +419,11 @@ class Ref:
 
 class OracleModel:
     """CPU composition of the decoder graph (llama / qwen2 layers) over the oracle's kinds, in the
-    order tsrc_model_forward runs them: GET_ROWS, RMS_NORM + MUL, MUL_MAT (+ bias), ROPE, KVST into
-    ggml q8_0 cache rows, FA, MUL_MAT + residual, RMS_NORM + MUL, gate / up, SWIGLU, down + residual,
-    output norm and head of the last token. Test and baseline infrastructure only."""
+    order tsrc_model_forward runs them: GET_ROWS, RMS_NORM + MUL, MUL_MAT of the stacked q | k | v rows
+    (+ bias), ROPE, KVST into ggml q8_0 cache rows, FA, MUL_MAT + residual, RMS_NORM + MUL, the stacked
+    gate | up rows, SWIGLU, down + residual, output norm and head of the last token. A layer dict holds
+    wqkv, wo, wgu, wd (ggml rows), attn_norm, ffn_norm and optionally bqkv. Test and baseline
+    infrastructure only."""
 
     def __init__(self, tsro: "Tsro", cfg: dict, layers: list, emb, head, out_norm, ts: float, kq_scale: float,
                  threads: int | None = None):
@@ -448,13 +450,14 @@ class OracleModel:
         x = o.dequant(fmt, self.emb[ids], E)
         th = self.threads
         rope = dict(head_dim=D, n_dims=D, mode=c["rope_mode"], ts=self.ts)
+        Hkv = nkv * D
         for li, L in enumerate(self.layers):
             h = o.rms_norm(x, L["attn_norm"], c["rms_eps"], inv_n)
-            q = o.matvec(fmt, L["wq"], E, h, add=None if L.get("bq") is None else L["bq"][None, :], add_stride=0, threads=th)
-            k = o.matvec(fmt, L["wk"], E, h, add=None if L.get("bk") is None else L["bk"][None, :], add_stride=0, threads=th)
-            v = o.matvec(fmt, L["wv"], E, h, add=None if L.get("bv") is None else L["bv"][None, :], add_stride=0, threads=th)
-            q = o.rope(q, pos, n_heads=nh, **rope)
-            k = o.rope(k, pos, n_heads=nkv, **rope)
+            b = L.get("bqkv")
+            qkv = o.matvec(fmt, L["wqkv"], E, h, add=None if b is None else b[None, :], add_stride=0, threads=th)
+            q = o.rope(np.ascontiguousarray(qkv[:, :Hq]), pos, n_heads=nh, **rope)
+            k = o.rope(np.ascontiguousarray(qkv[:, Hq:Hq + Hkv]), pos, n_heads=nkv, **rope)
+            v = np.ascontiguousarray(qkv[:, Hq + Hkv:])
             self.kc[li][pos0:n_kv] = o.quantize(FMT_Q8_0, k)
             self.vc[li][pos0:n_kv] = o.quantize(FMT_Q8_0, v)
             rc, att = o.fa(q.reshape(T, nh, D), self.kc[li], self.vc[li], D=D, n_head=nh, n_head_kv=nkv, n_kv=n_kv,
@@ -463,9 +466,8 @@ class OracleModel:
                 raise RuntimeError(f"tsro_fa returned {rc}")
             x = o.matvec(fmt, L["wo"], Hq, att.reshape(T, Hq), add=x, add_stride=E, threads=th)
             h = o.rms_norm(x, L["ffn_norm"], c["rms_eps"], inv_n)
-            g = o.matvec(fmt, L["wg"], E, h, threads=th)
-            u = o.matvec(fmt, L["wu"], E, h, threads=th)
-            s = o.vop(7, g, u)
+            gu = o.matvec(fmt, L["wgu"], E, h, threads=th)
+            s = o.vop(7, np.ascontiguousarray(gu[:, :F]), np.ascontiguousarray(gu[:, F:]))
             x = o.matvec(fmt, L["wd"], F, s, add=x, add_stride=E, threads=th)
         h = o.rms_norm(x[-1:], self.out_norm, c["rms_eps"], inv_n)
         return o.matvec(fmt, self.head, E, h, threads=th)[0]

@@ -333,6 +333,7 @@ int tsrc_rms_norm(tsrc_ctx* ctx, const float* x, uint32_t x_stride, float* y, ui
     if (x_stride == 0) x_stride = n;
     if (y_stride == 0) y_stride = n;
     if (x_stride < n || y_stride < n) return fail(TSRC_E_ARG, "tsrc_rms_norm: stride below n");
+    if (n > 51200u) return fail(TSRC_E_SHAPE, "tsrc_rms_norm: n %u above 51200 (one row in shared memory)", n);
     int rc = use_device(ctx);
     if (rc) return rc;
     cudaError_t e = tsrc::launch_rms_norm(x, x_stride, y, y_stride, w, n, rows, daz_host(eps), daz_host(inv_n),

@@ -51,6 +51,11 @@ cudaError_t launch_rms_norm(const float* x, uint32_t xs, float* y, uint32_t ys, 
                             float eps, float inv_n, cudaStream_t st);
 cudaError_t launch_rope(const float* x, uint32_t xs, float* y, uint32_t ys, const int32_t* pos, uint32_t T, uint32_t n_heads,
                         uint32_t hd, uint32_t nd, uint32_t neox, float ts, float m, cudaStream_t st);
+// ROPE from per-position tables [n_pos][n_dims / 2] of c_i and s_i (filled by launch_rope_table)
+cudaError_t launch_rope_table(uint32_t n_pos, uint32_t nd, float ts, float m, float* cs_tab, float* sn_tab, cudaStream_t st);
+cudaError_t launch_rope_apply(const float* x, uint32_t xs, float* y, uint32_t ys, const int32_t* pos, uint32_t T,
+                              uint32_t n_heads, uint32_t hd, uint32_t nd, uint32_t neox, const float* cs_tab,
+                              const float* sn_tab, cudaStream_t st);
 cudaError_t launch_vop(uint32_t func, const float* a, uint32_t as, const float* b, uint32_t bs, float* y, uint32_t ys,
                        uint32_t n, uint32_t rows, cudaStream_t st);
 cudaError_t launch_get_rows(uint32_t fmt, const uint8_t* qs, const void* meta, uint32_t n_rows, uint32_t K, const int32_t* ids,

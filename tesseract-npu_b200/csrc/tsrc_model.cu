@@ -6,7 +6,10 @@
 // residual ADD; then the output RMS_NORM + MUL and the head MUL_MAT of the last token.
 //
 // Each residual ADD is the MUL_MAT's addend epilogue (fadd(x, dot): the same value as the ADD
-// node). Weights come from tsrc_weight_synth (seeded); the f32 vectors (norm weights, biases) from
+// node). q, k and v are one MUL_MAT over the rows of the three matrices stacked (every output row is
+// its own dot product, so the values are those of three MUL_MATs), and so are gate and up; ROPE of
+// q and k is one launch over their heads, with c_i and s_i of every position precomputed once per
+// model by the same device code (a table lookup instead of the per-token angle recurrence). Weights come from tsrc_weight_synth (seeded); the f32 vectors (norm weights, biases) from
 // splitmix64 (tsrc_model_f32_value), so a checker can rebuild them.
 #include <cmath>
 #include <cstdio>
@@ -25,15 +28,16 @@ struct tsrc_model {
     float* f32 = nullptr;                                // every f32 vector, one allocation
     float* out_norm = nullptr;
     struct Layer {
-        tsrc_weight *wq, *wk, *wv, *wo, *wg, *wu, *wd;
-        float *attn_norm, *ffn_norm, *bq, *bk, *bv;
+        tsrc_weight *wqkv, *wo, *wgu, *wd;               // [q | k | v] rows, o, [gate | up] rows, down
+        float *attn_norm, *ffn_norm, *bqkv;
         tsrc_kv* kv;
     };
     std::vector<Layer> layers;
     int32_t* pos = nullptr;                              // 0 .. n_ctx - 1 (device)
+    float* rope_tab = nullptr;                           // c_i then s_i of every position [2][n_ctx][head_dim / 2]
     float* buf = nullptr;                                // activations for t_alloc tokens
     uint32_t t_alloc = 0;
-    float *x, *h, *q, *k, *v, *att, *g, *u;
+    float *x, *h, *qkv, *q, *att, *gu;
     std::vector<uint16_t> mask;                          // host causal mask of a multi-token call
 };
 
@@ -48,7 +52,7 @@ uint64_t splitmix64(uint64_t z) {
 
 
 // f32 vector kinds of the model (tsrc_model_f32_value)
-constexpr uint32_t kVecAttnNorm = 0, kVecFfnNorm = 1, kVecBq = 2, kVecBk = 3, kVecBv = 4, kVecOutNorm = 5;
+constexpr uint32_t kVecAttnNorm = 0, kVecFfnNorm = 1, kVecBqkv = 2, kVecOutNorm = 5;
 
 }  // namespace
 
@@ -64,7 +68,7 @@ int tsrc_model_free(tsrc_model* m) {
     if (!m) return TSRC_OK;
     cudaDeviceSynchronize();
     for (auto& L : m->layers) {
-        tsrc_weight* ws[] = {L.wq, L.wk, L.wv, L.wo, L.wg, L.wu, L.wd};
+        tsrc_weight* ws[] = {L.wqkv, L.wo, L.wgu, L.wd};
         for (tsrc_weight* w : ws)
             if (w) tsrc_weight_free(w);
         if (L.kv) tsrc_kv_free(L.kv);
@@ -73,6 +77,7 @@ int tsrc_model_free(tsrc_model* m) {
     if (m->output) tsrc_weight_free(m->output);
     cudaFree(m->f32);
     cudaFree(m->pos);
+    cudaFree(m->rope_tab);
     cudaFree(m->buf);
     delete m;
     return TSRC_OK;
@@ -98,7 +103,7 @@ int tsrc_model_create(tsrc_ctx* ctx, const tsrc_model_cfg* cfg, uint64_t seed, t
     };
     synth(c.n_vocab, E, seed * 1000u + 1u, &m->tok_embd);
     if (!c.tied_head) synth(c.n_vocab, E, seed * 1000u + 2u, &m->output);
-    // f32 vectors: per layer attn_norm, ffn_norm (E) and the biases (Hq, Hkv, Hkv); out_norm (E)
+    // f32 vectors: per layer attn_norm, ffn_norm (E) and the q | k | v bias (Hq + 2 Hkv); out_norm (E)
     const size_t per_layer = 2u * E + (c.qkv_bias ? (size_t)Hq + 2u * Hkv : 0u);
     const size_t n_f32 = per_layer * c.n_layer + E;
     std::vector<float> host(n_f32);
@@ -115,20 +120,13 @@ int tsrc_model_create(tsrc_ctx* ctx, const tsrc_model_cfg* cfg, uint64_t seed, t
         tsrc_model::Layer& L = m->layers[l];
         std::memset(&L, 0, sizeof L);
         const uint64_t s = seed * 1000u + 16u * (l + 1u);
-        synth(Hq, E, s + 0, &L.wq);
-        synth(Hkv, E, s + 1, &L.wk);
-        synth(Hkv, E, s + 2, &L.wv);
-        synth(E, Hq, s + 3, &L.wo);
-        synth(F, E, s + 4, &L.wg);
-        synth(F, E, s + 5, &L.wu);
-        synth(E, F, s + 6, &L.wd);
+        synth(Hq + 2u * Hkv, E, s + 0, &L.wqkv);
+        synth(E, Hq, s + 1, &L.wo);
+        synth(2u * F, E, s + 2, &L.wgu);
+        synth(E, F, s + 3, &L.wd);
         L.attn_norm = vec(l, kVecAttnNorm, E);
         L.ffn_norm = vec(l, kVecFfnNorm, E);
-        if (c.qkv_bias) {
-            L.bq = vec(l, kVecBq, Hq);
-            L.bk = vec(l, kVecBk, Hkv);
-            L.bv = vec(l, kVecBv, Hkv);
-        }
+        if (c.qkv_bias) L.bqkv = vec(l, kVecBqkv, Hq + 2u * Hkv);
         if (rc == TSRC_OK) rc = tsrc_kv_create(ctx, c.n_head_kv, D, c.n_ctx, &L.kv);
     }
     m->out_norm = vec(c.n_layer, kVecOutNorm, E);
@@ -139,6 +137,12 @@ int tsrc_model_create(tsrc_ctx* ctx, const tsrc_model_cfg* cfg, uint64_t seed, t
     if (rc == TSRC_OK && (cudaMalloc(&m->pos, c.n_ctx * sizeof(int32_t)) != cudaSuccess ||
                           cudaMemcpy(m->pos, pos.data(), c.n_ctx * sizeof(int32_t), cudaMemcpyHostToDevice) != cudaSuccess))
         rc = TSRC_E_NOMEM;
+    const size_t half = D / 2u;
+    if (rc == TSRC_OK && cudaMalloc(&m->rope_tab, 2u * c.n_ctx * half * sizeof(float)) != cudaSuccess) rc = TSRC_E_NOMEM;
+    if (rc == TSRC_OK &&
+        (tsrc::launch_rope_table(c.n_ctx, D, m->ts, 1.0f, m->rope_tab, m->rope_tab + c.n_ctx * half, nullptr) != cudaSuccess ||
+         cudaDeviceSynchronize() != cudaSuccess))
+        rc = tsrc::api_fail(TSRC_E_CUDA, "tsrc_model_create: ROPE tables");
     if (rc != TSRC_OK) {
         tsrc_model_free(m);
         return rc;
@@ -155,9 +159,9 @@ int tsrc_model_weight(const tsrc_model* m, uint32_t layer, uint32_t which, tsrc_
         else if (which == 1u) *out = m->c.tied_head ? m->tok_embd : m->output;
         return *out ? TSRC_OK : TSRC_E_ARG;
     }
-    if (layer >= m->c.n_layer || which > 6u) return tsrc::api_fail(TSRC_E_ARG, "tsrc_model_weight: no such weight");
+    if (layer >= m->c.n_layer || which > 3u) return tsrc::api_fail(TSRC_E_ARG, "tsrc_model_weight: no such weight");
     const tsrc_model::Layer& L = m->layers[layer];
-    tsrc_weight* ws[] = {L.wq, L.wk, L.wv, L.wo, L.wg, L.wu, L.wd};
+    tsrc_weight* ws[] = {L.wqkv, L.wo, L.wgu, L.wd};
     *out = ws[which];
     return TSRC_OK;
 }
@@ -175,11 +179,12 @@ int tsrc_model_forward(tsrc_model* m, const int32_t* ids, uint32_t T, uint32_t p
     if ((uint64_t)pos0 + T > c.n_ctx) return tsrc::api_fail(TSRC_E_ARG, "tsrc_model_forward: positions beyond n_ctx");
     tsrc_ctx* ctx = m->ctx;
     const uint32_t E = c.n_embd, D = c.head_dim, Hq = c.n_head * D, Hkv = c.n_head_kv * D, F = c.n_ff;
+    const uint32_t QKV = Hq + 2u * Hkv;
     if (T > m->t_alloc) {
         cudaDeviceSynchronize();
         cudaFree(m->buf);
         m->buf = nullptr;
-        const size_t per = 2u * E + Hq + 2u * Hkv + Hq + 2u * F;
+        const size_t per = 2u * E + QKV + 2u * Hq + 2u * F;
         if (cudaMalloc(&m->buf, per * T * sizeof(float)) != cudaSuccess) {
             m->t_alloc = 0;
             return tsrc::api_fail(TSRC_E_NOMEM, "tsrc_model_forward: activation buffers");
@@ -188,12 +193,10 @@ int tsrc_model_forward(tsrc_model* m, const int32_t* ids, uint32_t T, uint32_t p
         float* p = m->buf;
         m->x = p; p += (size_t)E * T;
         m->h = p; p += (size_t)E * T;
+        m->qkv = p; p += (size_t)QKV * T;
         m->q = p; p += (size_t)Hq * T;
-        m->k = p; p += (size_t)Hkv * T;
-        m->v = p; p += (size_t)Hkv * T;
         m->att = p; p += (size_t)Hq * T;
-        m->g = p; p += (size_t)F * T;
-        m->u = p;
+        m->gu = p;
     }
     const uint32_t n_kv = pos0 + T;
     const uint16_t* mask = nullptr;
@@ -205,34 +208,43 @@ int tsrc_model_forward(tsrc_model* m, const int32_t* ids, uint32_t T, uint32_t p
     }
     const float inv_n = 1.0f / (float)E;
     const int32_t* pos = m->pos + pos0;
+    const size_t half = D / 2u;
+    const cudaStream_t st = static_cast<cudaStream_t>(stream);
     tsrc_fa_cfg fa = c.fa;
     if (fa.C == 0) fa = tsrc_fa_cfg{4u, 4u, 9344u, 32768u, 0u};
     int rc = tsrc_get_rows(ctx, m->tok_embd, ids, T, m->x, E, stream);
 #define TSRC_M(call) \
     if (rc == TSRC_OK) rc = (call)
+#define TSRC_MC(call, what) \
+    if (rc == TSRC_OK && (call) != cudaSuccess) rc = tsrc::api_fail(TSRC_E_CUDA, what)
     for (uint32_t l = 0; l < c.n_layer; ++l) {
         const tsrc_model::Layer& L = m->layers[l];
         TSRC_M(tsrc_rms_norm(ctx, m->x, E, m->h, E, L.attn_norm, E, T, c.rms_eps, inv_n, stream));
-        TSRC_M(tsrc_mul_mat(ctx, L.wq, m->h, T, E, m->q, Hq, L.bq, 0, L.bq ? TSRC_MM_ADD : 0u, 1.0f, 1.0f, stream));
-        TSRC_M(tsrc_mul_mat(ctx, L.wk, m->h, T, E, m->k, Hkv, L.bk, 0, L.bk ? TSRC_MM_ADD : 0u, 1.0f, 1.0f, stream));
-        TSRC_M(tsrc_mul_mat(ctx, L.wv, m->h, T, E, m->v, Hkv, L.bv, 0, L.bv ? TSRC_MM_ADD : 0u, 1.0f, 1.0f, stream));
-        TSRC_M(tsrc_rope(ctx, m->q, Hq, m->q, Hq, pos, T, c.n_head, D, D, c.rope_mode, m->ts, 1.0f, stream));
-        TSRC_M(tsrc_rope(ctx, m->k, Hkv, m->k, Hkv, pos, T, c.n_head_kv, D, D, c.rope_mode, m->ts, 1.0f, stream));
-        TSRC_M(tsrc_kv_set_rows(ctx, L.kv, TSRC_KV_K, m->k, T, Hkv, nullptr, pos0, stream));
-        TSRC_M(tsrc_kv_set_rows(ctx, L.kv, TSRC_KV_V, m->v, T, Hkv, nullptr, pos0, stream));
-        TSRC_M(tsrc_flash_attn(ctx, L.kv, m->q, T, c.n_head, n_kv, mask, n_kv, m->kq_scale, pos0, n_kv, &fa, m->att, stream));
+        TSRC_M(tsrc_mul_mat(ctx, L.wqkv, m->h, T, E, m->qkv, QKV, L.bqkv, 0, L.bqkv ? TSRC_MM_ADD : 0u, 1.0f, 1.0f, stream));
+        TSRC_MC(tsrc::launch_rope_apply(m->qkv, QKV, m->qkv, QKV, pos, T, c.n_head + c.n_head_kv, D, D, c.rope_mode,
+                                        m->rope_tab, m->rope_tab + (size_t)c.n_ctx * half, st),
+                "tsrc_model_forward: ROPE launch");
+        TSRC_M(tsrc_kv_set_rows(ctx, L.kv, TSRC_KV_K, m->qkv + Hq, T, QKV, nullptr, pos0, stream));
+        TSRC_M(tsrc_kv_set_rows(ctx, L.kv, TSRC_KV_V, m->qkv + Hq + Hkv, T, QKV, nullptr, pos0, stream));
+        const float* q = m->qkv;
+        if (T > 1) {                                      // FA takes q rows [T][n_head][D] contiguous
+            TSRC_MC(cudaMemcpy2DAsync(m->q, (size_t)Hq * 4u, m->qkv, (size_t)QKV * 4u, (size_t)Hq * 4u, T, cudaMemcpyDeviceToDevice, st),
+                    "tsrc_model_forward: q copy");
+            q = m->q;
+        }
+        TSRC_M(tsrc_flash_attn(ctx, L.kv, q, T, c.n_head, n_kv, mask, n_kv, m->kq_scale, pos0, n_kv, &fa, m->att, stream));
         TSRC_M(tsrc_mul_mat(ctx, L.wo, m->att, T, Hq, m->x, E, m->x, E, TSRC_MM_ADD, 1.0f, 1.0f, stream));
         TSRC_M(tsrc_rms_norm(ctx, m->x, E, m->h, E, L.ffn_norm, E, T, c.rms_eps, inv_n, stream));
-        TSRC_M(tsrc_mul_mat(ctx, L.wg, m->h, T, E, m->g, F, nullptr, 0, 0u, 1.0f, 1.0f, stream));
-        TSRC_M(tsrc_mul_mat(ctx, L.wu, m->h, T, E, m->u, F, nullptr, 0, 0u, 1.0f, 1.0f, stream));
-        TSRC_M(tsrc_vop(ctx, TSRC_VOP_SWIGLU, m->g, F, m->u, F, m->g, F, F, T, stream));
-        TSRC_M(tsrc_mul_mat(ctx, L.wd, m->g, T, F, m->x, E, m->x, E, TSRC_MM_ADD, 1.0f, 1.0f, stream));
+        TSRC_M(tsrc_mul_mat(ctx, L.wgu, m->h, T, E, m->gu, 2u * F, nullptr, 0, 0u, 1.0f, 1.0f, stream));
+        TSRC_M(tsrc_vop(ctx, TSRC_VOP_SWIGLU, m->gu, 2u * F, m->gu + F, 2u * F, m->gu, 2u * F, F, T, stream));
+        TSRC_M(tsrc_mul_mat(ctx, L.wd, m->gu, T, 2u * F, m->x, E, m->x, E, TSRC_MM_ADD, 1.0f, 1.0f, stream));
     }
     // the last token: output norm and head
     const float* xl = m->x + (size_t)(T - 1u) * E;
     TSRC_M(tsrc_rms_norm(ctx, xl, E, m->h, E, m->out_norm, E, 1, c.rms_eps, inv_n, stream));
     TSRC_M(tsrc_mul_mat(ctx, c.tied_head ? m->tok_embd : m->output, m->h, 1, E, logits, c.n_vocab, nullptr, 0, 0u, 1.0f, 1.0f,
                         stream));
+#undef TSRC_MC
 #undef TSRC_M
     return rc;
 }

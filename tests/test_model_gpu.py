@@ -24,12 +24,12 @@ def oracle_of(tsro, m, shape):
     import oracle
     L = []
     for l in range(shape["n_layer"]):
-        w = {n: m.weight(l, i).download() for i, n in enumerate(("wq", "wk", "wv", "wo", "wg", "wu", "wd"))}
+        w = {n: m.weight(l, i).download() for i, n in enumerate(("wqkv", "wo", "wgu", "wd"))}
         E, Hq, Hkv = shape["n_embd"], shape["n_head"] * shape["head_dim"], shape["n_head_kv"] * shape["head_dim"]
         w["attn_norm"] = m.f32_vector(l, 0, E)
         w["ffn_norm"] = m.f32_vector(l, 1, E)
         if shape["qkv_bias"]:
-            w["bq"], w["bk"], w["bv"] = m.f32_vector(l, 2, Hq), m.f32_vector(l, 3, Hkv), m.f32_vector(l, 4, Hkv)
+            w["bqkv"] = m.f32_vector(l, 2, Hq + 2 * Hkv)
         L.append(w)
     emb = m.weight(tsrc.MODEL_GLOBAL, 0).download()
     head = m.weight(tsrc.MODEL_GLOBAL, 1).download()
