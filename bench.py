@@ -154,26 +154,28 @@ def model_measure(dev, tsrc, torch, name, steps, warmup, e2e_steps=32):
     torch.cuda.synchronize()
     prefill_ms = e0.elapsed_time(e1)
     pos = prompt
+    one = torch.empty(1, dtype=torch.int32, device="cuda")     # the graph's token buffer
     for _ in range(warmup):
-        model.forward(ids[pos:], 1, pos, logits)
+        one.copy_(ids[pos:pos + 1])
+        model.decode(one, pos, logits)
         pos += 1
     torch.cuda.synchronize()
     kv0 = pos
     e0.record()
     for _ in range(steps):
-        model.forward(ids[pos:], 1, pos, logits)
+        one.copy_(ids[pos:pos + 1])
+        model.decode(one, pos, logits)
         pos += 1
     e1.record()
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / steps
     host_ids = ids[pos:pos + e2e_steps].cpu().pin_memory()
     host_logits = torch.empty(s["n_vocab"], pin_memory=True)
-    one = torch.empty(1, dtype=torch.int32, device="cuda")
     torch.cuda.synchronize()
     e0.record()
     for i in range(e2e_steps):
         one.copy_(host_ids[i:i + 1], non_blocking=True)
-        model.forward(one, 1, pos, logits)
+        model.decode(one, pos, logits)
         host_logits.copy_(logits, non_blocking=True)
         pos += 1
     e1.record()

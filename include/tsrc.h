@@ -297,6 +297,11 @@ TSRC_API int tsrc_model_free(tsrc_model * m);
 // receives the head output of the last token. Queued on `stream`.
 TSRC_API int tsrc_model_forward(tsrc_model * m, const int32_t * ids, uint32_t T, uint32_t pos0, float * logits,
                                 void * stream);
+// One decode token (T = 1) through a CUDA graph of the whole step: the first call (and any call
+// whose ids / logits pointers, stream or FA plan shape differ from the captured ones) captures the
+// step; later calls rewrite the position and the FA plans in the instantiated graph and launch it,
+// so a token costs one graph launch on the host. Same results as tsrc_model_forward(m, ids, 1, ...).
+TSRC_API int tsrc_model_decode(tsrc_model * m, const int32_t * ids, uint32_t pos0, float * logits, void * stream);
 // The model's weight handles (owned by the model): layer < n_layer, which 0 = the q, k, v rows
 // stacked (n_head + 2 n_head_kv heads), 1 = o, 2 = the gate and up rows stacked (2 n_ff), 3 = down;
 // or TSRC_MODEL_GLOBAL.

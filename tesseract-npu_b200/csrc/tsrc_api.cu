@@ -771,9 +771,15 @@ int tsrc_kv_get_bytes(const tsrc_kv* kv, uint32_t which, void* ggml_rows, uint32
     return kv_bytes_io(const_cast<tsrc_kv*>(kv), which, ggml_rows, cell0, n, false);
 }
 
-int tsrc_flash_attn(tsrc_ctx* ctx, const tsrc_kv* kv, const float* q, uint32_t T, uint32_t n_head, uint32_t n_kv,
-                    const uint16_t* mask, uint32_t mask_stride, float scale, uint32_t new_lo, uint32_t new_hi,
-                    const tsrc_fa_cfg* cfg, float* out, void* stream) {
+}  // extern "C"
+
+namespace tsrc {
+// Everything of one FLASH_ATTN_EXT call up to the kernel launches: checks, the plan, the scratch
+// layout, the H2D copies of a large plan or a GENERAL mask (queued on st); *la receives the launch
+// arguments and *n_max_groups the chunk size bound the launch needs.
+int fa_setup(tsrc_ctx* ctx, const tsrc_kv* kv, const float* q, uint32_t T, uint32_t n_head, uint32_t n_kv,
+             const uint16_t* mask, uint32_t mask_stride, float scale, uint32_t new_lo, uint32_t new_hi,
+             const tsrc_fa_cfg* cfg, float* out, cudaStream_t st, FaLaunch* la, uint32_t* n_max_groups) {
     if (!ctx || !kv || !q || !out) return fail(TSRC_E_ARG, "tsrc_flash_attn: NULL argument");
     if (kv->ctx != ctx) return fail(TSRC_E_ARG, "tsrc_flash_attn: the cache belongs to another context");
     if (n_kv > kv->n_cells) return fail(TSRC_E_ARG, "tsrc_flash_attn: n_kv %u exceeds the cache's %u cells", n_kv, kv->n_cells);
@@ -832,7 +838,8 @@ int tsrc_flash_attn(tsrc_ctx* ctx, const tsrc_kv* kv, const float* q, uint32_t T
         return rc;
     }
     uint8_t* p = ctx->fa_scratch;
-    tsrc::FaLaunch a{};
+    tsrc::FaLaunch& a = *la;
+    a = tsrc::FaLaunch{};
     a.items = reinterpret_cast<const tsrc::FaItem*>(p);
     a.tile_items = reinterpret_cast<const uint32_t*>(p + b_items);
     a.ok = reinterpret_cast<float*>(p + b_items + b_tiles);
@@ -840,7 +847,6 @@ int tsrc_flash_attn(tsrc_ctx* ctx, const tsrc_kv* kv, const float* q, uint32_t T
     a.mk = reinterpret_cast<float*>(p + b_items + b_tiles + b_oc + b_lc);
     uint16_t* m16 = reinterpret_cast<uint16_t*>(p + b_items + b_tiles + b_oc + b_lc + b_mk);
     float* mf = reinterpret_cast<float*>(p + b_items + b_tiles + b_oc + b_lc + b_mk + b_m16);
-    cudaStream_t st = static_cast<cudaStream_t>(stream);
     cudaError_t e = cudaSuccess;
     if (n_items <= tsrc::kFaInlineItems) {
         // a small plan travels in the kernel parameters (no copy: the call can be graph-captured)
@@ -881,7 +887,22 @@ int tsrc_flash_attn(tsrc_ctx* ctx, const tsrc_kv* kv, const float* q, uint32_t T
     a.n_tiles = po.n_tiles;
     a.Tq0 = po.Tq0;
     a.out = out;
-    e = tsrc::launch_fa(a, po.n_max_groups, st);
+    *n_max_groups = po.n_max_groups;
+    return TSRC_OK;
+}
+}  // namespace tsrc
+
+extern "C" {
+
+int tsrc_flash_attn(tsrc_ctx* ctx, const tsrc_kv* kv, const float* q, uint32_t T, uint32_t n_head, uint32_t n_kv,
+                    const uint16_t* mask, uint32_t mask_stride, float scale, uint32_t new_lo, uint32_t new_hi,
+                    const tsrc_fa_cfg* cfg, float* out, void* stream) {
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    tsrc::FaLaunch a;
+    uint32_t n_max_groups = 0;
+    int rc = tsrc::fa_setup(ctx, kv, q, T, n_head, n_kv, mask, mask_stride, scale, new_lo, new_hi, cfg, out, st, &a, &n_max_groups);
+    if (rc) return rc;
+    cudaError_t e = tsrc::launch_fa(a, n_max_groups, st);
     if (e != cudaSuccess) return cuda_fail(e, "FLASH_ATTN launch");
     return TSRC_OK;
 }

@@ -690,6 +690,17 @@ cudaError_t launch_fa_maskf(const uint16_t* m16, uint32_t stride, uint32_t T, ui
     return cudaGetLastError();
 }
 
+const void* fa_chunk_fn(uint32_t D) {
+    switch (D) {
+        case 64: return reinterpret_cast<const void*>(fa_chunk_kernel<64>);
+        case 128: return reinterpret_cast<const void*>(fa_chunk_kernel<128>);
+        case 256: return reinterpret_cast<const void*>(fa_chunk_kernel<256>);
+        case 512: return reinterpret_cast<const void*>(fa_chunk_kernel<512>);
+        default: return nullptr;
+    }
+}
+const void* fa_merge_fn() { return reinterpret_cast<const void*>(fa_merge_kernel); }
+
 cudaError_t launch_fa(const FaLaunch& a, uint32_t n_max_groups, cudaStream_t st) {
     const uint32_t ncell_max = 16u * ((n_max_groups + a.C - 1u) / a.C);
     cudaError_t e;

@@ -5,6 +5,10 @@
 #include <stddef.h>
 #include <stdint.h>
 
+struct tsrc_ctx;
+struct tsrc_kv;
+struct tsrc_fa_cfg;
+
 namespace tsrc {
 
 constexpr uint32_t kMmAdd = 0x1u;
@@ -112,6 +116,13 @@ struct FaLaunch {
 };
 
 cudaError_t launch_fa(const FaLaunch& a, uint32_t n_max_groups, cudaStream_t st);
+// the kernels launch_fa runs (to find their nodes in a captured CUDA graph)
+const void* fa_chunk_fn(uint32_t D);
+const void* fa_merge_fn();
+// tsrc_flash_attn up to the kernel launches (tsrc_api.cu)
+int fa_setup(::tsrc_ctx* ctx, const ::tsrc_kv* kv, const float* q, uint32_t T, uint32_t n_head, uint32_t n_kv,
+             const uint16_t* mask, uint32_t mask_stride, float scale, uint32_t new_lo, uint32_t new_hi,
+             const ::tsrc_fa_cfg* cfg, float* out, cudaStream_t st, FaLaunch* la, uint32_t* n_max_groups);
 size_t fa_smem_bytes(uint32_t D, uint32_t n_max_groups, uint32_t C);
 cudaError_t launch_fa_maskf(const uint16_t* m16, uint32_t stride, uint32_t T, uint32_t n_kv, float scale, float* out,
                             cudaStream_t st);

@@ -39,6 +39,25 @@ struct tsrc_model {
     uint32_t t_alloc = 0;
     float *x, *h, *qkv, *q, *att, *gu;
     std::vector<uint16_t> mask;                          // host causal mask of a multi-token call
+    // decode graph (tsrc_model_decode): one token's kernels captured once; per token the position
+    // kernel's argument and the FA nodes' plans are rewritten in the instantiated graph
+    int32_t* dstate = nullptr;                           // device: [0] position (int32), [2..3] cell (int64)
+    cudaStream_t own = nullptr;                          // a blocking stream for callers on the legacy stream
+    cudaGraph_t graph = nullptr;
+    cudaGraphExec_t gexec = nullptr;
+    const int32_t* g_ids = nullptr;
+    float* g_logits = nullptr;
+    cudaStream_t g_stream = nullptr;
+    cudaGraphNode_t pos_node = nullptr;
+    cudaKernelNodeParams pos_params{};
+    struct FaNode {
+        cudaGraphNode_t node;
+        cudaKernelNodeParams params;
+        tsrc::FaLaunch arg;
+    };
+    std::vector<FaNode> fa_nodes;
+    uint32_t g_n_items = 0, g_n_tiles = 0, g_Tq0 = 0, g_nmax = 0;
+    const void* g_ok = nullptr;
 };
 
 namespace {
@@ -55,6 +74,12 @@ uint64_t splitmix64(uint64_t z) {
 constexpr uint32_t kVecAttnNorm = 0, kVecFfnNorm = 1, kVecBqkv = 2, kVecOutNorm = 5;
 
 }  // namespace
+
+// the decode graph's per-token state: the token's position and its KV cell
+__global__ void model_state_kernel(int32_t* st, int32_t pos) {
+    st[0] = pos;
+    reinterpret_cast<int64_t*>(st)[1] = (int64_t)pos;
+}
 
 extern "C" {
 
@@ -75,6 +100,10 @@ int tsrc_model_free(tsrc_model* m) {
     }
     if (m->tok_embd) tsrc_weight_free(m->tok_embd);
     if (m->output) tsrc_weight_free(m->output);
+    if (m->gexec) cudaGraphExecDestroy(m->gexec);
+    if (m->graph) cudaGraphDestroy(m->graph);
+    cudaFree(m->dstate);
+    if (m->own) cudaStreamDestroy(m->own);
     cudaFree(m->f32);
     cudaFree(m->pos);
     cudaFree(m->rope_tab);
@@ -173,11 +202,12 @@ int tsrc_model_params(const tsrc_model* m, float* ts, float* kq_scale) {
     return TSRC_OK;
 }
 
-int tsrc_model_forward(tsrc_model* m, const int32_t* ids, uint32_t T, uint32_t pos0, float* logits, void* stream) {
-    if (!m || !ids || !logits || T == 0) return tsrc::api_fail(TSRC_E_ARG, "tsrc_model_forward: NULL argument or T = 0");
+}  // extern "C"
+
+namespace {
+
+int ensure_buffers(tsrc_model* m, uint32_t T) {
     const tsrc_model_cfg& c = m->c;
-    if ((uint64_t)pos0 + T > c.n_ctx) return tsrc::api_fail(TSRC_E_ARG, "tsrc_model_forward: positions beyond n_ctx");
-    tsrc_ctx* ctx = m->ctx;
     const uint32_t E = c.n_embd, D = c.head_dim, Hq = c.n_head * D, Hkv = c.n_head_kv * D, F = c.n_ff;
     const uint32_t QKV = Hq + 2u * Hkv;
     if (T > m->t_alloc) {
@@ -198,6 +228,17 @@ int tsrc_model_forward(tsrc_model* m, const int32_t* ids, uint32_t T, uint32_t p
         m->att = p; p += (size_t)Hq * T;
         m->gu = p;
     }
+    return TSRC_OK;
+}
+
+// The model's graph for T tokens at pos0. pos: device positions of the tokens; cells: device KV
+// cells of the tokens (NULL: cells pos0 .. pos0 + T - 1).
+int forward_body(tsrc_model* m, const int32_t* ids, uint32_t T, uint32_t pos0, float* logits, void* stream, const int32_t* pos,
+                 const int64_t* cells) {
+    const tsrc_model_cfg& c = m->c;
+    tsrc_ctx* ctx = m->ctx;
+    const uint32_t E = c.n_embd, D = c.head_dim, Hq = c.n_head * D, Hkv = c.n_head_kv * D, F = c.n_ff;
+    const uint32_t QKV = Hq + 2u * Hkv;
     const uint32_t n_kv = pos0 + T;
     const uint16_t* mask = nullptr;
     if (T > 1) {                                          // causal: token t sees cells [0, pos0 + t]
@@ -207,7 +248,6 @@ int tsrc_model_forward(tsrc_model* m, const int32_t* ids, uint32_t T, uint32_t p
         mask = m->mask.data();
     }
     const float inv_n = 1.0f / (float)E;
-    const int32_t* pos = m->pos + pos0;
     const size_t half = D / 2u;
     const cudaStream_t st = static_cast<cudaStream_t>(stream);
     tsrc_fa_cfg fa = c.fa;
@@ -224,8 +264,8 @@ int tsrc_model_forward(tsrc_model* m, const int32_t* ids, uint32_t T, uint32_t p
         TSRC_MC(tsrc::launch_rope_apply(m->qkv, QKV, m->qkv, QKV, pos, T, c.n_head + c.n_head_kv, D, D, c.rope_mode,
                                         m->rope_tab, m->rope_tab + (size_t)c.n_ctx * half, st),
                 "tsrc_model_forward: ROPE launch");
-        TSRC_M(tsrc_kv_set_rows(ctx, L.kv, TSRC_KV_K, m->qkv + Hq, T, QKV, nullptr, pos0, stream));
-        TSRC_M(tsrc_kv_set_rows(ctx, L.kv, TSRC_KV_V, m->qkv + Hq + Hkv, T, QKV, nullptr, pos0, stream));
+        TSRC_M(tsrc_kv_set_rows(ctx, L.kv, TSRC_KV_K, m->qkv + Hq, T, QKV, cells, pos0, stream));
+        TSRC_M(tsrc_kv_set_rows(ctx, L.kv, TSRC_KV_V, m->qkv + Hq + Hkv, T, QKV, cells, pos0, stream));
         const float* q = m->qkv;
         if (T > 1) {                                      // FA takes q rows [T][n_head][D] contiguous
             TSRC_MC(cudaMemcpy2DAsync(m->q, (size_t)Hq * 4u, m->qkv, (size_t)QKV * 4u, (size_t)Hq * 4u, T, cudaMemcpyDeviceToDevice, st),
@@ -247,6 +287,139 @@ int tsrc_model_forward(tsrc_model* m, const int32_t* ids, uint32_t T, uint32_t p
 #undef TSRC_MC
 #undef TSRC_M
     return rc;
+}
+
+bool same_plan(const tsrc_model* m, const tsrc::FaLaunch& a, uint32_t nmax) {
+    return a.n_items == m->g_n_items && a.n_tiles == m->g_n_tiles && a.Tq0 == m->g_Tq0 && nmax == m->g_nmax &&
+           a.n_items <= tsrc::kFaInlineItems && (const void*)a.ok == m->g_ok;
+}
+
+void drop_graph(tsrc_model* m) {
+    if (m->gexec) cudaGraphExecDestroy(m->gexec);
+    if (m->graph) cudaGraphDestroy(m->graph);
+    m->gexec = nullptr;
+    m->graph = nullptr;
+    m->fa_nodes.clear();
+    m->pos_node = nullptr;
+}
+
+// captures one decode token at pos0 (the FA plans of that position) and instantiates it
+int capture_decode(tsrc_model* m, const int32_t* ids, uint32_t pos0, float* logits, cudaStream_t st, const tsrc::FaLaunch& a0,
+                   uint32_t nmax) {
+    drop_graph(m);
+    if (cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal) != cudaSuccess)
+        return tsrc::api_fail(TSRC_E_CUDA, "tsrc_model_decode: stream capture");
+    model_state_kernel<<<1, 1, 0, st>>>(m->dstate, (int32_t)pos0);
+    int rc = forward_body(m, ids, 1, pos0, logits, st, m->dstate, reinterpret_cast<const int64_t*>(m->dstate + 2));
+    cudaGraph_t g = nullptr;
+    const cudaError_t e = cudaStreamEndCapture(st, &g);
+    if (rc != TSRC_OK || e != cudaSuccess) {
+        if (g) cudaGraphDestroy(g);
+        return rc != TSRC_OK ? rc : tsrc::api_fail(TSRC_E_CUDA, "tsrc_model_decode: capture failed");
+    }
+    m->graph = g;
+    if (cudaGraphInstantiate(&m->gexec, g, 0) != cudaSuccess) {
+        drop_graph(m);
+        return tsrc::api_fail(TSRC_E_CUDA, "tsrc_model_decode: graph instantiation");
+    }
+    size_t n = 0;
+    cudaGraphGetNodes(g, nullptr, &n);
+    std::vector<cudaGraphNode_t> nodes(n);
+    cudaGraphGetNodes(g, nodes.data(), &n);
+    const void* fchunk = tsrc::fa_chunk_fn(m->c.head_dim);
+    const void* fmerge = tsrc::fa_merge_fn();
+    const void* fstate = reinterpret_cast<const void*>(model_state_kernel);
+    for (cudaGraphNode_t nd : nodes) {
+        cudaGraphNodeType t;
+        if (cudaGraphNodeGetType(nd, &t) != cudaSuccess || t != cudaGraphNodeTypeKernel) continue;
+        cudaKernelNodeParams p{};
+        if (cudaGraphKernelNodeGetParams(nd, &p) != cudaSuccess) continue;
+        if (p.func == fchunk || p.func == fmerge) {
+            tsrc_model::FaNode f;
+            f.node = nd;
+            f.params = p;
+            f.arg = *static_cast<const tsrc::FaLaunch*>(p.kernelParams[0]);
+            m->fa_nodes.push_back(f);
+        } else if (p.func == fstate) {
+            m->pos_node = nd;
+            m->pos_params = p;
+        }
+    }
+    if (!m->pos_node || m->fa_nodes.size() != 2u * m->c.n_layer) {
+        drop_graph(m);
+        return tsrc::api_fail(TSRC_E_CUDA, "tsrc_model_decode: the captured graph lacks the expected kernels");
+    }
+    m->g_ids = ids;
+    m->g_logits = logits;
+    m->g_stream = st;
+    m->g_n_items = a0.n_items;
+    m->g_n_tiles = a0.n_tiles;
+    m->g_Tq0 = a0.Tq0;
+    m->g_nmax = nmax;
+    m->g_ok = a0.ok;
+    return TSRC_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int tsrc_model_forward(tsrc_model* m, const int32_t* ids, uint32_t T, uint32_t pos0, float* logits, void* stream) {
+    if (!m || !ids || !logits || T == 0) return tsrc::api_fail(TSRC_E_ARG, "tsrc_model_forward: NULL argument or T = 0");
+    if ((uint64_t)pos0 + T > m->c.n_ctx) return tsrc::api_fail(TSRC_E_ARG, "tsrc_model_forward: positions beyond n_ctx");
+    int rc = ensure_buffers(m, T);
+    if (rc) return rc;
+    return forward_body(m, ids, T, pos0, logits, stream, m->pos + pos0, nullptr);
+}
+
+int tsrc_model_decode(tsrc_model* m, const int32_t* ids, uint32_t pos0, float* logits, void* stream) {
+    if (!m || !ids || !logits) return tsrc::api_fail(TSRC_E_ARG, "tsrc_model_decode: NULL argument");
+    const tsrc_model_cfg& c = m->c;
+    if ((uint64_t)pos0 + 1u > c.n_ctx) return tsrc::api_fail(TSRC_E_ARG, "tsrc_model_decode: position beyond n_ctx");
+    int rc = ensure_buffers(m, 1);
+    if (rc) return rc;
+    if (!m->dstate && cudaMalloc(&m->dstate, 16) != cudaSuccess) return tsrc::api_fail(TSRC_E_NOMEM, "tsrc_model_decode: state");
+    // a graph cannot be captured on the legacy default stream: a NULL stream runs on the model's
+    // own blocking stream, which that stream orders with
+    if (!stream && !m->own && cudaStreamCreate(&m->own) != cudaSuccess)
+        return tsrc::api_fail(TSRC_E_CUDA, "tsrc_model_decode: stream");
+    const cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : m->own;
+    // the plan of this position (the same for every layer: same shapes and n_kv)
+    tsrc_fa_cfg fa = c.fa;
+    if (fa.C == 0) fa = tsrc_fa_cfg{4u, 4u, 9344u, 32768u, 0u};
+    tsrc::FaLaunch a0;
+    uint32_t nmax = 0;
+    rc = tsrc::fa_setup(m->ctx, m->layers[0].kv, m->qkv, 1, c.n_head, pos0 + 1u, nullptr, 0, m->kq_scale, pos0, pos0 + 1u, &fa,
+                        m->att, st, &a0, &nmax);
+    if (rc) return rc;
+    if (a0.n_items > tsrc::kFaInlineItems) return forward_body(m, ids, 1, pos0, logits, st, m->pos + pos0, nullptr);
+    if (!m->gexec || ids != m->g_ids || logits != m->g_logits || st != m->g_stream || !same_plan(m, a0, nmax)) {
+        rc = capture_decode(m, ids, pos0, logits, st, a0, nmax);
+        if (rc) return rc;
+    } else {
+        int32_t p = (int32_t)pos0;
+        void* pa[2] = {&m->dstate, &p};
+        cudaKernelNodeParams pp = m->pos_params;
+        pp.kernelParams = pa;
+        if (cudaGraphExecKernelNodeSetParams(m->gexec, m->pos_node, &pp) != cudaSuccess)
+            return tsrc::api_fail(TSRC_E_CUDA, "tsrc_model_decode: position update");
+        for (auto& f : m->fa_nodes) {
+            tsrc::FaLaunch a = f.arg;                    // this node's layer pointers, the new plan
+            a.n_kv = a0.n_kv;
+            a.n_items = a0.n_items;
+            a.n_tiles = a0.n_tiles;
+            a.Tq0 = a0.Tq0;
+            std::memcpy(a.inl_items, a0.inl_items, sizeof a.inl_items);
+            std::memcpy(a.inl_tiles, a0.inl_tiles, sizeof a.inl_tiles);
+            void* ka[1] = {&a};
+            cudaKernelNodeParams kp = f.params;
+            kp.kernelParams = ka;
+            if (cudaGraphExecKernelNodeSetParams(m->gexec, f.node, &kp) != cudaSuccess)
+                return tsrc::api_fail(TSRC_E_CUDA, "tsrc_model_decode: FA plan update");
+        }
+    }
+    if (cudaGraphLaunch(m->gexec, st) != cudaSuccess) return tsrc::api_fail(TSRC_E_CUDA, "tsrc_model_decode: graph launch");
+    return TSRC_OK;
 }
 
 }  // extern "C"

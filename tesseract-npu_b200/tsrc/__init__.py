@@ -60,6 +60,7 @@ _SIGS = {
     "tsrc_model_create": (_i, [_p, _p, _u64, ct.POINTER(_p)]),
     "tsrc_model_free": (_i, [_p]),
     "tsrc_model_forward": (_i, [_p, _p, _u32, _u32, _p, _p]),
+    "tsrc_model_decode": (_i, [_p, _p, _u32, _p, _p]),
     "tsrc_model_weight": (_i, [_p, _u32, _u32, ct.POINTER(_p)]),
     "tsrc_model_params": (_i, [_p, ct.POINTER(_f32), ct.POINTER(_f32)]),
     "tsrc_model_f32_value": (_f32, [_u64, _u32, _u32, _u32]),
@@ -359,6 +360,10 @@ class Model:
 
     def forward(self, ids, T: int, pos0: int, logits, stream=None) -> None:
         _check(lib().tsrc_model_forward(self.handle, _addr(ids), T, pos0, _addr(logits), _stream(stream)))
+
+    def decode(self, ids, pos0: int, logits, stream=None) -> None:
+        """One token through the captured decode graph (keep ids / logits at fixed addresses)."""
+        _check(lib().tsrc_model_decode(self.handle, _addr(ids), pos0, _addr(logits), _stream(stream)))
 
     def weight(self, layer: int, which: int) -> "Weight":
         h = _p()

@@ -1,8 +1,9 @@
 """End-to-end decoder (tsrc_model_forward) against the oracle's composition of the same graph
 (oracle.OracleModel over the kinds pinned to the reference): a prompt through the prefill path (more
 than eight tokens: the tensor-core MUL_MAT and FA query tiles), then decode steps through the
-matvec path. Small random-init models of both architectures; tolerance: equal f32 bit patterns of
-the logits."""
+matvec path, eagerly and through the captured decode graph (whose FA plans are rewritten per
+token). Small random-init models of both architectures; tolerance: equal f32 bit patterns of the
+logits."""
 import numpy as np
 import pytest
 
@@ -55,9 +56,13 @@ def test_model_prefill_then_decode_bit_exact(dev, tsro, name):
         np.testing.assert_array_equal(logits.cpu().numpy().view(np.uint32), want.view(np.uint32))
         pos = prompt.size
         tok = int(np.argmax(want))
-        for _ in range(3):                                   # greedy decode, one token at a time
-            one = torch.tensor([tok], dtype=torch.int32, device="cuda")
-            m.forward(one, 1, pos, logits)
+        one = torch.zeros(1, dtype=torch.int32, device="cuda")
+        for step in range(5):                                # greedy decode: eagerly, then through the graph
+            one.fill_(tok)
+            if step == 0:
+                m.forward(one, 1, pos, logits)
+            else:
+                m.decode(one, pos, logits)                   # step 1 captures, later steps patch the graph
             dev.sync()
             want = ref.forward(np.array([tok], np.int32), pos)
             np.testing.assert_array_equal(logits.cpu().numpy().view(np.uint32), want.view(np.uint32))
