@@ -147,6 +147,7 @@ def model_measure(dev, tsrc, torch, name, steps, warmup, e2e_steps=32):
     ids = torch.randint(0, s["n_vocab"], (n_ctx,), dtype=torch.int32, device="cuda", generator=g)
     logits = torch.empty(s["n_vocab"], device="cuda")
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    model.forward(ids, prompt, 0, logits)                      # warm-up prefill (first launches), then timed
     torch.cuda.synchronize()
     e0.record()
     model.forward(ids, prompt, 0, logits)

@@ -50,20 +50,12 @@ __device__ __forceinline__ float maxt(float a, float b) {
 // exponent is <= es (zero for a zero w), and RNE to 24 bits of A * 2^k with underflow to a signed
 // zero below 2^-126 and overflow to infinity.
 __device__ __forceinline__ int32_t bf_int(float w, int32_t es) {
+    // branch-free: RNE(m / 2^sh) = (m + 2^(sh-1) - 1 + ((m >> sh) & 1)) >> sh for 1 <= sh <= 31
+    // (m < 2^24, so sh >= 26 gives 0); sh = 0 keeps m
     const uint32_t u = fbits(w), a = u & ~kSign;
-    if ((a >> 23) == 0) return 0;
-    const int32_t sh = es - ((int32_t)(a >> 23) - 127);
-    const uint32_t m = 0x00800000u | (a & kMant);
-    uint32_t v;
-    if (sh == 0) {
-        v = m;
-    } else if (sh >= 26) {
-        v = 0;
-    } else {
-        v = m >> sh;
-        const uint32_t rem = m & ((1u << sh) - 1u), half = 1u << (sh - 1);
-        if (rem > half || (rem == half && (v & 1u))) v++;
-    }
+    const uint32_t m = (a >> 23) ? (0x00800000u | (a & kMant)) : 0u;
+    const uint32_t sh = (uint32_t)min(es - ((int32_t)(a >> 23) - 127), 31);
+    const uint32_t v = sh == 0u ? m : (m + (1u << (sh - 1u)) - 1u + ((m >> sh) & 1u)) >> sh;
     return (u & kSign) ? -(int32_t)v : (int32_t)v;
 }
 
@@ -424,9 +416,10 @@ __global__ void __launch_bounds__(kFaThreads, 1) fa_chunk_kernel(FaLaunch a) {
                             }
                         }
                         const int32_t es = (int32_t)__reduce_max_sync(0xFFFFFFFFu, (uint32_t)(le + 1000)) - 1000;
-                        bad0 = __any_sync(0xFFFFFFFFu, bad0);
-                        bad1 = __any_sync(0xFFFFFFFFu, bad1);
-                        any = __any_sync(0xFFFFFFFFu, any);
+                        const uint32_t fl3 = __reduce_or_sync(0xFFFFFFFFu, (bad0 ? 1u : 0u) | (bad1 ? 2u : 0u) | (any ? 4u : 0u));
+                        bad0 = (fl3 & 1u) != 0;
+                        bad1 = (fl3 & 2u) != 0;
+                        any = (fl3 & 4u) != 0;
                         // W = RNE_int(w 2^(23 - es)) (|W| <= 2^24) as four balanced base-256 digits,
                         // the B operand of the int8 tensor-core products: table (sl, e), row r*4 + digit
 #pragma unroll
@@ -465,8 +458,9 @@ __global__ void __launch_bounds__(kFaThreads, 1) fa_chunk_kernel(FaLaunch a) {
                             }
                         }
                         const int32_t ep = (int32_t)__reduce_max_sync(0xFFFFFFFFu, (uint32_t)(le + 1000)) - 1000;
-                        bad = __any_sync(0xFFFFFFFFu, bad);
-                        any = __any_sync(0xFFFFFFFFu, any);
+                        const uint32_t fl2 = __reduce_or_sync(0xFFFFFFFFu, (bad ? 1u : 0u) | (any ? 2u : 0u));
+                        bad = (fl2 & 1u) != 0;
+                        any = (fl2 & 2u) != 0;
                         int32_t part = 0;
                         if (!bad && any) part = bf_int(pv[0], ep) + bf_int(pv[1], ep);
                         const int32_t sum = __reduce_add_sync(0xFFFFFFFFu, part);
@@ -488,7 +482,7 @@ __global__ void __launch_bounds__(kFaThreads, 1) fa_chunk_kernel(FaLaunch a) {
                         cp_async_wait_all();
                         __syncwarp();
                     }
-#pragma unroll 1
+#pragma unroll 2
                     for (uint32_t mt = 0; mt < VP / 16u; ++mt) {
                         const uint32_t v0 = ph * VP + 16u * mt, sl = v0 / 64u, e = (v0 % 64u) / 32u;
                         const uint8_t* Wt_se = Wd + (sl * 2u + e) * kWdRows * kWdStride;
