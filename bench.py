@@ -183,7 +183,9 @@ def model_measure(dev, tsrc, torch, name, steps, warmup, e2e_steps=32):
     torch.cuda.synchronize()
     e2e_ms = e0.elapsed_time(e1) / e2e_steps
     algo = model_algo_bytes(s, kv0 + steps // 2)
-    launches = 3 + 11 * s["n_layer"]
+    # state, GET_ROWS; per layer RMS_NORM, 4 MUL_MATs, ROPE + KVST, FA chunk + merge, RMS_NORM,
+    # SWIGLU; then RMS_NORM and the head MUL_MAT
+    launches = 4 + 10 * s["n_layer"]
     return dict(shape=s, prefill_ms=prefill_ms, ms=ms, e2e_ms=e2e_ms, algo_bytes=algo, launches=launches,
                 n_kv=(kv0, pos)), model
 
@@ -895,7 +897,8 @@ def main():
                                                            if team is not None else "NCCL all_gather of y")},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "traffic": traffic, "peak_kind": peak_kind,
-                     "kernel": f"matvec_kernel<{fmt},1> (QACT fused)", "us_per_launch": round(kern_us, 3),
+                     "kernel": f"matvec_kernel<{fmt},1> (QACT fused)",
+                     "us_per_launch": round(kern_us, 3),
                      "algorithmic_bytes_per_launch": shard_algo},
         "e2e": {"value": round(e2e, 2), "unit": "GB/s", "h2d_bytes_per_step": 4 * K,
                 "d2h_bytes_per_step": 4 * (R * world if world > 1 else n_rows),

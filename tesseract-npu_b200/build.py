@@ -37,16 +37,33 @@ def up_to_date() -> bool:
 
 
 def build(force: bool = False, verbose: bool = False) -> str:
+    """Compiles every .cu to an object in parallel (each translation unit is self-contained),
+    then links the shared library."""
     if not force and up_to_date():
         return OUT
+    from concurrent.futures import ThreadPoolExecutor
     subprocess.run([sys.executable, os.path.join(CSRC, "gen_exp_tables.py")], check=True)
-    cmd = [NVCC, *FLAGS, "-o", OUT + ".tmp", *sources()]
-    r = subprocess.run(cmd, capture_output=True, text=True)
+    objdir = os.path.join(HERE, "_build")
+    os.makedirs(objdir, exist_ok=True)
+    compile_flags = [f for f in FLAGS if f != "-shared"]
+
+    def one(src):
+        obj = os.path.join(objdir, os.path.basename(src)[:-3] + ".o")
+        return subprocess.run([NVCC, *compile_flags, "-c", "-o", obj, src], capture_output=True, text=True), obj
+
+    with ThreadPoolExecutor(max_workers=max(1, min(len(sources()), os.cpu_count() or 1))) as ex:
+        results = list(ex.map(one, sources()))
+    for r, _ in results:
+        if r.returncode != 0:
+            sys.stderr.write(r.stdout + r.stderr)
+            raise RuntimeError("nvcc failed building libtsrc.so")
+        if verbose:
+            sys.stderr.write(r.stderr)
+    r = subprocess.run([NVCC, "-gencode", "arch=compute_100a,code=sm_100a", "-shared", "-o", OUT + ".tmp",
+                        *[o for _, o in results]], capture_output=True, text=True)
     if r.returncode != 0:
         sys.stderr.write(r.stdout + r.stderr)
-        raise RuntimeError("nvcc failed building libtsrc.so")
-    if verbose:
-        sys.stderr.write(r.stderr)
+        raise RuntimeError("nvcc failed linking libtsrc.so")
     os.replace(OUT + ".tmp", OUT)
     return OUT
 

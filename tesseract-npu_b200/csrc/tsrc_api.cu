@@ -256,6 +256,21 @@ int mm_check(tsrc_ctx* ctx, const tsrc_weight* w, const float* x, uint32_t T, ui
 
 }  // namespace tsrc
 
+namespace tsrc {
+// the planes of a cache for a fused ROPE + KVST launch (tsrc_model.cu)
+int kv_fill_planes(const tsrc_kv* kv, RopeKvst* a) {
+    if (!kv) return TSRC_E_ARG;
+    a->n_head_kv = kv->n_head_kv;
+    a->n_cells = kv->n_alloc;
+    a->kq = kv->q[TSRC_KV_K];
+    a->vq = kv->q[TSRC_KV_V];
+    a->kd = kv->d[TSRC_KV_K];
+    a->vd = kv->d[TSRC_KV_V];
+    return kv_error_flag(&a->err) == cudaSuccess ? TSRC_OK : fail(TSRC_E_CUDA, "KVST error flag");
+}
+uint32_t kv_cells(const tsrc_kv* kv) { return kv->n_cells; }
+}  // namespace tsrc
+
 extern "C" {
 
 const char* tsrc_last_error(void) { return g_err.c_str(); }

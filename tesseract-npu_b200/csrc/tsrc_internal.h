@@ -144,6 +144,37 @@ struct FaPlanOut {
 int fa_plan(const FaPlanIn& in, FaPlanOut* out, FaItem** items, uint32_t* n_items, uint32_t** tile_items, const char** why);
 void fa_plan_free(FaItem* items, uint32_t* tile_items);
 
+#ifdef __CUDACC__
+// Byte offset of (cell, value k of head g) in a KV quant plane of n_cells cells per head (head-major;
+// K cell-major [head][cell][D]; vt: the V plane's value-major 16-cell groups [head][group][D][16]).
+__device__ __forceinline__ size_t kv_qoff(bool vt, uint32_t g, uint32_t n_cells, uint32_t D, size_t cell, uint32_t k) {
+    const size_t hc = (size_t)g * n_cells + cell;
+    return vt ? (hc - (cell & 15u)) * D + (size_t)k * 16u + (cell & 15u) : hc * D + k;
+}
+#endif
+
+// ROPE of the q and k heads of T fused q | k | v rows (in place, from the per-position tables),
+// then KVST of each token's k and v rows into a layer's K and V planes: one launch for what the
+// decoder layer's ROPE, ROPE and two SET_ROWS nodes do (tsrc_vu.cu). err: the KVST error flag.
+struct RopeKvst {
+    float* qkv;
+    uint32_t stride;            // floats per token row
+    const int32_t* pos;         // [T]
+    uint32_t n_rot_heads, hd, nd, neox;   // q heads + k heads are rotated
+    const float *cs_tab, *sn_tab;
+    uint32_t k_off, v_off;      // the k and v rows inside a token row
+    const int64_t* cells;       // [T] or NULL: cell0 + t
+    uint32_t cell0, n_head_kv, n_cells;   // n_cells: the planes' cells per head (padded to 16)
+    int8_t *kq, *vq;
+    uint16_t *kd, *vd;
+    unsigned int* err;
+};
+cudaError_t launch_rope_kvst(const RopeKvst& a, uint32_t T, cudaStream_t st);
+// fills n_head_kv, n_cells and the plane pointers of `a` from a cache (tsrc_api.cu); cells of the cache
+int kv_fill_planes(const ::tsrc_kv* kv, RopeKvst* a);
+uint32_t kv_cells(const ::tsrc_kv* kv);
+cudaError_t kv_error_flag(unsigned int** err);
+
 // KV cache planes (tsrc_kv.cu): KVST of f32 rows (QACT A32), and ggml q8_0 rows <-> planes.
 // vt: the V plane (value-major inside each 16-cell group); K is cell-major.
 cudaError_t launch_kv_store(const float* rows, uint32_t n, uint32_t row_stride, const int64_t* cells, uint32_t cell0,

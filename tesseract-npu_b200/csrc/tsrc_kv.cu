@@ -23,10 +23,8 @@ namespace tsrc {
 
 namespace {
 
-// Byte offset of (cell, value k of head g) in a quant plane; vt: the V plane's value-major groups.
 __device__ __forceinline__ size_t qoff(bool vt, uint32_t g, uint32_t n_cells, uint32_t D, size_t cell, uint32_t k) {
-    const size_t hc = (size_t)g * n_cells + cell;
-    return vt ? (hc - (cell & 15u)) * D + (size_t)k * 16u + (cell & 15u) : hc * D + k;
+    return kv_qoff(vt, g, n_cells, D, cell, k);
 }
 
 // one warp per 32-value block of a row
@@ -106,6 +104,8 @@ __global__ void kv_to_ggml_kernel(const int8_t* q, const uint16_t* d, uint32_t n
 __device__ unsigned int g_kv_error;
 
 }  // namespace
+
+cudaError_t kv_error_flag(unsigned int** err) { return cudaGetSymbolAddress(reinterpret_cast<void**>(err), g_kv_error); }
 
 cudaError_t launch_kv_store(const float* rows, uint32_t n, uint32_t row_stride, const int64_t* cells, uint32_t cell0,
                             uint32_t n_head_kv, uint32_t D, uint32_t n_cells, bool vt, int8_t* q, uint16_t* d, cudaStream_t st) {

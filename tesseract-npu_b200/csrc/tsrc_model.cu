@@ -261,11 +261,26 @@ int forward_body(tsrc_model* m, const int32_t* ids, uint32_t T, uint32_t pos0, f
         const tsrc_model::Layer& L = m->layers[l];
         TSRC_M(tsrc_rms_norm(ctx, m->x, E, m->h, E, L.attn_norm, E, T, c.rms_eps, inv_n, stream));
         TSRC_M(tsrc_mul_mat(ctx, L.wqkv, m->h, T, E, m->qkv, QKV, L.bqkv, 0, L.bqkv ? TSRC_MM_ADD : 0u, 1.0f, 1.0f, stream));
-        TSRC_MC(tsrc::launch_rope_apply(m->qkv, QKV, m->qkv, QKV, pos, T, c.n_head + c.n_head_kv, D, D, c.rope_mode,
-                                        m->rope_tab, m->rope_tab + (size_t)c.n_ctx * half, st),
-                "tsrc_model_forward: ROPE launch");
-        TSRC_M(tsrc_kv_set_rows(ctx, L.kv, TSRC_KV_K, m->qkv + Hq, T, QKV, cells, pos0, stream));
-        TSRC_M(tsrc_kv_set_rows(ctx, L.kv, TSRC_KV_V, m->qkv + Hq + Hkv, T, QKV, cells, pos0, stream));
+        {   // ROPE of q and k, SET_ROWS of k and v into the layer's q8_0 cache: one launch
+            tsrc::RopeKvst rk{};
+            rk.qkv = m->qkv;
+            rk.stride = QKV;
+            rk.pos = pos;
+            rk.n_rot_heads = c.n_head + c.n_head_kv;
+            rk.hd = D;
+            rk.nd = D;
+            rk.neox = c.rope_mode;
+            rk.cs_tab = m->rope_tab;
+            rk.sn_tab = m->rope_tab + (size_t)c.n_ctx * half;
+            rk.k_off = Hq;
+            rk.v_off = Hq + Hkv;
+            rk.cells = cells;
+            rk.cell0 = pos0;
+            if (rc == TSRC_OK && !cells && (uint64_t)pos0 + T > tsrc::kv_cells(L.kv))
+                rc = tsrc::api_fail(TSRC_E_ARG, "tsrc_model_forward: cells outside the cache");
+            TSRC_M(tsrc::kv_fill_planes(L.kv, &rk));
+            TSRC_MC(tsrc::launch_rope_kvst(rk, T, st), "tsrc_model_forward: ROPE + KVST launch");
+        }
         const float* q = m->qkv;
         if (T > 1) {                                      // FA takes q rows [T][n_head][D] contiguous
             TSRC_MC(cudaMemcpy2DAsync(m->q, (size_t)Hq * 4u, m->qkv, (size_t)QKV * 4u, (size_t)Hq * 4u, T, cudaMemcpyDeviceToDevice, st),
