@@ -5,8 +5,9 @@
 Metric: matvec HBM GB/s. The N = 1 workload is BASELINE config 2 (Q4_K
 14336 x 4096, one token); config 1 (Q8_0 4864 x 896) with --config cfg1. A step is one MUL_MAT of
 one token over one weight matrix: QACT of the f32 activation, then the matvec; on N > 1 GPUs each
-rank holds a contiguous row shard (the reference's symmetric row split) and the step ends with an
-NCCL all-gather of y. Algorithmic bytes per step: N*(K/256)*144 (or N*(K/32)*34) + 4K + 4N.
+rank holds a contiguous row shard (the reference's symmetric row split) and the step ends with the
+all-gather of y fused into the matvec kernel (P2P stores of tagged words over NVLink; an NCCL
+all_gather with --collective nccl). Algorithmic bytes per step: N*(K/256)*144 (or N*(K/32)*34) + 4K + 4N.
 
   value      K steps with x resident in HBM, inputs larger than L2 (each step reads the next of a
              ring of distinct weight copies, >= 4x L2 per GPU); CUDA graph replay on one GPU.

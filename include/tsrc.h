@@ -152,7 +152,7 @@ TSRC_API int tsrc_qact(tsrc_ctx * ctx, uint32_t kind, const float * x, uint32_t 
 TSRC_API int tsrc_mul_mat_isums(tsrc_ctx * ctx, const tsrc_weight * w, const float * x, float * y, int32_t * isum,
                        void * stream);
 // Connects a team with other teams of the same process and GPU (members[r] = rank r's team, this
-// one included) instead of IPC handles: for tests of the team's flag protocol on one GPU (only
+// one included) instead of IPC handles: for tests of the team's exchange on one GPU (only
 // one rank's launches may run there: ranks wait for each other, and two of them on one GPU are
 // not guaranteed to run at the same time).
 TSRC_API int tsrc_team_connect_local(tsrc_team * team, const tsrc_team * const * members);
@@ -171,9 +171,9 @@ TSRC_API int tsrc_team_free(tsrc_team * team);
 // MUL_MAT of one token over this rank's row shard of an N-row weight (N <= n_max) whose rows go
 // to every rank: y (device, N floats) receives the whole vector on every rank, bit for bit the
 // single-GPU result. The shard's rows are stored into every rank's buffer by the matvec kernel
-// itself (P2P stores over NVLink); its last CTA exchanges step flags with the peers (a bounded
-// wait: a rank that does not take part makes tsrc_sync return TSRC_E_DEVICE) and copies the vector
-// out. Every rank must make the same sequence of calls; queued on `stream`, no host sync. (The
+// itself (P2P stores over NVLink, each value with its step's tag in one 64-bit word); every CTA
+// copies its share of the vector out once the share's words carry the step's tag (a bounded wait:
+// a rank that does not take part makes tsrc_sync return TSRC_E_DEVICE). Every rank must make the same sequence of calls; queued on `stream`, no host sync. (The
 // reference's row split: sw/sim/tsr_ref.c:335-357; its host then had all rows in one memory.)
 TSRC_API int tsrc_mul_mat_allgather(tsrc_ctx * ctx, tsrc_team * team, const tsrc_weight * w, const float * x, float * y,
                                     void * stream);

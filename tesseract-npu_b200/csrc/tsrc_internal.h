@@ -36,10 +36,10 @@ struct MvArgs {
     float s0, s1;
     int32_t* isum_out;        // optional: the kernel's exact block sums of token 0
     // fused all-gather over a team of GPUs (one token; team_world = 0: off). Row n of the shard
-    // is stored into every rank's staging buffer at team_row0 + n (half (step & 1) of [2][team_n]);
-    // the last CTA signals the peers, waits for them and copies the full vector into y.
-    float* const* team_y;     // device array [world]: each rank's staging buffer
-    uint32_t* const* team_flags;  // device array [world]: each rank's flags [world]
+    // is stored into every rank's staging buffer at team_row0 + n (half (step & 1) of [2][team_n])
+    // as one 64-bit word {value bits, step + 1}; every CTA then copies its share of the full
+    // vector into y once each word of the share carries this step's tag.
+    unsigned long long* const* team_y;  // device array [world]: each rank's staging [2][team_n] tagged words
     uint32_t* team_state;     // this rank: [0] steps done, [1] CTAs finished in this launch
     uint32_t team_world, team_rank, team_row0, team_n;
 };

@@ -498,68 +498,60 @@ __device__ __forceinline__ void stream_rows(const MvArgs& a, const Qa& qa, uint3
 }
 
 // ---- fused all-gather: the end of a team launch ----------------------------------------------------
-// Every CTA's P2P stores are ordered (system scope) before it counts itself done; the last CTA
-// releases this step's flag to every rank, waits (bounded) until every rank's flag has arrived,
-// then copies the full vector from its own staging buffer into y and advances the step counter.
-// Double buffering by step parity keeps a rank that runs one step ahead from overwriting a half
-// that a slower rank still copies. A wait that runs out records error code 2 (tsrc_sync reports
-// it) and the launch ends; nothing else spins.
+// Every CTA stores each of its rows into every rank's staging half (step parity) as ONE 64-bit
+// word {value bits, step + 1}: a naturally aligned 8-byte store is single-copy atomic, so a reader
+// that sees the tag sees the value with it, and no fence, flag or counter is needed between ranks.
+// Every CTA of every rank then copies its share of the vector out, polling each word of the share
+// (bounded) until it carries this step's tag. Double buffering by step parity keeps a rank that
+// runs one step ahead from overwriting a half that a slower rank still reads: it cannot finish
+// step s + 1 (and so start writing step s + 2 into half s & 1) before every rank has stored its
+// rows of step s + 1, which a rank does only after its launch of step s has completed. The step
+// count advances when the launch's last CTA counts itself done (every CTA reads it at entry).
+// A word that never arrives records error code 2 (tsrc_sync reports it) and the launch ends.
 constexpr uint32_t kTeamSpin = 1u << 22;             // x ~100 ns: a peer absent for ~0.4 s is an error
 
-__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
-    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+__device__ __forceinline__ void st_relaxed_sys64(unsigned long long* p, unsigned long long v) {
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
-    uint32_t v;
-    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+__device__ __forceinline__ unsigned long long ld_relaxed_sys64(const unsigned long long* p) {
+    unsigned long long v;
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
     return v;
 }
 
 __device__ __forceinline__ void team_finish(const MvArgs& a, uint32_t step, uint32_t* sflag, const float* rows,
                                             uint32_t r_begin, uint32_t r_end) {
-    // this CTA's rows (contiguous) go to every rank's staging half as coalesced P2P stores
-    __syncthreads();
+    __syncthreads();                                     // the CTA's rows are in shared memory
+    const unsigned long long tag = (unsigned long long)(step + 1u) << 32;
     const size_t o = (size_t)(step & 1u) * a.team_n + a.team_row0 + r_begin;
     for (uint32_t r = 0; r < a.team_world; ++r)
-        for (uint32_t i = threadIdx.x; i < r_end - r_begin; i += blockDim.x) a.team_y[r][o + i] = rows[i];
-    // the CTA's stores happen before thread 0's system-scope fence (barrier, then a cumulative
-    // fence), which orders them before the count and, through it, before the flags
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        __threadfence_system();
-        *sflag = atomicAdd(a.team_state + 1, 1u) + 1u == gridDim.x ? 1u : 0u;
-    }
-    __syncthreads();
-    if (*sflag == 0u) return;
-    const uint32_t target = step + 1u;
-    if (threadIdx.x == 0) {
-        a.team_state[1] = 0u;
-        __threadfence_system();
-    }
-    __syncthreads();
-    // thread r releases this rank's flag to rank r, then waits for rank r's flag here
-    for (uint32_t r = threadIdx.x; r < a.team_world; r += blockDim.x) {
-        st_release_sys(a.team_flags[r] + a.team_rank, target);
-        const uint32_t* f = a.team_flags[a.team_rank] + r;
+        for (uint32_t i = threadIdx.x; i < r_end - r_begin; i += blockDim.x)
+            st_relaxed_sys64(a.team_y[r] + o + i, tag | __float_as_uint(rows[i]));
+    // this CTA's share of the gathered vector
+    const unsigned long long* src = a.team_y[a.team_rank] + (size_t)(step & 1u) * a.team_n;
+    const uint32_t n = a.team_n, share = (n + gridDim.x - 1u) / gridDim.x, i0 = blockIdx.x * share;
+    const uint32_t i1 = min(n, i0 + share);
+    bool gave_up = false;
+    for (uint32_t i = i0 + threadIdx.x; i < i1; i += blockDim.x) {
+        unsigned long long w = ld_relaxed_sys64(src + i);
         uint32_t it = 0;
-        while (ld_acquire_sys(f) < target && ++it < kTeamSpin) __nanosleep(64);
-        if (it >= kTeamSpin) atomicCAS(&g_mv_error, 0u, 2u);
+        while ((w & 0xFFFFFFFF00000000ull) != tag && !gave_up) {
+            if (++it >= kTeamSpin) {
+                gave_up = true;
+                atomicCAS(&g_mv_error, 0u, 2u);
+            }
+            __nanosleep(64);
+            w = ld_relaxed_sys64(src + i);
+        }
+        a.y[i] = __uint_as_float((uint32_t)w);
     }
+    // the step count: every CTA has read it at entry before the last one counts itself done
     __syncthreads();
-    // the gathered vector: L2 loads (the peers wrote it through L2; no stale L1 lines), eight in
-    // flight per thread
-    const float* src = a.team_y[a.team_rank] + (size_t)(step & 1u) * a.team_n;
-    const uint32_t n = a.team_n, stride = blockDim.x;
-    for (uint32_t i0 = threadIdx.x; i0 < n; i0 += 8u * stride) {
-        float v[8];
-#pragma unroll
-        for (uint32_t q = 0; q < 8; ++q) v[q] = i0 + q * stride < n ? __ldcg(src + i0 + q * stride) : 0.0f;
-#pragma unroll
-        for (uint32_t q = 0; q < 8; ++q)
-            if (i0 + q * stride < n) a.y[i0 + q * stride] = v[q];
+    if (threadIdx.x == 0 && atomicAdd(a.team_state + 1, 1u) + 1u == gridDim.x) {
+        a.team_state[1] = 0u;
+        a.team_state[0] = step + 1u;
     }
-    __syncthreads();
-    if (threadIdx.x == 0) a.team_state[0] = target;
+    (void)sflag;
 }
 
 // ---- the kernel ---------------------------------------------------------------------------------

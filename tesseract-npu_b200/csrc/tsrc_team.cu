@@ -4,14 +4,13 @@
 // jwkim04/tesseract-npu sw/sim/tsr_ref.c:335-357); every rank then needs every row of y for the
 // next layer. Instead of a matvec followed by a collective, the matvec kernel itself stores each
 // finished row into every rank's staging buffer over NVLink (CUDA IPC mappings of the peers'
-// buffers: plain P2P stores, no multicast) and its last CTA exchanges per-step flags with the
-// peers (release / acquire at system scope, a bounded wait) before it copies the gathered vector
-// out. The reference has no counterpart (its channels live on one card).
+// buffers: plain P2P stores, no multicast) as one 64-bit word {value, step + 1}, and each CTA
+// copies its share of the gathered vector out once every word of the share carries the step's tag
+// (a bounded wait). The reference has no counterpart (its channels live on one card).
 //
-// A team's buffer on each rank: staging [2][n_max] f32 (double-buffered by step parity) | flags
-// [world] u32 (the last step each rank has completed) | state [2] u32 (this rank's steps, CTAs
-// finished in the current launch). All start at zero; every rank must run the same sequence of
-// tsrc_mul_mat_allgather calls (one step each).
+// A team's buffer on each rank: staging [2][n_max] tagged u64 words (double-buffered by step
+// parity) | state [2] u32 (this rank's steps, CTAs finished in the current launch). All start at
+// zero; every rank must run the same sequence of tsrc_mul_mat_allgather calls (one step each).
 #include <cuda_runtime.h>
 
 #include <cstdio>
@@ -37,8 +36,7 @@ struct tsrc_team {
     uint8_t* peer[64];          // every rank's buffer (this rank's is `local`)
     bool opened[64];
     bool connected;
-    float** dev_y;              // device arrays of the staging / flag pointers of every rank
-    uint32_t** dev_flags;
+    unsigned long long** dev_y;  // device array of every rank's staging pointer
 };
 
 namespace {
@@ -69,18 +67,16 @@ int tsrc_team_create(tsrc_ctx* ctx, uint32_t rank, uint32_t world, uint32_t n_ma
     t->rank = rank;
     t->world = world;
     t->n_max = n_max;
-    t->staging_bytes = a256((size_t)2 * n_max * 4u);
-    t->bytes = t->staging_bytes + a256((size_t)world * 4u) + 256u;
+    t->staging_bytes = a256((size_t)2 * n_max * 8u);
+    t->bytes = t->staging_bytes + 256u;
     e = cudaMalloc(&t->local, t->bytes);
     if (e == cudaSuccess) e = cudaMemset(t->local, 0, t->bytes);
-    if (e == cudaSuccess) e = cudaMalloc(&t->dev_y, sizeof(float*) * world);
-    if (e == cudaSuccess) e = cudaMalloc(&t->dev_flags, sizeof(uint32_t*) * world);
+    if (e == cudaSuccess) e = cudaMalloc(&t->dev_y, sizeof(unsigned long long*) * world);
     cudaIpcMemHandle_t h;
     if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, t->local);
     if (e != cudaSuccess) {
         cudaFree(t->local);
         cudaFree(t->dev_y);
-        cudaFree(t->dev_flags);
         delete t;
         return cuda_err(e, "tsrc_team_create");
     }
@@ -108,14 +104,9 @@ int tsrc_team_connect(tsrc_team* t, const void* handles) {
         t->peer[r] = static_cast<uint8_t*>(p);
         t->opened[r] = true;
     }
-    float* ys[64];
-    uint32_t* fs[64];
-    for (uint32_t r = 0; r < t->world; ++r) {
-        ys[r] = reinterpret_cast<float*>(t->peer[r]);
-        fs[r] = reinterpret_cast<uint32_t*>(t->peer[r] + t->staging_bytes);
-    }
-    cudaError_t e = cudaMemcpy(t->dev_y, ys, sizeof(float*) * t->world, cudaMemcpyHostToDevice);
-    if (e == cudaSuccess) e = cudaMemcpy(t->dev_flags, fs, sizeof(uint32_t*) * t->world, cudaMemcpyHostToDevice);
+    unsigned long long* ys[64];
+    for (uint32_t r = 0; r < t->world; ++r) ys[r] = reinterpret_cast<unsigned long long*>(t->peer[r]);
+    cudaError_t e = cudaMemcpy(t->dev_y, ys, sizeof(unsigned long long*) * t->world, cudaMemcpyHostToDevice);
     if (e != cudaSuccess) return cuda_err(e, "tsrc_team_connect");
     t->connected = true;
     return TSRC_OK;
@@ -124,18 +115,15 @@ int tsrc_team_connect(tsrc_team* t, const void* handles) {
 int tsrc_team_connect_local(tsrc_team* t, const tsrc_team* const* members) {
     if (!t || !members) return tsrc::set_error(TSRC_E_ARG, "tsrc_team_connect_local: NULL argument");
     if (t->connected) return tsrc::set_error(TSRC_E_ARG, "tsrc_team_connect_local: already connected");
-    float* ys[64];
-    uint32_t* fs[64];
+    unsigned long long* ys[64];
     for (uint32_t r = 0; r < t->world; ++r) {
         const tsrc_team* m = members[r];
         if (!m || m->world != t->world || m->rank != r || m->n_max != t->n_max)
             return tsrc::set_error(TSRC_E_ARG, "tsrc_team_connect_local: members must be ranks 0..world-1 of equal teams");
         t->peer[r] = m->local;
-        ys[r] = reinterpret_cast<float*>(m->local);
-        fs[r] = reinterpret_cast<uint32_t*>(m->local + m->staging_bytes);
+        ys[r] = reinterpret_cast<unsigned long long*>(m->local);
     }
-    cudaError_t e = cudaMemcpy(t->dev_y, ys, sizeof(float*) * t->world, cudaMemcpyHostToDevice);
-    if (e == cudaSuccess) e = cudaMemcpy(t->dev_flags, fs, sizeof(uint32_t*) * t->world, cudaMemcpyHostToDevice);
+    cudaError_t e = cudaMemcpy(t->dev_y, ys, sizeof(unsigned long long*) * t->world, cudaMemcpyHostToDevice);
     if (e != cudaSuccess) return cuda_err(e, "tsrc_team_connect_local");
     t->connected = true;
     return TSRC_OK;
@@ -148,7 +136,6 @@ int tsrc_team_free(tsrc_team* t) {
         if (t->opened[r]) cudaIpcCloseMemHandle(t->peer[r]);
     cudaFree(t->local);
     cudaFree(t->dev_y);
-    cudaFree(t->dev_flags);
     delete t;
     return TSRC_OK;
 }
@@ -168,8 +155,7 @@ int tsrc_mul_mat_allgather(tsrc_ctx* ctx, tsrc_team* t, const tsrc_weight* w, co
     a.T = 1;
     a.y = y;
     a.team_y = t->dev_y;
-    a.team_flags = t->dev_flags;
-    a.team_state = reinterpret_cast<uint32_t*>(t->local + t->staging_bytes + a256((size_t)t->world * 4u));
+    a.team_state = reinterpret_cast<uint32_t*>(t->local + t->staging_bytes);
     a.team_world = t->world;
     a.team_rank = t->rank;
     a.team_row0 = row0;
