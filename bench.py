@@ -836,11 +836,10 @@ def main():
         step(i)
         y_host.copy_(y_full if world > 1 else y_loc, non_blocking=True)
 
-    # the ring's end-to-end steps (copy in, MUL_MAT, copy out) replayed from a CUDA graph, as the
-    # device-resident loop is: the copies stay inside every step, the Python issue cost does not
+    # (1) serial: copy in, MUL_MAT, copy out, one after the other on one stream
     egraph = capture(torch, lambda: [e2e_step(i) for i in range(n_copies)], barrier) if use_graph else None
 
-    def e2e_loop(n):
+    def e2e_serial(n):
         if egraph is not None:
             reps, rem = divmod(n, n_copies)
             for _ in range(reps):
@@ -851,13 +850,70 @@ def main():
             for i in range(n):
                 e2e_step(i)
 
+    # (2) pipelined over steps: step i's activation comes in on one copy stream while step i - 1
+    # computes, and its result goes out on another while step i + 1 computes (the device buffers
+    # alternate by step parity); every step still copies its own input in and its own result out
+    xb = [x, torch.empty_like(x)]
+    yb_loc = [y_loc, torch.empty_like(y_loc)]
+    yb_full = [y_full, torch.empty_like(y_full)]
+    s_in, s_out = torch.cuda.Stream(), torch.cuda.Stream()
+
+    def mm_step(i, b):
+        if team is not None:
+            dev.mul_mat_allgather(team, weights[i % n_copies], xb[b], yb_full[b])
+            return
+        dev.mul_mat(weights[i % n_copies], xb[b], yb_loc[b], T=1)
+        if world > 1:
+            dist.all_gather_into_tensor(yb_full[b], torch.nn.functional.pad(yb_loc[b], (0, R - n_rows)))
+
+    def e2e_steps(n):
+        comp = torch.cuda.current_stream()
+        s_in.wait_stream(comp)
+        s_out.wait_stream(comp)
+        k_done, out_done = {}, {}
+        for i in range(n):
+            b = i % 2
+            ev_in = torch.cuda.Event()
+            with torch.cuda.stream(s_in):
+                if i >= 2:
+                    s_in.wait_event(k_done[i - 2])          # MUL_MAT i - 2 read xb[b]
+                xb[b].copy_(x_host, non_blocking=True)
+                ev_in.record(s_in)
+            comp.wait_event(ev_in)
+            if i >= 2:
+                comp.wait_event(out_done[i - 2])            # the copy out of step i - 2 read yb[b]
+            mm_step(i, b)
+            k_done[i] = torch.cuda.Event()
+            k_done[i].record(comp)
+            with torch.cuda.stream(s_out):
+                s_out.wait_event(k_done[i])
+                y_host.copy_(yb_full[b] if world > 1 else yb_loc[b], non_blocking=True)
+                out_done[i] = torch.cuda.Event()
+                out_done[i].record(s_out)
+        comp.wait_stream(s_in)
+        comp.wait_stream(s_out)
+
+    pgraph = capture(torch, lambda: e2e_steps(n_copies), barrier) if use_graph else None
+
+    def e2e_loop(n):
+        if pgraph is not None:
+            reps, rem = divmod(n, n_copies)
+            for _ in range(reps):
+                pgraph.replay()
+            if rem:
+                e2e_steps(rem)
+        else:
+            e2e_steps(n)
+
     kernel_loop(n_copies)
     e2e_loop(10)
+    e2e_serial(10)
     torch.cuda.synchronize()
     with Clocks(local) as clk:
         ms_value = timed(value_loop, args.steps)
         ms_kernel = timed(kernel_loop, n_kernel)
         ms_e2e = timed(e2e_loop, n_e2e)
+        ms_e2e_serial = timed(e2e_serial, n_e2e)
     clocks = clk.summary()
 
     total_bytes = algo_bytes(fmt, N, K)
@@ -930,7 +986,10 @@ def main():
                      "algorithmic_bytes_per_launch": shard_algo},
         "e2e": {"value": round(e2e, 2), "unit": "GB/s", "h2d_bytes_per_step": 4 * K,
                 "d2h_bytes_per_step": 4 * (R * world if world > 1 else n_rows),
-                "ms_per_step": round(ms_e2e / n_e2e, 6), "cuda_graph": egraph is not None},
+                "ms_per_step": round(ms_e2e / n_e2e, 6), "cuda_graph": pgraph is not None,
+                "pipelined": "step i+1's copy in and step i-1's copy out overlap step i's MUL_MAT (two copy streams)",
+                "serial_value": round(n_e2e * total_bytes / (ms_e2e_serial * 1e-3) / 1e9, 2),
+                "serial_ms_per_step": round(ms_e2e_serial / n_e2e, 6)},
         "gpu_launches": args.steps,
         "clocks": clocks,
         "cpu_baseline": cpu,
@@ -939,7 +998,7 @@ def main():
         line["also"] = also
     if rank == 0:
         print(json.dumps(line), flush=True)
-    del graph, kgraph, egraph
+    del graph, kgraph, egraph, pgraph
     if world > 1:
         dist.barrier()
     if team is not None:
