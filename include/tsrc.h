@@ -242,6 +242,13 @@ TSRC_API int tsrc_flash_attn(tsrc_ctx * ctx, const tsrc_kv * kv, const float * q
 // inv_n is 1/n as the backend computes it (tsr-build.cpp:405).
 TSRC_API int tsrc_rms_norm(tsrc_ctx * ctx, const float * x, uint32_t x_stride, float * y, uint32_t y_stride,
                            const float * w, uint32_t n, uint32_t rows, float eps, float inv_n, void * stream);
+// RMS_NORM + MUL of one token followed by its MUL_MAT, in one launch: y = MUL_MAT(W, RMS_NORM(x) * w)
+// with the values of tsrc_rms_norm (n = K) then tsrc_mul_mat (T = 1), bit for bit. No single
+// counterpart in the reference, whose graph runs the RMS_NORM kind and then the MUL_MAT kind
+// (ggml-tesseract tsr-build.cpp:405, ggml-tesseract.cpp:2790-2928); the normalised row never
+// goes through device memory. add / flags / s0 / s1 as tsrc_mul_mat; device pointers, on `stream`.
+TSRC_API int tsrc_mul_mat_rms(tsrc_ctx * ctx, const tsrc_weight * wt, const float * x, const float * norm_w, float eps,
+                              float inv_n, float * y, const float * add, uint32_t flags, float s0, float s1, void * stream);
 
 #define TSRC_ROPE_NORM 0u          // adjacent pairs (2i, 2i + 1)  (TSR_ROPE_MODE_NORM)
 #define TSRC_ROPE_NEOX 1u          // half-split pairs (i, i + n_dims / 2)

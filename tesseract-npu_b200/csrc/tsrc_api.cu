@@ -356,6 +356,25 @@ int tsrc_rms_norm(tsrc_ctx* ctx, const float* x, uint32_t x_stride, float* y, ui
     return e == cudaSuccess ? TSRC_OK : cuda_fail(e, "rms_norm launch");
 }
 
+int tsrc_mul_mat_rms(tsrc_ctx* ctx, const tsrc_weight* w, const float* x, const float* norm_w, float eps, float inv_n, float* y,
+                     const float* add, uint32_t flags, float s0, float s1, void* stream) {
+    tsrc::MvArgs a{};
+    uint32_t fmt = 0, x_stride = 0, y_stride = 0;
+    int rc = tsrc::mm_check(ctx, w, x, 1, &x_stride, y, &y_stride, add, 0, flags, s0, s1, &a, &fmt, "tsrc_mul_mat_rms");
+    if (rc != TSRC_OK) return rc;
+    a.x = x;
+    a.x_stride = x_stride;
+    a.T = 1;
+    a.y = y;
+    a.add = (flags & TSRC_MM_ADD) ? add : nullptr;
+    a.rms = 1u;
+    a.rms_w = norm_w;
+    a.rms_eps = daz_host(eps);
+    a.rms_inv_n = daz_host(inv_n);
+    cudaError_t e = tsrc::launch_matvec(fmt, a, static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? TSRC_OK : cuda_fail(e, "matvec launch");
+}
+
 int tsrc_rope(tsrc_ctx* ctx, const float* x, uint32_t x_stride, float* y, uint32_t y_stride, const int32_t* pos, uint32_t T,
               uint32_t n_heads, uint32_t head_dim, uint32_t n_dims, uint32_t mode, float ts, float attn_factor, void* stream) {
     if (!ctx || !x || !y || !pos) return fail(TSRC_E_ARG, "tsrc_rope: NULL argument");

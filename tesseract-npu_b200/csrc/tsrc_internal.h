@@ -35,6 +35,11 @@ struct MvArgs {
     uint32_t flags;
     float s0, s1;
     int32_t* isum_out;        // optional: the kernel's exact block sums of token 0
+    // RMS_NORM (+ MUL) of the token fused in front of QACT (T = 1; rms = 0: off): the activation is
+    // y_j = canon(FM(fmul(daz(x_j), scale), w_j)) with the RMS_NORM kind's scale (tsrc_vu.cu)
+    const float* rms_w;       // the norm weight, or NULL (no MUL)
+    float rms_eps, rms_inv_n;
+    uint32_t rms;
     // fused all-gather over a team of GPUs (one token; team_world = 0: off). Row n of the shard
     // is stored into every rank's staging buffer at team_row0 + n (half (step & 1) of [2][team_n])
     // as one 64-bit word {value bits, step + 1}; every CTA then copies its share of the full

@@ -6,7 +6,8 @@
 // residual ADD; then the output RMS_NORM + MUL and the head MUL_MAT of the last token.
 //
 // Each residual ADD is the MUL_MAT's addend epilogue (fadd(x, dot): the same value as the ADD
-// node). q, k and v are one MUL_MAT over the rows of the three matrices stacked (every output row is
+// node); for one token each RMS_NORM + MUL runs inside the MUL_MAT that consumes it
+// (tsrc_mul_mat_rms: the same values, one launch and no round trip of the normalised row). q, k and v are one MUL_MAT over the rows of the three matrices stacked (every output row is
 // its own dot product, so the values are those of three MUL_MATs), and so are gate and up; ROPE of
 // q and k is one launch over their heads, with c_i and s_i of every position precomputed once per
 // model by the same device code (a table lookup instead of the per-token angle recurrence). Weights come from tsrc_weight_synth (seeded); the f32 vectors (norm weights, biases) from
@@ -259,8 +260,13 @@ int forward_body(tsrc_model* m, const int32_t* ids, uint32_t T, uint32_t pos0, f
     if (rc == TSRC_OK && (call) != cudaSuccess) rc = tsrc::api_fail(TSRC_E_CUDA, what)
     for (uint32_t l = 0; l < c.n_layer; ++l) {
         const tsrc_model::Layer& L = m->layers[l];
-        TSRC_M(tsrc_rms_norm(ctx, m->x, E, m->h, E, L.attn_norm, E, T, c.rms_eps, inv_n, stream));
-        TSRC_M(tsrc_mul_mat(ctx, L.wqkv, m->h, T, E, m->qkv, QKV, L.bqkv, 0, L.bqkv ? TSRC_MM_ADD : 0u, 1.0f, 1.0f, stream));
+        if (T == 1) {                                     // one token: RMS_NORM + MUL fused into the MUL_MAT
+            TSRC_M(tsrc_mul_mat_rms(ctx, L.wqkv, m->x, L.attn_norm, c.rms_eps, inv_n, m->qkv, L.bqkv,
+                                    L.bqkv ? TSRC_MM_ADD : 0u, 1.0f, 1.0f, stream));
+        } else {
+            TSRC_M(tsrc_rms_norm(ctx, m->x, E, m->h, E, L.attn_norm, E, T, c.rms_eps, inv_n, stream));
+            TSRC_M(tsrc_mul_mat(ctx, L.wqkv, m->h, T, E, m->qkv, QKV, L.bqkv, 0, L.bqkv ? TSRC_MM_ADD : 0u, 1.0f, 1.0f, stream));
+        }
         {   // ROPE of q and k, SET_ROWS of k and v into the layer's q8_0 cache: one launch
             tsrc::RopeKvst rk{};
             rk.qkv = m->qkv;
@@ -289,16 +295,19 @@ int forward_body(tsrc_model* m, const int32_t* ids, uint32_t T, uint32_t pos0, f
         }
         TSRC_M(tsrc_flash_attn(ctx, L.kv, q, T, c.n_head, n_kv, mask, n_kv, m->kq_scale, pos0, n_kv, &fa, m->att, stream));
         TSRC_M(tsrc_mul_mat(ctx, L.wo, m->att, T, Hq, m->x, E, m->x, E, TSRC_MM_ADD, 1.0f, 1.0f, stream));
-        TSRC_M(tsrc_rms_norm(ctx, m->x, E, m->h, E, L.ffn_norm, E, T, c.rms_eps, inv_n, stream));
-        TSRC_M(tsrc_mul_mat(ctx, L.wgu, m->h, T, E, m->gu, 2u * F, nullptr, 0, 0u, 1.0f, 1.0f, stream));
+        if (T == 1) {
+            TSRC_M(tsrc_mul_mat_rms(ctx, L.wgu, m->x, L.ffn_norm, c.rms_eps, inv_n, m->gu, nullptr, 0u, 1.0f, 1.0f, stream));
+        } else {
+            TSRC_M(tsrc_rms_norm(ctx, m->x, E, m->h, E, L.ffn_norm, E, T, c.rms_eps, inv_n, stream));
+            TSRC_M(tsrc_mul_mat(ctx, L.wgu, m->h, T, E, m->gu, 2u * F, nullptr, 0, 0u, 1.0f, 1.0f, stream));
+        }
         TSRC_M(tsrc_vop(ctx, TSRC_VOP_SWIGLU, m->gu, 2u * F, m->gu + F, 2u * F, m->gu, 2u * F, F, T, stream));
         TSRC_M(tsrc_mul_mat(ctx, L.wd, m->gu, T, 2u * F, m->x, E, m->x, E, TSRC_MM_ADD, 1.0f, 1.0f, stream));
     }
     // the last token: output norm and head
     const float* xl = m->x + (size_t)(T - 1u) * E;
-    TSRC_M(tsrc_rms_norm(ctx, xl, E, m->h, E, m->out_norm, E, 1, c.rms_eps, inv_n, stream));
-    TSRC_M(tsrc_mul_mat(ctx, c.tied_head ? m->tok_embd : m->output, m->h, 1, E, logits, c.n_vocab, nullptr, 0, 0u, 1.0f, 1.0f,
-                        stream));
+    TSRC_M(tsrc_mul_mat_rms(ctx, c.tied_head ? m->tok_embd : m->output, xl, m->out_norm, c.rms_eps, inv_n, logits, nullptr, 0u,
+                            1.0f, 1.0f, stream));
 #undef TSRC_MC
 #undef TSRC_M
     return rc;

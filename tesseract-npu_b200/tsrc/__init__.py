@@ -57,6 +57,7 @@ _SIGS = {
     "tsrc_weight_free": (_i, [_p]),
     "tsrc_mul_mat": (_i, [_p, _p, _p, _u32, _u32, _p, _u32, _p, _u32, _u32, _f32, _f32, _p]),
     "tsrc_rms_norm": (_i, [_p, _p, _u32, _p, _u32, _p, _u32, _u32, _f32, _f32, _p]),
+    "tsrc_mul_mat_rms": (_i, [_p, _p, _p, _p, _f32, _f32, _p, _p, _u32, _f32, _f32, _p]),
     "tsrc_model_create": (_i, [_p, _p, _u64, ct.POINTER(_p)]),
     "tsrc_model_free": (_i, [_p]),
     "tsrc_model_forward": (_i, [_p, _p, _u32, _u32, _p, _p]),
@@ -226,6 +227,16 @@ class Device:
         inv_n = float(np.float32(1.0) / np.float32(n)) if inv_n is None else inv_n
         _check(lib().tsrc_rms_norm(self.handle, _addr(x), x_stride, _addr(y), y_stride, _addr(w), n, rows, eps, inv_n,
                                    _stream(stream)))
+
+    def mul_mat_rms(self, w: "Weight", x, y, norm_w=None, eps: float = 1e-5, inv_n: float | None = None, add=None,
+                    flags: int = 0, s0: float = 1.0, s1: float = 1.0, stream=None) -> None:
+        """y = MUL_MAT(w, RMS_NORM(x) * norm_w) for one token in one launch (bit for bit rms_norm then
+        mul_mat)."""
+        inv_n = float(np.float32(1.0) / np.float32(w.K)) if inv_n is None else inv_n
+        if add is not None:
+            flags |= MM_ADD
+        _check(lib().tsrc_mul_mat_rms(self.handle, w.handle, _addr(x), _addr(norm_w), eps, inv_n, _addr(y), _addr(add),
+                                      flags, s0, s1, _stream(stream)))
 
     def rope(self, x, y, pos, T: int, n_heads: int, head_dim: int, n_dims: int, mode: int, ts: float,
              attn_factor: float = 1.0, x_stride: int = 0, y_stride: int = 0, stream=None) -> None:
