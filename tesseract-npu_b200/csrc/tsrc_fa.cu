@@ -406,7 +406,9 @@ __global__ void __launch_bounds__(kFaThreads, 1) fa_chunk_kernel(FaLaunch a) {
                 if (sg0 > 0) stage_v(sg, 0, true);
                 cp_async_wait_all();
                 __syncwarp();
-#pragma unroll
+                // rows one at a time (their state lives in shared memory): a quarter of the code of
+                // the unrolled form for the same work (the kernel's second stall is instruction fetch)
+#pragma unroll 1
                 for (uint32_t r = 0; r < RB; ++r) {
                     if (r >= nr) break;
 #pragma unroll
