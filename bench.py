@@ -62,6 +62,37 @@ def capture(torch, body, sync):
         return None
 
 
+def pipelined(torch, n, copy_in, compute, copy_out, s_in, s_out):
+    """Issues n end-to-end steps with step i + 1's copy in (stream s_in) and step i - 1's copy out
+    (stream s_out) under step i's compute on the current stream; the device buffers alternate by
+    step parity (b = i % 2), and every step still copies its own input in and its result out."""
+    comp = torch.cuda.current_stream()
+    s_in.wait_stream(comp)
+    s_out.wait_stream(comp)
+    k_done, out_done = {}, {}
+    for i in range(n):
+        b = i % 2
+        ev_in = torch.cuda.Event()
+        with torch.cuda.stream(s_in):
+            if i >= 2:
+                s_in.wait_event(k_done[i - 2])              # step i - 2 computed from buffer b
+            copy_in(b)
+            ev_in.record(s_in)
+        comp.wait_event(ev_in)
+        if i >= 2:
+            comp.wait_event(out_done[i - 2])                # step i - 2's result left buffer b
+        compute(i, b)
+        k_done[i] = torch.cuda.Event()
+        k_done[i].record(comp)
+        with torch.cuda.stream(s_out):
+            s_out.wait_event(k_done[i])
+            copy_out(b)
+            out_done[i] = torch.cuda.Event()
+            out_done[i].record(s_out)
+    comp.wait_stream(s_in)
+    comp.wait_stream(s_out)
+
+
 # prefill MUL_MAT on the tensor cores (many tokens): BASELINE configs 5 and 4 FFN shapes
 PREFILL = [
     (1, 14336, 4096, 2048, 501, "cfg5 FFN gate/up: Q4_K 14336x4096, 2048-token prefill"),
@@ -308,23 +339,32 @@ def fa_measure(dev, tsrc, torch, steps, warmup, world=1, rank=0, dist=None):
     o_host = torch.empty((world, h_loc * G, D)).pin_memory()
     n_e2e = min(steps, 2000)
 
-    def e2e_step(i):
-        q.copy_(q_host, non_blocking=True)
-        step(i)
-        o_host.copy_(out_all if world > 1 else out.view(1, h_loc * G, D), non_blocking=True)
+    # end to end, pipelined over steps as for the matvec (q and out alternate by step parity)
+    qb, ob, oab = [q, torch.empty_like(q)], [out, torch.empty_like(out)], [out_all, torch.empty_like(out_all)]
+    s_in, s_out = torch.cuda.Stream(), torch.cuda.Stream()
 
-    egraph = capture(torch, lambda: [e2e_step(i) for i in range(n_ring)], sync_all)
+    def fa_step(i, b):
+        dev.flash_attn(kvs[i % n_ring], qb[b], ob[b], T=1, n_head=h_loc * G, n_kv=n_kv, scale=scale,
+                       new=(n_kv - 1, n_kv), cfg=cfg)
+        if world > 1:
+            dist.all_gather_into_tensor(oab[b], ob[b])
+
+    def e2e_steps(n):
+        pipelined(torch, n, lambda b: qb[b].copy_(q_host, non_blocking=True), fa_step,
+                  lambda b: o_host.copy_(oab[b] if world > 1 else ob[b].view(1, h_loc * G, D), non_blocking=True),
+                  s_in, s_out)
+
+    egraph = capture(torch, lambda: e2e_steps(n_ring), sync_all)
 
     def e2e(n):
         if egraph is not None:
             reps, rem = divmod(n, n_ring)
             for _ in range(reps):
                 egraph.replay()
-            for i in range(rem):
-                e2e_step(i)
+            if rem:
+                e2e_steps(rem)
         else:
-            for i in range(n):
-                e2e_step(i)
+            e2e_steps(n)
 
     def timed(fn, n):
         if world > 1:
@@ -557,7 +597,8 @@ def run_fa(args):
                      "algorithmic_bytes_per_launch": shard},
         "e2e": {"value": round(info["e2e_steps"] * total / (ms_e2e * 1e-3) / 1e9, 2), "unit": "GB/s",
                 "h2d_bytes_per_step": info["h2d_bytes_per_step"], "d2h_bytes_per_step": info["d2h_bytes_per_step"],
-                "ms_per_step": round(ms_e2e / info["e2e_steps"], 6), "cuda_graph": info["e2e_cuda_graph"]},
+                "ms_per_step": round(ms_e2e / info["e2e_steps"], 6), "cuda_graph": info["e2e_cuda_graph"],
+                "pipelined": "step i+1's copy in and step i-1's copy out overlap step i's FA (two copy streams)"},
         "gpu_launches": 2 * steps,
         "clocks": clk.summary(),
         "cpu_baseline": cpu,
@@ -867,31 +908,8 @@ def main():
             dist.all_gather_into_tensor(yb_full[b], torch.nn.functional.pad(yb_loc[b], (0, R - n_rows)))
 
     def e2e_steps(n):
-        comp = torch.cuda.current_stream()
-        s_in.wait_stream(comp)
-        s_out.wait_stream(comp)
-        k_done, out_done = {}, {}
-        for i in range(n):
-            b = i % 2
-            ev_in = torch.cuda.Event()
-            with torch.cuda.stream(s_in):
-                if i >= 2:
-                    s_in.wait_event(k_done[i - 2])          # MUL_MAT i - 2 read xb[b]
-                xb[b].copy_(x_host, non_blocking=True)
-                ev_in.record(s_in)
-            comp.wait_event(ev_in)
-            if i >= 2:
-                comp.wait_event(out_done[i - 2])            # the copy out of step i - 2 read yb[b]
-            mm_step(i, b)
-            k_done[i] = torch.cuda.Event()
-            k_done[i].record(comp)
-            with torch.cuda.stream(s_out):
-                s_out.wait_event(k_done[i])
-                y_host.copy_(yb_full[b] if world > 1 else yb_loc[b], non_blocking=True)
-                out_done[i] = torch.cuda.Event()
-                out_done[i].record(s_out)
-        comp.wait_stream(s_in)
-        comp.wait_stream(s_out)
+        pipelined(torch, n, lambda b: xb[b].copy_(x_host, non_blocking=True), mm_step,
+                  lambda b: y_host.copy_(yb_full[b] if world > 1 else yb_loc[b], non_blocking=True), s_in, s_out)
 
     pgraph = capture(torch, lambda: e2e_steps(n_copies), barrier) if use_graph else None
 
