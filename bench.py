@@ -215,11 +215,86 @@ def model_measure(dev, tsrc, torch, name, steps, warmup, e2e_steps=32):
     torch.cuda.synchronize()
     e2e_ms = e0.elapsed_time(e1) / e2e_steps
     algo = model_algo_bytes(s, kv0 + steps // 2)
-    # state, GET_ROWS; per layer RMS_NORM, 4 MUL_MATs, ROPE + KVST, FA chunk + merge, RMS_NORM,
-    # SWIGLU; then RMS_NORM and the head MUL_MAT
-    launches = 4 + 10 * s["n_layer"]
+    # state, GET_ROWS; per layer 4 MUL_MATs (two with RMS_NORM fused in), ROPE + KVST, FA chunk +
+    # merge, SWIGLU; then the head MUL_MAT (RMS_NORM fused in)
+    launches = 3 + 8 * s["n_layer"]
     return dict(shape=s, prefill_ms=prefill_ms, ms=ms, e2e_ms=e2e_ms, algo_bytes=algo, launches=launches,
                 n_kv=(kv0, pos)), model
+
+
+def model_measure_tp(dev, tsrc, torch, dist, name, steps, warmup, rank, world, e2e_steps=32):
+    """Decode of the config split over `world` GPUs (tsrc_model_create_tp over a team): every
+    layer's cache cells [0, prompt) are loaded with seeded rows through KVST (this rank's KV heads'
+    columns) in place of the prompt's prefill, then `warmup` + `steps` timed decode tokens and
+    `e2e_steps` with the token id in from pinned host memory and the logits out. Device times are
+    the maximum over the ranks."""
+    spec = MODELS[name]
+    prompt = spec["prompt"]
+    n_ctx = prompt + warmup + steps + e2e_steps
+    s = dict(spec["shape"], n_ctx=n_ctx)
+    n_max = max(s["n_vocab"], s["n_ff"], s["n_head"] * s["head_dim"], s["n_embd"])
+    team = dev.team_create(rank, world, n_max)
+    hs = [None] * world
+    dist.all_gather_object(hs, team.ipc_handle)
+    team.connect(b"".join(hs))
+    model = tsrc.Model(dev, tsrc.ModelCfg(**s), seed=spec["seed"], team=team)
+    E = s["n_head_kv"] * s["head_dim"]
+    w = E // world
+    for l in range(s["n_layer"]):
+        g = torch.Generator(device="cuda").manual_seed(spec["seed"] * 100 + l)
+        kv = model.kv(l)
+        for which in (tsrc.KV_K, tsrc.KV_V):
+            rows = torch.randn((prompt, E), device="cuda", generator=g)
+            kv.set_rows(which, rows[:, rank * w:(rank + 1) * w].contiguous())
+    g = torch.Generator(device="cuda")
+    g.manual_seed(spec["seed"])
+    ids = torch.randint(0, s["n_vocab"], (n_ctx,), dtype=torch.int32, device="cuda", generator=g)
+    logits = torch.empty(s["n_vocab"], device="cuda")
+    one = torch.empty(1, dtype=torch.int32, device="cuda")
+
+    def barrier():
+        dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(v):
+        t = torch.tensor([v], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    pos = prompt
+    for _ in range(warmup):
+        one.copy_(ids[pos:pos + 1])
+        model.decode(one, pos, logits)
+        pos += 1
+    barrier()
+    kv0 = pos
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        one.copy_(ids[pos:pos + 1])
+        model.decode(one, pos, logits)
+        pos += 1
+    e1.record()
+    barrier()
+    ms = max_over_ranks(e0.elapsed_time(e1) / steps)
+    host_ids = ids[pos:pos + e2e_steps].cpu().pin_memory()
+    host_logits = torch.empty(s["n_vocab"], pin_memory=True)
+    barrier()
+    e0.record()
+    for i in range(e2e_steps):
+        one.copy_(host_ids[i:i + 1], non_blocking=True)
+        model.decode(one, pos, logits)
+        host_logits.copy_(logits, non_blocking=True)
+        pos += 1
+    e1.record()
+    barrier()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1) / e2e_steps)
+    # state, GET_ROWS; per layer q / k / v (RMS_NORM fused), ROPE + KVST, FA chunk + merge, the
+    # attention gather, o (+ gather), gate / up (RMS_NORM fused), SWIGLU, the SWIGLU gather, down
+    # (+ gather); then the head (RMS_NORM and the gather fused)
+    launches = 3 + 10 * s["n_layer"]
+    return dict(shape=s, ms=ms, e2e_ms=e2e_ms, algo_bytes=model_algo_bytes(s, kv0 + steps // 2), launches=launches,
+                n_kv=(kv0, pos)), model, team
 
 
 def cpu_reference_model(name, threads, model=None):
@@ -618,12 +693,9 @@ def run_model(args):
     import tsrc
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
-    if world > 1:
-        if rank == 0:
-            print(json.dumps({"metric": "decode tokens/s", "unavailable": "the model runner is single-GPU (tensor-parallel "
-                              "model not built); the matvec and FA configs shard across GPUs"}), flush=True)
-        return 0
     spec = MODELS[args.config]
+    if world > 1:
+        return run_model_tp(args, spec, world, rank)
     args.warmup = min(args.warmup, 8)                      # decode tokens before timing (>= 3)
     steps = max(1, min(args.steps, spec["decode"] - args.warmup))
     torch.cuda.set_device(0)
@@ -661,6 +733,61 @@ def run_model(args):
         "cpu_baseline": cpu,
     }
     print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_model_tp(args, spec, world, rank):
+    """--config cfg4 / cfg5 on N > 1 GPUs: decode tokens/s of the model split over the GPUs."""
+    import datetime
+    import torch
+    import torch.distributed as dist
+    import tsrc
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+    s = spec["shape"]
+    if s["n_head_kv"] % world:
+        if rank == 0:
+            print(json.dumps({"metric": "decode tokens/s", "impl": "ours", "n_gpus": world,
+                              "unavailable": f"{s['n_head_kv']} KV heads do not split over {world} GPUs"}), flush=True)
+        dist.barrier()
+        dist.destroy_process_group()
+        return 0
+    args.warmup = min(args.warmup, 8)
+    steps = max(1, min(args.steps, spec["decode"] - args.warmup))
+    dev = tsrc.Device(local)
+    with Clocks(local) as clk:
+        r, model, team = model_measure_tp(dev, tsrc, torch, dist, args.config, steps, args.warmup, rank, world)
+    clocks = clk.summary()
+    dist.barrier()
+    model.free()
+    team.free()
+    peak, peak_kind = peaks()
+    achieved = r["algo_bytes"] / (r["ms"] * 1e-3) / 1e9
+    line = {
+        "metric": "decode tokens/s", "value": round(1e3 / r["ms"], 2), "unit": "tokens/s", "n_gpus": world, "steps": steps,
+        "warmup": args.warmup, "ms_per_step": round(r["ms"], 4), "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "int8",
+        "data": "synthetic (random-init weights quantized on device, random token ids, seeded KV cache rows)",
+        "config": {"workload": spec["desc"], "parallelism": f"tensor-parallel x{world} (heads, rows)",
+                   "kv_cells_during_timing": list(r["n_kv"]),
+                   "kv": f"cells [0, {spec['prompt']}) loaded with seeded rows through KVST in place of the prompt's prefill",
+                   "collective": "tagged-word gathers over NVLink (attention output, SWIGLU row; fused into o, down, head)",
+                   "l2": f"inputs larger than L2 (a token reads {r['algo_bytes'] / 1e6:.0f} MB over all GPUs)", "cuda_graph": True},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak * world, "unit": "GB/s",
+                     "frac": round(achieved / (peak * world), 4), "traffic": None, "peak_kind": peak_kind + " x GPUs",
+                     "kernel": "whole decode step (all kernels, all GPUs)", "algorithmic_bytes_per_step": r["algo_bytes"]},
+        "e2e": {"value": round(1e3 / r["e2e_ms"], 2), "unit": "tokens/s", "h2d_bytes_per_step": 4,
+                "d2h_bytes_per_step": 4 * r["shape"]["n_vocab"], "ms_per_step": round(r["e2e_ms"], 4)},
+        "gpu_launches": r["launches"] * steps,
+        "clocks": clocks,
+        "cpu_baseline": None,
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    dev.close()
+    dist.barrier()
+    dist.destroy_process_group()
     return 0
 
 

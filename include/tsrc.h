@@ -298,7 +298,20 @@ typedef struct tsrc_model_cfg {
 // 16 (l + 1) + i for layer l's i = 0 [q | k | v] rows, 1 o, 2 [gate | up] rows, 3 down; sigma 0.02);
 // f32 vectors from tsrc_model_f32_value.
 TSRC_API int tsrc_model_create(tsrc_ctx * ctx, const tsrc_model_cfg * cfg, uint64_t seed, tsrc_model ** out);
+// The same model split over a connected team (no counterpart in the reference, whose channels live
+// on one card): this rank holds the q heads and KV heads [rank, rank + 1) x (heads / world) (n_head_kv
+// must split evenly) with their q / k / v rows and cache, and the symmetric row shards (R = ceil(N /
+// world), sw/sim/tsr_ref.c:335-357) of o, gate / up (of n_ff), down and the head; every exchange is
+// the team's tagged-word gather (the attention output and the SWIGLU row, then o, down and the head
+// fused with their gathers). Runs one token at a time (tsrc_model_forward with T = 1, or
+// tsrc_model_decode): logits (all n_vocab) on every rank equal the single-GPU model's. The team's
+// n_max must hold max(n_vocab, n_ff, n_head * head_dim, n_embd).
+TSRC_API int tsrc_model_create_tp(tsrc_ctx * ctx, const tsrc_model_cfg * cfg, uint64_t seed, tsrc_team * team,
+                                  tsrc_model ** out);
 TSRC_API int tsrc_model_free(tsrc_model * m);
+// Layer `layer`'s q8_0 KV cache (owned by the model; a tensor-parallel rank's holds its KV heads),
+// e.g. to load cells written elsewhere with tsrc_kv_set_rows / tsrc_kv_set_bytes.
+TSRC_API int tsrc_model_kv(const tsrc_model * m, uint32_t layer, tsrc_kv ** out);
 // Runs tokens ids[0..T) (device int32) at positions pos0 .. pos0 + T - 1: their K / V rows are stored
 // at cells pos0 .. and attention is causal over cells [0, pos0 + t]. logits (device f32 [n_vocab])
 // receives the head output of the last token. Queued on `stream`.

@@ -213,6 +213,32 @@ namespace tsrc {
 
 int set_error(int code, const char* msg) { return fail(code, "%s", msg); }
 
+int weight_synth_ranges(tsrc_ctx* ctx, uint32_t fmt, uint32_t N, uint32_t K, const uint32_t* r0, const uint32_t* n,
+                        uint32_t count, uint64_t seed, float sigma, tsrc_weight** out) {
+    uint32_t total = 0;
+    for (uint32_t i = 0; i < count; ++i) {
+        if ((uint64_t)r0[i] + n[i] > N) return fail(TSRC_E_ARG, "weight_synth_ranges: range outside [0, %u)", N);
+        total += n[i];
+    }
+    tsrc_weight* w = nullptr;
+    int rc = new_weight(ctx, fmt, total, K, 0, total, &w);
+    if (rc) return rc;
+    cudaError_t e = cudaSuccess;
+    uint32_t at = 0;
+    for (uint32_t i = 0; i < count && e == cudaSuccess; ++i) {
+        e = launch_synth(fmt, K, r0[i], n[i], seed, sigma, w->qs + qs_row_bytes(fmt, K) * at, w->meta + meta_row_bytes(fmt, K) * at,
+                         nullptr);
+        at += n[i];
+    }
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) {
+        drop_weight(w);
+        return cuda_fail(e, "synth launch");
+    }
+    *out = w;
+    return TSRC_OK;
+}
+
 int weight_rows(const tsrc_weight* w, uint32_t* N, uint32_t* row0, uint32_t* n_rows) {
     *N = w->N;
     *row0 = w->row0;

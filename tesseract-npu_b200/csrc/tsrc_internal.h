@@ -47,11 +47,36 @@ struct MvArgs {
     unsigned long long* const* team_y;  // device array [world]: each rank's staging [2][team_n] tagged words
     uint32_t* team_state;     // this rank: [0] steps done, [1] CTAs finished in this launch
     uint32_t team_world, team_rank, team_row0, team_n;
+    uint32_t team_half;       // words per staging half (the team's capacity; calls of any N alternate halves)
 };
 
 cudaError_t launch_qact(uint32_t kind, const float* x, uint32_t K, uint32_t T, uint32_t x_stride, int8_t* q, float* d,
                         int16_t* bs, cudaStream_t st);
 cudaError_t launch_matvec(uint32_t fmt, const MvArgs& a, cudaStream_t st);
+// All-gather of a plain vector over a team (the tagged-word exchange of the fused MUL_MAT, without
+// the MUL_MAT): src [n_local] of this rank lands at dst[offset .. offset + n_local) on every rank.
+struct TeamGather {
+    unsigned long long* const* team_y;
+    uint32_t* team_state;
+    uint32_t world, rank, half;
+    const float* src;
+    uint32_t n_local, offset, n;
+    float* dst;
+};
+cudaError_t launch_team_gather(const TeamGather& g, cudaStream_t st);
+}  // namespace tsrc
+struct tsrc_team;
+struct tsrc_weight;
+namespace tsrc {
+// tsrc_team.cu: the model runner's tensor-parallel steps (see there)
+int team_info(const tsrc_team* t, uint32_t* rank, uint32_t* world, uint32_t* n_max);
+int team_mul_mat(tsrc_ctx* ctx, tsrc_team* t, const tsrc_weight* w, const float* x, float* y, const float* add,
+                 const float* rms_w, float eps, float inv_n, bool rms, void* stream);
+int team_gather(tsrc_team* t, const float* src, uint32_t n_local, uint32_t offset, float* dst, uint32_t n, void* stream);
+// tsrc_api.cu: a weight whose rows are row ranges [r0[i], r0[i] + n[i]) of one synthetic N-row
+// matrix, stacked in that order (the rows equal those of tsrc_weight_synth's full matrix)
+int weight_synth_ranges(tsrc_ctx* ctx, uint32_t fmt, uint32_t N, uint32_t K, const uint32_t* r0, const uint32_t* n,
+                        uint32_t count, uint64_t seed, float sigma, tsrc_weight** out);
 // Many-token MUL_MAT on the tcgen05 tensor cores (Q8_0; the QA image in qx / dx, any T).
 cudaError_t launch_mm_tc(uint32_t fmt, const MvArgs& a, cudaStream_t st);
 

@@ -572,12 +572,12 @@ __device__ __forceinline__ void team_finish(const MvArgs& a, uint32_t step, uint
                                             uint32_t r_begin, uint32_t r_end) {
     __syncthreads();                                     // the CTA's rows are in shared memory
     const unsigned long long tag = (unsigned long long)(step + 1u) << 32;
-    const size_t o = (size_t)(step & 1u) * a.team_n + a.team_row0 + r_begin;
+    const size_t o = (size_t)(step & 1u) * a.team_half + a.team_row0 + r_begin;
     for (uint32_t r = 0; r < a.team_world; ++r)
         for (uint32_t i = threadIdx.x; i < r_end - r_begin; i += blockDim.x)
             st_relaxed_sys64(a.team_y[r] + o + i, tag | __float_as_uint(rows[i]));
     // this CTA's share of the gathered vector
-    const unsigned long long* src = a.team_y[a.team_rank] + (size_t)(step & 1u) * a.team_n;
+    const unsigned long long* src = a.team_y[a.team_rank] + (size_t)(step & 1u) * a.team_half;
     const uint32_t n = a.team_n, share = (n + gridDim.x - 1u) / gridDim.x, i0 = blockIdx.x * share;
     const uint32_t i1 = min(n, i0 + share);
     bool gave_up = false;
@@ -601,6 +601,47 @@ __device__ __forceinline__ void team_finish(const MvArgs& a, uint32_t step, uint
         a.team_state[0] = step + 1u;
     }
     (void)sflag;
+}
+
+// The same exchange for a plain vector: every CTA stores its share of this rank's src into every
+// rank's staging half as tagged words, then copies its share of the whole vector out.
+__global__ void __launch_bounds__(256) team_gather_kernel(TeamGather g) {
+    const uint32_t step = *reinterpret_cast<volatile uint32_t*>(g.team_state);
+    const unsigned long long tag = (unsigned long long)(step + 1u) << 32;
+    const size_t half = (size_t)(step & 1u) * g.half;
+    const uint32_t ls = (g.n_local + gridDim.x - 1u) / gridDim.x, l0 = blockIdx.x * ls, l1 = min(g.n_local, l0 + ls);
+    for (uint32_t r = 0; r < g.world; ++r)
+        for (uint32_t i = l0 + threadIdx.x; i < l1; i += blockDim.x)
+            st_relaxed_sys64(g.team_y[r] + half + g.offset + i, tag | __float_as_uint(g.src[i]));
+    const unsigned long long* src = g.team_y[g.rank] + half;
+    const uint32_t share = (g.n + gridDim.x - 1u) / gridDim.x, i0 = blockIdx.x * share, i1 = min(g.n, i0 + share);
+    bool gave_up = false;
+    for (uint32_t i = i0 + threadIdx.x; i < i1; i += blockDim.x) {
+        unsigned long long w = ld_relaxed_sys64(src + i);
+        uint32_t it = 0;
+        while ((w & 0xFFFFFFFF00000000ull) != tag && !gave_up) {
+            if (++it >= kTeamSpin) {
+                gave_up = true;
+                atomicCAS(&g_mv_error, 0u, 2u);
+            }
+            __nanosleep(64);
+            w = ld_relaxed_sys64(src + i);
+        }
+        g.dst[i] = __uint_as_float((uint32_t)w);
+    }
+    __syncthreads();
+    if (threadIdx.x == 0 && atomicAdd(g.team_state + 1, 1u) + 1u == gridDim.x) {
+        g.team_state[1] = 0u;
+        g.team_state[0] = step + 1u;
+    }
+}
+
+cudaError_t launch_team_gather(const TeamGather& g, cudaStream_t st) {
+    if (g.n == 0) return cudaSuccess;
+    uint32_t blocks = (g.n + 1023u) / 1024u;
+    blocks = blocks < 1u ? 1u : (blocks > 64u ? 64u : blocks);
+    team_gather_kernel<<<blocks, 256, 0, st>>>(g);
+    return cudaGetLastError();
 }
 
 // ---- the kernel ---------------------------------------------------------------------------------

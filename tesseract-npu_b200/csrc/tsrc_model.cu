@@ -12,7 +12,9 @@
 // q and k is one launch over their heads, with c_i and s_i of every position precomputed once per
 // model by the same device code (a table lookup instead of the per-token angle recurrence). Weights come from tsrc_weight_synth (seeded); the f32 vectors (norm weights, biases) from
 // splitmix64 (tsrc_model_f32_value), so a checker can rebuild them.
+#include <algorithm>
 #include <cmath>
+#include <initializer_list>
 #include <cstdio>
 #include <cstring>
 #include <vector>
@@ -59,6 +61,13 @@ struct tsrc_model {
     std::vector<FaNode> fa_nodes;
     uint32_t g_n_items = 0, g_n_tiles = 0, g_Tq0 = 0, g_nmax = 0;
     const void* g_ok = nullptr;
+    // tensor parallelism (tsrc_model_create_tp): this rank's heads and row ranges
+    tsrc_team* team = nullptr;
+    uint32_t rank = 0, world = 1;
+    uint32_t hq_loc = 0, hkv_loc = 0, f0 = 0, f_n = 0;   // local q / kv heads; gate / up rows [f0, f0 + f_n)
+    tsrc_weight* head_shard = nullptr;                   // rows of the head (the embedding when tied)
+    float* tp_bias = nullptr;                            // [n_layer][local q | k | v] bias slices
+    float* tp_act = nullptr;                             // SWIGLU rows of this rank [F], then the gathered [F]
 };
 
 namespace {
@@ -101,6 +110,9 @@ int tsrc_model_free(tsrc_model* m) {
     }
     if (m->tok_embd) tsrc_weight_free(m->tok_embd);
     if (m->output) tsrc_weight_free(m->output);
+    if (m->head_shard) tsrc_weight_free(m->head_shard);
+    cudaFree(m->tp_bias);
+    cudaFree(m->tp_act);
     if (m->gexec) cudaGraphExecDestroy(m->gexec);
     if (m->graph) cudaGraphDestroy(m->graph);
     cudaFree(m->dstate);
@@ -113,16 +125,30 @@ int tsrc_model_free(tsrc_model* m) {
     return TSRC_OK;
 }
 
-int tsrc_model_create(tsrc_ctx* ctx, const tsrc_model_cfg* cfg, uint64_t seed, tsrc_model** out) {
+}  // extern "C"
+
+static int model_create(tsrc_ctx* ctx, const tsrc_model_cfg* cfg, uint64_t seed, tsrc_team* team, tsrc_model** out) {
     if (!ctx || !cfg || !out) return tsrc::api_fail(TSRC_E_ARG, "tsrc_model_create: NULL argument");
     *out = nullptr;
     const tsrc_model_cfg& c = *cfg;
     if (c.n_layer == 0 || c.n_embd == 0 || c.n_ff == 0 || c.n_head == 0 || c.n_head_kv == 0 || c.n_head % c.n_head_kv ||
         c.n_vocab == 0 || c.n_ctx == 0 || (c.fmt != TSRC_FMT_Q8_0 && c.fmt != TSRC_FMT_Q4_K) || c.rope_mode > TSRC_ROPE_NEOX)
         return tsrc::api_fail(TSRC_E_ARG, "tsrc_model_create: a shape field is zero or out of range");
+    uint32_t rank = 0, world = 1, n_max = 0;
+    if (team) {
+        int rc = tsrc::team_info(team, &rank, &world, &n_max);
+        if (rc) return rc;
+        if (c.n_head_kv % world) return tsrc::api_fail(TSRC_E_ARG, "tsrc_model_create_tp: the KV heads do not split over the ranks");
+        const uint32_t need = std::max(std::max(c.n_vocab, c.n_ff), std::max(c.n_head * c.head_dim, c.n_embd));
+        if (n_max < need)
+            return tsrc::api_fail(TSRC_E_ARG, "tsrc_model_create_tp: the team's n_max is below max(n_vocab, n_ff, n_head * head_dim, n_embd)");
+    }
     tsrc_model* m = new tsrc_model();
     m->ctx = ctx;
     m->c = c;
+    m->team = team;
+    m->rank = rank;
+    m->world = world;
     m->ts = powf(c.rope_base, -2.0f / (float)c.head_dim);       // the backend's theta scale (host libm)
     m->kq_scale = 1.0f / sqrtf((float)c.head_dim);              // llama.cpp's kq_scale
     const uint32_t E = c.n_embd, D = c.head_dim, Hq = c.n_head * D, Hkv = c.n_head_kv * D, F = c.n_ff;
@@ -131,8 +157,28 @@ int tsrc_model_create(tsrc_ctx* ctx, const tsrc_model_cfg* cfg, uint64_t seed, t
     auto synth = [&](uint32_t N, uint32_t K, uint64_t s, tsrc_weight** w) {
         if (rc == TSRC_OK) rc = tsrc_weight_synth(ctx, c.fmt, N, K, 0, N, s, sigma, nullptr, w);
     };
+    // a rank's share of the rows (the symmetric split R = ceil(N / world), sw/sim/tsr_ref.c:335-357)
+    auto shard = [&](uint32_t N, uint32_t* r0, uint32_t* n) {
+        const uint32_t R = (N + world - 1u) / world;
+        *r0 = std::min(N, rank * R);
+        *n = std::min(N, *r0 + R) - *r0;
+    };
+    auto synth_shard = [&](uint32_t N, uint32_t K, uint64_t s, tsrc_weight** w) {
+        uint32_t r0 = 0, n = 0;
+        shard(N, &r0, &n);
+        if (rc == TSRC_OK) rc = tsrc_weight_synth(ctx, c.fmt, N, K, r0, n, s, sigma, nullptr, w);
+    };
+    auto synth_ranges = [&](uint32_t N, uint32_t K, std::initializer_list<uint32_t> r0, std::initializer_list<uint32_t> n,
+                            uint64_t s, tsrc_weight** w) {
+        if (rc == TSRC_OK)
+            rc = tsrc::weight_synth_ranges(ctx, c.fmt, N, K, r0.begin(), n.begin(), (uint32_t)r0.size(), s, sigma, w);
+    };
+    m->hq_loc = c.n_head / world;
+    m->hkv_loc = c.n_head_kv / world;
+    shard(F, &m->f0, &m->f_n);
     synth(c.n_vocab, E, seed * 1000u + 1u, &m->tok_embd);
-    if (!c.tied_head) synth(c.n_vocab, E, seed * 1000u + 2u, &m->output);
+    if (!c.tied_head && !team) synth(c.n_vocab, E, seed * 1000u + 2u, &m->output);
+    if (team) synth_shard(c.n_vocab, E, seed * 1000u + (c.tied_head ? 1u : 2u), &m->head_shard);
     // f32 vectors: per layer attn_norm, ffn_norm (E) and the q | k | v bias (Hq + 2 Hkv); out_norm (E)
     const size_t per_layer = 2u * E + (c.qkv_bias ? (size_t)Hq + 2u * Hkv : 0u);
     const size_t n_f32 = per_layer * c.n_layer + E;
@@ -150,18 +196,43 @@ int tsrc_model_create(tsrc_ctx* ctx, const tsrc_model_cfg* cfg, uint64_t seed, t
         tsrc_model::Layer& L = m->layers[l];
         std::memset(&L, 0, sizeof L);
         const uint64_t s = seed * 1000u + 16u * (l + 1u);
-        synth(Hq + 2u * Hkv, E, s + 0, &L.wqkv);
-        synth(E, Hq, s + 1, &L.wo);
-        synth(2u * F, E, s + 2, &L.wgu);
-        synth(E, F, s + 3, &L.wd);
+        if (team) {
+            const uint32_t qn = m->hq_loc * D, kn = m->hkv_loc * D;
+            synth_ranges(Hq + 2u * Hkv, E, {rank * qn, Hq + rank * kn, Hq + Hkv + rank * kn}, {qn, kn, kn}, s + 0, &L.wqkv);
+            synth_shard(E, Hq, s + 1, &L.wo);
+            synth_ranges(2u * F, E, {m->f0, F + m->f0}, {m->f_n, m->f_n}, s + 2, &L.wgu);
+            synth_shard(E, F, s + 3, &L.wd);
+        } else {
+            synth(Hq + 2u * Hkv, E, s + 0, &L.wqkv);
+            synth(E, Hq, s + 1, &L.wo);
+            synth(2u * F, E, s + 2, &L.wgu);
+            synth(E, F, s + 3, &L.wd);
+        }
         L.attn_norm = vec(l, kVecAttnNorm, E);
         L.ffn_norm = vec(l, kVecFfnNorm, E);
         if (c.qkv_bias) L.bqkv = vec(l, kVecBqkv, Hq + 2u * Hkv);
-        if (rc == TSRC_OK) rc = tsrc_kv_create(ctx, c.n_head_kv, D, c.n_ctx, &L.kv);
+        if (rc == TSRC_OK) rc = tsrc_kv_create(ctx, c.n_head_kv / world, D, c.n_ctx, &L.kv);
     }
     m->out_norm = vec(c.n_layer, kVecOutNorm, E);
     if (rc == TSRC_OK && cudaMemcpy(m->f32, host.data(), n_f32 * sizeof(float), cudaMemcpyHostToDevice) != cudaSuccess)
         rc = TSRC_E_CUDA;
+    if (team && rc == TSRC_OK) {
+        // the rank's q | k | v bias slices, and its SWIGLU / gathered activation rows
+        const uint32_t qn = m->hq_loc * D, kn = m->hkv_loc * D, qkv_loc = qn + 2u * kn;
+        if (c.qkv_bias) {
+            std::vector<float> hb((size_t)c.n_layer * qkv_loc);
+            for (uint32_t l = 0; l < c.n_layer; ++l) {
+                float* d = hb.data() + (size_t)l * qkv_loc;
+                for (uint32_t i = 0; i < qn; ++i) d[i] = tsrc_model_f32_value(seed, l, kVecBqkv, rank * qn + i);
+                for (uint32_t i = 0; i < kn; ++i) d[qn + i] = tsrc_model_f32_value(seed, l, kVecBqkv, Hq + rank * kn + i);
+                for (uint32_t i = 0; i < kn; ++i) d[qn + kn + i] = tsrc_model_f32_value(seed, l, kVecBqkv, Hq + Hkv + rank * kn + i);
+            }
+            if (cudaMalloc(&m->tp_bias, hb.size() * sizeof(float)) != cudaSuccess ||
+                cudaMemcpy(m->tp_bias, hb.data(), hb.size() * sizeof(float), cudaMemcpyHostToDevice) != cudaSuccess)
+                rc = TSRC_E_NOMEM;
+        }
+        if (rc == TSRC_OK && cudaMalloc(&m->tp_act, 2u * (size_t)F * sizeof(float)) != cudaSuccess) rc = TSRC_E_NOMEM;
+    }
     std::vector<int32_t> pos(c.n_ctx);
     for (uint32_t i = 0; i < c.n_ctx; ++i) pos[i] = (int32_t)i;
     if (rc == TSRC_OK && (cudaMalloc(&m->pos, c.n_ctx * sizeof(int32_t)) != cudaSuccess ||
@@ -178,6 +249,23 @@ int tsrc_model_create(tsrc_ctx* ctx, const tsrc_model_cfg* cfg, uint64_t seed, t
         return rc;
     }
     *out = m;
+    return TSRC_OK;
+}
+
+extern "C" {
+
+int tsrc_model_create(tsrc_ctx* ctx, const tsrc_model_cfg* cfg, uint64_t seed, tsrc_model** out) {
+    return model_create(ctx, cfg, seed, nullptr, out);
+}
+
+int tsrc_model_create_tp(tsrc_ctx* ctx, const tsrc_model_cfg* cfg, uint64_t seed, tsrc_team* team, tsrc_model** out) {
+    if (!team) return tsrc::api_fail(TSRC_E_ARG, "tsrc_model_create_tp: NULL team");
+    return model_create(ctx, cfg, seed, team, out);
+}
+
+int tsrc_model_kv(const tsrc_model* m, uint32_t layer, tsrc_kv** out) {
+    if (!m || !out || layer >= m->c.n_layer) return tsrc::api_fail(TSRC_E_ARG, "tsrc_model_kv: no such layer");
+    *out = m->layers[layer].kv;
     return TSRC_OK;
 }
 
@@ -253,11 +341,59 @@ int forward_body(tsrc_model* m, const int32_t* ids, uint32_t T, uint32_t pos0, f
     const cudaStream_t st = static_cast<cudaStream_t>(stream);
     tsrc_fa_cfg fa = c.fa;
     if (fa.C == 0) fa = tsrc_fa_cfg{4u, 4u, 9344u, 32768u, 0u};
+    if (m->team && T != 1)
+        return tsrc::api_fail(TSRC_E_ARG, "tsrc_model_forward: a tensor-parallel model runs one token at a time");
     int rc = tsrc_get_rows(ctx, m->tok_embd, ids, T, m->x, E, stream);
 #define TSRC_M(call) \
     if (rc == TSRC_OK) rc = (call)
 #define TSRC_MC(call, what) \
     if (rc == TSRC_OK && (call) != cudaSuccess) rc = tsrc::api_fail(TSRC_E_CUDA, what)
+    if (m->team) {
+        // one token over the team: q / k / v of this rank's heads, its KV heads' cache and FA, then
+        // the exchanges: attention output (gather), o rows (+ residual, fused gather), gate / up rows
+        // and SWIGLU of this rank's F slice (gather), down rows (+ residual, fused gather), head rows
+        // (fused gather). Every row is one GPU's dot product: the logits are the single GPU's.
+        tsrc_team* tm = m->team;
+        const uint32_t qn = m->hq_loc * D, kn = m->hkv_loc * D, qkv_loc = qn + 2u * kn;
+        float* att_loc = m->q;
+        float* act_loc = m->tp_act;
+        float* act_all = m->tp_act + F;
+        fa.plan_n_head_kv = c.n_head_kv;
+        for (uint32_t l = 0; l < c.n_layer; ++l) {
+            const tsrc_model::Layer& L = m->layers[l];
+            const float* bias = m->tp_bias ? m->tp_bias + (size_t)l * qkv_loc : nullptr;
+            TSRC_M(tsrc_mul_mat_rms(ctx, L.wqkv, m->x, L.attn_norm, c.rms_eps, inv_n, m->qkv, bias, bias ? TSRC_MM_ADD : 0u,
+                                    1.0f, 1.0f, stream));
+            tsrc::RopeKvst rk{};
+            rk.qkv = m->qkv;
+            rk.stride = qkv_loc;
+            rk.pos = pos;
+            rk.n_rot_heads = m->hq_loc + m->hkv_loc;
+            rk.hd = D;
+            rk.nd = D;
+            rk.neox = c.rope_mode;
+            rk.cs_tab = m->rope_tab;
+            rk.sn_tab = m->rope_tab + (size_t)c.n_ctx * half;
+            rk.k_off = qn;
+            rk.v_off = qn + kn;
+            rk.cells = cells;
+            rk.cell0 = pos0;
+            if (rc == TSRC_OK && !cells && (uint64_t)pos0 + 1u > tsrc::kv_cells(L.kv))
+                rc = tsrc::api_fail(TSRC_E_ARG, "tsrc_model_forward: cells outside the cache");
+            TSRC_M(tsrc::kv_fill_planes(L.kv, &rk));
+            TSRC_MC(tsrc::launch_rope_kvst(rk, 1, st), "tsrc_model_forward: ROPE + KVST launch");
+            TSRC_M(tsrc_flash_attn(ctx, L.kv, m->qkv, 1, m->hq_loc, n_kv, nullptr, n_kv, m->kq_scale, pos0, n_kv, &fa, att_loc,
+                                   stream));
+            TSRC_M(tsrc::team_gather(tm, att_loc, qn, m->rank * qn, m->att, Hq, stream));
+            TSRC_M(tsrc::team_mul_mat(ctx, tm, L.wo, m->att, m->x, m->x, nullptr, 0.0f, 0.0f, false, stream));
+            TSRC_M(tsrc_mul_mat_rms(ctx, L.wgu, m->x, L.ffn_norm, c.rms_eps, inv_n, m->gu, nullptr, 0u, 1.0f, 1.0f, stream));
+            TSRC_M(tsrc_vop(ctx, TSRC_VOP_SWIGLU, m->gu, m->f_n, m->gu + m->f_n, m->f_n, act_loc, m->f_n, m->f_n, 1, stream));
+            TSRC_M(tsrc::team_gather(tm, act_loc, m->f_n, m->f0, act_all, F, stream));
+            TSRC_M(tsrc::team_mul_mat(ctx, tm, L.wd, act_all, m->x, m->x, nullptr, 0.0f, 0.0f, false, stream));
+        }
+        TSRC_M(tsrc::team_mul_mat(ctx, tm, m->head_shard, m->x, logits, nullptr, m->out_norm, c.rms_eps, inv_n, true, stream));
+        return rc;
+    }
     for (uint32_t l = 0; l < c.n_layer; ++l) {
         const tsrc_model::Layer& L = m->layers[l];
         if (T == 1) {                                     // one token: RMS_NORM + MUL fused into the MUL_MAT
@@ -413,8 +549,9 @@ int tsrc_model_decode(tsrc_model* m, const int32_t* ids, uint32_t pos0, float* l
     if (fa.C == 0) fa = tsrc_fa_cfg{4u, 4u, 9344u, 32768u, 0u};
     tsrc::FaLaunch a0;
     uint32_t nmax = 0;
-    rc = tsrc::fa_setup(m->ctx, m->layers[0].kv, m->qkv, 1, c.n_head, pos0 + 1u, nullptr, 0, m->kq_scale, pos0, pos0 + 1u, &fa,
-                        m->att, st, &a0, &nmax);
+    if (m->team) fa.plan_n_head_kv = c.n_head_kv;         // shards plan as the single device does
+    rc = tsrc::fa_setup(m->ctx, m->layers[0].kv, m->qkv, 1, m->team ? m->hq_loc : c.n_head, pos0 + 1u, nullptr, 0, m->kq_scale,
+                        pos0, pos0 + 1u, &fa, m->team ? m->q : m->att, st, &a0, &nmax);
     if (rc) return rc;
     if (a0.n_items > tsrc::kFaInlineItems) return forward_body(m, ids, 1, pos0, logits, st, m->pos + pos0, nullptr);
     if (!m->gexec || ids != m->g_ids || logits != m->g_logits || st != m->g_stream || !same_plan(m, a0, nmax)) {

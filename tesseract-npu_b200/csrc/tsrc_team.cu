@@ -160,9 +160,76 @@ int tsrc_mul_mat_allgather(tsrc_ctx* ctx, tsrc_team* t, const tsrc_weight* w, co
     a.team_rank = t->rank;
     a.team_row0 = row0;
     a.team_n = N;
+    a.team_half = t->n_max;
     cudaError_t e = tsrc::launch_matvec(fmt, a, static_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) return cuda_err(e, "tsrc_mul_mat_allgather launch");
     return TSRC_OK;
 }
 
 }  // extern "C"
+
+namespace tsrc {
+
+int team_info(const tsrc_team* t, uint32_t* rank, uint32_t* world, uint32_t* n_max) {
+    if (!t || !t->connected) return set_error(TSRC_E_ARG, "team missing or not connected");
+    *rank = t->rank;
+    *world = t->world;
+    *n_max = t->n_max;
+    return TSRC_OK;
+}
+
+// The fused MUL_MAT + all-gather with the options the model runner needs: the residual addend (the
+// full vector; row n of the shard adds add[row0 + n]) and RMS_NORM + MUL of x in front.
+int team_mul_mat(tsrc_ctx* ctx, tsrc_team* t, const tsrc_weight* w, const float* x, float* y, const float* add,
+                 const float* rms_w, float eps, float inv_n, bool rms, void* stream) {
+    if (!t || !t->connected) return set_error(TSRC_E_ARG, "team_mul_mat: team missing or not connected");
+    MvArgs a{};
+    uint32_t fmt = 0, x_stride = 0, y_stride = 0;
+    int rc = mm_check(ctx, w, x, 1, &x_stride, y, &y_stride, add, 0, add ? TSRC_MM_ADD : 0u, 1.0f, 1.0f, &a, &fmt,
+                      "team_mul_mat");
+    if (rc != TSRC_OK) return rc;
+    uint32_t N = 0, row0 = 0, n_rows = 0;
+    weight_rows(w, &N, &row0, &n_rows);
+    if (N > t->n_max) return set_error(TSRC_E_ARG, "team_mul_mat: N exceeds the team's n_max");
+    a.x = x;
+    a.x_stride = x_stride;
+    a.T = 1;
+    a.y = y;
+    a.add = add ? add + row0 : nullptr;
+    a.rms = rms ? 1u : 0u;
+    a.rms_w = rms_w;
+    a.rms_eps = eps;
+    a.rms_inv_n = inv_n;
+    a.team_y = t->dev_y;
+    a.team_state = reinterpret_cast<uint32_t*>(t->local + t->staging_bytes);
+    a.team_world = t->world;
+    a.team_rank = t->rank;
+    a.team_row0 = row0;
+    a.team_n = N;
+    a.team_half = t->n_max;
+    cudaError_t e = launch_matvec(fmt, a, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_err(e, "team_mul_mat launch");
+    return TSRC_OK;
+}
+
+// dst[offset .. offset + n_local) = src on every rank (dst holds n values)
+int team_gather(tsrc_team* t, const float* src, uint32_t n_local, uint32_t offset, float* dst, uint32_t n, void* stream) {
+    if (!t || !t->connected) return set_error(TSRC_E_ARG, "team_gather: team missing or not connected");
+    if (n > t->n_max || offset + n_local > n) return set_error(TSRC_E_ARG, "team_gather: sizes exceed the team's n_max");
+    TeamGather g{};
+    g.team_y = t->dev_y;
+    g.team_state = reinterpret_cast<uint32_t*>(t->local + t->staging_bytes);
+    g.world = t->world;
+    g.rank = t->rank;
+    g.half = t->n_max;
+    g.src = src;
+    g.n_local = n_local;
+    g.offset = offset;
+    g.n = n;
+    g.dst = dst;
+    cudaError_t e = launch_team_gather(g, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_err(e, "team_gather launch");
+    return TSRC_OK;
+}
+
+}  // namespace tsrc

@@ -59,7 +59,9 @@ _SIGS = {
     "tsrc_rms_norm": (_i, [_p, _p, _u32, _p, _u32, _p, _u32, _u32, _f32, _f32, _p]),
     "tsrc_mul_mat_rms": (_i, [_p, _p, _p, _p, _f32, _f32, _p, _p, _u32, _f32, _f32, _p]),
     "tsrc_model_create": (_i, [_p, _p, _u64, ct.POINTER(_p)]),
+    "tsrc_model_create_tp": (_i, [_p, _p, _u64, _p, ct.POINTER(_p)]),
     "tsrc_model_free": (_i, [_p]),
+    "tsrc_model_kv": (_i, [_p, _u32, ct.POINTER(_p)]),
     "tsrc_model_forward": (_i, [_p, _p, _u32, _u32, _p, _p]),
     "tsrc_model_decode": (_i, [_p, _p, _u32, _p, _p]),
     "tsrc_model_weight": (_i, [_p, _u32, _u32, ct.POINTER(_p)]),
@@ -360,10 +362,14 @@ class Weight:
 class Model:
     """A random-init decoder on the device (tsrc_model_*)."""
 
-    def __init__(self, dev: Device, cfg: ModelCfg, seed: int):
+    def __init__(self, dev: Device, cfg: ModelCfg, seed: int, team: "Team | None" = None):
+        """team: a connected team -> this rank's tensor-parallel share (tsrc_model_create_tp)."""
         h = _p()
-        self.dev, self.cfg, self.seed = dev, cfg, seed
-        _check(lib().tsrc_model_create(dev.handle, ct.byref(cfg), seed, ct.byref(h)))
+        self.dev, self.cfg, self.seed, self.team = dev, cfg, seed, team
+        if team is None:
+            _check(lib().tsrc_model_create(dev.handle, ct.byref(cfg), seed, ct.byref(h)))
+        else:
+            _check(lib().tsrc_model_create_tp(dev.handle, ct.byref(cfg), seed, team.handle, ct.byref(h)))
         self.handle = h
         ts, ks = _f32(), _f32()
         _check(lib().tsrc_model_params(h, ct.byref(ts), ct.byref(ks)))
@@ -382,6 +388,15 @@ class Model:
         w = Weight(self.dev, h)
         w.free = lambda: None                       # owned by the model
         return w
+
+    def kv(self, layer: int) -> "KvCache":
+        """Layer `layer`'s cache (owned by the model; a rank's holds its KV heads)."""
+        h = _p()
+        _check(lib().tsrc_model_kv(self.handle, layer, ct.byref(h)))
+        world = 1 if self.team is None else self.team.world
+        kv = KvCache(self.dev, h, self.cfg.n_head_kv // world, self.cfg.head_dim, self.cfg.n_ctx)
+        kv.free = lambda: None                      # owned by the model
+        return kv
 
     def f32_vector(self, layer: int, which: int, n: int):
         f = lib().tsrc_model_f32_value
