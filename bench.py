@@ -215,9 +215,9 @@ def model_measure(dev, tsrc, torch, name, steps, warmup, e2e_steps=32):
     torch.cuda.synchronize()
     e2e_ms = e0.elapsed_time(e1) / e2e_steps
     algo = model_algo_bytes(s, kv0 + steps // 2)
-    # state, GET_ROWS; per layer 4 MUL_MATs (two with RMS_NORM fused in), ROPE + KVST, FA chunk +
-    # merge, SWIGLU; then the head MUL_MAT (RMS_NORM fused in)
-    launches = 3 + 8 * s["n_layer"]
+    # state, GET_ROWS; per layer 4 MUL_MATs (q / k / v and gate / up with RMS_NORM fused in, gate / up
+    # with SWIGLU as its epilogue), ROPE + KVST, FA chunk + merge; then the head (RMS_NORM fused in)
+    launches = 3 + 7 * s["n_layer"]
     return dict(shape=s, prefill_ms=prefill_ms, ms=ms, e2e_ms=e2e_ms, algo_bytes=algo, launches=launches,
                 n_kv=(kv0, pos)), model
 
@@ -290,9 +290,9 @@ def model_measure_tp(dev, tsrc, torch, dist, name, steps, warmup, rank, world, e
     barrier()
     e2e_ms = max_over_ranks(e0.elapsed_time(e1) / e2e_steps)
     # state, GET_ROWS; per layer q / k / v (RMS_NORM fused), ROPE + KVST, FA chunk + merge, the
-    # attention gather, o (+ gather), gate / up (RMS_NORM fused), SWIGLU, the SWIGLU gather, down
+    # attention gather, o (+ gather), gate / up (RMS_NORM, SWIGLU and the gather fused), down
     # (+ gather); then the head (RMS_NORM and the gather fused)
-    launches = 3 + 10 * s["n_layer"]
+    launches = 3 + 8 * s["n_layer"]
     return dict(shape=s, ms=ms, e2e_ms=e2e_ms, algo_bytes=model_algo_bytes(s, kv0 + steps // 2), launches=launches,
                 n_kv=(kv0, pos)), model, team
 
@@ -316,6 +316,7 @@ def cpu_reference_model(name, threads, model=None):
     shapes = ((Hq + 2 * Hkv, E), (E, Hq), (2 * F, E), (E, F))
     if model is not None:
         L = {n: model.weight(0, i).download() for i, n in enumerate(names)}
+        L["wgu"] = np.concatenate([L["wgu"][0::2], L["wgu"][1::2]])     # the model interleaves (gate_j, up_j)
         head = model.weight(0xFFFFFFFF, 1).download()
         emb = model.weight(0xFFFFFFFF, 0).download()[:16]
         src = "the device model's layer-0 and head rows"

@@ -323,7 +323,8 @@ TSRC_API int tsrc_model_forward(tsrc_model * m, const int32_t * ids, uint32_t T,
 // so a token costs one graph launch on the host. Same results as tsrc_model_forward(m, ids, 1, ...).
 TSRC_API int tsrc_model_decode(tsrc_model * m, const int32_t * ids, uint32_t pos0, float * logits, void * stream);
 // The model's weight handles (owned by the model): layer < n_layer, which 0 = the q, k, v rows
-// stacked (n_head + 2 n_head_kv heads), 1 = o, 2 = the gate and up rows stacked (2 n_ff), 3 = down;
+// stacked (n_head + 2 n_head_kv heads), 1 = o, 2 = the gate and up rows interleaved (row 2j gate_j,
+// 2j + 1 up_j; 2 n_ff rows: the MUL_MAT applies SWIGLU to the pairs as its epilogue), 3 = down;
 // or TSRC_MODEL_GLOBAL.
 TSRC_API int tsrc_model_weight(const tsrc_model * m, uint32_t layer, uint32_t which, tsrc_weight ** out);
 // The host-computed ROPE theta scale and attention scale the model passes to the kinds.

@@ -239,6 +239,25 @@ int weight_synth_ranges(tsrc_ctx* ctx, uint32_t fmt, uint32_t N, uint32_t K, con
     return TSRC_OK;
 }
 
+int weight_interleave_halves(tsrc_ctx* ctx, tsrc_weight* w, tsrc_weight** out) {
+    if (w->n_rows & 1u) return fail(TSRC_E_ARG, "weight_interleave_halves: odd row count");
+    tsrc_weight* o = nullptr;
+    int rc = new_weight(ctx, w->fmt, w->N, w->K, w->row0, w->n_rows, &o);
+    if (rc) return rc;
+    const size_t qr = qs_row_bytes(w->fmt, w->K), mr = meta_row_bytes(w->fmt, w->K), h = w->n_rows / 2u;
+    cudaError_t e = cudaMemcpy2D(o->qs, 2u * qr, w->qs, qr, qr, h, cudaMemcpyDeviceToDevice);
+    if (e == cudaSuccess) e = cudaMemcpy2D(o->qs + qr, 2u * qr, w->qs + h * qr, qr, qr, h, cudaMemcpyDeviceToDevice);
+    if (e == cudaSuccess) e = cudaMemcpy2D(o->meta, 2u * mr, w->meta, mr, mr, h, cudaMemcpyDeviceToDevice);
+    if (e == cudaSuccess) e = cudaMemcpy2D(o->meta + mr, 2u * mr, w->meta + h * mr, mr, mr, h, cudaMemcpyDeviceToDevice);
+    if (e != cudaSuccess) {
+        drop_weight(o);
+        return cuda_fail(e, "weight_interleave_halves");
+    }
+    drop_weight(w);
+    *out = o;
+    return TSRC_OK;
+}
+
 int weight_rows(const tsrc_weight* w, uint32_t* N, uint32_t* row0, uint32_t* n_rows) {
     *N = w->N;
     *row0 = w->row0;
@@ -278,6 +297,26 @@ int mm_check(tsrc_ctx* ctx, const tsrc_weight* w, const float* x, uint32_t T, ui
     a.s1 = daz_host(s1);
     *base = a;
     return TSRC_OK;
+}
+
+int mul_mat_rms_swiglu(tsrc_ctx* ctx, const tsrc_weight* w, const float* x, const float* norm_w, float eps, float inv_n,
+                       float* y, void* stream) {
+    MvArgs a{};
+    uint32_t fmt = 0, x_stride = 0, y_stride = 0;
+    int rc = mm_check(ctx, w, x, 1, &x_stride, y, &y_stride, nullptr, 0, 0u, 1.0f, 1.0f, &a, &fmt, "mul_mat_rms_swiglu");
+    if (rc != TSRC_OK) return rc;
+    if (w->n_rows & 1u) return fail(TSRC_E_ARG, "mul_mat_rms_swiglu: odd row count");
+    a.x = x;
+    a.x_stride = x_stride;
+    a.T = 1;
+    a.y = y;
+    a.rms = 1u;
+    a.rms_w = norm_w;
+    a.rms_eps = daz_host(eps);
+    a.rms_inv_n = daz_host(inv_n);
+    a.swiglu_pairs = 1u;
+    cudaError_t e = launch_matvec(fmt, a, static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? TSRC_OK : cuda_fail(e, "matvec launch");
 }
 
 }  // namespace tsrc

@@ -40,6 +40,9 @@ struct MvArgs {
     const float* rms_w;       // the norm weight, or NULL (no MUL)
     float rms_eps, rms_inv_n;
     uint32_t rms;
+    // SWIGLU of row pairs as the epilogue (T = 1; 0: off): rows 2j, 2j + 1 are gate_j, up_j and
+    // y[j] = canon(FM(SILU(gate_j), up_j)), the SWIGLU kind's value (tsrc_vu.cu); y has n_rows / 2
+    uint32_t swiglu_pairs;
     // fused all-gather over a team of GPUs (one token; team_world = 0: off). Row n of the shard
     // is stored into every rank's staging buffer at team_row0 + n (half (step & 1) of [2][team_n])
     // as one 64-bit word {value bits, step + 1}; every CTA then copies its share of the full
@@ -72,6 +75,16 @@ namespace tsrc {
 int team_info(const tsrc_team* t, uint32_t* rank, uint32_t* world, uint32_t* n_max);
 int team_mul_mat(tsrc_ctx* ctx, tsrc_team* t, const tsrc_weight* w, const float* x, float* y, const float* add,
                  const float* rms_w, float eps, float inv_n, bool rms, void* stream);
+// RMS_NORM in front and SWIGLU of row pairs behind, the pairs' outputs gathered over the team at
+// [out0, out0 + n_rows / 2) of y (out_n values)
+int team_mul_mat_swiglu(tsrc_ctx* ctx, tsrc_team* t, const tsrc_weight* w, const float* x, float* y, uint32_t out0,
+                        uint32_t out_n, const float* rms_w, float eps, float inv_n, void* stream);
+// tsrc_api.cu: one-token MUL_MAT with RMS_NORM in front and SWIGLU of row pairs behind
+int mul_mat_rms_swiglu(tsrc_ctx* ctx, const tsrc_weight* w, const float* x, const float* norm_w, float eps, float inv_n,
+                       float* y, void* stream);
+// a copy of w with its two halves of rows interleaved (row j of the first half -> 2j, of the
+// second -> 2j + 1); w is freed
+int weight_interleave_halves(tsrc_ctx* ctx, tsrc_weight* w, tsrc_weight** out);
 int team_gather(tsrc_team* t, const float* src, uint32_t n_local, uint32_t offset, float* dst, uint32_t n, void* stream);
 // tsrc_api.cu: a weight whose rows are row ranges [r0[i], r0[i] + n[i]) of one synthetic N-row
 // matrix, stacked in that order (the rows equal those of tsrc_weight_synth's full matrix)

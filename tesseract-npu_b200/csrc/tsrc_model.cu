@@ -40,7 +40,7 @@ struct tsrc_model {
     float* rope_tab = nullptr;                           // c_i then s_i of every position [2][n_ctx][head_dim / 2]
     float* buf = nullptr;                                // activations for t_alloc tokens
     uint32_t t_alloc = 0;
-    float *x, *h, *qkv, *q, *att, *gu;
+    float *x, *h, *qkv, *q, *att, *gu, *act;          // gu: (gate, up) pairs interleaved; act: their SWIGLU
     std::vector<uint16_t> mask;                          // host causal mask of a multi-token call
     // decode graph (tsrc_model_decode): one token's kernels captured once; per token the position
     // kernel's argument and the FA nodes' plans are rewritten in the instantiated graph
@@ -67,7 +67,7 @@ struct tsrc_model {
     uint32_t hq_loc = 0, hkv_loc = 0, f0 = 0, f_n = 0;   // local q / kv heads; gate / up rows [f0, f0 + f_n)
     tsrc_weight* head_shard = nullptr;                   // rows of the head (the embedding when tied)
     float* tp_bias = nullptr;                            // [n_layer][local q | k | v] bias slices
-    float* tp_act = nullptr;                             // SWIGLU rows of this rank [F], then the gathered [F]
+    float* tp_act = nullptr;                             // the gathered SWIGLU row [F]
 };
 
 namespace {
@@ -208,6 +208,9 @@ static int model_create(tsrc_ctx* ctx, const tsrc_model_cfg* cfg, uint64_t seed,
             synth(2u * F, E, s + 2, &L.wgu);
             synth(E, F, s + 3, &L.wd);
         }
+        // gate and up rows interleaved (gate_j, up_j adjacent): the MUL_MAT kernel's warp then holds
+        // both values of a SWIGLU pair and applies it as its epilogue
+        if (rc == TSRC_OK) rc = tsrc::weight_interleave_halves(ctx, L.wgu, &L.wgu);
         L.attn_norm = vec(l, kVecAttnNorm, E);
         L.ffn_norm = vec(l, kVecFfnNorm, E);
         if (c.qkv_bias) L.bqkv = vec(l, kVecBqkv, Hq + 2u * Hkv);
@@ -231,7 +234,7 @@ static int model_create(tsrc_ctx* ctx, const tsrc_model_cfg* cfg, uint64_t seed,
                 cudaMemcpy(m->tp_bias, hb.data(), hb.size() * sizeof(float), cudaMemcpyHostToDevice) != cudaSuccess)
                 rc = TSRC_E_NOMEM;
         }
-        if (rc == TSRC_OK && cudaMalloc(&m->tp_act, 2u * (size_t)F * sizeof(float)) != cudaSuccess) rc = TSRC_E_NOMEM;
+        if (rc == TSRC_OK && cudaMalloc(&m->tp_act, (size_t)F * sizeof(float)) != cudaSuccess) rc = TSRC_E_NOMEM;
     }
     std::vector<int32_t> pos(c.n_ctx);
     for (uint32_t i = 0; i < c.n_ctx; ++i) pos[i] = (int32_t)i;
@@ -303,7 +306,7 @@ int ensure_buffers(tsrc_model* m, uint32_t T) {
         cudaDeviceSynchronize();
         cudaFree(m->buf);
         m->buf = nullptr;
-        const size_t per = 2u * E + QKV + 2u * Hq + 2u * F;
+        const size_t per = 2u * E + QKV + 2u * Hq + 3u * F;
         if (cudaMalloc(&m->buf, per * T * sizeof(float)) != cudaSuccess) {
             m->t_alloc = 0;
             return tsrc::api_fail(TSRC_E_NOMEM, "tsrc_model_forward: activation buffers");
@@ -315,7 +318,8 @@ int ensure_buffers(tsrc_model* m, uint32_t T) {
         m->qkv = p; p += (size_t)QKV * T;
         m->q = p; p += (size_t)Hq * T;
         m->att = p; p += (size_t)Hq * T;
-        m->gu = p;
+        m->gu = p; p += 2u * (size_t)F * T;
+        m->act = p;
     }
     return TSRC_OK;
 }
@@ -350,14 +354,14 @@ int forward_body(tsrc_model* m, const int32_t* ids, uint32_t T, uint32_t pos0, f
     if (rc == TSRC_OK && (call) != cudaSuccess) rc = tsrc::api_fail(TSRC_E_CUDA, what)
     if (m->team) {
         // one token over the team: q / k / v of this rank's heads, its KV heads' cache and FA, then
-        // the exchanges: attention output (gather), o rows (+ residual, fused gather), gate / up rows
-        // and SWIGLU of this rank's F slice (gather), down rows (+ residual, fused gather), head rows
-        // (fused gather). Every row is one GPU's dot product: the logits are the single GPU's.
+        // the exchanges: attention output (gather), o rows (+ residual, fused gather), gate / up row
+        // pairs of this rank's F slice with SWIGLU as their epilogue (fused gather), down rows
+        // (+ residual, fused gather), head rows (fused gather). Every row is one GPU's dot product:
+        // the logits are the single GPU's.
         tsrc_team* tm = m->team;
         const uint32_t qn = m->hq_loc * D, kn = m->hkv_loc * D, qkv_loc = qn + 2u * kn;
         float* att_loc = m->q;
-        float* act_loc = m->tp_act;
-        float* act_all = m->tp_act + F;
+        float* act_all = m->tp_act;
         fa.plan_n_head_kv = c.n_head_kv;
         for (uint32_t l = 0; l < c.n_layer; ++l) {
             const tsrc_model::Layer& L = m->layers[l];
@@ -386,9 +390,7 @@ int forward_body(tsrc_model* m, const int32_t* ids, uint32_t T, uint32_t pos0, f
                                    stream));
             TSRC_M(tsrc::team_gather(tm, att_loc, qn, m->rank * qn, m->att, Hq, stream));
             TSRC_M(tsrc::team_mul_mat(ctx, tm, L.wo, m->att, m->x, m->x, nullptr, 0.0f, 0.0f, false, stream));
-            TSRC_M(tsrc_mul_mat_rms(ctx, L.wgu, m->x, L.ffn_norm, c.rms_eps, inv_n, m->gu, nullptr, 0u, 1.0f, 1.0f, stream));
-            TSRC_M(tsrc_vop(ctx, TSRC_VOP_SWIGLU, m->gu, m->f_n, m->gu + m->f_n, m->f_n, act_loc, m->f_n, m->f_n, 1, stream));
-            TSRC_M(tsrc::team_gather(tm, act_loc, m->f_n, m->f0, act_all, F, stream));
+            TSRC_M(tsrc::team_mul_mat_swiglu(ctx, tm, L.wgu, m->x, act_all, m->f0, F, L.ffn_norm, c.rms_eps, inv_n, stream));
             TSRC_M(tsrc::team_mul_mat(ctx, tm, L.wd, act_all, m->x, m->x, nullptr, 0.0f, 0.0f, false, stream));
         }
         TSRC_M(tsrc::team_mul_mat(ctx, tm, m->head_shard, m->x, logits, nullptr, m->out_norm, c.rms_eps, inv_n, true, stream));
@@ -431,14 +433,14 @@ int forward_body(tsrc_model* m, const int32_t* ids, uint32_t T, uint32_t pos0, f
         }
         TSRC_M(tsrc_flash_attn(ctx, L.kv, q, T, c.n_head, n_kv, mask, n_kv, m->kq_scale, pos0, n_kv, &fa, m->att, stream));
         TSRC_M(tsrc_mul_mat(ctx, L.wo, m->att, T, Hq, m->x, E, m->x, E, TSRC_MM_ADD, 1.0f, 1.0f, stream));
-        if (T == 1) {
-            TSRC_M(tsrc_mul_mat_rms(ctx, L.wgu, m->x, L.ffn_norm, c.rms_eps, inv_n, m->gu, nullptr, 0u, 1.0f, 1.0f, stream));
+        if (T == 1) {                                     // RMS_NORM, gate / up and SWIGLU: one launch
+            TSRC_M(tsrc::mul_mat_rms_swiglu(ctx, L.wgu, m->x, L.ffn_norm, c.rms_eps, inv_n, m->act, stream));
         } else {
             TSRC_M(tsrc_rms_norm(ctx, m->x, E, m->h, E, L.ffn_norm, E, T, c.rms_eps, inv_n, stream));
             TSRC_M(tsrc_mul_mat(ctx, L.wgu, m->h, T, E, m->gu, 2u * F, nullptr, 0, 0u, 1.0f, 1.0f, stream));
+            TSRC_MC(tsrc::launch_vop(8u, m->gu, 2u * F, nullptr, 0u, m->act, F, F, T, st), "tsrc_model_forward: SWIGLU launch");
         }
-        TSRC_M(tsrc_vop(ctx, TSRC_VOP_SWIGLU, m->gu, 2u * F, m->gu + F, 2u * F, m->gu, 2u * F, F, T, stream));
-        TSRC_M(tsrc_mul_mat(ctx, L.wd, m->gu, T, 2u * F, m->x, E, m->x, E, TSRC_MM_ADD, 1.0f, 1.0f, stream));
+        TSRC_M(tsrc_mul_mat(ctx, L.wd, m->act, T, F, m->x, E, m->x, E, TSRC_MM_ADD, 1.0f, 1.0f, stream));
     }
     // the last token: output norm and head
     const float* xl = m->x + (size_t)(T - 1u) * E;

@@ -212,6 +212,38 @@ int team_mul_mat(tsrc_ctx* ctx, tsrc_team* t, const tsrc_weight* w, const float*
     return TSRC_OK;
 }
 
+int team_mul_mat_swiglu(tsrc_ctx* ctx, tsrc_team* t, const tsrc_weight* w, const float* x, float* y, uint32_t out0,
+                        uint32_t out_n, const float* rms_w, float eps, float inv_n, void* stream) {
+    if (!t || !t->connected) return set_error(TSRC_E_ARG, "team_mul_mat_swiglu: team missing or not connected");
+    MvArgs a{};
+    uint32_t fmt = 0, x_stride = 0, y_stride = 0;
+    int rc = mm_check(ctx, w, x, 1, &x_stride, y, &y_stride, nullptr, 0, 0u, 1.0f, 1.0f, &a, &fmt, "team_mul_mat_swiglu");
+    if (rc != TSRC_OK) return rc;
+    uint32_t N = 0, row0 = 0, n_rows = 0;
+    weight_rows(w, &N, &row0, &n_rows);
+    if ((n_rows & 1u) || out_n > t->n_max || out0 + n_rows / 2u > out_n)
+        return set_error(TSRC_E_ARG, "team_mul_mat_swiglu: rows and output range do not fit");
+    a.x = x;
+    a.x_stride = x_stride;
+    a.T = 1;
+    a.y = y;
+    a.rms = 1u;
+    a.rms_w = rms_w;
+    a.rms_eps = eps;
+    a.rms_inv_n = inv_n;
+    a.swiglu_pairs = 1u;
+    a.team_y = t->dev_y;
+    a.team_state = reinterpret_cast<uint32_t*>(t->local + t->staging_bytes);
+    a.team_world = t->world;
+    a.team_rank = t->rank;
+    a.team_row0 = out0;
+    a.team_n = out_n;
+    a.team_half = t->n_max;
+    cudaError_t e = launch_matvec(fmt, a, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_err(e, "team_mul_mat_swiglu launch");
+    return TSRC_OK;
+}
+
 // dst[offset .. offset + n_local) = src on every rank (dst holds n values)
 int team_gather(tsrc_team* t, const float* src, uint32_t n_local, uint32_t offset, float* dst, uint32_t n, void* stream) {
     if (!t || !t->connected) return set_error(TSRC_E_ARG, "team_gather: team missing or not connected");

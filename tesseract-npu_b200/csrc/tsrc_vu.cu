@@ -342,6 +342,7 @@ __global__ void vop_kernel(uint32_t func, const float* a, uint32_t as, const flo
             case 0u: v = FA(ar[j], br[j]); break;
             case 2u: v = FM(ar[j], br[j]); break;
             case 6u: v = silu_vu(ar[j]); break;
+            case 8u: v = FM(silu_vu(ar[2u * j]), ar[2u * j + 1u]); break;     // SWIGLU of interleaved (gate, up) pairs
             default: v = FM(silu_vu(ar[j]), br[j]); break;
         }
         yr[j] = canon(v);

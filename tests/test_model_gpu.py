@@ -26,6 +26,7 @@ def oracle_of(tsro, m, shape):
     L = []
     for l in range(shape["n_layer"]):
         w = {n: m.weight(l, i).download() for i, n in enumerate(("wqkv", "wo", "wgu", "wd"))}
+        w["wgu"] = np.concatenate([w["wgu"][0::2], w["wgu"][1::2]])      # the model interleaves (gate_j, up_j)
         E, Hq, Hkv = shape["n_embd"], shape["n_head"] * shape["head_dim"], shape["n_head_kv"] * shape["head_dim"]
         w["attn_norm"] = m.f32_vector(l, 0, E)
         w["ffn_norm"] = m.f32_vector(l, 1, E)
