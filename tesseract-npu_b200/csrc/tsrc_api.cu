@@ -213,6 +213,15 @@ namespace tsrc {
 
 int set_error(int code, const char* msg) { return fail(code, "%s", msg); }
 
+// Makes the context's device current (for translation units that do not see tsrc_ctx) and returns
+// its ordinal in *dev.
+int ctx_device(const tsrc_ctx* ctx, int* dev) {
+    int rc = use_device(ctx);
+    if (rc) return rc;
+    *dev = ctx->device;
+    return TSRC_OK;
+}
+
 int weight_synth_ranges(tsrc_ctx* ctx, uint32_t fmt, uint32_t N, uint32_t K, const uint32_t* r0, const uint32_t* n,
                         uint32_t count, uint64_t seed, float sigma, tsrc_weight** out) {
     uint32_t total = 0;
@@ -272,6 +281,10 @@ int mm_check(tsrc_ctx* ctx, const tsrc_weight* w, const float* x, uint32_t T, ui
              const char* who) {
     if (!ctx || !w || !x || !y) return fail(TSRC_E_ARG, "%s: NULL argument", who);
     if (w->ctx != ctx) return fail(TSRC_E_ARG, "%s: the weight belongs to another context", who);
+    if (T == 0) {                        // nothing to do, and no further checks (as tsrc_mul_mat)
+        *fmt = w->fmt;
+        return TSRC_OK;
+    }
     if (flags & ~(TSRC_MM_ADD | TSRC_MM_SCALE | TSRC_MM_SOFTCAP)) return fail(TSRC_E_ARG, "%s: undefined flag bits 0x%x", who, flags);
     if ((flags & TSRC_MM_ADD) && (flags & (TSRC_MM_SCALE | TSRC_MM_SOFTCAP)))
         return fail(TSRC_E_ARG, "%s: an addend cannot be combined with SCALE or SOFTCAP", who);
@@ -281,7 +294,6 @@ int mm_check(tsrc_ctx* ctx, const tsrc_weight* w, const float* x, uint32_t T, ui
     if (*y_stride == 0) *y_stride = w->n_rows;
     if (*x_stride < w->K || *y_stride < w->n_rows) return fail(TSRC_E_ARG, "%s: a stride is shorter than its row", who);
     if ((flags & TSRC_MM_ADD) && add_stride != 0 && add_stride < w->n_rows) return fail(TSRC_E_ARG, "%s: addend stride", who);
-    (void)T;
     int rc = use_device(ctx);
     if (rc) return rc;
     *fmt = w->fmt;

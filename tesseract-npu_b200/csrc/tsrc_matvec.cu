@@ -28,6 +28,8 @@
 //     a multiple of 2^-126 of magnitude >= 2^-126 (|d_w| >= 2^-24 for a nonzero fp16), so no
 //     result can be subnormal and the flush tests are skipped (a CTA-uniform choice; the values
 //     are the same either way).
+#include <algorithm>
+#include <cstdlib>
 #include <type_traits>
 
 #include "tsrc_internal.h"
@@ -702,6 +704,429 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) matvec_kernel(MvArgs a, 
                     a.swiglu_pairs ? r_begin / 2u : r_begin, a.swiglu_pairs ? r_end / 2u : r_end);
 }
 
+// ---- one-token decode kernel: QACT fused, weights staged in shared memory ------------------------
+// The MUL_MAT of one token (the decode step) is the hot path. Its structure (measured on B200: the
+// launch is bound by the SM-side chain, not by HBM, unless every byte is requested at CTA start):
+//   - a warp owns pairs of rows (lane L: row L / 16 of the pair, block / superblock L % 16 of each
+//     tile, so a lane owns whole block sums and exactly partial p[L % 16] of its row, the
+//     reference's term order);
+//   - before it waits for the previous kernel (weights are read-only), every lane issues cp.async
+//     copies of exactly the bytes it will read, for all of its units if the CTA's share fits in
+//     shared memory (a 33 MB Q4_K 14336 x 4096 matrix does: 98 rows x 2304 B per SM), else for the
+//     first R units of a warp-private ring refilled as units are consumed; every byte of the share
+//     is in flight while the previous kernel finishes and QACT runs;
+//   - QACT (optionally after RMS_NORM) writes the chunk-major image; a lane keeps the activation of
+//     its block / superblock of a one-unit row in registers;
+//   - the 16-partial tree is four xor-shuffle levels inside each half-warp.
+namespace dec {
+
+constexpr uint32_t kWarps = 16;
+constexpr uint32_t kThreads = kWarps * 32;
+constexpr uint32_t kTpuQ8 = 4;           // Q8_0 tiles per unit (Q4_K: 1)
+
+__device__ __forceinline__ void cpa16(void* dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(su32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cpa_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cpa_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+// waits until at most n of this thread's copy groups are pending (n above 7 waits for 7)
+__device__ __forceinline__ void cpa_wait_dyn(uint32_t n) {
+    switch (n) {
+        case 0: cpa_wait<0>(); break;
+        case 1: cpa_wait<1>(); break;
+        case 2: cpa_wait<2>(); break;
+        case 3: cpa_wait<3>(); break;
+        case 4: cpa_wait<4>(); break;
+        case 5: cpa_wait<5>(); break;
+        case 6: cpa_wait<6>(); break;
+        default: cpa_wait<7>(); break;
+    }
+}
+
+struct Geo {
+    uint32_t nb, tiles, tpu, upp, qt, mt, qg, mg, slot;
+    uint32_t qrow, mrow;                     // bytes of a row's quants / meta
+    Geo() = default;
+    __host__ __device__ Geo(uint32_t fmt, uint32_t K) {
+        nb = fmt == 0 ? K / 32u : K / 256u;
+        tiles = (nb + 15u) / 16u;
+        tpu = fmt == 0 ? kTpuQ8 : 1u;
+        upp = (tiles + tpu - 1u) / tpu;
+        qt = fmt == 0 ? 512u : 2048u;        // quant bytes of a full tile of one row
+        mt = fmt == 0 ? 32u : 256u;          // meta bytes of a full tile of one row
+        qg = tpu * qt;
+        mg = tpu * mt;
+        slot = 2u * (qg + mg);               // a unit: both rows' quants, then both rows' meta
+        qrow = fmt == 0 ? K : K / 2u;
+        mrow = fmt == 0 ? ((K / 32u) * 2u + 15u) & ~15u : (K / 256u) * 16u;
+    }
+};
+
+// Shared-memory plan and geometry of one launch (computed on the host: no divisions on the device).
+struct Plan {
+    Geo g;
+    uint32_t rpc;         // rows per CTA (even)
+    uint32_t ring;        // 0: every unit of the CTA has its own slot; else slots per warp
+    uint32_t slots_off;   // byte offset of the unit slots
+    uint32_t qa_q, qa_d;  // QA image: quant bytes, scale bytes (Q4_K sums follow)
+    uint32_t team_off;    // the CTA's rows before the fused all-gather sends them
+    uint32_t flags_off;   // one word per warp (the fast-path vote)
+};
+
+// A walk over a warp's units in order: pair pr (of the CTA), unit u of the pair, and the unit's
+// shared-memory slot (own slot pr * upp + u, or the warp's ring slot warp + 16 rs).
+template <bool RING>
+struct Cursor {
+    uint32_t pr, u, rs;
+    __device__ __forceinline__ uint32_t slot(const Plan& P, uint32_t warp) const {
+        return RING ? warp + 16u * rs : pr * P.g.upp + u;
+    }
+    __device__ __forceinline__ void next(const Plan& P) {
+        if (++u == P.g.upp) {
+            u = 0;
+            pr += 16u;
+        }
+        if (RING && ++rs == P.ring) rs = 0;
+    }
+};
+
+// QACT A256 of one superblock into the image (tsr_ref.c:488-518), one warp, lane l holds values
+// 8 l .. 8 l + 7. When the largest |value| is at least 2^-100, DAZ of a value and the flush of its
+// product cannot change the rounded result (|iscale * v| < 2^-19 for any subnormal v), so they are
+// skipped. Returns (uniform over the warp) whether the stored scale is 0 or >= 2^-79.
+__device__ __forceinline__ bool qact256_img(const float (&v)[8], uint32_t s, uint32_t lane, uint8_t* q, float* d, uint8_t* bs) {
+    uint32_t best = 0;
+    float mine = v[0];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const uint32_t a = fbits(v[i]) & ~kSign;
+        const uint32_t key = (a - 0x00800000u <= 0x7F000000u) ? a : 0u;   // |DAZ(v)| of a non-NaN v, else 0
+        if (key > best) {
+            best = key;
+            mine = v[i];
+        }
+    }
+    const uint32_t amax = __reduce_max_sync(0xFFFFFFFFu, best);
+    const uint32_t owner = __reduce_min_sync(0xFFFFFFFFu, (best == amax && amax != 0u) ? lane : 32u);
+    const float mx = __shfl_sync(0xFFFFFFFFu, mine, owner & 31u);       // normal or infinite when amax != 0
+    int32_t qv[8];
+    float db = 0.0f;
+    if (amax != 0u) {
+        const float iscale = fdiv(-127.0f, mx);
+        if (amax >= 0x0D800000u) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) qv[i] = round_even_sat8(__fmul_rn(iscale, v[i]));
+        } else {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) qv[i] = round_even_sat8(fmul(iscale, daz(v[i])));
+        }
+        db = frecip(iscale);
+    } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) qv[i] = 0;
+    }
+    uint32_t lo = 0, hi = 0;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        lo |= ((uint32_t)qv[i] & 0xFFu) << (8 * i);
+        hi |= ((uint32_t)qv[i + 4] & 0xFFu) << (8 * i);
+    }
+    *reinterpret_cast<uint2*>(q + (s >> 4) * 4096u + 256u * (lane >> 1) + 16u * (s & 15u) + 8u * (lane & 1u)) = make_uint2(lo, hi);
+    int32_t sum = __dp4a((int)lo, 0x01010101, __dp4a((int)hi, 0x01010101, 0));
+    sum += __shfl_xor_sync(0xFFFFFFFFu, sum, 1);
+    sum += __shfl_xor_sync(0xFFFFFFFFu, sum, 2);      // lanes 4j .. 4j+3: sub-block j (32 values)
+    if ((lane & 3u) == 0)
+        *reinterpret_cast<int16_t*>(bs + (s >> 4) * 256u + 16u * (s & 15u) + 2u * (lane >> 2)) = (int16_t)sum;
+    if (lane == 0) d[s] = db;
+    const uint32_t u = fbits(db) & ~kSign;
+    return u == 0u || u >= kSafeDx;
+}
+
+// The image of the one token x (RMS_NORM + MUL in front when a.rms). Returns (uniform over the
+// CTA) whether every nonzero scale is >= 2^-79.
+template <int FMT>
+__device__ __forceinline__ bool stage_x1(const MvArgs& a, uint8_t* q, float* d, uint8_t* bs, uint32_t* flags) {
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+    const uint32_t nb = FMT == 0 ? a.K / 32u : a.K / 256u;
+    const bool rms = a.rms != 0u, rms_w = a.rms_w != nullptr;
+    const float sc = rms ? rms_scale(a) : 0.0f;
+    bool ok = true;
+    if (FMT == 0) {
+        constexpr uint32_t B = 8;
+        for (uint32_t i0 = warp; i0 < nb; i0 += B * kWarps) {
+            float v[B], wv[B];
+#pragma unroll
+            for (uint32_t j = 0; j < B; ++j) {
+                const uint32_t i = i0 + j * kWarps;
+                v[j] = i < nb ? a.x[32u * i + lane] : 0.0f;
+                wv[j] = (rms_w && i < nb) ? a.rms_w[32u * i + lane] : 0.0f;
+            }
+#pragma unroll
+            for (uint32_t j = 0; j < B; ++j) {
+                const uint32_t i = i0 + j * kWarps;
+                if (i < nb) ok &= qact32_to_smem(rms ? rms_apply(v[j], wv[j], rms_w, sc) : v[j], i, lane, q, d);
+            }
+        }
+    } else {
+        for (uint32_t i = warp; i < nb; i += kWarps) {
+            float v[8];
+            const float* src = a.x + 256u * i + 8u * lane;
+            if ((reinterpret_cast<uintptr_t>(src) & 15u) == 0) {
+                const float4 f0 = reinterpret_cast<const float4*>(src)[0], f1 = reinterpret_cast<const float4*>(src)[1];
+                v[0] = f0.x; v[1] = f0.y; v[2] = f0.z; v[3] = f0.w;
+                v[4] = f1.x; v[5] = f1.y; v[6] = f1.z; v[7] = f1.w;
+            } else {
+#pragma unroll
+                for (int e = 0; e < 8; ++e) v[e] = src[e];
+            }
+            if (rms) {
+#pragma unroll
+                for (int e = 0; e < 8; ++e) v[e] = rms_apply(v[e], rms_w ? a.rms_w[256u * i + 8u * lane + e] : 0.0f, rms_w, sc);
+            }
+            ok &= qact256_img(v, i, lane, q, d, bs);
+        }
+    }
+    const uint32_t bad = __any_sync(0xFFFFFFFFu, !ok);
+    if (lane == 0) flags[warp] = bad;
+    __syncthreads();
+    uint32_t any = 0;
+#pragma unroll
+    for (uint32_t w = 0; w < kWarps; w += 4) {
+        const uint4 f = *reinterpret_cast<const uint4*>(flags + w);
+        any |= f.x | f.y | f.z | f.w;
+    }
+    return any == 0u;
+}
+
+// Registers of a lane's activation for a one-unit row (Q4_K: superblock k, 16 chunks + its 8
+// sub-block sums + scale; Q8_0: block 16 t + k of tiles t < 4, 2 chunks + scale each).
+template <int FMT>
+struct XReg;
+template <>
+struct XReg<1> {
+    uint4 x[16];
+    uint4 B;
+    float dx;
+};
+template <>
+struct XReg<0> {
+    uint4 x[8];
+    float dx[4];
+};
+
+// Copies the bytes lane (h, k) reads of unit (pair p, unit u) into slot sl.
+template <int FMT>
+__device__ __forceinline__ void stage_unit(const MvArgs& a, const Geo& G, uint32_t r_begin, uint32_t n, uint32_t p, uint32_t u,
+                                           uint8_t* sl, uint32_t k, uint32_t h) {
+    const uint32_t r = 2u * p + h;
+    if (r < n) {
+        const size_t grow = r_begin + r;
+        const uint32_t t0 = u * G.tpu;
+        const uint8_t* gq = a.qs + grow * G.qrow + (size_t)t0 * G.qt;
+        const uint8_t* gm = static_cast<const uint8_t*>(a.meta) + grow * G.mrow + (size_t)t0 * G.mt;
+        uint8_t* sq = sl + h * G.qg;
+        uint8_t* sm = sl + 2u * G.qg + h * G.mg;
+        if (FMT == 1) {
+            const uint32_t sb = 16u * t0 + k;
+            if (sb < G.nb) {
+                const uint32_t rest = G.nb - 16u * t0, cs = rest >= 16u ? 256u : 16u * rest;
+#pragma unroll
+                for (uint32_t j = 0; j < 8; ++j) cpa16(sq + j * cs + 16u * k, gq + j * cs + 16u * k);
+                cpa16(sm + 16u * k, gm + 16u * k);
+            }
+        } else {
+#pragma unroll
+            for (uint32_t ti = 0; ti < kTpuQ8; ++ti) {
+                const uint32_t t = t0 + ti;
+                if (t < G.tiles && 16u * t + k < G.nb) {
+                    const uint32_t rest = G.nb - 16u * t, cs = rest >= 16u ? 256u : 16u * rest;
+                    cpa16(sq + ti * 512u + 16u * k, gq + ti * 512u + 16u * k);
+                    cpa16(sq + ti * 512u + cs + 16u * k, gq + ti * 512u + cs + 16u * k);
+                }
+            }
+            // the unit's scales of this row: 2 bytes per block, rounded up to 16 (the meta row is
+            // padded to 16 bytes, so the last copy stays inside the row)
+            const uint32_t blocks = min(16u * kTpuQ8, G.nb - 16u * t0);
+            if (16u * k < 2u * blocks) cpa16(sm + 16u * k, gm + 16u * k);
+        }
+    }
+    cpa_commit();
+}
+
+template <int FMT, bool XR, bool FULL, bool SAFE>
+__device__ __forceinline__ void unit_math(const MvArgs& a, const Geo& G, const uint8_t* sl, uint32_t u, uint32_t k, uint32_t h,
+                                          const uint8_t* q, const float* d, const uint8_t* bs, const XReg<FMT>& xr, float& p,
+                                          int32_t* isum_row) {
+    const uint8_t* sq = sl + h * G.qg;
+    const uint8_t* sm = sl + 2u * G.qg + h * G.mg;
+    const uint32_t t0 = u * G.tpu;
+    if constexpr (FMT == 1) {
+        const uint32_t sb = 16u * t0 + k;
+        if (!FULL && sb >= G.nb) return;
+        const uint32_t rest = G.nb - 16u * t0, cs = (FULL || rest >= 16u) ? 256u : 16u * rest;
+        uint4 w[8];
+#pragma unroll
+        for (uint32_t j = 0; j < 8; ++j) w[j] = lds<uint4>(sq + j * cs + 16u * k);
+        const uint4 m = lds<uint4>(sm + 16u * k);
+        const uint32_t sc_lo = m.y & 0x3F3F3F3Fu, mn_lo = m.z & 0x3F3F3F3Fu;
+        const uint32_t sc_hi = (m.w & 0x0F0F0F0Fu) | ((m.y >> 2) & 0x30303030u);
+        const uint32_t mn_hi = ((m.w >> 4) & 0x0F0F0F0Fu) | ((m.z >> 2) & 0x30303030u);
+        const uint8_t* xq = q + (size_t)t0 * 4096u + 16u * k;
+        int32_t S[8];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            const uint4 a0 = w[2 * c], a1 = w[2 * c + 1];
+            const uint4 l0 = make_uint4(a0.x & 0x0F0F0F0Fu, a0.y & 0x0F0F0F0Fu, a0.z & 0x0F0F0F0Fu, a0.w & 0x0F0F0F0Fu);
+            const uint4 l1 = make_uint4(a1.x & 0x0F0F0F0Fu, a1.y & 0x0F0F0F0Fu, a1.z & 0x0F0F0F0Fu, a1.w & 0x0F0F0F0Fu);
+            const uint4 h0 = make_uint4(a0.x & 0xF0F0F0F0u, a0.y & 0xF0F0F0F0u, a0.z & 0xF0F0F0F0u, a0.w & 0xF0F0F0F0u);
+            const uint4 h1 = make_uint4(a1.x & 0xF0F0F0F0u, a1.y & 0xF0F0F0F0u, a1.z & 0xF0F0F0F0u, a1.w & 0xF0F0F0F0u);
+            const uint4 x0 = XR ? xr.x[4 * c] : lds<uint4>(xq + 256u * (4 * c));
+            const uint4 x1 = XR ? xr.x[4 * c + 1] : lds<uint4>(xq + 256u * (4 * c + 1));
+            const uint4 x2 = XR ? xr.x[4 * c + 2] : lds<uint4>(xq + 256u * (4 * c + 2));
+            const uint4 x3 = XR ? xr.x[4 * c + 3] : lds<uint4>(xq + 256u * (4 * c + 3));
+            S[2 * c] = dot16s(l1, x1, dot16s(l0, x0, 0));
+            S[2 * c + 1] = dot16us(h1, x3, dot16us(h0, x2, 0)) >> 4;
+        }
+        int32_t isum = 0;
+#pragma unroll
+        for (uint32_t j = 0; j < 4; ++j) isum += ubyte(sc_lo, j) * S[j] + ubyte(sc_hi, j) * S[4 + j];
+        const uint4 B = XR ? xr.B : lds<uint4>(bs + (size_t)t0 * 256u + 16u * k);
+        const int32_t msum = dp2a_hi(B.w, mn_hi, dp2a_lo(B.z, mn_hi, dp2a_hi(B.y, mn_lo, dp2a_lo(B.x, mn_lo, 0))));
+        if (isum_row) {
+            isum_row[2u * sb] = isum;
+            isum_row[2u * sb + 1u] = msum;
+        }
+        const float Dx = XR ? xr.dx : d[sb];
+        const float dw = h2f((uint16_t)(m.x & 0xFFFFu)), dmw = h2f((uint16_t)(m.x >> 16));
+        const float t1v = mul_<SAFE>(mul_<SAFE>(dw, Dx), i2f(isum));
+        const float t2v = mul_<SAFE>(mul_<SAFE>(dmw, Dx), i2f(msum));
+        p = add_<SAFE>(p, sub_<SAFE>(t1v, t2v));
+    } else {
+#pragma unroll
+        for (uint32_t ti = 0; ti < kTpuQ8; ++ti) {
+            const uint32_t t = t0 + ti, b = 16u * t + k;
+            if (!FULL && t >= G.tiles) break;
+            if (FULL || b < G.nb) {
+                const uint32_t rest = G.nb - 16u * t, cs = (FULL || rest >= 16u) ? 256u : 16u * rest;
+                const uint4 w0 = lds<uint4>(sq + ti * 512u + 16u * k), w1 = lds<uint4>(sq + ti * 512u + cs + 16u * k);
+                const float dw = h2f(lds<uint16_t>(sm + 2u * (16u * ti + k)));
+                const uint8_t* xq = q + (size_t)t * 512u + 16u * k;
+                const uint4 x0 = XR ? xr.x[2 * ti] : lds<uint4>(xq);
+                const uint4 x1 = XR ? xr.x[2 * ti + 1] : lds<uint4>(xq + 256u);
+                const int32_t isum = dot16s(w1, x1, dot16s(w0, x0, 0));
+                if (isum_row) isum_row[b] = isum;
+                const float Dx = XR ? xr.dx[ti] : d[b];
+                p = add_<SAFE>(p, mul_<SAFE>(mul_<SAFE>(dw, Dx), i2f(isum)));
+            }
+        }
+    }
+}
+
+// EPI 0: y[row] = the MUL_MAT epilogue (addend / scale / softcap); EPI 1: also the isum hook,
+// SWIGLU pairs and the fused all-gather (a separate instance keeps the common case's registers free)
+template <int FMT, bool XR, bool FULL, bool SAFE, bool RING, int EPI>
+__device__ __forceinline__ void run_units(const MvArgs& a, const Plan& P, uint8_t* slots, uint32_t r_begin, uint32_t n, uint32_t nu,
+                                          uint32_t staged, Cursor<RING> ahead, const uint8_t* q, const float* d, const uint8_t* bs,
+                                          const XReg<FMT>& xr, float* team_rows) {
+    const Geo& G = P.g;
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u, k = lane & 15u, h = lane >> 4;
+    const uint32_t isum_stride = FMT == 0 ? G.nb : 2u * G.nb;
+    float pacc = 0.0f;
+    Cursor<RING> cur{warp, 0u, 0u};
+    for (uint32_t i = 0; i < nu; ++i) {
+        cpa_wait_dyn(staged - i - 1u);
+        __syncwarp();
+        const uint32_t pr = cur.pr, u = cur.u;
+        uint8_t* sl = slots + (size_t)cur.slot(P, warp) * G.slot;
+        const uint32_t r = 2u * pr + h;
+        const bool rv = r < n;
+        int32_t* isum_row = (EPI == 1 && a.isum_out && rv) ? a.isum_out + (size_t)(r_begin + r) * isum_stride : nullptr;
+        unit_math<FMT, XR, FULL, SAFE>(a, G, sl, u, k, h, q, d, bs, xr, pacc, isum_row);
+        if (RING && staged < nu) {                  // refill the slot with this warp's unit i + R
+            __syncwarp();
+            stage_unit<FMT>(a, G, r_begin, n, ahead.pr, ahead.u, sl, k, h);
+            ahead.next(P);
+            ++staged;
+        }
+        cur.next(P);
+        if (u + 1u == G.upp) {                       // the pair is complete: tree, epilogue, store
+            float v = pacc;
+            v = add_<SAFE>(v, __shfl_xor_sync(0xFFFFFFFFu, v, 1));
+            v = add_<SAFE>(v, __shfl_xor_sync(0xFFFFFFFFu, v, 2));
+            v = add_<SAFE>(v, __shfl_xor_sync(0xFFFFFFFFu, v, 4));
+            v = add_<SAFE>(v, __shfl_xor_sync(0xFFFFFFFFu, v, 8));
+            pacc = 0.0f;
+            const uint32_t row = r_begin + r;
+            if (EPI == 1 && a.swiglu_pairs) {        // gate (half 0) and up (half 1) rows
+                const float up = __shfl_sync(0xFFFFFFFFu, v, 16);
+                if (lane == 0 && rv) {
+                    const float yv = canon(fmul(daz(silu_mv(canon(v))), daz(canon(up))));
+                    if (a.team_world) team_rows[pr] = yv;
+                    else a.y[row >> 1] = yv;
+                }
+            } else if (k == 0 && rv) {
+                const float yv = mm_epilogue(v, a, 0u, row);
+                if (EPI == 1 && a.team_world) team_rows[r] = yv;
+                else a.y[row] = yv;
+            }
+        }
+    }
+}
+
+template <int FMT, bool XR, bool FULL, bool RING, int EPI>
+__global__ void __launch_bounds__(kThreads, 1) dec_kernel(MvArgs a, Plan P) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    const Geo& G = P.g;
+    const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31u, k = lane & 15u, h = lane >> 4;
+    const uint32_t r_begin = blockIdx.x * P.rpc;
+    if (r_begin >= a.n_rows) return;
+    const uint32_t n = min(a.n_rows - r_begin, P.rpc);
+    const uint32_t npairs = (n + 1u) / 2u;
+    uint32_t nu = 0;                                 // units of this warp: pairs warp, warp + 16, ...
+    for (uint32_t pr = warp; pr < npairs; pr += kWarps) nu += G.upp;
+    uint8_t* slots = smem + P.slots_off;
+    // every byte this lane reads: the whole share when it fits, else the first R units of the ring
+    const uint32_t staged = RING ? min(nu, P.ring) : nu;
+    Cursor<RING> ahead{warp, 0u, 0u};
+    for (uint32_t i = 0; i < staged; ++i) {
+        stage_unit<FMT>(a, G, r_begin, n, ahead.pr, ahead.u, slots + (size_t)ahead.slot(P, warp) * G.slot, k, h);
+        ahead.next(P);
+    }
+    asm volatile("griddepcontrol.launch_dependents;");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    const uint32_t team_step = (EPI == 1 && a.team_world) ? *reinterpret_cast<volatile uint32_t*>(a.team_state) : 0u;
+    uint8_t* q = smem;
+    float* d = reinterpret_cast<float*>(smem + P.qa_q);
+    uint8_t* bs = smem + P.qa_q + P.qa_d;
+    uint32_t* flags = reinterpret_cast<uint32_t*>(smem + P.flags_off);
+    float* team_rows = reinterpret_cast<float*>(smem + P.team_off);
+    const bool safe = stage_x1<FMT>(a, q, d, bs, flags);
+    XReg<FMT> xr;
+    if (XR) {
+        if constexpr (FMT == 1) {
+#pragma unroll
+            for (int c = 0; c < 16; ++c) xr.x[c] = lds<uint4>(q + 16u * k + 256u * c);
+            xr.B = lds<uint4>(bs + 16u * k);
+            xr.dx = d[k];
+        } else {
+#pragma unroll
+            for (uint32_t t = 0; t < kTpuQ8; ++t) {
+                xr.x[2 * t] = lds<uint4>(q + t * 512u + 16u * k);
+                xr.x[2 * t + 1] = lds<uint4>(q + t * 512u + 256u + 16u * k);
+                xr.dx[t] = d[16u * t + k];
+            }
+        }
+    }
+    if (safe) run_units<FMT, XR, FULL, true, RING, EPI>(a, P, slots, r_begin, n, nu, staged, ahead, q, d, bs, xr, team_rows);
+    else run_units<FMT, XR, FULL, false, RING, EPI>(a, P, slots, r_begin, n, nu, staged, ahead, q, d, bs, xr, team_rows);
+    if (EPI == 1 && a.team_world)
+        team_finish(a, team_step, flags, team_rows, a.swiglu_pairs ? r_begin / 2u : r_begin,
+                    a.swiglu_pairs ? (r_begin + n) / 2u : r_begin + n);
+}
+
+}  // namespace dec
+
 // ---- host side ------------------------------------------------------------------------------------
 size_t mv_smem_bytes(uint32_t fmt, uint32_t K, uint32_t T) { return make_plan(fmt, K).total(T); }
 
@@ -761,8 +1186,104 @@ static cudaError_t launch_fmt(const MvArgs& a, cudaStream_t st) {
     return launch_t<FMT, kMvMaxT>(a, st);
 }
 
+// ---- the one-token decode kernel: plan and launch ----
+static int g_smem_optin[64];
+
+template <int FMT, bool XR, bool FULL, bool RING, int EPI>
+static cudaError_t dec_launch(const MvArgs& a, const dec::Plan& P, uint32_t blocks, size_t smem, int dev, cudaStream_t st) {
+    static int done_dev[64];
+    if (dev < 64 && done_dev[dev] != dev + 1) {
+        cudaError_t e = cudaFuncSetAttribute(dec::dec_kernel<FMT, XR, FULL, RING, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             g_smem_optin[dev]);
+        if (e != cudaSuccess) return e;
+        done_dev[dev] = dev + 1;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(blocks);
+    cfg.blockDim = dim3(dec::kThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, dec::dec_kernel<FMT, XR, FULL, RING, EPI>, a, P);
+}
+
+template <int FMT, bool XR, bool FULL>
+static cudaError_t dec_launch_ring(const MvArgs& a, const dec::Plan& P, uint32_t blocks, size_t smem, int dev, cudaStream_t st) {
+    const bool general = a.isum_out || a.swiglu_pairs || a.team_world;
+    if (P.ring) return general ? dec_launch<FMT, XR, FULL, true, 1>(a, P, blocks, smem, dev, st)
+                               : dec_launch<FMT, XR, FULL, true, 0>(a, P, blocks, smem, dev, st);
+    return general ? dec_launch<FMT, XR, FULL, false, 1>(a, P, blocks, smem, dev, st)
+                   : dec_launch<FMT, XR, FULL, false, 0>(a, P, blocks, smem, dev, st);
+}
+
+// One token with QACT fused (a.x set): rows split evenly over the SMs in pairs; the CTA's units
+// get slots of their own when they fit in shared memory, else a ring of R units per warp.
+static cudaError_t launch_dec(uint32_t fmt, const MvArgs& a, cudaStream_t st) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev >= 64) return cudaErrorInvalidDevice;
+    if (g_num_sms[dev] == 0) {
+        int n = 0;
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+        g_num_sms[dev] = n > 0 ? n : 148;
+    }
+    if (g_smem_optin[dev] == 0) {
+        int n = 0;
+        e = cudaDeviceGetAttribute(&n, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+        if (e != cudaSuccess) return e;
+        g_smem_optin[dev] = n - 1024;          // room for the kernel's static shared memory
+    }
+    const uint32_t sms = (uint32_t)g_num_sms[dev];
+    const dec::Geo G(fmt, a.K);
+    dec::Plan P{};
+    P.g = G;
+    P.rpc = (a.n_rows + sms - 1u) / sms;
+    P.rpc = (P.rpc + 1u) & ~1u;
+    const uint32_t blocks = (a.n_rows + P.rpc - 1u) / P.rpc;
+    P.qa_q = G.tiles * (fmt == 0 ? 512u : 4096u);
+    P.qa_d = (uint32_t)a16((size_t)G.nb * 4u);
+    const uint32_t qa_bs = fmt == 0 ? 0u : G.tiles * 256u;
+    P.flags_off = (uint32_t)a16((size_t)P.qa_q + P.qa_d + qa_bs);
+    P.team_off = P.flags_off + 4u * dec::kWarps;
+    const uint32_t team_bytes = a.team_world ? 4u * P.rpc : 0u;
+    P.slots_off = (P.team_off + team_bytes + 127u) & ~127u;
+    const size_t optin = (size_t)g_smem_optin[dev];
+    if (P.slots_off + (size_t)16u * G.slot > optin) return cudaErrorInvalidValue;
+    const size_t avail = optin - P.slots_off;
+    const size_t units_cta = (size_t)(P.rpc / 2u) * G.upp;
+    size_t smem;
+    if (units_cta * G.slot <= avail) {
+        P.ring = 0;
+        smem = P.slots_off + units_cta * G.slot;
+    } else {
+        P.ring = (uint32_t)std::min<size_t>(8u, avail / ((size_t)dec::kWarps * G.slot));
+        smem = P.slots_off + (size_t)dec::kWarps * P.ring * G.slot;
+    }
+    // every unit of every row complete (no partial tile, no missing tile of a unit)
+    const bool full = (G.nb % (16u * G.tpu)) == 0;
+    const bool xr = fmt == 0 ? G.tiles <= dec::kTpuQ8 : G.tiles == 1;
+    if (fmt == 0) {
+        if (xr) return full ? dec_launch_ring<0, true, true>(a, P, blocks, smem, dev, st) : dec_launch_ring<0, true, false>(a, P, blocks, smem, dev, st);
+        return full ? dec_launch_ring<0, false, true>(a, P, blocks, smem, dev, st) : dec_launch_ring<0, false, false>(a, P, blocks, smem, dev, st);
+    }
+    if (xr) return full ? dec_launch_ring<1, true, true>(a, P, blocks, smem, dev, st) : dec_launch_ring<1, true, false>(a, P, blocks, smem, dev, st);
+    return full ? dec_launch_ring<1, false, true>(a, P, blocks, smem, dev, st) : dec_launch_ring<1, false, false>(a, P, blocks, smem, dev, st);
+}
+
+// TSRC_MV_LEGACY=1 runs one-token MUL_MATs through the multi-token kernel (same bits; for comparison)
+static bool dec_enabled() {
+    static const bool on = std::getenv("TSRC_MV_LEGACY") == nullptr;
+    return on;
+}
+
 cudaError_t launch_matvec(uint32_t fmt, const MvArgs& a, cudaStream_t st) {
     if (a.n_rows == 0 || a.T == 0) return cudaSuccess;
+    if (a.T == 1 && a.x && dec_enabled()) return launch_dec(fmt, a, st);
     return fmt == 0 ? launch_fmt<0>(a, st) : launch_fmt<1>(a, st);
 }
 

@@ -31,6 +31,12 @@
 namespace {
 
 constexpr size_t kNoAllocScratchBytes = 1u << 20;     // 1 MiB: the quantized image of up to 8 tokens of K <= 65536
+constexpr uint32_t kKMax = 65536;                     // the matvec's own bound on K (its shared-memory image)
+// The image of a full tile of 8 tokens at the largest K the matvec accepts fits the array (Q8_0, the
+// larger image: q 8 K + d 8 K / 32 * 4 + bs 8 K / 16 * 2 bytes, each rounded up to 256), so the
+// TSRC_E_SHAPE branch below is a defensive check that valid weights never reach.
+static_assert(8u * kKMax + 8u * (kKMax / 32u) * 4u + 8u * (kKMax / 16u) * 2u <= kNoAllocScratchBytes,
+              "the array must hold 8 tokens of the largest K");
 
 static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
 

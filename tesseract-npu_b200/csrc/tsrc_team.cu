@@ -25,6 +25,7 @@ int mm_check(tsrc_ctx* ctx, const tsrc_weight* w, const float* x, uint32_t T, ui
              const float* add, uint32_t add_stride, uint32_t flags, float s0, float s1, MvArgs* base, uint32_t* fmt,
              const char* who);
 int weight_rows(const tsrc_weight* w, uint32_t* N, uint32_t* row0, uint32_t* n_rows);
+int ctx_device(const tsrc_ctx* ctx, int* dev);
 }  // namespace tsrc
 
 struct tsrc_team {
@@ -59,8 +60,8 @@ int tsrc_team_create(tsrc_ctx* ctx, uint32_t rank, uint32_t world, uint32_t n_ma
     if (world < 1 || world > 64 || rank >= world) return tsrc::set_error(TSRC_E_ARG, "tsrc_team_create: rank / world out of range");
     if (n_max == 0) return tsrc::set_error(TSRC_E_ARG, "tsrc_team_create: n_max is 0");
     int dev = 0;
-    cudaError_t e = cudaGetDevice(&dev);
-    if (e != cudaSuccess) return cuda_err(e, "cudaGetDevice");
+    int rc = tsrc::ctx_device(ctx, &dev);      // the buffers live on the context's device
+    if (rc != TSRC_OK) return rc;
     tsrc_team* t = new tsrc_team{};
     t->ctx = ctx;
     t->device = dev;
@@ -69,7 +70,7 @@ int tsrc_team_create(tsrc_ctx* ctx, uint32_t rank, uint32_t world, uint32_t n_ma
     t->n_max = n_max;
     t->staging_bytes = a256((size_t)2 * n_max * 8u);
     t->bytes = t->staging_bytes + 256u;
-    e = cudaMalloc(&t->local, t->bytes);
+    cudaError_t e = cudaMalloc(&t->local, t->bytes);
     if (e == cudaSuccess) e = cudaMemset(t->local, 0, t->bytes);
     if (e == cudaSuccess) e = cudaMalloc(&t->dev_y, sizeof(unsigned long long*) * world);
     cudaIpcMemHandle_t h;
@@ -90,6 +91,9 @@ int tsrc_team_create(tsrc_ctx* ctx, uint32_t rank, uint32_t world, uint32_t n_ma
 int tsrc_team_connect(tsrc_team* t, const void* handles) {
     if (!t || !handles) return tsrc::set_error(TSRC_E_ARG, "tsrc_team_connect: NULL argument");
     if (t->connected) return tsrc::set_error(TSRC_E_ARG, "tsrc_team_connect: already connected");
+    int dev = 0;
+    int rc = tsrc::ctx_device(t->ctx, &dev);   // the peers' buffers are mapped into the team's device
+    if (rc != TSRC_OK) return rc;
     for (uint32_t r = 0; r < t->world; ++r) {
         if (r == t->rank) continue;
         cudaIpcMemHandle_t h;
@@ -120,6 +124,10 @@ int tsrc_team_connect_local(tsrc_team* t, const tsrc_team* const* members) {
         const tsrc_team* m = members[r];
         if (!m || m->world != t->world || m->rank != r || m->n_max != t->n_max)
             return tsrc::set_error(TSRC_E_ARG, "tsrc_team_connect_local: members must be ranks 0..world-1 of equal teams");
+        // the kernels store through these pointers with no peer mapping: members on other GPUs
+        // must connect through tsrc_team_connect (IPC handles, which enable peer access)
+        if (m->device != t->device)
+            return tsrc::set_error(TSRC_E_ARG, "tsrc_team_connect_local: every member must be on the team's device");
         t->peer[r] = m->local;
         ys[r] = reinterpret_cast<unsigned long long*>(m->local);
     }
@@ -131,6 +139,9 @@ int tsrc_team_connect_local(tsrc_team* t, const tsrc_team* const* members) {
 
 int tsrc_team_free(tsrc_team* t) {
     if (!t) return tsrc::set_error(TSRC_E_ARG, "tsrc_team_free: NULL team");
+    int cur = -1;
+    cudaGetDevice(&cur);
+    if (cur != t->device) cudaSetDevice(t->device);     // the team's device, not the caller's current one
     cudaDeviceSynchronize();
     for (uint32_t r = 0; r < t->world; ++r)
         if (t->opened[r]) cudaIpcCloseMemHandle(t->peer[r]);
