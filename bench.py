@@ -132,8 +132,8 @@ def prefill_measure(dev, tsrc, torch, reps=10, warmup=3):
         w.free()
     return {"metric": "prefill MUL_MAT int8 TOPS (tcgen05 kind::i8, bit-exact f32 block scaling)", "runs": res,
             "peak_kind": "2x measured bf16 dense (MEASURED_PEAKS.json)" if peak else None,
-            "note": "the reference's per-32-value f32 scale-and-accumulate runs on the CUDA cores; ncu tensor-pipe "
-                    "activity in profiles/mm_tc_prefill.md"}
+            "note": "the reference's per-32-value f32 scale-and-accumulate runs on the CUDA cores (tensor-pipe "
+                    "activity: the committed ncu summary of the prefill kernels)"}
 
 
 # end-to-end random-init models (BASELINE configs 4 and 5): decode tokens/s
@@ -298,14 +298,18 @@ def model_measure_tp(dev, tsrc, torch, dist, name, steps, warmup, rank, world, e
 
 
 def cpu_reference_model(name, threads, model=None):
-    """One decode token of the config on the host cores with the oracle's composition of the graph
-    (the reference's kinds): one layer at the config's KV length (synthetic q8_0 cache rows) plus
-    the head, the layer time scaled to all layers. Weights: the device model's rows when given, else
-    quantized on the host from seeded normals. Returns (tokens/s, kind, sample text)."""
+    """One decode token of the config on the host cores: one decoder layer at the config's KV length
+    (synthetic q8_0 cache rows) and the output norm + head, each timed directly (a second run of
+    each, after a first that faults the pages in), the layer time times the layer count plus the
+    head. The kinds are the reference's own functions (oracle/_ref: MUL_MAT, FA, RMS_NORM, ROPE, VOP,
+    GET_ROWS) when that library was built, else the restatement. Weights: the device model's rows
+    when given, else quantized on the host from seeded normals. Returns (tokens/s, kind, sample)."""
     import numpy as np
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle
     tsro = oracle.Tsro()
+    kind = "reference" if oracle.Ref.available() else "port"
+    ops = oracle.RefOps(oracle.Ref(), tsro) if kind == "reference" else tsro
     spec = MODELS[name]
     prompt = spec["prompt"]
     s = dict(spec["shape"], n_ctx=prompt + 1)
@@ -330,24 +334,26 @@ def cpu_reference_model(name, threads, model=None):
     if s["qkv_bias"]:
         L["bqkv"] = np.zeros(Hq + 2 * Hkv, np.float32)
     ts = float(np.power(np.float32(s["rope_base"]), np.float32(-2.0) / np.float32(D), dtype=np.float32))
-    om = oracle.OracleModel(tsro, dict(s, n_layer=1), [L], emb, head, np.ones(E, np.float32), ts,
+    om = oracle.OracleModel(ops, dict(s, n_layer=1), [L], emb, head, np.ones(E, np.float32), ts,
                             float(np.float32(1.0) / np.sqrt(np.float32(D))), threads=threads)
     kv = tsro.quantize(0, rng.standard_normal((prompt, Hkv), dtype=np.float32))
     om.kc[0][:prompt] = kv
     om.vc[0][:prompt] = kv[::-1]
-    x1 = np.zeros((1, E), np.float32)
-    t0 = time.perf_counter()
-    om.forward(np.array([3], np.int32), prompt)
-    t_fwd = time.perf_counter() - t0
-    t0 = time.perf_counter()
-    tsro.matvec(fmt, head, E, x1, threads=threads)
-    t_head = time.perf_counter() - t0
-    t_layer = max(t_fwd - t_head, 1e-9)
+    x = om.embed(np.array([3], np.int32))
+    t_layer = t_head = None
+    for _ in range(2):                      # the second run of each piece is the one reported
+        t0 = time.perf_counter()
+        y = om.layer(0, x, prompt)
+        t_layer = time.perf_counter() - t0
+        t0 = time.perf_counter()
+        om.logits(y)
+        t_head = time.perf_counter() - t0
     t_tok = s["n_layer"] * t_layer + t_head
-    kind = "port"
-    sample = (f"one decode token at KV length {prompt}: layer 0 timed ({t_layer * 1e3:.1f} ms) x {s['n_layer']} layers "
-              f"+ head ({t_head * 1e3:.1f} ms); {src}; oracle composition of the reference's kinds, {threads} host threads "
-              f"for the MUL_MATs")
+    what = ("the reference's own kinds (oracle/_ref)" if kind == "reference"
+            else "the restatement of the reference's kinds (oracle/_ref not built)")
+    sample = (f"one decode token at KV length {prompt}: one layer timed directly ({t_layer * 1e3:.1f} ms) x "
+              f"{s['n_layer']} layers + output norm and head ({t_head * 1e3:.1f} ms); {src}; {what}, {threads} host "
+              f"threads for the MUL_MATs")
     return 1.0 / t_tok, kind, sample
 
 
@@ -970,13 +976,22 @@ def main():
         graph = capture(torch, lambda: [step(i) for i in range(n_copies)], barrier)
         use_graph = graph is not None
 
+    # K steps = whole replays of the ring graph plus one replay of a graph of the remaining steps
+    # (so no step of the timed region is an eager launch)
+    rem_graph = None
+    if graph is not None and args.steps % n_copies:
+        rem_graph = capture(torch, lambda: [step(i) for i in range(args.steps % n_copies)], barrier)
+
     def value_loop(n):
         if graph is not None:
             reps, rem = divmod(n, n_copies)
             for _ in range(reps):
                 graph.replay()
-            for i in range(rem):
-                step(i)
+            if rem and rem_graph is not None and rem == args.steps % n_copies:
+                rem_graph.replay()
+            else:
+                for i in range(rem):
+                    step(i)
         else:
             for i in range(n):
                 step(i)
@@ -1007,14 +1022,19 @@ def main():
 
     # (1) serial: copy in, MUL_MAT, copy out, one after the other on one stream
     egraph = capture(torch, lambda: [e2e_step(i) for i in range(n_copies)], barrier) if use_graph else None
+    egraph_rem = (capture(torch, lambda: [e2e_step(i) for i in range(n_e2e % n_copies)], barrier)
+                  if egraph is not None and n_e2e % n_copies else None)
 
     def e2e_serial(n):
         if egraph is not None:
             reps, rem = divmod(n, n_copies)
             for _ in range(reps):
                 egraph.replay()
-            for i in range(rem):
-                e2e_step(i)
+            if rem and egraph_rem is not None and rem == n_e2e % n_copies:
+                egraph_rem.replay()
+            else:
+                for i in range(rem):
+                    e2e_step(i)
         else:
             for i in range(n):
                 e2e_step(i)
@@ -1040,13 +1060,17 @@ def main():
                   lambda b: y_host.copy_(yb_full[b] if world > 1 else yb_loc[b], non_blocking=True), s_in, s_out)
 
     pgraph = capture(torch, lambda: e2e_steps(n_copies), barrier) if use_graph else None
+    pgraph_rem = (capture(torch, lambda: e2e_steps(n_e2e % n_copies), barrier)
+                  if pgraph is not None and n_e2e % n_copies else None)
 
     def e2e_loop(n):
         if pgraph is not None:
             reps, rem = divmod(n, n_copies)
             for _ in range(reps):
                 pgraph.replay()
-            if rem:
+            if rem and pgraph_rem is not None and rem == n_e2e % n_copies:
+                pgraph_rem.replay()
+            elif rem:
                 e2e_steps(rem)
         else:
             e2e_steps(n)
@@ -1126,8 +1150,11 @@ def main():
                    "collective": None if world == 1 else ("all-gather fused in the matvec kernel (P2P stores over NVLink)"
                                                            if team is not None else "NCCL all_gather of y")},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                     "frac": round(achieved / peak, 4), "traffic": traffic, "peak_kind": peak_kind,
-                     "kernel": f"matvec_kernel<{fmt},1> (QACT fused)",
+                     "frac": round(achieved / peak, 4), "traffic": traffic,
+                     "traffic_source": ("ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch, copied from the "
+                                        "committed profile summary (not measured in this run)") if traffic else None,
+                     "peak_kind": peak_kind,
+                     "kernel": "dec_kernel (one-token MUL_MAT: QACT fused, weights staged in shared memory by TMA bulk copies)",
                      "us_per_launch": round(kern_us, 3),
                      "algorithmic_bytes_per_launch": shard_algo},
         "e2e": {"value": round(e2e, 2), "unit": "GB/s", "h2d_bytes_per_step": 4 * K,
@@ -1144,7 +1171,7 @@ def main():
         line["also"] = also
     if rank == 0:
         print(json.dumps(line), flush=True)
-    del graph, kgraph, egraph, pgraph
+    del graph, kgraph, egraph, pgraph, rem_graph, egraph_rem, pgraph_rem
     if world > 1:
         dist.barrier()
     if team is not None:

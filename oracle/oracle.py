@@ -37,7 +37,8 @@ def _ptr(a):
 def build(ref: bool = True) -> None:
     """Builds libtsro.so (always) and, where the reference tree is present, the reference driver."""
     subprocess.run(["make", "-s", "-C", HERE, "all"], check=True)
-    if ref and os.path.isdir(os.environ.get("REF_ROOT", "/root/reference") + "/sw/sim"):
+    root = os.environ.get("REF_ROOT")
+    if ref and root and os.path.isdir(os.path.join(root, "sw", "sim")):
         subprocess.run(["make", "-s", "-C", HERE, "ref"], check=True)
 
 
@@ -434,12 +435,18 @@ class OracleModel:
         self.kc = [np.zeros((cfg["n_ctx"], E // 32 * 34), np.uint8) for _ in layers]
         self.vc = [np.zeros((cfg["n_ctx"], E // 32 * 34), np.uint8) for _ in layers]
 
-    def forward(self, ids, pos0: int):
-        o, c = self.o, self.c
+    def embed(self, ids):
+        """GET_ROWS of the token embedding: [T, n_embd] f32."""
         ids = np.asarray(ids, np.int64)
-        T = ids.size
+        return self.o.dequant(self.c["fmt"], self.emb[ids], self.c["n_embd"])
+
+    def layer(self, li: int, x, pos0: int):
+        """Decoder layer li over the T rows of x at positions pos0 .. pos0 + T - 1 (causal); writes
+        the layer's cache cells and returns the layer's output rows."""
+        o, c = self.o, self.c
+        T = x.shape[0]
         E, D, nh, nkv, F, fmt = c["n_embd"], c["head_dim"], c["n_head"], c["n_head_kv"], c["n_ff"], c["fmt"]
-        Hq, n_kv = nh * D, pos0 + T
+        Hq, Hkv, n_kv = nh * D, nkv * D, pos0 + T
         inv_n = np.float32(1.0) / np.float32(E)
         pos = np.arange(pos0, pos0 + T, dtype=np.int32)
         mask = None
@@ -447,27 +454,58 @@ class OracleModel:
             mask = np.full((T, n_kv), -np.inf, np.float16)
             for t in range(T):
                 mask[t, :pos0 + t + 1] = 0
-        x = o.dequant(fmt, self.emb[ids], E)
         th = self.threads
         rope = dict(head_dim=D, n_dims=D, mode=c["rope_mode"], ts=self.ts)
-        Hkv = nkv * D
-        for li, L in enumerate(self.layers):
-            h = o.rms_norm(x, L["attn_norm"], c["rms_eps"], inv_n)
-            b = L.get("bqkv")
-            qkv = o.matvec(fmt, L["wqkv"], E, h, add=None if b is None else b[None, :], add_stride=0, threads=th)
-            q = o.rope(np.ascontiguousarray(qkv[:, :Hq]), pos, n_heads=nh, **rope)
-            k = o.rope(np.ascontiguousarray(qkv[:, Hq:Hq + Hkv]), pos, n_heads=nkv, **rope)
-            v = np.ascontiguousarray(qkv[:, Hq + Hkv:])
-            self.kc[li][pos0:n_kv] = o.quantize(FMT_Q8_0, k)
-            self.vc[li][pos0:n_kv] = o.quantize(FMT_Q8_0, v)
-            rc, att = o.fa(q.reshape(T, nh, D), self.kc[li], self.vc[li], D=D, n_head=nh, n_head_kv=nkv, n_kv=n_kv,
-                           scale=self.kq_scale, mask=mask, new=(pos0, n_kv))
-            if rc != 0:
-                raise RuntimeError(f"tsro_fa returned {rc}")
-            x = o.matvec(fmt, L["wo"], Hq, att.reshape(T, Hq), add=x, add_stride=E, threads=th)
-            h = o.rms_norm(x, L["ffn_norm"], c["rms_eps"], inv_n)
-            gu = o.matvec(fmt, L["wgu"], E, h, threads=th)
-            s = o.vop(7, np.ascontiguousarray(gu[:, :F]), np.ascontiguousarray(gu[:, F:]))
-            x = o.matvec(fmt, L["wd"], F, s, add=x, add_stride=E, threads=th)
-        h = o.rms_norm(x[-1:], self.out_norm, c["rms_eps"], inv_n)
-        return o.matvec(fmt, self.head, E, h, threads=th)[0]
+        L = self.layers[li]
+        h = o.rms_norm(x, L["attn_norm"], c["rms_eps"], inv_n)
+        b = L.get("bqkv")
+        qkv = o.matvec(fmt, L["wqkv"], E, h, add=None if b is None else b[None, :], add_stride=0, threads=th)
+        q = o.rope(np.ascontiguousarray(qkv[:, :Hq]), pos, n_heads=nh, **rope)
+        k = o.rope(np.ascontiguousarray(qkv[:, Hq:Hq + Hkv]), pos, n_heads=nkv, **rope)
+        v = np.ascontiguousarray(qkv[:, Hq + Hkv:])
+        self.kc[li][pos0:n_kv] = o.quantize(FMT_Q8_0, k)
+        self.vc[li][pos0:n_kv] = o.quantize(FMT_Q8_0, v)
+        rc, att = o.fa(q.reshape(T, nh, D), self.kc[li], self.vc[li], D=D, n_head=nh, n_head_kv=nkv, n_kv=n_kv,
+                       scale=self.kq_scale, mask=mask, new=(pos0, n_kv))
+        if rc != 0:
+            raise RuntimeError(f"FA returned {rc}")
+        x = o.matvec(fmt, L["wo"], Hq, att.reshape(T, Hq), add=x, add_stride=E, threads=th)
+        h = o.rms_norm(x, L["ffn_norm"], c["rms_eps"], inv_n)
+        gu = o.matvec(fmt, L["wgu"], E, h, threads=th)
+        s = o.vop(7, np.ascontiguousarray(gu[:, :F]), np.ascontiguousarray(gu[:, F:]))
+        return o.matvec(fmt, L["wd"], F, s, add=x, add_stride=E, threads=th)
+
+    def logits(self, x):
+        """Output RMS_NORM + MUL and the head of the last row of x."""
+        c = self.c
+        h = self.o.rms_norm(x[-1:], self.out_norm, c["rms_eps"], np.float32(1.0) / np.float32(c["n_embd"]))
+        return self.o.matvec(c["fmt"], self.head, c["n_embd"], h, threads=self.threads)[0]
+
+    def forward(self, ids, pos0: int):
+        x = self.embed(ids)
+        for li in range(len(self.layers)):
+            x = self.layer(li, x, pos0)
+        return self.logits(x)
+
+
+class RefOps:
+    """The reference library's kinds in the shape OracleModel calls them: MUL_MAT, FA, RMS_NORM,
+    ROPE, VOP and GET_ROWS run the reference's own functions (weights are repacked to its row
+    layout once, as its weight upload does); the KV rows are quantized by the restatement's Q8_0
+    quantizer, which the tests pin to the reference's QACT A32 bit for bit. Baseline timing only."""
+
+    def __init__(self, ref: "Ref", tsro: "Tsro"):
+        self.ref, self.tsro = ref, tsro
+        self._rows = {}
+
+    def matvec(self, fmt: int, w, K: int, x, **kw):
+        key = (id(w), fmt, K)
+        if key not in self._rows:
+            self._rows[key] = (w, self.ref.repack(fmt, w, K))
+        return self.ref.matvec_repacked(fmt, self._rows[key][1], K, x, **kw)
+
+    def quantize(self, fmt: int, x):
+        return self.tsro.quantize(fmt, x)
+
+    def __getattr__(self, name):
+        return getattr(self.ref, name)

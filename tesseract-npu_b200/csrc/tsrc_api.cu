@@ -404,7 +404,8 @@ int tsrc_sync(tsrc_ctx* ctx, void* stream) {
     e = tsrc::matvec_error(&code, true);
     if (e != cudaSuccess) return cuda_fail(e, "reading the kernel error flag");
     if (code) return fail(TSRC_E_DEVICE, "a matvec kernel gave up a bounded wait (code %u%s)", code,
-                          code == 2 ? ": a team peer did not signal its step" : "");
+                          code == 2 ? ": a team peer did not signal its step"
+                                    : code == 3 ? ": a weight copy into shared memory did not complete" : "");
     e = tsrc::tc_error(&code, true);
     if (e != cudaSuccess) return cuda_fail(e, "reading the tensor-core kernel error flag");
     if (code) return fail(TSRC_E_DEVICE, "a tensor-core MUL_MAT kernel gave up waiting for its MMA (code %u)", code);

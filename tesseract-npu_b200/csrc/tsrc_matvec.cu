@@ -210,7 +210,8 @@ __device__ __forceinline__ bool qact256_to_smem(const float (&v)[8], uint32_t s,
 // x_p, x_p+128, ...), the pairwise tree over the lanes of each of four warps (levels 1-5), then
 // ((q0 + q1) + (q2 + q3)); scale = RC(SQ(FA(FM(s, inv_n), eps))). Every CTA computes it (a few
 // microseconds of one kernel saved per norm on a decode step); ends with a barrier of the CTA.
-__device__ __forceinline__ float rms_scale(const MvArgs& a) {
+template <uint32_t NBAR>      // threads of the named barrier 1 (the warps that call this)
+__device__ __forceinline__ float rms_scale_n(const MvArgs& a) {
     __shared__ float part[4];
     const uint32_t tid = threadIdx.x;
     if (tid < 128u) {
@@ -223,11 +224,12 @@ __device__ __forceinline__ float rms_scale(const MvArgs& a) {
         for (uint32_t off = 1; off < 32u; off <<= 1) p = fadd(p, __shfl_down_sync(0xFFFFFFFFu, p, off));
         if ((tid & 31u) == 0) part[tid >> 5] = p;
     }
-    consumer_sync();
+    asm volatile("bar.sync 1, %0;" ::"n"(NBAR) : "memory");
     const float s = fadd(fadd(part[0], part[1]), fadd(part[2], part[3]));
     const float m = fadd(daz(fmul(daz(s), daz(a.rms_inv_n))), daz(a.rms_eps));     // FA(FM(s, inv_n), eps)
     return frecip(daz(flush(__fsqrt_rn(daz(m)))));                                    // RC(SQ(.))
 }
+__device__ __forceinline__ float rms_scale(const MvArgs& a) { return rms_scale_n<kCWarps * 32>(a); }
 // the normalised activation value j (raw = x_j; w_j of the norm weight, if any)
 __device__ __forceinline__ float rms_apply(float raw, float wj, bool has_w, float sc) {
     const float v = fmul(daz(raw), sc);
@@ -704,49 +706,71 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) matvec_kernel(MvArgs a, 
                     a.swiglu_pairs ? r_begin / 2u : r_begin, a.swiglu_pairs ? r_end / 2u : r_end);
 }
 
-// ---- one-token decode kernel: QACT fused, weights staged in shared memory ------------------------
-// The MUL_MAT of one token (the decode step) is the hot path. Its structure (measured on B200: the
-// launch is bound by the SM-side chain, not by HBM, unless every byte is requested at CTA start):
-//   - a warp owns pairs of rows (lane L: row L / 16 of the pair, block / superblock L % 16 of each
+// ---- one-token decode kernel: QACT fused, weights staged in shared memory by TMA ----------------
+// The MUL_MAT of one token (the decode step) is the hot path. Its structure (measured on B200):
+//   - a producer warp issues bulk copies (cp.async.bulk, the TMA engine; no multicast) of the
+//     CTA's rows into shared memory before the kernel waits for the previous one on the stream
+//     (weights are read-only): 32 rows per chunk, one mbarrier per chunk. When the CTA's share fits
+//     (a Q4_K 14336 x 4096 matrix: 98 rows x 2304 B per SM) every chunk has its own place, else the
+//     chunks (32 rows x one unit of tiles) cycle through a ring and are refilled as the consumers
+//     release them. Bulk copies leave the SM's load/store path free: per-thread cp.async copies of
+//     the same bytes slowed QACT's shuffles and shared-memory stores by 8x (7.3k against 0.9k
+//     cycles for one superblock);
+//   - 16 consumer warps run QACT (optionally after RMS_NORM) into the chunk-major image, then take
+//     one row pair per chunk (lane L: row L / 16 of the pair, block / superblock L % 16 of each
 //     tile, so a lane owns whole block sums and exactly partial p[L % 16] of its row, the
-//     reference's term order);
-//   - before it waits for the previous kernel (weights are read-only), every lane issues cp.async
-//     copies of exactly the bytes it will read, for all of its units if the CTA's share fits in
-//     shared memory (a 33 MB Q4_K 14336 x 4096 matrix does: 98 rows x 2304 B per SM), else for the
-//     first R units of a warp-private ring refilled as units are consumed; every byte of the share
-//     is in flight while the previous kernel finishes and QACT runs;
-//   - QACT (optionally after RMS_NORM) writes the chunk-major image; a lane keeps the activation of
-//     its block / superblock of a one-unit row in registers;
+//     reference's term order); a lane keeps the activation of a one-unit row in registers;
+//   - every consumer warp waits on every chunk in order (an mbarrier parity never aliases), and
+//     every wait is bounded (about a second of SM clock; then error code 3, which tsrc_sync
+//     reports, and the producer waits for its copies before the CTA ends);
 //   - the 16-partial tree is four xor-shuffle levels inside each half-warp.
 namespace dec {
 
-constexpr uint32_t kWarps = 16;
-constexpr uint32_t kThreads = kWarps * 32;
-constexpr uint32_t kTpuQ8 = 4;           // Q8_0 tiles per unit (Q4_K: 1)
+// NW consumer warps + one producer warp; rows per chunk at most 2 NW (one pair per consumer warp).
+// NW = 16 uses a whole SM; NW = 8 uses at most half of one (registers and shared memory), so the
+// next launch's CTA can stage its first chunks beside the running one.
+template <int NW>
+struct Shape {
+    static constexpr uint32_t kThreads = (NW + 1u) * 32u;
+    static constexpr uint32_t kRowGroup = 2u * NW;
+    static constexpr int kMinBlocks = NW <= 8 ? 2 : 1;
+};
+constexpr uint32_t kTpuQ8 = 4;                        // Q8_0 tiles per unit (Q4_K: 1)
+constexpr long long kWaitCycles = 2000000000ll;       // ~1 s of SM clock
 
-__device__ __forceinline__ void cpa16(void* dst, const void* src) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(su32(dst)), "l"(src) : "memory");
+__device__ __forceinline__ void mbar_init(uint64_t* b, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(su32(b)), "r"(count) : "memory");
 }
-__device__ __forceinline__ void cpa_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cpa_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
-// waits until at most n of this thread's copy groups are pending (n above 7 waits for 7)
-__device__ __forceinline__ void cpa_wait_dyn(uint32_t n) {
-    switch (n) {
-        case 0: cpa_wait<0>(); break;
-        case 1: cpa_wait<1>(); break;
-        case 2: cpa_wait<2>(); break;
-        case 3: cpa_wait<3>(); break;
-        case 4: cpa_wait<4>(); break;
-        case 5: cpa_wait<5>(); break;
-        case 6: cpa_wait<6>(); break;
-        default: cpa_wait<7>(); break;
-    }
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* b, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(su32(b)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* b) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(su32(b)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try(uint64_t* b, uint32_t parity) {
+    uint32_t ok;
+    asm volatile("{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+                 : "=r"(ok)
+                 : "r"(su32(b)), "r"(parity)
+                 : "memory");
+    return ok != 0;
+}
+// false when about a second of SM clock passed without the phase completing
+__device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity) {
+    if (mbar_try(b, parity)) return true;
+    const long long t0 = clock64();
+    while (!mbar_try(b, parity))
+        if (clock64() - t0 > kWaitCycles) return false;
+    return true;
+}
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(su32(dst)),
+                 "l"(src), "r"(bytes), "r"(su32(bar))
+                 : "memory");
 }
 
 struct Geo {
-    uint32_t nb, tiles, tpu, upp, qt, mt, qg, mg, slot;
-    uint32_t qrow, mrow;                     // bytes of a row's quants / meta
+    uint32_t nb, tiles, tpu, upp, qt, mt, qrow, mrow, bpb;
     Geo() = default;
     __host__ __device__ Geo(uint32_t fmt, uint32_t K) {
         nb = fmt == 0 ? K / 32u : K / 256u;
@@ -755,40 +779,24 @@ struct Geo {
         upp = (tiles + tpu - 1u) / tpu;
         qt = fmt == 0 ? 512u : 2048u;        // quant bytes of a full tile of one row
         mt = fmt == 0 ? 32u : 256u;          // meta bytes of a full tile of one row
-        qg = tpu * qt;
-        mg = tpu * mt;
-        slot = 2u * (qg + mg);               // a unit: both rows' quants, then both rows' meta
-        qrow = fmt == 0 ? K : K / 2u;
-        mrow = fmt == 0 ? ((K / 32u) * 2u + 15u) & ~15u : (K / 256u) * 16u;
+        bpb = fmt == 0 ? 32u : 128u;         // quant bytes per block / superblock
+        qrow = nb * bpb;
+        mrow = fmt == 0 ? (nb * 2u + 15u) & ~15u : nb * 16u;
     }
 };
 
 // Shared-memory plan and geometry of one launch (computed on the host: no divisions on the device).
 struct Plan {
     Geo g;
-    uint32_t rpc;         // rows per CTA (even)
-    uint32_t ring;        // 0: every unit of the CTA has its own slot; else slots per warp
-    uint32_t slots_off;   // byte offset of the unit slots
-    uint32_t qa_q, qa_d;  // QA image: quant bytes, scale bytes (Q4_K sums follow)
-    uint32_t team_off;    // the CTA's rows before the fused all-gather sends them
-    uint32_t flags_off;   // one word per warp (the fast-path vote)
-};
-
-// A walk over a warp's units in order: pair pr (of the CTA), unit u of the pair, and the unit's
-// shared-memory slot (own slot pr * upp + u, or the warp's ring slot warp + 16 rs).
-template <bool RING>
-struct Cursor {
-    uint32_t pr, u, rs;
-    __device__ __forceinline__ uint32_t slot(const Plan& P, uint32_t warp) const {
-        return RING ? warp + 16u * rs : pr * P.g.upp + u;
-    }
-    __device__ __forceinline__ void next(const Plan& P) {
-        if (++u == P.g.upp) {
-            u = 0;
-            pr += 16u;
-        }
-        if (RING && ++rs == P.ring) rs = 0;
-    }
+    uint32_t rpc;                 // rows per CTA (even)
+    uint32_t ring;                // 0: the CTA's rows all resident; else chunk slots in the ring
+    uint32_t R;                   // rows per chunk (even, <= 32: at most one pair per consumer warp)
+    uint32_t tt;                  // tiles per chunk: every tile (whole rows, one contiguous copy) or one unit
+    uint32_t kchunks;             // chunks per row group (1 for whole rows)
+    uint32_t qstride, mstride;    // shared-memory bytes per row of a chunk
+    uint32_t slot_bytes;          // ring: bytes of a slot (R rows)
+    uint32_t qa_q, qa_d;          // QA image: quant bytes, scale bytes (Q4_K sums follow)
+    uint32_t flags_off, team_off, slots_off, bars_off, nbars;
 };
 
 // QACT A256 of one superblock into the image (tsr_ref.c:488-518), one warp, lane l holds values
@@ -843,14 +851,15 @@ __device__ __forceinline__ bool qact256_img(const float (&v)[8], uint32_t s, uin
     return u == 0u || u >= kSafeDx;
 }
 
-// The image of the one token x (RMS_NORM + MUL in front when a.rms). Returns (uniform over the
-// CTA) whether every nonzero scale is >= 2^-79.
-template <int FMT>
+// The image of the one token x (RMS_NORM + MUL in front when a.rms), by the consumer warps.
+// Returns (uniform over them) whether every nonzero scale is >= 2^-79.
+template <int FMT, int NW>
 __device__ __forceinline__ bool stage_x1(const MvArgs& a, uint8_t* q, float* d, uint8_t* bs, uint32_t* flags) {
+    constexpr uint32_t kWarps = NW;
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
     const uint32_t nb = FMT == 0 ? a.K / 32u : a.K / 256u;
     const bool rms = a.rms != 0u, rms_w = a.rms_w != nullptr;
-    const float sc = rms ? rms_scale(a) : 0.0f;
+    const float sc = rms ? rms_scale_n<NW * 32u>(a) : 0.0f;
     bool ok = true;
     if (FMT == 0) {
         constexpr uint32_t B = 8;
@@ -889,7 +898,7 @@ __device__ __forceinline__ bool stage_x1(const MvArgs& a, uint8_t* q, float* d, 
     }
     const uint32_t bad = __any_sync(0xFFFFFFFFu, !ok);
     if (lane == 0) flags[warp] = bad;
-    __syncthreads();
+    asm volatile("bar.sync 1, %0;" ::"n"(NW * 32) : "memory");
     uint32_t any = 0;
 #pragma unroll
     for (uint32_t w = 0; w < kWarps; w += 4) {
@@ -915,60 +924,21 @@ struct XReg<0> {
     float dx[4];
 };
 
-// Copies the bytes lane (h, k) reads of unit (pair p, unit u) into slot sl.
-template <int FMT>
-__device__ __forceinline__ void stage_unit(const MvArgs& a, const Geo& G, uint32_t r_begin, uint32_t n, uint32_t p, uint32_t u,
-                                           uint8_t* sl, uint32_t k, uint32_t h) {
-    const uint32_t r = 2u * p + h;
-    if (r < n) {
-        const size_t grow = r_begin + r;
-        const uint32_t t0 = u * G.tpu;
-        const uint8_t* gq = a.qs + grow * G.qrow + (size_t)t0 * G.qt;
-        const uint8_t* gm = static_cast<const uint8_t*>(a.meta) + grow * G.mrow + (size_t)t0 * G.mt;
-        uint8_t* sq = sl + h * G.qg;
-        uint8_t* sm = sl + 2u * G.qg + h * G.mg;
-        if (FMT == 1) {
-            const uint32_t sb = 16u * t0 + k;
-            if (sb < G.nb) {
-                const uint32_t rest = G.nb - 16u * t0, cs = rest >= 16u ? 256u : 16u * rest;
-#pragma unroll
-                for (uint32_t j = 0; j < 8; ++j) cpa16(sq + j * cs + 16u * k, gq + j * cs + 16u * k);
-                cpa16(sm + 16u * k, gm + 16u * k);
-            }
-        } else {
-#pragma unroll
-            for (uint32_t ti = 0; ti < kTpuQ8; ++ti) {
-                const uint32_t t = t0 + ti;
-                if (t < G.tiles && 16u * t + k < G.nb) {
-                    const uint32_t rest = G.nb - 16u * t, cs = rest >= 16u ? 256u : 16u * rest;
-                    cpa16(sq + ti * 512u + 16u * k, gq + ti * 512u + 16u * k);
-                    cpa16(sq + ti * 512u + cs + 16u * k, gq + ti * 512u + cs + 16u * k);
-                }
-            }
-            // the unit's scales of this row: 2 bytes per block, rounded up to 16 (the meta row is
-            // padded to 16 bytes, so the last copy stays inside the row)
-            const uint32_t blocks = min(16u * kTpuQ8, G.nb - 16u * t0);
-            if (16u * k < 2u * blocks) cpa16(sm + 16u * k, gm + 16u * k);
-        }
-    }
-    cpa_commit();
-}
-
+// One unit (tiles t0 .. t0 + tpu - 1) of the lane's row: rq / rm address the row's tile 0 in shared
+// memory (tile t at rq + t * qt, rm + t * mt).
 template <int FMT, bool XR, bool FULL, bool SAFE>
-__device__ __forceinline__ void unit_math(const MvArgs& a, const Geo& G, const uint8_t* sl, uint32_t u, uint32_t k, uint32_t h,
+__device__ __forceinline__ void unit_math(const Geo& G, const uint8_t* rq, const uint8_t* rm, uint32_t t0, uint32_t k,
                                           const uint8_t* q, const float* d, const uint8_t* bs, const XReg<FMT>& xr, float& p,
                                           int32_t* isum_row) {
-    const uint8_t* sq = sl + h * G.qg;
-    const uint8_t* sm = sl + 2u * G.qg + h * G.mg;
-    const uint32_t t0 = u * G.tpu;
     if constexpr (FMT == 1) {
         const uint32_t sb = 16u * t0 + k;
         if (!FULL && sb >= G.nb) return;
         const uint32_t rest = G.nb - 16u * t0, cs = (FULL || rest >= 16u) ? 256u : 16u * rest;
+        const uint8_t* sq = rq + (size_t)t0 * 2048u + 16u * k;
         uint4 w[8];
 #pragma unroll
-        for (uint32_t j = 0; j < 8; ++j) w[j] = lds<uint4>(sq + j * cs + 16u * k);
-        const uint4 m = lds<uint4>(sm + 16u * k);
+        for (uint32_t j = 0; j < 8; ++j) w[j] = lds<uint4>(sq + j * cs);
+        const uint4 m = lds<uint4>(rm + (size_t)t0 * 256u + 16u * k);
         const uint32_t sc_lo = m.y & 0x3F3F3F3Fu, mn_lo = m.z & 0x3F3F3F3Fu;
         const uint32_t sc_hi = (m.w & 0x0F0F0F0Fu) | ((m.y >> 2) & 0x30303030u);
         const uint32_t mn_hi = ((m.w >> 4) & 0x0F0F0F0Fu) | ((m.z >> 2) & 0x30303030u);
@@ -1009,8 +979,9 @@ __device__ __forceinline__ void unit_math(const MvArgs& a, const Geo& G, const u
             if (!FULL && t >= G.tiles) break;
             if (FULL || b < G.nb) {
                 const uint32_t rest = G.nb - 16u * t, cs = (FULL || rest >= 16u) ? 256u : 16u * rest;
-                const uint4 w0 = lds<uint4>(sq + ti * 512u + 16u * k), w1 = lds<uint4>(sq + ti * 512u + cs + 16u * k);
-                const float dw = h2f(lds<uint16_t>(sm + 2u * (16u * ti + k)));
+                const uint8_t* sq = rq + (size_t)t * 512u + 16u * k;
+                const uint4 w0 = lds<uint4>(sq), w1 = lds<uint4>(sq + cs);
+                const float dw = h2f(lds<uint16_t>(rm + 2u * b));
                 const uint8_t* xq = q + (size_t)t * 512u + 16u * k;
                 const uint4 x0 = XR ? xr.x[2 * ti] : lds<uint4>(xq);
                 const uint4 x1 = XR ? xr.x[2 * ti + 1] : lds<uint4>(xq + 256u);
@@ -1023,34 +994,65 @@ __device__ __forceinline__ void unit_math(const MvArgs& a, const Geo& G, const u
     }
 }
 
+// The consumer warps' walk over the chunks: every chunk in order (row group rg, k-chunk kc), the
+// warp's pair of the row group (pair 16 rg + warp) over the chunk's units.
 // EPI 0: y[row] = the MUL_MAT epilogue (addend / scale / softcap); EPI 1: also the isum hook,
-// SWIGLU pairs and the fused all-gather (a separate instance keeps the common case's registers free)
-template <int FMT, bool XR, bool FULL, bool SAFE, bool RING, int EPI>
-__device__ __forceinline__ void run_units(const MvArgs& a, const Plan& P, uint8_t* slots, uint32_t r_begin, uint32_t n, uint32_t nu,
-                                          uint32_t staged, Cursor<RING> ahead, const uint8_t* q, const float* d, const uint8_t* bs,
-                                          const XReg<FMT>& xr, float* team_rows) {
+// SWIGLU pairs and the fused all-gather (a separate instance keeps the common case's registers free).
+template <int FMT, bool XR, bool FULL, bool SAFE, bool RING, int EPI, int NW>
+__device__ __forceinline__ bool consume(const MvArgs& a, const Plan& P, uint8_t* slots, uint64_t* full, uint64_t* empty,
+                                        uint32_t r_begin, uint32_t n, const uint8_t* q, const float* d, const uint8_t* bs,
+                                        const XReg<FMT>& xr, float* team_rows) {
+    constexpr uint32_t kWarps = NW;
     const Geo& G = P.g;
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u, k = lane & 15u, h = lane >> 4;
     const uint32_t isum_stride = FMT == 0 ? G.nb : 2u * G.nb;
+    const uint32_t npairs = (n + 1u) / 2u, ngroups = (n + P.R - 1u) / P.R;
     float pacc = 0.0f;
-    Cursor<RING> cur{warp, 0u, 0u};
-    for (uint32_t i = 0; i < nu; ++i) {
-        cpa_wait_dyn(staged - i - 1u);
-        __syncwarp();
-        const uint32_t pr = cur.pr, u = cur.u;
-        uint8_t* sl = slots + (size_t)cur.slot(P, warp) * G.slot;
-        const uint32_t r = 2u * pr + h;
-        const bool rv = r < n;
-        int32_t* isum_row = (EPI == 1 && a.isum_out && rv) ? a.isum_out + (size_t)(r_begin + r) * isum_stride : nullptr;
-        unit_math<FMT, XR, FULL, SAFE>(a, G, sl, u, k, h, q, d, bs, xr, pacc, isum_row);
-        if (RING && staged < nu) {                  // refill the slot with this warp's unit i + R
-            __syncwarp();
-            stage_unit<FMT>(a, G, r_begin, n, ahead.pr, ahead.u, sl, k, h);
-            ahead.next(P);
-            ++staged;
+    uint32_t c = 0, s = 0, ph = 0;              // chunk, its slot, the slot's phase parity
+    uint32_t row0 = 0;                           // first row of the row group
+    for (uint32_t rg = 0; rg < ngroups; ++rg, row0 += P.R) {
+        // the row group's pairs go to warps (pair mod 16): this warp's pair, if any
+        const uint32_t p0 = row0 >> 1;
+        const uint32_t pr = p0 + ((warp + kWarps - (p0 & (kWarps - 1u))) & (kWarps - 1u));
+        const uint32_t r = 2u * pr + h;          // the lane's row within the CTA
+        const bool has = pr < min(npairs, p0 + (P.R >> 1)), rv = r < n;
+        for (uint32_t kc = 0; kc < P.kchunks; ++kc, ++c) {
+            if (!__all_sync(0xFFFFFFFFu, mbar_wait(full + s, ph))) {     // a warp-uniform outcome
+                if (lane == 0) atomicCAS(&g_mv_error, 0u, 3u);
+                return false;
+            }
+            if (has) {
+                const uint8_t* rq;
+                const uint8_t* rm;
+                if (RING) {     // the chunk holds tiles kc tt .. of rows row0 ..: tile t at (t - kc tt) qt
+                    const uint8_t* sl = slots + (size_t)s * P.slot_bytes;
+                    rq = sl + (size_t)(r - row0) * P.qstride - (size_t)kc * P.tt * G.qt;
+                    rm = sl + (size_t)P.R * P.qstride + (size_t)(r - row0) * P.mstride - (size_t)kc * P.tt * G.mt;
+                } else {
+                    rq = slots + (size_t)r * G.qrow;
+                    rm = slots + (size_t)P.rpc * G.qrow + (size_t)r * G.mrow;
+                }
+                int32_t* isum_row = (EPI == 1 && a.isum_out && rv) ? a.isum_out + (size_t)(r_begin + r) * isum_stride : nullptr;
+                if (XR) {
+                    unit_math<FMT, XR, FULL, SAFE>(G, rq, rm, 0u, k, q, d, bs, xr, pacc, isum_row);
+                } else {
+                    const uint32_t t_end = RING ? min(G.tiles, (kc + 1u) * P.tt) : G.tiles;
+                    for (uint32_t t0 = RING ? kc * P.tt : 0u; t0 < t_end; t0 += G.tpu)
+                        unit_math<FMT, XR, FULL, SAFE>(G, rq, rm, t0, k, q, d, bs, xr, pacc, isum_row);
+                }
+            }
+            if (RING) {
+                __syncwarp();
+                if (lane == 0) mbar_arrive(empty + s);
+                if (++s == P.ring) {
+                    s = 0;
+                    ph ^= 1u;
+                }
+            } else {
+                ++s;
+            }
         }
-        cur.next(P);
-        if (u + 1u == G.upp) {                       // the pair is complete: tree, epilogue, store
+        if (has) {                               // the pair is complete: tree, epilogue, store
             float v = pacc;
             v = add_<SAFE>(v, __shfl_xor_sync(0xFFFFFFFFu, v, 1));
             v = add_<SAFE>(v, __shfl_xor_sync(0xFFFFFFFFu, v, 2));
@@ -1072,54 +1074,126 @@ __device__ __forceinline__ void run_units(const MvArgs& a, const Plan& P, uint8_
             }
         }
     }
+    return true;
 }
 
-template <int FMT, bool XR, bool FULL, bool RING, int EPI>
-__global__ void __launch_bounds__(kThreads, 1) dec_kernel(MvArgs a, Plan P) {
-    extern __shared__ __align__(128) uint8_t smem[];
+// The producer warp: the chunks' bulk copies (lane i copies row i of a ring chunk; resident chunks
+// are two contiguous copies), refills of ring slots as the consumers release them, and at the end
+// a bounded wait for every copy it issued.
+template <bool RING>
+__device__ __forceinline__ void produce(const MvArgs& a, const Plan& P, uint8_t* slots, uint64_t* full, uint64_t* empty,
+                                        uint32_t r_begin, uint32_t n) {
     const Geo& G = P.g;
-    const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31u, k = lane & 15u, h = lane >> 4;
+    const uint32_t lane = threadIdx.x & 31u;
+    const uint32_t ngroups = (n + P.R - 1u) / P.R, nch = ngroups * P.kchunks;
+    const uint8_t* meta = static_cast<const uint8_t*>(a.meta);
+    uint32_t issued = 0;
+    bool ok = true;
+    for (uint32_t c = 0; c < nch; ++c) {
+        const uint32_t rg = c / P.kchunks, kc = c - rg * P.kchunks;
+        const uint32_t row0 = P.R * rg, rows = min(P.R, n - row0);
+        uint32_t s = c;
+        if (RING) {
+            s = c % P.ring;
+            if (c >= P.ring && !__all_sync(0xFFFFFFFFu, mbar_wait(empty + s, ((c / P.ring) - 1u) & 1u))) {
+                if (lane == 0) atomicCAS(&g_mv_error, 0u, 3u);
+                ok = false;
+                break;
+            }
+            uint8_t* sl = slots + (size_t)s * P.slot_bytes;
+            if (P.kchunks == 1u) {               // whole rows: one contiguous copy of quants, one of meta
+                if (lane == 0) {
+                    mbar_expect_tx(full + s, rows * (G.qrow + G.mrow));
+                    bulk_g2s(sl, a.qs + (size_t)(r_begin + row0) * G.qrow, rows * G.qrow, full + s);
+                    bulk_g2s(sl + (size_t)P.R * G.qrow, meta + (size_t)(r_begin + row0) * G.mrow, rows * G.mrow, full + s);
+                }
+                issued = c + 1u;
+                continue;
+            }
+            const uint32_t t0 = kc * P.tt, t1 = min(G.tiles, t0 + P.tt);
+            const uint32_t qb = min(16u * t1, G.nb) * G.bpb - 16u * t0 * G.bpb;
+            const uint32_t mb = G.tpu == 1u ? (min(16u * t1, G.nb) - 16u * t0) * 16u
+                                            : ((min(16u * t1, G.nb) - 16u * t0) * 2u + 15u) & ~15u;
+            if (lane == 0) mbar_expect_tx(full + s, rows * (qb + mb));
+            __syncwarp();
+            if (lane < rows) {                   // one unit of each row: lane i copies row i
+                const size_t grow = r_begin + row0 + lane;
+                bulk_g2s(sl + (size_t)lane * P.qstride, a.qs + grow * G.qrow + (size_t)t0 * G.qt, qb, full + s);
+                bulk_g2s(sl + (size_t)P.R * P.qstride + (size_t)lane * P.mstride, meta + grow * G.mrow + (size_t)t0 * G.mt, mb,
+                         full + s);
+            }
+        } else if (lane == 0) {
+            mbar_expect_tx(full + s, rows * (G.qrow + G.mrow));
+            bulk_g2s(slots + (size_t)row0 * G.qrow, a.qs + (size_t)(r_begin + row0) * G.qrow, rows * G.qrow, full + s);
+            bulk_g2s(slots + (size_t)P.rpc * G.qrow + (size_t)row0 * G.mrow, meta + (size_t)(r_begin + row0) * G.mrow,
+                     rows * G.mrow, full + s);
+        }
+        issued = c + 1u;
+    }
+    // the CTA must not end while a copy is still writing its shared memory
+    const uint32_t first = RING ? (issued > P.ring ? issued - P.ring : 0u) : 0u;
+    for (uint32_t c = first; c < issued; ++c) {
+        const uint32_t s = RING ? c % P.ring : c, ph = RING ? (c / P.ring) & 1u : 0u;
+        if (!mbar_wait(full + s, ph)) {
+            if (lane == 0) atomicCAS(&g_mv_error, 0u, 3u);
+            break;
+        }
+    }
+    (void)ok;
+}
+
+template <int FMT, bool XR, bool FULL, bool RING, int EPI, int NW>
+__global__ void __launch_bounds__(Shape<NW>::kThreads, Shape<NW>::kMinBlocks) dec_kernel(MvArgs a, Plan P) {
+    constexpr uint32_t kWarps = NW;
+    extern __shared__ __align__(128) uint8_t smem[];
+    const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31u, k = lane & 15u;
     const uint32_t r_begin = blockIdx.x * P.rpc;
     if (r_begin >= a.n_rows) return;
     const uint32_t n = min(a.n_rows - r_begin, P.rpc);
-    const uint32_t npairs = (n + 1u) / 2u;
-    uint32_t nu = 0;                                 // units of this warp: pairs warp, warp + 16, ...
-    for (uint32_t pr = warp; pr < npairs; pr += kWarps) nu += G.upp;
     uint8_t* slots = smem + P.slots_off;
-    // every byte this lane reads: the whole share when it fits, else the first R units of the ring
-    const uint32_t staged = RING ? min(nu, P.ring) : nu;
-    Cursor<RING> ahead{warp, 0u, 0u};
-    for (uint32_t i = 0; i < staged; ++i) {
-        stage_unit<FMT>(a, G, r_begin, n, ahead.pr, ahead.u, slots + (size_t)ahead.slot(P, warp) * G.slot, k, h);
-        ahead.next(P);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + P.bars_off);
+    uint64_t* empty = full + P.nbars;
+    if (tid == 0) {
+        for (uint32_t i = 0; i < P.nbars; ++i) {
+            mbar_init(full + i, 1u);
+            if (RING) mbar_init(empty + i, kWarps);
+        }
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
+    __syncthreads();
     asm volatile("griddepcontrol.launch_dependents;");
-    asm volatile("griddepcontrol.wait;" ::: "memory");
     const uint32_t team_step = (EPI == 1 && a.team_world) ? *reinterpret_cast<volatile uint32_t*>(a.team_state) : 0u;
-    uint8_t* q = smem;
-    float* d = reinterpret_cast<float*>(smem + P.qa_q);
-    uint8_t* bs = smem + P.qa_q + P.qa_d;
     uint32_t* flags = reinterpret_cast<uint32_t*>(smem + P.flags_off);
     float* team_rows = reinterpret_cast<float*>(smem + P.team_off);
-    const bool safe = stage_x1<FMT>(a, q, d, bs, flags);
-    XReg<FMT> xr;
-    if (XR) {
-        if constexpr (FMT == 1) {
+    if (warp == kWarps) {
+        produce<RING>(a, P, slots, full, empty, r_begin, n);        // weights only: no wait for the previous kernel
+    } else {
+        asm volatile("griddepcontrol.wait;" ::: "memory");
+        uint8_t* q = smem;
+        float* d = reinterpret_cast<float*>(smem + P.qa_q);
+        uint8_t* bs = smem + P.qa_q + P.qa_d;
+        const bool safe = stage_x1<FMT, NW>(a, q, d, bs, flags);
+        XReg<FMT> xr;
+        if (XR) {
+            if constexpr (FMT == 1) {
 #pragma unroll
-            for (int c = 0; c < 16; ++c) xr.x[c] = lds<uint4>(q + 16u * k + 256u * c);
-            xr.B = lds<uint4>(bs + 16u * k);
-            xr.dx = d[k];
-        } else {
+                for (int c = 0; c < 16; ++c) xr.x[c] = lds<uint4>(q + 16u * k + 256u * c);
+                xr.B = lds<uint4>(bs + 16u * k);
+                xr.dx = d[k];
+            } else {
 #pragma unroll
-            for (uint32_t t = 0; t < kTpuQ8; ++t) {
-                xr.x[2 * t] = lds<uint4>(q + t * 512u + 16u * k);
-                xr.x[2 * t + 1] = lds<uint4>(q + t * 512u + 256u + 16u * k);
-                xr.dx[t] = d[16u * t + k];
+                for (uint32_t t = 0; t < kTpuQ8; ++t) {      // the image holds P.g.tiles tiles
+                    if (t < P.g.tiles) {
+                        xr.x[2 * t] = lds<uint4>(q + t * 512u + 16u * k);
+                        xr.x[2 * t + 1] = lds<uint4>(q + t * 512u + 256u + 16u * k);
+                        xr.dx[t] = d[16u * t + k];
+                    }
+                }
             }
         }
+        if (safe) consume<FMT, XR, FULL, true, RING, EPI, NW>(a, P, slots, full, empty, r_begin, n, q, d, bs, xr, team_rows);
+        else consume<FMT, XR, FULL, false, RING, EPI, NW>(a, P, slots, full, empty, r_begin, n, q, d, bs, xr, team_rows);
     }
-    if (safe) run_units<FMT, XR, FULL, true, RING, EPI>(a, P, slots, r_begin, n, nu, staged, ahead, q, d, bs, xr, team_rows);
-    else run_units<FMT, XR, FULL, false, RING, EPI>(a, P, slots, r_begin, n, nu, staged, ahead, q, d, bs, xr, team_rows);
     if (EPI == 1 && a.team_world)
         team_finish(a, team_step, flags, team_rows, a.swiglu_pairs ? r_begin / 2u : r_begin,
                     a.swiglu_pairs ? (r_begin + n) / 2u : r_begin + n);
@@ -1188,19 +1262,20 @@ static cudaError_t launch_fmt(const MvArgs& a, cudaStream_t st) {
 
 // ---- the one-token decode kernel: plan and launch ----
 static int g_smem_optin[64];
+static int g_smem_sm[64];
 
-template <int FMT, bool XR, bool FULL, bool RING, int EPI>
+template <int FMT, bool XR, bool FULL, bool RING, int EPI, int NW>
 static cudaError_t dec_launch(const MvArgs& a, const dec::Plan& P, uint32_t blocks, size_t smem, int dev, cudaStream_t st) {
     static int done_dev[64];
     if (dev < 64 && done_dev[dev] != dev + 1) {
-        cudaError_t e = cudaFuncSetAttribute(dec::dec_kernel<FMT, XR, FULL, RING, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        cudaError_t e = cudaFuncSetAttribute(dec::dec_kernel<FMT, XR, FULL, RING, EPI, NW>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              g_smem_optin[dev]);
         if (e != cudaSuccess) return e;
         done_dev[dev] = dev + 1;
     }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(blocks);
-    cfg.blockDim = dim3(dec::kThreads);
+    cfg.blockDim = dim3(dec::Shape<NW>::kThreads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
@@ -1208,20 +1283,91 @@ static cudaError_t dec_launch(const MvArgs& a, const dec::Plan& P, uint32_t bloc
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, dec::dec_kernel<FMT, XR, FULL, RING, EPI>, a, P);
+    return cudaLaunchKernelEx(&cfg, dec::dec_kernel<FMT, XR, FULL, RING, EPI, NW>, a, P);
 }
 
-template <int FMT, bool XR, bool FULL>
+template <int FMT, bool XR, bool FULL, int NW>
 static cudaError_t dec_launch_ring(const MvArgs& a, const dec::Plan& P, uint32_t blocks, size_t smem, int dev, cudaStream_t st) {
     const bool general = a.isum_out || a.swiglu_pairs || a.team_world;
-    if (P.ring) return general ? dec_launch<FMT, XR, FULL, true, 1>(a, P, blocks, smem, dev, st)
-                               : dec_launch<FMT, XR, FULL, true, 0>(a, P, blocks, smem, dev, st);
-    return general ? dec_launch<FMT, XR, FULL, false, 1>(a, P, blocks, smem, dev, st)
-                   : dec_launch<FMT, XR, FULL, false, 0>(a, P, blocks, smem, dev, st);
+    if (P.ring) return general ? dec_launch<FMT, XR, FULL, true, 1, NW>(a, P, blocks, smem, dev, st)
+                               : dec_launch<FMT, XR, FULL, true, 0, NW>(a, P, blocks, smem, dev, st);
+    return general ? dec_launch<FMT, XR, FULL, false, 1, NW>(a, P, blocks, smem, dev, st)
+                   : dec_launch<FMT, XR, FULL, false, 0, NW>(a, P, blocks, smem, dev, st);
 }
 
-// One token with QACT fused (a.x set): rows split evenly over the SMs in pairs; the CTA's units
-// get slots of their own when they fit in shared memory, else a ring of R units per warp.
+// One token with QACT fused (a.x set): rows split evenly over the SMs in pairs; the CTA's rows all
+// resident in shared memory when they fit its budget, else chunks of whole rows (or of one unit of
+// 2 NW rows, for rows too long for three chunks) through a ring. NW = 8 keeps every CTA within half
+// an SM (the next launch's CTA stages its first chunks while this one runs); NW = 16 uses the SM.
+template <int NW>
+static cudaError_t launch_dec_nw(uint32_t fmt, const MvArgs& a, int dev, uint32_t sms, cudaStream_t st) {
+    using S = dec::Shape<NW>;
+    const dec::Geo G(fmt, a.K);
+    dec::Plan P{};
+    P.g = G;
+    P.rpc = (a.n_rows + sms - 1u) / sms;
+    P.rpc = (P.rpc + 1u) & ~1u;
+    const uint32_t blocks = (a.n_rows + P.rpc - 1u) / P.rpc;
+    P.qa_q = G.tiles * (fmt == 0 ? 512u : 4096u);
+    P.qa_d = (uint32_t)a16((size_t)G.nb * 4u);
+    const uint32_t qa_bs = fmt == 0 ? 0u : G.tiles * 256u;
+    P.flags_off = (uint32_t)a16((size_t)P.qa_q + P.qa_d + qa_bs);
+    P.team_off = P.flags_off + 4u * NW;
+    const uint32_t team_bytes = a.team_world ? 4u * P.rpc : 0u;
+    P.slots_off = (P.team_off + team_bytes + 127u) & ~127u;
+    // the CTA's budget: the opt-in maximum, or half an SM's shared memory for two CTAs per SM
+    const size_t budget = S::kMinBlocks == 1 ? (size_t)g_smem_optin[dev] : (size_t)g_smem_sm[dev] / 2u - 1024u - 256u;
+    const size_t row_bytes = (size_t)G.qrow + G.mrow;
+    const size_t resident = (size_t)P.rpc * row_bytes;
+    const uint32_t ngroups = (P.rpc + S::kRowGroup - 1u) / S::kRowGroup;
+    if (P.slots_off + 256u > budget) return cudaErrorInvalidValue;
+    size_t slots_end;
+    if (P.slots_off + resident + 16u * ngroups <= budget) {
+        P.ring = 0;                              // the CTA's rows all resident
+        P.R = S::kRowGroup;
+        P.tt = G.tiles;
+        P.kchunks = 1;
+        P.qstride = G.qrow;
+        P.mstride = G.mrow;
+        P.nbars = ngroups;
+        slots_end = P.slots_off + resident;
+    } else {
+        const size_t room = budget - P.slots_off - 256u;
+        // whole-row chunks (contiguous copies) if three of at least two rows fit, else one unit of
+        // 2 NW rows per chunk (a copy per row)
+        uint32_t R = (uint32_t)std::min<size_t>(S::kRowGroup, room / (3u * row_bytes)) & ~1u;
+        if (R >= 2u) {
+            P.R = R;
+            P.tt = G.tiles;
+            P.kchunks = 1;
+            P.qstride = G.qrow;
+            P.mstride = G.mrow;
+        } else {
+            P.R = S::kRowGroup;
+            P.tt = std::min(G.tpu, G.tiles);
+            P.kchunks = (G.tiles + P.tt - 1u) / P.tt;
+            P.qstride = P.tt * G.qt;
+            P.mstride = P.tt * G.mt;
+        }
+        P.slot_bytes = P.R * (P.qstride + P.mstride);
+        if (2u * (size_t)P.slot_bytes > room) return cudaErrorInvalidValue;
+        P.ring = (uint32_t)std::min<size_t>(8u, room / P.slot_bytes);
+        P.nbars = P.ring;
+        slots_end = P.slots_off + (size_t)P.ring * P.slot_bytes;
+    }
+    P.bars_off = (uint32_t)((slots_end + 15u) & ~(size_t)15u);
+    const size_t smem = P.bars_off + 16u * (size_t)P.nbars;
+    // every unit of every row complete (no partial tile, no missing tile of a unit)
+    const bool full = (G.nb % (16u * G.tpu)) == 0;
+    const bool xr = fmt == 0 ? G.tiles <= dec::kTpuQ8 : G.tiles == 1;
+    if (fmt == 0) {
+        if (xr) return full ? dec_launch_ring<0, true, true, NW>(a, P, blocks, smem, dev, st) : dec_launch_ring<0, true, false, NW>(a, P, blocks, smem, dev, st);
+        return full ? dec_launch_ring<0, false, true, NW>(a, P, blocks, smem, dev, st) : dec_launch_ring<0, false, false, NW>(a, P, blocks, smem, dev, st);
+    }
+    if (xr) return full ? dec_launch_ring<1, true, true, NW>(a, P, blocks, smem, dev, st) : dec_launch_ring<1, true, false, NW>(a, P, blocks, smem, dev, st);
+    return full ? dec_launch_ring<1, false, true, NW>(a, P, blocks, smem, dev, st) : dec_launch_ring<1, false, false, NW>(a, P, blocks, smem, dev, st);
+}
+
 static cudaError_t launch_dec(uint32_t fmt, const MvArgs& a, cudaStream_t st) {
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
@@ -1233,46 +1379,14 @@ static cudaError_t launch_dec(uint32_t fmt, const MvArgs& a, cudaStream_t st) {
         g_num_sms[dev] = n > 0 ? n : 148;
     }
     if (g_smem_optin[dev] == 0) {
-        int n = 0;
+        int n = 0, m = 0;
         e = cudaDeviceGetAttribute(&n, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+        if (e == cudaSuccess) e = cudaDeviceGetAttribute(&m, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev);
         if (e != cudaSuccess) return e;
+        g_smem_sm[dev] = m;
         g_smem_optin[dev] = n - 1024;          // room for the kernel's static shared memory
     }
-    const uint32_t sms = (uint32_t)g_num_sms[dev];
-    const dec::Geo G(fmt, a.K);
-    dec::Plan P{};
-    P.g = G;
-    P.rpc = (a.n_rows + sms - 1u) / sms;
-    P.rpc = (P.rpc + 1u) & ~1u;
-    const uint32_t blocks = (a.n_rows + P.rpc - 1u) / P.rpc;
-    P.qa_q = G.tiles * (fmt == 0 ? 512u : 4096u);
-    P.qa_d = (uint32_t)a16((size_t)G.nb * 4u);
-    const uint32_t qa_bs = fmt == 0 ? 0u : G.tiles * 256u;
-    P.flags_off = (uint32_t)a16((size_t)P.qa_q + P.qa_d + qa_bs);
-    P.team_off = P.flags_off + 4u * dec::kWarps;
-    const uint32_t team_bytes = a.team_world ? 4u * P.rpc : 0u;
-    P.slots_off = (P.team_off + team_bytes + 127u) & ~127u;
-    const size_t optin = (size_t)g_smem_optin[dev];
-    if (P.slots_off + (size_t)16u * G.slot > optin) return cudaErrorInvalidValue;
-    const size_t avail = optin - P.slots_off;
-    const size_t units_cta = (size_t)(P.rpc / 2u) * G.upp;
-    size_t smem;
-    if (units_cta * G.slot <= avail) {
-        P.ring = 0;
-        smem = P.slots_off + units_cta * G.slot;
-    } else {
-        P.ring = (uint32_t)std::min<size_t>(8u, avail / ((size_t)dec::kWarps * G.slot));
-        smem = P.slots_off + (size_t)dec::kWarps * P.ring * G.slot;
-    }
-    // every unit of every row complete (no partial tile, no missing tile of a unit)
-    const bool full = (G.nb % (16u * G.tpu)) == 0;
-    const bool xr = fmt == 0 ? G.tiles <= dec::kTpuQ8 : G.tiles == 1;
-    if (fmt == 0) {
-        if (xr) return full ? dec_launch_ring<0, true, true>(a, P, blocks, smem, dev, st) : dec_launch_ring<0, true, false>(a, P, blocks, smem, dev, st);
-        return full ? dec_launch_ring<0, false, true>(a, P, blocks, smem, dev, st) : dec_launch_ring<0, false, false>(a, P, blocks, smem, dev, st);
-    }
-    if (xr) return full ? dec_launch_ring<1, true, true>(a, P, blocks, smem, dev, st) : dec_launch_ring<1, true, false>(a, P, blocks, smem, dev, st);
-    return full ? dec_launch_ring<1, false, true>(a, P, blocks, smem, dev, st) : dec_launch_ring<1, false, false>(a, P, blocks, smem, dev, st);
+    return launch_dec_nw<16>(fmt, a, dev, (uint32_t)g_num_sms[dev], st);
 }
 
 // TSRC_MV_LEGACY=1 runs one-token MUL_MATs through the multi-token kernel (same bits; for comparison)

@@ -79,6 +79,25 @@ def test_fa_special_values(dev, tsro):
     np.testing.assert_array_equal(got.view(np.uint32), want.view(np.uint32))
 
 
+@pytest.mark.parametrize("shape", ["cfg4", "cfg5"])
+def test_fa_prefill_bench_shapes(dev, tsro, shape):
+    """Prefill attention of the bench's models at their prompt lengths, all query rows: config 4
+    (Qwen2.5-0.5B: 14 q / 2 KV heads of 64, 512 tokens) and config 5 (Llama-3-8B: 32 q / 8 KV heads
+    of 128, 2048 tokens), causal from position 0, the release attention configuration."""
+    D, nkvh, G, T, seed = {"cfg4": (64, 2, 7, 512, 81), "cfg5": (128, 8, 4, 2048, 85)}[shape]
+    E = nkvh * D
+    k = H.kv_rows(tsro, T, E, seed)
+    v = H.kv_rows(tsro, T, E, seed + 1)
+    q = np.random.default_rng(seed + 2).standard_normal((T, nkvh * G, D)).astype(np.float32)
+    mask = H.fa_mask("causal", T, T, 0, seed=seed + 3)
+    kw = dict(D=D, n_head=nkvh * G, n_head_kv=nkvh, n_kv=T, scale=float(np.float32(1.0) / np.sqrt(np.float32(D))),
+              mask=mask, C=4, t_max=4, pcap=9344, new=(0, T))
+    rc, want = tsro.fa(q, k, v, **kw)
+    assert rc == 0
+    got = _fa_gpu(dev, q, k, v, kw)
+    np.testing.assert_array_equal(got.view(np.uint32), want.view(np.uint32))
+
+
 @pytest.mark.parametrize("C,t_max,pcap", [(1, 1, 9344), (2, 8, 4096), (8, 4, 9344), (16, 2, 16384)])
 def test_fa_attention_configs(dev, tsro, C, t_max, pcap):
     """The output depends on C, T_MAX and PCAP (chunking and channel trees); the kernels follow."""

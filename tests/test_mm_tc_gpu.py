@@ -91,3 +91,35 @@ def test_prefill_special_values_and_epilogues(dev, tsro, fmt):
         np.testing.assert_array_equal(got.view(np.uint32), want_sc.view(np.uint32))
     finally:
         wd.free()
+
+
+@pytest.mark.parametrize("fmt,N,K,T,seed", [(1, 14336, 4096, 2048, 501), (0, 4864, 896, 512, 401)],
+                         ids=["cfg5_ffn_q4k_14336x4096_T2048", "cfg4_ffn_q80_4864x896_T512"])
+def test_prefill_bench_shapes_bit_exact(dev, tsro, fmt, N, K, T, seed):
+    """The bench's prefill workloads at their full size (the seeded weights bench.py times, every
+    row and every token) against the oracle, bit for bit."""
+    wd = dev.synth(fmt, N, K, seed=seed)
+    try:
+        w = wd.download()
+        x = H.acts(K, T, seed + 1)
+        got = _mul_mat(dev, wd, x, T)
+        want = tsro.matvec(fmt, w, K, x)
+        np.testing.assert_array_equal(got.view(np.uint32), want.view(np.uint32))
+    finally:
+        wd.free()
+
+
+@pytest.mark.parametrize("fmt,T", [(0, 16), (0, 32), (0, 100), (1, 16), (1, 33)])
+def test_prefill_tile_widths_large_n(dev, tsro, fmt, T):
+    """Each token-tile width of the tensor-core kernels (Q8_0: 16 / 32 / 64 tokens, Q4_K: 16 / 32)
+    at N = K = 4096, every row."""
+    N, K = 4096, 4096
+    wd = dev.synth(fmt, N, K, seed=600 + T + fmt)
+    try:
+        w = wd.download()
+        x = H.acts(K, T, 700 + T + fmt)
+        got = _mul_mat(dev, wd, x, T)
+        want = tsro.matvec(fmt, w, K, x)
+        np.testing.assert_array_equal(got.view(np.uint32), want.view(np.uint32))
+    finally:
+        wd.free()
