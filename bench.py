@@ -675,7 +675,7 @@ def run_fa(args):
                    "cuda_graph": info["cuda_graph"], "collective": "NCCL all_gather of out" if world > 1 else None},
         "roofline": {"bound": "hbm", "achieved": round(shard / (us * 1e-6) / 1e9, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(shard / (us * 1e-6) / 1e9 / peak, 4), "traffic": traffic, "peak_kind": peak_kind,
-                     "kernel": "fa_chunk_kernel<128> + fa_merge_kernel (one step)", "us_per_launch": round(us, 3),
+                     "kernel": "fa_chunk_kernel<128> + fa_merge_kernel<4> (one step)", "us_per_launch": round(us, 3),
                      "algorithmic_bytes_per_launch": shard},
         "e2e": {"value": round(info["e2e_steps"] * total / (ms_e2e * 1e-3) / 1e9, 2), "unit": "GB/s",
                 "h2d_bytes_per_step": info["h2d_bytes_per_step"], "d2h_bytes_per_step": info["d2h_bytes_per_step"],
@@ -727,7 +727,7 @@ def run_model(args):
         "data": "synthetic (random-init weights quantized on device, random token ids)",
         "config": {"workload": spec["desc"], "prompt_tokens": spec["prompt"], "kv_cells_during_timing": list(r["n_kv"]),
                    "l2": "inputs larger than L2 (every decode token reads all weights: "
-                         f"{r['algo_bytes'] / 1e6:.0f} MB)", "cuda_graph": False,
+                         f"{r['algo_bytes'] / 1e6:.0f} MB)", "cuda_graph": "one graph launch per token (tsrc_model_decode)",
                    "prefill_ms": round(r["prefill_ms"], 2),
                    "prefill_tokens_per_s": round(spec["prompt"] / (r["prefill_ms"] * 1e-3), 1)},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4),

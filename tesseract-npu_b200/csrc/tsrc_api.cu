@@ -939,8 +939,8 @@ int fa_setup(tsrc_ctx* ctx, const tsrc_kv* kv, const float* q, uint32_t T, uint3
     const uint32_t rows_max = po.Tq0 * po.G;
     const size_t b_items = align256((size_t)n_items * sizeof(tsrc::FaItem));
     const size_t b_tiles = align256((size_t)(po.n_tiles + 1u) * 4u);
-    const size_t b_oc = align256((size_t)n_items * kv->n_head_kv * rows_max * kv->D * 4u);
-    const size_t b_lc = align256((size_t)n_items * kv->n_head_kv * rows_max * 4u);
+    const size_t b_oc = align256((size_t)n_items * kv->n_head_kv * c.C * rows_max * kv->D * 4u);
+    const size_t b_lc = align256((size_t)n_items * kv->n_head_kv * c.C * rows_max * 4u);
     const size_t b_mk = align256((size_t)n_items * kv->n_head_kv * rows_max * 4u);
     const size_t b_m16 = po.general ? align256((size_t)T * mask_stride * 2u) : 0u;
     const size_t b_mf = po.general ? align256((size_t)T * n_kv * 4u) : 0u;

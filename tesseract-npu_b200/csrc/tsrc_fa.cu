@@ -9,15 +9,19 @@
 // the reference's rules (tsrc_numerics.cuh); every sum that the reference makes exact is an
 // integer sum here too, so the result does not depend on how the work is spread over threads.
 //
-// Work split (one launch of fa_chunk_kernel + one of fa_merge_kernel):
+// Work split (one launch of fa_chunk_kernel, then one of fa_merge_kernel; both are programmatic
+// dependent launches: each starts its prologue while the kernel before it finishes):
 //   - a thread-block cluster per (work item = query tile x chunk, KV head g), one CTA per channel
-//     (cluster rank = channel); the CTA prefetches its groups' K and V bytes into L2 on entry;
+//     (cluster rank = channel); the CTA prefetches its groups' K and V bytes into L2 on entry,
+//     before it waits for the kernel it depends on;
 //   - a CTA computes the scores of its channel's cells for RB rows (query heads of g x tokens of
 //     the tile) at a time, the cluster exchanges the per-channel row maxima through distributed
 //     shared memory (the chunk max is a max over all channels), then the CTA applies EXP and runs
-//     the channel's segments, one warp per segment, folding the segment results in order;
-//   - fa_merge_kernel reduces the C channel partials (CTREE), merges the chunks of a tile in
-//     execution order (AMERGE) and normalises (ANORM), one thread per output value.
+//     the channel's segments, one warp per (segment, 64-value slice), folding the segment
+//     results in order, and writes its channel result and row sums to global scratch;
+//   - fa_merge_kernel<C> reduces the C channel results of every chunk (CTREE), merges the
+//     chunks of a tile in execution order (AMERGE) and normalises (ANORM), one thread per output
+//     value, over the whole GPU.
 #include <cooperative_groups.h>
 
 #include "tsrc_internal.h"
@@ -134,7 +138,7 @@ __host__ __device__ inline uint32_t fa_segs(uint32_t D) { return kFaWarps / (D /
 __host__ __device__ inline uint32_t fa_wd_rows(uint32_t D) { return 4u * (512u / D); }
 
 __host__ __device__ inline FaSmem fa_smem(uint32_t D, uint32_t ncell_max) {
-    const uint32_t RB = 512u / D, ND = D / 32u, NSL = D / 64u;
+    const uint32_t RB = 512u / D, ND = D / 32u;
     FaSmem s{};
     uint32_t o = fa_a16(64u * 4u + 4u * 8u);                    // EXPK tables
     s.qx_off = o;
@@ -146,7 +150,7 @@ __host__ __device__ inline FaSmem fa_smem(uint32_t D, uint32_t ncell_max) {
     s.w_off = o;
     o += fa_a16(kFaWarps * 2u * fa_wd_rows(D) * kWdStride);     // W digits [warp][2][rows][kWdStride] (its slice)
     s.cv_off = o;
-    o += fa_a16(fa_segs(D) * RB * D * 4u);                      // CV [segment of the round][RB][D]; then the channel's O [RB][D]
+    o += fa_a16(fa_segs(D) * RB * D * 4u);                      // CV [segment of the round][RB][D]
     s.vq_off = o;
     o += fa_a16(kFaWarps * 64u * fa_vp(D));                     // V quants of a segment [warp][4 groups][VP][16]
     s.vs_off = o;
@@ -165,20 +169,10 @@ __device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src)
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
 
-// CTREE (tsr_ref_at.c:588-598) of n <= 16 values: pairwise by levels, an unpaired last element
-// passes through. Fully unrolled (static indices, values stay in registers).
-__device__ __forceinline__ float ctree16(float (&v)[16], uint32_t n) {
-#pragma unroll
-    for (int lvl = 0; lvl < 4; ++lvl) {
-#pragma unroll
-        for (uint32_t k = 0; k < 8; ++k) {
-            if (2u * k + 1u < n) v[k] = fadd(v[2 * k], v[2 * k + 1]);
-            else if (2u * k + 1u == n) v[k] = v[2 * k];
-        }
-        n = (n + 1u) / 2u;
-    }
-    return v[0];
-}
+// The cluster barrier in two halves: arrive once this CTA is done reading its peers' shared
+// memory, wait before it exits (a peer's shared memory must outlive every remote read of it).
+__device__ __forceinline__ void cluster_arrive() { asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory"); }
+__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
 
 // ---------------------------------------------------------------------------------------------------
 template <int D>
@@ -235,6 +229,10 @@ __global__ void __launch_bounds__(kFaThreads, 1) fa_chunk_kernel(FaLaunch a) {
     uint32_t* flw = reinterpret_cast<uint32_t*>(esw + kFaWarps * RB);
     if (tid < 64) t64s[tid] = g_expk_t64[tid];
     if (tid < 4) lks[tid] = g_expk_lk[tid];
+    // the next kernel may start its own prologue; q, the KV cache and the mask copy are read only
+    // after the kernel this one depends on has finished
+    asm volatile("griddepcontrol.launch_dependents;");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
 
     const uint32_t nseg = (nu + 3u) / 4u;
     const float scale = a.scale;
@@ -261,10 +259,12 @@ __global__ void __launch_bounds__(kFaThreads, 1) fa_chunk_kernel(FaLaunch a) {
         cp_async_commit();
     };
 
+    float* ok_ch = a.ok + (((size_t)item * a.n_head_kv + g) * C + cc) * rows_max * D;
+    float* lk_ch = a.lk + (((size_t)item * a.n_head_kv + g) * C + cc) * rows_max;
+    bool arrived = false;
     uint32_t pass = 0;
     for (uint32_t r0 = 0; r0 < rows; r0 += RB, ++pass) {
         const uint32_t nr = min(RB, rows - r0);
-        if (wseg < nseg) stage_v(wseg, wsl, true);               // round 0's V, in flight during ATTQK
         // ---- QACT A32 of the pass's query rows (tsr_ref.c:472-487): one warp per 32-block ----
         constexpr uint32_t kQB = (RB * ND + kFaWarps - 1u) / kFaWarps;     // blocks per warp
         float qv[kQB];
@@ -366,6 +366,9 @@ __global__ void __launch_bounds__(kFaThreads, 1) fa_chunk_kernel(FaLaunch a) {
                 rmax[r] = maxt(rmax[r], s);
             }
         }
+        // round 0's V slices, in flight during the maximum and EXP (issued after ATTQK, whose K
+        // loads they would otherwise compete with); one round holds every segment: staged once
+        if (wseg < nseg && (pass == 0 || nseg > SEGS)) stage_v(wseg, wsl, true);
 #pragma unroll
         for (uint32_t r = 0; r < RB; ++r) {
             const float m = warp_maxt(rmax[r]);
@@ -379,12 +382,23 @@ __global__ void __launch_bounds__(kFaThreads, 1) fa_chunk_kernel(FaLaunch a) {
             slot[tid] = m;
         }
         // ---- the chunk maximum: MAXOUT over every channel of the chunk ----
-        cluster.sync();
+        // (the slots alternate between passes: a peer writes this pass's slot again only after the
+        // next pass's barrier, which every CTA reaches after its reads of this one)
+        cluster_arrive();
+        cluster_wait();
         if (tid < RB) {
+            float mv[16];                    // every channel's max in flight at once
+#pragma unroll
+            for (uint32_t c = 0; c < 16; ++c) mv[c] = c < C ? *cluster.map_shared_rank(slot + tid, c) : ffrom(kMFloor);
             float m = ffrom(kMFloor);
-            for (uint32_t c = 0; c < C; ++c) m = maxt(m, *cluster.map_shared_rank(slot + tid, c));
+#pragma unroll
+            for (uint32_t c = 0; c < 16; ++c) m = maxt(m, mv[c]);
             mk[tid] = m;
             if (cc == 0 && tid < nr) a.mk[((size_t)item * a.n_head_kv + g) * rows_max + r0 + tid] = m;
+        }
+        if (r0 + RB >= rows) {               // the last pass: no more remote reads
+            cluster_arrive();
+            arrived = true;
         }
         __syncthreads();
         // ---- ASMAX: p = EXP(fmul(fsub(s, m), scale)) ----
@@ -564,31 +578,42 @@ __global__ void __launch_bounds__(kFaThreads, 1) fa_chunk_kernel(FaLaunch a) {
             }
             __syncthreads();
         }
-        // ---- CTREE over the cluster's channels; CTA cc writes every C-th (row, value) ----
+        // ---- the channel's result and row sums of the pass's rows ----
 #pragma unroll
-        for (uint32_t i = 0; i < kPer; ++i) CV[tid + i * kFaThreads] = oacc[i];
-        cluster.sync();
-        float* ok_base = a.ok + ((size_t)item * a.n_head_kv + g) * rows_max * D + (size_t)r0 * D;
-        for (uint32_t pidx = cc * kFaThreads + tid; pidx < nr * D; pidx += C * kFaThreads) {
-            float xv[16];
-#pragma unroll
-            for (uint32_t c = 0; c < 16; ++c) xv[c] = c < C ? *cluster.map_shared_rank(CV + pidx, c) : 0.0f;
-            ok_base[pidx] = ctree16(xv, C);
+        for (uint32_t i = 0; i < kPer; ++i) {
+            const uint32_t pidx = tid + i * kFaThreads;
+            if (pidx < nr * D) ok_ch[(size_t)r0 * D + pidx] = oacc[i];
         }
-        if (tid < nr && tid % C == cc) {
-            float xv[16];
-#pragma unroll
-            for (uint32_t c = 0; c < 16; ++c) xv[c] = c < C ? *cluster.map_shared_rank(lacc + tid, c) : 0.0f;
-            a.lk[((size_t)item * a.n_head_kv + g) * rows_max + r0 + tid] = ctree16(xv, C);
-        }
-        // no CTA may overwrite (next pass) or release (exit) what another still reads
-        cluster.sync();
+        if (tid < nr) lk_ch[r0 + tid] = lacc[tid];
     }
+    if (!arrived) cluster_arrive();
+    cluster_wait();
 }
 
-// AMERGE over the chunks of each tile in execution order, then ANORM (tsr_ref_at.c:600-641).
-// One thread per output value; the chunk values of 4 items are loaded before they are folded.
+// CTREE (tsr_ref_at.c:588-598) of N values: pairwise by levels, an unpaired last element passes
+// through.
+template <uint32_t N>
+__device__ __forceinline__ float ctree(float (&v)[N]) {
+    uint32_t n = N;
+#pragma unroll
+    for (uint32_t lvl = 0; lvl < 5; ++lvl) {
+        if (n <= 1u) break;
+#pragma unroll
+        for (uint32_t k = 0; k < (N + 1u) / 2u; ++k) {
+            if (2u * k + 1u < n) v[k] = fadd(v[2u * k], v[2u * k + 1u]);
+            else if (2u * k + 1u == n) v[k] = v[2u * k];
+        }
+        n = (n + 1u) / 2u;
+    }
+    return v[0];
+}
+
+// CTREE of the C channel results of each chunk, AMERGE over the chunks of each tile in execution
+// order, then ANORM (tsr_ref_at.c:588-641). One thread per output value; the values of two chunks
+// are loaded before they are folded.
+template <uint32_t C>
 __global__ void __launch_bounds__(256) fa_merge_kernel(FaLaunch a) {
+    asm volatile("griddepcontrol.launch_dependents;");
     const uint32_t G = a.G, D = a.D, rows_max = a.Tq0 * G;
     const size_t per_tile = (size_t)a.n_head_kv * rows_max * D;
     const size_t idx = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -603,33 +628,38 @@ __global__ void __launch_bounds__(256) fa_merge_kernel(FaLaunch a) {
     const FaItem first = inl ? a.inl_items[i0] : a.items[i0];
     if (ri >= first.Tq * G) return;
     const float scale = a.scale;
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     float O = 0.0f, lrun = 0.0f, mrun = 0.0f;
-    constexpr uint32_t kB = 4;
+    constexpr uint32_t kB = 2;
     for (uint32_t k0 = i0; k0 < i1; k0 += kB) {
-        float ok[kB], lk[kB], mkk[kB];
+        float ok[kB][C], lk[kB][C], mkk[kB];
 #pragma unroll
         for (uint32_t j = 0; j < kB; ++j) {
             if (k0 + j < i1) {
-                const size_t base = (size_t)(k0 + j) * a.n_head_kv + g;
-                ok[j] = a.ok[(base * rows_max + ri) * D + v];
-                lk[j] = a.lk[base * rows_max + ri];
-                mkk[j] = a.mk[base * rows_max + ri];
+                const size_t hb = (size_t)(k0 + j) * a.n_head_kv + g;
+#pragma unroll
+                for (uint32_t c = 0; c < C; ++c) {
+                    ok[j][c] = a.ok[((hb * C + c) * rows_max + ri) * D + v];
+                    lk[j][c] = a.lk[(hb * C + c) * rows_max + ri];
+                }
+                mkk[j] = a.mk[hb * rows_max + ri];
             }
         }
 #pragma unroll
         for (uint32_t j = 0; j < kB; ++j) {
             if (k0 + j >= i1) break;
+            const float oj = ctree<C>(ok[j]), lj = ctree<C>(lk[j]);
             if (k0 + j == i0) {
-                O = ok[j];
-                lrun = lk[j];
+                O = oj;
+                lrun = lj;
                 mrun = mkk[j];
             } else {
                 const float mn = maxt(mrun, mkk[j]);
                 const float ea = expk(fmul(fsub(mrun, mn), scale), 0u, g_expk_t64, g_expk_lk);
                 const float eb = expk(fmul(fsub(mkk[j], mn), scale), 0u, g_expk_t64, g_expk_lk);
-                lrun = fadd(fmul(lrun, ea), fmul(lk[j], eb));
+                lrun = fadd(fmul(lrun, ea), fmul(lj, eb));
                 mrun = mn;
-                O = fadd(fmul(O, ea), fmul(ok[j], eb));
+                O = fadd(fmul(O, ea), fmul(oj, eb));
             }
         }
     }
@@ -637,6 +667,12 @@ __global__ void __launch_bounds__(256) fa_merge_kernel(FaLaunch a) {
     const uint32_t t = ri / G, h = g * G + (ri - t * G);
     a.out[((size_t)(first.q0 + t) * a.n_head + h) * D + v] = canon(fmul(O, rinv));
 }
+
+using MergeFn = void (*)(FaLaunch);
+constexpr MergeFn kMerge[16] = {fa_merge_kernel<1>,  fa_merge_kernel<2>,  fa_merge_kernel<3>,  fa_merge_kernel<4>,
+                                fa_merge_kernel<5>,  fa_merge_kernel<6>,  fa_merge_kernel<7>,  fa_merge_kernel<8>,
+                                fa_merge_kernel<9>,  fa_merge_kernel<10>, fa_merge_kernel<11>, fa_merge_kernel<12>,
+                                fa_merge_kernel<13>, fa_merge_kernel<14>, fa_merge_kernel<15>, fa_merge_kernel<16>};
 
 // f32 mask copy of the GENERAL path (tsr_ref_at.c:694-715): fdiv(f32(mask), scale), -inf kept.
 __global__ void fa_maskf_kernel(const uint16_t* m16, uint32_t stride, uint32_t T, uint32_t n_kv, float scale, float* out) {
@@ -672,13 +708,15 @@ cudaError_t launch_chunks(const FaLaunch& a, uint32_t ncell_max, cudaStream_t st
     cfg.blockDim = dim3(kFaThreads);
     cfg.dynamicSmemBytes = P.total;
     cfg.stream = st;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = a.C;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = 2;
     if (a.C > 8) {        // a non-portable cluster size: make sure one cluster can be resident
         int n = 0;
         e = cudaOccupancyMaxActiveClusters(&n, (const void*)fa_chunk_kernel<D>, &cfg);
@@ -702,6 +740,8 @@ cudaError_t launch_fa_maskf(const uint16_t* m16, uint32_t stride, uint32_t T, ui
     return cudaGetLastError();
 }
 
+const void* fa_merge_fn(uint32_t C) { return C >= 1u && C <= 16u ? reinterpret_cast<const void*>(kMerge[C - 1u]) : nullptr; }
+
 const void* fa_chunk_fn(uint32_t D) {
     switch (D) {
         case 64: return reinterpret_cast<const void*>(fa_chunk_kernel<64>);
@@ -711,7 +751,6 @@ const void* fa_chunk_fn(uint32_t D) {
         default: return nullptr;
     }
 }
-const void* fa_merge_fn() { return reinterpret_cast<const void*>(fa_merge_kernel); }
 
 cudaError_t launch_fa(const FaLaunch& a, uint32_t n_max_groups, cudaStream_t st) {
     const uint32_t ncell_max = 16u * ((n_max_groups + a.C - 1u) / a.C);
@@ -724,9 +763,18 @@ cudaError_t launch_fa(const FaLaunch& a, uint32_t n_max_groups, cudaStream_t st)
         default: return cudaErrorInvalidValue;
     }
     if (e != cudaSuccess) return e;
+    if (a.C < 1u || a.C > 16u) return cudaErrorInvalidValue;
     const size_t n = (size_t)a.n_tiles * a.n_head_kv * a.Tq0 * a.G * a.D;
-    fa_merge_kernel<<<(unsigned)((n + 255u) / 256u), 256, 0, st>>>(a);
-    return cudaGetLastError();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)((n + 255u) / 256u));
+    cfg.blockDim = dim3(256);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kMerge[a.C - 1u], a);
 }
 
 }  // namespace tsrc

@@ -148,9 +148,9 @@ struct FaLaunch {
     uint32_t n_items;
     const uint32_t* tile_items; // [n_tiles + 1]: items of tile i are [tile_items[i], tile_items[i + 1])
     uint32_t n_tiles, Tq0;
-    float* ok;                  // chunk results (channel tree done) [n_items][n_head_kv][Tq0 G][D]
-    float* lk;                  // chunk row sums                    [n_items][n_head_kv][Tq0 G]
-    float* mk;                  // chunk maxima                      [n_items][n_head_kv][Tq0 G]
+    float* ok;                  // channel results  [n_items][n_head_kv][C][Tq0 G][D]
+    float* lk;                  // channel row sums [n_items][n_head_kv][C][Tq0 G]
+    float* mk;                  // chunk maxima     [n_items][n_head_kv][Tq0 G]
     float* out;                 // [T][n_head][D] f32
     // small plans: the items and tile offsets themselves (no host -> device copy, so a call can be
     // captured in a CUDA graph); used when n_items <= kFaInlineItems
@@ -161,7 +161,7 @@ struct FaLaunch {
 cudaError_t launch_fa(const FaLaunch& a, uint32_t n_max_groups, cudaStream_t st);
 // the kernels launch_fa runs (to find their nodes in a captured CUDA graph)
 const void* fa_chunk_fn(uint32_t D);
-const void* fa_merge_fn();
+const void* fa_merge_fn(uint32_t C);
 // tsrc_flash_attn up to the kernel launches (tsrc_api.cu)
 int fa_setup(::tsrc_ctx* ctx, const ::tsrc_kv* kv, const float* q, uint32_t T, uint32_t n_head, uint32_t n_kv,
              const uint16_t* mask, uint32_t mask_stride, float scale, uint32_t new_lo, uint32_t new_hi,

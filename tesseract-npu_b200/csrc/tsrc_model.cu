@@ -489,7 +489,7 @@ int capture_decode(tsrc_model* m, const int32_t* ids, uint32_t pos0, float* logi
     std::vector<cudaGraphNode_t> nodes(n);
     cudaGraphGetNodes(g, nodes.data(), &n);
     const void* fchunk = tsrc::fa_chunk_fn(m->c.head_dim);
-    const void* fmerge = tsrc::fa_merge_fn();
+    const void* fmerge = tsrc::fa_merge_fn(a0.C);
     const void* fstate = reinterpret_cast<const void*>(model_state_kernel);
     for (cudaGraphNode_t nd : nodes) {
         cudaGraphNodeType t;
