@@ -411,154 +411,159 @@ __global__ void __launch_bounds__(kFaThreads, 1) fa_chunk_kernel(FaLaunch a) {
         if (tid < RB) lacc[tid] = 0.0f;
         __syncthreads();
 
-        // ---- ATTPV + LSUM: one warp per 64-cell segment, results folded in segment order ----
+        // ---- ATTPV + LSUM, results folded in segment order ----
+        // A round holds up to SEGS segments; warp (wseg, wsl) stages the V quants of slice wsl of
+        // the round's segment wseg (and the segment's scales). Then every warp takes work units
+        // of the round in turn: first (segment, slice, row) -- the W digits of the row and, for
+        // slice 0, its LSUM -- then (segment, slice, 16-value tile) -- the tensor-core products
+        // of the tile for every row.
         constexpr uint32_t kPer = RB * D / kFaThreads;        // (row, value) pairs folded per thread
+        constexpr uint32_t kMt = VP / 16u;                    // 16-value tiles of a slice
         float oacc[kPer];
 #pragma unroll
         for (uint32_t i = 0; i < kPer; ++i) oacc[i] = 0.0f;
         for (uint32_t sg0 = 0; sg0 < nseg; sg0 += SEGS) {
-            const uint32_t sg = sg0 + wseg;
-            if (sg < nseg) {
-                const uint32_t ng = min(4u, nu - 4u * sg), nc = 16u * ng;
-                uint8_t* Wd = Wbase + warp * kWdWarp;
-                if (sg0 > 0) stage_v(sg, wsl, true);
-                cp_async_wait_all();
-                __syncwarp();
-                // rows one at a time (their state lives in shared memory): a quarter of the code of
-                // the unrolled form for the same work (the kernel's second stall is instruction fetch)
+            const uint32_t nsr = min(SEGS, nseg - sg0);        // segments of this round
+            if (sg0 > 0 && wseg < nsr) stage_v(sg0 + wseg, wsl, true);
+            cp_async_wait_all();
+            __syncthreads();
+            // W digits (+ LSUM) of unit (segment s, slice sl, row r)
 #pragma unroll 1
-                for (uint32_t r = 0; r < RB; ++r) {
-                    if (r >= nr) break;
-                    {
-                        const uint32_t sl = wsl;
-                        // w = p (*) dV of the lane's two cells and the slice's two blocks
-                        float w[2][2];
-                        int32_t le = -1000;
-                        bool bad0 = false, bad1 = false, any = false;
+            for (uint32_t u = warp; u < nsr * NSL * nr; u += kFaWarps) {
+                const uint32_t r = u % nr, ss = u / nr, sl = ss % NSL, s = ss / NSL, sg = sg0 + s;
+                const uint32_t owner = s * NSL + sl;           // the warp that staged (s, sl)
+                const uint16_t* vsso = reinterpret_cast<const uint16_t*>(smem + P.vs_off) + owner * 64u * ND;
+                uint8_t* Wd = Wbase + owner * kWdWarp;
+                const uint32_t ng = min(4u, nu - 4u * sg), nc = 16u * ng;
+                {
+                    // w = p (*) dV of the lane's two cells and the slice's two blocks
+                    float w[2][2];
+                    int32_t le = -1000;
+                    bool bad0 = false, bad1 = false, any = false;
 #pragma unroll
-                        for (uint32_t h = 0; h < 2; ++h) {
-                            const uint32_t i = lane + 32u * h;
-                            const float p = i < nc ? S[r * ncell_max + 64u * sg + i] : 0.0f;
-                            const bool pz = (fbits(p) & kExp) == 0;
-                            const uint32_t pr = i < nc ? *reinterpret_cast<const uint32_t*>(vss + i * ND + 2u * sl) : 0u;
+                    for (uint32_t h = 0; h < 2; ++h) {
+                        const uint32_t i = lane + 32u * h;
+                        const float p = i < nc ? S[r * ncell_max + 64u * sg + i] : 0.0f;
+                        const bool pz = (fbits(p) & kExp) == 0;
+                        const uint32_t pr = i < nc ? *reinterpret_cast<const uint32_t*>(vsso + i * ND + 2u * sl) : 0u;
 #pragma unroll
-                            for (uint32_t e = 0; e < 2; ++e) {
-                                const float wv = pz ? 0.0f : fmul(p, h2f((uint16_t)(e ? pr >> 16 : pr & 0xFFFFu)));
-                                w[h][e] = wv;
-                                const uint32_t u = fbits(wv);
-                                if (nonfinite(u)) {
-                                    if (e == 0) bad0 = true;
-                                    else bad1 = true;
-                                } else if (u & ~kSign) {
-                                    le = max(le, (int32_t)((u >> 23) & 0xFFu) - 127);
-                                    any = true;
-                                }
-                            }
-                        }
-                        const int32_t es = (int32_t)__reduce_max_sync(0xFFFFFFFFu, (uint32_t)(le + 1000)) - 1000;
-                        const uint32_t fl3 = __reduce_or_sync(0xFFFFFFFFu, (bad0 ? 1u : 0u) | (bad1 ? 2u : 0u) | (any ? 4u : 0u));
-                        bad0 = (fl3 & 1u) != 0;
-                        bad1 = (fl3 & 2u) != 0;
-                        any = (fl3 & 4u) != 0;
-                        // W = RNE_int(w 2^(23 - es)) (|W| <= 2^24) as four balanced base-256 digits,
-                        // the B operand of the int8 tensor-core products: table (sl, e), row r*4 + digit
-#pragma unroll
-                        for (uint32_t h = 0; h < 2; ++h)
-#pragma unroll
-                            for (uint32_t e = 0; e < 2; ++e) {
-                                const int32_t Wv = (any && !(e ? bad1 : bad0)) ? bf_int(w[h][e], es) : 0;
-                                const uint32_t dg = digits4(Wv);
-                                uint8_t* col = Wd + (e * kWdRows + r * 4u) * kWdStride + lane + 32u * h;
-                                col[0] = (uint8_t)dg;
-                                col[kWdStride] = (uint8_t)(dg >> 8);
-                                col[2u * kWdStride] = (uint8_t)(dg >> 16);
-                                col[3u * kWdStride] = (uint8_t)(dg >> 24);
-                            }
-                        if (lane == 0) {
-                            esw[warp * RB + r] = es;
-                            flw[warp * RB + r] = (bad0 ? 1u : 0u) | (bad1 ? 2u : 0u) | (any ? 4u : 0u);
-                        }
-                    }
-                    // LSUM of the segment (tsr_ref_at.c:520-553), by the segment's slice-0 warp
-                    if (wsl == 0) {
-                        int32_t le = -1000;
-                        bool bad = false, any = false;
-                        float pv[2];
-#pragma unroll
-                        for (uint32_t h = 0; h < 2; ++h) {
-                            const uint32_t i = lane + 32u * h;
-                            pv[h] = i < nc ? daz(S[r * ncell_max + 64u * sg + i]) : 0.0f;
-                            const uint32_t u = fbits(pv[h]);
-                            if (nonfinite(u)) bad = true;
-                            else if (u & ~kSign) {
-                                le = max(le, (int32_t)((u >> 23) & 0xFFu) - 127);
+                        for (uint32_t e = 0; e < 2; ++e) {
+                            const float wv = pz ? 0.0f : fmul(p, h2f((uint16_t)(e ? pr >> 16 : pr & 0xFFFFu)));
+                            w[h][e] = wv;
+                            const uint32_t uu = fbits(wv);
+                            if (nonfinite(uu)) {
+                                if (e == 0) bad0 = true;
+                                else bad1 = true;
+                            } else if (uu & ~kSign) {
+                                le = max(le, (int32_t)((uu >> 23) & 0xFFu) - 127);
                                 any = true;
                             }
                         }
-                        const int32_t ep = (int32_t)__reduce_max_sync(0xFFFFFFFFu, (uint32_t)(le + 1000)) - 1000;
-                        const uint32_t fl2 = __reduce_or_sync(0xFFFFFFFFu, (bad ? 1u : 0u) | (any ? 2u : 0u));
-                        bad = (fl2 & 1u) != 0;
-                        any = (fl2 & 2u) != 0;
-                        int32_t part = 0;
-                        if (!bad && any) part = bf_int(pv[0], ep) + bf_int(pv[1], ep);
-                        const int32_t sum = __reduce_add_sync(0xFFFFFFFFu, part);
-                        if (lane == 0)
-                            ls[wseg * RB + r] = bad ? ffrom(kCanonNaN) : !any ? 0.0f : bf_f((int64_t)sum, ep - 23);
+                    }
+                    const int32_t es = (int32_t)__reduce_max_sync(0xFFFFFFFFu, (uint32_t)(le + 1000)) - 1000;
+                    const uint32_t fl3 = __reduce_or_sync(0xFFFFFFFFu, (bad0 ? 1u : 0u) | (bad1 ? 2u : 0u) | (any ? 4u : 0u));
+                    bad0 = (fl3 & 1u) != 0;
+                    bad1 = (fl3 & 2u) != 0;
+                    any = (fl3 & 4u) != 0;
+                    // W = RNE_int(w 2^(23 - es)) (|W| <= 2^24) as four balanced base-256 digits,
+                    // the B operand of the int8 tensor-core products: table (owner, e), row r*4 + digit
+#pragma unroll
+                    for (uint32_t h = 0; h < 2; ++h)
+#pragma unroll
+                        for (uint32_t e = 0; e < 2; ++e) {
+                            const int32_t Wv = (any && !(e ? bad1 : bad0)) ? bf_int(w[h][e], es) : 0;
+                            const uint32_t dg = digits4(Wv);
+                            uint8_t* col = Wd + (e * kWdRows + r * 4u) * kWdStride + lane + 32u * h;
+                            col[0] = (uint8_t)dg;
+                            col[kWdStride] = (uint8_t)(dg >> 8);
+                            col[2u * kWdStride] = (uint8_t)(dg >> 16);
+                            col[3u * kWdStride] = (uint8_t)(dg >> 24);
+                        }
+                    if (lane == 0) {
+                        esw[owner * RB + r] = es;
+                        flw[owner * RB + r] = (bad0 ? 1u : 0u) | (bad1 ? 2u : 0u) | (any ? 4u : 0u);
                     }
                 }
-                __syncwarp();
-                // exact sums A[r][v] = sum_cells W * qV on the int8 tensor cores (m16n8k32): A operand
-                // = V^T (16 values x 32 cells, from the value-major groups), B operand = the W digits
-                // (32 cells x 8 = 2 rows x 4 digits); digit sums are exact in int32 (|.| <= 2^20)
-                const uint32_t gid = lane >> 2, tig = lane & 3u;
-                const uint32_t nks = (ng + 1u) / 2u;
-                float* cvw = CV + wseg * RB * D;
-                {
-#pragma unroll 2
-                    for (uint32_t mt = 0; mt < VP / 16u; ++mt) {
-                        const uint32_t v0 = wsl * VP + 16u * mt, e = (16u * mt) / 32u;
-                        const uint8_t* Wt_se = Wd + e * kWdRows * kWdStride;
-                        int32_t acc[kNT][4];
+                // LSUM of the segment (tsr_ref_at.c:520-553), with slice 0's unit
+                if (sl == 0) {
+                    int32_t le = -1000;
+                    bool bad = false, any = false;
+                    float pv[2];
 #pragma unroll
-                        for (uint32_t nt = 0; nt < kNT; ++nt)
-#pragma unroll
-                            for (uint32_t j = 0; j < 4; ++j) acc[nt][j] = 0;
-                        for (uint32_t ks = 0; ks < nks; ++ks) {
-                            const uint8_t* va = reinterpret_cast<const uint8_t*>(vqs) + ((2u * ks) * VP + 16u * mt + gid) * 16u + tig * 4u;
-                            const uint32_t a0 = *reinterpret_cast<const uint32_t*>(va);
-                            const uint32_t a1 = *reinterpret_cast<const uint32_t*>(va + 8u * 16u);
-                            const uint32_t a2 = *reinterpret_cast<const uint32_t*>(va + VP * 16u);
-                            const uint32_t a3 = *reinterpret_cast<const uint32_t*>(va + VP * 16u + 8u * 16u);
-#pragma unroll
-                            for (uint32_t nt = 0; nt < kNT; ++nt) {
-                                const uint8_t* wb = Wt_se + ((nt * 8u + gid) % kWdRows) * kWdStride + 32u * ks + tig * 4u;
-                                const uint32_t b0 = *reinterpret_cast<const uint32_t*>(wb);
-                                const uint32_t b1 = *reinterpret_cast<const uint32_t*>(wb + 16u);
-                                asm volatile(
-                                    "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-                                    "{%0,%1,%2,%3};"
-                                    : "+r"(acc[nt][0]), "+r"(acc[nt][1]), "+r"(acc[nt][2]), "+r"(acc[nt][3])
-                                    : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-                            }
+                    for (uint32_t h = 0; h < 2; ++h) {
+                        const uint32_t i = lane + 32u * h;
+                        pv[h] = i < nc ? daz(S[r * ncell_max + 64u * sg + i]) : 0.0f;
+                        const uint32_t uu = fbits(pv[h]);
+                        if (nonfinite(uu)) bad = true;
+                        else if (uu & ~kSign) {
+                            le = max(le, (int32_t)((uu >> 23) & 0xFFu) - 127);
+                            any = true;
                         }
-                        // digits 0,1 sit in even lanes (tig even), 2,3 in the odd neighbour: even lanes
-                        // finish value gid, odd lanes value gid + 8
-                        const bool odd = (tig & 1u) != 0;
+                    }
+                    const int32_t ep = (int32_t)__reduce_max_sync(0xFFFFFFFFu, (uint32_t)(le + 1000)) - 1000;
+                    const uint32_t fl2 = __reduce_or_sync(0xFFFFFFFFu, (bad ? 1u : 0u) | (any ? 2u : 0u));
+                    bad = (fl2 & 1u) != 0;
+                    any = (fl2 & 2u) != 0;
+                    int32_t part = 0;
+                    if (!bad && any) part = bf_int(pv[0], ep) + bf_int(pv[1], ep);
+                    const int32_t sum = __reduce_add_sync(0xFFFFFFFFu, part);
+                    if (lane == 0) ls[s * RB + r] = bad ? ffrom(kCanonNaN) : !any ? 0.0f : bf_f((int64_t)sum, ep - 23);
+                }
+            }
+            __syncthreads();
+            // exact sums A[r][v] = sum_cells W * qV on the int8 tensor cores (m16n8k32): A operand
+            // = V^T (16 values x 32 cells, from the value-major groups), B operand = the W digits
+            // (32 cells x 8 = 2 rows x 4 digits); digit sums are exact in int32 (|.| <= 2^20)
+            const uint32_t gid = lane >> 2, tig = lane & 3u;
+#pragma unroll 1
+            for (uint32_t u = warp; u < nsr * NSL * kMt; u += kFaWarps) {
+                const uint32_t mt = u % kMt, ss = u / kMt, sl = ss % NSL, s = ss / NSL, sg = sg0 + s;
+                const uint32_t owner = s * NSL + sl;
+                const int8_t* vqo = reinterpret_cast<const int8_t*>(smem + P.vq_off) + owner * 64u * VP;
+                const uint8_t* Wd = Wbase + owner * kWdWarp;
+                const uint32_t ng = min(4u, nu - 4u * sg), nks = (ng + 1u) / 2u;
+                float* cvw = CV + s * RB * D;
+                const uint32_t v0 = sl * VP + 16u * mt, e = (16u * mt) / 32u;
+                const uint8_t* Wt_se = Wd + e * kWdRows * kWdStride;
+                int32_t acc[kNT][4];
 #pragma unroll
-                        for (uint32_t nt = 0; nt < kNT; ++nt) {
-                            const int32_t s0 = odd ? acc[nt][0] : acc[nt][2], s1 = odd ? acc[nt][1] : acc[nt][3];
-                            const int32_t o0 = __shfl_xor_sync(0xFFFFFFFFu, s0, 1), o1 = __shfl_xor_sync(0xFFFFFFFFu, s1, 1);
-                            int64_t Av;
-                            if (!odd) Av = (int64_t)acc[nt][0] + ((int64_t)acc[nt][1] << 8) + ((int64_t)o0 << 16) + ((int64_t)o1 << 24);
-                            else Av = (int64_t)o0 + ((int64_t)o1 << 8) + ((int64_t)acc[nt][2] << 16) + ((int64_t)acc[nt][3] << 24);
-                            const uint32_t r = nt * 2u + (tig >> 1), v = v0 + gid + (odd ? 8u : 0u);
-                            if (r < nr) {
-                                const int32_t es = esw[warp * RB + r];
-                                const uint32_t fl = flw[warp * RB + r];
-                                const bool bad = (fl >> e) & 1u, any = (fl & 4u) != 0;
-                                cvw[r * D + v] = bad ? ffrom(kCanonNaN) : !any ? 0.0f : bf_f(Av, es - 23);
-                            }
-                        }
+                for (uint32_t nt = 0; nt < kNT; ++nt)
+#pragma unroll
+                    for (uint32_t j = 0; j < 4; ++j) acc[nt][j] = 0;
+                for (uint32_t ks = 0; ks < nks; ++ks) {
+                    const uint8_t* va = reinterpret_cast<const uint8_t*>(vqo) + ((2u * ks) * VP + 16u * mt + gid) * 16u + tig * 4u;
+                    const uint32_t a0 = *reinterpret_cast<const uint32_t*>(va);
+                    const uint32_t a1 = *reinterpret_cast<const uint32_t*>(va + 8u * 16u);
+                    const uint32_t a2 = *reinterpret_cast<const uint32_t*>(va + VP * 16u);
+                    const uint32_t a3 = *reinterpret_cast<const uint32_t*>(va + VP * 16u + 8u * 16u);
+#pragma unroll
+                    for (uint32_t nt = 0; nt < kNT; ++nt) {
+                        const uint8_t* wb = Wt_se + ((nt * 8u + gid) % kWdRows) * kWdStride + 32u * ks + tig * 4u;
+                        const uint32_t b0 = *reinterpret_cast<const uint32_t*>(wb);
+                        const uint32_t b1 = *reinterpret_cast<const uint32_t*>(wb + 16u);
+                        asm volatile(
+                            "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+                            "{%0,%1,%2,%3};"
+                            : "+r"(acc[nt][0]), "+r"(acc[nt][1]), "+r"(acc[nt][2]), "+r"(acc[nt][3])
+                            : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+                    }
+                }
+                // digits 0,1 sit in even lanes (tig even), 2,3 in the odd neighbour: even lanes
+                // finish value gid, odd lanes value gid + 8
+                const bool odd = (tig & 1u) != 0;
+#pragma unroll
+                for (uint32_t nt = 0; nt < kNT; ++nt) {
+                    const int32_t s0 = odd ? acc[nt][0] : acc[nt][2], s1 = odd ? acc[nt][1] : acc[nt][3];
+                    const int32_t o0 = __shfl_xor_sync(0xFFFFFFFFu, s0, 1), o1 = __shfl_xor_sync(0xFFFFFFFFu, s1, 1);
+                    int64_t Av;
+                    if (!odd) Av = (int64_t)acc[nt][0] + ((int64_t)acc[nt][1] << 8) + ((int64_t)o0 << 16) + ((int64_t)o1 << 24);
+                    else Av = (int64_t)o0 + ((int64_t)o1 << 8) + ((int64_t)acc[nt][2] << 16) + ((int64_t)acc[nt][3] << 24);
+                    const uint32_t r = nt * 2u + (tig >> 1), v = v0 + gid + (odd ? 8u : 0u);
+                    if (r < nr) {
+                        const int32_t es = esw[owner * RB + r];
+                        const uint32_t fl = flw[owner * RB + r];
+                        const bool bad = (fl >> e) & 1u, any = (fl & 4u) != 0;
+                        cvw[r * D + v] = bad ? ffrom(kCanonNaN) : !any ? 0.0f : bf_f(Av, es - 23);
                     }
                 }
             }
