@@ -83,10 +83,16 @@ __device__ __forceinline__ uint32_t digits4(int32_t W) { return ((uint32_t)W + 0
 __device__ __forceinline__ bool nonfinite(uint32_t u) { return (u & kExp) == kExp; }
 
 // maxt over a warp (every lane gets the result)
-__device__ __forceinline__ float warp_maxt(float v) {
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v = maxt(v, __shfl_xor_sync(0xFFFFFFFFu, v, o));
-    return v;
+// MAXT as an unsigned key: the largest key is the MAXT of the values (NaN above every number,
+// -0 below +0), so a maximum over many values is one integer max (a warp reduction, an atomic).
+__device__ __forceinline__ uint32_t maxt_key(float x) {
+    const uint32_t u = fbits(daz(x));
+    if ((u & ~kSign) > kExp) return 0xFFFFFFFFu;
+    return (u & kSign) ? ~u : (u | kSign);
+}
+__device__ __forceinline__ float maxt_val(uint32_t k) {
+    if (k == 0xFFFFFFFFu) return ffrom(kCanonNaN);
+    return ffrom((k & kSign) ? (k & ~kSign) : ~k);
 }
 
 __device__ __forceinline__ int32_t dot32(const uint4 a0, const uint4 a1, const uint4 b0, const uint4 b1) {
@@ -156,8 +162,8 @@ __host__ __device__ inline FaSmem fa_smem(uint32_t D, uint32_t ncell_max) {
     s.vs_off = o;
     o += fa_a16(kFaWarps * 64u * ND * 2u);                      // V scales of a segment [warp][64][ND]
     s.misc_off = o;
-    // mx [2][RB], mk [RB], wmax [warps][RB], ls [segments][RB], lacc [RB], es [warps][RB], fl [warps][RB]
-    o += 4u * (2u * RB + RB + kFaWarps * RB + kFaWarps * RB + RB + 2u * kFaWarps * RB);
+    // mx [2][RB] (max keys), mk [RB], ls [segments][RB], lacc [RB], es [warps][RB], fl [warps][RB]
+    o += 4u * (2u * RB + RB + kFaWarps * RB + RB + 2u * kFaWarps * RB);
     s.total = fa_a16(o);
     return s;
 }
@@ -220,10 +226,9 @@ __global__ void __launch_bounds__(kFaThreads, 1) fa_chunk_kernel(FaLaunch a) {
     float* CV = reinterpret_cast<float*>(smem + P.cv_off);
     int8_t* vqs = reinterpret_cast<int8_t*>(smem + P.vq_off) + warp * 64u * VP;
     uint16_t* vss = reinterpret_cast<uint16_t*>(smem + P.vs_off) + warp * 64u * ND;
-    float* mx = reinterpret_cast<float*>(smem + P.misc_off);   // [2][RB]
-    float* mk = mx + 2u * RB;                                    // [RB]
-    float* wmax = mk + RB;                                       // [warps][RB]
-    float* ls = wmax + kFaWarps * RB;                            // [segments][RB]
+    uint32_t* mx = reinterpret_cast<uint32_t*>(smem + P.misc_off);   // [2][RB] the CTA's row max keys
+    float* mk = reinterpret_cast<float*>(mx + 2u * RB);              // [RB]
+    float* ls = mk + RB;                                             // [segments][RB]
     float* lacc = ls + kFaWarps * RB;                            // [RB]
     int32_t* esw = reinterpret_cast<int32_t*>(lacc + RB);        // [warps][RB]
     uint32_t* flw = reinterpret_cast<uint32_t*>(esw + kFaWarps * RB);
@@ -263,8 +268,13 @@ __global__ void __launch_bounds__(kFaThreads, 1) fa_chunk_kernel(FaLaunch a) {
     float* lk_ch = a.lk + (((size_t)item * a.n_head_kv + g) * C + cc) * rows_max;
     bool arrived = false;
     uint32_t pass = 0;
+    constexpr uint32_t kFloorKey = ~kMFloor;                    // maxt_key(-2^100)
     for (uint32_t r0 = 0; r0 < rows; r0 += RB, ++pass) {
         const uint32_t nr = min(RB, rows - r0);
+        // this pass's max slot (the slots alternate between passes: a peer reads a slot between the
+        // barrier of its pass and the next pass's barrier, which this CTA has passed by now)
+        uint32_t* slot = mx + (pass & 1u) * RB;
+        if (tid < RB) slot[tid] = kFloorKey;
         // ---- QACT A32 of the pass's query rows (tsr_ref.c:472-487): one warp per 32-block ----
         constexpr uint32_t kQB = (RB * ND + kFaWarps - 1u) / kFaWarps;     // blocks per warp
         float qv[kQB];
@@ -290,9 +300,9 @@ __global__ void __launch_bounds__(kFaThreads, 1) fa_chunk_kernel(FaLaunch a) {
         __syncthreads();
 
         // ---- ATTQK (+ AMASK for GENERAL chunks) and the CTA's row maxima ----
-        float rmax[RB];
+        uint32_t rkey[RB];
 #pragma unroll
-        for (uint32_t r = 0; r < RB; ++r) rmax[r] = ffrom(kMFloor);
+        for (uint32_t r = 0; r < RB; ++r) rkey[r] = kFloorKey;
         // D <= 128: a cell's K bytes stay in registers across the rows, and the thread's next cell is
         // loaded while this one is computed; larger D reads them per row (L1 hits after the first row)
         constexpr uint32_t KW = D <= 128 ? 2 * ND : 1, KD = D <= 128 ? ND : 1;
@@ -363,36 +373,30 @@ __global__ void __launch_bounds__(kFaThreads, 1) fa_chunk_kernel(FaLaunch a) {
                     s = fbits(m) == kNegInf ? ffrom(kNegInf) : fadd(s, m);
                 }
                 S[r * ncell_max + j] = s;
-                rmax[r] = maxt(rmax[r], s);
+                rkey[r] = max(rkey[r], maxt_key(s));
             }
         }
         // round 0's V slices, in flight during the maximum and EXP (issued after ATTQK, whose K
         // loads they would otherwise compete with); one round holds every segment: staged once
         if (wseg < nseg && (pass == 0 || nseg > SEGS)) stage_v(wseg, wsl, true);
+        // the CTA's row maxima: a warp reduction and a shared-memory atomic per row
 #pragma unroll
         for (uint32_t r = 0; r < RB; ++r) {
-            const float m = warp_maxt(rmax[r]);
-            if (lane == 0) wmax[warp * RB + r] = m;
-        }
-        __syncthreads();
-        float* slot = mx + (pass & 1u) * RB;
-        if (tid < RB) {
-            float m = ffrom(kMFloor);
-            for (uint32_t w = 0; w < kFaWarps; ++w) m = maxt(m, wmax[w * RB + tid]);
-            slot[tid] = m;
+            const uint32_t k = __reduce_max_sync(0xFFFFFFFFu, rkey[r]);
+            if (lane == 0 && r < nr) atomicMax(slot + r, k);
         }
         // ---- the chunk maximum: MAXOUT over every channel of the chunk ----
-        // (the slots alternate between passes: a peer writes this pass's slot again only after the
-        // next pass's barrier, which every CTA reaches after its reads of this one)
+        // (the cluster barrier also orders every thread's atomics of this CTA before the reads)
         cluster_arrive();
         cluster_wait();
         if (tid < RB) {
-            float mv[16];                    // every channel's max in flight at once
+            uint32_t mv[16];                 // every channel's max in flight at once
 #pragma unroll
-            for (uint32_t c = 0; c < 16; ++c) mv[c] = c < C ? *cluster.map_shared_rank(slot + tid, c) : ffrom(kMFloor);
-            float m = ffrom(kMFloor);
+            for (uint32_t c = 0; c < 16; ++c) mv[c] = c < C ? *cluster.map_shared_rank(slot + tid, c) : kFloorKey;
+            uint32_t km = kFloorKey;
 #pragma unroll
-            for (uint32_t c = 0; c < 16; ++c) m = maxt(m, mv[c]);
+            for (uint32_t c = 0; c < 16; ++c) km = max(km, mv[c]);
+            const float m = maxt_val(km);
             mk[tid] = m;
             if (cc == 0 && tid < nr) a.mk[((size_t)item * a.n_head_kv + g) * rows_max + r0 + tid] = m;
         }
