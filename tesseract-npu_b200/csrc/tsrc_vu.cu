@@ -272,6 +272,10 @@ constexpr uint32_t kRkThreads = 512;
 constexpr uint32_t kRkBatch = 4;
 
 __global__ void __launch_bounds__(kRkThreads) rope_kvst_kernel(RopeKvst a) {
+    // a programmatic dependent launch: the next kernel (attention) may start its prologue now;
+    // this one reads the projections only after the kernel that wrote them has finished
+    asm volatile("griddepcontrol.launch_dependents;");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     const uint32_t t = blockIdx.x, half = a.nd / 2u, tid = threadIdx.x;
     const float* ct = a.cs_tab + (size_t)a.pos[t] * half;
     const float* st = a.sn_tab + (size_t)a.pos[t] * half;
@@ -435,8 +439,16 @@ cudaError_t launch_rope(const float* x, uint32_t xs, float* y, uint32_t ys, cons
 cudaError_t launch_rope_kvst(const RopeKvst& a, uint32_t T, cudaStream_t st) {
     if (T == 0) return cudaSuccess;
     if (a.nd / 2u > kMaxHalf || a.nd > a.hd || a.hd % 32u) return cudaErrorInvalidValue;
-    rope_kvst_kernel<<<T, kRkThreads, 0, st>>>(a);
-    return cudaGetLastError();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(T);
+    cfg.blockDim = dim3(kRkThreads);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, rope_kvst_kernel, a);
 }
 
 cudaError_t launch_vop(uint32_t func, const float* a, uint32_t as, const float* b, uint32_t bs, float* y, uint32_t ys,
