@@ -264,7 +264,8 @@ __global__ void __launch_bounds__(256) rope_apply_kernel(const float* x, uint32_
         }
 }
 
-// ROPE of q and k, then KVST of k and v, per token (one CTA of 512 threads): the rotation is
+// ROPE of q and k, then KVST of k and v: one CTA of 512 threads per (token, KV head g), which
+// rotates the g-th group of q heads and k head g, then stores k and v head g. The rotation is
 // rope_apply_kernel's, item by item, with each thread's loads issued before its stores (the rows
 // are rotated in place); after the barrier one warp per 32-value block of k or v runs KVST
 // (QACT A32, tsr_ref_at.c:244-264) exactly as kv_store_kernel.
@@ -276,11 +277,12 @@ __global__ void __launch_bounds__(kRkThreads) rope_kvst_kernel(RopeKvst a) {
     // this one reads the projections only after the kernel that wrote them has finished
     asm volatile("griddepcontrol.launch_dependents;");
     asm volatile("griddepcontrol.wait;" ::: "memory");
-    const uint32_t t = blockIdx.x, half = a.nd / 2u, tid = threadIdx.x;
+    const uint32_t t = blockIdx.x, g = blockIdx.y, half = a.nd / 2u, tid = threadIdx.x;
+    const uint32_t nkv = a.n_head_kv, nq = a.n_rot_heads - nkv, G = nq / nkv;
     const float* ct = a.cs_tab + (size_t)a.pos[t] * half;
     const float* st = a.sn_tab + (size_t)a.pos[t] * half;
     float* xt = a.qkv + (size_t)t * a.stride;
-    const uint32_t items = a.n_rot_heads * half;
+    const uint32_t items = (G + 1u) * half;               // q heads g G .. g G + G - 1, then k head g
     for (uint32_t i0 = tid; i0 < items; i0 += kRkBatch * kRkThreads) {
         float x0[kRkBatch], x1[kRkBatch], c[kRkBatch], s[kRkBatch];
         uint32_t j0[kRkBatch], j1[kRkBatch];
@@ -288,7 +290,8 @@ __global__ void __launch_bounds__(kRkThreads) rope_kvst_kernel(RopeKvst a) {
         for (uint32_t b = 0; b < kRkBatch; ++b) {
             const uint32_t idx = i0 + b * kRkThreads;
             if (idx < items) {
-                const uint32_t h = idx / half, i = idx - h * half;
+                const uint32_t lh = idx / half, i = idx - lh * half;
+                const uint32_t h = lh < G ? g * G + lh : nq + g;
                 j0[b] = h * a.hd + (a.neox ? i : 2u * i);
                 j1[b] = h * a.hd + (a.neox ? i + half : 2u * i + 1u);
                 x0[b] = xt[j0[b]];
@@ -307,7 +310,7 @@ __global__ void __launch_bounds__(kRkThreads) rope_kvst_kernel(RopeKvst a) {
     }
     // (nd < hd: the values past nd stay as they are, in place)
     __syncthreads();
-    const uint32_t D = a.hd, nb = a.n_head_kv * D / 32u, warp = tid >> 5, lane = tid & 31u;
+    const uint32_t D = a.hd, nb = D / 32u, warp = tid >> 5, lane = tid & 31u;
     const int64_t cell = a.cells ? a.cells[t] : (int64_t)a.cell0 + t;
     if (cell < 0 || cell >= (int64_t)a.n_cells) {
         if (tid == 0) atomicCAS(a.err, 0u, 1u);           // a row index outside the cache: not stored
@@ -315,12 +318,11 @@ __global__ void __launch_bounds__(kRkThreads) rope_kvst_kernel(RopeKvst a) {
     }
     for (uint32_t wi = warp; wi < 2u * nb; wi += kRkThreads / 32u) {
         const bool vt = wi >= nb;
-        const uint32_t b = vt ? wi - nb : wi;
-        const float v = xt[(vt ? a.v_off : a.k_off) + 32u * b + lane];
+        const uint32_t k = 32u * (vt ? wi - nb : wi);      // the block's first value inside head g
+        const float v = xt[(vt ? a.v_off : a.k_off) + g * D + k + lane];
         const uint32_t amax = __reduce_max_sync(0xFFFFFFFFu, amax_key(v));
         const float db = fdiv(ffrom(amax), 127.0f);
         const float id = (fbits(db) & ~kSign) ? frecip(db) : 0.0f;
-        const uint32_t g = 32u * b / D, k = 32u * b - g * D;
         const size_t hc = (size_t)g * a.n_cells + (size_t)cell;
         (vt ? a.vq : a.kq)[kv_qoff(vt, g, a.n_cells, D, (size_t)cell, k + lane)] = (int8_t)round_away_sat8(fmul(daz(v), id));
         if (lane == 0) (vt ? a.vd : a.kd)[hc * (D / 32u) + k / 32u] = f2h(db);
@@ -439,8 +441,12 @@ cudaError_t launch_rope(const float* x, uint32_t xs, float* y, uint32_t ys, cons
 cudaError_t launch_rope_kvst(const RopeKvst& a, uint32_t T, cudaStream_t st) {
     if (T == 0) return cudaSuccess;
     if (a.nd / 2u > kMaxHalf || a.nd > a.hd || a.hd % 32u) return cudaErrorInvalidValue;
+    // q heads then k heads are rotated, the q heads in n_head_kv equal groups, k right after q
+    if (a.n_head_kv == 0 || a.n_rot_heads <= a.n_head_kv || (a.n_rot_heads - a.n_head_kv) % a.n_head_kv ||
+        a.k_off != (a.n_rot_heads - a.n_head_kv) * a.hd)
+        return cudaErrorInvalidValue;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(T);
+    cfg.gridDim = dim3(T, a.n_head_kv);
     cfg.blockDim = dim3(kRkThreads);
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
