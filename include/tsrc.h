@@ -93,6 +93,21 @@ TSRC_API int tsrc_weight_upload_device(tsrc_ctx * ctx, uint32_t fmt, const void 
 // `stream` and returns when the weight is in place.
 TSRC_API int tsrc_weight_synth(tsrc_ctx * ctx, uint32_t fmt, uint32_t N, uint32_t K, uint32_t row0, uint32_t n_rows,
                       uint64_t seed, float sigma, void * stream, tsrc_weight ** out);
+// ggml tensor types at load time (tsr_dev_fmt_for_type / tsr_type_loadable / tsr_row_to_dev_blocks,
+// sw/ggml-tesseract/tsr-weights.h:14-30). ggml_type is ggml.h's enum value. Q8_0 (8) and Q4_K (12)
+// load as shipped; F32 (0), F16 (1), BF16 (30), Q4_0 (2), Q4_1 (3), Q5_0 (6), Q5_1 (7), Q5_K (13)
+// and Q6_K (14) are converted to Q8_0 on the host: ggml's to_float of the type, then
+// quantize_row_q8_0_ref. Other types are refused with TSRC_E_SHAPE.
+// Block geometry of a type and the device format it loads as (TSRC_FMT_*).
+TSRC_API int tsrc_ggml_type_info(uint32_t ggml_type, uint32_t * block_elems, uint32_t * block_bytes, uint32_t * dev_fmt);
+// Host-only: n_rows rows of K values of ggml_type (ggml layout, packed) -> rows of the device format's
+// ggml blocks at dst (K / 32 * 34 bytes a row for Q8_0, K / 256 * 144 for Q4_K; native types are
+// copied). Large tensors are converted on several host threads.
+TSRC_API int tsrc_ggml_rows_to_dev(uint32_t ggml_type, const void * src, uint32_t n_rows, uint32_t K, void * dst);
+// tsrc_weight_upload for rows of any loadable ggml type (converted on the host first when the type is
+// not native). Synchronous.
+TSRC_API int tsrc_weight_upload_ggml(tsrc_ctx * ctx, uint32_t ggml_type, const void * ggml_rows, uint32_t N, uint32_t K,
+                                     uint32_t row0, uint32_t n_rows, tsrc_weight ** out);
 // Reads the shard back as ggml rows (n_rows rows) into host memory (get_tensor; the inverse repack,
 // tsr_unrepack_row, sw/sim/tsr_ref.c:316-333). Synchronous.
 TSRC_API int tsrc_weight_download(const tsrc_weight * w, void * ggml_rows);
@@ -327,6 +342,17 @@ TSRC_API int tsrc_model_decode(tsrc_model * m, const int32_t * ids, uint32_t pos
 // 2j + 1 up_j; 2 n_ff rows: the MUL_MAT applies SWIGLU to the pairs as its epilogue), 3 = down;
 // or TSRC_MODEL_GLOBAL.
 TSRC_API int tsrc_model_weight(const tsrc_model * m, uint32_t layer, uint32_t which, tsrc_weight ** out);
+// Replaces a weight of a single-device model with rows of a loadable ggml type (host memory; the
+// load of a GGUF model's tensors, llama.cpp's set_tensor of each weight). layer / which as
+// tsrc_model_weight; N x K must be the weight's shape. which 0 takes the q, k, v rows stacked (q rows,
+// then k, then v); which 2 the gate rows then the up rows (the model interleaves them); the head
+// (TSRC_MODEL_GLOBAL, 1) exists only without a tied head. The next decode token captures a new graph.
+TSRC_API int tsrc_model_set_weight(tsrc_model * m, uint32_t layer, uint32_t which, uint32_t ggml_type, const void * rows,
+                                   uint32_t N, uint32_t K);
+// Replaces an f32 vector of a single-device model (host memory, n values): which 0 attn_norm, 1
+// ffn_norm (n_embd), 2 the q | k | v bias (n_head + 2 n_head_kv heads; models with qkv_bias), 5 the
+// output norm (layer = n_layer), as tsrc_model_f32_value numbers them.
+TSRC_API int tsrc_model_set_f32(tsrc_model * m, uint32_t layer, uint32_t which, const float * values, uint32_t n);
 // The host-computed ROPE theta scale and attention scale the model passes to the kinds.
 TSRC_API int tsrc_model_params(const tsrc_model * m, float * ts, float * kq_scale);
 // f32 vector element i of the model: which 0 attn_norm, 1 ffn_norm, 2 the q | k | v bias (layer l),

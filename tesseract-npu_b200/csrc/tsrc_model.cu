@@ -585,4 +585,73 @@ int tsrc_model_decode(tsrc_model* m, const int32_t* ids, uint32_t pos0, float* l
     return TSRC_OK;
 }
 
+int tsrc_model_set_weight(tsrc_model* m, uint32_t layer, uint32_t which, uint32_t ggml_type, const void* rows, uint32_t N,
+                          uint32_t K) {
+    if (!m || !rows) return tsrc::api_fail(TSRC_E_ARG, "tsrc_model_set_weight: NULL argument");
+    if (m->team) return tsrc::api_fail(TSRC_E_ARG, "tsrc_model_set_weight: single-device models only");
+    const tsrc_model_cfg& c = m->c;
+    const uint32_t E = c.n_embd, Hq = c.n_head * c.head_dim, Hkv = c.n_head_kv * c.head_dim, F = c.n_ff;
+    tsrc_weight** slot = nullptr;
+    uint32_t eN = 0, eK = 0;
+    if (layer == TSRC_MODEL_GLOBAL) {
+        if (which == 0u) {
+            slot = &m->tok_embd;
+        } else if (which == 1u && !c.tied_head) {
+            slot = &m->output;
+        } else {
+            return tsrc::api_fail(TSRC_E_ARG, "tsrc_model_set_weight: no such global weight (a tied head is the embedding)");
+        }
+        eN = c.n_vocab;
+        eK = E;
+    } else {
+        if (layer >= c.n_layer || which > 3u) return tsrc::api_fail(TSRC_E_ARG, "tsrc_model_set_weight: no such weight");
+        tsrc_model::Layer& L = m->layers[layer];
+        tsrc_weight** slots[] = {&L.wqkv, &L.wo, &L.wgu, &L.wd};
+        const uint32_t ns[] = {Hq + 2u * Hkv, E, 2u * F, E}, ks[] = {E, Hq, E, F};
+        slot = slots[which];
+        eN = ns[which];
+        eK = ks[which];
+    }
+    if (N != eN || K != eK) return tsrc::api_fail(TSRC_E_SHAPE, "tsrc_model_set_weight: the rows do not have the weight's shape");
+    tsrc_weight* w = nullptr;
+    int rc = tsrc_weight_upload_ggml(m->ctx, ggml_type, rows, N, K, 0, N, &w);
+    if (rc) return rc;
+    if (layer != TSRC_MODEL_GLOBAL && which == 2u) {      // gate rows then up rows -> interleaved pairs
+        rc = tsrc::weight_interleave_halves(m->ctx, w, &w);
+        if (rc) {
+            tsrc_weight_free(w);
+            return rc;
+        }
+    }
+    drop_graph(m);                                       // the captured step holds the old weight
+    tsrc_weight_free(*slot);
+    *slot = w;
+    return TSRC_OK;
+}
+
+int tsrc_model_set_f32(tsrc_model* m, uint32_t layer, uint32_t which, const float* values, uint32_t n) {
+    if (!m || !values) return tsrc::api_fail(TSRC_E_ARG, "tsrc_model_set_f32: NULL argument");
+    if (m->team) return tsrc::api_fail(TSRC_E_ARG, "tsrc_model_set_f32: single-device models only");
+    const tsrc_model_cfg& c = m->c;
+    const uint32_t E = c.n_embd, Hq = c.n_head * c.head_dim, Hkv = c.n_head_kv * c.head_dim;
+    float* dst = nullptr;
+    uint32_t en = 0;
+    if (which == kVecOutNorm && layer == c.n_layer) {
+        dst = m->out_norm;
+        en = E;
+    } else if (layer < c.n_layer && (which == kVecAttnNorm || which == kVecFfnNorm)) {
+        dst = which == kVecAttnNorm ? m->layers[layer].attn_norm : m->layers[layer].ffn_norm;
+        en = E;
+    } else if (layer < c.n_layer && which == kVecBqkv && c.qkv_bias) {
+        dst = m->layers[layer].bqkv;
+        en = Hq + 2u * Hkv;
+    } else {
+        return tsrc::api_fail(TSRC_E_ARG, "tsrc_model_set_f32: no such vector");
+    }
+    if (n != en) return tsrc::api_fail(TSRC_E_SHAPE, "tsrc_model_set_f32: wrong length");
+    if (cudaMemcpy(dst, values, (size_t)n * sizeof(float), cudaMemcpyHostToDevice) != cudaSuccess)
+        return tsrc::api_fail(TSRC_E_CUDA, "tsrc_model_set_f32: copy");
+    return TSRC_OK;
+}
+
 }  // extern "C"

@@ -52,6 +52,9 @@ _SIGS = {
     "tsrc_weight_upload": (_i, [_p, _u32, _p, _u32, _u32, _u32, _u32, ct.POINTER(_p)]),
     "tsrc_weight_upload_device": (_i, [_p, _u32, _p, _u32, _u32, _u32, _u32, _p, ct.POINTER(_p)]),
     "tsrc_weight_synth": (_i, [_p, _u32, _u32, _u32, _u32, _u32, _u64, _f32, _p, ct.POINTER(_p)]),
+    "tsrc_ggml_type_info": (_i, [_u32, ct.POINTER(_u32), ct.POINTER(_u32), ct.POINTER(_u32)]),
+    "tsrc_ggml_rows_to_dev": (_i, [_u32, _p, _u32, _u32, _p]),
+    "tsrc_weight_upload_ggml": (_i, [_p, _u32, _p, _u32, _u32, _u32, _u32, ct.POINTER(_p)]),
     "tsrc_weight_download": (_i, [_p, _p]),
     "tsrc_weight_info": (_i, [_p] + [ct.POINTER(_u32)] * 5 + [ct.POINTER(_u64)]),
     "tsrc_weight_free": (_i, [_p]),
@@ -65,6 +68,8 @@ _SIGS = {
     "tsrc_model_forward": (_i, [_p, _p, _u32, _u32, _p, _p]),
     "tsrc_model_decode": (_i, [_p, _p, _u32, _p, _p]),
     "tsrc_model_weight": (_i, [_p, _u32, _u32, ct.POINTER(_p)]),
+    "tsrc_model_set_weight": (_i, [_p, _u32, _u32, _u32, _p, _u32, _u32]),
+    "tsrc_model_set_f32": (_i, [_p, _u32, _u32, _p, _u32]),
     "tsrc_model_params": (_i, [_p, ct.POINTER(_f32), ct.POINTER(_f32)]),
     "tsrc_model_f32_value": (_f32, [_u64, _u32, _u32, _u32]),
     "tsrc_rope": (_i, [_p, _p, _u32, _p, _u32, _p, _u32, _u32, _u32, _u32, _u32, _f32, _f32, _p]),
@@ -165,6 +170,31 @@ def ggml_row_bytes(fmt: int, K: int) -> int:
     return K // BLOCK[fmt] * BLOCK_BYTES[fmt]
 
 
+# ggml_type values (ggml.h) of the tensor types the loader knows
+GGML_F32, GGML_F16, GGML_Q4_0, GGML_Q4_1, GGML_Q5_0, GGML_Q5_1, GGML_Q8_0 = 0, 1, 2, 3, 6, 7, 8
+GGML_Q4_K, GGML_Q5_K, GGML_Q6_K, GGML_BF16 = 12, 13, 14, 30
+
+
+def ggml_type_info(ggml_type: int) -> tuple[int, int, int]:
+    """(block elements, block bytes, device format) of a loadable ggml type; TsrcError otherwise."""
+    be, bb, fmt = _u32(), _u32(), _u32()
+    _check(lib().tsrc_ggml_type_info(ggml_type, ct.byref(be), ct.byref(bb), ct.byref(fmt)))
+    return be.value, bb.value, fmt.value
+
+
+def ggml_rows_to_dev(ggml_type: int, rows, n_rows: int, K: int):
+    """Host-only load-time conversion: rows of a ggml type -> numpy uint8 [n_rows, row bytes] of the
+    device format's ggml blocks (Q8_0 unless the type is Q4_K)."""
+    import numpy as np
+    be, bb, fmt = ggml_type_info(ggml_type)
+    a = np.ascontiguousarray(rows).view(np.uint8).reshape(-1)
+    if a.size != n_rows * (K // be) * bb:
+        raise TsrcError(E_ARG, f"ggml_rows_to_dev: {a.size} bytes for {n_rows} rows of K={K}")
+    out = np.empty((n_rows, ggml_row_bytes(fmt, K)), np.uint8)
+    _check(lib().tsrc_ggml_rows_to_dev(ggml_type, a.ctypes.data, n_rows, K, out.ctypes.data))
+    return out
+
+
 def mul_mat_unsupported(fmt: int, N: int, K: int, T: int = 1) -> str | None:
     r = lib().tsrc_mul_mat_unsupported(fmt, N, K, T)
     return None if r is None else r.decode()
@@ -204,6 +234,19 @@ class Device:
             raise TsrcError(E_ARG, f"upload: {a.size} bytes for {n_rows} rows of K={K}")
         h = _p()
         _check(lib().tsrc_weight_upload(self.handle, fmt, a.ctypes.data, N, K, row0, n_rows, ct.byref(h)))
+        return Weight(self, h)
+
+    def upload_ggml(self, ggml_type: int, rows, N: int, K: int, row0: int = 0, n_rows: int | None = None) -> "Weight":
+        """Rows of any loadable ggml type (host) -> a device weight shard (non-native types are
+        converted to Q8_0 on the host first)."""
+        import numpy as np
+        n_rows = N - row0 if n_rows is None else n_rows
+        be, bb, _ = ggml_type_info(ggml_type)
+        a = np.ascontiguousarray(rows).view(np.uint8).reshape(-1)
+        if a.size != n_rows * (K // be) * bb:
+            raise TsrcError(E_ARG, f"upload_ggml: {a.size} bytes for {n_rows} rows of K={K}")
+        h = _p()
+        _check(lib().tsrc_weight_upload_ggml(self.handle, ggml_type, a.ctypes.data, N, K, row0, n_rows, ct.byref(h)))
         return Weight(self, h)
 
     def upload_device(self, fmt: int, rows_dev, N: int, K: int, row0: int = 0, n_rows: int | None = None,
@@ -388,6 +431,20 @@ class Model:
         w = Weight(self.dev, h)
         w.free = lambda: None                       # owned by the model
         return w
+
+    def set_weight(self, layer: int, which: int, ggml_type: int, rows, N: int, K: int) -> None:
+        """Replaces a weight with host rows of a loadable ggml type (tsrc_model_set_weight)."""
+        import numpy as np
+        a = np.ascontiguousarray(rows).view(np.uint8).reshape(-1)
+        be, bb, _ = ggml_type_info(ggml_type)
+        if a.size != N * (K // be) * bb:
+            raise TsrcError(E_ARG, f"set_weight: {a.size} bytes for {N} rows of K={K}")
+        _check(lib().tsrc_model_set_weight(self.handle, layer, which, ggml_type, a.ctypes.data, N, K))
+
+    def set_f32(self, layer: int, which: int, values) -> None:
+        """Replaces an f32 vector (norms, q | k | v bias) from host values (tsrc_model_set_f32)."""
+        a = np.ascontiguousarray(values, dtype=np.float32)
+        _check(lib().tsrc_model_set_f32(self.handle, layer, which, a.ctypes.data, a.size))
 
     def kv(self, layer: int) -> "KvCache":
         """Layer `layer`'s cache (owned by the model; a rank's holds its KV heads)."""
