@@ -223,29 +223,21 @@ def model_measure(dev, tsrc, torch, name, steps, warmup, e2e_steps=32):
 
 
 def model_measure_tp(dev, tsrc, torch, dist, name, steps, warmup, rank, world, e2e_steps=32):
-    """Decode of the config split over `world` GPUs (tsrc_model_create_tp over a team): every
-    layer's cache cells [0, prompt) are loaded with seeded rows through KVST (this rank's KV heads'
-    columns) in place of the prompt's prefill, then `warmup` + `steps` timed decode tokens and
-    `e2e_steps` with the token id in from pinned host memory and the logits out. Device times are
-    the maximum over the ranks."""
+    """The config split over `world` GPUs (tsrc_model_create_tp over a team): the prompt's prefill
+    through tsrc_model_forward (timed: a warm-up pass, then the measured one), then `warmup` +
+    `steps` timed decode tokens and `e2e_steps` with the token id in from pinned host memory and the
+    logits out. Device times are the maximum over the ranks. The team's staging holds 64 rows of
+    the widest exchanged vector, so a prompt's gathers take few team steps."""
     spec = MODELS[name]
     prompt = spec["prompt"]
     n_ctx = prompt + warmup + steps + e2e_steps
     s = dict(spec["shape"], n_ctx=n_ctx)
-    n_max = max(s["n_vocab"], s["n_ff"], s["n_head"] * s["head_dim"], s["n_embd"])
+    n_max = 64 * max(s["n_vocab"], s["n_ff"], s["n_head"] * s["head_dim"], s["n_embd"])
     team = dev.team_create(rank, world, n_max)
     hs = [None] * world
     dist.all_gather_object(hs, team.ipc_handle)
     team.connect(b"".join(hs))
     model = tsrc.Model(dev, tsrc.ModelCfg(**s), seed=spec["seed"], team=team)
-    E = s["n_head_kv"] * s["head_dim"]
-    w = E // world
-    for l in range(s["n_layer"]):
-        g = torch.Generator(device="cuda").manual_seed(spec["seed"] * 100 + l)
-        kv = model.kv(l)
-        for which in (tsrc.KV_K, tsrc.KV_V):
-            rows = torch.randn((prompt, E), device="cuda", generator=g)
-            kv.set_rows(which, rows[:, rank * w:(rank + 1) * w].contiguous())
     g = torch.Generator(device="cuda")
     g.manual_seed(spec["seed"])
     ids = torch.randint(0, s["n_vocab"], (n_ctx,), dtype=torch.int32, device="cuda", generator=g)
@@ -261,6 +253,14 @@ def model_measure_tp(dev, tsrc, torch, dist, name, steps, warmup, rank, world, e
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    model.forward(ids, prompt, 0, logits)                      # warm-up prefill (first launches), then timed
+    barrier()
+    e0.record()
+    model.forward(ids, prompt, 0, logits)
+    e1.record()
+    barrier()
+    prefill_ms = max_over_ranks(e0.elapsed_time(e1))
     pos = prompt
     for _ in range(warmup):
         one.copy_(ids[pos:pos + 1])
@@ -293,8 +293,8 @@ def model_measure_tp(dev, tsrc, torch, dist, name, steps, warmup, rank, world, e
     # attention gather, o (+ gather), gate / up (RMS_NORM, SWIGLU and the gather fused), down
     # (+ gather); then the head (RMS_NORM and the gather fused)
     launches = 3 + 8 * s["n_layer"]
-    return dict(shape=s, ms=ms, e2e_ms=e2e_ms, algo_bytes=model_algo_bytes(s, kv0 + steps // 2), launches=launches,
-                n_kv=(kv0, pos)), model, team
+    return dict(shape=s, prefill_ms=prefill_ms, ms=ms, e2e_ms=e2e_ms, algo_bytes=model_algo_bytes(s, kv0 + steps // 2),
+                launches=launches, n_kv=(kv0, pos)), model, team
 
 
 def cpu_reference_model(name, threads, model=None):
@@ -775,10 +775,11 @@ def run_model_tp(args, spec, world, rank):
         "metric": "decode tokens/s", "value": round(1e3 / r["ms"], 2), "unit": "tokens/s", "n_gpus": world, "steps": steps,
         "warmup": args.warmup, "ms_per_step": round(r["ms"], 4), "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "int8",
-        "data": "synthetic (random-init weights quantized on device, random token ids, seeded KV cache rows)",
+        "data": "synthetic (random-init weights quantized on device, random token ids)",
         "config": {"workload": spec["desc"], "parallelism": f"tensor-parallel x{world} (heads, rows)",
-                   "kv_cells_during_timing": list(r["n_kv"]),
-                   "kv": f"cells [0, {spec['prompt']}) loaded with seeded rows through KVST in place of the prompt's prefill",
+                   "kv_cells_during_timing": list(r["n_kv"]), "prompt_tokens": spec["prompt"],
+                   "prefill_ms": round(r["prefill_ms"], 2),
+                   "prefill_tokens_per_s": round(spec["prompt"] / (r["prefill_ms"] * 1e-3), 1),
                    "collective": "tagged-word gathers over NVLink (attention output, SWIGLU row; fused into o, down, head)",
                    "l2": f"inputs larger than L2 (a token reads {r['algo_bytes'] / 1e6:.0f} MB over all GPUs)", "cuda_graph": True},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak * world, "unit": "GB/s",

@@ -318,9 +318,10 @@ TSRC_API int tsrc_model_create(tsrc_ctx * ctx, const tsrc_model_cfg * cfg, uint6
 // must split evenly) with their q / k / v rows and cache, and the symmetric row shards (R = ceil(N /
 // world), sw/sim/tsr_ref.c:335-357) of o, gate / up (of n_ff), down and the head; every exchange is
 // the team's tagged-word gather (the attention output and the SWIGLU row, then o, down and the head
-// fused with their gathers). Runs one token at a time (tsrc_model_forward with T = 1, or
-// tsrc_model_decode): logits (all n_vocab) on every rank equal the single-GPU model's. The team's
-// n_max must hold max(n_vocab, n_ff, n_head * head_dim, n_embd).
+// fused with their gathers). tsrc_model_decode runs one token; tsrc_model_forward any T (a prompt:
+// tensor-core MUL_MATs of the rank's rows, then gathers of T rows, as many rows per team step as
+// n_max holds): logits (all n_vocab) on every rank equal the single-GPU model's. The team's n_max
+// must hold max(n_vocab, n_ff, n_head * head_dim, n_embd); a multiple of it speeds prompts up.
 TSRC_API int tsrc_model_create_tp(tsrc_ctx * ctx, const tsrc_model_cfg * cfg, uint64_t seed, tsrc_team * team,
                                   tsrc_model ** out);
 TSRC_API int tsrc_model_free(tsrc_model * m);

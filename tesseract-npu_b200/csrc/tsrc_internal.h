@@ -65,6 +65,7 @@ struct TeamGather {
     const float* src;
     uint32_t n_local, offset, n;
     float* dst;
+    uint32_t T, src_stride, dst_stride;   // T token rows: src [T][src_stride], dst [T][dst_stride]; T n <= half
 };
 cudaError_t launch_team_gather(const TeamGather& g, cudaStream_t st);
 }  // namespace tsrc
@@ -85,7 +86,11 @@ int mul_mat_rms_swiglu(tsrc_ctx* ctx, const tsrc_weight* w, const float* x, cons
 // a copy of w with its two halves of rows interleaved (row j of the first half -> 2j, of the
 // second -> 2j + 1); w is freed
 int weight_interleave_halves(tsrc_ctx* ctx, tsrc_weight* w, tsrc_weight** out);
+int weight_rows(const tsrc_weight* w, uint32_t* N, uint32_t* row0, uint32_t* n_rows);
 int team_gather(tsrc_team* t, const float* src, uint32_t n_local, uint32_t offset, float* dst, uint32_t n, void* stream);
+// T token rows of such vectors (row strides in floats), several rows per team step
+int team_gather_rows(tsrc_team* t, const float* src, uint32_t src_stride, uint32_t n_local, uint32_t offset, float* dst,
+                     uint32_t dst_stride, uint32_t n, uint32_t T, void* stream);
 // tsrc_api.cu: a weight whose rows are row ranges [r0[i], r0[i] + n[i]) of one synthetic N-row
 // matrix, stacked in that order (the rows equal those of tsrc_weight_synth's full matrix)
 int weight_synth_ranges(tsrc_ctx* ctx, uint32_t fmt, uint32_t N, uint32_t K, const uint32_t* r0, const uint32_t* n,

@@ -620,21 +620,28 @@ __device__ __forceinline__ void team_finish(const MvArgs& a, uint32_t step, uint
     (void)sflag;
 }
 
-// The same exchange for a plain vector: every CTA stores its share of this rank's src into every
-// rank's staging half as tagged words, then copies its share of the whole vector out.
+// The same exchange for plain vectors: T token rows, each of n values of which this rank holds
+// [offset, offset + n_local). Token t's row sits at words [t n, t n + n) of the staging half. Every
+// CTA stores its share of this rank's values into every rank's staging half as tagged words, then
+// copies its share of all T n words out.
 __global__ void __launch_bounds__(256) team_gather_kernel(TeamGather g) {
     const uint32_t step = *reinterpret_cast<volatile uint32_t*>(g.team_state);
     const unsigned long long tag = (unsigned long long)(step + 1u) << 32;
     const size_t half = (size_t)(step & 1u) * g.half;
-    const uint32_t ls = (g.n_local + gridDim.x - 1u) / gridDim.x, l0 = blockIdx.x * ls, l1 = min(g.n_local, l0 + ls);
+    const uint32_t nl = g.T * g.n_local;
+    const uint32_t ls = (nl + gridDim.x - 1u) / gridDim.x, l0 = blockIdx.x * ls, l1 = min(nl, l0 + ls);
     for (uint32_t r = 0; r < g.world; ++r)
-        for (uint32_t i = l0 + threadIdx.x; i < l1; i += blockDim.x)
-            st_relaxed_sys64(g.team_y[r] + half + g.offset + i, tag | __float_as_uint(g.src[i]));
+        for (uint32_t k = l0 + threadIdx.x; k < l1; k += blockDim.x) {
+            const uint32_t t = k / g.n_local, i = k - t * g.n_local;
+            st_relaxed_sys64(g.team_y[r] + half + (size_t)t * g.n + g.offset + i,
+                             tag | __float_as_uint(g.src[(size_t)t * g.src_stride + i]));
+        }
     const unsigned long long* src = g.team_y[g.rank] + half;
-    const uint32_t share = (g.n + gridDim.x - 1u) / gridDim.x, i0 = blockIdx.x * share, i1 = min(g.n, i0 + share);
+    const uint32_t na = g.T * g.n;
+    const uint32_t share = (na + gridDim.x - 1u) / gridDim.x, i0 = blockIdx.x * share, i1 = min(na, i0 + share);
     bool gave_up = false;
-    for (uint32_t i = i0 + threadIdx.x; i < i1; i += blockDim.x) {
-        unsigned long long w = ld_relaxed_sys64(src + i);
+    for (uint32_t k = i0 + threadIdx.x; k < i1; k += blockDim.x) {
+        unsigned long long w = ld_relaxed_sys64(src + k);
         uint32_t it = 0;
         while ((w & 0xFFFFFFFF00000000ull) != tag && !gave_up) {
             if (++it >= kTeamSpin) {
@@ -642,9 +649,10 @@ __global__ void __launch_bounds__(256) team_gather_kernel(TeamGather g) {
                 atomicCAS(&g_mv_error, 0u, 2u);
             }
             __nanosleep(64);
-            w = ld_relaxed_sys64(src + i);
+            w = ld_relaxed_sys64(src + k);
         }
-        g.dst[i] = __uint_as_float((uint32_t)w);
+        const uint32_t t = k / g.n, j = k - t * g.n;
+        g.dst[(size_t)t * g.dst_stride + j] = __uint_as_float((uint32_t)w);
     }
     __syncthreads();
     if (threadIdx.x == 0 && atomicAdd(g.team_state + 1, 1u) + 1u == gridDim.x) {
@@ -654,9 +662,10 @@ __global__ void __launch_bounds__(256) team_gather_kernel(TeamGather g) {
 }
 
 cudaError_t launch_team_gather(const TeamGather& g, cudaStream_t st) {
-    if (g.n == 0) return cudaSuccess;
-    uint32_t blocks = (g.n + 1023u) / 1024u;
-    blocks = blocks < 1u ? 1u : (blocks > 64u ? 64u : blocks);
+    const uint32_t na = g.T * g.n;
+    if (na == 0) return cudaSuccess;
+    uint32_t blocks = (na + 1023u) / 1024u;
+    blocks = blocks < 1u ? 1u : (blocks > 148u ? 148u : blocks);
     team_gather_kernel<<<blocks, 256, 0, st>>>(g);
     return cudaGetLastError();
 }

@@ -345,13 +345,67 @@ int forward_body(tsrc_model* m, const int32_t* ids, uint32_t T, uint32_t pos0, f
     const cudaStream_t st = static_cast<cudaStream_t>(stream);
     tsrc_fa_cfg fa = c.fa;
     if (fa.C == 0) fa = tsrc_fa_cfg{4u, 4u, 9344u, 32768u, 0u};
-    if (m->team && T != 1)
-        return tsrc::api_fail(TSRC_E_ARG, "tsrc_model_forward: a tensor-parallel model runs one token at a time");
     int rc = tsrc_get_rows(ctx, m->tok_embd, ids, T, m->x, E, stream);
 #define TSRC_M(call) \
     if (rc == TSRC_OK) rc = (call)
 #define TSRC_MC(call, what) \
     if (rc == TSRC_OK && (call) != cudaSuccess) rc = tsrc::api_fail(TSRC_E_CUDA, what)
+    if (m->team && T > 1) {
+        // a prompt over the team: every rank holds all T rows of the residual stream x. Per layer:
+        // RMS_NORM; q / k / v of this rank's heads (tensor-core MUL_MAT for T > 8) with its bias
+        // slice; ROPE + KVST into its KV heads; FA of its q heads (planned with the model's E); then
+        // the exchanges of T rows each: the attention output (gather), o rows + residual (gather
+        // into x), gate / up pairs of its F slice and SWIGLU (gather), down rows + residual (gather
+        // into x). The head runs on the last token as in decode. Every value is one GPU's result,
+        // so the logits are the single GPU's.
+        tsrc_team* tm = m->team;
+        const uint32_t qn = m->hq_loc * D, kn = m->hkv_loc * D, qkv_loc = qn + 2u * kn;
+        uint32_t on = 0, o0 = 0, dn = 0, d0 = 0, wN = 0;
+        if (rc == TSRC_OK) rc = tsrc::weight_rows(m->layers[0].wo, &wN, &o0, &on);
+        if (rc == TSRC_OK) rc = tsrc::weight_rows(m->layers[0].wd, &wN, &d0, &dn);
+        fa.plan_n_head_kv = c.n_head_kv;
+        for (uint32_t l = 0; l < c.n_layer; ++l) {
+            const tsrc_model::Layer& L = m->layers[l];
+            const float* bias = m->tp_bias ? m->tp_bias + (size_t)l * qkv_loc : nullptr;
+            TSRC_M(tsrc_rms_norm(ctx, m->x, E, m->h, E, L.attn_norm, E, T, c.rms_eps, inv_n, stream));
+            TSRC_M(tsrc_mul_mat(ctx, L.wqkv, m->h, T, E, m->qkv, qkv_loc, bias, 0, bias ? TSRC_MM_ADD : 0u, 1.0f, 1.0f, stream));
+            tsrc::RopeKvst rk{};
+            rk.qkv = m->qkv;
+            rk.stride = qkv_loc;
+            rk.pos = pos;
+            rk.n_rot_heads = m->hq_loc + m->hkv_loc;
+            rk.hd = D;
+            rk.nd = D;
+            rk.neox = c.rope_mode;
+            rk.cs_tab = m->rope_tab;
+            rk.sn_tab = m->rope_tab + (size_t)c.n_ctx * half;
+            rk.k_off = qn;
+            rk.v_off = qn + kn;
+            rk.cells = cells;
+            rk.cell0 = pos0;
+            if (rc == TSRC_OK && !cells && (uint64_t)pos0 + T > tsrc::kv_cells(L.kv))
+                rc = tsrc::api_fail(TSRC_E_ARG, "tsrc_model_forward: cells outside the cache");
+            TSRC_M(tsrc::kv_fill_planes(L.kv, &rk));
+            TSRC_MC(tsrc::launch_rope_kvst(rk, T, st), "tsrc_model_forward: ROPE + KVST launch");
+            // FA takes q rows [T][heads][D] contiguous: the rank's q rows go to att first
+            TSRC_MC(cudaMemcpy2DAsync(m->att, (size_t)qn * 4u, m->qkv, (size_t)qkv_loc * 4u, (size_t)qn * 4u, T,
+                                      cudaMemcpyDeviceToDevice, st), "tsrc_model_forward: q copy");
+            TSRC_M(tsrc_flash_attn(ctx, L.kv, m->att, T, m->hq_loc, n_kv, mask, n_kv, m->kq_scale, pos0, n_kv, &fa, m->q, stream));
+            TSRC_M(tsrc::team_gather_rows(tm, m->q, qn, qn, m->rank * qn, m->att, Hq, Hq, T, stream));
+            TSRC_M(tsrc_mul_mat(ctx, L.wo, m->att, T, Hq, m->h, on, m->x + o0, E, TSRC_MM_ADD, 1.0f, 1.0f, stream));
+            TSRC_M(tsrc::team_gather_rows(tm, m->h, on, on, o0, m->x, E, E, T, stream));
+            TSRC_M(tsrc_rms_norm(ctx, m->x, E, m->h, E, L.ffn_norm, E, T, c.rms_eps, inv_n, stream));
+            TSRC_M(tsrc_mul_mat(ctx, L.wgu, m->h, T, E, m->gu, 2u * m->f_n, nullptr, 0, 0u, 1.0f, 1.0f, stream));
+            TSRC_MC(tsrc::launch_vop(8u, m->gu, 2u * m->f_n, nullptr, 0u, m->act, m->f_n, m->f_n, T, st),
+                    "tsrc_model_forward: SWIGLU launch");
+            TSRC_M(tsrc::team_gather_rows(tm, m->act, m->f_n, m->f_n, m->f0, m->gu, F, F, T, stream));
+            TSRC_M(tsrc_mul_mat(ctx, L.wd, m->gu, T, F, m->h, dn, m->x + d0, E, TSRC_MM_ADD, 1.0f, 1.0f, stream));
+            TSRC_M(tsrc::team_gather_rows(tm, m->h, dn, dn, d0, m->x, E, E, T, stream));
+        }
+        const float* xl = m->x + (size_t)(T - 1u) * E;
+        TSRC_M(tsrc::team_mul_mat(ctx, tm, m->head_shard, xl, logits, nullptr, m->out_norm, c.rms_eps, inv_n, true, stream));
+        return rc;
+    }
     if (m->team) {
         // one token over the team: q / k / v of this rank's heads, its KV heads' cache and FA, then
         // the exchanges: attention output (gather), o rows (+ residual, fused gather), gate / up row

@@ -257,21 +257,35 @@ int team_mul_mat_swiglu(tsrc_ctx* ctx, tsrc_team* t, const tsrc_weight* w, const
 
 // dst[offset .. offset + n_local) = src on every rank (dst holds n values)
 int team_gather(tsrc_team* t, const float* src, uint32_t n_local, uint32_t offset, float* dst, uint32_t n, void* stream) {
+    return team_gather_rows(t, src, n_local, n_local, offset, dst, n, n, 1u, stream);
+}
+
+// T token rows: dst[t dst_stride + offset .. + n_local) = src[t src_stride ..] on every rank (a row
+// of dst holds n values); as many rows per launch (one team step each) as the staging half holds
+int team_gather_rows(tsrc_team* t, const float* src, uint32_t src_stride, uint32_t n_local, uint32_t offset, float* dst,
+                     uint32_t dst_stride, uint32_t n, uint32_t T, void* stream) {
     if (!t || !t->connected) return set_error(TSRC_E_ARG, "team_gather: team missing or not connected");
-    if (n > t->n_max || offset + n_local > n) return set_error(TSRC_E_ARG, "team_gather: sizes exceed the team's n_max");
-    TeamGather g{};
-    g.team_y = t->dev_y;
-    g.team_state = reinterpret_cast<uint32_t*>(t->local + t->staging_bytes);
-    g.world = t->world;
-    g.rank = t->rank;
-    g.half = t->n_max;
-    g.src = src;
-    g.n_local = n_local;
-    g.offset = offset;
-    g.n = n;
-    g.dst = dst;
-    cudaError_t e = launch_team_gather(g, static_cast<cudaStream_t>(stream));
-    if (e != cudaSuccess) return cuda_err(e, "team_gather launch");
+    if (n == 0 || n > t->n_max || offset + n_local > n || src_stride < n_local || dst_stride < n)
+        return set_error(TSRC_E_ARG, "team_gather: sizes exceed the team's n_max");
+    const uint32_t per = t->n_max / n;                   // token rows per step
+    for (uint32_t t0 = 0; t0 < T; t0 += per) {
+        TeamGather g{};
+        g.team_y = t->dev_y;
+        g.team_state = reinterpret_cast<uint32_t*>(t->local + t->staging_bytes);
+        g.world = t->world;
+        g.rank = t->rank;
+        g.half = t->n_max;
+        g.src = src + (size_t)t0 * src_stride;
+        g.n_local = n_local;
+        g.offset = offset;
+        g.n = n;
+        g.dst = dst + (size_t)t0 * dst_stride;
+        g.T = T - t0 < per ? T - t0 : per;
+        g.src_stride = src_stride;
+        g.dst_stride = dst_stride;
+        cudaError_t e = launch_team_gather(g, static_cast<cudaStream_t>(stream));
+        if (e != cudaSuccess) return cuda_err(e, "team_gather launch");
+    }
     return TSRC_OK;
 }
 

@@ -1,9 +1,12 @@
-"""Tensor-parallel decode (tsrc_model_create_tp) against the single-GPU model, bit for bit: both get
-the same KV cache cells (seeded rows through KVST; a rank's cache holds its KV heads' columns), then
-decode tokens eagerly and through the captured decode graph. On one GPU a team of one runs every
-step of the tensor-parallel path (shards, the tagged-word gathers, the fused gathers of o, down and
-the head); on two GPUs (skipped when the box has one) two processes, one per GPU, each hold half the
-heads and rows."""
+"""Tensor-parallel decode and prefill (tsrc_model_create_tp) against the single-GPU model, bit for
+bit. Decode: both get the same KV cache cells (seeded rows through KVST; a rank's cache holds its KV
+heads' columns), then decode tokens eagerly and through the captured decode graph. Prefill: two
+prompt chunks (12 tokens at position 0, then 9 at position 12: the tensor-core MUL_MATs of the
+rank's rows and the gathers of token rows, several team steps per gather since the team's n_max
+holds only one or two rows) and then decode tokens. On one GPU a team of one runs every step of the
+tensor-parallel path (shards, the tagged-word gathers, the fused gathers of o, down and the head);
+on two GPUs (skipped when the box has one) two processes, one per GPU, each hold half the heads and
+rows."""
 import os
 import socket
 
@@ -55,6 +58,26 @@ def decode_run(torch, dev, model, shape, steps=4):
     return out
 
 
+def prefill_run(torch, dev, model, shape, steps=2):
+    """Two prompt chunks through tsrc_model_forward, then greedy decode; the logits of each call."""
+    out = []
+    logits = torch.full((shape["n_vocab"],), float("nan"), device="cuda")
+    ids = torch.from_numpy(np.random.default_rng(5).integers(0, shape["n_vocab"], 21).astype(np.int32)).cuda()
+    for t0, T in ((0, 12), (12, 9)):
+        model.forward(ids[t0:t0 + T], T, t0, logits)
+        dev.sync()
+        out.append(logits.cpu().numpy().copy())
+    one = torch.zeros(1, dtype=torch.int32, device="cuda")
+    pos = 21
+    for _ in range(steps):
+        one.fill_(int(np.argmax(out[-1])))
+        model.decode(one, pos, logits)
+        dev.sync()
+        out.append(logits.cpu().numpy().copy())
+        pos += 1
+    return out
+
+
 def n_max_of(shape):
     return max(shape["n_vocab"], shape["n_ff"], shape["n_head"] * shape["head_dim"], shape["n_embd"])
 
@@ -83,13 +106,35 @@ def test_team_of_one_equals_single_gpu(dev, name):
         team.free()
 
 
+@pytest.mark.parametrize("name", sorted(SHAPES))
+def test_team_of_one_prefill_equals_single_gpu(dev, name):
+    import torch
+    shape = SHAPES[name]
+    cfg = tsrc.ModelCfg(**shape)
+    single = tsrc.Model(dev, cfg, seed=13)
+    team = dev.team_create(0, 1, n_max_of(shape))
+    tp = None
+    try:
+        team.connect_local([team])
+        tp = tsrc.Model(dev, cfg, seed=13, team=team)
+        want = prefill_run(torch, dev, single, shape)
+        got = prefill_run(torch, dev, tp, shape)
+        for a, b in zip(got, want):
+            np.testing.assert_array_equal(a.view(np.uint32), b.view(np.uint32))
+    finally:
+        if tp is not None:
+            tp.free()
+        single.free()
+        team.free()
+
+
 def _free_port():
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
         return s.getsockname()[1]
 
 
-def _rank(rank, world, port, out_dir, name):
+def _rank(rank, world, port, out_dir, name, mode):
     import sys
     import datetime
     here = os.path.dirname(os.path.abspath(__file__))
@@ -111,11 +156,15 @@ def _rank(rank, world, port, out_dir, name):
         dist.all_gather_object(hs, team.ipc_handle)
         team.connect(b"".join(hs))
         tp = T.Model(dev, cfg, seed=11, team=team)
-        fill_caches(torch, tp, shape, rank, world)
-        got = decode_run(torch, dev, tp, shape)
         single = T.Model(dev, cfg, seed=11)
-        fill_caches(torch, single, shape, 0, 1)
-        want = decode_run(torch, dev, single, shape)
+        if mode == "prefill":
+            got = prefill_run(torch, dev, tp, shape)
+            want = prefill_run(torch, dev, single, shape)
+        else:
+            fill_caches(torch, tp, shape, rank, world)
+            got = decode_run(torch, dev, tp, shape)
+            fill_caches(torch, single, shape, 0, 1)
+            want = decode_run(torch, dev, single, shape)
         ok = all(np.array_equal(a.view(np.uint32), b.view(np.uint32)) for a, b in zip(got, want))
         dist.barrier()
         single.free()
@@ -129,12 +178,13 @@ def _rank(rank, world, port, out_dir, name):
         dist.destroy_process_group()
 
 
+@pytest.mark.parametrize("mode", ["decode", "prefill"])
 @pytest.mark.parametrize("name", sorted(SHAPES))
-def test_two_gpus_equal_single_gpu(tmp_path, name):
+def test_two_gpus_equal_single_gpu(tmp_path, name, mode):
     import torch
     import torch.multiprocessing as mp
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
-    mp.start_processes(_rank, args=(2, _free_port(), str(tmp_path), name), nprocs=2, start_method="spawn", join=True)
+    mp.start_processes(_rank, args=(2, _free_port(), str(tmp_path), name, mode), nprocs=2, start_method="spawn", join=True)
     for r in range(2):
         assert (tmp_path / f"rank{r}.txt").read_text() == "ok", f"rank {r}"
