@@ -33,8 +33,9 @@ namespace tsrc {
 
 namespace {
 
-constexpr uint32_t kFaWarps = 16;
-constexpr uint32_t kFaThreads = kFaWarps * 32u;
+// Warps of a chunk CTA: 16 for few large items (decode: the latency of one item matters), 4 for
+// many small ones (a prompt's query tiles: several CTAs per SM hide each other's latency).
+constexpr uint32_t kFaWarpsLarge = 16, kFaWarpsSmall = 4;
 constexpr uint32_t kNegInf = 0xFF800000u;
 constexpr uint32_t kMFloor = 0xF1800000u;      // -2^100: MAXOUT's floor (sw/sim/include/tsr_tables.h:89)
 constexpr uint32_t kLFloor = 0x00800000u;      // 2^-126: ANORM's floor of the row sum (tsr_tables.h:90)
@@ -138,12 +139,12 @@ __host__ __device__ inline uint32_t fa_a16(uint32_t n) { return (n + 15u) & ~15u
 // values of a 64-cell segment whose V quants one warp stages: its 64-value slice (4 KB)
 __host__ __device__ inline uint32_t fa_vp(uint32_t) { return 64u; }
 // segments a round of the P.V phase runs at once: one warp per (segment, 64-value slice)
-__host__ __device__ inline uint32_t fa_segs(uint32_t D) { return kFaWarps / (D / 64u); }
+__host__ __device__ inline uint32_t fa_segs(uint32_t D, uint32_t W) { return W / (D / 64u); }
 // rows of a W-digit table: RB rows x 4 digits (an 8-wide tensor-core tile wraps around a 4-row
 // table; the extra output columns are not used)
 __host__ __device__ inline uint32_t fa_wd_rows(uint32_t D) { return 4u * (512u / D); }
 
-__host__ __device__ inline FaSmem fa_smem(uint32_t D, uint32_t ncell_max) {
+__host__ __device__ inline FaSmem fa_smem(uint32_t D, uint32_t ncell_max, uint32_t W) {
     const uint32_t RB = 512u / D, ND = D / 32u;
     FaSmem s{};
     uint32_t o = fa_a16(64u * 4u + 4u * 8u);                    // EXPK tables
@@ -154,16 +155,16 @@ __host__ __device__ inline FaSmem fa_smem(uint32_t D, uint32_t ncell_max) {
     s.s_off = o;
     o += fa_a16(RB * ncell_max * 4u);                           // S [RB][ncell_max]
     s.w_off = o;
-    o += fa_a16(kFaWarps * 2u * fa_wd_rows(D) * kWdStride);     // W digits [warp][2][rows][kWdStride] (its slice)
+    o += fa_a16(W * 2u * fa_wd_rows(D) * kWdStride);            // W digits [warp][2][rows][kWdStride] (its slice)
     s.cv_off = o;
-    o += fa_a16(fa_segs(D) * RB * D * 4u);                      // CV [segment of the round][RB][D]
+    o += fa_a16(fa_segs(D, W) * RB * D * 4u);                   // CV [segment of the round][RB][D]
     s.vq_off = o;
-    o += fa_a16(kFaWarps * 64u * fa_vp(D));                     // V quants of a segment [warp][4 groups][VP][16]
+    o += fa_a16(W * 64u * fa_vp(D));                            // V quants of a segment [warp][4 groups][VP][16]
     s.vs_off = o;
-    o += fa_a16(kFaWarps * 64u * ND * 2u);                      // V scales of a segment [warp][64][ND]
+    o += fa_a16(W * 64u * ND * 2u);                             // V scales of a segment [warp][64][ND]
     s.misc_off = o;
     // mx [2][RB] (max keys), mk [RB], ls [segments][RB], lacc [RB], es [warps][RB], fl [warps][RB]
-    o += 4u * (2u * RB + RB + kFaWarps * RB + RB + 2u * kFaWarps * RB);
+    o += 4u * (2u * RB + RB + W * RB + RB + 2u * W * RB);
     s.total = fa_a16(o);
     return s;
 }
@@ -181,8 +182,9 @@ __device__ __forceinline__ void cluster_arrive() { asm volatile("barrier.cluster
 __device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
 
 // ---------------------------------------------------------------------------------------------------
-template <int D>
-__global__ void __launch_bounds__(kFaThreads, 1) fa_chunk_kernel(FaLaunch a) {
+template <int D, uint32_t W>
+__global__ void __launch_bounds__(W * 32u, W <= kFaWarpsSmall ? 4 : 1) fa_chunk_kernel(FaLaunch a) {
+    constexpr uint32_t kFaWarps = W, kFaThreads = W * 32u;
     constexpr uint32_t ND = D / 32, NSL = D / 64, RB = 512 / D;
     extern __shared__ __align__(16) uint8_t smem[];
     cg::cluster_group cluster = cg::this_cluster();
@@ -197,9 +199,10 @@ __global__ void __launch_bounds__(kFaThreads, 1) fa_chunk_kernel(FaLaunch a) {
     const uint32_t nu = ufirst < it.u0 + it.n ? (it.u0 + it.n - ufirst + C - 1u) / C : 0u;
     const uint32_t ncell = 16u * nu;
     const uint32_t ncell_max = 16u * ((it.n + C - 1u) / C);
-    const FaSmem P = fa_smem(D, ncell_max);
+    const FaSmem P = fa_smem(D, ncell_max, W);
     constexpr uint32_t VP = 64u;                               // fa_vp(D): a warp's 64-value slice
-    constexpr uint32_t SEGS = kFaWarps / NSL;                  // fa_segs(D)
+    constexpr uint32_t SEGS = kFaWarps / NSL;                  // fa_segs(D, W)
+    static_assert(SEGS >= 1, "a round needs at least one segment");
     const uint32_t wseg = warp / NSL, wsl = warp - wseg * NSL; // the warp's segment of a round and slice
     constexpr uint32_t kWdRows = 4u * RB;                      // fa_wd_rows(D)
     constexpr uint32_t kNT = kWdRows < 8u ? 1u : kWdRows / 8u; // 8-wide tensor-core tiles of the W digits
@@ -694,27 +697,27 @@ __global__ void fa_maskf_kernel(const uint16_t* m16, uint32_t stride, uint32_t T
 
 // The kernel's attributes, set once per device: the largest shared-memory plan any call can need
 // and non-portable cluster sizes (C up to 16).
-template <int D>
+template <int D, uint32_t W>
 cudaError_t fa_attributes() {
     static int done_dev[64];
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
     if (dev < 64 && done_dev[dev] == dev + 1) return cudaSuccess;
-    e = cudaFuncSetAttribute(fa_chunk_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(227u * 1024u));
-    if (e == cudaSuccess) e = cudaFuncSetAttribute(fa_chunk_kernel<D>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    e = cudaFuncSetAttribute(fa_chunk_kernel<D, W>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(227u * 1024u));
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(fa_chunk_kernel<D, W>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
     if (e == cudaSuccess && dev < 64) done_dev[dev] = dev + 1;
     return e;
 }
 
-template <int D>
-cudaError_t launch_chunks(const FaLaunch& a, uint32_t ncell_max, cudaStream_t st) {
-    const FaSmem P = fa_smem(D, ncell_max);
-    cudaError_t e = fa_attributes<D>();
+template <int D, uint32_t W>
+cudaError_t launch_chunks_w(const FaLaunch& a, uint32_t ncell_max, cudaStream_t st) {
+    const FaSmem P = fa_smem(D, ncell_max, W);
+    cudaError_t e = fa_attributes<D, W>();
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(a.n_items * a.n_head_kv * a.C);
-    cfg.blockDim = dim3(kFaThreads);
+    cfg.blockDim = dim3(W * 32u);
     cfg.dynamicSmemBytes = P.total;
     cfg.stream = st;
     cudaLaunchAttribute attr[2];
@@ -728,17 +731,29 @@ cudaError_t launch_chunks(const FaLaunch& a, uint32_t ncell_max, cudaStream_t st
     cfg.numAttrs = 2;
     if (a.C > 8) {        // a non-portable cluster size: make sure one cluster can be resident
         int n = 0;
-        e = cudaOccupancyMaxActiveClusters(&n, (const void*)fa_chunk_kernel<D>, &cfg);
+        e = cudaOccupancyMaxActiveClusters(&n, (const void*)fa_chunk_kernel<D, W>, &cfg);
         if (e != cudaSuccess) return e;
         if (n == 0) return cudaErrorInvalidConfiguration;
     }
-    return cudaLaunchKernelEx(&cfg, fa_chunk_kernel<D>, a);
+    return cudaLaunchKernelEx(&cfg, fa_chunk_kernel<D, W>, a);
+}
+
+// 4-warp CTAs when the call has enough of them to fill every SM four times over (a prompt), else
+// 16-warp CTAs (decode)
+template <int D>
+cudaError_t launch_chunks(const FaLaunch& a, uint32_t ncell_max, cudaStream_t st) {
+    if constexpr (D <= 256) {
+        int dev = 0, sms = 148;
+        if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        if ((uint64_t)a.n_items * a.n_head_kv * a.C >= 4u * (uint64_t)sms) return launch_chunks_w<D, kFaWarpsSmall>(a, ncell_max, st);
+    }
+    return launch_chunks_w<D, kFaWarpsLarge>(a, ncell_max, st);
 }
 
 }  // namespace
 
 size_t fa_smem_bytes(uint32_t D, uint32_t n_max_groups, uint32_t C) {
-    return fa_smem(D, 16u * ((n_max_groups + C - 1u) / C)).total;
+    return fa_smem(D, 16u * ((n_max_groups + C - 1u) / C), kFaWarpsLarge).total;
 }
 
 cudaError_t launch_fa_maskf(const uint16_t* m16, uint32_t stride, uint32_t T, uint32_t n_kv, float scale, float* out,
@@ -751,12 +766,15 @@ cudaError_t launch_fa_maskf(const uint16_t* m16, uint32_t stride, uint32_t T, ui
 
 const void* fa_merge_fn(uint32_t C) { return C >= 1u && C <= 16u ? reinterpret_cast<const void*>(kMerge[C - 1u]) : nullptr; }
 
-const void* fa_chunk_fn(uint32_t D) {
+const void* fa_chunk_fn(uint32_t D, bool small) {
     switch (D) {
-        case 64: return reinterpret_cast<const void*>(fa_chunk_kernel<64>);
-        case 128: return reinterpret_cast<const void*>(fa_chunk_kernel<128>);
-        case 256: return reinterpret_cast<const void*>(fa_chunk_kernel<256>);
-        case 512: return reinterpret_cast<const void*>(fa_chunk_kernel<512>);
+        case 64: return small ? reinterpret_cast<const void*>(fa_chunk_kernel<64, kFaWarpsSmall>)
+                              : reinterpret_cast<const void*>(fa_chunk_kernel<64, kFaWarpsLarge>);
+        case 128: return small ? reinterpret_cast<const void*>(fa_chunk_kernel<128, kFaWarpsSmall>)
+                               : reinterpret_cast<const void*>(fa_chunk_kernel<128, kFaWarpsLarge>);
+        case 256: return small ? reinterpret_cast<const void*>(fa_chunk_kernel<256, kFaWarpsSmall>)
+                               : reinterpret_cast<const void*>(fa_chunk_kernel<256, kFaWarpsLarge>);
+        case 512: return small ? nullptr : reinterpret_cast<const void*>(fa_chunk_kernel<512, kFaWarpsLarge>);
         default: return nullptr;
     }
 }

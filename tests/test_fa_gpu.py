@@ -79,12 +79,13 @@ def test_fa_special_values(dev, tsro):
     np.testing.assert_array_equal(got.view(np.uint32), want.view(np.uint32))
 
 
-@pytest.mark.parametrize("shape", ["cfg4", "cfg5"])
+@pytest.mark.parametrize("shape", ["cfg4", "cfg5", "d256"])
 def test_fa_prefill_bench_shapes(dev, tsro, shape):
     """Prefill attention of the bench's models at their prompt lengths, all query rows: config 4
     (Qwen2.5-0.5B: 14 q / 2 KV heads of 64, 512 tokens) and config 5 (Llama-3-8B: 32 q / 8 KV heads
-    of 128, 2048 tokens), causal from position 0, the release attention configuration."""
-    D, nkvh, G, T, seed = {"cfg4": (64, 2, 7, 512, 81), "cfg5": (128, 8, 4, 2048, 85)}[shape]
+    of 128, 2048 tokens), causal from position 0, the release attention configuration; and a head
+    size of 256 (4 KV heads, 300 tokens). Calls with this many work items run the 4-warp chunk CTAs."""
+    D, nkvh, G, T, seed = {"cfg4": (64, 2, 7, 512, 81), "cfg5": (128, 8, 4, 2048, 85), "d256": (256, 4, 2, 300, 89)}[shape]
     E = nkvh * D
     k = H.kv_rows(tsro, T, E, seed)
     v = H.kv_rows(tsro, T, E, seed + 1)
