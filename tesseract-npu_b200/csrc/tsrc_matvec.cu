@@ -585,9 +585,12 @@ __device__ __forceinline__ unsigned long long ld_relaxed_sys64(const unsigned lo
     return v;
 }
 
-__device__ __forceinline__ void team_finish(const MvArgs& a, uint32_t step, uint32_t* sflag, const float* rows,
+// step: the team step this launch read after its wait for the previous kernel; or, with step_smem,
+// the shared-memory word where one thread stored it (read after the barrier)
+__device__ __forceinline__ void team_finish(const MvArgs& a, uint32_t step, const uint32_t* step_smem, const float* rows,
                                             uint32_t r_begin, uint32_t r_end) {
-    __syncthreads();                                     // the CTA's rows are in shared memory
+    __syncthreads();                                     // the CTA's rows (and step_smem) are in shared memory
+    if (step_smem) step = *step_smem;
     const unsigned long long tag = (unsigned long long)(step + 1u) << 32;
     const size_t o = (size_t)(step & 1u) * a.team_half + a.team_row0 + r_begin;
     for (uint32_t r = 0; r < a.team_world; ++r)
@@ -617,7 +620,6 @@ __device__ __forceinline__ void team_finish(const MvArgs& a, uint32_t step, uint
         a.team_state[1] = 0u;
         a.team_state[0] = step + 1u;
     }
-    (void)sflag;
 }
 
 // The same exchange for plain vectors: T token rows, each of n values of which this rank holds
@@ -711,7 +713,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) matvec_kernel(MvArgs a, 
     if (stage_qa<FMT>(a, qa, L, flags)) stream_rows<FMT, MAXT, true>(a, qa, r_begin, r_end, warp, lane, team_rows);
     else stream_rows<FMT, MAXT, false>(a, qa, r_begin, r_end, warp, lane, team_rows);
     if (a.team_world)
-        team_finish(a, team_step, reinterpret_cast<uint32_t*>(smem + a16(P.qa_bytes(a.T))), team_rows,
+        team_finish(a, team_step, nullptr, team_rows,
                     a.swiglu_pairs ? r_begin / 2u : r_begin, a.swiglu_pairs ? r_end / 2u : r_end);
 }
 
@@ -1171,13 +1173,15 @@ __global__ void __launch_bounds__(Shape<NW>::kThreads, Shape<NW>::kMinBlocks) de
     }
     __syncthreads();
     asm volatile("griddepcontrol.launch_dependents;");
-    const uint32_t team_step = (EPI == 1 && a.team_world) ? *reinterpret_cast<volatile uint32_t*>(a.team_state) : 0u;
     uint32_t* flags = reinterpret_cast<uint32_t*>(smem + P.flags_off);
     float* team_rows = reinterpret_cast<float*>(smem + P.team_off);
     if (warp == kWarps) {
         produce<RING>(a, P, slots, full, empty, r_begin, n);        // weights only: no wait for the previous kernel
     } else {
         asm volatile("griddepcontrol.wait;" ::: "memory");
+        // the team step, read only once the previous kernel (possibly a team launch that advances
+        // it) has completed; the producer warp, which never waits, takes it from shared memory
+        if (EPI == 1 && a.team_world && tid == 0) flags[NW] = *reinterpret_cast<volatile uint32_t*>(a.team_state);
         uint8_t* q = smem;
         float* d = reinterpret_cast<float*>(smem + P.qa_q);
         uint8_t* bs = smem + P.qa_q + P.qa_d;
@@ -1204,7 +1208,7 @@ __global__ void __launch_bounds__(Shape<NW>::kThreads, Shape<NW>::kMinBlocks) de
         else consume<FMT, XR, FULL, false, RING, EPI, NW>(a, P, slots, full, empty, r_begin, n, q, d, bs, xr, team_rows);
     }
     if (EPI == 1 && a.team_world)
-        team_finish(a, team_step, flags, team_rows, a.swiglu_pairs ? r_begin / 2u : r_begin,
+        team_finish(a, 0u, flags + NW, team_rows, a.swiglu_pairs ? r_begin / 2u : r_begin,
                     a.swiglu_pairs ? (r_begin + n) / 2u : r_begin + n);
 }
 
@@ -1321,7 +1325,7 @@ static cudaError_t launch_dec_nw(uint32_t fmt, const MvArgs& a, int dev, uint32_
     P.qa_d = (uint32_t)a16((size_t)G.nb * 4u);
     const uint32_t qa_bs = fmt == 0 ? 0u : G.tiles * 256u;
     P.flags_off = (uint32_t)a16((size_t)P.qa_q + P.qa_d + qa_bs);
-    P.team_off = P.flags_off + 4u * NW;
+    P.team_off = P.flags_off + 4u * NW + 16u;           // NW warp flags, then the team step
     const uint32_t team_bytes = a.team_world ? 4u * P.rpc : 0u;
     P.slots_off = (P.team_off + team_bytes + 127u) & ~127u;
     // the CTA's budget: the opt-in maximum, or half an SM's shared memory for two CTAs per SM
