@@ -33,9 +33,9 @@ namespace tsrc {
 
 namespace {
 
-// Warps of a chunk CTA: 16 for few large items (decode: the latency of one item matters), 4 for
-// many small ones (a prompt's query tiles: several CTAs per SM hide each other's latency).
-constexpr uint32_t kFaWarpsLarge = 16, kFaWarpsSmall = 4;
+// Warps of a chunk CTA: 16 for few large items (decode: the latency of one item matters), 4 or 2
+// for many small ones (a prompt's query tiles: four or eight CTAs per SM hide each other's latency).
+constexpr uint32_t kFaWarpsLarge = 16, kFaWarpsSmall = 4, kFaWarpsTiny = 2;
 constexpr uint32_t kNegInf = 0xFF800000u;
 constexpr uint32_t kMFloor = 0xF1800000u;      // -2^100: MAXOUT's floor (sw/sim/include/tsr_tables.h:89)
 constexpr uint32_t kLFloor = 0x00800000u;      // 2^-126: ANORM's floor of the row sum (tsr_tables.h:90)
@@ -183,7 +183,7 @@ __device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.w
 
 // ---------------------------------------------------------------------------------------------------
 template <int D, uint32_t W>
-__global__ void __launch_bounds__(W * 32u, W <= kFaWarpsSmall ? 4 : 1) fa_chunk_kernel(FaLaunch a) {
+__global__ void __launch_bounds__(W * 32u, W <= kFaWarpsTiny ? 8 : (W <= kFaWarpsSmall ? 4 : 1)) fa_chunk_kernel(FaLaunch a) {
     constexpr uint32_t kFaWarps = W, kFaThreads = W * 32u;
     constexpr uint32_t ND = D / 32, NSL = D / 64, RB = 512 / D;
     extern __shared__ __align__(16) uint8_t smem[];
@@ -738,14 +738,17 @@ cudaError_t launch_chunks_w(const FaLaunch& a, uint32_t ncell_max, cudaStream_t 
     return cudaLaunchKernelEx(&cfg, fa_chunk_kernel<D, W>, a);
 }
 
-// 4-warp CTAs when the call has enough of them to fill every SM four times over (a prompt), else
-// 16-warp CTAs (decode)
+// 2-warp CTAs (head sizes up to 128) when the call has enough of them to fill every SM eight times
+// over, 4-warp CTAs at four times (a prompt), else 16-warp CTAs (decode)
 template <int D>
 cudaError_t launch_chunks(const FaLaunch& a, uint32_t ncell_max, cudaStream_t st) {
     if constexpr (D <= 256) {
         int dev = 0, sms = 148;
         if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-        if ((uint64_t)a.n_items * a.n_head_kv * a.C >= 4u * (uint64_t)sms) return launch_chunks_w<D, kFaWarpsSmall>(a, ncell_max, st);
+        const uint64_t ctas = (uint64_t)a.n_items * a.n_head_kv * a.C;
+        if constexpr (D <= 128)
+            if (ctas >= 8u * (uint64_t)sms) return launch_chunks_w<D, kFaWarpsTiny>(a, ncell_max, st);
+        if (ctas >= 4u * (uint64_t)sms) return launch_chunks_w<D, kFaWarpsSmall>(a, ncell_max, st);
     }
     return launch_chunks_w<D, kFaWarpsLarge>(a, ncell_max, st);
 }
@@ -766,15 +769,19 @@ cudaError_t launch_fa_maskf(const uint16_t* m16, uint32_t stride, uint32_t T, ui
 
 const void* fa_merge_fn(uint32_t C) { return C >= 1u && C <= 16u ? reinterpret_cast<const void*>(kMerge[C - 1u]) : nullptr; }
 
-const void* fa_chunk_fn(uint32_t D, bool small) {
+const void* fa_chunk_fn(uint32_t D, uint32_t warps) {
+    const bool small = warps == kFaWarpsSmall, tiny = warps == kFaWarpsTiny;
     switch (D) {
-        case 64: return small ? reinterpret_cast<const void*>(fa_chunk_kernel<64, kFaWarpsSmall>)
+        case 64: return tiny ? reinterpret_cast<const void*>(fa_chunk_kernel<64, kFaWarpsTiny>)
+                      : small ? reinterpret_cast<const void*>(fa_chunk_kernel<64, kFaWarpsSmall>)
                               : reinterpret_cast<const void*>(fa_chunk_kernel<64, kFaWarpsLarge>);
-        case 128: return small ? reinterpret_cast<const void*>(fa_chunk_kernel<128, kFaWarpsSmall>)
+        case 128: return tiny ? reinterpret_cast<const void*>(fa_chunk_kernel<128, kFaWarpsTiny>)
+                       : small ? reinterpret_cast<const void*>(fa_chunk_kernel<128, kFaWarpsSmall>)
                                : reinterpret_cast<const void*>(fa_chunk_kernel<128, kFaWarpsLarge>);
-        case 256: return small ? reinterpret_cast<const void*>(fa_chunk_kernel<256, kFaWarpsSmall>)
+        case 256: return tiny ? nullptr
+                       : small ? reinterpret_cast<const void*>(fa_chunk_kernel<256, kFaWarpsSmall>)
                                : reinterpret_cast<const void*>(fa_chunk_kernel<256, kFaWarpsLarge>);
-        case 512: return small ? nullptr : reinterpret_cast<const void*>(fa_chunk_kernel<512, kFaWarpsLarge>);
+        case 512: return (small || tiny) ? nullptr : reinterpret_cast<const void*>(fa_chunk_kernel<512, kFaWarpsLarge>);
         default: return nullptr;
     }
 }

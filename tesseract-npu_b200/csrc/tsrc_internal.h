@@ -165,8 +165,8 @@ struct FaLaunch {
 
 cudaError_t launch_fa(const FaLaunch& a, uint32_t n_max_groups, cudaStream_t st);
 // the kernels launch_fa runs (to find their nodes in a captured CUDA graph)
-// the chunk kernel of head size D: 16-warp CTAs, or (small) the 4-warp ones of calls with many items
-const void* fa_chunk_fn(uint32_t D, bool small);
+// the chunk kernel of head size D with CTAs of `warps` warps (16; 4 or 2 for calls with many items)
+const void* fa_chunk_fn(uint32_t D, uint32_t warps);
 const void* fa_merge_fn(uint32_t C);
 // tsrc_flash_attn up to the kernel launches (tsrc_api.cu)
 int fa_setup(::tsrc_ctx* ctx, const ::tsrc_kv* kv, const float* q, uint32_t T, uint32_t n_head, uint32_t n_kv,

@@ -542,8 +542,9 @@ int capture_decode(tsrc_model* m, const int32_t* ids, uint32_t pos0, float* logi
     cudaGraphGetNodes(g, nullptr, &n);
     std::vector<cudaGraphNode_t> nodes(n);
     cudaGraphGetNodes(g, nodes.data(), &n);
-    const void* fchunk = tsrc::fa_chunk_fn(m->c.head_dim, false);
-    const void* fchunk_s = tsrc::fa_chunk_fn(m->c.head_dim, true);
+    const void* fchunk = tsrc::fa_chunk_fn(m->c.head_dim, 16u);
+    const void* fchunk_s = tsrc::fa_chunk_fn(m->c.head_dim, 4u);
+    const void* fchunk_t = tsrc::fa_chunk_fn(m->c.head_dim, 2u);
     const void* fmerge = tsrc::fa_merge_fn(a0.C);
     const void* fstate = reinterpret_cast<const void*>(model_state_kernel);
     for (cudaGraphNode_t nd : nodes) {
@@ -551,7 +552,7 @@ int capture_decode(tsrc_model* m, const int32_t* ids, uint32_t pos0, float* logi
         if (cudaGraphNodeGetType(nd, &t) != cudaSuccess || t != cudaGraphNodeTypeKernel) continue;
         cudaKernelNodeParams p{};
         if (cudaGraphKernelNodeGetParams(nd, &p) != cudaSuccess) continue;
-        if (p.func == fchunk || (fchunk_s && p.func == fchunk_s) || p.func == fmerge) {
+        if (p.func == fchunk || (fchunk_s && p.func == fchunk_s) || (fchunk_t && p.func == fchunk_t) || p.func == fmerge) {
             tsrc_model::FaNode f;
             f.node = nd;
             f.params = p;
