@@ -738,8 +738,8 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) matvec_kernel(MvArgs a, 
 namespace dec {
 
 // NW consumer warps + one producer warp; rows per chunk at most 2 NW (one pair per consumer warp).
-// NW = 16 uses a whole SM; NW = 8 uses at most half of one (registers and shared memory), so the
-// next launch's CTA can stage its first chunks beside the running one.
+// NW = 16 (x of a one-unit row in registers) or 24 (x read from shared memory); either uses a
+// whole SM.
 template <int NW>
 struct Shape {
     static constexpr uint32_t kThreads = (NW + 1u) * 32u;
@@ -1024,7 +1024,7 @@ __device__ __forceinline__ bool consume(const MvArgs& a, const Plan& P, uint8_t*
     for (uint32_t rg = 0; rg < ngroups; ++rg, row0 += P.R) {
         // the row group's pairs go to warps (pair mod 16): this warp's pair, if any
         const uint32_t p0 = row0 >> 1;
-        const uint32_t pr = p0 + ((warp + kWarps - (p0 & (kWarps - 1u))) & (kWarps - 1u));
+        const uint32_t pr = p0 + ((warp + kWarps - (p0 % kWarps)) % kWarps);
         const uint32_t r = 2u * pr + h;          // the lane's row within the CTA
         const bool has = pr < min(npairs, p0 + (P.R >> 1)), rv = r < n;
         for (uint32_t kc = 0; kc < P.kchunks; ++kc, ++c) {
@@ -1310,8 +1310,7 @@ static cudaError_t dec_launch_ring(const MvArgs& a, const dec::Plan& P, uint32_t
 
 // One token with QACT fused (a.x set): rows split evenly over the SMs in pairs; the CTA's rows all
 // resident in shared memory when they fit its budget, else chunks of whole rows (or of one unit of
-// 2 NW rows, for rows too long for three chunks) through a ring. NW = 8 keeps every CTA within half
-// an SM (the next launch's CTA stages its first chunks while this one runs); NW = 16 uses the SM.
+// 2 NW rows, for rows too long for three chunks) through a ring.
 template <int NW>
 static cudaError_t launch_dec_nw(uint32_t fmt, const MvArgs& a, int dev, uint32_t sms, cudaStream_t st) {
     using S = dec::Shape<NW>;
@@ -1373,11 +1372,11 @@ static cudaError_t launch_dec_nw(uint32_t fmt, const MvArgs& a, int dev, uint32_
     // every unit of every row complete (no partial tile, no missing tile of a unit)
     const bool full = (G.nb % (16u * G.tpu)) == 0;
     const bool xr = fmt == 0 ? G.tiles <= dec::kTpuQ8 : G.tiles == 1;
-    if (fmt == 0) {
-        if (xr) return full ? dec_launch_ring<0, true, true, NW>(a, P, blocks, smem, dev, st) : dec_launch_ring<0, true, false, NW>(a, P, blocks, smem, dev, st);
-        return full ? dec_launch_ring<0, false, true, NW>(a, P, blocks, smem, dev, st) : dec_launch_ring<0, false, false, NW>(a, P, blocks, smem, dev, st);
+    if constexpr (NW == 16) {       // x in registers needs the register budget of 17 warps
+        if (fmt == 0 && xr) return full ? dec_launch_ring<0, true, true, NW>(a, P, blocks, smem, dev, st) : dec_launch_ring<0, true, false, NW>(a, P, blocks, smem, dev, st);
+        if (fmt == 1 && xr) return full ? dec_launch_ring<1, true, true, NW>(a, P, blocks, smem, dev, st) : dec_launch_ring<1, true, false, NW>(a, P, blocks, smem, dev, st);
     }
-    if (xr) return full ? dec_launch_ring<1, true, true, NW>(a, P, blocks, smem, dev, st) : dec_launch_ring<1, true, false, NW>(a, P, blocks, smem, dev, st);
+    if (fmt == 0) return full ? dec_launch_ring<0, false, true, NW>(a, P, blocks, smem, dev, st) : dec_launch_ring<0, false, false, NW>(a, P, blocks, smem, dev, st);
     return full ? dec_launch_ring<1, false, true, NW>(a, P, blocks, smem, dev, st) : dec_launch_ring<1, false, false, NW>(a, P, blocks, smem, dev, st);
 }
 
@@ -1399,6 +1398,12 @@ static cudaError_t launch_dec(uint32_t fmt, const MvArgs& a, cudaStream_t st) {
         g_smem_sm[dev] = m;
         g_smem_optin[dev] = n - 1024;          // room for the kernel's static shared memory
     }
+    // rows whose activation slice fits a lane's registers (one Q4_K tile, up to four Q8_0 tiles) run
+    // 16 consumer warps with x in registers; longer rows read x from shared memory, and then 24
+    // warps (fewer registers each) keep more row pairs in flight
+    const dec::Geo G(fmt, a.K);
+    const bool xr = fmt == 0 ? G.tiles <= dec::kTpuQ8 : G.tiles == 1;
+    if (!xr) return launch_dec_nw<24>(fmt, a, dev, (uint32_t)g_num_sms[dev], st);
     return launch_dec_nw<16>(fmt, a, dev, (uint32_t)g_num_sms[dev], st);
 }
 
