@@ -889,22 +889,36 @@ __device__ __forceinline__ bool stage_x1(const MvArgs& a, uint8_t* q, float* d, 
             }
         }
     } else {
-        for (uint32_t i = warp; i < nb; i += kWarps) {
-            float v[8];
-            const float* src = a.x + 256u * i + 8u * lane;
-            if ((reinterpret_cast<uintptr_t>(src) & 15u) == 0) {
-                const float4 f0 = reinterpret_cast<const float4*>(src)[0], f1 = reinterpret_cast<const float4*>(src)[1];
-                v[0] = f0.x; v[1] = f0.y; v[2] = f0.z; v[3] = f0.w;
-                v[4] = f1.x; v[5] = f1.y; v[6] = f1.z; v[7] = f1.w;
-            } else {
+        // a warp's superblocks B at a time: every load of the batch is issued before the first
+        // quantization, so long rows (several superblocks per warp) wait for one load latency
+        constexpr uint32_t B = 3;
+        for (uint32_t i0 = warp; i0 < nb; i0 += B * kWarps) {
+            float v[B][8];
 #pragma unroll
-                for (int e = 0; e < 8; ++e) v[e] = src[e];
-            }
-            if (rms) {
+            for (uint32_t j = 0; j < B; ++j) {
+                const uint32_t i = i0 + j * kWarps;
+                if (i >= nb) break;
+                const float* src = a.x + 256u * i + 8u * lane;
+                if ((reinterpret_cast<uintptr_t>(src) & 15u) == 0) {
+                    const float4 f0 = reinterpret_cast<const float4*>(src)[0], f1 = reinterpret_cast<const float4*>(src)[1];
+                    v[j][0] = f0.x; v[j][1] = f0.y; v[j][2] = f0.z; v[j][3] = f0.w;
+                    v[j][4] = f1.x; v[j][5] = f1.y; v[j][6] = f1.z; v[j][7] = f1.w;
+                } else {
 #pragma unroll
-                for (int e = 0; e < 8; ++e) v[e] = rms_apply(v[e], rms_w ? a.rms_w[256u * i + 8u * lane + e] : 0.0f, rms_w, sc);
+                    for (int e = 0; e < 8; ++e) v[j][e] = src[e];
+                }
             }
-            ok &= qact256_img(v, i, lane, q, d, bs);
+#pragma unroll
+            for (uint32_t j = 0; j < B; ++j) {
+                const uint32_t i = i0 + j * kWarps;
+                if (i >= nb) break;
+                if (rms) {
+#pragma unroll
+                    for (int e = 0; e < 8; ++e)
+                        v[j][e] = rms_apply(v[j][e], rms_w ? a.rms_w[256u * i + 8u * lane + e] : 0.0f, rms_w, sc);
+                }
+                ok &= qact256_img(v[j], i, lane, q, d, bs);
+            }
         }
     }
     const uint32_t bad = __any_sync(0xFFFFFFFFu, !ok);
