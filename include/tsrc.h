@@ -145,6 +145,19 @@ TSRC_API int tsrc_mvm(tsrc_ctx * ctx, const tsrc_weight * w, const int8_t * q, c
 // the array's device address (cudaGetSymbolAddress): make it before any stream capture. All calls
 // share the array: calls that may run at the same time on one device (other streams, other
 // contexts) race and must be serialised by the caller; calls queued on one stream are ordered.
+// MUL_MAT_ID (ggml's expert-routed product, the reference's MUL_MAT_ID kind: tsr_lower_mul_mat_id_node,
+// sw/ggml-tesseract/ggml-tesseract.cpp:3317-3350): w holds n_exp experts of N / n_exp rows each, stacked
+// (upload ggml's 3D expert tensor [n_exp][N/n_exp][K] as N rows). For token t < T and slot j < n_used,
+// with e = ids[t * ids_stride + j] (device int32, written by the router before the call):
+//   y[t * y_tok_stride + j * y_slot_stride + n] = MUL_MAT of expert e's row n with
+//   x[t * x_tok_stride + (j mod x_slots) * x_slot_stride ..]   (x_slots 1: one activation row per token
+//   shared by its slots, or n_used: one per slot)
+// -- each (t, j) exactly as a one-token tsrc_mul_mat of that expert (same bits). Strides in floats / ints,
+// 0 = dense. An id outside [0, n_exp) leaves its outputs unwritten; tsrc_sync then returns TSRC_E_ARG.
+// At most 65535 (token, slot) pairs per call. Queued on `stream`.
+TSRC_API int tsrc_mul_mat_id(tsrc_ctx * ctx, const tsrc_weight * w, uint32_t n_exp, const float * x, uint32_t x_slots,
+                             uint32_t x_slot_stride, uint32_t x_tok_stride, const int32_t * ids, uint32_t ids_stride,
+                             uint32_t n_used, uint32_t T, float * y, uint32_t y_slot_stride, uint32_t y_tok_stride, void * stream);
 TSRC_API int tsrc_mul_mat_noalloc(tsrc_ctx * ctx, const tsrc_weight * w, const float * x, uint32_t T, uint32_t x_stride,
                                   float * y, uint32_t y_stride, const float * add, uint32_t add_stride, uint32_t flags,
                                   float s0, float s1, void * stream);

@@ -403,6 +403,7 @@ int tsrc_sync(tsrc_ctx* ctx, void* stream) {
     uint32_t code = 0;
     e = tsrc::matvec_error(&code, true);
     if (e != cudaSuccess) return cuda_fail(e, "reading the kernel error flag");
+    if (code == 5) return fail(TSRC_E_ARG, "tsrc_mul_mat_id: an expert id outside [0, n_exp) (those pairs were not computed)");
     if (code) return fail(TSRC_E_DEVICE, "a matvec kernel gave up a bounded wait (code %u%s)", code,
                           code == 2 ? ": a team peer did not signal its step"
                                     : code == 3 ? ": a weight copy into shared memory did not complete" : "");
@@ -612,6 +613,57 @@ int tsrc_weight_free(tsrc_weight* w) {
 
 const char* tsrc_mul_mat_unsupported(uint32_t fmt, uint64_t N, uint64_t K, uint64_t T) { return shape_reason(fmt, N, K, T); }
 
+// MUL_MAT_ID (expert-routed MUL_MAT): one token per (token, slot) pair through the one-token
+// kernel, the pair's expert chosen on the device from ids
+static int mul_mat_id_impl(tsrc_ctx* ctx, const tsrc_weight* w, uint32_t n_exp, const float* x, uint32_t x_slots,
+                           uint32_t x_slot_stride, uint32_t x_tok_stride, const int32_t* ids, uint32_t ids_stride, uint32_t n_used,
+                           uint32_t T, float* y, uint32_t y_slot_stride, uint32_t y_tok_stride, void* stream) {
+    if (!ctx || !w || !x || !ids || !y) return fail(TSRC_E_ARG, "tsrc_mul_mat_id: NULL argument");
+    if (w->ctx != ctx) return fail(TSRC_E_ARG, "tsrc_mul_mat_id: the weight belongs to another context");
+    if (T == 0) return TSRC_OK;
+    if (n_exp == 0 || n_used == 0 || w->row0 != 0 || w->n_rows != w->N || w->N % n_exp)
+        return fail(TSRC_E_ARG, "tsrc_mul_mat_id: the weight must be whole and hold n_exp experts of equal row counts");
+    if (x_slots != 1u && x_slots != n_used) return fail(TSRC_E_ARG, "tsrc_mul_mat_id: x_slots must be 1 or n_used");
+    if ((uint64_t)T * n_used > 65535u) return fail(TSRC_E_SHAPE, "tsrc_mul_mat_id: more than 65535 (token, slot) pairs");
+    if (std::getenv("TSRC_MV_LEGACY")) return fail(TSRC_E_SHAPE, "tsrc_mul_mat_id: not available with TSRC_MV_LEGACY");
+    const uint32_t K = w->K, fmt = w->fmt, Ne = w->N / n_exp;
+    if (const char* why = tsrc_mul_mat_unsupported(fmt, Ne, K, 1))
+        return fail(TSRC_E_SHAPE, "tsrc_mul_mat_id: %s", why);
+    if (x_slot_stride == 0) x_slot_stride = K;
+    if (x_tok_stride == 0) x_tok_stride = x_slots * x_slot_stride;
+    if (ids_stride == 0) ids_stride = n_used;
+    if (y_slot_stride == 0) y_slot_stride = Ne;
+    if (y_tok_stride == 0) y_tok_stride = n_used * y_slot_stride;
+    if ((x_slots > 1u && x_slot_stride < K) || (T > 1u && x_tok_stride < K) || ids_stride < n_used ||
+        (n_used > 1u && y_slot_stride < Ne) || (T > 1u && y_tok_stride < Ne))
+        return fail(TSRC_E_ARG, "tsrc_mul_mat_id: a stride is shorter than its row");
+    int rc = use_device(ctx);
+    if (rc) return rc;
+    tsrc::MvArgs a{};
+    a.qs = w->qs;
+    a.meta = w->meta;
+    a.n_rows = Ne;
+    a.K = K;
+    a.x = x;
+    a.x_stride = K;
+    a.T = 1;
+    a.y = y;
+    a.y_stride = Ne;
+    a.ids = ids;
+    a.moe_pairs = T * n_used;
+    a.n_used = n_used;
+    a.n_exp = n_exp;
+    a.ids_stride = ids_stride;
+    a.x_slots = x_slots;
+    a.x_slot = x_slot_stride;
+    a.x_tok = x_tok_stride;
+    a.y_slot = y_slot_stride;
+    a.y_tok = y_tok_stride;
+    cudaError_t e = tsrc::launch_matvec(fmt, a, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "MUL_MAT_ID launch");
+    return TSRC_OK;
+}
+
 static int mul_mat_impl(tsrc_ctx* ctx, const tsrc_weight* w, const float* x, uint32_t T, uint32_t x_stride, float* y,
                         uint32_t y_stride, const float* add, uint32_t add_stride, uint32_t flags, float s0, float s1,
                         int32_t* isum_out, void* stream) {
@@ -759,6 +811,13 @@ int tsrc_mvm(tsrc_ctx* ctx, const tsrc_weight* w, const int8_t* q, const float* 
 int tsrc_mul_mat(tsrc_ctx* ctx, const tsrc_weight* w, const float* x, uint32_t T, uint32_t x_stride, float* y, uint32_t y_stride,
                  const float* add, uint32_t add_stride, uint32_t flags, float s0, float s1, void* stream) {
     return mul_mat_impl(ctx, w, x, T, x_stride, y, y_stride, add, add_stride, flags, s0, s1, nullptr, stream);
+}
+
+int tsrc_mul_mat_id(tsrc_ctx* ctx, const tsrc_weight* w, uint32_t n_exp, const float* x, uint32_t x_slots, uint32_t x_slot_stride,
+                    uint32_t x_tok_stride, const int32_t* ids, uint32_t ids_stride, uint32_t n_used, uint32_t T, float* y,
+                    uint32_t y_slot_stride, uint32_t y_tok_stride, void* stream) {
+    return mul_mat_id_impl(ctx, w, n_exp, x, x_slots, x_slot_stride, x_tok_stride, ids, ids_stride, n_used, T, y, y_slot_stride,
+                           y_tok_stride, stream);
 }
 
 int tsrc_mul_mat_isums(tsrc_ctx* ctx, const tsrc_weight* w, const float* x, float* y, int32_t* isum, void* stream) {

@@ -51,6 +51,11 @@ struct MvArgs {
     uint32_t* team_state;     // this rank: [0] steps done, [1] CTAs finished in this launch
     uint32_t team_world, team_rank, team_row0, team_n;
     uint32_t team_half;       // words per staging half (the team's capacity; calls of any N alternate halves)
+    // MUL_MAT_ID (one token per slot; moe_pairs = 0: off): grid row p = (t, j) of moe_pairs = T n_used
+    // runs expert e = ids[t ids_stride + j] -- rows [e n_rows, (e + 1) n_rows) of the stacked weight --
+    // on x + t x_tok + (j mod x_slots) x_slot, into y + t y_tok + j y_slot
+    const int32_t* ids;
+    uint32_t moe_pairs, n_used, n_exp, ids_stride, x_slots, x_slot, x_tok, y_slot, y_tok;
 };
 
 cudaError_t launch_qact(uint32_t kind, const float* x, uint32_t K, uint32_t T, uint32_t x_stride, int8_t* q, float* d,

@@ -1172,6 +1172,21 @@ __global__ void __launch_bounds__(Shape<NW>::kThreads, Shape<NW>::kMinBlocks) de
     constexpr uint32_t kWarps = NW;
     extern __shared__ __align__(128) uint8_t smem[];
     const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31u, k = lane & 15u;
+    if (EPI == 0 && a.moe_pairs) {
+        // MUL_MAT_ID: the expert ids come from the previous kernel, so every warp (the producer
+        // included) waits for it before the expert's rows are known
+        asm volatile("griddepcontrol.wait;" ::: "memory");
+        const uint32_t p = blockIdx.y, t = p / a.n_used, j = p - t * a.n_used;
+        const int32_t e = a.ids[(size_t)t * a.ids_stride + j];
+        if (e < 0 || (uint32_t)e >= a.n_exp) {
+            if (tid == 0) atomicCAS(&g_mv_error, 0u, 5u);     // an expert id outside the weight: not computed
+            return;
+        }
+        a.qs += (size_t)e * a.n_rows * P.g.qrow;
+        a.meta = static_cast<const uint8_t*>(a.meta) + (size_t)e * a.n_rows * P.g.mrow;
+        a.x += (size_t)t * a.x_tok + (size_t)(j % a.x_slots) * a.x_slot;
+        a.y += (size_t)t * a.y_tok + (size_t)j * a.y_slot;
+    }
     const uint32_t r_begin = blockIdx.x * P.rpc;
     if (r_begin >= a.n_rows) return;
     const uint32_t n = min(a.n_rows - r_begin, P.rpc);
@@ -1301,7 +1316,7 @@ static cudaError_t dec_launch(const MvArgs& a, const dec::Plan& P, uint32_t bloc
         done_dev[dev] = dev + 1;
     }
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(blocks);
+    cfg.gridDim = dim3(blocks, a.moe_pairs ? a.moe_pairs : 1u);
     cfg.blockDim = dim3(dec::Shape<NW>::kThreads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;

@@ -75,6 +75,7 @@ _SIGS = {
     "tsrc_rope": (_i, [_p, _p, _u32, _p, _u32, _p, _u32, _u32, _u32, _u32, _u32, _f32, _f32, _p]),
     "tsrc_vop": (_i, [_p, _u32, _p, _u32, _p, _u32, _p, _u32, _u32, _u32, _p]),
     "tsrc_get_rows": (_i, [_p, _p, _p, _u32, _p, _u32, _p]),
+    "tsrc_mul_mat_id": (_i, [_p, _p, _u32, _p, _u32, _u32, _u32, _p, _u32, _u32, _u32, _p, _u32, _u32, _p]),
     "tsrc_mul_mat_noalloc": (_i, [_p, _p, _p, _u32, _u32, _p, _u32, _p, _u32, _u32, _f32, _f32, _p]),
     "tsrc_mvm": (_i, [_p, _p, _p, _p, _p, _u32, _p, _u32, _p, _u32, _u32, _f32, _f32, _p]),
     "tsrc_mul_mat_unsupported": (ct.c_char_p, [_u32, _u64, _u64, _u64]),
@@ -308,6 +309,13 @@ class Device:
                 add_stride = 0 if (len(add.shape) == 1 or add.shape[0] == 1) else w.n_rows
         _check(lib().tsrc_mul_mat(self.handle, w.handle, _addr(x), T, x_stride, _addr(y), y_stride, _addr(add),
                                   add_stride or 0, flags, s0, s1, _stream(stream)))
+
+    def mul_mat_id(self, w: "Weight", n_exp: int, x, ids, y, n_used: int, T: int, x_slots: int = 1, x_slot_stride: int = 0,
+                   x_tok_stride: int = 0, ids_stride: int = 0, y_slot_stride: int = 0, y_tok_stride: int = 0,
+                   stream=None) -> None:
+        """MUL_MAT_ID: y[t][j] = MUL_MAT of expert ids[t][j] (rows of the stacked weight) with x[t][j mod x_slots]."""
+        _check(lib().tsrc_mul_mat_id(self.handle, w.handle, n_exp, _addr(x), x_slots, x_slot_stride, x_tok_stride, _addr(ids),
+                                     ids_stride, n_used, T, _addr(y), y_slot_stride, y_tok_stride, _stream(stream)))
 
     def mul_mat_noalloc(self, w: "Weight", x, y, T: int | None = None, add=None, add_stride: int | None = None,
                         flags: int = 0, s0: float = 1.0, s1: float = 1.0, x_stride: int = 0, y_stride: int = 0,
