@@ -145,6 +145,13 @@ TSRC_API int tsrc_mvm(tsrc_ctx * ctx, const tsrc_weight * w, const int8_t * q, c
 // the array's device address (cudaGetSymbolAddress): make it before any stream capture. All calls
 // share the array: calls that may run at the same time on one device (other streams, other
 // contexts) race and must be serialised by the caller; calls queued on one stream are ordered.
+// Device memory and copies for hosts that do not link the CUDA runtime themselves (the C++ runtime
+// front end, include/tsrc_rt.hpp): a buffer on the context's device; an asynchronous copy between host
+// and device memory on `stream` (to_device 1: host -> device, 0: device -> host; tsrc_sync waits).
+TSRC_API int tsrc_dev_alloc(tsrc_ctx * ctx, size_t bytes, void ** out);
+TSRC_API int tsrc_dev_free(tsrc_ctx * ctx, void * p);
+TSRC_API int tsrc_copy(tsrc_ctx * ctx, void * dst, const void * src, size_t bytes, uint32_t to_device, void * stream);
+
 // MUL_MAT_ID (ggml's expert-routed product, the reference's MUL_MAT_ID kind: tsr_lower_mul_mat_id_node,
 // sw/ggml-tesseract/ggml-tesseract.cpp:3317-3350): w holds n_exp experts of N / n_exp rows each, stacked
 // (upload ggml's 3D expert tensor [n_exp][N/n_exp][K] as N rows). For token t < T and slot j < n_used,

@@ -813,6 +813,36 @@ int tsrc_mul_mat(tsrc_ctx* ctx, const tsrc_weight* w, const float* x, uint32_t T
     return mul_mat_impl(ctx, w, x, T, x_stride, y, y_stride, add, add_stride, flags, s0, s1, nullptr, stream);
 }
 
+int tsrc_dev_alloc(tsrc_ctx* ctx, size_t bytes, void** out) {
+    if (!ctx || !out) return fail(TSRC_E_ARG, "tsrc_dev_alloc: NULL argument");
+    *out = nullptr;
+    int rc = use_device(ctx);
+    if (rc) return rc;
+    if (bytes == 0) return TSRC_OK;
+    const cudaError_t e = cudaMalloc(out, bytes);
+    if (e != cudaSuccess) return fail(TSRC_E_NOMEM, "tsrc_dev_alloc: %zu bytes: %s", bytes, cudaGetErrorString(e));
+    return TSRC_OK;
+}
+
+int tsrc_dev_free(tsrc_ctx* ctx, void* p) {
+    if (!ctx) return fail(TSRC_E_ARG, "tsrc_dev_free: NULL context");
+    if (!p) return TSRC_OK;
+    int rc = use_device(ctx);
+    if (rc) return rc;
+    const cudaError_t e = cudaFree(p);
+    return e == cudaSuccess ? TSRC_OK : cuda_fail(e, "tsrc_dev_free");
+}
+
+int tsrc_copy(tsrc_ctx* ctx, void* dst, const void* src, size_t bytes, uint32_t to_device, void* stream) {
+    if (!ctx || (bytes && (!dst || !src))) return fail(TSRC_E_ARG, "tsrc_copy: NULL argument");
+    if (bytes == 0) return TSRC_OK;
+    int rc = use_device(ctx);
+    if (rc) return rc;
+    const cudaError_t e = cudaMemcpyAsync(dst, src, bytes, to_device ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToHost,
+                                          static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? TSRC_OK : cuda_fail(e, "tsrc_copy");
+}
+
 int tsrc_mul_mat_id(tsrc_ctx* ctx, const tsrc_weight* w, uint32_t n_exp, const float* x, uint32_t x_slots, uint32_t x_slot_stride,
                     uint32_t x_tok_stride, const int32_t* ids, uint32_t ids_stride, uint32_t n_used, uint32_t T, float* y,
                     uint32_t y_slot_stride, uint32_t y_tok_stride, void* stream) {

@@ -75,6 +75,9 @@ _SIGS = {
     "tsrc_rope": (_i, [_p, _p, _u32, _p, _u32, _p, _u32, _u32, _u32, _u32, _u32, _f32, _f32, _p]),
     "tsrc_vop": (_i, [_p, _u32, _p, _u32, _p, _u32, _p, _u32, _u32, _u32, _p]),
     "tsrc_get_rows": (_i, [_p, _p, _p, _u32, _p, _u32, _p]),
+    "tsrc_dev_alloc": (_i, [_p, ct.c_size_t, ct.POINTER(_p)]),
+    "tsrc_dev_free": (_i, [_p, _p]),
+    "tsrc_copy": (_i, [_p, _p, _p, ct.c_size_t, _u32, _p]),
     "tsrc_mul_mat_id": (_i, [_p, _p, _u32, _p, _u32, _u32, _u32, _p, _u32, _u32, _u32, _p, _u32, _u32, _p]),
     "tsrc_mul_mat_noalloc": (_i, [_p, _p, _p, _u32, _u32, _p, _u32, _p, _u32, _u32, _f32, _f32, _p]),
     "tsrc_mvm": (_i, [_p, _p, _p, _p, _p, _u32, _p, _u32, _p, _u32, _u32, _f32, _f32, _p]),
