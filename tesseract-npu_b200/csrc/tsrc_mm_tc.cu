@@ -104,6 +104,9 @@ __device__ __forceinline__ bool mbar_wait_ab(uint64_t* b, uint32_t parity, volat
             : "r"(bar), "r"(parity), "r"(1000u)
             : "memory");
         if (ok) return true;
+        // the abort flag and the clock every 64 polls: a poll is a shared-memory access, and warps
+        // spinning here take issue slots and shared-memory bandwidth from the warps doing the work
+        if ((it & 63u) != 0u) continue;
         if (*abort_flag) return false;
         if (it == 0) t0 = clock64();
         else if (clock64() - t0 > kWaitCycles) break;
@@ -428,85 +431,110 @@ cudaError_t launch_nt(const MvArgs& a, cudaStream_t st) {
 
 
 // ---- Q4_K ---------------------------------------------------------------------------------------
-// Per superblock (256 values) eight MMAs, one per 32-value sub-block j: A = the sub-block's nibbles
-// expanded to int8 (0..15) in shared memory, B = the tokens' quantized activation of the same 32
-// values; D = S_j[row][token] exactly. Then isum = sum_j sc_j S_j and msum = sum_j m_j (BS_2j +
-// BS_2j+1) in int32 (exact, as tsr_ref.c:540-567), and the term d Dx isum - dmin Dx msum with the
-// f32 rules. The A256 scale Dx is an arbitrary f32: when every Dx of the CTA's tokens is 0 or at
-// least 2^-79 in magnitude, every product and sum is a multiple of 2^-126 and the flush tests are
-// skipped (SAFE); otherwise they run.
+// The reference's superblock term (tsr_ref.c:540-567): isum = sum_j sc_j S_j over the eight 32-value
+// sub-blocks j (S_j = the int dot product of the nibbles and the activation), msum = sum_j m_j
+// (BS_2j + BS_2j+1), both int32, then d Dx isum - dmin Dx msum with the f32 rules. The tensor cores
+// apply the 6-bit scales themselves: with sc_j = 8 sh_j + sl_j (sh_j, sl_j in 0..7) the expanders
+// write two int8 A images of the superblock, sh_j q and sl_j q (each at most 7 x 15 = 105, so one
+// 32-bit multiply scales four packed nibbles without carries between them), and two MMA chains over
+// the whole superblock (K = 256, eight K = 32 steps each) give H = sum_j sh_j S_j and
+// L = sum_j sl_j S_j; isum = 8 H + L is the same integer (|isum| < 2^31). So an output costs two TMEM
+// values per superblock, not eight. The A256 scale Dx is an arbitrary f32: when every Dx of the CTA's
+// tokens is 0 or at least 2^-79 in magnitude, every product and sum is a multiple of 2^-126 and the
+// flush tests are skipped (SAFE); otherwise they run.
 //
 // Warp roles: E epilogue warps (32 rows x 16 tokens each), P producer warps (cp.async of the raw
 // quants, with the 16-byte chunks of a row rotated by the row so that the expanders read without
 // bank conflicts, the B tiles, Dx, the pair sums BS_2j + BS_2j+1 and the 16-byte row metadata into
-// a ring of S stages), X expander warps (one row per thread: nibbles -> two int8 A tiles, into one
-// of NA expanded slots), one MMA warp. mbarriers: full/empty[S], afull/aempty[NA], tfull/tempty[NB].
+// three rings: the raw quants (S entries, free once expanded), the B tiles (SB entries, free once the
+// MMA has read them) and Dx, the pair sums and the metadata (SE entries, free once the expanders and
+// the epilogue have used them), so that no copy waits for a later role than the one that reads it),
+// X expander warps (one row per thread; a superblock in two halves of 128 values, each into one of
+// NA slots holding the H and L images of four K steps), one MMA warp. TMEM: NB accumulator pairs
+// (H then L, NT columns each) and the four levels of the partial trees' stacks (NT columns each).
+// mbarriers: full/empty[S], bfull/bempty[SB], efull/eempty[SE], afull/aempty[NA], tfull/tempty[NB].
 constexpr uint32_t kSafeDxQ4 = 0x18000000u;            // 2^-79
 
 template <uint32_t NT>
 struct Q4Cfg {
     static constexpr uint32_t E = 4u * (NT / 16u), P = 2u, X = 4u;
     static constexpr uint32_t WARPS = E + P + X + 1u, MMA_WARP = E + P + X;
-    static constexpr uint32_t S = 3u, NB = 2u, NA = 2u;
+    static constexpr uint32_t S = 3u, SB = 4u, SE = 6u, NB = 2u, NA = 2u;
     static constexpr uint32_t RAW = kTileM * 128u, BT = NT * 32u, ATILE = kTileM * 32u;
-    static constexpr uint32_t B_OFF = RAW, DX_OFF = B_OFF + 8u * BT, BS_OFF = DX_OFF + NT * 4u;
-    static constexpr uint32_t META_OFF = BS_OFF + NT * 16u, STAGE = META_OFF + kTileM * 16u;
-    static constexpr size_t AX_OFF = (size_t)S * STAGE, ASLOT = 8u * ATILE;
-    static constexpr size_t STACK_OFF = AX_OFF + NA * ASLOT;
-    static constexpr uint32_t LSTRIDE = NT * kTileM;
-    static constexpr size_t BAR_OFF = STACK_OFF + 4u * LSTRIDE * 4u;
-    static constexpr size_t SMEM = BAR_OFF + (2u * S + 2u * NA + 2u * NB) * 8u + 16u;
-    static constexpr uint32_t TCOLS = NB * 8u * NT;
-    static_assert(TCOLS == 256u || TCOLS == 512u, "TMEM allocation is a power of two");
+    static constexpr uint32_t DX_OFF = 0u, BS_OFF = NT * 4u, META_OFF = BS_OFF + NT * 16u, EPI = META_OFF + kTileM * 16u;
+    static constexpr size_t B_OFF = (size_t)S * RAW, E_OFF = B_OFF + (size_t)SB * 8u * BT;
+    static constexpr size_t AX_OFF = E_OFF + (size_t)SE * EPI, ASLOT = 8u * ATILE;    // H steps 0..3, L steps 0..3
+    static constexpr size_t BAR_OFF = AX_OFF + NA * ASLOT;
+    static constexpr size_t SMEM = BAR_OFF + (2u * S + 2u * SB + 2u * SE + 2u * NA + 2u * NB) * 8u + 16u;
+    static constexpr uint32_t ACC_COLS = 2u * NT, STK_COL = NB * ACC_COLS, TCOLS = STK_COL + 4u * NT;
+    static_assert(TCOLS == 128u || TCOLS == 256u || TCOLS == 512u, "TMEM allocation is a power of two");
     static_assert(SMEM <= 227u * 1024u, "shared memory");
 };
 
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const float (&v)[16]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};"
+        ::"r"(taddr), "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
+          "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])), "r"(__float_as_uint(v[6])),
+          "r"(__float_as_uint(v[7])), "r"(__float_as_uint(v[8])), "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])),
+          "r"(__float_as_uint(v[11])), "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])),
+          "r"(__float_as_uint(v[15]))
+        : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// tree_push_smem with the four stack levels in TMEM columns s, s + NT, s + 2 NT, s + 3 NT of the
+// thread's lane (same order of additions: the stacked, earlier partial is the left operand)
+template <uint32_t NT, bool FLUSH>
+__device__ __forceinline__ void tree_push_tmem(uint32_t s, uint32_t j, float (&v)[16]) {
+#pragma unroll
+    for (uint32_t lvl = 0; lvl < 4; ++lvl) {
+        if (((j >> lvl) & 1u) == 0u) {
+            tmem_st16(s + lvl * NT, v);
+            tmem_wait_st();
+            return;
+        }
+        uint32_t p[16];
+        tmem_ld16(s + lvl * NT, p);
+        tmem_wait_ld();
+#pragma unroll
+        for (uint32_t i = 0; i < 16; ++i)
+            v[i] = FLUSH ? fadd(__uint_as_float(p[i]), v[i]) : __fadd_rn(__uint_as_float(p[i]), v[i]);
+    }
+    tmem_st16(s, v);
+    tmem_wait_st();
+}
+
 template <uint32_t NT, bool SAFE>
-__device__ __forceinline__ void q4k_epilogue(const MvArgs& a, uint8_t* smem, uint64_t* full, uint64_t* empty,
+__device__ __forceinline__ void q4k_epilogue(const MvArgs& a, uint8_t* smem, uint64_t* efull, uint64_t* eempty,
                                              uint64_t* tfull, uint64_t* tempty, volatile uint32_t* abort_flag, uint32_t tmem,
                                              uint32_t warp, uint32_t lane) {
     using C = Q4Cfg<NT>;
     const uint32_t nsb = a.K / 256u, q = nsb >> 4, rem = nsb & 15u;
     const uint32_t rq = warp & 3u, cq = warp >> 2;
     const uint32_t row = blockIdx.x * kTileM + 32u * rq + lane, tok0 = blockIdx.y * NT;
-    const uint32_t tl = tmem + ((32u * rq) << 16) + 16u * cq;
-    float* stk = reinterpret_cast<float*>(smem + C::STACK_OFF) + 16u * cq * kTileM + 32u * rq + lane;
+    const uint32_t tl = tmem + ((32u * rq) << 16) + 16u * cq, ts = tl + C::STK_COL;
     float acc[16];
 #pragma unroll
     for (uint32_t i = 0; i < 16; ++i) acc[i] = 0.0f;
     uint32_t j = 0, ii = 0, cnt = q + (rem > 0u ? 1u : 0u);
     bool aborted = false;
     for (uint32_t u = 0; u < nsb; ++u) {
-        const uint32_t st = u % C::S, buf = u % C::NB;
+        const uint32_t se = u % C::SE, buf = u % C::NB;
         if (!mbar_wait_ab(&tfull[buf], (u / C::NB) & 1u, abort_flag)) { aborted = true; break; }
-        if (!mbar_wait_ab(&full[st], (u / C::S) & 1u, abort_flag)) { aborted = true; break; }
+        if (!mbar_wait_ab(&efull[se], (u / C::SE) & 1u, abort_flag)) { aborted = true; break; }
         asm volatile("tcgen05.fence::after_thread_sync;");
-        const uint8_t* sb = smem + (size_t)st * C::STAGE;
+        uint32_t h[16], l[16];
+        tmem_ld16(tl + buf * C::ACC_COLS, h);
+        tmem_ld16(tl + buf * C::ACC_COLS + NT, l);
+        const uint8_t* sb = smem + C::E_OFF + (size_t)se * C::EPI;
         const uint4 m = reinterpret_cast<const uint4*>(sb + C::META_OFF)[32u * rq + lane];
-        const uint32_t sc_lo = m.y & 0x3F3F3F3Fu, mn_lo = m.z & 0x3F3F3F3Fu;
-        const uint32_t sc_hi = (m.w & 0x0F0F0F0Fu) | ((m.y >> 2) & 0x30303030u);
-        const uint32_t mn_hi = ((m.w >> 4) & 0x0F0F0F0Fu) | ((m.z >> 2) & 0x30303030u);
-        int32_t isum[16];
-#pragma unroll
-        for (uint32_t i = 0; i < 16; ++i) isum[i] = 0;
-#pragma unroll
-        for (uint32_t g = 0; g < 2u; ++g) {                      // sub-blocks 4 g .. 4 g + 3: four loads, one wait
-            uint32_t v[4][16];
-#pragma unroll
-            for (uint32_t x = 0; x < 4u; ++x) tmem_ld16(tl + (buf * 8u + 4u * g + x) * NT, v[x]);
-            tmem_wait_ld();
-            const uint32_t scw = g ? sc_hi : sc_lo;
-#pragma unroll
-            for (uint32_t x = 0; x < 4u; ++x) {
-                const int32_t sc = (int32_t)__byte_perm(scw, 0u, 0x4440u | x);
-#pragma unroll
-                for (uint32_t i = 0; i < 16; ++i) isum[i] += sc * (int32_t)v[x][i];
-            }
-        }
+        const uint32_t mn_lo = m.z & 0x3F3F3F3Fu, mn_hi = ((m.w >> 4) & 0x0F0F0F0Fu) | ((m.z >> 2) & 0x30303030u);
+        const float dw = h2f((uint16_t)(m.x & 0xFFFFu)), dmw = h2f((uint16_t)(m.x >> 16));
+        tmem_wait_ld();
         asm volatile("tcgen05.fence::before_thread_sync;");
         __syncwarp();
         if (lane == 0) mbar_arrive(&tempty[buf]);
-        const float dw = h2f((uint16_t)(m.x & 0xFFFFu)), dmw = h2f((uint16_t)(m.x >> 16));
         const float4* dx4 = reinterpret_cast<const float4*>(sb + C::DX_OFF + 64u * cq);
         const uint4* bs4 = reinterpret_cast<const uint4*>(sb + C::BS_OFF) + 16u * cq;
 #pragma unroll
@@ -518,22 +546,23 @@ __device__ __forceinline__ void q4k_epilogue(const MvArgs& a, uint8_t* smem, uin
                 const uint32_t i = 4u * k + e;
                 const uint4 B = bs4[i];
                 const int32_t msum = dp2a_hi(B.w, mn_hi, dp2a_lo(B.z, mn_hi, dp2a_hi(B.y, mn_lo, dp2a_lo(B.x, mn_lo, 0))));
+                const int32_t isum = (int32_t)(8u * h[i] + l[i]);
                 const float Dx = d4[e];
                 if (SAFE) {
-                    const float t1 = __fmul_rn(__fmul_rn(dw, Dx), __int2float_rn(isum[i]));
+                    const float t1 = __fmul_rn(__fmul_rn(dw, Dx), __int2float_rn(isum));
                     const float t2 = __fmul_rn(__fmul_rn(dmw, Dx), __int2float_rn(msum));
                     acc[i] = __fadd_rn(acc[i], __fsub_rn(t1, t2));
                 } else {
-                    const float t1 = fmul(fmul(dw, Dx), i2f(isum[i]));
+                    const float t1 = fmul(fmul(dw, Dx), i2f(isum));
                     const float t2 = fmul(fmul(dmw, Dx), i2f(msum));
                     acc[i] = fadd(acc[i], fsub(t1, t2));
                 }
             }
         }
         __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[st]);
+        if (lane == 0) mbar_arrive(&eempty[se]);
         if (++ii == cnt) {                                       // partial j is complete
-            tree_push_smem<!SAFE>(stk, C::LSTRIDE, j, acc);
+            tree_push_tmem<NT, !SAFE>(ts, j, acc);
 #pragma unroll
             for (uint32_t i = 0; i < 16; ++i) acc[i] = 0.0f;
             ++j;
@@ -546,14 +575,17 @@ __device__ __forceinline__ void q4k_epilogue(const MvArgs& a, uint8_t* smem, uin
         float z[16];
 #pragma unroll
         for (uint32_t i = 0; i < 16; ++i) z[i] = 0.0f;
-        tree_push_smem<!SAFE>(stk, C::LSTRIDE, j, z);
+        tree_push_tmem<NT, !SAFE>(ts, j, z);
     }
+    uint32_t out[16];
+    tmem_ld16(ts, out);                                          // the tree's value: level 0
+    tmem_wait_ld();
     if (row < a.n_rows) {
 #pragma unroll
         for (uint32_t i = 0; i < 16; ++i) {
             const uint32_t tok = tok0 + 16u * cq + i;
             if (tok < a.T) {
-                float y = stk[i * kTileM];
+                float y = __uint_as_float(out[i]);
                 if (a.flags & kMmAdd) y = fadd(daz(a.add[(size_t)tok * a.add_stride + row]), y);
                 if (a.flags & kMmSoftcap) y = fmul(tanh_vu(fmul(y, a.s0), g_expk_t64, g_expk_lk), a.s1);
                 else if (a.flags & kMmScale) y = fmul(y, a.s1);
@@ -569,7 +601,11 @@ __global__ void __launch_bounds__(32 * Q4Cfg<NT>::WARPS, 1) mm_q4k_tc_kernel(MvA
     extern __shared__ __align__(128) uint8_t smem[];
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::BAR_OFF);
     uint64_t* empty = full + C::S;
-    uint64_t* afull = empty + C::S;
+    uint64_t* bfull = empty + C::S;
+    uint64_t* bempty = bfull + C::SB;
+    uint64_t* efull = bempty + C::SB;
+    uint64_t* eempty = efull + C::SE;
+    uint64_t* afull = eempty + C::SE;
     uint64_t* aempty = afull + C::NA;
     uint64_t* tfull = aempty + C::NA;
     uint64_t* tempty = tfull + C::NB;
@@ -588,7 +624,15 @@ __global__ void __launch_bounds__(32 * Q4Cfg<NT>::WARPS, 1) mm_q4k_tc_kernel(MvA
     if (threadIdx.x == 0) {
         for (uint32_t i = 0; i < C::S; ++i) {
             mbar_init(&full[i], 32u * C::P);
-            mbar_init(&empty[i], 1u + C::X + C::E);
+            mbar_init(&empty[i], C::X);
+        }
+        for (uint32_t i = 0; i < C::SB; ++i) {
+            mbar_init(&bfull[i], 32u * C::P);
+            mbar_init(&bempty[i], 1u);
+        }
+        for (uint32_t i = 0; i < C::SE; ++i) {
+            mbar_init(&efull[i], 32u * C::P);
+            mbar_init(&eempty[i], C::E + C::X);
         }
         for (uint32_t i = 0; i < C::NA; ++i) {
             mbar_init(&afull[i], C::X);
@@ -623,36 +667,42 @@ __global__ void __launch_bounds__(32 * Q4Cfg<NT>::WARPS, 1) mm_q4k_tc_kernel(MvA
         const uint32_t pl = (warp - C::E) * 32u + lane, kk = pl & 7u;
         const size_t qrow = L.qs_row_bytes(), mrow = L.meta_row_bytes();
         for (uint32_t u = 0; u < nsb; ++u) {
-            const uint32_t st = u % C::S;
-            if (u >= C::S && !mbar_wait_ab(&empty[st], ((u / C::S) - 1u) & 1u, abort_flag)) break;
+            const uint32_t st = u % C::S, sbi = u % C::SB, se = u % C::SE;
             uint32_t jb;
             bool lb;
             const uint32_t sbk = Seq{nsb, q, rem}.block(u, &jb, &lb);
-            uint8_t* sb = smem + (size_t)st * C::STAGE;
+            if (u >= C::SE && !mbar_wait_ab(&eempty[se], ((u / C::SE) - 1u) & 1u, abort_flag)) break;
+            uint8_t* eb = smem + C::E_OFF + (size_t)se * C::EPI;
+#pragma unroll
+            for (uint32_t k = 0; k < kTileM / LN; ++k) {
+                const uint32_t r = pl + LN * k;
+                cp_async16(eb + C::META_OFF + 16u * r,
+                           static_cast<const uint8_t*>(a.meta) + (size_t)min(row0 + r, a.n_rows - 1u) * mrow + 16u * sbk);
+            }
+            if (pl < NT) {
+                const uint32_t tok = min(tok0 + pl, a.T - 1u);
+                cp_async4(eb + C::DX_OFF + 4u * pl, a.dx + (size_t)tok * nsb + sbk);
+                cp_async16(eb + C::BS_OFF + 16u * pl, a.bs2x + (size_t)tok * (K / 32u) + 8u * sbk);
+            }
+            cp_async_arrive(&efull[se]);                         // each entry is published when its copies land
+            if (u >= C::S && !mbar_wait_ab(&empty[st], ((u / C::S) - 1u) & 1u, abort_flag)) break;
+            uint8_t* sb = smem + (size_t)st * C::RAW;
             const size_t qoff = L.qs_off(0u, sbk, kk);
 #pragma unroll 4
             for (uint32_t k = 0; k < 1024u / LN; ++k) {          // raw quants: row (pl / 8) + 8 k, chunk pl & 7
                 const uint32_t r = (pl >> 3) + (LN / 8u) * k;
                 cp_async16(sb + r * 128u + ((kk ^ (r & 7u)) * 16u), a.qs + (size_t)min(row0 + r, a.n_rows - 1u) * qrow + qoff);
             }
-#pragma unroll
+            cp_async_arrive(&full[st]);
+            if (u >= C::SB && !mbar_wait_ab(&bempty[sbi], ((u / C::SB) - 1u) & 1u, abort_flag)) break;
+            uint8_t* bb = smem + C::B_OFF + (size_t)sbi * 8u * C::BT;
+#pragma unroll 4
             for (uint32_t k = 0; k < 16u * NT / LN; ++k) {       // B tiles: (sub-block, token, half)
                 const uint32_t idx = pl + LN * k, h = idx & 1u, t = (idx >> 1) % NT, jj = (idx >> 1) / NT;
-                cp_async16(sb + C::B_OFF + jj * C::BT + (t >> 3) * 256u + h * 128u + (t & 7u) * 16u,
+                cp_async16(bb + jj * C::BT + (t >> 3) * 256u + h * 128u + (t & 7u) * 16u,
                            a.qx + (size_t)min(tok0 + t, a.T - 1u) * K + 256u * sbk + 32u * jj + 16u * h);
             }
-            if (pl < NT) {
-                const uint32_t tok = min(tok0 + pl, a.T - 1u);
-                cp_async4(sb + C::DX_OFF + 4u * pl, a.dx + (size_t)tok * nsb + sbk);
-                cp_async16(sb + C::BS_OFF + 16u * pl, a.bs2x + (size_t)tok * (K / 32u) + 8u * sbk);
-            }
-#pragma unroll
-            for (uint32_t k = 0; k < kTileM / LN; ++k) {
-                const uint32_t r = pl + LN * k;
-                cp_async16(sb + C::META_OFF + 16u * r,
-                           static_cast<const uint8_t*>(a.meta) + (size_t)min(row0 + r, a.n_rows - 1u) * mrow + 16u * sbk);
-            }
-            cp_async_arrive(&full[st]);                          // the stage is published when its copies land
+            cp_async_arrive(&bfull[sbi]);
         }
         cp_async_wait<0>();
     } else if (warp >= C::E + C::P && warp < C::MMA_WARP) {
@@ -660,46 +710,75 @@ __global__ void __launch_bounds__(32 * Q4Cfg<NT>::WARPS, 1) mm_q4k_tc_kernel(MvA
         const uint32_t r = (warp - C::E - C::P) * 32u + lane;
         const uint32_t off = (r >> 3) * 256u + (r & 7u) * 16u;
         for (uint32_t u = 0; u < nsb; ++u) {
-            const uint32_t st = u % C::S, slot = u % C::NA;
-            if (!mbar_wait_ab(&full[st], (u / C::S) & 1u, abort_flag)) break;
-            if (u >= C::NA && !mbar_wait_ab(&aempty[slot], ((u / C::NA) - 1u) & 1u, abort_flag)) break;
-            const uint8_t* raw = smem + (size_t)st * C::STAGE + r * 128u;
-            uint8_t* ax = smem + C::AX_OFF + slot * C::ASLOT + off;
-#pragma unroll
-            for (uint32_t k = 0; k < 8u; ++k) {                  // chunk k: low nibbles -> sub-block 2 (k / 2), high -> +1
-                const uint4 w = *reinterpret_cast<const uint4*>(raw + ((k ^ (r & 7u)) * 16u));
-                const uint4 lo = make_uint4(w.x & 0x0F0F0F0Fu, w.y & 0x0F0F0F0Fu, w.z & 0x0F0F0F0Fu, w.w & 0x0F0F0F0Fu);
-                const uint4 hi = make_uint4((w.x >> 4) & 0x0F0F0F0Fu, (w.y >> 4) & 0x0F0F0F0Fu, (w.z >> 4) & 0x0F0F0F0Fu,
-                                            (w.w >> 4) & 0x0F0F0F0Fu);
-                const uint32_t c = k >> 1, h = k & 1u;
-                *reinterpret_cast<uint4*>(ax + (2u * c) * C::ATILE + h * 128u) = lo;
-                *reinterpret_cast<uint4*>(ax + (2u * c + 1u) * C::ATILE + h * 128u) = hi;
-            }
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            const uint32_t st = u % C::S, se = u % C::SE;
+            if (!mbar_wait_ab(&efull[se], (u / C::SE) & 1u, abort_flag)) break;
+            const uint4 m = reinterpret_cast<const uint4*>(smem + C::E_OFF + (size_t)se * C::EPI + C::META_OFF)[r];
             __syncwarp();
-            if (lane == 0) {
-                mbar_arrive(&afull[slot]);
-                mbar_arrive(&empty[st]);
+            if (lane == 0) mbar_arrive(&eempty[se]);
+            // the eight 6-bit scales (sub-blocks 0..3 in sc_lo, 4..7 in sc_hi, a byte each), split 8 sh + sl
+            const uint32_t sc_lo = m.y & 0x3F3F3F3Fu, sc_hi = (m.w & 0x0F0F0F0Fu) | ((m.y >> 2) & 0x30303030u);
+            const uint32_t shw[2] = {(sc_lo >> 3) & 0x07070707u, (sc_hi >> 3) & 0x07070707u};
+            const uint32_t slw[2] = {sc_lo & 0x07070707u, sc_hi & 0x07070707u};
+            if (!mbar_wait_ab(&full[st], (u / C::S) & 1u, abort_flag)) break;
+            const uint8_t* raw = smem + (size_t)st * C::RAW + r * 128u;
+            bool quit = false;
+#pragma unroll
+            for (uint32_t hf = 0; hf < 2u; ++hf) {               // values 128 hf .. 128 hf + 127: sub-blocks 4 hf .. 4 hf + 3
+                const uint32_t hc = 2u * u + hf, slot = hc % C::NA;
+                if (hc >= C::NA && !mbar_wait_ab(&aempty[slot], ((hc / C::NA) - 1u) & 1u, abort_flag)) { quit = true; break; }
+                uint8_t* ax = smem + C::AX_OFF + slot * C::ASLOT + off;
+#pragma unroll
+                for (uint32_t kq = 0; kq < 4u; ++kq) {           // chunk k: low nibbles -> sub-block 2 (k / 2), high -> +1
+                    const uint32_t k = 4u * hf + kq, c = k >> 1, h = k & 1u;
+                    const uint4 w = *reinterpret_cast<const uint4*>(raw + ((k ^ (r & 7u)) * 16u));
+                    const uint4 lo = make_uint4(w.x & 0x0F0F0F0Fu, w.y & 0x0F0F0F0Fu, w.z & 0x0F0F0F0Fu, w.w & 0x0F0F0F0Fu);
+                    const uint4 hi = make_uint4((w.x >> 4) & 0x0F0F0F0Fu, (w.y >> 4) & 0x0F0F0F0Fu, (w.z >> 4) & 0x0F0F0F0Fu,
+                                                (w.w >> 4) & 0x0F0F0F0Fu);
+                    const uint32_t sa = 2u * c, sbb = 2u * c + 1u;   // sub-blocks of the low and high nibbles
+                    const uint32_t ha = (shw[sa >> 2] >> (8u * (sa & 3u))) & 0xFFu, la = (slw[sa >> 2] >> (8u * (sa & 3u))) & 0xFFu;
+                    const uint32_t hb = (shw[sbb >> 2] >> (8u * (sbb & 3u))) & 0xFFu, lb = (slw[sbb >> 2] >> (8u * (sbb & 3u))) & 0xFFu;
+                    const uint32_t ka = sa - 4u * hf, kb = sbb - 4u * hf;   // K steps within the half
+                    *reinterpret_cast<uint4*>(ax + ka * C::ATILE + h * 128u) = make_uint4(lo.x * ha, lo.y * ha, lo.z * ha, lo.w * ha);
+                    *reinterpret_cast<uint4*>(ax + (4u + ka) * C::ATILE + h * 128u) = make_uint4(lo.x * la, lo.y * la, lo.z * la, lo.w * la);
+                    *reinterpret_cast<uint4*>(ax + kb * C::ATILE + h * 128u) = make_uint4(hi.x * hb, hi.y * hb, hi.z * hb, hi.w * hb);
+                    *reinterpret_cast<uint4*>(ax + (4u + kb) * C::ATILE + h * 128u) = make_uint4(hi.x * lb, hi.y * lb, hi.z * lb, hi.w * lb);
+                }
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&afull[slot]);
             }
+            if (quit) break;
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[st]);
         }
     } else if (warp == C::MMA_WARP) {
         if (lane == 0) {
             uint32_t issued = 0;
-            for (uint32_t u = 0; u < nsb; ++u) {
-                const uint32_t st = u % C::S, slot = u % C::NA, buf = u % C::NB;
-                if (!mbar_wait_ab(&full[st], (u / C::S) & 1u, abort_flag)) break;
-                if (!mbar_wait_ab(&afull[slot], (u / C::NA) & 1u, abort_flag)) break;
+            bool quit = false;
+            for (uint32_t u = 0; u < nsb && !quit; ++u) {
+                const uint32_t sbi = u % C::SB, buf = u % C::NB;
+                if (!mbar_wait_ab(&bfull[sbi], (u / C::SB) & 1u, abort_flag)) break;
                 if (u >= C::NB && !mbar_wait_ab(&tempty[buf], ((u / C::NB) - 1u) & 1u, abort_flag)) break;
-                asm volatile("tcgen05.fence::after_thread_sync;");
-                uint8_t* sb = smem + (size_t)st * C::STAGE;
-                uint8_t* ax = smem + C::AX_OFF + slot * C::ASLOT;
+                uint8_t* bb = smem + C::B_OFF + (size_t)sbi * 8u * C::BT;
+                const uint32_t dh = tmem + buf * C::ACC_COLS, dl = dh + NT;
 #pragma unroll
-                for (uint32_t jj = 0; jj < 8u; ++jj)
-                    mma_i8(tmem + (buf * 8u + jj) * NT, umma_desc(ax + jj * C::ATILE), umma_desc(sb + C::B_OFF + jj * C::BT),
-                           umma_idesc<NT>(), 0u);
+                for (uint32_t hf = 0; hf < 2u; ++hf) {
+                    const uint32_t hc = 2u * u + hf, slot = hc % C::NA;
+                    if (!mbar_wait_ab(&afull[slot], (hc / C::NA) & 1u, abort_flag)) { quit = true; break; }
+                    asm volatile("tcgen05.fence::after_thread_sync;");
+                    uint8_t* ax = smem + C::AX_OFF + slot * C::ASLOT;
+#pragma unroll
+                    for (uint32_t ks = 0; ks < 4u; ++ks) {
+                        const uint32_t acc = (hf | ks) != 0u ? 1u : 0u;
+                        const uint64_t db = umma_desc(bb + (4u * hf + ks) * C::BT);
+                        mma_i8(dh, umma_desc(ax + ks * C::ATILE), db, umma_idesc<NT>(), acc);
+                        mma_i8(dl, umma_desc(ax + (4u + ks) * C::ATILE), db, umma_idesc<NT>(), acc);
+                    }
+                    mma_commit(&aempty[slot]);
+                }
+                if (quit) break;
                 mma_commit(&tfull[buf]);
-                mma_commit(&aempty[slot]);
-                mma_commit(&empty[st]);
+                mma_commit(&bempty[sbi]);
                 ++issued;
             }
             if (issued) {
@@ -709,9 +788,9 @@ __global__ void __launch_bounds__(32 * Q4Cfg<NT>::WARPS, 1) mm_q4k_tc_kernel(MvA
         }
         __syncwarp();
     } else if (safe) {
-        q4k_epilogue<NT, true>(a, smem, full, empty, tfull, tempty, abort_flag, tmem, warp, lane);
+        q4k_epilogue<NT, true>(a, smem, efull, eempty, tfull, tempty, abort_flag, tmem, warp, lane);
     } else {
-        q4k_epilogue<NT, false>(a, smem, full, empty, tfull, tempty, abort_flag, tmem, warp, lane);
+        q4k_epilogue<NT, false>(a, smem, efull, eempty, tfull, tempty, abort_flag, tmem, warp, lane);
     }
     asm volatile("tcgen05.fence::before_thread_sync;");
     __syncthreads();
@@ -770,7 +849,7 @@ cudaError_t tc_error(uint32_t* code, bool clear) {
 // Q8_0 / Q4_K MUL_MAT of T tokens (their QA image in a.qx / a.dx / a.bsx) on the tensor cores.
 cudaError_t launch_mm_tc(uint32_t fmt, const MvArgs& a, cudaStream_t st) {
     if (a.T == 0 || a.n_rows == 0 || fmt > 1u) return cudaErrorInvalidValue;
-    if (fmt == 1u) return a.T <= 16 ? launch_q4k_nt<16>(a, st) : launch_q4k_nt<32>(a, st);
+    if (fmt == 1u) return a.T <= 16 ? launch_q4k_nt<16>(a, st) : a.T <= 32 ? launch_q4k_nt<32>(a, st) : launch_q4k_nt<64>(a, st);
     if (a.T <= 16) return launch_nt<16>(a, st);
     if (a.T <= 32) return launch_nt<32>(a, st);
     return launch_nt<64>(a, st);
