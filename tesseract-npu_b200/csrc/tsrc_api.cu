@@ -707,12 +707,11 @@ static int mul_mat_impl(tsrc_ctx* ctx, const tsrc_weight* w, const float* x, uin
     }
     if (T > tsrc::kMvMaxT && !isum_out && tc_enabled()) {
         // prefill: QACT of every token, then one tensor-core MUL_MAT over all of them
-        rc = ensure_scratch(ctx, qa_bytes(fmt, K, T) + align256((size_t)T * (K / 32u) * 2u));
+        rc = ensure_scratch(ctx, qa_bytes(fmt, K, T));
         if (rc) return rc;
         int8_t* q = reinterpret_cast<int8_t*>(ctx->scratch);
         float* d = reinterpret_cast<float*>(ctx->scratch + align256((size_t)T * K));
         int16_t* bs = reinterpret_cast<int16_t*>(ctx->scratch + align256((size_t)T * K) + align256((size_t)T * (K / block_of(fmt)) * 4u));
-        int16_t* bs2 = reinterpret_cast<int16_t*>(ctx->scratch + qa_bytes(fmt, K, T));
         cudaError_t e = tsrc::launch_qact(fmt == TSRC_FMT_Q8_0 ? 0u : 1u, x, K, T, x_stride, q, d, bs, st);
         if (e != cudaSuccess) return cuda_fail(e, "QACT launch");
         tsrc::MvArgs a{};
@@ -723,7 +722,6 @@ static int mul_mat_impl(tsrc_ctx* ctx, const tsrc_weight* w, const float* x, uin
         a.qx = q;
         a.dx = d;
         a.bsx = bs;
-        a.bs2x = bs2;
         a.T = T;
         a.y = y;
         a.y_stride = y_stride;

@@ -26,7 +26,6 @@ struct MvArgs {
     const int8_t* qx;         // QA of T tokens: q [T][K]
     const float* dx;          //                 d [T][K/bs]
     const int16_t* bsx;       //                 bs [T][K/16] (Q4_K)
-    int16_t* bs2x;            // Q4_K on the tensor cores: scratch for the pair sums bs2 [T][K/32]
     uint32_t T;
     float* y;                 // y [t * y_stride + n]
     uint32_t y_stride;

@@ -433,25 +433,29 @@ cudaError_t launch_nt(const MvArgs& a, cudaStream_t st) {
 // ---- Q4_K ---------------------------------------------------------------------------------------
 // The reference's superblock term (tsr_ref.c:540-567): isum = sum_j sc_j S_j over the eight 32-value
 // sub-blocks j (S_j = the int dot product of the nibbles and the activation), msum = sum_j m_j
-// (BS_2j + BS_2j+1), both int32, then d Dx isum - dmin Dx msum with the f32 rules. The tensor cores
-// apply the 6-bit scales themselves: with sc_j = 8 sh_j + sl_j (sh_j, sl_j in 0..7) the expanders
-// write two int8 A images of the superblock, sh_j q and sl_j q (each at most 7 x 15 = 105, so one
-// 32-bit multiply scales four packed nibbles without carries between them), and two MMA chains over
-// the whole superblock (K = 256, eight K = 32 steps each) give H = sum_j sh_j S_j and
-// L = sum_j sl_j S_j; isum = 8 H + L is the same integer (|isum| < 2^31). So an output costs two TMEM
-// values per superblock, not eight. The A256 scale Dx is an arbitrary f32: when every Dx of the CTA's
-// tokens is 0 or at least 2^-79 in magnitude, every product and sum is a multiple of 2^-126 and the
-// flush tests are skipped (SAFE); otherwise they run.
+// (BS_2j + BS_2j+1), both int32, then d Dx isum - dmin Dx msum with the f32 rules. All three integer
+// sums come from the tensor cores, over the whole superblock (K = 256, eight K = 32 steps):
+//  - with sc_j = 8 sh_j + sl_j (sh_j, sl_j in 0..7) the expanders write two int8 A images, sh_j q and
+//    sl_j q (each at most 7 x 15 = 105, so one 32-bit multiply scales four packed nibbles without
+//    carries between them); their chains give H = sum_j sh_j S_j and L = sum_j sl_j S_j, and
+//    isum = 8 H + L is the same integer (|isum| < 2^31);
+//  - a third image holds m_j in each of sub-block j's 32 columns: its chain gives sum_k m_j(k) x_k,
+//    which is msum, because the activation sums BS are the exact sums of the quantized activations
+//    (QACT writes them so: the reference's A256 rule).
+// So an output costs three TMEM values per superblock and a few f32 operations. The A256 scale Dx is
+// an arbitrary f32: when every Dx of the CTA's tokens is 0 or at least 2^-79 in magnitude, every
+// product and sum is a multiple of 2^-126 and the flush tests are skipped (SAFE); otherwise they run.
 //
 // Warp roles: E epilogue warps (32 rows x 16 tokens each), P producer warps (cp.async of the raw
 // quants, with the 16-byte chunks of a row rotated by the row so that the expanders read without
-// bank conflicts, the B tiles, Dx, the pair sums BS_2j + BS_2j+1 and the 16-byte row metadata into
-// three rings: the raw quants (S entries, free once expanded), the B tiles (SB entries, free once the
-// MMA has read them) and Dx, the pair sums and the metadata (SE entries, free once the expanders and
-// the epilogue have used them), so that no copy waits for a later role than the one that reads it),
-// X expander warps (one row per thread; a superblock in two halves of 128 values, each into one of
-// NA slots holding the H and L images of four K steps), one MMA warp. TMEM: NB accumulator pairs
-// (H then L, NT columns each) and the four levels of the partial trees' stacks (NT columns each).
+// bank conflicts, the B tiles, Dx and the 16-byte row metadata into three rings: the raw quants
+// (S entries, free once expanded), the B tiles (SB entries, free once the MMA has read them) and Dx
+// and the metadata (SE entries, free once the expanders and the epilogue have used them), so that no
+// copy waits for a later role than the one that reads it), X expander warps (one row per thread; a
+// superblock in two halves of 128 values, each into one of NA slots holding the H, L and M images of
+// four K steps), one MMA warp. TMEM: one accumulator triple (H, L, M: NT columns each; the epilogue
+// frees it as soon as it has read it, so the next superblock's MMAs overlap the f32 work) and the
+// four levels of the partial trees' stacks (NT columns each).
 // mbarriers: full/empty[S], bfull/bempty[SB], efull/eempty[SE], afull/aempty[NA], tfull/tempty[NB].
 constexpr uint32_t kSafeDxQ4 = 0x18000000u;            // 2^-79
 
@@ -459,15 +463,16 @@ template <uint32_t NT>
 struct Q4Cfg {
     static constexpr uint32_t E = 4u * (NT / 16u), P = 2u, X = 4u;
     static constexpr uint32_t WARPS = E + P + X + 1u, MMA_WARP = E + P + X;
-    static constexpr uint32_t S = 3u, SB = 4u, SE = 6u, NB = 2u, NA = 2u;
+    static constexpr uint32_t S = 3u, SB = 4u, SE = 6u, NB = 1u, NA = 2u;
     static constexpr uint32_t RAW = kTileM * 128u, BT = NT * 32u, ATILE = kTileM * 32u;
-    static constexpr uint32_t DX_OFF = 0u, BS_OFF = NT * 4u, META_OFF = BS_OFF + NT * 16u, EPI = META_OFF + kTileM * 16u;
+    static constexpr uint32_t DX_OFF = 0u, META_OFF = NT * 4u, EPI = META_OFF + kTileM * 16u;
     static constexpr size_t B_OFF = (size_t)S * RAW, E_OFF = B_OFF + (size_t)SB * 8u * BT;
-    static constexpr size_t AX_OFF = E_OFF + (size_t)SE * EPI, ASLOT = 8u * ATILE;    // H steps 0..3, L steps 0..3
+    static constexpr size_t AX_OFF = E_OFF + (size_t)SE * EPI, ASLOT = 12u * ATILE;   // H, L, M: steps 0..3 each
     static constexpr size_t BAR_OFF = AX_OFF + NA * ASLOT;
     static constexpr size_t SMEM = BAR_OFF + (2u * S + 2u * SB + 2u * SE + 2u * NA + 2u * NB) * 8u + 16u;
-    static constexpr uint32_t ACC_COLS = 2u * NT, STK_COL = NB * ACC_COLS, TCOLS = STK_COL + 4u * NT;
-    static_assert(TCOLS == 128u || TCOLS == 256u || TCOLS == 512u, "TMEM allocation is a power of two");
+    static constexpr uint32_t ACC_COLS = 3u * NT, STK_COL = NB * ACC_COLS, USED = STK_COL + 4u * NT;
+    static constexpr uint32_t TCOLS = USED <= 128u ? 128u : USED <= 256u ? 256u : 512u;
+    static_assert(USED <= 512u, "TMEM columns");
     static_assert(SMEM <= 227u * 1024u, "shared memory");
 };
 
@@ -528,15 +533,17 @@ __device__ __forceinline__ void q4k_epilogue(const MvArgs& a, uint8_t* smem, uin
         tmem_ld16(tl + buf * C::ACC_COLS, h);
         tmem_ld16(tl + buf * C::ACC_COLS + NT, l);
         const uint8_t* sb = smem + C::E_OFF + (size_t)se * C::EPI;
-        const uint4 m = reinterpret_cast<const uint4*>(sb + C::META_OFF)[32u * rq + lane];
-        const uint32_t mn_lo = m.z & 0x3F3F3F3Fu, mn_hi = ((m.w >> 4) & 0x0F0F0F0Fu) | ((m.z >> 2) & 0x30303030u);
-        const float dw = h2f((uint16_t)(m.x & 0xFFFFu)), dmw = h2f((uint16_t)(m.x >> 16));
+        const uint32_t mx = reinterpret_cast<const uint4*>(sb + C::META_OFF)[32u * rq + lane].x;
+        const float dw = h2f((uint16_t)(mx & 0xFFFFu)), dmw = h2f((uint16_t)(mx >> 16));
+        tmem_wait_ld();
+#pragma unroll
+        for (uint32_t i = 0; i < 16; ++i) h[i] = 8u * h[i] + l[i];            // isum = 8 H + L
+        tmem_ld16(tl + buf * C::ACC_COLS + 2u * NT, l);                     // msum
         tmem_wait_ld();
         asm volatile("tcgen05.fence::before_thread_sync;");
         __syncwarp();
         if (lane == 0) mbar_arrive(&tempty[buf]);
         const float4* dx4 = reinterpret_cast<const float4*>(sb + C::DX_OFF + 64u * cq);
-        const uint4* bs4 = reinterpret_cast<const uint4*>(sb + C::BS_OFF) + 16u * cq;
 #pragma unroll
         for (uint32_t k = 0; k < 4; ++k) {
             const float4 f = dx4[k];
@@ -544,9 +551,7 @@ __device__ __forceinline__ void q4k_epilogue(const MvArgs& a, uint8_t* smem, uin
 #pragma unroll
             for (uint32_t e = 0; e < 4; ++e) {
                 const uint32_t i = 4u * k + e;
-                const uint4 B = bs4[i];
-                const int32_t msum = dp2a_hi(B.w, mn_hi, dp2a_lo(B.z, mn_hi, dp2a_hi(B.y, mn_lo, dp2a_lo(B.x, mn_lo, 0))));
-                const int32_t isum = (int32_t)(8u * h[i] + l[i]);
+                const int32_t isum = (int32_t)h[i], msum = (int32_t)l[i];
                 const float Dx = d4[e];
                 if (SAFE) {
                     const float t1 = __fmul_rn(__fmul_rn(dw, Dx), __int2float_rn(isum));
@@ -663,7 +668,7 @@ __global__ void __launch_bounds__(32 * Q4Cfg<NT>::WARPS, 1) mm_q4k_tc_kernel(MvA
     if (warp >= C::E && warp < C::E + C::P) {
         // ---- producers
         constexpr uint32_t LN = 32u * C::P;
-        static_assert(LN >= NT && LN <= kTileM && LN % 8u == 0u, "one Dx / pair-sum copy per token, META rows by LN");
+        static_assert(LN >= NT && LN <= kTileM && LN % 8u == 0u, "one Dx copy per token, META rows by LN");
         const uint32_t pl = (warp - C::E) * 32u + lane, kk = pl & 7u;
         const size_t qrow = L.qs_row_bytes(), mrow = L.meta_row_bytes();
         for (uint32_t u = 0; u < nsb; ++u) {
@@ -679,11 +684,7 @@ __global__ void __launch_bounds__(32 * Q4Cfg<NT>::WARPS, 1) mm_q4k_tc_kernel(MvA
                 cp_async16(eb + C::META_OFF + 16u * r,
                            static_cast<const uint8_t*>(a.meta) + (size_t)min(row0 + r, a.n_rows - 1u) * mrow + 16u * sbk);
             }
-            if (pl < NT) {
-                const uint32_t tok = min(tok0 + pl, a.T - 1u);
-                cp_async4(eb + C::DX_OFF + 4u * pl, a.dx + (size_t)tok * nsb + sbk);
-                cp_async16(eb + C::BS_OFF + 16u * pl, a.bs2x + (size_t)tok * (K / 32u) + 8u * sbk);
-            }
+            if (pl < NT) cp_async4(eb + C::DX_OFF + 4u * pl, a.dx + (size_t)min(tok0 + pl, a.T - 1u) * nsb + sbk);
             cp_async_arrive(&efull[se]);                         // each entry is published when its copies land
             if (u >= C::S && !mbar_wait_ab(&empty[st], ((u / C::S) - 1u) & 1u, abort_flag)) break;
             uint8_t* sb = smem + (size_t)st * C::RAW;
@@ -719,6 +720,7 @@ __global__ void __launch_bounds__(32 * Q4Cfg<NT>::WARPS, 1) mm_q4k_tc_kernel(MvA
             const uint32_t sc_lo = m.y & 0x3F3F3F3Fu, sc_hi = (m.w & 0x0F0F0F0Fu) | ((m.y >> 2) & 0x30303030u);
             const uint32_t shw[2] = {(sc_lo >> 3) & 0x07070707u, (sc_hi >> 3) & 0x07070707u};
             const uint32_t slw[2] = {sc_lo & 0x07070707u, sc_hi & 0x07070707u};
+            const uint32_t mnw[2] = {m.z & 0x3F3F3F3Fu, ((m.w >> 4) & 0x0F0F0F0Fu) | ((m.z >> 2) & 0x30303030u)};
             if (!mbar_wait_ab(&full[st], (u / C::S) & 1u, abort_flag)) break;
             const uint8_t* raw = smem + (size_t)st * C::RAW + r * 128u;
             bool quit = false;
@@ -737,11 +739,15 @@ __global__ void __launch_bounds__(32 * Q4Cfg<NT>::WARPS, 1) mm_q4k_tc_kernel(MvA
                     const uint32_t sa = 2u * c, sbb = 2u * c + 1u;   // sub-blocks of the low and high nibbles
                     const uint32_t ha = (shw[sa >> 2] >> (8u * (sa & 3u))) & 0xFFu, la = (slw[sa >> 2] >> (8u * (sa & 3u))) & 0xFFu;
                     const uint32_t hb = (shw[sbb >> 2] >> (8u * (sbb & 3u))) & 0xFFu, lb = (slw[sbb >> 2] >> (8u * (sbb & 3u))) & 0xFFu;
+                    const uint32_t ma = ((mnw[sa >> 2] >> (8u * (sa & 3u))) & 0xFFu) * 0x01010101u;
+                    const uint32_t mb = ((mnw[sbb >> 2] >> (8u * (sbb & 3u))) & 0xFFu) * 0x01010101u;
                     const uint32_t ka = sa - 4u * hf, kb = sbb - 4u * hf;   // K steps within the half
                     *reinterpret_cast<uint4*>(ax + ka * C::ATILE + h * 128u) = make_uint4(lo.x * ha, lo.y * ha, lo.z * ha, lo.w * ha);
                     *reinterpret_cast<uint4*>(ax + (4u + ka) * C::ATILE + h * 128u) = make_uint4(lo.x * la, lo.y * la, lo.z * la, lo.w * la);
                     *reinterpret_cast<uint4*>(ax + kb * C::ATILE + h * 128u) = make_uint4(hi.x * hb, hi.y * hb, hi.z * hb, hi.w * hb);
                     *reinterpret_cast<uint4*>(ax + (4u + kb) * C::ATILE + h * 128u) = make_uint4(hi.x * lb, hi.y * lb, hi.z * lb, hi.w * lb);
+                    *reinterpret_cast<uint4*>(ax + (8u + ka) * C::ATILE + h * 128u) = make_uint4(ma, ma, ma, ma);
+                    *reinterpret_cast<uint4*>(ax + (8u + kb) * C::ATILE + h * 128u) = make_uint4(mb, mb, mb, mb);
                 }
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
                 __syncwarp();
@@ -760,7 +766,7 @@ __global__ void __launch_bounds__(32 * Q4Cfg<NT>::WARPS, 1) mm_q4k_tc_kernel(MvA
                 if (!mbar_wait_ab(&bfull[sbi], (u / C::SB) & 1u, abort_flag)) break;
                 if (u >= C::NB && !mbar_wait_ab(&tempty[buf], ((u / C::NB) - 1u) & 1u, abort_flag)) break;
                 uint8_t* bb = smem + C::B_OFF + (size_t)sbi * 8u * C::BT;
-                const uint32_t dh = tmem + buf * C::ACC_COLS, dl = dh + NT;
+                const uint32_t dh = tmem + buf * C::ACC_COLS, dl = dh + NT, dm = dh + 2u * NT;
 #pragma unroll
                 for (uint32_t hf = 0; hf < 2u; ++hf) {
                     const uint32_t hc = 2u * u + hf, slot = hc % C::NA;
@@ -773,6 +779,7 @@ __global__ void __launch_bounds__(32 * Q4Cfg<NT>::WARPS, 1) mm_q4k_tc_kernel(MvA
                         const uint64_t db = umma_desc(bb + (4u * hf + ks) * C::BT);
                         mma_i8(dh, umma_desc(ax + ks * C::ATILE), db, umma_idesc<NT>(), acc);
                         mma_i8(dl, umma_desc(ax + (4u + ks) * C::ATILE), db, umma_idesc<NT>(), acc);
+                        mma_i8(dm, umma_desc(ax + (8u + ks) * C::ATILE), db, umma_idesc<NT>(), acc);
                     }
                     mma_commit(&aempty[slot]);
                 }
@@ -800,11 +807,6 @@ __global__ void __launch_bounds__(32 * Q4Cfg<NT>::WARPS, 1) mm_q4k_tc_kernel(MvA
     }
 }
 
-// BS_2j + BS_2j+1 of every token (the Q4_K min sums' activation side), int16 exact (|sum| <= 4064)
-__global__ void bs_pairs_kernel(const int16_t* __restrict__ bs, int16_t* __restrict__ bs2, uint32_t n) {
-    const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
-    if (i < n) bs2[i] = (int16_t)((int32_t)bs[2u * i] + (int32_t)bs[2u * i + 1u]);
-}
 
 template <uint32_t NT>
 cudaError_t launch_q4k_nt(const MvArgs& a, cudaStream_t st) {
@@ -818,10 +820,6 @@ cudaError_t launch_q4k_nt(const MvArgs& a, cudaStream_t st) {
         if (e != cudaSuccess) return e;
         done_dev[dev] = dev + 1;
     }
-    const uint32_t n = a.T * (a.K / 32u);
-    bs_pairs_kernel<<<(n + 255u) / 256u, 256, 0, st>>>(a.bsx, const_cast<int16_t*>(a.bs2x), n);
-    e = cudaGetLastError();
-    if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((a.n_rows + kTileM - 1u) / kTileM, (a.T + NT - 1u) / NT);
     cfg.blockDim = dim3(32u * C::WARPS);
