@@ -20,6 +20,10 @@
 // handing work over through mbarriers. Every wait is bounded by the SM clock (~1 s); a wait that
 // runs out sets a CTA-wide abort flag that ends every role's loop, and error code 3, reported by
 // tsrc_sync.
+#include <cuda.h>                                  // CUtensorMap (the encoder is reached through the runtime)
+
+#include <mutex>
+
 #include "tsrc_internal.h"
 #include "tsrc_layout.cuh"
 #include "tsrc_numerics.cuh"
@@ -461,11 +465,12 @@ constexpr uint32_t kSafeDxQ4 = 0x18000000u;            // 2^-79
 
 template <uint32_t NT>
 struct Q4Cfg {
-    static constexpr uint32_t E = 4u * (NT / 16u), P = 2u, X = 4u;
+    static constexpr uint32_t E = 4u * (NT / 16u), P = 1u, X = 4u;
     static constexpr uint32_t WARPS = E + P + X + 1u, MMA_WARP = E + P + X;
     static constexpr uint32_t S = 3u, SB = 4u, SE = 6u, NB = 1u, NA = 2u;
     static constexpr uint32_t RAW = kTileM * 128u, BT = NT * 32u, ATILE = kTileM * 32u;
-    static constexpr uint32_t DX_OFF = 0u, META_OFF = NT * 4u, EPI = META_OFF + kTileM * 16u;
+    // ring entries start on 128-byte boundaries (TMA destinations); META first, then Dx
+    static constexpr uint32_t META_OFF = 0u, DX_OFF = kTileM * 16u, EPI = DX_OFF + ((NT * 4u + 127u) & ~127u);
     static constexpr size_t B_OFF = (size_t)S * RAW, E_OFF = B_OFF + (size_t)SB * 8u * BT;
     static constexpr size_t AX_OFF = E_OFF + (size_t)SE * EPI, ASLOT = 12u * ATILE;   // H, L, M: steps 0..3 each
     static constexpr size_t BAR_OFF = AX_OFF + NA * ASLOT;
@@ -474,7 +479,61 @@ struct Q4Cfg {
     static constexpr uint32_t TCOLS = USED <= 128u ? 128u : USED <= 256u ? 256u : 512u;
     static_assert(USED <= 512u, "TMEM columns");
     static_assert(SMEM <= 227u * 1024u, "shared memory");
+    static_assert(NT % 32u == 0u || NT < 32u, "Dx copies by the producer warp's lanes");
 };
+
+// Tensor maps of one launch (TMA, no swizzle, no multicast):
+//  raw:  the Q4_K quants of the full 16-superblock tiles, dims {256 B of a chunk line, row, chunk, tile}
+//        (strides {qrow, 256, 2048}), box {16, 128, 8, 1}: superblock b of 128 rows lands as
+//        smem[2048 chunk + 16 row + byte], so the expanders' reads of one chunk of consecutive rows are
+//        consecutive 16-byte words;
+//  tail: the same for the last tile when it holds nv < 16 superblocks (chunk stride 16 nv);
+//  b:    the QA image, dims {16 B, token, half, 32-value group} (strides {K, 16, 32}), box {16, NT, 2, 8}:
+//        a superblock's B tiles land as smem[32 NT group + 16 NT half + 16 token + byte], the K-major
+//        no-swizzle UMMA layout with LBO = 16 NT (K halves) and SBO = 128 (8-token groups);
+//  meta: the 16-byte metadata, dims {16 nsb, row}, box {16, 128}.
+struct alignas(64) Q4Maps {
+    CUtensorMap raw, tail, b, meta;
+    uint32_t nfull;        // tiles of 16 superblocks in a row; superblocks from 16 nfull on are in the tail
+};
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* b, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(b)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* m, int32_t c0, int32_t c1, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+        ::"r"(smem_u32(dst)), "l"(m), "r"(c0), "r"(c1), "r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* m, int32_t c0, int32_t c1, int32_t c2, int32_t c3,
+                                            uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], [%6];"
+        ::"r"(smem_u32(dst)), "l"(m), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_u32(bar)) : "memory");
+}
+// Bounded wait that ignores the abort flag: the producer's last look at the loads it issued, so that
+// no TMA write lands in this CTA's shared memory after it has exited
+__device__ __forceinline__ void mbar_wait_drain(uint64_t* b, uint32_t parity) {
+    const uint32_t bar = smem_u32(b);
+    const long long t0 = clock64();
+    for (;;) {
+        uint32_t ok;
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+            "selp.u32 %0, 1, 0, p;\n\t}"
+            : "=r"(ok)
+            : "r"(bar), "r"(parity), "r"(1000u)
+            : "memory");
+        if (ok || clock64() - t0 > kWaitCycles) return;
+    }
+}
+// UMMA descriptor of a B image laid out by the b map: K-major, no swizzle, LBO = 16 NT, SBO = 128
+template <uint32_t NT>
+__device__ __forceinline__ uint64_t umma_desc_b(const void* p) {
+    const uint64_t a = (smem_u32(p) >> 4) & 0x3FFFu;
+    return a | (uint64_t((16u * NT) >> 4) << 16) | (uint64_t(128u >> 4) << 32) | (uint64_t(1) << 46);
+}
 
 __device__ __forceinline__ void tmem_st16(uint32_t taddr, const float (&v)[16]) {
     asm volatile(
@@ -601,7 +660,7 @@ __device__ __forceinline__ void q4k_epilogue(const MvArgs& a, uint8_t* smem, uin
 }
 
 template <uint32_t NT>
-__global__ void __launch_bounds__(32 * Q4Cfg<NT>::WARPS, 1) mm_q4k_tc_kernel(MvArgs a) {
+__global__ void __launch_bounds__(32 * Q4Cfg<NT>::WARPS, 1) mm_q4k_tc_kernel(MvArgs a, const __grid_constant__ Q4Maps tm) {
     using C = Q4Cfg<NT>;
     extern __shared__ __align__(128) uint8_t smem[];
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::BAR_OFF);
@@ -628,15 +687,15 @@ __global__ void __launch_bounds__(32 * Q4Cfg<NT>::WARPS, 1) mm_q4k_tc_kernel(MvA
     }
     if (threadIdx.x == 0) {
         for (uint32_t i = 0; i < C::S; ++i) {
-            mbar_init(&full[i], 32u * C::P);
+            mbar_init(&full[i], 1u);                             // the TMA issuer's arrive.expect_tx
             mbar_init(&empty[i], C::X);
         }
         for (uint32_t i = 0; i < C::SB; ++i) {
-            mbar_init(&bfull[i], 32u * C::P);
+            mbar_init(&bfull[i], 1u);
             mbar_init(&bempty[i], 1u);
         }
         for (uint32_t i = 0; i < C::SE; ++i) {
-            mbar_init(&efull[i], 32u * C::P);
+            mbar_init(&efull[i], 1u + 32u);                      // expect_tx (META) + every lane's Dx cp.async
             mbar_init(&eempty[i], C::E + C::X);
         }
         for (uint32_t i = 0; i < C::NA; ++i) {
@@ -666,11 +725,9 @@ __global__ void __launch_bounds__(32 * Q4Cfg<NT>::WARPS, 1) mm_q4k_tc_kernel(MvA
     const uint32_t tmem = *tslot;
 
     if (warp >= C::E && warp < C::E + C::P) {
-        // ---- producers
-        constexpr uint32_t LN = 32u * C::P;
-        static_assert(LN >= NT && LN <= kTileM && LN % 8u == 0u, "one Dx copy per token, META rows by LN");
-        const uint32_t pl = (warp - C::E) * 32u + lane, kk = pl & 7u;
-        const size_t qrow = L.qs_row_bytes(), mrow = L.meta_row_bytes();
+        // ---- producer warp: lane 0 issues the TMA loads (META, raw quants, B tiles); the lanes copy Dx
+        const uint32_t nfull = tm.nfull;
+        uint32_t ne = 0, nr = 0, nb = 0;                         // loads issued into each ring
         for (uint32_t u = 0; u < nsb; ++u) {
             const uint32_t st = u % C::S, sbi = u % C::SB, se = u % C::SE;
             uint32_t jb;
@@ -678,34 +735,40 @@ __global__ void __launch_bounds__(32 * Q4Cfg<NT>::WARPS, 1) mm_q4k_tc_kernel(MvA
             const uint32_t sbk = Seq{nsb, q, rem}.block(u, &jb, &lb);
             if (u >= C::SE && !mbar_wait_ab(&eempty[se], ((u / C::SE) - 1u) & 1u, abort_flag)) break;
             uint8_t* eb = smem + C::E_OFF + (size_t)se * C::EPI;
-#pragma unroll
-            for (uint32_t k = 0; k < kTileM / LN; ++k) {
-                const uint32_t r = pl + LN * k;
-                cp_async16(eb + C::META_OFF + 16u * r,
-                           static_cast<const uint8_t*>(a.meta) + (size_t)min(row0 + r, a.n_rows - 1u) * mrow + 16u * sbk);
+            if (lane == 0) {
+                mbar_expect_tx(&efull[se], kTileM * 16u);
+                tma_load_2d(eb + C::META_OFF, &tm.meta, (int32_t)(16u * sbk), (int32_t)row0, &efull[se]);
             }
-            if (pl < NT) cp_async4(eb + C::DX_OFF + 4u * pl, a.dx + (size_t)min(tok0 + pl, a.T - 1u) * nsb + sbk);
+            ++ne;
+#pragma unroll
+            for (uint32_t t = lane; t < NT; t += 32u)
+                cp_async4(eb + C::DX_OFF + 4u * t, a.dx + (size_t)min(tok0 + t, a.T - 1u) * nsb + sbk);
             cp_async_arrive(&efull[se]);                         // each entry is published when its copies land
             if (u >= C::S && !mbar_wait_ab(&empty[st], ((u / C::S) - 1u) & 1u, abort_flag)) break;
-            uint8_t* sb = smem + (size_t)st * C::RAW;
-            const size_t qoff = L.qs_off(0u, sbk, kk);
-#pragma unroll 4
-            for (uint32_t k = 0; k < 1024u / LN; ++k) {          // raw quants: row (pl / 8) + 8 k, chunk pl & 7
-                const uint32_t r = (pl >> 3) + (LN / 8u) * k;
-                cp_async16(sb + r * 128u + ((kk ^ (r & 7u)) * 16u), a.qs + (size_t)min(row0 + r, a.n_rows - 1u) * qrow + qoff);
+            if (lane == 0) {
+                mbar_expect_tx(&full[st], C::RAW);
+                const bool in_full = (sbk >> 4) < nfull;
+                tma_load_4d(smem + (size_t)st * C::RAW, in_full ? &tm.raw : &tm.tail, (int32_t)(16u * (sbk & 15u)),
+                            (int32_t)row0, 0, in_full ? (int32_t)(sbk >> 4) : 0, &full[st]);
             }
-            cp_async_arrive(&full[st]);
+            ++nr;
             if (u >= C::SB && !mbar_wait_ab(&bempty[sbi], ((u / C::SB) - 1u) & 1u, abort_flag)) break;
-            uint8_t* bb = smem + C::B_OFF + (size_t)sbi * 8u * C::BT;
-#pragma unroll 4
-            for (uint32_t k = 0; k < 16u * NT / LN; ++k) {       // B tiles: (sub-block, token, half)
-                const uint32_t idx = pl + LN * k, h = idx & 1u, t = (idx >> 1) % NT, jj = (idx >> 1) / NT;
-                cp_async16(bb + jj * C::BT + (t >> 3) * 256u + h * 128u + (t & 7u) * 16u,
-                           a.qx + (size_t)min(tok0 + t, a.T - 1u) * K + 256u * sbk + 32u * jj + 16u * h);
+            if (lane == 0) {
+                mbar_expect_tx(&bfull[sbi], 8u * C::BT);
+                tma_load_4d(smem + C::B_OFF + (size_t)sbi * 8u * C::BT, &tm.b, 0, (int32_t)tok0, 0, (int32_t)(8u * sbk),
+                            &bfull[sbi]);
             }
-            cp_async_arrive(&bfull[sbi]);
+            ++nb;
         }
         cp_async_wait<0>();
+        if (lane == 0) {
+            // the last load into each ring entry has landed before the CTA may exit (on every path: a
+            // consumer has waited for it already unless a wait gave up)
+            for (uint32_t v = ne > C::SE ? ne - C::SE : 0u; v < ne; ++v) mbar_wait_drain(&efull[v % C::SE], (v / C::SE) & 1u);
+            for (uint32_t v = nr > C::S ? nr - C::S : 0u; v < nr; ++v) mbar_wait_drain(&full[v % C::S], (v / C::S) & 1u);
+            for (uint32_t v = nb > C::SB ? nb - C::SB : 0u; v < nb; ++v) mbar_wait_drain(&bfull[v % C::SB], (v / C::SB) & 1u);
+        }
+        __syncwarp();
     } else if (warp >= C::E + C::P && warp < C::MMA_WARP) {
         // ---- expanders: thread r owns row r of the tile
         const uint32_t r = (warp - C::E - C::P) * 32u + lane;
@@ -722,7 +785,7 @@ __global__ void __launch_bounds__(32 * Q4Cfg<NT>::WARPS, 1) mm_q4k_tc_kernel(MvA
             const uint32_t slw[2] = {sc_lo & 0x07070707u, sc_hi & 0x07070707u};
             const uint32_t mnw[2] = {m.z & 0x3F3F3F3Fu, ((m.w >> 4) & 0x0F0F0F0Fu) | ((m.z >> 2) & 0x30303030u)};
             if (!mbar_wait_ab(&full[st], (u / C::S) & 1u, abort_flag)) break;
-            const uint8_t* raw = smem + (size_t)st * C::RAW + r * 128u;
+            const uint8_t* raw = smem + (size_t)st * C::RAW + r * 16u;         // chunk k at + 2048 k
             bool quit = false;
 #pragma unroll
             for (uint32_t hf = 0; hf < 2u; ++hf) {               // values 128 hf .. 128 hf + 127: sub-blocks 4 hf .. 4 hf + 3
@@ -732,7 +795,7 @@ __global__ void __launch_bounds__(32 * Q4Cfg<NT>::WARPS, 1) mm_q4k_tc_kernel(MvA
 #pragma unroll
                 for (uint32_t kq = 0; kq < 4u; ++kq) {           // chunk k: low nibbles -> sub-block 2 (k / 2), high -> +1
                     const uint32_t k = 4u * hf + kq, c = k >> 1, h = k & 1u;
-                    const uint4 w = *reinterpret_cast<const uint4*>(raw + ((k ^ (r & 7u)) * 16u));
+                    const uint4 w = *reinterpret_cast<const uint4*>(raw + k * 2048u);
                     const uint4 lo = make_uint4(w.x & 0x0F0F0F0Fu, w.y & 0x0F0F0F0Fu, w.z & 0x0F0F0F0Fu, w.w & 0x0F0F0F0Fu);
                     const uint4 hi = make_uint4((w.x >> 4) & 0x0F0F0F0Fu, (w.y >> 4) & 0x0F0F0F0Fu, (w.z >> 4) & 0x0F0F0F0Fu,
                                                 (w.w >> 4) & 0x0F0F0F0Fu);
@@ -776,7 +839,7 @@ __global__ void __launch_bounds__(32 * Q4Cfg<NT>::WARPS, 1) mm_q4k_tc_kernel(MvA
 #pragma unroll
                     for (uint32_t ks = 0; ks < 4u; ++ks) {
                         const uint32_t acc = (hf | ks) != 0u ? 1u : 0u;
-                        const uint64_t db = umma_desc(bb + (4u * hf + ks) * C::BT);
+                        const uint64_t db = umma_desc_b<NT>(bb + (4u * hf + ks) * C::BT);
                         mma_i8(dh, umma_desc(ax + ks * C::ATILE), db, umma_idesc<NT>(), acc);
                         mma_i8(dl, umma_desc(ax + (4u + ks) * C::ATILE), db, umma_idesc<NT>(), acc);
                         mma_i8(dm, umma_desc(ax + (8u + ks) * C::ATILE), db, umma_idesc<NT>(), acc);
@@ -808,6 +871,51 @@ __global__ void __launch_bounds__(32 * Q4Cfg<NT>::WARPS, 1) mm_q4k_tc_kernel(MvA
 }
 
 
+// cuTensorMapEncodeTiled, from the driver through the runtime (no link against libcuda)
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*, const cuuint64_t*,
+                                   const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+EncodeTiledFn encode_tiled() {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    });
+    return fn;
+}
+
+// a rank-R uint8 tiled map, no swizzle; dims / strides in bytes (strides of dims 1 .. R-1)
+template <int R>
+bool encode_u8(CUtensorMap* m, const void* base, const cuuint64_t (&dims)[R], const cuuint64_t (&strides)[R - 1],
+               const cuuint32_t (&box)[R]) {
+    EncodeTiledFn fn = encode_tiled();
+    if (!fn) return false;
+    cuuint32_t es[R];
+    for (int i = 0; i < R; ++i) es[i] = 1;
+    return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, (cuuint32_t)R, const_cast<void*>(base), dims, strides, box, es,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <uint32_t NT>
+bool make_q4_maps(const MvArgs& a, Q4Maps* tm) {
+    const Layout L{1u, a.K};
+    const uint32_t nsb = a.K / 256u, nfull = nsb / 16u, nv = nsb % 16u;
+    const cuuint64_t qrow = L.qs_row_bytes(), rows = a.n_rows;
+    *tm = Q4Maps{};
+    tm->nfull = nfull;
+    if (nfull && !encode_u8<4>(&tm->raw, a.qs, {256, rows, 8, nfull}, {qrow, 256, 2048}, {16, kTileM, 8, 1})) return false;
+    if (nv && !encode_u8<4>(&tm->tail, a.qs + (size_t)nfull * 2048u, {16ull * nv, rows, 8, 1}, {qrow, 16ull * nv, 128ull * nv},
+                            {16, kTileM, 8, 1}))
+        return false;
+    if (!encode_u8<4>(&tm->b, a.qx, {16, a.T, 2, a.K / 32u}, {a.K, 16, 32}, {16, NT, 2, 8})) return false;
+    return encode_u8<2>(&tm->meta, a.meta, {16ull * nsb, rows}, {L.meta_row_bytes()}, {16, kTileM});
+}
+
 template <uint32_t NT>
 cudaError_t launch_q4k_nt(const MvArgs& a, cudaStream_t st) {
     using C = Q4Cfg<NT>;
@@ -830,7 +938,9 @@ cudaError_t launch_q4k_nt(const MvArgs& a, cudaStream_t st) {
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, mm_q4k_tc_kernel<NT>, a);
+    Q4Maps tm;
+    if (!make_q4_maps<NT>(a, &tm)) return cudaErrorInvalidValue;
+    return cudaLaunchKernelEx(&cfg, mm_q4k_tc_kernel<NT>, a, tm);
 }
 
 }  // namespace
