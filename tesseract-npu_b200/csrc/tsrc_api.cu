@@ -707,12 +707,14 @@ static int mul_mat_impl(tsrc_ctx* ctx, const tsrc_weight* w, const float* x, uin
     }
     if (T > tsrc::kMvMaxT && !isum_out && tc_enabled()) {
         // prefill: QACT of every token, then one tensor-core MUL_MAT over all of them
-        rc = ensure_scratch(ctx, qa_bytes(fmt, K, T));
+        const bool q4 = fmt == TSRC_FMT_Q4_K;
+        rc = ensure_scratch(ctx, qa_bytes(fmt, K, T) + (q4 ? align256((size_t)T * (K / 16u)) : 0u));
         if (rc) return rc;
         int8_t* q = reinterpret_cast<int8_t*>(ctx->scratch);
         float* d = reinterpret_cast<float*>(ctx->scratch + align256((size_t)T * K));
         int16_t* bs = reinterpret_cast<int16_t*>(ctx->scratch + align256((size_t)T * K) + align256((size_t)T * (K / block_of(fmt)) * 4u));
-        cudaError_t e = tsrc::launch_qact(fmt == TSRC_FMT_Q8_0 ? 0u : 1u, x, K, T, x_stride, q, d, bs, st);
+        int8_t* bsd = q4 ? reinterpret_cast<int8_t*>(ctx->scratch + qa_bytes(fmt, K, T)) : nullptr;
+        cudaError_t e = tsrc::launch_qact(fmt == TSRC_FMT_Q8_0 ? 0u : 1u, x, K, T, x_stride, q, d, bs, st, bsd);
         if (e != cudaSuccess) return cuda_fail(e, "QACT launch");
         tsrc::MvArgs a{};
         a.qs = w->qs;
@@ -722,6 +724,7 @@ static int mul_mat_impl(tsrc_ctx* ctx, const tsrc_weight* w, const float* x, uin
         a.qx = q;
         a.dx = d;
         a.bsx = bs;
+        a.bsd = bsd;
         a.T = T;
         a.y = y;
         a.y_stride = y_stride;

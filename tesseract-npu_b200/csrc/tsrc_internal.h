@@ -26,6 +26,7 @@ struct MvArgs {
     const int8_t* qx;         // QA of T tokens: q [T][K]
     const float* dx;          //                 d [T][K/bs]
     const int16_t* bsx;       //                 bs [T][K/16] (Q4_K)
+    const int8_t* bsd;        //                 Q4_K on the tensor cores: pair-sum digits [T][K/256][16]
     uint32_t T;
     float* y;                 // y [t * y_stride + n]
     uint32_t y_stride;
@@ -58,7 +59,7 @@ struct MvArgs {
 };
 
 cudaError_t launch_qact(uint32_t kind, const float* x, uint32_t K, uint32_t T, uint32_t x_stride, int8_t* q, float* d,
-                        int16_t* bs, cudaStream_t st);
+                        int16_t* bs, cudaStream_t st, int8_t* bsd = nullptr);
 cudaError_t launch_matvec(uint32_t fmt, const MvArgs& a, cudaStream_t st);
 // All-gather of a plain vector over a team (the tagged-word exchange of the fused MUL_MAT, without
 // the MUL_MAT): src [n_local] of this rank lands at dst[offset .. offset + n_local) on every rank.

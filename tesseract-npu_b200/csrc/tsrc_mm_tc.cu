@@ -443,10 +443,11 @@ cudaError_t launch_nt(const MvArgs& a, cudaStream_t st) {
 //    sl_j q (each at most 7 x 15 = 105, so one 32-bit multiply scales four packed nibbles without
 //    carries between them); their chains give H = sum_j sh_j S_j and L = sum_j sl_j S_j, and
 //    isum = 8 H + L is the same integer (|isum| < 2^31);
-//  - a third image holds m_j in each of sub-block j's 32 columns: its chain gives sum_k m_j(k) x_k,
-//    which is msum, because the activation sums BS are the exact sums of the quantized activations
-//    (QACT writes them so: the reference's A256 rule).
-// So an output costs three TMEM values per superblock and a few f32 operations. The A256 scale Dx is
+//  - msum = sum_j m_j p_j with the sub-block sums p_j = BS_2j + BS_2j+1 of the activation: QACT writes
+//    p_j as two int8 digits, p_j = 64 hi_j + lo_j, 16 bytes per token and superblock; two K = 32 MMAs
+//    with A rows {m_0 .. m_7, 0 ...} and {0 x 8, m_0 .. m_7, 0 ...} against the digit rows give
+//    Dlo = sum_j m_j lo_j and Dhi = sum_j m_j hi_j, and msum = Dlo + 64 Dhi.
+// So an output costs four TMEM values per superblock and a few f32 operations. The A256 scale Dx is
 // an arbitrary f32: when every Dx of the CTA's tokens is 0 or at least 2^-79 in magnitude, every
 // product and sum is a multiple of 2^-126 and the flush tests are skipped (SAFE); otherwise they run.
 //
@@ -456,10 +457,11 @@ cudaError_t launch_nt(const MvArgs& a, cudaStream_t st) {
 // (S entries, free once expanded), the B tiles (SB entries, free once the MMA has read them) and Dx
 // and the metadata (SE entries, free once the expanders and the epilogue have used them), so that no
 // copy waits for a later role than the one that reads it), X expander warps (one row per thread; a
-// superblock in two halves of 128 values, each into one of NA slots holding the H, L and M images of
-// four K steps), one MMA warp. TMEM: one accumulator triple (H, L, M: NT columns each; the epilogue
-// frees it as soon as it has read it, so the next superblock's MMAs overlap the f32 work) and the
-// four levels of the partial trees' stacks (NT columns each).
+// superblock in two halves of 128 values, each into one of NA slots holding the H and L images of
+// four K steps; slot 0 also holds the two mins rows), one MMA warp. TMEM: one accumulator set (H, L,
+// Dlo, Dhi: NT columns each; the epilogue frees it as soon as it has read it, so the next
+// superblock's MMAs overlap the f32 work) and the four levels of the partial trees' stacks (NT
+// columns each). The second K halves of the mins rows and of the digit rows are zero, written once.
 // mbarriers: full/empty[S], bfull/bempty[SB], efull/eempty[SE], afull/aempty[NA], tfull/tempty[NB].
 constexpr uint32_t kSafeDxQ4 = 0x18000000u;            // 2^-79
 
@@ -471,15 +473,17 @@ struct Q4Cfg {
     static constexpr uint32_t RAW = kTileM * 128u, BT = NT * 32u, ATILE = kTileM * 32u;
     // ring entries start on 128-byte boundaries (TMA destinations); META first, then Dx
     static constexpr uint32_t META_OFF = 0u, DX_OFF = kTileM * 16u, EPI = DX_OFF + ((NT * 4u + 127u) & ~127u);
-    static constexpr size_t B_OFF = (size_t)S * RAW, E_OFF = B_OFF + (size_t)SB * 8u * BT;
-    static constexpr size_t AX_OFF = E_OFF + (size_t)SE * EPI, ASLOT = 12u * ATILE;   // H, L, M: steps 0..3 each
+    static constexpr uint32_t BENT = 9u * BT;            // B ring entry: eight sub-block tiles, the digit rows
+    static constexpr size_t B_OFF = (size_t)S * RAW, E_OFF = B_OFF + (size_t)SB * BENT;
+    static constexpr size_t AX_OFF = E_OFF + (size_t)SE * EPI, ASLOT = 10u * ATILE;   // H 0..3, L 0..3, mins lo, hi
     static constexpr size_t BAR_OFF = AX_OFF + NA * ASLOT;
     static constexpr size_t SMEM = BAR_OFF + (2u * S + 2u * SB + 2u * SE + 2u * NA + 2u * NB) * 8u + 16u;
-    static constexpr uint32_t ACC_COLS = 3u * NT, STK_COL = NB * ACC_COLS, USED = STK_COL + 4u * NT;
+    static constexpr uint32_t ACC_COLS = 4u * NT, STK_COL = NB * ACC_COLS, USED = STK_COL + 4u * NT;
     static constexpr uint32_t TCOLS = USED <= 128u ? 128u : USED <= 256u ? 256u : 512u;
     static_assert(USED <= 512u, "TMEM columns");
     static_assert(SMEM <= 227u * 1024u, "shared memory");
     static_assert(NT % 32u == 0u || NT < 32u, "Dx copies by the producer warp's lanes");
+    static_assert(NA == 2u, "half 0 of every superblock (and the mins rows) in slot 0");
 };
 
 // Tensor maps of one launch (TMA, no swizzle, no multicast):
@@ -491,9 +495,10 @@ struct Q4Cfg {
 //  b:    the QA image, dims {16 B, token, half, 32-value group} (strides {K, 16, 32}), box {16, NT, 2, 8}:
 //        a superblock's B tiles land as smem[32 NT group + 16 NT half + 16 token + byte], the K-major
 //        no-swizzle UMMA layout with LBO = 16 NT (K halves) and SBO = 128 (8-token groups);
-//  meta: the 16-byte metadata, dims {16 nsb, row}, box {16, 128}.
+//  meta: the 16-byte metadata, dims {16 nsb, row}, box {16, 128};
+//  dig:  QACT's pair-sum digits, dims {16 nsb, token}, box {16, NT}: the first K half of the digit rows.
 struct alignas(64) Q4Maps {
-    CUtensorMap raw, tail, b, meta;
+    CUtensorMap raw, tail, b, meta, dig;
     uint32_t nfull;        // tiles of 16 superblocks in a row; superblocks from 16 nfull on are in the tail
 };
 
@@ -597,8 +602,12 @@ __device__ __forceinline__ void q4k_epilogue(const MvArgs& a, uint8_t* smem, uin
         tmem_wait_ld();
 #pragma unroll
         for (uint32_t i = 0; i < 16; ++i) h[i] = 8u * h[i] + l[i];            // isum = 8 H + L
-        tmem_ld16(tl + buf * C::ACC_COLS + 2u * NT, l);                     // msum
+        uint32_t g[16];
+        tmem_ld16(tl + buf * C::ACC_COLS + 2u * NT, l);                     // Dlo
+        tmem_ld16(tl + buf * C::ACC_COLS + 3u * NT, g);                     // Dhi
         tmem_wait_ld();
+#pragma unroll
+        for (uint32_t i = 0; i < 16; ++i) l[i] += 64u * g[i];              // msum = Dlo + 64 Dhi
         asm volatile("tcgen05.fence::before_thread_sync;");
         __syncwarp();
         if (lane == 0) mbar_arrive(&tempty[buf]);
@@ -719,6 +728,14 @@ __global__ void __launch_bounds__(32 * Q4Cfg<NT>::WARPS, 1) mm_q4k_tc_kernel(MvA
             ok = ok && (u == 0u || u >= kSafeDxQ4);
         }
     }
+    // the zero second K halves of the digit rows (one per B ring entry) and of the mins rows (slot 0)
+    for (uint32_t i = threadIdx.x; i < C::SB * NT + 2u * kTileM; i += 32u * C::WARPS) {
+        uint8_t* z = i < C::SB * NT ? smem + C::B_OFF + (size_t)(i / NT) * C::BENT + 8u * C::BT + 16u * NT + 16u * (i % NT)
+                                    : smem + C::AX_OFF + (8u + (i - C::SB * NT) / kTileM) * C::ATILE + 128u +
+                                          ((i - C::SB * NT) % kTileM >> 3) * 256u + ((i - C::SB * NT) % 8u) * 16u;
+        *reinterpret_cast<uint4*>(z) = make_uint4(0u, 0u, 0u, 0u);
+    }
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     asm volatile("tcgen05.fence::before_thread_sync;");
     const bool safe = __syncthreads_and(ok) != 0;
     asm volatile("tcgen05.fence::after_thread_sync;");
@@ -754,9 +771,10 @@ __global__ void __launch_bounds__(32 * Q4Cfg<NT>::WARPS, 1) mm_q4k_tc_kernel(MvA
             ++nr;
             if (u >= C::SB && !mbar_wait_ab(&bempty[sbi], ((u / C::SB) - 1u) & 1u, abort_flag)) break;
             if (lane == 0) {
-                mbar_expect_tx(&bfull[sbi], 8u * C::BT);
-                tma_load_4d(smem + C::B_OFF + (size_t)sbi * 8u * C::BT, &tm.b, 0, (int32_t)tok0, 0, (int32_t)(8u * sbk),
-                            &bfull[sbi]);
+                uint8_t* bb = smem + C::B_OFF + (size_t)sbi * C::BENT;
+                mbar_expect_tx(&bfull[sbi], 8u * C::BT + 16u * NT);
+                tma_load_4d(bb, &tm.b, 0, (int32_t)tok0, 0, (int32_t)(8u * sbk), &bfull[sbi]);
+                tma_load_2d(bb + 8u * C::BT, &tm.dig, (int32_t)(16u * sbk), (int32_t)tok0, &bfull[sbi]);
             }
             ++nb;
         }
@@ -783,7 +801,7 @@ __global__ void __launch_bounds__(32 * Q4Cfg<NT>::WARPS, 1) mm_q4k_tc_kernel(MvA
             const uint32_t sc_lo = m.y & 0x3F3F3F3Fu, sc_hi = (m.w & 0x0F0F0F0Fu) | ((m.y >> 2) & 0x30303030u);
             const uint32_t shw[2] = {(sc_lo >> 3) & 0x07070707u, (sc_hi >> 3) & 0x07070707u};
             const uint32_t slw[2] = {sc_lo & 0x07070707u, sc_hi & 0x07070707u};
-            const uint32_t mnw[2] = {m.z & 0x3F3F3F3Fu, ((m.w >> 4) & 0x0F0F0F0Fu) | ((m.z >> 2) & 0x30303030u)};
+            const uint32_t mn_lo = m.z & 0x3F3F3F3Fu, mn_hi = ((m.w >> 4) & 0x0F0F0F0Fu) | ((m.z >> 2) & 0x30303030u);
             if (!mbar_wait_ab(&full[st], (u / C::S) & 1u, abort_flag)) break;
             const uint8_t* raw = smem + (size_t)st * C::RAW + r * 16u;         // chunk k at + 2048 k
             bool quit = false;
@@ -802,15 +820,15 @@ __global__ void __launch_bounds__(32 * Q4Cfg<NT>::WARPS, 1) mm_q4k_tc_kernel(MvA
                     const uint32_t sa = 2u * c, sbb = 2u * c + 1u;   // sub-blocks of the low and high nibbles
                     const uint32_t ha = (shw[sa >> 2] >> (8u * (sa & 3u))) & 0xFFu, la = (slw[sa >> 2] >> (8u * (sa & 3u))) & 0xFFu;
                     const uint32_t hb = (shw[sbb >> 2] >> (8u * (sbb & 3u))) & 0xFFu, lb = (slw[sbb >> 2] >> (8u * (sbb & 3u))) & 0xFFu;
-                    const uint32_t ma = ((mnw[sa >> 2] >> (8u * (sa & 3u))) & 0xFFu) * 0x01010101u;
-                    const uint32_t mb = ((mnw[sbb >> 2] >> (8u * (sbb & 3u))) & 0xFFu) * 0x01010101u;
                     const uint32_t ka = sa - 4u * hf, kb = sbb - 4u * hf;   // K steps within the half
                     *reinterpret_cast<uint4*>(ax + ka * C::ATILE + h * 128u) = make_uint4(lo.x * ha, lo.y * ha, lo.z * ha, lo.w * ha);
                     *reinterpret_cast<uint4*>(ax + (4u + ka) * C::ATILE + h * 128u) = make_uint4(lo.x * la, lo.y * la, lo.z * la, lo.w * la);
                     *reinterpret_cast<uint4*>(ax + kb * C::ATILE + h * 128u) = make_uint4(hi.x * hb, hi.y * hb, hi.z * hb, hi.w * hb);
                     *reinterpret_cast<uint4*>(ax + (4u + kb) * C::ATILE + h * 128u) = make_uint4(hi.x * lb, hi.y * lb, hi.z * lb, hi.w * lb);
-                    *reinterpret_cast<uint4*>(ax + (8u + ka) * C::ATILE + h * 128u) = make_uint4(ma, ma, ma, ma);
-                    *reinterpret_cast<uint4*>(ax + (8u + kb) * C::ATILE + h * 128u) = make_uint4(mb, mb, mb, mb);
+                }
+                if (hf == 0u) {                                  // the mins rows: {m_0 .. m_7, 0 x 8}, {0 x 8, m_0 .. m_7}
+                    *reinterpret_cast<uint4*>(ax + 8u * C::ATILE) = make_uint4(mn_lo, mn_hi, 0u, 0u);
+                    *reinterpret_cast<uint4*>(ax + 9u * C::ATILE) = make_uint4(0u, 0u, mn_lo, mn_hi);
                 }
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
                 __syncwarp();
@@ -828,8 +846,8 @@ __global__ void __launch_bounds__(32 * Q4Cfg<NT>::WARPS, 1) mm_q4k_tc_kernel(MvA
                 const uint32_t sbi = u % C::SB, buf = u % C::NB;
                 if (!mbar_wait_ab(&bfull[sbi], (u / C::SB) & 1u, abort_flag)) break;
                 if (u >= C::NB && !mbar_wait_ab(&tempty[buf], ((u / C::NB) - 1u) & 1u, abort_flag)) break;
-                uint8_t* bb = smem + C::B_OFF + (size_t)sbi * 8u * C::BT;
-                const uint32_t dh = tmem + buf * C::ACC_COLS, dl = dh + NT, dm = dh + 2u * NT;
+                uint8_t* bb = smem + C::B_OFF + (size_t)sbi * C::BENT;
+                const uint32_t dh = tmem + buf * C::ACC_COLS, dl = dh + NT, dlo = dh + 2u * NT, dhi = dh + 3u * NT;
 #pragma unroll
                 for (uint32_t hf = 0; hf < 2u; ++hf) {
                     const uint32_t hc = 2u * u + hf, slot = hc % C::NA;
@@ -842,7 +860,11 @@ __global__ void __launch_bounds__(32 * Q4Cfg<NT>::WARPS, 1) mm_q4k_tc_kernel(MvA
                         const uint64_t db = umma_desc_b<NT>(bb + (4u * hf + ks) * C::BT);
                         mma_i8(dh, umma_desc(ax + ks * C::ATILE), db, umma_idesc<NT>(), acc);
                         mma_i8(dl, umma_desc(ax + (4u + ks) * C::ATILE), db, umma_idesc<NT>(), acc);
-                        mma_i8(dm, umma_desc(ax + (8u + ks) * C::ATILE), db, umma_idesc<NT>(), acc);
+                    }
+                    if (hf == 0u) {                                  // the min sums' digit MMAs
+                        const uint64_t dd = umma_desc_b<NT>(bb + 8u * C::BT);
+                        mma_i8(dlo, umma_desc(ax + 8u * C::ATILE), dd, umma_idesc<NT>(), 0u);
+                        mma_i8(dhi, umma_desc(ax + 9u * C::ATILE), dd, umma_idesc<NT>(), 0u);
                     }
                     mma_commit(&aempty[slot]);
                 }
@@ -913,6 +935,7 @@ bool make_q4_maps(const MvArgs& a, Q4Maps* tm) {
                             {16, kTileM, 8, 1}))
         return false;
     if (!encode_u8<4>(&tm->b, a.qx, {16, a.T, 2, a.K / 32u}, {a.K, 16, 32}, {16, NT, 2, 8})) return false;
+    if (!encode_u8<2>(&tm->dig, a.bsd, {16ull * nsb, a.T}, {16ull * nsb}, {16, NT})) return false;
     return encode_u8<2>(&tm->meta, a.meta, {16ull * nsb, rows}, {L.meta_row_bytes()}, {16, kTileM});
 }
 

@@ -5,7 +5,10 @@
 //        id = d ? 1 (/) d : 0, q = round-half-away(x (*) id) saturated, D = f32(fp16(d)).
 //   A256 (Q4_K weights): per 256 values max = the signed DAZ(x) of the first largest |x|,
 //        iscale = -127 (/) max, q = round-half-even(iscale (*) x) saturated, d = 1 (/) iscale,
-//        bs = int16 sums of 16 q; an all-zero block gives d = 0, q = 0, bs = 0.
+//        bs = int16 sums of 16 q; an all-zero block gives d = 0, q = 0, bs = 0. Optionally also the
+//        sums of the eight 32-value sub-blocks p_j = bs_2j + bs_2j+1 (|p_j| <= 4064) as two int8
+//        digits each, p_j = 64 hi_j + lo_j with lo_j = p_j & 63, hi_j = p_j >> 6 (in [-64, 63]), as
+//        16 bytes per block {lo_0 .. lo_7, hi_0 .. hi_7}: the tensor-core operand of the Q4_K min sums.
 // One warp per block; the reductions are exact (integer max on |x| bits, first index on ties).
 #include "tsrc_internal.h"
 #include "tsrc_numerics.cuh"
@@ -32,7 +35,8 @@ __global__ void __launch_bounds__(256) qact_a32_kernel(const float* __restrict__
 
 __global__ void __launch_bounds__(256) qact_a256_kernel(const float* __restrict__ x, uint32_t K, uint32_t T,
                                                         uint32_t x_stride, int8_t* __restrict__ q,
-                                                        float* __restrict__ d, int16_t* __restrict__ bs) {
+                                                        float* __restrict__ d, int16_t* __restrict__ bs,
+                                                        int8_t* __restrict__ bsd) {
     asm volatile("griddepcontrol.launch_dependents;");
     const uint32_t nb = K >> 8;
     const uint32_t gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
@@ -85,11 +89,19 @@ __global__ void __launch_bounds__(256) qact_a256_kernel(const float* __restrict_
     *reinterpret_cast<uint2*>(q + (size_t)t * K + 256u * b + 8u * lane) = make_uint2(lo, hi);
     s += __shfl_xor_sync(0xFFFFFFFFu, s, 1);
     if ((lane & 1u) == 0) bs[(size_t)t * (K >> 4) + 16u * b + (lane >> 1)] = (int16_t)s;
+    if (bsd) {
+        const int32_t p = s + __shfl_xor_sync(0xFFFFFFFFu, s, 2);  // sub-block lane / 4: lanes 4 j .. 4 j + 3
+        if ((lane & 3u) == 0) {
+            int8_t* o = bsd + ((size_t)t * nb + b) * 16u;
+            o[lane >> 2] = (int8_t)(p & 63);
+            o[8u + (lane >> 2)] = (int8_t)(p >> 6);
+        }
+    }
     if (lane == 0) d[(size_t)t * nb + b] = db;
 }
 
 cudaError_t launch_qact(uint32_t kind, const float* x, uint32_t K, uint32_t T, uint32_t x_stride, int8_t* q, float* d,
-                        int16_t* bs, cudaStream_t st) {
+                        int16_t* bs, cudaStream_t st, int8_t* bsd) {
     const uint32_t bsz = kind == 0 ? 32u : 256u;
     const uint64_t warps = (uint64_t)T * (K / bsz);
     const uint32_t blocks = (uint32_t)((warps + 7u) / 8u);
@@ -97,7 +109,7 @@ cudaError_t launch_qact(uint32_t kind, const float* x, uint32_t K, uint32_t T, u
     if (kind == 0)
         qact_a32_kernel<<<blocks, 256, 0, st>>>(x, K, T, x_stride, q, d);
     else
-        qact_a256_kernel<<<blocks, 256, 0, st>>>(x, K, T, x_stride, q, d, bs);
+        qact_a256_kernel<<<blocks, 256, 0, st>>>(x, K, T, x_stride, q, d, bs, bsd);
     return cudaGetLastError();
 }
 
