@@ -7,15 +7,15 @@
 // into fresh TMEM tiles (no accumulation across blocks: each block has its own scales). The f32
 // part runs on the CUDA cores: blocks are visited partial by partial (i = j, j + 16, j + 32, ... for
 // j = 0..15), so a thread keeps one running partial per output and folds the partials into the
-// tree as they complete (((p0 + p1) + (p2 + p3)) + ...) through a four-level stack in shared memory.
+// tree as they complete (((p0 + p1) + (p2 + p3)) + ...) through a four-level stack in TMEM.
 // Q8_0: every factor is a multiple of 2^-24 (fp16 weight scales, the A32 activation scale stored as
 // fp16, integer sums), so every product and sum is a multiple of 2^-48 and never subnormal: the
 // flush tests are not needed.
 //
-// Work split: a CTA computes 128 rows x NT tokens with warp-specialised roles (producer warps
-// copying operands with cp.async into a ring of shared-memory stages in the canonical K-major,
-// no-swizzle layout of the UMMA descriptors -- 8-row x 16-byte core matrices, the two 16-byte
-// halves of a block 128 bytes apart, 8-row groups 256 bytes apart --, one thread issuing the MMAs,
+// Work split: a CTA computes 128 rows x NT tokens with warp-specialised roles (a producer warp
+// loading the operand tiles by TMA into rings of shared-memory stages in K-major, no-swizzle layouts
+// of the UMMA descriptors -- 8-row x 16-byte core matrices, the strides between them set by each
+// tensor map's box order --, one thread issuing the MMAs,
 // epilogue warps reading TMEM lanes 32 (w mod 4) .. + 31 and token columns 16 (w / 4) .. + 15),
 // handing work over through mbarriers. Every wait is bounded by the SM clock (~1 s); a wait that
 // runs out sets a CTA-wide abort flag that ends every role's loop, and error code 3, reported by
@@ -38,9 +38,6 @@ constexpr uint32_t kTileM = 128;
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
-__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
-}
 template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
@@ -137,74 +134,140 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
 }
 // waits for every tcgen05.ld of the thread: their registers are valid after it, not before
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
-// Folds partial j (16 values, one per token of the thread) into the 16-partial tree whose four
-// stack levels live in shared memory (level l of token i at s[l * lstride + i * kTileM]); after
-// partial 15 the tree's value is level 0. FLUSH: the reference's flush test on every sum.
-template <bool FLUSH>
-__device__ __forceinline__ void tree_push_smem(float* s, uint32_t lstride, uint32_t j, float (&v)[16]) {
-#pragma unroll
-    for (uint32_t lvl = 0; lvl < 4; ++lvl) {
-        float* p = s + lvl * lstride;
-        if (((j >> lvl) & 1u) == 0u) {
-#pragma unroll
-            for (uint32_t i = 0; i < 16; ++i) p[i * kTileM] = v[i];
-            return;
-        }
-#pragma unroll
-        for (uint32_t i = 0; i < 16; ++i) v[i] = FLUSH ? fadd(p[i * kTileM], v[i]) : __fadd_rn(p[i * kTileM], v[i]);
+// ---- TMA and TMEM helpers (both kernels) -------------------------------------------------------
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* b, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(b)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* m, int32_t c0, int32_t c1, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+        ::"r"(smem_u32(dst)), "l"(m), "r"(c0), "r"(c1), "r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* m, int32_t c0, int32_t c1, int32_t c2, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];"
+        ::"r"(smem_u32(dst)), "l"(m), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* m, int32_t c0, int32_t c1, int32_t c2, int32_t c3,
+                                            uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], [%6];"
+        ::"r"(smem_u32(dst)), "l"(m), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_u32(bar)) : "memory");
+}
+// Bounded wait that ignores the abort flag: the producer's last look at the loads it issued, so that
+// no TMA write lands in this CTA's shared memory after it has exited
+__device__ __forceinline__ void mbar_wait_drain(uint64_t* b, uint32_t parity) {
+    const uint32_t bar = smem_u32(b);
+    const long long t0 = clock64();
+    for (;;) {
+        uint32_t ok;
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+            "selp.u32 %0, 1, 0, p;\n\t}"
+            : "=r"(ok)
+            : "r"(bar), "r"(parity), "r"(1000u)
+            : "memory");
+        if (ok || clock64() - t0 > kWaitCycles) return;
     }
-#pragma unroll
-    for (uint32_t i = 0; i < 16; ++i) s[i * kTileM] = v[i];
+}
+// UMMA descriptor of a B image laid out by a b map (box {16, NT, 2, ...}): K-major, no swizzle,
+// LBO = 16 NT (K halves), SBO = 128 (8-token groups)
+template <uint32_t NT>
+__device__ __forceinline__ uint64_t umma_desc_b(const void* p) {
+    const uint64_t a = (smem_u32(p) >> 4) & 0x3FFFu;
+    return a | (uint64_t((16u * NT) >> 4) << 16) | (uint64_t(128u >> 4) << 32) | (uint64_t(1) << 46);
 }
 
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const float (&v)[16]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};"
+        ::"r"(taddr), "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
+          "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])), "r"(__float_as_uint(v[6])),
+          "r"(__float_as_uint(v[7])), "r"(__float_as_uint(v[8])), "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])),
+          "r"(__float_as_uint(v[11])), "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])),
+          "r"(__float_as_uint(v[15]))
+        : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// Folds partial j (16 values, one per token of the thread) into the 16-partial tree whose four stack
+// levels live in TMEM columns s, s + CS, s + 2 CS, s + 3 CS of the thread's lane (the stacked, earlier
+// partial is the left operand of each sum); after partial 15 the tree's value is level 0. FLUSH: the
+// reference's flush test on every sum.
+template <uint32_t CS, bool FLUSH>
+__device__ __forceinline__ void tree_push_tmem(uint32_t s, uint32_t j, float (&v)[16]) {
+#pragma unroll
+    for (uint32_t lvl = 0; lvl < 4; ++lvl) {
+        if (((j >> lvl) & 1u) == 0u) {
+            tmem_st16(s + lvl * CS, v);
+            tmem_wait_st();
+            return;
+        }
+        uint32_t p[16];
+        tmem_ld16(s + lvl * CS, p);
+        tmem_wait_ld();
+#pragma unroll
+        for (uint32_t i = 0; i < 16; ++i)
+            v[i] = FLUSH ? fadd(__uint_as_float(p[i]), v[i]) : __fadd_rn(__uint_as_float(p[i]), v[i]);
+    }
+    tmem_st16(s, v);
+    tmem_wait_st();
+}
+
+
 // ---- Q8_0 ---------------------------------------------------------------------------------------
-// Warp roles: E epilogue warps (warp w: TMEM lanes 32 (w mod 4) .., tokens 16 (w / 4) ..), P producer
-// warps (cp.async of the operand tiles, activation scales and weight scales of BPS consecutive
-// blocks of the sequence into one of S ring stages; each copying thread arrives on the stage's
-// full barrier when its copies have landed, cp.async.mbarrier.arrive), one MMA warp (TMEM allocation; one thread issues the stage's MMAs into
-// one of NB accumulator groups of BPS tiles, all of TMEM). The partial trees' stacks live in shared
-// memory. Grouping blocks per stage divides the barrier work per output element by BPS.
-// mbarriers: full[S] (producers -> MMA, epilogue), empty[S] (MMA commit + epilogue warps ->
-// producers), tfull[NB] (MMA commit -> epilogue), tempty[NB] (epilogue warps -> MMA).
-// pipeline shape (compile-time tuning knobs)
-#ifndef TSRC_Q8TC_P
-#define TSRC_Q8TC_P 2u
-#endif
-#ifndef TSRC_Q8TC_BPS
-#define TSRC_Q8TC_BPS 2u
-#endif
-#ifndef TSRC_Q8TC_S
-#define TSRC_Q8TC_S 6u
-#endif
-#ifndef TSRC_Q8TC_NB
-#define TSRC_Q8TC_NB 4u
-#endif
+// Warp roles: E epilogue warps (warp w: TMEM lanes 32 (w mod 4) .., tokens 16 (w / 4) ..), one producer
+// warp (lane 0 loads the weight and activation tiles of BPS consecutive blocks of the sequence by TMA
+// into one of S ring stages; the lanes copy the blocks' activation and weight scales with cp.async and
+// arrive when they have landed), one MMA warp (TMEM allocation; one thread issues the stage's MMAs into
+// one of NB accumulator groups of BPS tiles). The partial trees' stacks live in TMEM after the
+// accumulators. mbarriers: full[S] (producer -> MMA, epilogue), empty[S] (MMA commit + epilogue warps ->
+// producer), tfull[NB] (MMA commit -> epilogue), tempty[NB] (epilogue warps -> MMA).
+// Tensor maps (TMA, no swizzle, no multicast):
+//  a:    the Q8_0 quants of the full 16-block tiles, dims {256 B of a chunk line, row, chunk, tile}
+//        (strides {qrow, 256, 512}), box {16, 128, 2, 1}: block b of 128 rows lands as
+//        smem[2048 chunk + 16 row + byte], the K-major UMMA layout with LBO = 2048, SBO = 128;
+//  tail: the same for the last tile when it holds nv < 16 blocks (chunk stride 16 nv);
+//  b:    the QA image, dims {16 B, token, 16-value half} (strides {K, 16}), box {16, NT, 2}: block b of
+//        NT tokens lands as smem[16 NT half + 16 token + byte] (LBO = 16 NT, SBO = 128).
 template <uint32_t NT>
 struct Q8Cfg {
-    static constexpr uint32_t E = 4u * (NT / 16u);
-    static constexpr uint32_t P = TSRC_Q8TC_P;
+    static constexpr uint32_t E = 4u * (NT / 16u), P = 1u;
     static constexpr uint32_t WARPS = E + P + 1u;
-    static constexpr uint32_t BPS = TSRC_Q8TC_BPS;     // blocks per stage
-    static constexpr uint32_t S = TSRC_Q8TC_S;
-    static constexpr uint32_t NB = TSRC_Q8TC_NB;
+    static constexpr uint32_t BPS = 2u;                  // blocks per stage
+    static constexpr uint32_t S = 8u;
+    static constexpr uint32_t NB = 2u;                   // with the stack: 128 / 256 / 512 TMEM columns
     static constexpr uint32_t A_BYTES = kTileM * 32u, B_BYTES = NT * 32u;
     static constexpr uint32_t B_OFF = BPS * A_BYTES;
     static constexpr uint32_t DX_OFF = B_OFF + BPS * B_BYTES, DW_OFF = DX_OFF + BPS * NT * 4u;
-    static constexpr uint32_t STAGE = DW_OFF + BPS * kTileM * 4u;
-    static constexpr uint32_t TCOLS = NB * BPS * NT;
-    static constexpr size_t STACK_OFF = (size_t)S * STAGE;
-    static constexpr uint32_t LSTRIDE = NT * kTileM;   // floats per stack level
-    static constexpr size_t BAR_OFF = STACK_OFF + 4u * LSTRIDE * 4u;
+    static constexpr uint32_t STAGE = (DW_OFF + BPS * kTileM * 4u + 127u) & ~127u;
+    static constexpr uint32_t CS = NT == 48u ? 64u : NT;   // TMEM columns per accumulator tile / stack level
+    static constexpr uint32_t STK_COL = NB * BPS * CS, USED = STK_COL + 4u * CS;
+    static constexpr uint32_t TCOLS = USED <= 128u ? 128u : USED <= 256u ? 256u : 512u;
+    static constexpr size_t BAR_OFF = (size_t)S * STAGE;
     static constexpr size_t SMEM = BAR_OFF + (2u * S + 2u * NB) * 8u + 16u;
-    static_assert(TCOLS == 128u || TCOLS == 256u || TCOLS == 512u, "TMEM allocation is a power of two");
+    static_assert(USED <= 512u, "TMEM columns");
     static_assert(SMEM <= 227u * 1024u, "shared memory");
+    static_assert(NT <= 64u, "Dx copies: at most two per producer lane");
+    static_assert(NT % 16u == 0u, "M = 128 MMAs take N in multiples of 16");
 };
 
+struct alignas(64) Q8Maps {
+    CUtensorMap a, tail, b;
+    uint32_t nfull;        // tiles of 16 blocks in a row; blocks from 16 nfull on are in the tail
+};
+
+// UMMA descriptor of an A tile laid out by the a map: K-major, no swizzle, LBO = 2048, SBO = 128
+__device__ __forceinline__ uint64_t umma_desc_a8(const void* p) {
+    const uint64_t a = (smem_u32(p) >> 4) & 0x3FFFu;
+    return a | (uint64_t(2048u >> 4) << 16) | (uint64_t(128u >> 4) << 32) | (uint64_t(1) << 46);
+}
+
 template <uint32_t NT>
-__global__ void __launch_bounds__(32 * Q8Cfg<NT>::WARPS, 1) mm_q8_tc_kernel(MvArgs a) {
+__global__ void __launch_bounds__(32 * Q8Cfg<NT>::WARPS, 1) mm_q8_tc_kernel(MvArgs a, const __grid_constant__ Q8Maps tm) {
     using C = Q8Cfg<NT>;
     extern __shared__ __align__(128) uint8_t smem[];
-    float* stack = reinterpret_cast<float*>(smem + C::STACK_OFF);
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::BAR_OFF);
     uint64_t* empty = full + C::S;
     uint64_t* tfull = empty + C::S;
@@ -224,7 +287,7 @@ __global__ void __launch_bounds__(32 * Q8Cfg<NT>::WARPS, 1) mm_q8_tc_kernel(MvAr
     }
     if (threadIdx.x == 0) {
         for (uint32_t i = 0; i < C::S; ++i) {
-            mbar_init(&full[i], 32u * C::P);
+            mbar_init(&full[i], 1u + 32u * C::P);                // the TMA issuer's expect_tx + every lane's scale copies
             mbar_init(&empty[i], 1u + C::E);
         }
         for (uint32_t i = 0; i < C::NB; ++i) {
@@ -241,54 +304,38 @@ __global__ void __launch_bounds__(32 * Q8Cfg<NT>::WARPS, 1) mm_q8_tc_kernel(MvAr
     const uint32_t tmem = *tslot;
 
     if (warp >= C::E && warp < C::E + C::P) {
-        // ---- producers: lane pl copies A chunks of rows (pl / 2) + 32 P k, half pl & 1, ...
-        constexpr uint32_t LN = 32u * C::P, AR = 256u / LN, BR = (2u * NT + LN - 1u) / LN, WR = kTileM / LN;
-        constexpr uint32_t DR = (NT + LN - 1u) / LN;
-        const uint32_t pl = (warp - C::E) * 32u + lane, h = pl & 1u;
-        const uint8_t* arow[AR];
-        uint32_t adst[AR];
+        // ---- producer warp
+        const uint32_t nfull = tm.nfull;
+        const float* dxrow[2];
 #pragma unroll
-        for (uint32_t k = 0; k < AR; ++k) {
-            const uint32_t r = (pl >> 1) + (LN / 2u) * k;
-            arow[k] = a.qs + (size_t)min(row0 + r, a.n_rows - 1u) * L.qs_row_bytes();
-            adst[k] = (r >> 3) * 256u + h * 128u + (r & 7u) * 16u;
-        }
-        const int8_t* brow[BR];
-        uint32_t bdst[BR];
+        for (uint32_t k = 0; k < 2u; ++k) dxrow[k] = a.dx + (size_t)min(tok0 + lane + 32u * k, a.T - 1u) * nb;
+        const uint8_t* wrow[kTileM / 32u];
 #pragma unroll
-        for (uint32_t k = 0; k < BR; ++k) {
-            const uint32_t t = (pl >> 1) + (LN / 2u) * k;
-            brow[k] = a.qx + (size_t)min(tok0 + t, a.T - 1u) * K + 16u * h;
-            bdst[k] = t < NT ? C::B_OFF + (t >> 3) * 256u + h * 128u + (t & 7u) * 16u : 0xFFFFFFFFu;
-        }
-        const float* dxrow[DR];
-#pragma unroll
-        for (uint32_t k = 0; k < DR; ++k) dxrow[k] = a.dx + (size_t)min(tok0 + pl + LN * k, a.T - 1u) * nb;
-        const uint8_t* wrow[WR];
-#pragma unroll
-        for (uint32_t k = 0; k < WR; ++k)
-            wrow[k] = static_cast<const uint8_t*>(a.meta) + (size_t)min(row0 + pl + LN * k, a.n_rows - 1u) * L.meta_row_bytes();
-        uint32_t j = 0, ii = 0, cnt = q + (rem > 0u ? 1u : 0u);
+        for (uint32_t k = 0; k < kTileM / 32u; ++k)
+            wrow[k] = static_cast<const uint8_t*>(a.meta) + (size_t)min(row0 + lane + 32u * k, a.n_rows - 1u) * L.meta_row_bytes();
+        uint32_t j = 0, ii = 0, cnt = q + (rem > 0u ? 1u : 0u), issued = 0;
         for (uint32_t u = 0; u < nst; ++u) {
             const uint32_t st = u % C::S;
             if (u >= C::S && !mbar_wait_ab(&empty[st], ((u / C::S) - 1u) & 1u, abort_flag)) break;
             uint8_t* sb = smem + (size_t)st * C::STAGE;
+            const uint32_t nx = min(C::BPS, nb - u * C::BPS);    // blocks in this stage
+            if (lane == 0) mbar_expect_tx(&full[st], nx * (C::A_BYTES + C::B_BYTES));
 #pragma unroll
             for (uint32_t x = 0; x < C::BPS; ++x) {
-                if (u * C::BPS + x < nb) {
+                if (x < nx) {
                     const uint32_t b = j + 16u * ii;
-                    const size_t aoff = L.qs_off(0u, b, h);
+                    if (lane == 0) {
+                        const bool in_full = (b >> 4) < nfull;
+                        tma_load_4d(sb + x * C::A_BYTES, in_full ? &tm.a : &tm.tail, (int32_t)(16u * (b & 15u)), (int32_t)row0, 0,
+                                    in_full ? (int32_t)(b >> 4) : 0, &full[st]);
+                        tma_load_3d(sb + C::B_OFF + x * C::B_BYTES, &tm.b, 0, (int32_t)tok0, (int32_t)(2u * b), &full[st]);
+                    }
 #pragma unroll
-                    for (uint32_t k = 0; k < AR; ++k) cp_async16(sb + x * C::A_BYTES + adst[k], arow[k] + aoff);
+                    for (uint32_t k = 0; k < 2u; ++k)
+                        if (lane + 32u * k < NT) cp_async4(sb + C::DX_OFF + x * NT * 4u + 4u * (lane + 32u * k), dxrow[k] + b);
 #pragma unroll
-                    for (uint32_t k = 0; k < BR; ++k)
-                        if (bdst[k] != 0xFFFFFFFFu) cp_async16(sb + x * C::B_BYTES + bdst[k], brow[k] + 32u * b);
-#pragma unroll
-                    for (uint32_t k = 0; k < DR; ++k)
-                        if (pl + LN * k < NT) cp_async4(sb + C::DX_OFF + x * NT * 4u + 4u * (pl + LN * k), dxrow[k] + b);
-#pragma unroll
-                    for (uint32_t k = 0; k < WR; ++k)
-                        cp_async4(sb + C::DW_OFF + x * kTileM * 4u + 4u * (pl + LN * k), wrow[k] + 2u * (b & ~1u));
+                    for (uint32_t k = 0; k < kTileM / 32u; ++k)
+                        cp_async4(sb + C::DW_OFF + x * kTileM * 4u + 4u * (lane + 32u * k), wrow[k] + 2u * (b & ~1u));
                     if (++ii == cnt) {
                         ++j;
                         ii = 0;
@@ -297,8 +344,12 @@ __global__ void __launch_bounds__(32 * Q8Cfg<NT>::WARPS, 1) mm_q8_tc_kernel(MvAr
                 }
             }
             cp_async_arrive(&full[st]);                          // the stage is published when its copies land
+            ++issued;
         }
         cp_async_wait<0>();
+        if (lane == 0)      // the last loads into each stage have landed before the CTA may exit
+            for (uint32_t v = issued > C::S ? issued - C::S : 0u; v < issued; ++v) mbar_wait_drain(&full[v % C::S], (v / C::S) & 1u);
+        __syncwarp();
     } else if (warp == C::E + C::P) {
         // ---- MMA issuer
         if (lane == 0) {
@@ -312,8 +363,8 @@ __global__ void __launch_bounds__(32 * Q8Cfg<NT>::WARPS, 1) mm_q8_tc_kernel(MvAr
 #pragma unroll
                 for (uint32_t x = 0; x < C::BPS; ++x)
                     if (u * C::BPS + x < nb)
-                        mma_i8(tmem + (buf * C::BPS + x) * NT, umma_desc(sb + x * C::A_BYTES),
-                               umma_desc(sb + C::B_OFF + x * C::B_BYTES), umma_idesc<NT>(), 0u);
+                        mma_i8(tmem + (buf * C::BPS + x) * C::CS, umma_desc_a8(sb + x * C::A_BYTES),
+                               umma_desc_b<NT>(sb + C::B_OFF + x * C::B_BYTES), umma_idesc<NT>(), 0u);
                 mma_commit(&tfull[buf]);
                 mma_commit(&empty[st]);
                 ++issued;
@@ -328,8 +379,7 @@ __global__ void __launch_bounds__(32 * Q8Cfg<NT>::WARPS, 1) mm_q8_tc_kernel(MvAr
         // ---- epilogue: row = row0 + 32 rq + lane, tokens tok0 + 16 cq + i
         const uint32_t rq = warp & 3u, cq = warp >> 2;
         const uint32_t row = row0 + 32u * rq + lane;
-        const uint32_t tl = tmem + ((32u * rq) << 16) + 16u * cq;
-        float* stk = stack + 16u * cq * kTileM + 32u * rq + lane;
+        const uint32_t tl = tmem + ((32u * rq) << 16) + 16u * cq, ts = tl + C::STK_COL;
         float acc[16];
 #pragma unroll
         for (uint32_t i = 0; i < 16; ++i) acc[i] = 0.0f;
@@ -343,7 +393,7 @@ __global__ void __launch_bounds__(32 * Q8Cfg<NT>::WARPS, 1) mm_q8_tc_kernel(MvAr
             const uint8_t* sb = smem + (size_t)st * C::STAGE;
             uint32_t v[C::BPS][16];
 #pragma unroll
-            for (uint32_t x = 0; x < C::BPS; ++x) tmem_ld16(tl + (buf * C::BPS + x) * NT, v[x]);
+            for (uint32_t x = 0; x < C::BPS; ++x) tmem_ld16(tl + (buf * C::BPS + x) * C::CS, v[x]);
             tmem_wait_ld();
             asm volatile("tcgen05.fence::before_thread_sync;");
             __syncwarp();
@@ -366,7 +416,7 @@ __global__ void __launch_bounds__(32 * Q8Cfg<NT>::WARPS, 1) mm_q8_tc_kernel(MvAr
                         }
                     }
                     if (++ii == cnt) {                           // partial j is complete
-                        tree_push_smem<false>(stk, C::LSTRIDE, j, acc);
+                        tree_push_tmem<C::CS, false>(ts, j, acc);
 #pragma unroll
                         for (uint32_t i = 0; i < 16; ++i) acc[i] = 0.0f;
                         ++j;
@@ -383,14 +433,17 @@ __global__ void __launch_bounds__(32 * Q8Cfg<NT>::WARPS, 1) mm_q8_tc_kernel(MvAr
                 float z[16];
 #pragma unroll
                 for (uint32_t i = 0; i < 16; ++i) z[i] = 0.0f;
-                tree_push_smem<false>(stk, C::LSTRIDE, j, z);
+                tree_push_tmem<C::CS, false>(ts, j, z);
             }
+            uint32_t out[16];
+            tmem_ld16(ts, out);                                  // the tree's value: level 0
+            tmem_wait_ld();
             if (row < a.n_rows) {
 #pragma unroll
                 for (uint32_t i = 0; i < 16; ++i) {
                     const uint32_t tok = tok0 + 16u * cq + i;
                     if (tok < a.T) {
-                        float y = stk[i * kTileM];
+                        float y = __uint_as_float(out[i]);
                         if (a.flags & kMmAdd) y = fadd(daz(a.add[(size_t)tok * a.add_stride + row]), y);
                         if (a.flags & kMmSoftcap) y = fmul(tanh_vu(fmul(y, a.s0), g_expk_t64, g_expk_lk), a.s1);
                         else if (a.flags & kMmScale) y = fmul(y, a.s1);
@@ -407,32 +460,6 @@ __global__ void __launch_bounds__(32 * Q8Cfg<NT>::WARPS, 1) mm_q8_tc_kernel(MvAr
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(C::TCOLS));
     }
 }
-
-template <uint32_t NT>
-cudaError_t launch_nt(const MvArgs& a, cudaStream_t st) {
-    using C = Q8Cfg<NT>;
-    static int done_dev[64];
-    int dev = 0;
-    cudaError_t e = cudaGetDevice(&dev);
-    if (e != cudaSuccess) return e;
-    if (dev < 64 && done_dev[dev] != dev + 1) {
-        e = cudaFuncSetAttribute(mm_q8_tc_kernel<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM);
-        if (e != cudaSuccess) return e;
-        done_dev[dev] = dev + 1;
-    }
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((a.n_rows + kTileM - 1u) / kTileM, (a.T + NT - 1u) / NT);
-    cfg.blockDim = dim3(32u * C::WARPS);
-    cfg.dynamicSmemBytes = C::SMEM;
-    cfg.stream = st;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, mm_q8_tc_kernel<NT>, a);
-}
-
 
 // ---- Q4_K ---------------------------------------------------------------------------------------
 // The reference's superblock term (tsr_ref.c:540-567): isum = sum_j sc_j S_j over the eight 32-value
@@ -501,78 +528,6 @@ struct alignas(64) Q4Maps {
     CUtensorMap raw, tail, b, meta, dig;
     uint32_t nfull;        // tiles of 16 superblocks in a row; superblocks from 16 nfull on are in the tail
 };
-
-__device__ __forceinline__ void mbar_expect_tx(uint64_t* b, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(b)), "r"(bytes) : "memory");
-}
-__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* m, int32_t c0, int32_t c1, uint64_t* bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
-        ::"r"(smem_u32(dst)), "l"(m), "r"(c0), "r"(c1), "r"(smem_u32(bar)) : "memory");
-}
-__device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* m, int32_t c0, int32_t c1, int32_t c2, int32_t c3,
-                                            uint64_t* bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], [%6];"
-        ::"r"(smem_u32(dst)), "l"(m), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_u32(bar)) : "memory");
-}
-// Bounded wait that ignores the abort flag: the producer's last look at the loads it issued, so that
-// no TMA write lands in this CTA's shared memory after it has exited
-__device__ __forceinline__ void mbar_wait_drain(uint64_t* b, uint32_t parity) {
-    const uint32_t bar = smem_u32(b);
-    const long long t0 = clock64();
-    for (;;) {
-        uint32_t ok;
-        asm volatile(
-            "{\n\t.reg .pred p;\n\t"
-            "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
-            "selp.u32 %0, 1, 0, p;\n\t}"
-            : "=r"(ok)
-            : "r"(bar), "r"(parity), "r"(1000u)
-            : "memory");
-        if (ok || clock64() - t0 > kWaitCycles) return;
-    }
-}
-// UMMA descriptor of a B image laid out by the b map: K-major, no swizzle, LBO = 16 NT, SBO = 128
-template <uint32_t NT>
-__device__ __forceinline__ uint64_t umma_desc_b(const void* p) {
-    const uint64_t a = (smem_u32(p) >> 4) & 0x3FFFu;
-    return a | (uint64_t((16u * NT) >> 4) << 16) | (uint64_t(128u >> 4) << 32) | (uint64_t(1) << 46);
-}
-
-__device__ __forceinline__ void tmem_st16(uint32_t taddr, const float (&v)[16]) {
-    asm volatile(
-        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};"
-        ::"r"(taddr), "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
-          "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])), "r"(__float_as_uint(v[6])),
-          "r"(__float_as_uint(v[7])), "r"(__float_as_uint(v[8])), "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])),
-          "r"(__float_as_uint(v[11])), "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])),
-          "r"(__float_as_uint(v[15]))
-        : "memory");
-}
-__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
-
-// tree_push_smem with the four stack levels in TMEM columns s, s + NT, s + 2 NT, s + 3 NT of the
-// thread's lane (same order of additions: the stacked, earlier partial is the left operand)
-template <uint32_t NT, bool FLUSH>
-__device__ __forceinline__ void tree_push_tmem(uint32_t s, uint32_t j, float (&v)[16]) {
-#pragma unroll
-    for (uint32_t lvl = 0; lvl < 4; ++lvl) {
-        if (((j >> lvl) & 1u) == 0u) {
-            tmem_st16(s + lvl * NT, v);
-            tmem_wait_st();
-            return;
-        }
-        uint32_t p[16];
-        tmem_ld16(s + lvl * NT, p);
-        tmem_wait_ld();
-#pragma unroll
-        for (uint32_t i = 0; i < 16; ++i)
-            v[i] = FLUSH ? fadd(__uint_as_float(p[i]), v[i]) : __fadd_rn(__uint_as_float(p[i]), v[i]);
-    }
-    tmem_st16(s, v);
-    tmem_wait_st();
-}
 
 template <uint32_t NT, bool SAFE>
 __device__ __forceinline__ void q4k_epilogue(const MvArgs& a, uint8_t* smem, uint64_t* efull, uint64_t* eempty,
@@ -966,6 +921,47 @@ cudaError_t launch_q4k_nt(const MvArgs& a, cudaStream_t st) {
     return cudaLaunchKernelEx(&cfg, mm_q4k_tc_kernel<NT>, a, tm);
 }
 
+template <uint32_t NT>
+bool make_q8_maps(const MvArgs& a, Q8Maps* tm) {
+    const Layout L{0u, a.K};
+    const uint32_t nb = a.K / 32u, nfull = nb / 16u, nv = nb % 16u;
+    const cuuint64_t qrow = L.qs_row_bytes(), rows = a.n_rows;
+    *tm = Q8Maps{};
+    tm->nfull = nfull;
+    if (nfull && !encode_u8<4>(&tm->a, a.qs, {256, rows, 2, nfull}, {qrow, 256, 512}, {16, kTileM, 2, 1})) return false;
+    if (nv && !encode_u8<4>(&tm->tail, a.qs + (size_t)nfull * 512u, {16ull * nv, rows, 2, 1}, {qrow, 16ull * nv, 32ull * nv},
+                            {16, kTileM, 2, 1}))
+        return false;
+    return encode_u8<3>(&tm->b, a.qx, {16, a.T, a.K / 16u}, {a.K, 16}, {16, NT, 2});
+}
+
+template <uint32_t NT>
+cudaError_t launch_nt(const MvArgs& a, cudaStream_t st) {
+    using C = Q8Cfg<NT>;
+    static int done_dev[64];
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 64 && done_dev[dev] != dev + 1) {
+        e = cudaFuncSetAttribute(mm_q8_tc_kernel<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM);
+        if (e != cudaSuccess) return e;
+        done_dev[dev] = dev + 1;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((a.n_rows + kTileM - 1u) / kTileM, (a.T + NT - 1u) / NT);
+    cfg.blockDim = dim3(32u * C::WARPS);
+    cfg.dynamicSmemBytes = C::SMEM;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    Q8Maps tm;
+    if (!make_q8_maps<NT>(a, &tm)) return cudaErrorInvalidValue;
+    return cudaLaunchKernelEx(&cfg, mm_q8_tc_kernel<NT>, a, tm);
+}
+
 }  // namespace
 
 cudaError_t tc_error(uint32_t* code, bool clear) {
@@ -983,7 +979,14 @@ cudaError_t launch_mm_tc(uint32_t fmt, const MvArgs& a, cudaStream_t st) {
     if (fmt == 1u) return a.T <= 16 ? launch_q4k_nt<16>(a, st) : a.T <= 32 ? launch_q4k_nt<32>(a, st) : launch_q4k_nt<64>(a, st);
     if (a.T <= 16) return launch_nt<16>(a, st);
     if (a.T <= 32) return launch_nt<32>(a, st);
-    return launch_nt<64>(a, st);
+    // 64- or 48-token tiles (one CTA per SM either way): the width with fewer waves x tokens per CTA,
+    // so that a grid just past a whole number of waves (config 4: 304 CTAs of 64 on 148 SMs) does
+    // not leave most SMs idle in its last wave
+    int dev = 0, sms = 148;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const uint64_t rt = (a.n_rows + kTileM - 1u) / kTileM, sm = sms > 0 ? (uint64_t)sms : 148u;
+    const uint64_t c64 = (rt * ((a.T + 63u) / 64u) + sm - 1u) / sm * 64u, c48 = (rt * ((a.T + 47u) / 48u) + sm - 1u) / sm * 48u;
+    return c48 < c64 ? launch_nt<48>(a, st) : launch_nt<64>(a, st);
 }
 
 }  // namespace tsrc
