@@ -99,10 +99,10 @@ __device__ __forceinline__ bool mbar_wait_ab(uint64_t* b, uint32_t parity, volat
         uint32_t ok;
         asm volatile(
             "{\n\t.reg .pred p;\n\t"
-            "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+            "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"     // the default suspend time
             "selp.u32 %0, 1, 0, p;\n\t}"
             : "=r"(ok)
-            : "r"(bar), "r"(parity), "r"(1000u)
+            : "r"(bar), "r"(parity)
             : "memory");
         if (ok) return true;
         // the abort flag and the clock every 64 polls: a poll is a shared-memory access, and warps
@@ -235,9 +235,9 @@ template <uint32_t NT>
 struct Q8Cfg {
     static constexpr uint32_t E = 4u * (NT / 16u), P = 1u;
     static constexpr uint32_t WARPS = E + P + 1u;
-    static constexpr uint32_t BPS = 2u;                  // blocks per stage
-    static constexpr uint32_t S = 8u;
-    static constexpr uint32_t NB = 2u;                   // with the stack: 128 / 256 / 512 TMEM columns
+    static constexpr uint32_t BPS = 4u;                  // blocks per stage: fewer barrier rounds per block
+    static constexpr uint32_t S = 6u;
+    static constexpr uint32_t NB = 1u;                   // with the stack: 128 / 256 / 512 TMEM columns
     static constexpr uint32_t A_BYTES = kTileM * 32u, B_BYTES = NT * 32u;
     static constexpr uint32_t B_OFF = BPS * A_BYTES;
     static constexpr uint32_t DX_OFF = B_OFF + BPS * B_BYTES, DW_OFF = DX_OFF + BPS * NT * 4u;
