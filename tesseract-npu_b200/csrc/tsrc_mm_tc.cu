@@ -22,6 +22,7 @@
 // tsrc_sync.
 #include <cuda.h>                                  // CUtensorMap (the encoder is reached through the runtime)
 
+#include <algorithm>
 #include <mutex>
 
 #include "tsrc_internal.h"
@@ -276,9 +277,10 @@ __global__ void __launch_bounds__(32 * Q8Cfg<NT>::WARPS, 1) mm_q8_tc_kernel(MvAr
     volatile uint32_t* abort_flag = tslot + 1;
 
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
-    const uint32_t row0 = blockIdx.x * kTileM, tok0 = blockIdx.y * NT;
+    // persistent CTAs: tile t = (row tile t mod rt, token tile t / rt) for t = blockIdx.x, + gridDim.x, ...
+    const uint32_t rt = (a.n_rows + kTileM - 1u) / kTileM, n_tiles = rt * ((a.T + NT - 1u) / NT);
     const uint32_t K = a.K, nb = K / 32u, q = nb >> 4, rem = nb & 15u;
-    const uint32_t nst = (nb + C::BPS - 1u) / C::BPS;      // stage uses
+    const uint32_t nst = (nb + C::BPS - 1u) / C::BPS;      // stage uses per tile
     const Layout L{0u, K};
 
     if (warp == C::E + C::P) {
@@ -306,129 +308,137 @@ __global__ void __launch_bounds__(32 * Q8Cfg<NT>::WARPS, 1) mm_q8_tc_kernel(MvAr
     if (warp >= C::E && warp < C::E + C::P) {
         // ---- producer warp
         const uint32_t nfull = tm.nfull;
-        const float* dxrow[2];
+        uint32_t g = 0;                                          // stage uses issued, over all tiles
+        bool quit = false;
+        for (uint32_t tile = blockIdx.x; tile < n_tiles && !quit; tile += gridDim.x) {
+            const uint32_t row0 = (tile % rt) * kTileM, tok0 = (tile / rt) * NT;
+            const float* dxrow[2];
 #pragma unroll
-        for (uint32_t k = 0; k < 2u; ++k) dxrow[k] = a.dx + (size_t)min(tok0 + lane + 32u * k, a.T - 1u) * nb;
-        const uint8_t* wrow[kTileM / 32u];
+            for (uint32_t k = 0; k < 2u; ++k) dxrow[k] = a.dx + (size_t)min(tok0 + lane + 32u * k, a.T - 1u) * nb;
+            const uint8_t* wrow[kTileM / 32u];
 #pragma unroll
-        for (uint32_t k = 0; k < kTileM / 32u; ++k)
-            wrow[k] = static_cast<const uint8_t*>(a.meta) + (size_t)min(row0 + lane + 32u * k, a.n_rows - 1u) * L.meta_row_bytes();
-        uint32_t j = 0, ii = 0, cnt = q + (rem > 0u ? 1u : 0u), issued = 0;
-        for (uint32_t u = 0; u < nst; ++u) {
-            const uint32_t st = u % C::S;
-            if (u >= C::S && !mbar_wait_ab(&empty[st], ((u / C::S) - 1u) & 1u, abort_flag)) break;
-            uint8_t* sb = smem + (size_t)st * C::STAGE;
-            const uint32_t nx = min(C::BPS, nb - u * C::BPS);    // blocks in this stage
-            if (lane == 0) mbar_expect_tx(&full[st], nx * (C::A_BYTES + C::B_BYTES));
+            for (uint32_t k = 0; k < kTileM / 32u; ++k)
+                wrow[k] = static_cast<const uint8_t*>(a.meta) + (size_t)min(row0 + lane + 32u * k, a.n_rows - 1u) * L.meta_row_bytes();
+            uint32_t j = 0, ii = 0, cnt = q + (rem > 0u ? 1u : 0u);
+            for (uint32_t u = 0; u < nst; ++u, ++g) {
+                const uint32_t st = g % C::S;
+                if (g >= C::S && !mbar_wait_ab(&empty[st], ((g / C::S) - 1u) & 1u, abort_flag)) { quit = true; break; }
+                uint8_t* sb = smem + (size_t)st * C::STAGE;
+                const uint32_t nx = min(C::BPS, nb - u * C::BPS);    // blocks in this stage
+                if (lane == 0) mbar_expect_tx(&full[st], nx * (C::A_BYTES + C::B_BYTES));
 #pragma unroll
-            for (uint32_t x = 0; x < C::BPS; ++x) {
-                if (x < nx) {
-                    const uint32_t b = j + 16u * ii;
-                    if (lane == 0) {
-                        const bool in_full = (b >> 4) < nfull;
-                        tma_load_4d(sb + x * C::A_BYTES, in_full ? &tm.a : &tm.tail, (int32_t)(16u * (b & 15u)), (int32_t)row0, 0,
-                                    in_full ? (int32_t)(b >> 4) : 0, &full[st]);
-                        tma_load_3d(sb + C::B_OFF + x * C::B_BYTES, &tm.b, 0, (int32_t)tok0, (int32_t)(2u * b), &full[st]);
-                    }
+                for (uint32_t x = 0; x < C::BPS; ++x) {
+                    if (x < nx) {
+                        const uint32_t b = j + 16u * ii;
+                        if (lane == 0) {
+                            const bool in_full = (b >> 4) < nfull;
+                            tma_load_4d(sb + x * C::A_BYTES, in_full ? &tm.a : &tm.tail, (int32_t)(16u * (b & 15u)), (int32_t)row0,
+                                        0, in_full ? (int32_t)(b >> 4) : 0, &full[st]);
+                            tma_load_3d(sb + C::B_OFF + x * C::B_BYTES, &tm.b, 0, (int32_t)tok0, (int32_t)(2u * b), &full[st]);
+                        }
 #pragma unroll
-                    for (uint32_t k = 0; k < 2u; ++k)
-                        if (lane + 32u * k < NT) cp_async4(sb + C::DX_OFF + x * NT * 4u + 4u * (lane + 32u * k), dxrow[k] + b);
+                        for (uint32_t k = 0; k < 2u; ++k)
+                            if (lane + 32u * k < NT) cp_async4(sb + C::DX_OFF + x * NT * 4u + 4u * (lane + 32u * k), dxrow[k] + b);
 #pragma unroll
-                    for (uint32_t k = 0; k < kTileM / 32u; ++k)
-                        cp_async4(sb + C::DW_OFF + x * kTileM * 4u + 4u * (lane + 32u * k), wrow[k] + 2u * (b & ~1u));
-                    if (++ii == cnt) {
-                        ++j;
-                        ii = 0;
-                        cnt = q + (j < rem ? 1u : 0u);
+                        for (uint32_t k = 0; k < kTileM / 32u; ++k)
+                            cp_async4(sb + C::DW_OFF + x * kTileM * 4u + 4u * (lane + 32u * k), wrow[k] + 2u * (b & ~1u));
+                        if (++ii == cnt) {
+                            ++j;
+                            ii = 0;
+                            cnt = q + (j < rem ? 1u : 0u);
+                        }
                     }
                 }
+                cp_async_arrive(&full[st]);                      // the stage is published when its copies land
             }
-            cp_async_arrive(&full[st]);                          // the stage is published when its copies land
-            ++issued;
         }
         cp_async_wait<0>();
         if (lane == 0)      // the last loads into each stage have landed before the CTA may exit
-            for (uint32_t v = issued > C::S ? issued - C::S : 0u; v < issued; ++v) mbar_wait_drain(&full[v % C::S], (v / C::S) & 1u);
+            for (uint32_t v = g > C::S ? g - C::S : 0u; v < g; ++v) mbar_wait_drain(&full[v % C::S], (v / C::S) & 1u);
         __syncwarp();
     } else if (warp == C::E + C::P) {
         // ---- MMA issuer
         if (lane == 0) {
-            uint32_t issued = 0;
-            for (uint32_t u = 0; u < nst; ++u) {
-                const uint32_t st = u % C::S, buf = u % C::NB;
-                if (!mbar_wait_ab(&full[st], (u / C::S) & 1u, abort_flag)) break;
-                if (u >= C::NB && !mbar_wait_ab(&tempty[buf], ((u / C::NB) - 1u) & 1u, abort_flag)) break;
-                asm volatile("tcgen05.fence::after_thread_sync;");
-                uint8_t* sb = smem + (size_t)st * C::STAGE;
+            uint32_t g = 0;
+            bool quit = false;
+            for (uint32_t tile = blockIdx.x; tile < n_tiles && !quit; tile += gridDim.x) {
+                for (uint32_t u = 0; u < nst; ++u, ++g) {
+                    const uint32_t st = g % C::S, buf = g % C::NB;
+                    if (!mbar_wait_ab(&full[st], (g / C::S) & 1u, abort_flag)) { quit = true; break; }
+                    if (g >= C::NB && !mbar_wait_ab(&tempty[buf], ((g / C::NB) - 1u) & 1u, abort_flag)) { quit = true; break; }
+                    asm volatile("tcgen05.fence::after_thread_sync;");
+                    uint8_t* sb = smem + (size_t)st * C::STAGE;
 #pragma unroll
-                for (uint32_t x = 0; x < C::BPS; ++x)
-                    if (u * C::BPS + x < nb)
-                        mma_i8(tmem + (buf * C::BPS + x) * C::CS, umma_desc_a8(sb + x * C::A_BYTES),
-                               umma_desc_b<NT>(sb + C::B_OFF + x * C::B_BYTES), umma_idesc<NT>(), 0u);
-                mma_commit(&tfull[buf]);
-                mma_commit(&empty[st]);
-                ++issued;
+                    for (uint32_t x = 0; x < C::BPS; ++x)
+                        if (u * C::BPS + x < nb)
+                            mma_i8(tmem + (buf * C::BPS + x) * C::CS, umma_desc_a8(sb + x * C::A_BYTES),
+                                   umma_desc_b<NT>(sb + C::B_OFF + x * C::B_BYTES), umma_idesc<NT>(), 0u);
+                    mma_commit(&tfull[buf]);
+                    mma_commit(&empty[st]);
+                }
             }
-            if (issued) {     // the last MMA (and with it every earlier one) has completed
-                const uint32_t u = issued - 1u;
+            if (g) {          // the last MMA (and with it every earlier one) has completed
+                const uint32_t u = g - 1u;
                 mbar_wait_ab(&tfull[u % C::NB], (u / C::NB) & 1u, abort_flag);
             }
         }
         __syncwarp();
     } else {
-        // ---- epilogue: row = row0 + 32 rq + lane, tokens tok0 + 16 cq + i
+        // ---- epilogue: row = row0 + 32 rq + lane, tokens tok0 + 16 cq + i of each tile
         const uint32_t rq = warp & 3u, cq = warp >> 2;
-        const uint32_t row = row0 + 32u * rq + lane;
         const uint32_t tl = tmem + ((32u * rq) << 16) + 16u * cq, ts = tl + C::STK_COL;
-        float acc[16];
-#pragma unroll
-        for (uint32_t i = 0; i < 16; ++i) acc[i] = 0.0f;
-        uint32_t j = 0, ii = 0, cnt = q + (rem > 0u ? 1u : 0u);
+        uint32_t g = 0;
         bool aborted = false;
-        for (uint32_t u = 0; u < nst; ++u) {
-            const uint32_t st = u % C::S, buf = u % C::NB;
-            if (!mbar_wait_ab(&tfull[buf], (u / C::NB) & 1u, abort_flag)) { aborted = true; break; }
-            if (!mbar_wait_ab(&full[st], (u / C::S) & 1u, abort_flag)) { aborted = true; break; }
-            asm volatile("tcgen05.fence::after_thread_sync;");
-            const uint8_t* sb = smem + (size_t)st * C::STAGE;
-            uint32_t v[C::BPS][16];
+        for (uint32_t tile = blockIdx.x; tile < n_tiles && !aborted; tile += gridDim.x) {
+            const uint32_t row = (tile % rt) * kTileM + 32u * rq + lane, tok0 = (tile / rt) * NT;
+            float acc[16];
 #pragma unroll
-            for (uint32_t x = 0; x < C::BPS; ++x) tmem_ld16(tl + (buf * C::BPS + x) * C::CS, v[x]);
-            tmem_wait_ld();
-            asm volatile("tcgen05.fence::before_thread_sync;");
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&tempty[buf]);          // the accumulator group is free again
+            for (uint32_t i = 0; i < 16; ++i) acc[i] = 0.0f;
+            uint32_t j = 0, ii = 0, cnt = q + (rem > 0u ? 1u : 0u);
+            for (uint32_t u = 0; u < nst; ++u, ++g) {
+                const uint32_t st = g % C::S, buf = g % C::NB;
+                if (!mbar_wait_ab(&tfull[buf], (g / C::NB) & 1u, abort_flag)) { aborted = true; break; }
+                if (!mbar_wait_ab(&full[st], (g / C::S) & 1u, abort_flag)) { aborted = true; break; }
+                asm volatile("tcgen05.fence::after_thread_sync;");
+                const uint8_t* sb = smem + (size_t)st * C::STAGE;
+                uint32_t v[C::BPS][16];
 #pragma unroll
-            for (uint32_t x = 0; x < C::BPS; ++x) {
-                if (u * C::BPS + x < nb) {
-                    const float4* dx4 = reinterpret_cast<const float4*>(sb + C::DX_OFF + x * NT * 4u + 64u * cq);
-                    const uint32_t dwp = reinterpret_cast<const uint32_t*>(sb + C::DW_OFF + x * kTileM * 4u)[32u * rq + lane];
-                    const uint32_t b = j + 16u * ii;
-                    const float dw = h2f((uint16_t)((b & 1u) ? (dwp >> 16) : (dwp & 0xFFFFu)));
+                for (uint32_t x = 0; x < C::BPS; ++x) tmem_ld16(tl + (buf * C::BPS + x) * C::CS, v[x]);
+                tmem_wait_ld();
+                asm volatile("tcgen05.fence::before_thread_sync;");
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&tempty[buf]);      // the accumulator group is free again
 #pragma unroll
-                    for (uint32_t k = 0; k < 4; ++k) {
-                        const float4 f = dx4[k];
-                        const float d4[4] = {f.x, f.y, f.z, f.w};
+                for (uint32_t x = 0; x < C::BPS; ++x) {
+                    if (u * C::BPS + x < nb) {
+                        const float4* dx4 = reinterpret_cast<const float4*>(sb + C::DX_OFF + x * NT * 4u + 64u * cq);
+                        const uint32_t dwp = reinterpret_cast<const uint32_t*>(sb + C::DW_OFF + x * kTileM * 4u)[32u * rq + lane];
+                        const uint32_t b = j + 16u * ii;
+                        const float dw = h2f((uint16_t)((b & 1u) ? (dwp >> 16) : (dwp & 0xFFFFu)));
 #pragma unroll
-                        for (uint32_t e = 0; e < 4; ++e) {
-                            const uint32_t i = 4u * k + e;
-                            acc[i] = __fadd_rn(acc[i], __fmul_rn(__fmul_rn(dw, d4[e]), __int2float_rn((int32_t)v[x][i])));
+                        for (uint32_t k = 0; k < 4; ++k) {
+                            const float4 f = dx4[k];
+                            const float d4[4] = {f.x, f.y, f.z, f.w};
+#pragma unroll
+                            for (uint32_t e = 0; e < 4; ++e) {
+                                const uint32_t i = 4u * k + e;
+                                acc[i] = __fadd_rn(acc[i], __fmul_rn(__fmul_rn(dw, d4[e]), __int2float_rn((int32_t)v[x][i])));
+                            }
+                        }
+                        if (++ii == cnt) {                       // partial j is complete
+                            tree_push_tmem<C::CS, false>(ts, j, acc);
+#pragma unroll
+                            for (uint32_t i = 0; i < 16; ++i) acc[i] = 0.0f;
+                            ++j;
+                            ii = 0;
+                            cnt = q + (j < rem ? 1u : 0u);
                         }
                     }
-                    if (++ii == cnt) {                           // partial j is complete
-                        tree_push_tmem<C::CS, false>(ts, j, acc);
-#pragma unroll
-                        for (uint32_t i = 0; i < 16; ++i) acc[i] = 0.0f;
-                        ++j;
-                        ii = 0;
-                        cnt = q + (j < rem ? 1u : 0u);
-                    }
                 }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&empty[st]);
             }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&empty[st]);
-        }
-        if (!aborted) {
+            if (aborted) break;
             for (; j < 16u; ++j) {                               // partials nb .. 15 (fewer than 16 blocks) are +0
                 float z[16];
 #pragma unroll
@@ -939,7 +949,7 @@ template <uint32_t NT>
 cudaError_t launch_nt(const MvArgs& a, cudaStream_t st) {
     using C = Q8Cfg<NT>;
     static int done_dev[64];
-    int dev = 0;
+    int dev = 0, sms = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
     if (dev < 64 && done_dev[dev] != dev + 1) {
@@ -947,8 +957,11 @@ cudaError_t launch_nt(const MvArgs& a, cudaStream_t st) {
         if (e != cudaSuccess) return e;
         done_dev[dev] = dev + 1;
     }
+    e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return e;
+    const uint64_t tiles = (uint64_t)((a.n_rows + kTileM - 1u) / kTileM) * ((a.T + NT - 1u) / NT);
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((a.n_rows + kTileM - 1u) / kTileM, (a.T + NT - 1u) / NT);
+    cfg.gridDim = dim3((uint32_t)std::min<uint64_t>(tiles, (uint64_t)std::max(sms, 1)), 1);   // persistent CTAs
     cfg.blockDim = dim3(32u * C::WARPS);
     cfg.dynamicSmemBytes = C::SMEM;
     cfg.stream = st;
