@@ -992,13 +992,16 @@ cudaError_t launch_mm_tc(uint32_t fmt, const MvArgs& a, cudaStream_t st) {
     if (fmt == 1u) return a.T <= 16 ? launch_q4k_nt<16>(a, st) : a.T <= 32 ? launch_q4k_nt<32>(a, st) : launch_q4k_nt<64>(a, st);
     if (a.T <= 16) return launch_nt<16>(a, st);
     if (a.T <= 32) return launch_nt<32>(a, st);
-    // 64- or 48-token tiles (one CTA per SM either way): the width with fewer waves x tokens per CTA,
-    // so that a grid just past a whole number of waves (config 4: 304 CTAs of 64 on 148 SMs) does
-    // not leave most SMs idle in its last wave
+    // 64-, 48- or 32-token tiles: the width with the least (tiles per persistent CTA) x (tokens per tile
+    // + 16, the per-block work that does not grow with the width: the weight tile, the MMA issue),
+    // ties to the wider, so that neither a grid just past a whole number of SMs (config 4 FFN: 304
+    // tiles of 64 on 148 SMs) nor a narrow matrix (896 rows: 56 tiles of 64) leaves SMs idle
     int dev = 0, sms = 148;
     if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     const uint64_t rt = (a.n_rows + kTileM - 1u) / kTileM, sm = sms > 0 ? (uint64_t)sms : 148u;
-    const uint64_t c64 = (rt * ((a.T + 63u) / 64u) + sm - 1u) / sm * 64u, c48 = (rt * ((a.T + 47u) / 48u) + sm - 1u) / sm * 48u;
+    auto cost = [&](uint64_t nt) { return (rt * ((a.T + nt - 1u) / nt) + sm - 1u) / sm * (nt + 16u); };
+    const uint64_t c64 = cost(64), c48 = cost(48), c32 = cost(32);
+    if (c32 < c48 && c32 < c64) return launch_nt<32>(a, st);
     return c48 < c64 ? launch_nt<48>(a, st) : launch_nt<64>(a, st);
 }
 

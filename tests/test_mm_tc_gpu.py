@@ -111,8 +111,8 @@ def test_prefill_bench_shapes_bit_exact(dev, tsro, fmt, N, K, T, seed):
 
 @pytest.mark.parametrize("fmt,T", [(0, 16), (0, 32), (0, 100), (1, 16), (1, 32), (1, 100)])
 def test_prefill_tile_widths_large_n(dev, tsro, fmt, T):
-    """Each token-tile width of the tensor-core kernels (Q8_0 and Q4_K: 16 / 32 / 64 tokens)
-    at N = K = 4096, every row."""
+    """Token-tile widths of the tensor-core kernels at N = K = 4096, every row: Q4_K 16 / 32 / 64 tokens,
+    Q8_0 16 / 32 (at T = 100 its launch picks 32-token tiles)."""
     N, K = 4096, 4096
     wd = dev.synth(fmt, N, K, seed=600 + T + fmt)
     try:
@@ -120,6 +120,22 @@ def test_prefill_tile_widths_large_n(dev, tsro, fmt, T):
         x = H.acts(K, T, 700 + T + fmt)
         got = _mul_mat(dev, wd, x, T)
         want = tsro.matvec(fmt, w, K, x)
+        np.testing.assert_array_equal(got.view(np.uint32), want.view(np.uint32))
+    finally:
+        wd.free()
+
+
+@pytest.mark.parametrize("N,K,T", [(2048, 896, 1024), (896, 896, 512)])
+def test_prefill_q8_0_tile_width_choice(dev, tsro, N, K, T):
+    """Q8_0 shapes for which the launch picks 64-token tiles (2048 rows, 1024 tokens: a grid of many
+    tiles) and 32-token tiles (896 rows: 64-token tiles would fill 56 of the SMs), every row and token
+    bit for bit; the config-4 FFN shape, which picks 48, is checked above."""
+    wd = dev.synth(0, N, K, seed=900 + N)
+    try:
+        w = wd.download()
+        x = H.acts(K, T, 901 + N)
+        got = _mul_mat(dev, wd, x, T)
+        want = tsro.matvec(0, w, K, x)
         np.testing.assert_array_equal(got.view(np.uint32), want.view(np.uint32))
     finally:
         wd.free()
