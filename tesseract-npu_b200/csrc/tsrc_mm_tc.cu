@@ -3,9 +3,10 @@
 // Numerics: the reference's MVM row rule bit for bit (jwkim04/tesseract-npu sw/sim/tsr_ref.c:
 // 533-635): for each token and row, block i contributes t_i = (d_w (*) Dx_i) (*) f32(isum_i) to
 // partial p[i mod 16] (in order of i, from +0), then the fixed 16-partial tree. The exact int32
-// block sums isum_i come from tcgen05.mma (kind::i8, K = 32: one block or Q4_K sub-block per MMA)
-// into fresh TMEM tiles (no accumulation across blocks: each block has its own scales). The f32
-// part runs on the CUDA cores: blocks are visited partial by partial (i = j, j + 16, j + 32, ... for
+// block sums come from tcgen05.mma (kind::i8): Q8_0 one K = 32 MMA per block into a fresh TMEM tile
+// (each block has its own scales); Q4_K the superblock's scaled sums over K = 256 (its section below
+// says how the 6-bit sub-block scales and mins reach the tensor cores exactly). The f32 part runs on
+// the CUDA cores: blocks are visited partial by partial (i = j, j + 16, j + 32, ... for
 // j = 0..15), so a thread keeps one running partial per output and folds the partials into the
 // tree as they complete (((p0 + p1) + (p2 + p3)) + ...) through a four-level stack in TMEM.
 // Q8_0: every factor is a multiple of 2^-24 (fp16 weight scales, the A32 activation scale stored as
