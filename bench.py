@@ -62,25 +62,30 @@ def capture(torch, body, sync):
         return None
 
 
+E2E_BUFFERS = 4        # device input / output buffers the end-to-end pipeline rotates through
+
+
 def pipelined(torch, n, copy_in, compute, copy_out, s_in, s_out):
-    """Issues n end-to-end steps with step i + 1's copy in (stream s_in) and step i - 1's copy out
-    (stream s_out) under step i's compute on the current stream; the device buffers alternate by
-    step parity (b = i % 2), and every step still copies its own input in and its result out."""
+    """Issues n end-to-end steps with later steps' copies in (stream s_in) and earlier steps' copies
+    out (stream s_out) under step i's compute on the current stream; the device buffers rotate
+    (b = i % E2E_BUFFERS), so a copy waits only for the step E2E_BUFFERS back that used its buffer,
+    and every step still copies its own input in and its own result out."""
     comp = torch.cuda.current_stream()
     s_in.wait_stream(comp)
     s_out.wait_stream(comp)
     k_done, out_done = {}, {}
+    nb = E2E_BUFFERS
     for i in range(n):
-        b = i % 2
+        b = i % nb
         ev_in = torch.cuda.Event()
         with torch.cuda.stream(s_in):
-            if i >= 2:
-                s_in.wait_event(k_done[i - 2])              # step i - 2 computed from buffer b
+            if i >= nb:
+                s_in.wait_event(k_done[i - nb])             # the step that last computed from buffer b
             copy_in(b)
             ev_in.record(s_in)
         comp.wait_event(ev_in)
-        if i >= 2:
-            comp.wait_event(out_done[i - 2])                # step i - 2's result left buffer b
+        if i >= nb:
+            comp.wait_event(out_done[i - nb])               # that step's result left buffer b
         compute(i, b)
         k_done[i] = torch.cuda.Event()
         k_done[i].record(comp)
@@ -421,8 +426,10 @@ def fa_measure(dev, tsrc, torch, steps, warmup, world=1, rank=0, dist=None):
     o_host = torch.empty((world, h_loc * G, D)).pin_memory()
     n_e2e = min(steps, 2000)
 
-    # end to end, pipelined over steps as for the matvec (q and out alternate by step parity)
-    qb, ob, oab = [q, torch.empty_like(q)], [out, torch.empty_like(out)], [out_all, torch.empty_like(out_all)]
+    # end to end, pipelined over steps as for the matvec (q and out rotate over E2E_BUFFERS buffers)
+    qb = [q] + [torch.empty_like(q) for _ in range(E2E_BUFFERS - 1)]
+    ob = [out] + [torch.empty_like(out) for _ in range(E2E_BUFFERS - 1)]
+    oab = [out_all] + [torch.empty_like(out_all) for _ in range(E2E_BUFFERS - 1)]
     s_in, s_out = torch.cuda.Stream(), torch.cuda.Stream()
 
     def fa_step(i, b):
@@ -680,7 +687,7 @@ def run_fa(args):
         "e2e": {"value": round(info["e2e_steps"] * total / (ms_e2e * 1e-3) / 1e9, 2), "unit": "GB/s",
                 "h2d_bytes_per_step": info["h2d_bytes_per_step"], "d2h_bytes_per_step": info["d2h_bytes_per_step"],
                 "ms_per_step": round(ms_e2e / info["e2e_steps"], 6), "cuda_graph": info["e2e_cuda_graph"],
-                "pipelined": "step i+1's copy in and step i-1's copy out overlap step i's FA (two copy streams)"},
+                "pipelined": f"later steps' copies in and earlier steps' copies out overlap step i's FA (two copy streams, {E2E_BUFFERS} rotating device buffers)"},
         "gpu_launches": 2 * steps,
         "clocks": clk.summary(),
         "cpu_baseline": cpu,
@@ -1040,12 +1047,12 @@ def main():
             for i in range(n):
                 e2e_step(i)
 
-    # (2) pipelined over steps: step i's activation comes in on one copy stream while step i - 1
-    # computes, and its result goes out on another while step i + 1 computes (the device buffers
-    # alternate by step parity); every step still copies its own input in and its own result out
-    xb = [x, torch.empty_like(x)]
-    yb_loc = [y_loc, torch.empty_like(y_loc)]
-    yb_full = [y_full, torch.empty_like(y_full)]
+    # (2) pipelined over steps: step i's activation comes in on one copy stream while earlier steps
+    # compute, and its result goes out on another while later steps compute (the device buffers
+    # rotate over E2E_BUFFERS); every step still copies its own input in and its own result out
+    xb = [x] + [torch.empty_like(x) for _ in range(E2E_BUFFERS - 1)]
+    yb_loc = [y_loc] + [torch.empty_like(y_loc) for _ in range(E2E_BUFFERS - 1)]
+    yb_full = [y_full] + [torch.empty_like(y_full) for _ in range(E2E_BUFFERS - 1)]
     s_in, s_out = torch.cuda.Stream(), torch.cuda.Stream()
 
     def mm_step(i, b):
@@ -1161,7 +1168,7 @@ def main():
         "e2e": {"value": round(e2e, 2), "unit": "GB/s", "h2d_bytes_per_step": 4 * K,
                 "d2h_bytes_per_step": 4 * (R * world if world > 1 else n_rows),
                 "ms_per_step": round(ms_e2e / n_e2e, 6), "cuda_graph": pgraph is not None,
-                "pipelined": "step i+1's copy in and step i-1's copy out overlap step i's MUL_MAT (two copy streams)",
+                "pipelined": f"later steps' copies in and earlier steps' copies out overlap step i's MUL_MAT (two copy streams, {E2E_BUFFERS} rotating device buffers)",
                 "serial_value": round(n_e2e * total_bytes / (ms_e2e_serial * 1e-3) / 1e9, 2),
                 "serial_ms_per_step": round(ms_e2e_serial / n_e2e, 6)},
         "gpu_launches": args.steps,
