@@ -489,12 +489,13 @@ __global__ void __launch_bounds__(32 * Q8Cfg<NT>::WARPS, 1) mm_q8_tc_kernel(MvAr
 // an arbitrary f32: when every Dx of the CTA's tokens is 0 or at least 2^-79 in magnitude, every
 // product and sum is a multiple of 2^-126 and the flush tests are skipped (SAFE); otherwise they run.
 //
-// Warp roles: E epilogue warps (32 rows x 16 tokens each), P producer warps (cp.async of the raw
-// quants, with the 16-byte chunks of a row rotated by the row so that the expanders read without
-// bank conflicts, the B tiles, Dx and the 16-byte row metadata into three rings: the raw quants
-// (S entries, free once expanded), the B tiles (SB entries, free once the MMA has read them) and Dx
-// and the metadata (SE entries, free once the expanders and the epilogue have used them), so that no
-// copy waits for a later role than the one that reads it), X expander warps (one row per thread; a
+// Warp roles: E epilogue warps (32 rows x 16 tokens each), one producer warp (lane 0 loads the raw
+// quants, the B tiles with the digit rows, and the 16-byte row metadata by TMA through the tensor maps
+// below, whose box order lets the expanders read without bank conflicts; the lanes copy Dx with
+// cp.async) into three rings: the raw quants (S entries, free once expanded), the B tiles (SB entries,
+// free once the MMA has read them) and Dx and the metadata (SE entries, free once the expanders and the
+// epilogue have used them), so that no copy waits for a later role than the one that reads it), X
+// expander warps (one row per thread; a
 // superblock in two halves of 128 values, each into one of NA slots holding the H and L images of
 // four K steps; slot 0 also holds the two mins rows), one MMA warp. TMEM: one accumulator set (H, L,
 // Dlo, Dhi: NT columns each; the epilogue frees it as soon as it has read it, so the next
